@@ -1,0 +1,174 @@
+/*
+ * annb200.h - C ABI of libannb200.so, the B200 exact gather-scan.
+ *
+ * Plain pointers and sizes only. Device pointers are CUDA device addresses on
+ * the shard's device; streams are cudaStream_t passed as void * (NULL = the
+ * legacy default stream). Every entry point returns an AnnStatus value
+ * (0 = ANN_OK, 1 = ANN_INVALID, 2 = ANN_UNSUPPORTED, 4 = ANN_NOMEM,
+ * 5 = ANN_BACKEND_ERROR; ann/server/backend.h:12-28 in the reference) and
+ * leaves a message for AnnB200LastError() when it fails.
+ *
+ * Which reference interface each entry point replaces (reference paths are
+ * relative to the chenqin/pgvector project root):
+ *
+ *   AnnB200Backend()        the AnnBackend vtable constructor a worker selects
+ *                           with --backend (ann/server/backend.h:114-164,
+ *                           ann/server/worker.c:267-279); declared in
+ *                           annb200_backend.h.
+ *   AnnB200ShardCreate()    device upload of one index shard's rows plus the
+ *                           per-row norms the scan needs: the loaded-index
+ *                           shard upload of ann/server/cuvs.c:2677-2915 and
+ *                           AnnBlackwellUpload, ann/server/blackwell.c:961-1064.
+ *   AnnB200Search()         one exact gather-scan of a query batch over a
+ *                           shard and a candidate row list: SearchGather,
+ *                           ann/server/cuvs.c:4585-4930 (gather_f32/f16,
+ *                           cuvsSelectK, host re-score), the grouped
+ *                           tensor-core scan AnnBlackwellCandidates,
+ *                           ann/server/blackwell.c:1452-1548, and the CPU
+ *                           exact search it must equal, ann/server/cpu.c:82-276.
+ *   AnnB200MergeTopk()      the per-shard top-k merge AnnIndexTreeMerge,
+ *                           ann/server/indexfile.c:3235-3258 and MergeJob,
+ *                           ann/server/cuvs.c:3446-3455, on the device.
+ *   AnnB200BitmapRows()     filter bitmap to eligible row list, the expand_*
+ *                           kernels of ann/server/cuvs.c:1910-1968.
+ */
+#ifndef ANNB200_H
+#define ANNB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C"
+{
+#endif
+
+/* Row storage formats (ann/common/INDEX_FORMAT.md:38,54-57, plus bit rows). */
+#define ANNB200_F32 0			/* FP32, dims x 4 bytes a row */
+#define ANNB200_F16 1			/* IEEE half (halfvec), dims x 2 bytes */
+#define ANNB200_E4M3 2			/* FP8 codes, dims rounded up to 16 bytes, +
+								 * one FP32 row scale */
+#define ANNB200_NVFP4 3			/* E2M1 pairs, ceil(dims/16) x 8 bytes, + one
+								 * E4M3 scale per 16 dims + one FP32 row scale */
+#define ANNB200_BIT 4			/* packed bits, ceil(dims/8) bytes */
+
+/* Metrics: the worker's 0..2 (ann/server/cpu.c:139-142) plus Hamming. */
+#define ANNB200_L2 0			/* Euclidean distance */
+#define ANNB200_IP 1			/* negative inner product */
+#define ANNB200_COSINE 2		/* 1 - cosine similarity; zero-norm rows skipped */
+#define ANNB200_HAMMING 3		/* bit rows only */
+
+/* AnnB200ShardCreate flags */
+#define ANNB200_SHARD_HOST 1u	/* inputs are host pointers: copy them into
+								 * device memory the shard owns */
+
+/* AnnB200Search / AnnB200MergeTopk flags */
+#define ANNB200_WINDOW 1u		/* gathered-job results: every row within
+								 * d_k + 1e-3*|d_k| + 1e-6 of the k-th
+								 * distance (ann/server/backend.h:45-50) */
+#define ANNB200_FORCE_SIMT 2u	/* score on CUDA cores even where the tcgen05
+								 * tensor-core scan applies */
+
+typedef struct AnnB200Shard AnnB200Shard;
+
+/* The message of the calling thread's last failed call ("" if none). */
+const char *AnnB200LastError(void);
+
+/* Number of CUDA devices the library can use (0 without a GPU). */
+int			AnnB200DeviceCount(void);
+
+/*
+ * Make a shard of rows [0, rows) stored in one of the formats above, whose
+ * global row ids start at first_id. codes: rows x row-bytes; block_scales:
+ * NVFP4 only, rows x ceil(dims/16) E4M3 codes; row_scales: E4M3 and NVFP4,
+ * rows FP32. Without ANNB200_SHARD_HOST the pointers are device memory that
+ * the caller keeps alive until AnnB200ShardDestroy. The call computes each
+ * row's squared norm on the device and returns once the shard is usable.
+ */
+int			AnnB200ShardCreate(int device, uint32_t dtype, uint32_t dims, uint64_t rows,
+							   const void *codes, const void *block_scales,
+							   const float *row_scales, int64_t first_id,
+							   uint32_t flags, void *stream, AnnB200Shard **shard);
+void		AnnB200ShardDestroy(AnnB200Shard *shard);
+
+/*
+ * Re-point an existing shard at other rows already in device memory (same
+ * meaning as AnnB200ShardCreate without ANNB200_SHARD_HOST), reusing its
+ * buffers: for callers that search a new row set per request, such as the
+ * worker's gathered jobs (ann/server/backend.h:45-62).
+ */
+int			AnnB200ShardAssign(AnnB200Shard *shard, uint32_t dtype, uint32_t dims, uint64_t rows,
+							   const void *codes, const void *block_scales,
+							   const float *row_scales, int64_t first_id, void *stream);
+
+/*
+ * Exact k-nearest search of nq queries over the shard's candidate rows.
+ *
+ * queries  device, FP32 [nq][dims]; for Hamming, packed bits
+ *          [nq][ceil(dims/8)].
+ * rows     device u32 list of candidate row numbers within the shard,
+ *          strictly increasing, nrows long; NULL scans every row.
+ * Results  device [nq][out_cap] FP64 distances and int64 global row ids
+ *          (first_id + row), sorted by (distance, id), counts [nq]. Without
+ *          ANNB200_WINDOW each query gets min(k, eligible rows) results and
+ *          out_cap must be >= k; with it, every row within the gathered
+ *          tolerance of the k-th distance (out_cap >= nrows guarantees room).
+ * status   optional device int32 [nq]: ANN_INVALID for a query with a
+ *          non-finite value, or a zero norm under cosine.
+ *
+ * Distances equal, bit for bit, the reference CPU worker's on the rows
+ * decoded to FP32 (ann/server/cpu.c:82-276): L2 as sqrt of the eight-lane
+ * FP32 sum, inner product and cosine in FP64. The call is synchronous with
+ * respect to stream (it waits for its own kernels).
+ */
+int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
+						  const uint32_t *rows, uint64_t nrows, uint32_t k,
+						  uint32_t metric, uint32_t flags, uint32_t out_cap,
+						  double *out_dist, int64_t *out_id, uint32_t *out_count,
+						  int32_t *status, void *stream);
+
+/*
+ * Merge nlists per-shard result sets into one per query, on the device.
+ * Inputs: device [nlists][nq][list_cap] distances/ids and [nlists][nq]
+ * counts, each list sorted by (distance, id) with disjoint ids (the layout an
+ * all-gather of AnnB200Search outputs produces). Output as AnnB200Search:
+ * the k best by (distance, id), or with ANNB200_WINDOW every entry within
+ * the gathered tolerance of the merged k-th distance. nlists * list_cap must
+ * not exceed 4096.
+ */
+int			AnnB200MergeTopk(const double *dist, const int64_t *ids, const uint32_t *counts,
+							 uint32_t nlists, uint32_t nq, uint32_t list_cap, uint32_t k,
+							 uint32_t flags, uint32_t out_cap, double *out_dist,
+							 int64_t *out_id, uint32_t *out_count, void *stream);
+
+/*
+ * Expand a filter bitmap (bit r of word r/32, least significant bit first)
+ * into the strictly increasing list of set row numbers. rows must hold
+ * nbits entries; *count (host) receives how many were written. Synchronous.
+ */
+int			AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows,
+							  uint64_t *count, void *stream);
+
+/*
+ * Kernels this library has launched in this process (all devices). A caller
+ * that times a region reads it before and after to count its launches.
+ */
+unsigned long long AnnB200LaunchCount(void);
+
+/*
+ * Per-stage device time, accumulated over calls when the environment sets
+ * ANN_B200_KERNEL_TIMING=1 (CUDA events on each call's stream; the
+ * reference's ANN_KERNEL_TIMING, ann/server/cuvs.c:6999-7060). Stages, in
+ * order: 0 query preparation, 1 sample scan, 2 sample bound, 3 filter scan,
+ * 4 tighten, 5 finalize (exact rescoring and ordering), 6 bitmap expansion,
+ * 7 merge. Fills up to n entries of ms (milliseconds) and calls; reset
+ * clears the totals. Returns the number of stages, or 0 when timing is off.
+ */
+#define ANNB200_STAGES 8
+int			AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif							/* ANNB200_H */

@@ -1,0 +1,153 @@
+"""pgvector_b200: B200-native exact gather-scan behind the ANN worker's backend ABI.
+
+Host-side mirror of the reference worker's interface for this path:
+
+  * ``search_gathered(jobs)``  - the backend's search_gathered over gathered
+    jobs (ann/server/backend.h:45-62,130; ann/server/cpu.c:218-283): one query
+    against caller-supplied FP32 rows, results hold every row within the
+    gathered tolerance of the k-th distance, sorted by (distance, id).
+  * ``Shard`` / ``Shard.search`` - a device-resident shard in fp32, fp16
+    (halfvec), FP8-E4M3, NVFP4 or bit format, searched for a query batch over
+    a candidate row list (the loaded-index gather scan,
+    ann/server/cuvs.c:4585-4930).
+  * ``merge_topk`` - the on-device merge of per-shard lists
+    (AnnIndexTreeMerge, ann/server/indexfile.c:3235-3258).
+  * ``bitmap_rows`` - filter bitmap to row list (expand_*,
+    ann/server/cuvs.c:1910-1968).
+
+All compute runs in libannb200.so (AOT sm_100a CUDA); there is no CPU path.
+Tensors are torch CUDA tensors; torch only provides device memory and streams.
+"""
+import ctypes
+
+import numpy as np
+
+from . import _abi
+from ._lib import (OK, INVALID, UNSUPPORTED, NOMEM, BACKEND_ERROR, AnnB200Error, check, load)
+
+F32, F16, E4M3, NVFP4, BIT = 0, 1, 2, 3, 4
+L2, IP, COSINE, HAMMING = 0, 1, 2, 3
+SHARD_HOST = 1
+WINDOW, FORCE_SIMT = 1, 2
+
+DTYPE_NAMES = {'f32': F32, 'float32': F32, 'f16': F16, 'float16': F16, 'halfvec': F16, 'e4m3': E4M3,
+               'fp8': E4M3, 'nvfp4': NVFP4, 'bit': BIT}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def device_count():
+    return load().AnnB200DeviceCount()
+
+
+class Shard:
+    """A shard of rows on one GPU; codes (and scales) are torch CUDA tensors
+    kept alive by this object."""
+
+    def __init__(self, dtype, dims, codes, block_scales=None, row_scales=None, first_id=0, stream=None):
+        lib = load()
+        self.dtype = DTYPE_NAMES.get(dtype, dtype)
+        self.dims = int(dims)
+        self.codes, self.block_scales, self.row_scales = codes, block_scales, row_scales
+        self.rows = int(codes.shape[0])
+        self.first_id = int(first_id)
+        self.device = codes.device.index if codes.device.index is not None else 0
+        handle = ctypes.c_void_p()
+        check(lib.AnnB200ShardCreate(self.device, self.dtype, self.dims, self.rows, _ptr(codes),
+                                     _ptr(block_scales), _ptr(row_scales), self.first_id, 0, _stream(stream),
+                                     ctypes.byref(handle)))
+        self._handle = handle
+
+    def close(self):
+        if getattr(self, '_handle', None):
+            load().AnnB200ShardDestroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def search(self, queries, k, metric, rows=None, window=False, force_simt=False, out_cap=None,
+               stream=None, status=None):
+        """Exact search of a query batch; returns (dist f64 [nq][cap], id i64
+        [nq][cap], count u32 [nq]) CUDA tensors."""
+        import torch
+        nq = int(queries.shape[0])
+        nrows = int(rows.shape[0]) if rows is not None else self.rows
+        cap = int(out_cap if out_cap is not None else (max(nrows, 1) if window else max(k, 1)))
+        dev = queries.device
+        dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
+        ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
+        count = torch.empty((nq,), dtype=torch.int32, device=dev)
+        flags = (WINDOW if window else 0) | (FORCE_SIMT if force_simt else 0)
+        check(load().AnnB200Search(self._handle, _ptr(queries), nq, _ptr(rows), nrows if rows is not None else 0,
+                                   int(k), int(metric), flags, cap, _ptr(dist), _ptr(ids), _ptr(count),
+                                   _ptr(status), _stream(stream)))
+        return dist, ids, count
+
+
+def merge_topk(dist, ids, counts, k, window=False, out_cap=None, stream=None):
+    """Merge [nlists][nq][list_cap] per-shard results on the device."""
+    import torch
+    nlists, nq, list_cap = (int(x) for x in dist.shape)
+    cap = int(out_cap if out_cap is not None else (nlists * list_cap if window else max(k, 1)))
+    od = torch.empty((nq, cap), dtype=torch.float64, device=dist.device)
+    oi = torch.empty((nq, cap), dtype=torch.int64, device=dist.device)
+    oc = torch.empty((nq,), dtype=torch.int32, device=dist.device)
+    check(load().AnnB200MergeTopk(_ptr(dist), _ptr(ids), _ptr(counts), nlists, nq, list_cap, int(k),
+                                  WINDOW if window else 0, cap, _ptr(od), _ptr(oi), _ptr(oc), _stream(stream)))
+    return od, oi, oc
+
+
+def bitmap_rows(words, nbits, stream=None):
+    """Row numbers of the set bits of a u32 bitmap (CUDA tensor), ascending."""
+    import torch
+    rows = torch.empty((max(int(nbits), 1),), dtype=torch.int32, device=words.device)
+    n = ctypes.c_uint64()
+    check(load().AnnB200BitmapRows(_ptr(words), int(nbits), _ptr(rows), ctypes.byref(n), _stream(stream)))
+    return rows[:n.value]
+
+
+def backend():
+    """The AnnBackend vtable AnnB200Backend() returns."""
+    return load().AnnB200Backend().contents
+
+
+def search_gathered(jobs):
+    """Run gathered jobs through the backend: jobs are (query, vectors, k,
+    metric) with float32 numpy arrays; returns [(status, [(id, distance)])]."""
+    n = len(jobs)
+    arr = (_abi.AnnGatheredJob * n)()
+    keep = []
+    for i, (query, vectors, k, metric) in enumerate(jobs):
+        q = np.ascontiguousarray(query, dtype=np.float32)
+        v = np.ascontiguousarray(vectors, dtype=np.float32).reshape(-1, q.shape[0]) if q.shape[0] else \
+            np.zeros((0, 0), np.float32)
+        rows = v.shape[0]
+        res = (_abi.AnnCandidate * max(rows, 1))()
+        keep += [q, v, res]
+        arr[i].rows, arr[i].dimensions, arr[i].k, arr[i].metric = rows, q.shape[0], int(k), int(metric)
+        arr[i].query = q.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        arr[i].vectors = v.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        arr[i].results = res
+    backend().search_gathered(arr, n)
+    out = []
+    for i in range(n):
+        out.append((arr[i].status, [(arr[i].results[j].id, arr[i].results[j].distance)
+                                    for j in range(arr[i].nresults)]))
+    return out
+
+
+__all__ = ['Shard', 'merge_topk', 'bitmap_rows', 'backend', 'search_gathered', 'device_count', 'load', 'check',
+           'AnnB200Error', 'F32', 'F16', 'E4M3', 'NVFP4', 'BIT', 'L2', 'IP', 'COSINE', 'HAMMING', 'WINDOW',
+           'FORCE_SIMT', 'OK', 'INVALID', 'UNSUPPORTED', 'NOMEM', 'BACKEND_ERROR']

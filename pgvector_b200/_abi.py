@@ -1,0 +1,43 @@
+"""ctypes layouts of the worker backend ABI (include/annb200_backend.h).
+
+Field order and C types follow the reference worker's backend.h
+(ann/server/backend.h:30-151 in chenqin/pgvector), so a Python caller can
+drive AnnB200Backend() exactly as the worker's lane threads do.
+"""
+import ctypes
+
+
+class AnnCandidate(ctypes.Structure):
+    _fields_ = [('id', ctypes.c_uint32), ('distance', ctypes.c_double)]
+
+
+class AnnGatheredJob(ctypes.Structure):
+    _fields_ = [('rows', ctypes.c_uint32), ('dimensions', ctypes.c_uint32), ('k', ctypes.c_uint32),
+                ('metric', ctypes.c_uint32), ('query', ctypes.POINTER(ctypes.c_float)),
+                ('vectors', ctypes.POINTER(ctypes.c_float)), ('results', ctypes.POINTER(AnnCandidate)),
+                ('nresults', ctypes.c_uint32), ('status', ctypes.c_int)]
+
+
+class AnnIndex(ctypes.Structure):
+    _fields_ = [('generation', ctypes.c_uint64), ('rows', ctypes.c_uint32), ('dimensions', ctypes.c_uint32),
+                ('vectors', ctypes.POINTER(ctypes.c_float)), ('backend_state', ctypes.c_void_p)]
+
+
+BUILD = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(AnnIndex), ctypes.c_uint64, ctypes.c_uint32,
+                         ctypes.c_uint32, ctypes.POINTER(ctypes.c_float))
+SEARCH = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(AnnIndex), ctypes.POINTER(ctypes.c_float), ctypes.c_uint32,
+                          ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.c_uint32,
+                          ctypes.POINTER(AnnCandidate), ctypes.POINTER(ctypes.c_uint32))
+DESTROY = ctypes.CFUNCTYPE(None, ctypes.POINTER(AnnIndex))
+SEARCH_GATHERED = ctypes.CFUNCTYPE(None, ctypes.POINTER(AnnGatheredJob), ctypes.c_uint32)
+DEVICE_JOBS = ctypes.CFUNCTYPE(ctypes.c_uint64)
+LOST = ctypes.CFUNCTYPE(ctypes.c_char_p)
+
+
+class AnnBackend(ctypes.Structure):
+    _fields_ = [('name', ctypes.c_char_p), ('metrics', ctypes.c_uint32), ('filters', ctypes.c_uint32),
+                ('algorithm', ctypes.c_char_p), ('storage', ctypes.c_char_p), ('exact', ctypes.c_int),
+                ('min_rows', ctypes.c_uint32), ('max_k', ctypes.c_uint32), ('build', BUILD), ('search', SEARCH),
+                ('destroy', DESTROY), ('search_gathered', SEARCH_GATHERED), ('device_jobs', ctypes.c_void_p),
+                ('load_index', ctypes.c_void_p), ('search_index', ctypes.c_void_p), ('lost', ctypes.c_void_p),
+                ('scan_preferred', ctypes.c_void_p)]

@@ -1,0 +1,493 @@
+/*
+ * backend.c - AnnB200Backend(): the worker backend vtable over libannb200.
+ *
+ * Drop-in for the reference worker's backend slot (ann/server/backend.h:
+ * 114-151): gathered jobs (ops 7/10; the cpu backend's SearchGathered,
+ * ann/server/cpu.c:218-283) and in-memory index build/search/destroy (ops
+ * 0-6; cpu.c:10-154) run on a CUDA device through AnnB200Search, which
+ * returns the CPU worker's exact results. Loaded on-disk indexes are not
+ * served by this backend yet (load_index / search_index are NULL, which the
+ * worker answers as unsupported, ann/server/server.c:1952,3795).
+ *
+ * Threading: the worker calls search_gathered from many lane threads at once
+ * (ann/server/server.c:1541). Each thread keeps its own device context (a
+ * stream, a reusable shard and staging buffers, like the reference's
+ * _Thread_local lane state in ann/server/cuvs.c:103-124); lanes spread over
+ * the visible devices round robin.
+ *
+ * Host-side fault injection for tests, in the manner of the reference's mock
+ * GPU backend (ann/server/mockgpu.c:148-200): ANN_B200_LOST_AFTER=N makes
+ * every device job after the first N fail with ANN_BACKEND_ERROR, and lost()
+ * then names a simulated lost context, so the worker's exit-70 path can be
+ * exercised without faulting a GPU.
+ */
+#define _GNU_SOURCE
+#include "../../include/annb200.h"
+#include "../../include/annb200_backend.h"
+
+#include <cuda_runtime_api.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdatomic.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+static atomic_ullong DeviceJobs;
+static atomic_uint NextLane;
+static atomic_int LostSimulated;
+static char LostReason[256];
+static pthread_mutex_t LostLock = PTHREAD_MUTEX_INITIALIZER;
+
+typedef struct Lane
+{
+	int			ready;
+	int			device;
+	cudaStream_t stream;
+	AnnB200Shard *shard;
+	void	   *rows;			/* device: the job's FP32 rows */
+	size_t		rowsBytes;
+	float	   *query;			/* device */
+	size_t		queryBytes;
+	uint32_t   *ids;			/* device: candidate ids of an index search */
+	size_t		idsBytes;
+	double	   *dist;			/* device results */
+	int64_t    *id;
+	uint32_t   *count;
+	size_t		resultCap;
+	double	   *hostDist;		/* pinned result staging */
+	int64_t    *hostId;
+	size_t		hostCap;
+} Lane;
+
+static _Thread_local Lane LaneState;
+
+/* Per in-memory index: its rows on the device of the lane that built it. */
+typedef struct IndexState
+{
+	int			device;
+	AnnB200Shard *shard;
+	void	   *rows;
+} IndexState;
+
+static long
+EnvLong(const char *name, long fallback)
+{
+	const char *v = getenv(name);
+
+	return v && *v ? strtol(v, NULL, 10) : fallback;
+}
+
+/* Whether a simulated device loss has been reached; counts this job. */
+static int
+InjectLost(void)
+{
+	long		after = EnvLong("ANN_B200_LOST_AFTER", -1);
+
+	if (after < 0)
+		return 0;
+	if ((long) atomic_load(&DeviceJobs) >= after)
+	{
+		pthread_mutex_lock(&LostLock);
+		if (!atomic_load(&LostSimulated))
+		{
+			snprintf(LostReason, sizeof(LostReason),
+					 "GPU context lost (simulated after %ld device jobs)", after);
+			atomic_store(&LostSimulated, 1);
+		}
+		pthread_mutex_unlock(&LostLock);
+		return 1;
+	}
+	return 0;
+}
+
+static int
+Grow(void **p, size_t *have, size_t want)
+{
+	if (want <= *have)
+		return 1;
+	if (*p)
+		cudaFree(*p);
+	*p = NULL;
+	*have = 0;
+	if (cudaMalloc(p, want) != cudaSuccess)
+		return 0;
+	*have = want;
+	return 1;
+}
+
+static int
+GrowHost(void **p, size_t *have, size_t want)
+{
+	if (want <= *have)
+		return 1;
+	if (*p)
+		cudaFreeHost(*p);
+	*p = NULL;
+	*have = 0;
+	if (cudaMallocHost(p, want) != cudaSuccess)
+		return 0;
+	*have = want;
+	return 1;
+}
+
+static Lane *
+LaneGet(void)
+{
+	Lane	   *lane = &LaneState;
+	int			devices;
+
+	if (lane->ready)
+	{
+		cudaSetDevice(lane->device);
+		return lane;
+	}
+	devices = AnnB200DeviceCount();
+	if (devices <= 0)
+		return NULL;
+	lane->device = (int) (atomic_fetch_add(&NextLane, 1) % (unsigned) devices);
+	if (cudaSetDevice(lane->device) != cudaSuccess ||
+		cudaStreamCreateWithFlags(&lane->stream, cudaStreamNonBlocking) != cudaSuccess)
+		return NULL;
+	lane->ready = 1;
+	return lane;
+}
+
+/* Room for n results of one query on the device and in pinned memory. */
+static int
+LaneResults(Lane *lane, size_t n)
+{
+	size_t		dcap = lane->resultCap * sizeof(double);
+	size_t		icap = lane->resultCap * sizeof(int64_t);
+	size_t		hcap = lane->hostCap * sizeof(double);
+	size_t		hicap = lane->hostCap * sizeof(int64_t);
+	size_t		ccap = lane->resultCap ? 16 : 0;
+
+	if (n == 0)
+		n = 1;
+	if (n > lane->resultCap)
+	{
+		if (!Grow((void **) &lane->dist, &dcap, n * sizeof(double)) ||
+			!Grow((void **) &lane->id, &icap, n * sizeof(int64_t)) ||
+			!Grow((void **) &lane->count, &ccap, 16))
+			return 0;
+		lane->resultCap = n;
+	}
+	if (n > lane->hostCap)
+	{
+		if (!GrowHost((void **) &lane->hostDist, &hcap, n * sizeof(double)) ||
+			!GrowHost((void **) &lane->hostId, &hicap, n * sizeof(int64_t)))
+			return 0;
+		lane->hostCap = n;
+	}
+	return 1;
+}
+
+static int
+AllFinite(const float *v, size_t n)
+{
+	for (size_t i = 0; i < n; i++)
+		if (!isfinite(v[i]))
+			return 0;
+	return 1;
+}
+
+/*
+ * One gathered job (AnnGatheredExact semantics, ann/server/cpu.c:218-276):
+ * results hold every row within the gathered tolerance of the k-th distance,
+ * sorted by (distance, id).
+ */
+static void
+GatheredJob(AnnGatheredJob *job)
+{
+	Lane	   *lane;
+	size_t		values = (size_t) job->rows * job->dimensions;
+	uint32_t	count = 0;
+	double		qnorm = 0;
+	int			status;
+
+	job->nresults = 0;
+	if (job->dimensions == 0 || job->dimensions > ANN_MAX_DIM || job->metric > 2)
+	{
+		job->status = ANN_INVALID;
+		return;
+	}
+	if (!AllFinite(job->query, job->dimensions) || !AllFinite(job->vectors, values))
+	{
+		/* the reference rejects non-finite queries (cpu.c:97-99) and L2 rows
+		 * whose distance is not finite (cpu.c:246-251) */
+		job->status = ANN_INVALID;
+		return;
+	}
+	for (uint32_t d = 0; d < job->dimensions; d++)
+		qnorm += (double) job->query[d] * job->query[d];
+	if (job->metric == 2 && qnorm == 0)
+	{
+		job->status = ANN_INVALID;
+		return;
+	}
+	if (job->rows == 0 || job->k == 0)
+	{
+		job->status = ANN_OK;
+		return;
+	}
+	if (InjectLost())
+	{
+		job->status = ANN_BACKEND_ERROR;
+		return;
+	}
+	lane = LaneGet();
+	if (lane == NULL)
+	{
+		job->status = ANN_BACKEND_ERROR;
+		return;
+	}
+	if (!Grow(&lane->rows, &lane->rowsBytes, values * sizeof(float)) ||
+		!Grow((void **) &lane->query, &lane->queryBytes, job->dimensions * sizeof(float)) ||
+		!LaneResults(lane, job->rows))
+	{
+		job->status = ANN_NOMEM;
+		return;
+	}
+	if (cudaMemcpyAsync(lane->rows, job->vectors, values * sizeof(float), cudaMemcpyHostToDevice,
+						lane->stream) != cudaSuccess ||
+		cudaMemcpyAsync(lane->query, job->query, job->dimensions * sizeof(float), cudaMemcpyHostToDevice,
+						lane->stream) != cudaSuccess)
+	{
+		job->status = ANN_BACKEND_ERROR;
+		return;
+	}
+	if (lane->shard == NULL)
+		status = AnnB200ShardCreate(lane->device, ANNB200_F32, job->dimensions, job->rows, lane->rows,
+									NULL, NULL, 0, 0, lane->stream, &lane->shard);
+	else
+		status = AnnB200ShardAssign(lane->shard, ANNB200_F32, job->dimensions, job->rows, lane->rows,
+									NULL, NULL, 0, lane->stream);
+	if (status == ANN_OK)
+		status = AnnB200Search(lane->shard, lane->query, 1, NULL, 0, job->k, job->metric, ANNB200_WINDOW,
+							   job->rows, lane->dist, lane->id, lane->count, NULL, lane->stream);
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(&count, lane->count, sizeof(count), cudaMemcpyDeviceToHost, lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK && count &&
+		(cudaMemcpyAsync(lane->hostDist, lane->dist, count * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, count * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status != ANN_OK)
+	{
+		job->status = (AnnStatus) status;
+		return;
+	}
+	for (uint32_t i = 0; i < count; i++)
+	{
+		job->results[i].id = (uint32_t) lane->hostId[i];
+		job->results[i].distance = lane->hostDist[i];
+	}
+	job->nresults = count;
+	job->status = ANN_OK;
+	atomic_fetch_add(&DeviceJobs, 1);
+}
+
+static void
+SearchGathered(AnnGatheredJob *jobs, uint32_t count)
+{
+	for (uint32_t i = 0; i < count; i++)
+		GatheredJob(&jobs[i]);
+}
+
+static uint64_t
+DeviceJobCount(void)
+{
+	return (uint64_t) atomic_load(&DeviceJobs);
+}
+
+static void
+Destroy(AnnIndex *index)
+{
+	IndexState *state = index->backend_state;
+
+	if (state)
+	{
+		int			prev = 0;
+
+		cudaGetDevice(&prev);
+		cudaSetDevice(state->device);
+		AnnB200ShardDestroy(state->shard);
+		if (state->rows)
+			cudaFree(state->rows);
+		cudaSetDevice(prev);
+		free(state);
+	}
+	free(index->vectors);
+	memset(index, 0, sizeof(*index));
+}
+
+/* In-memory FP32 index, validated like the cpu backend's Build (cpu.c:19-44). */
+static AnnStatus
+Build(AnnIndex *index, uint64_t generation, uint32_t rows, uint32_t dimensions, const float *vectors)
+{
+	uint64_t	wide = (uint64_t) rows * dimensions;
+	size_t		count;
+	float	   *copy;
+	IndexState *state;
+	Lane	   *lane;
+
+	if (generation == 0 || dimensions == 0 || dimensions > ANN_MAX_DIM ||
+		wide > ANN_MAX_BYTES / sizeof(float) || (wide && vectors == NULL))
+		return ANN_INVALID;
+	count = (size_t) wide;
+	if (!AllFinite(vectors, count))
+		return ANN_INVALID;
+	lane = LaneGet();
+	if (lane == NULL)
+		return ANN_BACKEND_ERROR;
+	copy = malloc(count ? count * sizeof(float) : 1);
+	state = calloc(1, sizeof(*state));
+	if (copy == NULL || state == NULL)
+	{
+		free(copy);
+		free(state);
+		return ANN_NOMEM;
+	}
+	if (count)
+		memcpy(copy, vectors, count * sizeof(float));
+	state->device = lane->device;
+	if (count && (cudaMalloc(&state->rows, count * sizeof(float)) != cudaSuccess ||
+				  cudaMemcpy(state->rows, vectors, count * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess))
+	{
+		if (state->rows)
+			cudaFree(state->rows);
+		free(copy);
+		free(state);
+		return ANN_NOMEM;
+	}
+	if (rows && AnnB200ShardCreate(state->device, ANNB200_F32, dimensions, rows, state->rows, NULL, NULL, 0, 0,
+								   lane->stream, &state->shard) != ANN_OK)
+	{
+		cudaFree(state->rows);
+		free(copy);
+		free(state);
+		return ANN_BACKEND_ERROR;
+	}
+	Destroy(index);
+	index->vectors = copy;
+	index->rows = rows;
+	index->dimensions = dimensions;
+	index->generation = generation;
+	index->backend_state = state;
+	return ANN_OK;
+}
+
+/*
+ * The k best rows of an in-memory index by (distance, id), optionally among
+ * sorted unique ids (the cpu backend's Search, ann/server/cpu.c:82-154).
+ */
+static AnnStatus
+Search(const AnnIndex *index, const float *query, uint32_t metric, const uint32_t *ids, uint32_t nids,
+	   uint32_t k, AnnCandidate *results, uint32_t *nresults)
+{
+	IndexState *state = index->backend_state;
+	Lane	   *lane;
+	double		qnorm = 0;
+	uint32_t	count = 0;
+	int			status;
+
+	*nresults = 0;
+	if (metric > 2)
+		return ANN_UNSUPPORTED;
+	if (!AllFinite(query, index->dimensions))
+		return ANN_INVALID;
+	for (uint32_t d = 0; d < index->dimensions; d++)
+		qnorm += (double) query[d] * query[d];
+	if (metric == 2 && qnorm == 0)
+		return ANN_INVALID;
+	for (uint32_t i = 0; ids && i < nids; i++)
+		if (ids[i] >= index->rows || (i && ids[i] <= ids[i - 1]))
+			return ANN_INVALID;
+	if (k == 0 || index->rows == 0 || (ids && nids == 0) || state == NULL)
+		return ANN_OK;
+	if (InjectLost())
+		return ANN_BACKEND_ERROR;
+	lane = LaneGet();
+	if (lane == NULL)
+		return ANN_BACKEND_ERROR;
+	cudaSetDevice(state->device);
+	if (!Grow((void **) &lane->query, &lane->queryBytes, index->dimensions * sizeof(float)) ||
+		(ids && !Grow((void **) &lane->ids, &lane->idsBytes, (size_t) nids * sizeof(uint32_t))) ||
+		!LaneResults(lane, k))
+		return ANN_NOMEM;
+	if (cudaMemcpyAsync(lane->query, query, index->dimensions * sizeof(float), cudaMemcpyHostToDevice,
+						lane->stream) != cudaSuccess ||
+		(ids && cudaMemcpyAsync(lane->ids, ids, (size_t) nids * sizeof(uint32_t), cudaMemcpyHostToDevice,
+								lane->stream) != cudaSuccess))
+		return ANN_BACKEND_ERROR;
+	status = AnnB200Search(state->shard, lane->query, 1, ids ? lane->ids : NULL, ids ? nids : 0, k, metric, 0, k,
+						   lane->dist, lane->id, lane->count, NULL, lane->stream);
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(&count, lane->count, sizeof(count), cudaMemcpyDeviceToHost, lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK && count &&
+		(cudaMemcpyAsync(lane->hostDist, lane->dist, count * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, count * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status != ANN_OK)
+		return (AnnStatus) status;
+	for (uint32_t i = 0; i < count; i++)
+	{
+		results[i].id = (uint32_t) lane->hostId[i];
+		results[i].distance = lane->hostDist[i];
+	}
+	*nresults = count;
+	atomic_fetch_add(&DeviceJobs, 1);
+	return ANN_OK;
+}
+
+/*
+ * Why the device context is unusable, or NULL: a simulated loss, or a sticky
+ * CUDA error on this thread's device (the reference's cuVS check,
+ * ann/server/cuvs.c:8047-8080).
+ */
+static const char *
+Lost(void)
+{
+	static _Thread_local char reason[256];
+	cudaError_t e;
+
+	if (atomic_load(&LostSimulated))
+		return LostReason;
+	if (!LaneState.ready)
+		return NULL;
+	cudaSetDevice(LaneState.device);
+	e = cudaStreamSynchronize(LaneState.stream);
+	if (e == cudaSuccess || e == cudaErrorNotReady)
+		return NULL;
+	if (e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorIllegalInstruction ||
+		e == cudaErrorMisalignedAddress || e == cudaErrorHardwareStackError || e == cudaErrorInvalidPc ||
+		e == cudaErrorECCUncorrectable || e == cudaErrorAssert || e == cudaErrorInvalidAddressSpace ||
+		e == cudaErrorLaunchTimeout)
+	{
+		snprintf(reason, sizeof(reason), "GPU context lost: %s", cudaGetErrorString(e));
+		return reason;
+	}
+	return NULL;
+}
+
+const AnnBackend *
+AnnB200Backend(void)
+{
+	static const AnnBackend backend = {
+		"b200", 7, 7, "flat", "fp32", 1, 0, UINT32_MAX, Build, Search, Destroy,
+		SearchGathered, DeviceJobCount, NULL, NULL, Lost, NULL
+	};
+
+	return &backend;
+}

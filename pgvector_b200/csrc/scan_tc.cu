@@ -1,0 +1,378 @@
+// scan_tc.cu - tcgen05 tensor-core approximate scan of FP16 rows.
+//
+// Replaces the reference's grouped score-matrix scan, which stages up to 64
+// queries in shared memory and issues legacy warp-level mma.sync.m16n8k16
+// per 8-query tile (score_mma_half, ann/server/blackwell.c:289-525). Here one
+// persistent CTA per SM walks (128-row, BN-query) tiles, BN <= 256:
+//
+//   warps 0-3  producers: gather the tile's 128 candidate rows by id and the
+//              BN FP16 queries, 16 bytes a thread per cp.async, straight into
+//              the 128-byte-swizzled K-major layout tcgen05 reads, one
+//              64-dimension k-block per pipeline stage (4 stages).
+//   warp 4     one thread issues tcgen05.mma.cta_group::1.kind::f16
+//              (M=128, N=BN, K=16) into an FP32 accumulator in tensor memory,
+//              and tcgen05.commit frees each stage and publishes each tile.
+//   warps 5-8  epilogue: tcgen05.ld moves each row's BN scores to registers
+//              (warp w reads TMEM lanes 32*(w%4)..+31), applies the per-row
+//              affine map to the v-domain score and either stores it (sample
+//              matrix) or appends (v, row) when v passes the query's
+//              threshold. Two accumulators (2 x 256 columns) let the epilogue
+//              of tile t overlap the MMAs of tile t+1.
+//
+// Every wait is bounded (4 s of %globaltimer); a wait that runs out sets
+// FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are drained and
+// tensor memory is freed before the kernel returns.
+#include "internal.cuh"
+
+namespace annb200 {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int STAGES = 4;
+constexpr int MAXBN = 256;
+constexpr int A_BYTES = BM * 128;
+constexpr int B_BYTES = MAXBN * 128;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int LAG = STAGES - 1;   // cp.async groups a producer thread keeps in flight
+constexpr int NTHREADS = 288;
+constexpr int TMEM_COLS = 512;
+constexpr unsigned long long kWaitNs = 4000000000ull;
+
+struct TcArgs {
+  ScanArgs a;
+  const __half *q16;   // [qtiles * bn][kpad]
+  uint32_t kpad;       // halves per query row, multiple of 64
+  uint32_t kblocks;    // kpad / 64
+  uint32_t bn;         // queries per tile, multiple of 32, <= 256
+  uint32_t qtiles;
+  uint64_t rtiles;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase of `parity` to complete; false once the time limit
+// passes or another role has aborted.
+__device__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *flags) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    for (int i = 0; i < 32; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort = 1;
+      atomicOr(flags, FLAG_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte
+// swizzle layout: rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked
+// along M/N (stride byte offset 1024), start address advanced 32 bytes per
+// 16-element K step inside the atom.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu)   // start address
+         | ((uint64_t)1 << 16)                 // leading byte offset (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)       // stride byte offset
+         | ((uint64_t)1 << 46)                 // descriptor version (sm100)
+         | ((uint64_t)2 << 61);                // 128-byte swizzle
+}
+
+// Instruction descriptor: FP16 A and B, FP32 accumulator, both K-major.
+__device__ __forceinline__ uint32_t f16_idesc(uint32_t n) {
+  return (1u << 4)                  // D format F32
+         | ((n >> 3) << 17)         // N / 8
+         | ((uint32_t)(BM >> 4) << 24);  // M / 16
+}
+
+#define TMEM_LD32(taddr, r)                                                                          \
+  asm volatile(                                                                                      \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15," \
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                     \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),        \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),    \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), \
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), \
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                                         \
+      : "r"(taddr))
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile uint32_t *abort = tmem_slot + 1;
+  float *thr_s = reinterpret_cast<float *>(tmem_slot + 4);
+
+  const ScanArgs &a = t.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t ntiles = t.rtiles * t.qtiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full + s, 128);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (a.mode == MODE_FILTER)
+    for (uint32_t i = threadIdx.x; i < a.nq; i += NTHREADS) thr_s[i] = a.thr[i];
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ producers
+    const int pt = threadIdx.x;
+    const int prow = pt >> 3, pchunk = pt & 7;
+    const uint32_t swz = (uint32_t)(pchunk ^ (prow & 7)) << 4;  // (row & 7) == (prow & 7) for rows prow + 16j
+    uint64_t it = 0;
+    bool ok = true;
+    for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const uint64_t rt = tile / t.qtiles;
+      const uint32_t qt = (uint32_t)(tile % t.qtiles);
+      const uint8_t *asrc[8];
+      uint32_t abytes[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const uint64_t vi = rt * BM + j * 16 + prow;
+        if (vi < a.count) {
+          const uint64_t pos = a.base + vi * a.stride;
+          const uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
+          asrc[j] = a.s.codes + id * a.s.row_bytes + pchunk * 16;
+          abytes[j] = 16;
+        } else {
+          asrc[j] = a.s.codes;
+          abytes[j] = 0;
+        }
+      }
+      const __half *bsrc = t.q16 + (uint64_t)(qt * t.bn + prow) * t.kpad + pchunk * 8;
+      const uint32_t bgroups = t.bn / 16;
+      for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
+        const uint32_t s = (uint32_t)(it % STAGES);
+        const uint32_t ph = (uint32_t)((it / STAGES) & 1);
+        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t sb = sa + A_BYTES;
+        const bool kin = kb * 64 + pchunk * 8 < a.s.dims;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const uint32_t n = kin ? abytes[j] : 0;
+          const uint8_t *src = n ? asrc[j] + kb * 128 : a.s.codes;
+          cp_async16(sa + (uint32_t)(j * 16 + prow) * 128 + swz, src, n);
+        }
+        for (uint32_t j = 0; j < bgroups; j++)
+          cp_async16(sb + (j * 16 + prow) * 128 + swz, bsrc + (uint64_t)j * 16 * t.kpad + kb * 64, 16);
+        cp_commit();
+        if (it >= LAG) {
+          cp_wait<LAG>();
+          fence_proxy_async();
+          mbar_arrive(full + (uint32_t)((it - LAG) % STAGES));
+        }
+      }
+    }
+    cp_wait<0>();
+    fence_proxy_async();
+    for (uint64_t j = it > LAG ? it - LAG : 0; j < it; j++) mbar_arrive(full + (uint32_t)(j % STAGES));
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = f16_idesc(t.bn);
+      uint64_t it = 0, tc = 0;
+      bool ok = true;
+      for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
+        const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
+        if (!mbar_wait(tempty + ab, (use & 1) ^ 1, abort, a.flags)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * 256;
+        for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
+          const uint32_t s = (uint32_t)(it % STAGES);
+          const uint32_t ph = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(full + s, ph, abort, a.flags)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (uint32_t kk = 0; kk < 4; kk++)
+            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+          tc_commit(empty + s);
+        }
+        if (ok) tc_commit(tfull + ab);
+      }
+      // every MMA this thread issued has completed before tensor memory is freed
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitNs) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    uint64_t tc = 0;
+    for (uint64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, tc++) {
+      const uint64_t rt = tile / t.qtiles;
+      const uint32_t qt = (uint32_t)(tile % t.qtiles);
+      const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
+      bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint64_t vi = rt * BM + row;
+      const bool valid = vi < a.count;
+      const uint64_t pos = a.base + vi * a.stride;
+      float al = 0.0f, be = 0.0f;
+      if (valid) {
+        const uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
+        row_affine(a.s, id, a.metric, a.raw_scale, al, be);
+      }
+      const uint32_t taddr = tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16);
+      for (uint32_t c0 = 0; c0 < t.bn; c0 += 32) {
+        uint32_t r[32];
+        TMEM_LD32(taddr + c0, r);
+        tmem_ld_wait();
+        const uint32_t q0 = qt * t.bn + c0;
+        if (valid) {
+          if (a.mode == MODE_MATRIX) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (q0 + j < a.nq) a.mat[(uint64_t)(q0 + j) * a.mat_ld + vi] = fmaf(__uint_as_float(r[j]), al, be);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const float v = fmaf(__uint_as_float(r[j]), al, be);
+              if (q0 + j < a.nq && v <= thr_s[q0 + j]) append_candidate(a, v, pos, q0 + j);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + ab);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+// Shared memory the tensor scan needs for nq queries (thresholds included).
+size_t tc_scan_smem(uint32_t nq) {
+  return 1024 + (size_t)STAGES * STAGE_BYTES + 128 + (size_t)nq * sizeof(float);
+}
+
+// Largest query count one tensor-scan launch takes (thresholds in shared memory).
+uint32_t tc_scan_max_queries() { return 4096; }
+
+// Launch the tensor scan of a.count virtual rows against a.nq FP16 queries in
+// q16 ([qtiles*bn][kpad]). Returns a CUDA error from the launch.
+cudaError_t launch_tc_scan(const ScanArgs &a, const __half *q16, uint32_t kpad, uint32_t bn, int sms,
+                           cudaStream_t st) {
+  TcArgs t;
+  t.a = a;
+  t.q16 = q16;
+  t.kpad = kpad;
+  t.kblocks = kpad / 64;
+  t.bn = bn;
+  t.qtiles = (a.nq + bn - 1) / bn;
+  t.rtiles = (a.count + BM - 1) / BM;
+  if (a.count == 0 || a.nq == 0) return cudaSuccess;
+  const size_t smem = tc_scan_smem(a.nq);
+  cudaError_t e = cudaFuncSetAttribute(tc_scan_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const uint64_t ntiles = t.rtiles * t.qtiles;
+  const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
+  tc_scan_f16<<<grid, NTHREADS, smem, st>>>(t);
+  return cudaGetLastError();
+}
+
+}  // namespace annb200

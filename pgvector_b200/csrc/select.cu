@@ -1,0 +1,801 @@
+// select.cu - bounds, candidate pruning, exact rescoring and merging.
+//
+// Reference counterparts: the sampled-bound candidate lists of
+// AnnBlackwellCandidates (stride_rows / select32 / merge32 / fuse_mma,
+// ann/server/blackwell.c:1452-1548), the radix prune-select and final
+// rank/bucket kernels (prune_select_s, final_rank, final_bucket,
+// ann/server/cuvs.c:3882-4248), the FP64 rerank kernels (rerank8_*,
+// rerank_final_*, ann/server/cuvs.c:3912-3990,4149-4248), the host merge of
+// per-shard top-k lists (AnnIndexTreeMerge, ann/server/indexfile.c:3235-3258)
+// and bitmap expansion (expand_*, ann/server/cuvs.c:1910-1968).
+//
+// Exactness: candidates are rescored with the reference CPU worker's own
+// arithmetic on the rows decoded to FP32 (ann/server/cpu.c:82-175): L2 as
+// eight FP32 partial sums combined ((sum + (s0+s1)+(s2+s3)) + ((s4+s5)+(s6+s7)))
+// then a double square root; inner product and cosine as FP64 sums in
+// dimension order. Every operation is an explicit round-to-nearest intrinsic
+// so no multiply-add is fused, which makes each distance identical to the
+// CPU's bit for bit.
+#include "internal.cuh"
+
+namespace annb200 {
+
+namespace {
+
+constexpr int NT = 512;  // threads of the per-query selection kernels
+
+// ---------------------------------------------------------------- block helpers
+
+// Exclusive prefix sum of one value a thread over the block; *total gets the sum.
+__device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *scratch, uint32_t *total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) scratch[lane] = w;
+  }
+  __syncthreads();
+  uint32_t before = (warp ? scratch[warp - 1] : 0) + x - v;
+  *total = scratch[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+// k-th smallest (1-based) 32-bit key among n, keys from key_at(i): three
+// radix passes of 11, 11 and 10 bits with a shared histogram.
+template <typename KeyAt>
+__device__ uint32_t block_radix_select(KeyAt key_at, uint32_t n, uint32_t k, uint32_t *hist,
+                                       uint32_t *scratch) {
+  __shared__ uint32_t s_prefix, s_k;
+  uint32_t prefix = 0, mask = 0;
+  if (threadIdx.x == 0) s_k = k;
+  const int shifts[3] = {21, 10, 0};
+  const int widths[3] = {11, 11, 10};
+  __syncthreads();
+  for (int p = 0; p < 3; p++) {
+    const int shift = shifts[p], nb = 1 << widths[p];
+    const uint32_t want = s_k;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    if (threadIdx.x == 0) s_prefix = prefix;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      uint32_t key = key_at(i);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & (nb - 1)], 1u);
+    }
+    __syncthreads();
+    // each thread owns a contiguous run of bins
+    const int per = (nb + blockDim.x - 1) / blockDim.x;
+    const int b0 = threadIdx.x * per;
+    uint32_t local = 0;
+    for (int b = b0; b < b0 + per && b < nb; b++) local += hist[b];
+    uint32_t total;
+    uint32_t before = block_exclusive_scan(local, scratch, &total);
+    if (before < want && want <= before + local) {
+      uint32_t c = before;
+      for (int b = b0; b < b0 + per && b < nb; b++) {
+        if (c + hist[b] >= want) {
+          s_prefix = prefix | ((uint32_t)b << shift);
+          s_k = want - c;
+          break;
+        }
+        c += hist[b];
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    mask |= (uint32_t)(nb - 1) << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// ---------------------------------------------------------------- exact distances
+
+// The reference CPU worker's distance of one decoded row (see file header).
+template <int DT>
+__device__ double exact_distance(const ShardView &s, uint64_t id, const float *q, uint32_t metric,
+                                 double qn2d) {
+  const uint32_t dims = s.dims;
+  if (DT == DT_BIT) {
+    const uint8_t *row = s.codes + id * s.row_bytes;
+    const uint8_t *qb = reinterpret_cast<const uint8_t *>(q);
+    uint32_t d = 0;
+    uint64_t b = 0;
+    if ((s.row_bytes & 3) == 0)
+      for (; b < s.row_bytes; b += 4)
+        d += __popc(__ldg(reinterpret_cast<const uint32_t *>(row + b)) ^ *reinterpret_cast<const uint32_t *>(qb + b));
+    for (; b < s.row_bytes; b++) d += __popc((uint32_t)(__ldg(row + b) ^ qb[b]));
+    return (double)d;
+  } else {
+    if (metric == M_L2) {
+      float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      float tail = 0.0f;
+      uint32_t d = 0;
+      float v[8];
+      for (; d + 8 <= dims; d += 8) {
+        decode8<DT>(s, id, d, v);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float diff = __fsub_rn(v[j], q[d + j]);
+          sums[j] = __fadd_rn(sums[j], __fmul_rn(diff, diff));
+        }
+      }
+      if (d < dims) {
+        decode8<DT>(s, id, d, v);
+        for (int j = 0; d + j < dims; j++) {
+          float diff = __fsub_rn(v[j], q[d + j]);
+          tail = __fadd_rn(tail, __fmul_rn(diff, diff));
+        }
+      }
+      float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
+      float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
+      float total = __fadd_rn(__fadd_rn(tail, left), right);
+      return __dsqrt_rn((double)total);
+    }
+    double dot = 0.0, nrm = 0.0;
+    float v[8];
+    for (uint32_t d = 0; d < dims; d += 8) {
+      decode8<DT>(s, id, d, v);
+      for (int j = 0; j < 8 && d + j < dims; j++) {
+        double x = v[j], y = q[d + j];
+        dot = __dadd_rn(dot, __dmul_rn(x, y));
+        nrm = __dadd_rn(nrm, __dmul_rn(x, x));
+      }
+    }
+    if (metric == M_IP) return -dot;
+    double r = __ddiv_rn(dot, __dsqrt_rn(__dmul_rn(nrm, qn2d)));
+    return __dsub_rn(1.0, fmax(-1.0, fmin(1.0, r)));
+  }
+}
+
+__device__ double exact_any(const ShardView &s, uint64_t id, const float *q, uint32_t metric, double qn2d) {
+  switch (s.dtype) {
+    case DT_F32: return exact_distance<DT_F32>(s, id, q, metric, qn2d);
+    case DT_F16: return exact_distance<DT_F16>(s, id, q, metric, qn2d);
+    case DT_E4M3: return exact_distance<DT_E4M3>(s, id, q, metric, qn2d);
+    case DT_NVFP4: return exact_distance<DT_NVFP4>(s, id, q, metric, qn2d);
+    default: return exact_distance<DT_BIT>(s, id, q, metric, qn2d);
+  }
+}
+
+// ---------------------------------------------------------------- shard stats
+
+// Per row: FP64 squared norm of the decoded values -> n2 (FP32) and
+// rn = 1/sqrt(n2) (0 for a zero row); the largest n2 goes to *maxn2 (as
+// float bits, which order like integers for non-negative values).
+template <int DT>
+__global__ void shard_stats(ShardView s, float *n2, float *rn, uint32_t *maxn2) {
+  const uint64_t row = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= s.rows) return;
+  double acc = 0.0;
+  float v[8];
+  for (uint32_t d = lane * 8; d < s.dims; d += 256) {
+    decode8<DT>(s, row, d, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc += (double)v[j] * (double)v[j];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    float f = (float)acc;
+    n2[row] = f;
+    rn[row] = acc > 0.0 ? (float)(1.0 / sqrt(acc)) : 0.0f;
+    atomicMax(maxn2, __float_as_uint(f));
+  }
+}
+
+// ---------------------------------------------------------------- queries
+
+struct PrepArgs {
+  const float *queries;
+  uint32_t nq, dims, metric, kpad;
+  int use_q16;
+  double gamma;            // relative accumulation error of the approximate scan
+  const uint32_t *maxn2;   // shard's largest squared row norm (float bits)
+  QueryState qs;
+};
+
+// One block a query: validity, norms, the FP16 copy and the error bound
+// (distance domain; squared distance for L2) of the approximate score:
+//   |acc - dot| <= gamma*||x||*||q16|| + ||x||*||q - q16|| + FP32 epilogue
+// rounding, with ||x|| <= sqrt(maxn2); the L2 bound also covers the rounding
+// of the reference's own FP32 eight-lane sum.
+__global__ void prep_queries(PrepArgs p) {
+  const uint32_t q = blockIdx.x;
+  const float *qv = p.queries + (uint64_t)q * p.dims;
+  __shared__ double red[3][32];
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  double r2 = 0.0, t2 = 0.0, n2 = 0.0;
+  for (uint32_t d = threadIdx.x; d < p.kpad || d < p.dims; d += blockDim.x) {
+    float x = d < p.dims ? qv[d] : 0.0f;
+    if (d < p.dims && !isfinite(x)) bad = 1;
+    if (p.use_q16 && d < p.kpad) {
+      __half h = __float2half_rn(x);
+      p.qs.q16[(uint64_t)q * p.kpad + d] = h;
+      double hx = (double)__half2float(h);
+      t2 += hx * hx;
+      r2 += ((double)x - hx) * ((double)x - hx);
+    }
+    n2 += (double)x * (double)x;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    r2 += __shfl_xor_sync(0xffffffffu, r2, o);
+    t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+    n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+  }
+  if (lane == 0) {
+    red[0][warp] = r2;
+    red[1][warp] = t2;
+    red[2][warp] = n2;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  r2 = t2 = n2 = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+    r2 += red[0][w];
+    t2 += red[1][w];
+    n2 += red[2][w];
+  }
+  // the reference's query norm: FP64, dimension order (cpu.c:96-101)
+  double qn = 0.0;
+  for (uint32_t d = 0; d < p.dims; d++) qn = __dadd_rn(qn, __dmul_rn((double)qv[d], (double)qv[d]));
+  if (!p.use_q16) {
+    t2 = n2;
+    r2 = 0.0;
+  }
+  const double mx2 = (double)__uint_as_float(*p.maxn2);
+  const double mx = sqrt(mx2), qnorm = sqrt(n2), tnorm = sqrt(t2), rnorm = sqrt(r2);
+  const double eps = 1.0 / 1048576.0;  // 2^-20
+  double err;
+  switch (p.metric) {
+    case M_L2: {
+      double edot = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm;
+      double span = (mx + qnorm) * (mx + qnorm);
+      err = 2.0 * edot + eps * (mx2 + n2 + mx * qnorm) + ((double)p.dims / 8.0 + 8.0) * 1.2e-7 * span;
+      break;
+    }
+    case M_IP: err = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm; break;
+    case M_COS: err = qnorm > 0.0 ? p.gamma * tnorm / qnorm + rnorm / qnorm + 2.0 * eps : 0.0; break;
+    default: err = 0.0; break;
+  }
+  p.qs.err[q] = err * 1.0001 + 1e-30;
+  p.qs.qn2d[q] = qn;
+  p.qs.qn2[q] = (float)qn;
+  p.qs.rnq[q] = qn > 0.0 ? (float)(1.0 / sqrt(qn)) : 0.0f;
+  p.qs.status[q] = (bad || (p.metric == M_COS && qn == 0.0)) ? 1 : 0;
+}
+
+__global__ void prep_queries_bits(uint32_t nq, QueryState qs) {
+  uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  qs.err[q] = 0.0;
+  qs.qn2d[q] = 0.0;
+  qs.qn2[q] = 0.0f;
+  qs.rnq[q] = 0.0f;
+  qs.status[q] = 0;
+}
+
+// Threshold for queries without a sample bound: +inf (everything eligible).
+__global__ void fill_thresholds(uint32_t nq, QueryState qs) {
+  uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  qs.thr[q] = qs.status[q] ? __int_as_float(0x7fc00000) : __int_as_float(0x7f800000);
+}
+
+// ---------------------------------------------------------------- candidate rows
+
+__global__ void check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t *flags) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  uint32_t v = ids[i];
+  if (v >= rows || (i && v <= ids[i - 1])) atomicOr(flags, FLAG_BAD_ROWS);
+}
+
+// ---------------------------------------------------------------- sample bound
+
+struct BoundArgs {
+  const float *mat;
+  uint64_t ld, n;
+  uint32_t k, metric;
+  int window;
+  QueryState qs;
+};
+
+// Per query: the k-th smallest sampled v bounds the k-th exact distance;
+// thr = threshold_v of it (or +inf when the sample holds fewer than k rows).
+__global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t scratch[32];
+  const uint32_t q = blockIdx.x;
+  if (b.qs.status[q]) {
+    if (threadIdx.x == 0) b.qs.thr[q] = __int_as_float(0x7fc00000);
+    return;
+  }
+  const float *m = b.mat + (uint64_t)q * b.ld;
+  uint32_t key = 0xffffffffu;
+  if (b.n >= b.k)
+    key = block_radix_select([&](uint32_t i) { return float_key(m[i]); }, (uint32_t)b.n, b.k, hist, scratch);
+  if (threadIdx.x == 0) {
+    float v = key == 0xffffffffu ? __int_as_float(0x7f800000) : key_float(key);
+    double rnq = (double)b.qs.rnq[q], qn2 = b.qs.qn2d[q];
+    double D = v_to_dist(b.metric, (double)v, qn2, rnq);
+    if (v != v || isinf(v)) b.qs.thr[q] = __int_as_float(0x7f800000);
+    else b.qs.thr[q] = threshold_v(b.metric, D, b.qs.err[q], b.window, qn2, rnq);
+  }
+}
+
+// ---------------------------------------------------------------- tighten / finalize
+
+struct SelectArgs {
+  ShardView s;
+  const uint32_t *ids;
+  const float *queries;
+  uint32_t nq, k, metric;
+  int window;
+  uint32_t qbytes;        // bytes a query (Hamming) or 4*dims
+  QueryState qs;
+  uint32_t *cnt;
+  uint2 *cand;
+  uint32_t cap;
+  uint32_t *flags;        // [0] flags, [1] largest count, [2] largest survivor set
+  uint32_t *big;          // [nq] survivor count of queries left to the big sort
+  double *out_dist;
+  int64_t *out_id;
+  uint32_t *out_count;
+  uint32_t out_cap;
+  int64_t first_id;
+};
+
+// Lower a query's threshold with the k-th smallest v among its candidates and
+// drop the entries above it. Returns the survivor count (all threads).
+__device__ uint32_t tighten_one(const SelectArgs &a, uint32_t q, uint32_t c, uint32_t *hist, uint32_t *scratch,
+                                float *thr_out) {
+  __shared__ uint32_t s_m;
+  __shared__ float s_thr;
+  uint2 *e = a.cand + (uint64_t)q * a.cap;
+  float t = a.qs.thr[q];
+  if (c > a.k) {
+    uint32_t key = block_radix_select([&](uint32_t i) { return float_key(__uint_as_float(e[i].x)); }, c, a.k, hist,
+                                      scratch);
+    if (threadIdx.x == 0) {
+      double rnq = (double)a.qs.rnq[q], qn2 = a.qs.qn2d[q];
+      float v = key_float(key);
+      float t2 = threshold_v(a.metric, v_to_dist(a.metric, (double)v, qn2, rnq), a.qs.err[q], a.window, qn2, rnq);
+      s_thr = t2 < t ? t2 : t;
+    }
+    __syncthreads();
+    t = s_thr;
+  }
+  if (threadIdx.x == 0) s_m = 0;
+  __syncthreads();
+  for (uint32_t base = 0; base < c; base += blockDim.x) {
+    uint32_t i = base + threadIdx.x;
+    uint2 val = make_uint2(0, 0);
+    uint32_t keep = 0;
+    if (i < c) {
+      val = e[i];
+      keep = __uint_as_float(val.x) <= t;
+    }
+    uint32_t total;
+    uint32_t off = block_exclusive_scan(keep, scratch, &total);
+    const uint32_t m0 = s_m;
+    if (keep) e[m0 + off] = val;
+    __syncthreads();
+    if (threadIdx.x == 0) s_m = m0 + total;
+    __syncthreads();
+  }
+  *thr_out = t;
+  return s_m;
+}
+
+__global__ void __launch_bounds__(NT) tighten(SelectArgs a) {
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t scratch[32];
+  const uint32_t q = blockIdx.x;
+  if (a.qs.status[q]) return;
+  const uint32_t c = a.cnt[q];
+  if (c > a.cap || c <= a.k) return;
+  float t;
+  uint32_t m = tighten_one(a, q, c, hist, scratch, &t);
+  if (threadIdx.x == 0) {
+    a.cnt[q] = m;
+    a.qs.thr[q] = t;
+  }
+}
+
+// Sort n (key, pos) pairs in shared or global memory, ascending by key then
+// pos (bitonic network over the next power of two; entries past n are
+// padding with the largest key).
+__device__ void bitonic_sort(unsigned long long *key, uint32_t *pos, uint32_t p2) {
+  for (uint32_t size = 2; size <= p2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = threadIdx.x; i < p2 / 2; i += blockDim.x) {
+        uint32_t lo = 2 * i - (i & (stride - 1));
+        uint32_t hi = lo + stride;
+        bool up = (lo & size) == 0;
+        unsigned long long ka = key[lo], kb = key[hi];
+        uint32_t pa = pos[lo], pb = pos[hi];
+        bool greater = ka > kb || (ka == kb && pa > pb);
+        if (greater == up) {
+          key[lo] = kb;
+          key[hi] = ka;
+          pos[lo] = pb;
+          pos[hi] = pa;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Write a sorted survivor list: the k best, or the gathered window.
+__device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned long long *key, const uint32_t *pos,
+                              uint32_t m) {
+  __shared__ uint32_t s_n;
+  if (threadIdx.x == 0) {
+    uint32_t n = m < a.k ? m : a.k;
+    if (a.window && m > a.k) {
+      double c = widen(key_double(key[a.k - 1]));
+      unsigned long long ck = double_key(c);
+      uint32_t lo = a.k, hi = m;  // first index with key > ck
+      while (lo < hi) {
+        uint32_t mid = (lo + hi) / 2;
+        if (key[mid] <= ck) lo = mid + 1;
+        else hi = mid;
+      }
+      n = lo;
+    }
+    if (n > a.out_cap) {
+      n = a.out_cap;
+      if (a.window) atomicOr(a.flags, FLAG_OUT_CAP);
+    }
+    s_n = n;
+    a.out_count[q] = n;
+  }
+  __syncthreads();
+  const uint32_t n = s_n;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uint32_t p = pos[i];
+    uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
+    a.out_dist[(uint64_t)q * a.out_cap + i] = key_double(key[i]);
+    a.out_id[(uint64_t)q * a.out_cap + i] = a.first_id + (int64_t)id;
+  }
+}
+
+__global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
+  extern __shared__ uint8_t dyn[];
+  unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
+  uint32_t *pos = reinterpret_cast<uint32_t *>(key + kSortCap);
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t scratch[32];
+  const uint32_t q = blockIdx.x;
+  if (a.qs.status[q]) {
+    if (threadIdx.x == 0) a.out_count[q] = 0;
+    return;
+  }
+  const uint32_t c = a.cnt[q];
+  if (c > a.cap) {
+    if (threadIdx.x == 0) {
+      atomicOr(a.flags, FLAG_OVERFLOW);
+      atomicMax(a.flags + 1, c);
+      a.out_count[q] = 0;
+    }
+    return;
+  }
+  float t;
+  const uint32_t m = tighten_one(a, q, c, hist, scratch, &t);
+  if (m > (uint32_t)kSortCap) {
+    if (threadIdx.x == 0) {
+      a.cnt[q] = m;
+      a.big[q] = m;
+      atomicOr(a.flags, FLAG_BIGSORT);
+      atomicMax(a.flags + 2, m);
+      a.out_count[q] = 0;
+    }
+    return;
+  }
+  uint32_t p2 = 1;
+  while (p2 < m) p2 <<= 1;
+  const uint2 *e = a.cand + (uint64_t)q * a.cap;
+  const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
+                                                    (uint64_t)q * a.qbytes);
+  const double qn2d = a.qs.qn2d[q];
+  for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
+    if (i < m) {
+      uint32_t p = e[i].y;
+      uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
+      key[i] = double_key(exact_any(a.s, id, qv, a.metric, qn2d));
+      pos[i] = p;
+    } else {
+      key[i] = ~0ull;
+      pos[i] = ~0u;
+    }
+  }
+  __syncthreads();
+  bitonic_sort(key, pos, p2);
+  write_results(a, q, key, pos, m);
+}
+
+// The same for one query whose survivors outgrew shared memory: rescoring and
+// sorting in a global scratch of p2 (key, pos) pairs.
+__global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, unsigned long long *key, uint32_t *pos,
+                                                   uint32_t p2) {
+  const uint32_t m = a.big[q];
+  const uint2 *e = a.cand + (uint64_t)q * a.cap;
+  const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
+                                                    (uint64_t)q * a.qbytes);
+  const double qn2d = a.qs.qn2d[q];
+  for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
+    if (i < m) {
+      uint32_t p = e[i].y;
+      uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
+      key[i] = double_key(exact_any(a.s, id, qv, a.metric, qn2d));
+      pos[i] = p;
+    } else {
+      key[i] = ~0ull;
+      pos[i] = ~0u;
+    }
+  }
+  __syncthreads();
+  bitonic_sort(key, pos, p2);
+  write_results(a, q, key, pos, m);
+}
+
+// ---------------------------------------------------------------- merge
+
+struct MergeArgs {
+  const double *dist;
+  const int64_t *ids;
+  const uint32_t *counts;
+  uint32_t nlists, nq, list_cap, k;
+  int window;
+  uint32_t out_cap;
+  double *out_dist;
+  int64_t *out_id;
+  uint32_t *out_count;
+  uint32_t *flags;
+};
+
+// Per query: gather every list's entries, sort by (distance, id), keep the k
+// best (or the gathered window of the merged k-th distance).
+__global__ void __launch_bounds__(NT) merge_lists(MergeArgs a) {
+  extern __shared__ uint8_t dyn[];
+  unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
+  unsigned long long *idk = key + kSortCap;
+  __shared__ uint32_t s_off[65];
+  __shared__ uint32_t s_n;
+  const uint32_t q = blockIdx.x;
+  if (threadIdx.x == 0) {
+    uint32_t o = 0;
+    for (uint32_t l = 0; l < a.nlists; l++) {
+      s_off[l] = o;
+      uint32_t c = a.counts[(uint64_t)l * a.nq + q];
+      o += c < a.list_cap ? c : a.list_cap;
+    }
+    s_off[a.nlists] = o;
+  }
+  __syncthreads();
+  const uint32_t total = s_off[a.nlists];
+  uint32_t p2 = 1;
+  while (p2 < total) p2 <<= 1;
+  for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
+    if (i < total) {
+      uint32_t l = 0;
+      while (s_off[l + 1] <= i) l++;
+      uint64_t src = ((uint64_t)l * a.nq + q) * a.list_cap + (i - s_off[l]);
+      key[i] = double_key(a.dist[src]);
+      idk[i] = (unsigned long long)a.ids[src] ^ 0x8000000000000000ull;
+    } else {
+      key[i] = ~0ull;
+      idk[i] = ~0ull;
+    }
+  }
+  __syncthreads();
+  // bitonic on (key, id) pairs
+  for (uint32_t size = 2; size <= p2; size <<= 1)
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = threadIdx.x; i < p2 / 2; i += blockDim.x) {
+        uint32_t lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        bool up = (lo & size) == 0;
+        unsigned long long ka = key[lo], kb = key[hi], ia = idk[lo], ib = idk[hi];
+        bool greater = ka > kb || (ka == kb && ia > ib);
+        if (greater == up) {
+          key[lo] = kb;
+          key[hi] = ka;
+          idk[lo] = ib;
+          idk[hi] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  if (threadIdx.x == 0) {
+    uint32_t n = total < a.k ? total : a.k;
+    if (a.window && total > a.k) {
+      unsigned long long ck = double_key(widen(key_double(key[a.k - 1])));
+      uint32_t lo = a.k, hi = total;
+      while (lo < hi) {
+        uint32_t mid = (lo + hi) / 2;
+        if (key[mid] <= ck) lo = mid + 1;
+        else hi = mid;
+      }
+      n = lo;
+    }
+    if (n > a.out_cap) {
+      n = a.out_cap;
+      if (a.window) atomicOr(a.flags, FLAG_OUT_CAP);
+    }
+    s_n = n;
+    a.out_count[q] = n;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < s_n; i += blockDim.x) {
+    a.out_dist[(uint64_t)q * a.out_cap + i] = key_double(key[i]);
+    a.out_id[(uint64_t)q * a.out_cap + i] = (int64_t)(idk[i] ^ 0x8000000000000000ull);
+  }
+}
+
+// ---------------------------------------------------------------- bitmap rows
+
+constexpr int BM_WORDS = 1024;  // words a block of the bitmap kernels
+
+__global__ void bitmap_count(const uint32_t *words, uint64_t nwords, uint64_t nbits, uint32_t *blockcnt) {
+  __shared__ uint32_t scratch[32];
+  uint64_t w = (uint64_t)blockIdx.x * BM_WORDS + threadIdx.x;
+  uint32_t c = 0;
+  if (w < nwords) {
+    uint32_t x = words[w];
+    uint64_t b0 = w * 32;
+    if (b0 + 32 > nbits) x &= (nbits - b0 >= 32) ? 0xffffffffu : ((1u << (nbits - b0)) - 1u);
+    c = __popc(x);
+  }
+  uint32_t total;
+  block_exclusive_scan(c, scratch, &total);
+  if (threadIdx.x == 0) blockcnt[blockIdx.x] = total;
+}
+
+__global__ void bitmap_scan(uint32_t *blockcnt, uint32_t nblocks, unsigned long long *total_out) {
+  __shared__ uint32_t scratch[32];
+  __shared__ unsigned long long carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (uint32_t base = 0; base < nblocks; base += blockDim.x) {
+    uint32_t i = base + threadIdx.x;
+    uint32_t v = i < nblocks ? blockcnt[i] : 0;
+    uint32_t total;
+    uint32_t before = block_exclusive_scan(v, scratch, &total);
+    unsigned long long c = carry;
+    if (i < nblocks) blockcnt[i] = (uint32_t)(c + before);
+    __syncthreads();
+    if (threadIdx.x == 0) carry = c + total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total_out = carry;
+}
+
+__global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nbits, const uint32_t *blockoff,
+                             uint32_t *rows) {
+  __shared__ uint32_t scratch[32];
+  uint64_t w = (uint64_t)blockIdx.x * BM_WORDS + threadIdx.x;
+  uint32_t x = 0;
+  if (w < nwords) {
+    x = words[w];
+    uint64_t b0 = w * 32;
+    if (b0 + 32 > nbits) x &= (nbits - b0 >= 32) ? 0xffffffffu : ((1u << (nbits - b0)) - 1u);
+  }
+  uint32_t total;
+  uint32_t before = block_exclusive_scan(__popc(x), scratch, &total);
+  uint32_t o = blockoff[blockIdx.x] + before;
+  while (x) {
+    uint32_t b = __ffs(x) - 1;
+    rows[o++] = (uint32_t)(w * 32 + b);
+    x &= x - 1;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- launchers
+
+void launch_shard_stats(const ShardView &s, float *n2, float *rn, uint32_t *maxn2, cudaStream_t st) {
+  if (s.rows == 0 || s.dtype == DT_BIT) return;
+  dim3 grid((unsigned)((s.rows + 7) / 8));
+  switch (s.dtype) {
+    case DT_F32: shard_stats<DT_F32><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
+    case DT_F16: shard_stats<DT_F16><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
+    case DT_E4M3: shard_stats<DT_E4M3><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
+    case DT_NVFP4: shard_stats<DT_NVFP4><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
+  }
+}
+
+void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
+                         int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
+                         cudaStream_t st) {
+  if (bits) {
+    prep_queries_bits<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
+    return;
+  }
+  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, gamma, maxn2, qs};
+  prep_queries<<<nq, 256, 0, st>>>(p);
+}
+
+void launch_fill_thresholds(uint32_t nq, const QueryState &qs, cudaStream_t st) {
+  fill_thresholds<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
+}
+
+void launch_check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t *flags, cudaStream_t st) {
+  if (n) check_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, n, rows, flags);
+}
+
+void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, uint32_t k, uint32_t metric,
+                      int window, const QueryState &qs, cudaStream_t st) {
+  BoundArgs b{mat, ld, n, k, metric, window, qs};
+  kth_bound<<<nq, NT, 0, st>>>(b);
+}
+
+static SelectArgs to_args(const SelectLaunch &l) {
+  SelectArgs a{l.s,   l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
+               l.cnt, l.cand,  l.cap,     l.flags, l.big,    l.out_dist, l.out_id,    l.out_count, l.out_cap,
+               l.first_id};
+  return a;
+}
+
+void launch_tighten(const SelectLaunch &l, cudaStream_t st) { tighten<<<l.nq, NT, 0, st>>>(to_args(l)); }
+
+cudaError_t launch_finalize(const SelectLaunch &l, cudaStream_t st) {
+  const size_t smem = (size_t)kSortCap * (8 + 4);
+  cudaError_t e = cudaFuncSetAttribute(finalize, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  finalize<<<l.nq, NT, smem, st>>>(to_args(l));
+  return cudaGetLastError();
+}
+
+void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,
+                         cudaStream_t st) {
+  finalize_big<<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2);
+}
+
+cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,
+                         uint32_t nq, uint32_t list_cap, uint32_t k, int window, uint32_t out_cap,
+                         double *out_dist, int64_t *out_id, uint32_t *out_count, uint32_t *flags,
+                         cudaStream_t st) {
+  MergeArgs a{dist, ids, counts, nlists, nq, list_cap, k, window, out_cap, out_dist, out_id, out_count, flags};
+  const size_t smem = (size_t)kSortCap * 16;
+  cudaError_t e = cudaFuncSetAttribute(merge_lists, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  merge_lists<<<nq, NT, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+uint32_t bitmap_blocks(uint64_t nbits) {
+  uint64_t nwords = (nbits + 31) / 32;
+  return (uint32_t)((nwords + BM_WORDS - 1) / BM_WORDS);
+}
+
+void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,
+                        unsigned long long *total, cudaStream_t st) {
+  uint64_t nwords = (nbits + 31) / 32;
+  uint32_t nb = bitmap_blocks(nbits);
+  if (nb == 0) return;
+  bitmap_count<<<nb, BM_WORDS, 0, st>>>(words, nwords, nbits, blockcnt);
+  bitmap_scan<<<1, 1024, 0, st>>>(blockcnt, nb, total);
+  bitmap_write<<<nb, BM_WORDS, 0, st>>>(words, nwords, nbits, blockcnt, rows);
+}
+
+}  // namespace annb200

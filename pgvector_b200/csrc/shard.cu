@@ -1,0 +1,628 @@
+// shard.cu - host side of libannb200.so: shards, search orchestration, merge.
+//
+// One AnnB200Search call is the device half of the reference's SearchGather
+// (ann/server/cuvs.c:4585-4930) for one shard, with the host re-score and
+// CPU repair steps removed: selection, exact rescoring and ordering all run
+// on the device, and the only host decisions are buffer sizes (a candidate
+// list that overflows its capacity is grown and the chunk re-scanned).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/annb200.h"
+#include "internal.cuh"
+
+using namespace annb200;
+
+namespace {
+
+enum Status { OK = 0, INVALID = 1, UNSUPPORTED = 2, NOMEM = 4, BACKEND_ERROR = 5 };
+
+thread_local std::string g_error;
+
+int fail(int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(e == cudaErrorMemoryAllocation ? NOMEM : BACKEND_ERROR, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(expr, what)                            \
+  do {                                            \
+    cudaError_t e_ = (expr);                      \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// Grow-only device allocation.
+struct DeviceBuffer {
+  void *p = nullptr;
+  size_t n = 0;
+  ~DeviceBuffer() {
+    if (p) cudaFree(p);
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  cudaError_t reserve(size_t bytes) {
+    if (bytes <= n) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) n = bytes;
+    return e;
+  }
+};
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+uint64_t row_bytes_of(uint32_t dtype, uint32_t dims) {
+  switch (dtype) {
+    case DT_F32: return (uint64_t)dims * 4;
+    case DT_F16: return (uint64_t)dims * 2;
+    case DT_E4M3: return ((uint64_t)dims + 15) / 16 * 16;
+    case DT_NVFP4: return ((uint64_t)dims + 15) / 16 * 8;
+    case DT_BIT: return ((uint64_t)dims + 7) / 8;
+  }
+  return 0;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Carves one allocation into 256-byte-aligned pieces.
+struct Carver {
+  size_t off = 0;
+  template <typename T>
+  size_t take(size_t count) {
+    size_t o = off;
+    off = align256(off + count * sizeof(T));
+    return o;
+  }
+};
+
+// ---- launch counting and stage timing (ANN_B200_KERNEL_TIMING=1)
+std::atomic<unsigned long long> g_launches{0};
+enum Stage { ST_PREP, ST_SAMPLE, ST_BOUND, ST_FILTER, ST_TIGHTEN, ST_FINAL, ST_BITMAP, ST_MERGE, ST_COUNT };
+std::mutex g_stage_mu;
+double g_stage_ms[ST_COUNT];
+unsigned long long g_stage_calls[ST_COUNT];
+
+bool timing_on() {
+  static const int on = [] {
+    const char *v = getenv("ANN_B200_KERNEL_TIMING");
+    return v && *v && *v != '0';
+  }();
+  return on;
+}
+
+// CUDA events around stages of one call, on the call's stream; read after
+// the call's own final synchronisation.
+struct StageClock {
+  cudaStream_t st;
+  bool on;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> spans;
+  explicit StageClock(cudaStream_t s) : st(s), on(timing_on()) {}
+  int begin(int stage) {
+    if (!on) return -1;
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, st);
+    spans.push_back({stage, {a, b}});
+    return (int)spans.size() - 1;
+  }
+  void end(int h) {
+    if (h >= 0) cudaEventRecord(spans[h].second.second, st);
+  }
+  ~StageClock() {
+    if (!on) return;
+    std::lock_guard<std::mutex> lock(g_stage_mu);
+    for (auto &sp : spans) {
+      float ms = 0;
+      if (cudaEventSynchronize(sp.second.second) == cudaSuccess &&
+          cudaEventElapsedTime(&ms, sp.second.first, sp.second.second) == cudaSuccess) {
+        g_stage_ms[sp.first] += ms;
+        g_stage_calls[sp.first] += 1;
+      }
+      cudaEventDestroy(sp.second.first);
+      cudaEventDestroy(sp.second.second);
+    }
+  }
+};
+
+void counted(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
+constexpr uint64_t kSampleRows = 32768;    // sample size of the bound
+constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
+
+}  // namespace
+
+struct AnnB200Shard {
+  int device = 0;
+  int sms = 148;
+  ShardView view{};
+  int64_t first = 0;
+  void *owned[3] = {nullptr, nullptr, nullptr};
+  float *n2 = nullptr;
+  float *rn = nullptr;
+  uint32_t *maxn2 = nullptr;
+  uint64_t norm_rows = 0;     // capacity of n2 / rn
+  std::mutex mu;
+  DeviceBuffer ws;      // per-search scratch
+  DeviceBuffer cand;    // candidate lists
+  DeviceBuffer big;     // survivor sort scratch of the rare large case
+  uint32_t *hflags = nullptr;  // pinned: flags readback
+};
+
+extern "C" const char *AnnB200LastError(void) { return g_error.c_str(); }
+
+extern "C" int AnnB200DeviceCount(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+extern "C" void AnnB200ShardDestroy(AnnB200Shard *s) {
+  if (!s) return;
+  {
+    DeviceGuard g(s->device);
+    for (void *p : s->owned)
+      if (p) cudaFree(p);
+    if (s->n2) cudaFree(s->n2);
+    if (s->rn) cudaFree(s->rn);
+    if (s->maxn2) cudaFree(s->maxn2);
+    if (s->hflags) cudaFreeHost(s->hflags);
+    s->ws.release();
+    s->cand.release();
+    s->big.release();
+  }
+  delete s;
+}
+
+// Point shard s at rows stored on its device (owning nothing) or copy them
+// from the host (owned), and compute the per-row norms.
+static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t rows, const void *codes,
+                      const void *block_scales, const float *row_scales, int64_t first_id, bool host,
+                      cudaStream_t st) {
+  if (dtype > DT_BIT) return fail(INVALID, "unknown storage format %u", dtype);
+  if (dims == 0 || dims > (dtype == DT_BIT ? 65536u : 16000u)) return fail(INVALID, "dimensions %u out of range", dims);
+  if (rows > 0xffffffffull) return fail(INVALID, "a shard holds at most 2^32-1 rows");
+  if (rows && !codes) return fail(INVALID, "rows without codes");
+  if ((dtype == DT_E4M3 || dtype == DT_NVFP4) && rows && !row_scales) return fail(INVALID, "row scales missing");
+  if (dtype == DT_NVFP4 && rows && !block_scales) return fail(INVALID, "block scales missing");
+  if (!host && ((uintptr_t)codes & 15)) return fail(INVALID, "codes must be 16-byte aligned");
+  for (void *&p : s->owned)
+    if (p) {
+      cudaFree(p);
+      p = nullptr;
+    }
+  s->first = first_id;
+  ShardView &v = s->view;
+  v.dims = dims;
+  v.dtype = dtype;
+  v.rows = rows;
+  v.row_bytes = row_bytes_of(dtype, dims);
+  v.bblocks = (dims + 15) / 16;
+  const size_t code_bytes = rows * v.row_bytes;
+  const size_t bs_bytes = dtype == DT_NVFP4 ? rows * v.bblocks : 0;
+  const size_t rs_bytes = (dtype == DT_E4M3 || dtype == DT_NVFP4) ? rows * sizeof(float) : 0;
+  cudaError_t e = cudaSuccess;
+  if (host) {
+    const void *src[3] = {codes, block_scales, row_scales};
+    const size_t bytes[3] = {code_bytes, bs_bytes, rs_bytes};
+    for (int i = 0; i < 3 && e == cudaSuccess; i++) {
+      if (!bytes[i]) continue;
+      e = cudaMalloc(&s->owned[i], bytes[i]);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(s->owned[i], src[i], bytes[i], cudaMemcpyHostToDevice, st);
+    }
+    v.codes = (const uint8_t *)s->owned[0];
+    v.bscales = (const uint8_t *)s->owned[1];
+    v.rowscale = (const float *)s->owned[2];
+  } else {
+    v.codes = (const uint8_t *)codes;
+    v.bscales = (const uint8_t *)block_scales;
+    v.rowscale = row_scales;
+  }
+  if (e == cudaSuccess && dtype != DT_BIT && rows > s->norm_rows) {
+    if (s->n2) cudaFree(s->n2);
+    if (s->rn) cudaFree(s->rn);
+    s->n2 = s->rn = nullptr;
+    s->norm_rows = 0;
+    e = cudaMalloc(&s->n2, rows * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s->rn, rows * sizeof(float));
+    if (e == cudaSuccess) s->norm_rows = rows;
+  }
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->maxn2, 0, 16, st);
+  if (e == cudaSuccess) {
+    v.n2 = s->n2;
+    v.rn = s->rn;
+    launch_shard_stats(v, s->n2, s->rn, s->maxn2, st);
+    if (dtype != DT_BIT && rows) counted(1);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "shard upload");
+  return OK;
+}
+
+extern "C" int AnnB200ShardCreate(int device, uint32_t dtype, uint32_t dims, uint64_t rows, const void *codes,
+                                  const void *block_scales, const float *row_scales, int64_t first_id,
+                                  uint32_t flags, void *stream, AnnB200Shard **out) {
+  if (!out) return fail(INVALID, "shard output pointer is NULL");
+  *out = nullptr;
+  if (device < 0 || device >= AnnB200DeviceCount()) return fail(INVALID, "no CUDA device %d", device);
+  DeviceGuard g(device);
+  AnnB200Shard *s = new AnnB200Shard();
+  s->device = device;
+  cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, device);
+  cudaError_t e = cudaMalloc(&s->maxn2, 16);
+  if (e == cudaSuccess) e = cudaMallocHost(&s->hflags, 64);
+  if (e != cudaSuccess) {
+    int r = cuda_fail(e, "shard");
+    AnnB200ShardDestroy(s);
+    return r;
+  }
+  int r = shard_bind(s, dtype, dims, rows, codes, block_scales, row_scales, first_id, flags & ANNB200_SHARD_HOST,
+                     (cudaStream_t)stream);
+  if (r != OK) {
+    std::string keep = g_error;
+    AnnB200ShardDestroy(s);
+    g_error = keep;
+    return r;
+  }
+  *out = s;
+  return OK;
+}
+
+extern "C" int AnnB200ShardAssign(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t rows, const void *codes,
+                                  const void *block_scales, const float *row_scales, int64_t first_id,
+                                  void *stream) {
+  if (!s) return fail(INVALID, "shard is NULL");
+  DeviceGuard g(s->device);
+  std::lock_guard<std::mutex> lock(s->mu);
+  return shard_bind(s, dtype, dims, rows, codes, block_scales, row_scales, first_id, false, (cudaStream_t)stream);
+}
+
+namespace {
+
+// One search over queries [q0, q0+nq) (nq within one tensor-scan launch).
+int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows, uint64_t nrows,
+                 uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                 uint32_t *out_count, int32_t *status, cudaStream_t st, bool *any_invalid) {
+  const ShardView &v = sh->view;
+  const bool bits = v.dtype == DT_BIT;
+  const bool window = flags & ANNB200_WINDOW;
+  const uint64_t n = rows ? nrows : v.rows;
+  const bool tc = v.dtype == DT_F16 && !(flags & ANNB200_FORCE_SIMT) && v.dims % 8 == 0 && nq >= 16;
+  const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
+  const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
+  const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
+  const uint32_t nq_pad = qtiles * bn;
+  const double gamma = bits ? 0.0 : (tc ? (double)kpad : (double)v.dims) * std::ldexp(1.0, -22);
+  const bool sample = k > 0 && n > kNoSampleRows;
+  const uint64_t stride = sample ? std::max<uint64_t>(1, n / std::max<uint64_t>(kSampleRows, 8ull * k)) : 1;
+  const uint64_t S = sample ? n / stride : 0;
+
+  // ---- workspace
+  Carver c;
+  const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
+               o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
+               o_q16 = c.take<__half>((size_t)nq_pad * kpad), o_mat = c.take<float>((size_t)S * nq),
+               o_cnt = c.take<uint32_t>(nq), o_snap = c.take<uint32_t>(nq), o_flags = c.take<uint32_t>(16),
+               o_big = c.take<uint32_t>(nq);
+  CK(sh->ws.reserve(c.off), "workspace");
+  uint8_t *w = (uint8_t *)sh->ws.p;
+  QueryState qs;
+  qs.qn2 = (float *)(w + o_qn2);
+  qs.rnq = (float *)(w + o_rnq);
+  qs.qn2d = (double *)(w + o_qn2d);
+  qs.err = (double *)(w + o_err);
+  qs.thr = (float *)(w + o_thr);
+  qs.status = (int32_t *)(w + o_status);
+  qs.q16 = (__half *)(w + o_q16);
+  float *mat = (float *)(w + o_mat);
+  uint32_t *cnt = (uint32_t *)(w + o_cnt);
+  uint32_t *snap = (uint32_t *)(w + o_snap);
+  uint32_t *dflags = (uint32_t *)(w + o_flags);
+  uint32_t *big = (uint32_t *)(w + o_big);
+
+  uint32_t cap = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(n, 1), std::max<uint64_t>(kBaseCap, 8ull * k));
+  if (!sample) cap = (uint32_t)std::max<uint64_t>(n, 1);
+  CK(sh->cand.reserve((size_t)nq * cap * sizeof(uint2)), "candidate lists");
+
+  CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
+  CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
+  CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
+  if (tc && nq_pad > nq)
+    CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
+  StageClock clock(st);
+  if (rows) {
+    // the scans index rows by these ids: reject a bad list before any scan runs
+    launch_check_rows(rows, nrows, v.rows, dflags, st);
+    counted(1);
+    CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
+    CK(cudaStreamSynchronize(st), "row check");
+    if (sh->hflags[0] & FLAG_BAD_ROWS)
+      return fail(INVALID, "candidate rows must be increasing and < %llu", (unsigned long long)v.rows);
+  }
+  int h = clock.begin(ST_PREP);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, st);
+  clock.end(h);
+  counted(1);
+  CK(cudaGetLastError(), "query preparation");
+
+  ScanArgs a{};
+  a.s = v;
+  a.ids = rows;
+  a.queries = (const float *)queries;
+  a.nq = nq;
+  a.metric = metric;
+  a.raw_scale = 0;
+  a.thr = qs.thr;
+  a.cnt = cnt;
+  a.flags = dflags;
+
+  auto scan = [&](void) -> cudaError_t {
+    if (tc) return launch_tc_scan(a, qs.q16, kpad, bn, sh->sms, st);
+    launch_simt_scan(a, st);
+    return cudaGetLastError();
+  };
+
+  SelectLaunch sl{};
+  sl.s = v;
+  sl.ids = rows;
+  sl.queries = (const float *)queries;
+  sl.nq = nq;
+  sl.k = k;
+  sl.metric = metric;
+  sl.window = window;
+  sl.qbytes = bits ? (uint32_t)v.row_bytes : v.dims * 4;
+  sl.qs = qs;
+  sl.cnt = cnt;
+  sl.flags = dflags;
+  sl.big = big;
+  sl.out_dist = out_dist;
+  sl.out_id = out_id;
+  sl.out_count = out_count;
+  sl.out_cap = out_cap;
+  sl.first_id = sh->first;
+
+  if (k > 0 && n > 0) {
+    if (sample) {
+      a.mode = MODE_MATRIX;
+      a.count = S;
+      a.base = 0;
+      a.stride = stride;
+      a.mat = mat;
+      a.mat_ld = S;
+      h = clock.begin(ST_SAMPLE);
+      CK(scan(), "sample scan");
+      clock.end(h);
+      h = clock.begin(ST_BOUND);
+      launch_kth_bound(mat, S, S, nq, k, metric, window, qs, st);
+      clock.end(h);
+      counted(2);
+    } else {
+      launch_fill_thresholds(nq, qs, st);
+      counted(1);
+    }
+    CK(cudaGetLastError(), "bound");
+    // filter scan in chunks sized so a chunk appends about cap/4 entries a query
+    uint64_t seen = sample ? S : n, start = 0;
+    a.mode = MODE_FILTER;
+    a.stride = 1;
+    while (start < n) {
+      uint64_t len = n - start;
+      if (sample) {
+        double room = (double)seen * (double)cap / (4.0 * (double)k);
+        len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)room));
+      }
+      CK(cudaMemcpyAsync(snap, cnt, nq * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st), "snapshot");
+      for (;;) {
+        a.count = len;
+        a.base = start;
+        a.cand = (uint2 *)sh->cand.p;
+        a.cap = cap;
+        h = clock.begin(ST_FILTER);
+        CK(scan(), "filter scan");
+        clock.end(h);
+        counted(1);
+        CK(cudaMemcpyAsync(sh->hflags, dflags, 16, cudaMemcpyDeviceToHost, st), "flags");
+        CK(cudaStreamSynchronize(st), "filter scan");
+        if (sh->hflags[0] & FLAG_BAD_ROWS) return fail(INVALID, "candidate rows must be increasing and < %llu",
+                                                       (unsigned long long)v.rows);
+        if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
+        if (!(sh->hflags[0] & FLAG_OVERFLOW)) break;
+        // grow the lists (keeping entries of earlier chunks) and re-scan this chunk
+        uint64_t need = std::max<uint64_t>(sh->hflags[1], (uint64_t)cap * 2);
+        uint32_t ncap = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(n, 1), need + need / 4);
+        if (ncap <= cap) ncap = cap + 1;
+        DeviceBuffer fresh;
+        CK(fresh.reserve((size_t)nq * ncap * sizeof(uint2)), "candidate lists");
+        CK(cudaMemcpy2DAsync(fresh.p, (size_t)ncap * sizeof(uint2), sh->cand.p, (size_t)cap * sizeof(uint2),
+                             (size_t)cap * sizeof(uint2), nq, cudaMemcpyDeviceToDevice, st),
+           "grow lists");
+        CK(cudaStreamSynchronize(st), "grow lists");
+        std::swap(sh->cand.p, fresh.p);
+        std::swap(sh->cand.n, fresh.n);
+        cap = ncap;
+        CK(cudaMemcpyAsync(cnt, snap, nq * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st), "restore");
+        CK(cudaMemsetAsync(dflags, 0, 8, st), "memset");
+      }
+      seen += len;
+      start += len;
+      sl.cand = (uint2 *)sh->cand.p;
+      sl.cap = cap;
+      if (start < n) {
+        h = clock.begin(ST_TIGHTEN);
+        launch_tighten(sl, st);
+        clock.end(h);
+        counted(1);
+      }
+    }
+    sl.cand = (uint2 *)sh->cand.p;
+    sl.cap = cap;
+    h = clock.begin(ST_FINAL);
+    CK(launch_finalize(sl, st), "finalize");
+    clock.end(h);
+    counted(1);
+    CK(cudaMemcpyAsync(sh->hflags, dflags, 16, cudaMemcpyDeviceToHost, st), "flags");
+    CK(cudaStreamSynchronize(st), "finalize");
+    if (sh->hflags[0] & FLAG_BIGSORT) {
+      std::vector<uint32_t> hbig(nq);
+      CK(cudaMemcpy(hbig.data(), big, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost), "big list");
+      for (uint32_t q = 0; q < nq; q++) {
+        if (!hbig[q]) continue;
+        uint32_t p2 = 1;
+        while (p2 < hbig[q]) p2 <<= 1;
+        CK(sh->big.reserve((size_t)p2 * 12), "sort scratch");
+        launch_finalize_big(sl, q, (unsigned long long *)sh->big.p, (uint32_t *)((uint8_t *)sh->big.p + (size_t)p2 * 8),
+                            p2, st);
+        counted(1);
+        CK(cudaGetLastError(), "large sort");
+      }
+      CK(cudaStreamSynchronize(st), "large sort");
+    }
+    if (sh->hflags[0] & FLAG_OVERFLOW) return fail(BACKEND_ERROR, "candidate list overflow after finalize");
+    if (sh->hflags[0] & FLAG_OUT_CAP) return fail(INVALID, "window results exceed out_cap");
+  } else {
+    CK(cudaMemsetAsync(out_count, 0, nq * sizeof(uint32_t), st), "memset");
+  }
+  if (status) CK(cudaMemcpyAsync(status, qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToDevice, st), "status");
+  std::vector<int32_t> hs(nq);
+  CK(cudaMemcpyAsync(hs.data(), qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "status");
+  CK(cudaStreamSynchronize(st), "search");
+  for (uint32_t q = 0; q < nq; q++)
+    if (hs[q]) *any_invalid = true;
+  return OK;
+}
+
+}  // namespace
+
+extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows, uint64_t nrows,
+                             uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist,
+                             int64_t *out_id, uint32_t *out_count, int32_t *status, void *stream) {
+  if (!sh) return fail(INVALID, "shard is NULL");
+  const ShardView &v = sh->view;
+  if (v.dtype == DT_BIT ? metric != M_HAM : metric > M_COS)
+    return fail(UNSUPPORTED, "metric %u does not apply to storage format %u", metric, v.dtype);
+  if (nq == 0) return OK;
+  if (!queries || !out_dist || !out_id || !out_count) return fail(INVALID, "NULL query or result pointer");
+  if (!(flags & ANNB200_WINDOW) && out_cap < k) return fail(INVALID, "out_cap %u < k %u", out_cap, k);
+  if (rows && nrows > v.rows) return fail(INVALID, "more candidate rows than the shard holds");
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t block = tc_scan_max_queries();
+  const uint64_t qbytes = v.dtype == DT_BIT ? v.row_bytes : (uint64_t)v.dims * 4;
+  bool any_invalid = false;
+  for (uint32_t q0 = 0; q0 < nq; q0 += block) {
+    uint32_t m = std::min(block, nq - q0);
+    int r = search_block(sh, (const uint8_t *)queries + q0 * qbytes, m, rows, nrows, k, metric, flags, out_cap,
+                         out_dist + (uint64_t)q0 * out_cap, out_id + (uint64_t)q0 * out_cap, out_count + q0,
+                         status ? status + q0 : nullptr, st, &any_invalid);
+    if (r != OK) return r;
+  }
+  if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  return OK;
+}
+
+extern "C" int AnnB200MergeTopk(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,
+                                uint32_t nq, uint32_t list_cap, uint32_t k, uint32_t flags, uint32_t out_cap,
+                                double *out_dist, int64_t *out_id, uint32_t *out_count, void *stream) {
+  if (nq == 0) return OK;
+  if (!dist || !ids || !counts || !out_dist || !out_id || !out_count) return fail(INVALID, "NULL pointer");
+  if (nlists == 0 || nlists > 64 || (uint64_t)nlists * list_cap > (uint64_t)kSortCap)
+    return fail(UNSUPPORTED, "merge takes at most 64 lists and 4096 entries a query");
+  if (!(flags & ANNB200_WINDOW) && out_cap < k) return fail(INVALID, "out_cap %u < k %u", out_cap, k);
+  cudaStream_t st = (cudaStream_t)stream;
+  static thread_local DeviceBuffer fl;
+  CK(fl.reserve(64), "merge flags");
+  CK(cudaMemsetAsync(fl.p, 0, 16, st), "memset");
+  StageClock clock(st);
+  int h = clock.begin(ST_MERGE);
+  CK(launch_merge(dist, ids, counts, nlists, nq, list_cap, k, flags & ANNB200_WINDOW, out_cap, out_dist, out_id,
+                  out_count, (uint32_t *)fl.p, st),
+     "merge");
+  clock.end(h);
+  counted(1);
+  uint32_t hf = 0;
+  CK(cudaMemcpyAsync(&hf, fl.p, 4, cudaMemcpyDeviceToHost, st), "merge flags");
+  CK(cudaStreamSynchronize(st), "merge");
+  if (hf & FLAG_OUT_CAP) return fail(INVALID, "window results exceed out_cap");
+  return OK;
+}
+
+extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint64_t *count,
+                                 void *stream) {
+  if (!count) return fail(INVALID, "count pointer is NULL");
+  *count = 0;
+  if (nbits == 0) return OK;
+  if (!words || !rows) return fail(INVALID, "NULL pointer");
+  if (nbits > 0xffffffffull) return fail(INVALID, "bitmap longer than 2^32 rows");
+  cudaStream_t st = (cudaStream_t)stream;
+  static thread_local DeviceBuffer scratch;
+  const uint32_t nb = bitmap_blocks(nbits);
+  CK(scratch.reserve(align256((size_t)nb * 4) + 8), "bitmap scratch");
+  unsigned long long *total = (unsigned long long *)((uint8_t *)scratch.p + align256((size_t)nb * 4));
+  StageClock clock(st);
+  int h = clock.begin(ST_BITMAP);
+  launch_bitmap_rows(words, nbits, rows, (uint32_t *)scratch.p, total, st);
+  clock.end(h);
+  counted(3);
+  CK(cudaGetLastError(), "bitmap rows");
+  unsigned long long found = 0;
+  CK(cudaMemcpyAsync(&found, total, 8, cudaMemcpyDeviceToHost, st), "bitmap count");
+  CK(cudaStreamSynchronize(st), "bitmap rows");
+  *count = found;
+  return OK;
+}
+
+extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(); }
+
+extern "C" int AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset) {
+  std::lock_guard<std::mutex> lock(g_stage_mu);
+  for (uint32_t i = 0; i < n && i < ST_COUNT; i++) {
+    if (ms) ms[i] = g_stage_ms[i];
+    if (calls) calls[i] = g_stage_calls[i];
+  }
+  if (reset)
+    for (int i = 0; i < ST_COUNT; i++) {
+      g_stage_ms[i] = 0;
+      g_stage_calls[i] = 0;
+    }
+  return timing_on() ? ST_COUNT : 0;
+}

@@ -1,0 +1,111 @@
+"""Seeded synthetic corpora with the shapes and distributions of the benchmark
+configurations (no public dataset is named for this path, so generated data
+stands in for real embeddings):
+
+  config 1  fp32, d=128, 100-centre Gaussian mixture, centres ~N(0,1),
+            per-point noise sigma 0.1
+  config 2  halfvec, d=768, 1,000-centre mixture, unit-normalised, 10%
+            uniform row-filter bitmap
+  config 3  FP8-E4M3 + per-row scale absmax/448, d=1024, 4,096-centre mixture
+  config 4  NVFP4 (E2M1 + E4M3 block scale per 16 + row scale), d=768
+  config 5  1,024-bit rows: 65,536 Bernoulli(0.5) prototypes, 5% bit flips
+
+numpy functions make small host arrays (tests); torch functions generate
+full-size data directly on a GPU in chunks (bench).
+"""
+import numpy as np
+
+
+# ---------------------------------------------------------------- numpy (small)
+
+def mixture(n, d, centres, sigma=0.1, seed=0, normalize=False, dtype=np.float32):
+    rng = np.random.default_rng(seed)
+    c = rng.standard_normal((centres, d)).astype(np.float32)
+    lab = rng.integers(0, centres, n)
+    x = c[lab] + sigma * rng.standard_normal((n, d)).astype(np.float32)
+    if normalize:
+        x /= np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-30)
+    return x.astype(dtype)
+
+
+def mixture_queries(q, d, centres, sigma=0.1, seed=0, normalize=False):
+    """Queries drawn the same way as the corpus (same centres: same seed)."""
+    rng = np.random.default_rng(seed)
+    c = rng.standard_normal((centres, d)).astype(np.float32)
+    rng2 = np.random.default_rng(seed + 7919)
+    lab = rng2.integers(0, centres, q)
+    x = c[lab] + sigma * rng2.standard_normal((q, d)).astype(np.float32)
+    if normalize:
+        x /= np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-30)
+    return x.astype(np.float32)
+
+
+def to_half_bits(x):
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32).astype(np.float16)).view(np.uint16)
+
+
+def bit_rows(n, dims, prototypes, flip=0.05, seed=0):
+    rng = np.random.default_rng(seed)
+    nbytes = dims // 8
+    proto = rng.integers(0, 256, (prototypes, nbytes), dtype=np.uint8)
+    lab = rng.integers(0, prototypes, n)
+    flips = np.packbits(rng.random((n, dims)) < flip, axis=1, bitorder='little')
+    return proto[lab] ^ flips, proto
+
+
+def bitmap(n, selectivity, seed=0):
+    """u32 words, bit r of word r//32 set with probability selectivity."""
+    rng = np.random.default_rng(seed)
+    bits = rng.random(n) < selectivity
+    padded = np.zeros((n + 31) // 32 * 32, dtype=bool)
+    padded[:n] = bits
+    return np.packbits(padded, bitorder='little').view(np.uint32), np.nonzero(bits)[0].astype(np.uint32)
+
+
+# ---------------------------------------------------------------- torch (full size, on the GPU)
+
+def torch_mixture(n, d, centres, sigma=0.1, seed=0, normalize=False, dtype=None, device='cuda',
+                  chunk=1 << 20, out=None):
+    """Gaussian-mixture rows generated on the device in chunks; returns a
+    [n, d] tensor of `dtype` (float16 by default)."""
+    import torch
+    dtype = dtype or torch.float16
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    c = torch.randn((centres, d), generator=g, device=device, dtype=torch.float32)
+    x = out if out is not None else torch.empty((n, d), dtype=dtype, device=device)
+    for s in range(0, n, chunk):
+        m = min(chunk, n - s)
+        lab = torch.randint(0, centres, (m,), generator=g, device=device)
+        v = c[lab] + sigma * torch.randn((m, d), generator=g, device=device, dtype=torch.float32)
+        if normalize:
+            v /= v.norm(dim=1, keepdim=True).clamp_min(1e-30)
+        x[s:s + m] = v.to(dtype)
+    return x
+
+
+def torch_mixture_queries(q, d, centres, sigma=0.1, seed=0, normalize=False, device='cuda'):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    c = torch.randn((centres, d), generator=g, device=device, dtype=torch.float32)
+    g2 = torch.Generator(device=device)
+    g2.manual_seed(seed + 7919)
+    lab = torch.randint(0, centres, (q,), generator=g2, device=device)
+    v = c[lab] + sigma * torch.randn((q, d), generator=g2, device=device, dtype=torch.float32)
+    if normalize:
+        v /= v.norm(dim=1, keepdim=True).clamp_min(1e-30)
+    return v
+
+
+def torch_bitmap(n, selectivity, seed=0, device='cuda'):
+    """u32 bitmap words with each row's bit set with probability selectivity."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    nw = (n + 31) // 32
+    bits = (torch.rand((nw * 32,), generator=g, device=device) < selectivity)
+    bits[n:] = False
+    w = (bits.view(nw, 32).to(torch.int64) << torch.arange(32, device=device, dtype=torch.int64)).sum(dim=1)
+    # the same 32 bits as a signed int32 (two's complement)
+    return torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)

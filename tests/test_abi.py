@@ -1,0 +1,108 @@
+"""The C ABI library without a GPU: it loads, exports every symbol
+include/*.h declares, fills the backend vtable as the worker expects, and the
+host-side validation and fault-injection paths need no device."""
+import ctypes
+import os
+import re
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INCLUDE = os.path.join(ROOT, 'include')
+
+import pgvector_b200 as pb
+from pgvector_b200 import _abi
+from pgvector_b200._lib import SIGNATURES
+
+
+def declared_functions():
+    names = set()
+    for f in os.listdir(INCLUDE):
+        text = open(os.path.join(INCLUDE, f)).read()
+        text = re.sub(r'/\*.*?\*/', '', text, flags=re.S)
+        for m in re.finditer(r'\b(AnnB200\w+)\s*\(', text):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = pb.load()
+    names = declared_functions()
+    assert {'AnnB200Backend', 'AnnB200Search', 'AnnB200ShardCreate', 'AnnB200MergeTopk'} <= names
+    for name in names:
+        assert hasattr(lib, name), name
+    assert names <= set(SIGNATURES), names - set(SIGNATURES)
+    out = subprocess.run(['nm', '-D', '--defined-only', pb._lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r' T (AnnB200\w+)', out))
+    assert names <= exported
+
+
+def test_library_is_sm100a_and_not_linked_to_oracle():
+    out = subprocess.run(['ldd', pb._lib.LIB_PATH], capture_output=True, text=True).stdout
+    assert 'oracle' not in out and 'annref' not in out
+
+
+def test_backend_vtable_matches_worker_layout():
+    b = pb.backend()
+    assert b.name == b'b200'
+    assert b.metrics == 7 and b.filters == 7
+    assert b.exact == 1 and b.max_k == 0xffffffff
+    assert b.algorithm == b'flat' and b.storage == b'fp32'
+    assert b.device_jobs and b.lost
+    assert not b.load_index and not b.search_index and not b.scan_preferred
+    # positional layout: 17 slots, pointers after the 8 scalar fields
+    assert ctypes.sizeof(_abi.AnnBackend) == 8 * 3 + 4 * 2 + 4 + 4 * 2 + 8 * 9 + 4
+
+
+def test_gathered_job_struct_layout():
+    # AnnCandidate {u32 id; f64 distance} is 16 bytes; AnnGatheredJob 48
+    assert ctypes.sizeof(_abi.AnnCandidate) == 16
+    assert ctypes.sizeof(_abi.AnnGatheredJob) == 48
+
+
+def test_invalid_gathered_jobs_rejected_on_host():
+    q = np.zeros(2, np.float32)
+    v = np.ones((3, 2), np.float32)
+    res = pb.search_gathered([
+        (q, v, 1, 3),                                  # metric beyond 2
+        (np.array([np.nan, 0], np.float32), v, 1, 0),  # non-finite query
+        (q, np.array([[np.inf, 0]], np.float32), 1, 0),
+        (q, v, 1, 2),                                  # zero query under cosine
+        (q, v, 0, 0),                                  # k = 0: no results, OK
+        (q, np.zeros((0, 2), np.float32), 5, 0),       # no rows: OK
+    ])
+    assert [s for s, _ in res] == [1, 1, 1, 1, 0, 0]
+    assert all(not r for _, r in res)
+
+
+def test_device_count_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip('a GPU is visible')
+    assert pb.device_count() == 0
+
+
+LOST_SCRIPT = r'''
+import os, sys, ctypes
+import numpy as np
+sys.path.insert(0, %r)
+import pgvector_b200 as pb
+res = pb.search_gathered([(np.ones(2, np.float32), np.ones((4, 2), np.float32), 1, 0)])
+lost = ctypes.CFUNCTYPE(ctypes.c_char_p)(pb.backend().lost)()
+print(res[0][0], lost.decode())
+'''
+
+
+def test_simulated_device_loss_reported_without_a_gpu():
+    # the mock-GPU style injection (ann/server/mockgpu.c:148-200): the
+    # worker would exit 70 on this lost() reason
+    env = dict(os.environ, ANN_B200_LOST_AFTER='0')
+    out = subprocess.run([sys.executable, '-c', LOST_SCRIPT % ROOT], capture_output=True, text=True, env=env,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr
+    status, reason = out.stdout.strip().split(' ', 1)
+    assert int(status) == pb.BACKEND_ERROR
+    assert 'GPU context lost (simulated' in reason

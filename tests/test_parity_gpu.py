@@ -1,0 +1,249 @@
+"""GPU parity: libannb200 through its C ABI against the CPU oracle.
+
+Bar: bit-exact. Result ids, counts and FP64 distances must equal the
+oracle's exactly (the oracle itself equals the reference worker bit for bit,
+tests/test_oracle.py), for every storage format, metric, candidate-set form
+and selection mode, on both scan paths (tcgen05 tensor cores and CUDA cores).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from pgvector_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(a, cuda):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).to(cuda)
+
+
+def gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, rs=None, window=False,
+               force_simt=False, cap=None):
+    import pgvector_b200 as pb
+    shard = pb.Shard(dtype, dims, to_dev(codes, cuda), None if bs is None else to_dev(bs, cuda),
+                     None if rs is None else to_dev(rs, cuda))
+    d, i, c = shard.search(to_dev(queries, cuda), k, metric, rows=None if ids is None else to_dev(ids, cuda),
+                           window=window, force_simt=force_simt, out_cap=cap)
+    return d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy()
+
+
+def assert_same(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, rs=None, window=False,
+                force_simt=False):
+    n = codes.shape[0] if ids is None else len(ids)
+    cap = max(n, 1) if window else max(k, 1)
+    od, oi, oc, os_ = oracle.search(dtype, dims, codes, queries, k, metric, ids=ids, block_scales=bs,
+                                    row_scales=rs, window=window, cap=cap)
+    assert (os_ == 0).all()
+    gd, gi, gc = gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids, bs, rs, window, force_simt, cap)
+    assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
+    for q in range(queries.shape[0]):
+        c = int(oc[q])
+        assert np.array_equal(gi[q, :c], oi[q, :c]), (q, gi[q, :c][:10], oi[q, :c][:10])
+        assert np.array_equal(gd[q, :c], od[q, :c]), (q, gd[q, :c][:10], od[q, :c][:10])
+    return oc
+
+
+# ---------------------------------------------------------------- fp32 (config 1 shape)
+
+@pytest.mark.parametrize('metric', [0, 1, 2])
+def test_f32_small_all_metrics(cuda, metric):
+    x = synth.mixture(5000, 37, 20, seed=1)
+    q = synth.mixture_queries(40, 37, 20, seed=1)
+    assert_same(cuda, oracle.F32, 37, x, q, 10, metric)
+
+
+def test_f32_config1_shape_sampled(cuda):
+    # config 1: 100-centre mixture, d=128, k=10 (fewer queries to keep the oracle quick)
+    x = synth.mixture(100000, 128, 100, seed=2)
+    q = synth.mixture_queries(64, 128, 100, seed=2)
+    assert_same(cuda, oracle.F32, 128, x, q, 10, 0)
+
+
+def test_f32_row_list_and_window(cuda):
+    x = synth.mixture(60000, 64, 50, seed=3)
+    q = synth.mixture_queries(24, 64, 50, seed=3)
+    _, ids = synth.bitmap(60000, 0.6, seed=3)
+    assert_same(cuda, oracle.F32, 64, x, q, 25, 0, ids=ids)
+    assert_same(cuda, oracle.F32, 64, x, q, 25, 0, ids=ids, window=True)
+    assert_same(cuda, oracle.F32, 64, x, q, 25, 2, ids=ids, window=True)
+
+
+# ---------------------------------------------------------------- fp16 / halfvec (config 2 shape)
+
+@pytest.mark.parametrize('metric', [2, 0, 1])
+def test_f16_tensor_path(cuda, metric):
+    x = synth.mixture(40000, 768, 100, seed=4, normalize=True)
+    h = synth.to_half_bits(x)
+    q = synth.mixture_queries(300, 768, 100, seed=4, normalize=True).astype(np.float16).astype(np.float32)
+    _, ids = synth.bitmap(40000, 0.9, seed=4)
+    assert_same(cuda, oracle.F16, 768, h, q, 100, metric, ids=ids)
+
+
+def test_f16_simt_path_matches(cuda):
+    x = synth.mixture(20000, 96, 30, seed=5, normalize=True)
+    h = synth.to_half_bits(x)
+    q = synth.mixture_queries(50, 96, 30, seed=5, normalize=True)
+    assert_same(cuda, oracle.F16, 96, h, q, 20, 2, force_simt=True)
+    assert_same(cuda, oracle.F16, 96, h, q, 20, 2)
+
+
+def test_f16_fp32_queries_and_odd_dims(cuda):
+    # FP32 queries over FP16 rows (query rounding covered by the bound), and
+    # dims not a multiple of 64 (zero-filled K tail in the tensor scan)
+    x = synth.mixture(35000, 200, 40, seed=6)
+    h = synth.to_half_bits(x)
+    q = synth.mixture_queries(40, 200, 40, seed=6)
+    assert_same(cuda, oracle.F16, 200, h, q, 30, 0)
+    x = synth.mixture(3000, 13, 10, seed=6)
+    assert_same(cuda, oracle.F16, 13, synth.to_half_bits(x), synth.mixture_queries(20, 13, 10, seed=6), 5, 2)
+
+
+# ---------------------------------------------------------------- FP8 / NVFP4 / bits
+
+def test_fp8_inner_product(cuda):
+    x = synth.mixture(36000, 256, 64, seed=7)
+    codes, scale = oracle.quantize_fp8(x)
+    q = synth.mixture_queries(32, 256, 64, seed=7)
+    assert_same(cuda, oracle.E4M3, 256, codes, q, 50, 1, rs=scale)
+    assert_same(cuda, oracle.E4M3, 256, codes, q, 50, 0, rs=scale)
+
+
+def test_nvfp4_l2_and_cosine(cuda):
+    x = synth.mixture(36000, 768, 64, seed=8)
+    packed, sc, row = oracle.quantize_nvfp4(x)
+    q = synth.mixture_queries(16, 768, 64, seed=8)
+    assert_same(cuda, oracle.NVFP4, 768, packed, q, 100, 0, bs=sc, rs=row)
+    assert_same(cuda, oracle.NVFP4, 768, packed, q, 10, 2, bs=sc, rs=row)
+
+
+def test_hamming_bit_exact_with_ties(cuda):
+    rows, proto = synth.bit_rows(60000, 1024, 256, flip=0.05, seed=9)
+    rng = np.random.default_rng(9)
+    qs = proto[rng.integers(0, 256, 48)] ^ np.packbits(rng.random((48, 1024)) < 0.05, axis=1, bitorder='little')
+    assert_same(cuda, oracle.BIT, 1024, rows, qs, 100, 3)
+    assert_same(cuda, oracle.BIT, 1024, rows[:500], qs[:4], 7, 3)
+
+
+# ---------------------------------------------------------------- edge cases
+
+def test_edge_k_values(cuda):
+    x = synth.mixture(1000, 16, 5, seed=10)
+    q = synth.mixture_queries(8, 16, 5, seed=10)
+    assert_same(cuda, oracle.F32, 16, x, q, 1000, 0)       # k = n
+    assert_same(cuda, oracle.F32, 16, x, q, 5000, 1)       # k > n
+    assert_same(cuda, oracle.F32, 16, x, q, 1, 2)
+    gd, gi, gc = gpu_search(cuda, oracle.F32, 16, x, q, 0, 0)
+    assert (gc == 0).all()
+    gd, gi, gc = gpu_search(cuda, oracle.F32, 16, x, q, 5, 0, ids=np.zeros(0, np.uint32))
+    assert (gc == 0).all()
+
+
+def test_heavy_ties_window(cuda):
+    # test_server.py:213-219 shape: 3000 identical rows must all come back
+    v = np.array([[1.0, 0.0]] * 3000 + [[5.0, 5.0]] * 100, dtype=np.float32)
+    assert_same(cuda, oracle.F32, 2, v, np.zeros((1, 2), np.float32), 5, 0, window=True)
+
+
+def test_overflow_regrowth_and_large_sort(cuda):
+    # 20,000 equal rows inside a 60,000-row shard: the window keeps all of
+    # them, more than the initial candidate capacity and the shared-memory sort
+    x = synth.mixture(60000, 32, 10, seed=11)
+    x[1000:21000] = x[5]
+    q = x[5:6] + 0.001
+    c = assert_same(cuda, oracle.F32, 32, x, q, 10, 0, window=True)
+    assert c[0] >= 20000
+    assert_same(cuda, oracle.F32, 32, x, q, 10, 0)
+
+
+def test_invalid_row_list_rejected(cuda):
+    import pgvector_b200 as pb
+    x = synth.mixture(100, 8, 3, seed=12)
+    with pytest.raises(pb.AnnB200Error) as e:
+        gpu_search(cuda, oracle.F32, 8, x, x[:2], 3, 0, ids=np.array([5, 3, 9], np.uint32))
+    assert e.value.status == pb.INVALID
+
+
+# ---------------------------------------------------------------- merge, bitmap, backend
+
+def test_merge_of_shards_equals_whole_search(cuda):
+    import torch
+    import pgvector_b200 as pb
+    x = synth.mixture(80000, 64, 40, seed=13)
+    q = synth.mixture_queries(32, 64, 40, seed=13)
+    k = 50
+    parts = np.array_split(np.arange(80000), 4)
+    ds, is_, cs = [], [], []
+    for p in parts:
+        shard = pb.Shard(pb.F32, 64, to_dev(x[p[0]:p[-1] + 1], cuda), first_id=int(p[0]))
+        d, i, c = shard.search(to_dev(q, cuda), k, 0)
+        ds.append(d), is_.append(i), cs.append(c)
+    md, mi, mc = pb.merge_topk(torch.stack(ds), torch.stack(is_), torch.stack(cs), k)
+    od, oi, oc, _ = oracle.search(oracle.F32, 64, x, q, k, 0)
+    assert np.array_equal(mi.cpu().numpy(), oi) and np.array_equal(md.cpu().numpy(), od)
+
+
+def test_bitmap_rows(cuda):
+    import pgvector_b200 as pb
+    for n, sel in ((1, 1.0), (33, 0.5), (100003, 0.1), (3 * 32768 + 5, 0.7)):
+        words, ids = synth.bitmap(n, sel, seed=n)
+        got = pb.bitmap_rows(to_dev(words, cuda), n).cpu().numpy().view(np.uint32)
+        assert np.array_equal(got, ids)
+
+
+def test_backend_gathered_jobs_match_reference(cuda):
+    import pgvector_b200 as pb
+    rng = np.random.default_rng(11)
+    jobs = []
+    for r in range(12):
+        dims = int(rng.choice([3, 16, 96]))
+        rows = int(rng.integers(2048, 5000))
+        v = np.round(rng.uniform(-2, 2, (rows, dims)), 2).astype(np.float32)
+        qv = np.round(rng.uniform(-2, 2, dims), 2).astype(np.float32)
+        jobs.append((qv, v, int(rng.choice([1, 10, 100, 400])), r % 3))
+    got = pb.search_gathered(jobs)
+    for (qv, v, k, metric), (status, res) in zip(jobs, got):
+        d, i, c, s = oracle.search(oracle.F32, qv.shape[0], v, qv[None], k, metric, window=True)
+        assert status == s[0] == 0
+        assert [r[0] for r in res] == list(i[0, :c[0]])
+        assert [r[1] for r in res] == list(d[0, :c[0]])
+        if oracle.ref_available():
+            rs, rres = oracle.ref_gathered_exact(qv, v, k, metric)
+            assert rres == res and rs == status
+    # boundary ties (test_server.py:189-195)
+    st, res = pb.search_gathered([(np.zeros(2, np.float32),
+                                   np.array([[1, 0], [0, 1], [-1, 0], [0, -1], [3, 3]], np.float32), 1, 0)])[0]
+    assert st == 0 and sorted(r[0] for r in res) == [0, 1, 2, 3]
+    jobs_done = pb.backend().device_jobs
+    import ctypes
+    assert ctypes.CFUNCTYPE(ctypes.c_uint64)(jobs_done)() >= 13
+
+
+def test_backend_in_memory_index(cuda):
+    import ctypes
+    import pgvector_b200 as pb
+    from pgvector_b200 import _abi
+    b = pb.backend()
+    rng = np.random.default_rng(42)
+    vectors = np.array([[rng.integers(-5, 6) for _ in range(7)] for _ in range(80)], dtype=np.float32)
+    index = _abi.AnnIndex()
+    assert b.build(ctypes.byref(index), 1, 80, 7, vectors.ctypes.data_as(ctypes.POINTER(ctypes.c_float))) == 0
+    query = np.array([1, 2, 3, 4, 5, 1, 2], dtype=np.float32)
+    ids = np.array(sorted(rng.choice(80, 25, replace=False)), dtype=np.uint32)
+    for metric in range(3):
+        for k in (1, 7, 100):
+            res = (_abi.AnnCandidate * 100)()
+            n = ctypes.c_uint32()
+            st = b.search(ctypes.byref(index), query.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), metric,
+                          ids.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), len(ids), k, res, ctypes.byref(n))
+            d, i, c, s = oracle.search(oracle.F32, 7, vectors, query[None], k, metric, ids=ids)
+            assert st == 0 and n.value == c[0]
+            assert [res[j].id for j in range(n.value)] == list(i[0, :c[0]])
+            assert [res[j].distance for j in range(n.value)] == list(d[0, :c[0]])
+    b.destroy(ctypes.byref(index))
