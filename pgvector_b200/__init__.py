@@ -90,6 +90,9 @@ class Shard:
         ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
         count = torch.empty((nq,), dtype=torch.int32, device=dev)
         flags = (WINDOW if window else 0) | (FORCE_SIMT if force_simt else 0)
+        if rows is not None and rows.numel() == 0:
+            # an empty list is a non-NULL pointer with no entries (NULL means every row)
+            rows = torch.zeros((1,), dtype=torch.int32, device=dev)
         check(load().AnnB200Search(self._handle, _ptr(queries), nq, _ptr(rows), nrows if rows is not None else 0,
                                    int(k), int(metric), flags, cap, _ptr(dist), _ptr(ids), _ptr(count),
                                    _ptr(status), _stream(stream)))

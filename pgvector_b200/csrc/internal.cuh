@@ -17,6 +17,7 @@
 // that bound their error, so the result equals the exact scan bit for bit.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -299,8 +300,8 @@ struct SelectLaunch {
 
 // ---------------------------------------------------------------- launchers
 void launch_simt_scan(const ScanArgs &a, cudaStream_t st);
-cudaError_t launch_tc_scan(const ScanArgs &a, const __half *q16, uint32_t kpad, uint32_t bn, int sms,
-                           cudaStream_t st);
+cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, const CUtensorMap &query_map,
+                           uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);
 size_t tc_scan_smem(uint32_t nq);
 uint32_t tc_scan_max_queries();
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, uint32_t *maxn2, cudaStream_t st);

@@ -5,14 +5,18 @@
 // per 8-query tile (score_mma_half, ann/server/blackwell.c:289-525). Here one
 // persistent CTA per SM walks (128-row, BN-query) tiles, BN <= 256:
 //
-//   warps 0-3  producers: gather the tile's 128 candidate rows by id and the
-//              BN FP16 queries, 16 bytes a thread per cp.async, straight into
-//              the 128-byte-swizzled K-major layout tcgen05 reads, one
-//              64-dimension k-block per pipeline stage (4 stages).
-//   warp 4     one thread issues tcgen05.mma.cta_group::1.kind::f16
+//   warp 0     TMA producer: per 64-dimension k-block (one pipeline stage of
+//              4), each lane issues one cp.async.bulk.tensor tile::gather4
+//              that gathers 4 of the tile's 128 candidate rows (128 bytes
+//              each) by row id, and lane 0 one tiled load of the BN x 64
+//              FP16 query block; both land in the 128-byte-swizzled K-major
+//              layout tcgen05 reads and complete on the stage's mbarrier.
+//              Row ids of the next tile are fetched while the current one
+//              streams.
+//   warp 1     one thread issues tcgen05.mma.cta_group::1.kind::f16
 //              (M=128, N=BN, K=16) into an FP32 accumulator in tensor memory,
 //              and tcgen05.commit frees each stage and publishes each tile.
-//   warps 5-8  epilogue: tcgen05.ld moves each row's BN scores to registers
+//   warps 2-5  epilogue: tcgen05.ld moves each row's BN scores to registers
 //              (warp w reads TMEM lanes 32*(w%4)..+31), applies the per-row
 //              affine map to the v-domain score and either stores it (sample
 //              matrix) or appends (v, row) when v passes the query's
@@ -22,6 +26,8 @@
 // Every wait is bounded (4 s of %globaltimer); a wait that runs out sets
 // FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are drained and
 // tensor memory is freed before the kernel returns.
+#include <cuda.h>
+
 #include "internal.cuh"
 
 namespace annb200 {
@@ -34,14 +40,13 @@ constexpr int MAXBN = 256;
 constexpr int A_BYTES = BM * 128;
 constexpr int B_BYTES = MAXBN * 128;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int LAG = STAGES - 1;   // cp.async groups a producer thread keeps in flight
-constexpr int NTHREADS = 288;
+constexpr int NTHREADS = 192;
+constexpr int EPI_BUF = 256;      // staged appends a warp buffers before a flush
 constexpr int TMEM_COLS = 512;
 constexpr unsigned long long kWaitNs = 4000000000ull;
 
 struct TcArgs {
   ScanArgs a;
-  const __half *q16;   // [qtiles * bn][kpad]
   uint32_t kpad;       // halves per query row, multiple of 64
   uint32_t kblocks;    // kpad / 64
   uint32_t bn;         // queries per tile, multiple of 32, <= 256
@@ -91,16 +96,30 @@ __device__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abo
   }
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+// Four rows (row coordinates r0..r3) x 64 FP16 columns from column x of the
+// row tensor, 128 bytes a row, swizzled, into dst; completes on bar.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t r0, int32_t r1,
+                                            int32_t r2, int32_t r3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+// A (box rows) x 64 tile at (x, y) of a 2-D tensor into dst; completes on bar.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -155,7 +174,9 @@ __device__ __forceinline__ uint32_t f16_idesc(uint32_t n) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tc_scan_f16(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
+                const TcArgs t) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
@@ -165,7 +186,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile uint32_t *abort = tmem_slot + 1;
-  float *thr_s = reinterpret_cast<float *>(tmem_slot + 4);
+  uint4 *stage_buf = reinterpret_cast<uint4 *>(smem + STAGES * STAGE_BYTES + 128);  // 4 warps x EPI_BUF
+  float *thr_s = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);
 
   const ScanArgs &a = t.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -173,7 +195,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
-      mbar_init(full + s, 128);
+      mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -184,9 +206,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // query slots past nq (padding of the last query tile) get NaN: never pass
   if (a.mode == MODE_FILTER)
-    for (uint32_t i = threadIdx.x; i < a.nq; i += NTHREADS) thr_s[i] = a.thr[i];
-  if (warp == 4) {
+    for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += NTHREADS)
+      thr_s[i] = i < a.nq ? a.thr[i] : __int_as_float(0x7fc00000);
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -197,33 +221,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 4) {
-    // ------------------------------------------------------------ producers
-    const int pt = threadIdx.x;
-    const int prow = pt >> 3, pchunk = pt & 7;
-    const uint32_t swz = (uint32_t)(pchunk ^ (prow & 7)) << 4;  // (row & 7) == (prow & 7) for rows prow + 16j
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    // lane g gathers tile rows 4g..4g+3; invalid slots (past the candidate
+    // list) re-read a valid row and are ignored by the epilogue
+    auto tile_ids = [&](uint64_t tile, int32_t (&r)[4]) {
+      const uint64_t rt = tile / t.qtiles;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        uint64_t vi = rt * BM + lane * 4 + i;
+        if (vi >= a.count) vi = a.count - 1;
+        const uint64_t pos = a.base + vi * a.stride;
+        r[i] = (int32_t)(a.ids ? (uint64_t)__ldg(a.ids + pos) : pos);
+      }
+    };
+    const uint32_t tx_bytes = (uint32_t)A_BYTES + t.bn * 128u;
     uint64_t it = 0;
     bool ok = true;
+    int32_t cur[4], nxt[4];
+    if (blockIdx.x < ntiles) tile_ids(blockIdx.x, cur);
     for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const uint64_t rt = tile / t.qtiles;
       const uint32_t qt = (uint32_t)(tile % t.qtiles);
-      const uint8_t *asrc[8];
-      uint32_t abytes[8];
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const uint64_t vi = rt * BM + j * 16 + prow;
-        if (vi < a.count) {
-          const uint64_t pos = a.base + vi * a.stride;
-          const uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
-          asrc[j] = a.s.codes + id * a.s.row_bytes + pchunk * 16;
-          abytes[j] = 16;
-        } else {
-          asrc[j] = a.s.codes;
-          abytes[j] = 0;
-        }
-      }
-      const __half *bsrc = t.q16 + (uint64_t)(qt * t.bn + prow) * t.kpad + pchunk * 8;
-      const uint32_t bgroups = t.bn / 16;
+      if (tile + gridDim.x < ntiles) tile_ids(tile + gridDim.x, nxt);
       for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
         const uint32_t s = (uint32_t)(it % STAGES);
         const uint32_t ph = (uint32_t)((it / STAGES) & 1);
@@ -233,28 +252,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
           break;
         }
         const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t sb = sa + A_BYTES;
-        const bool kin = kb * 64 + pchunk * 8 < a.s.dims;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const uint32_t n = kin ? abytes[j] : 0;
-          const uint8_t *src = n ? asrc[j] + kb * 128 : a.s.codes;
-          cp_async16(sa + (uint32_t)(j * 16 + prow) * 128 + swz, src, n);
-        }
-        for (uint32_t j = 0; j < bgroups; j++)
-          cp_async16(sb + (j * 16 + prow) * 128 + swz, bsrc + (uint64_t)j * 16 * t.kpad + kb * 64, 16);
-        cp_commit();
-        if (it >= LAG) {
-          cp_wait<LAG>();
-          fence_proxy_async();
-          mbar_arrive(full + (uint32_t)((it - LAG) % STAGES));
-        }
+        if (lane == 0) mbar_expect_tx(full + s, tx_bytes);
+        __syncwarp();
+        tma_gather4(sa + lane * 512, &rows_map, (int32_t)(kb * 64), cur[0], cur[1], cur[2], cur[3], full + s);
+        if (lane == 0) tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), full + s);
       }
+#pragma unroll
+      for (int i = 0; i < 4; i++) cur[i] = nxt[i];
     }
-    cp_wait<0>();
-    fence_proxy_async();
-    for (uint64_t j = it > LAG ? it - LAG : 0; j < it; j++) mbar_arrive(full + (uint32_t)(j % STAGES));
-  } else if (warp == 4) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = f16_idesc(t.bn);
@@ -291,8 +297,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    // Passing (query, v, position) triples are staged in this warp's shared
+    // buffer (warp-uniform slot arithmetic, no atomics) and flushed to the
+    // global lists with every lane's atomics issued back to back, so a flush
+    // costs one memory round trip rather than one per passing score.
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
+    uint4 *buf = stage_buf + (warp - 2) * EPI_BUF;
+    uint32_t nbuf = 0;
+    auto flush = [&]() {
+      __syncwarp();
+      uint32_t slot[EPI_BUF / 32];
+#pragma unroll
+      for (int u = 0; u < EPI_BUF / 32; u++) {
+        const uint32_t i = u * 32 + lane;
+        if (i < nbuf) slot[u] = atomicAdd(a.cnt + buf[i].x, 1u);
+      }
+#pragma unroll
+      for (int u = 0; u < EPI_BUF / 32; u++) {
+        const uint32_t i = u * 32 + lane;
+        if (i < nbuf) {
+          const uint4 e = buf[i];
+          if (slot[u] < a.cap) a.cand[(uint64_t)e.x * a.cap + slot[u]] = make_uint2(e.y, e.z);
+          else {
+            atomicOr(a.flags, FLAG_OVERFLOW);
+            atomicMax(a.flags + 1, slot[u] + 1);
+          }
+        }
+      }
+      __syncwarp();
+      nbuf = 0;
+    };
     uint64_t tc = 0;
     for (uint64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, tc++) {
       const uint64_t rt = tile / t.qtiles;
@@ -304,7 +339,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
       const uint64_t vi = rt * BM + row;
       const bool valid = vi < a.count;
       const uint64_t pos = a.base + vi * a.stride;
-      float al = 0.0f, be = 0.0f;
+      float al = 0.0f, be = __int_as_float(0x7fc00000);  // invalid rows score NaN: never pass
       if (valid) {
         const uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
         row_affine(a.s, id, a.metric, a.raw_scale, al, be);
@@ -315,16 +350,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
         TMEM_LD32(taddr + c0, r);
         tmem_ld_wait();
         const uint32_t q0 = qt * t.bn + c0;
-        if (valid) {
-          if (a.mode == MODE_MATRIX) {
+        if (a.mode == MODE_MATRIX) {
+          if (valid) {
 #pragma unroll
             for (int j = 0; j < 32; j++)
               if (q0 + j < a.nq) a.mat[(uint64_t)(q0 + j) * a.mat_ld + vi] = fmaf(__uint_as_float(r[j]), al, be);
-          } else {
+          }
+        } else {
+          const float4 *tq = reinterpret_cast<const float4 *>(thr_s + q0);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
+          for (int j4 = 0; j4 < 8; j4++) {
+            const float4 t4 = tq[j4];
+            const float th[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+              const int j = j4 * 4 + jj;
               const float v = fmaf(__uint_as_float(r[j]), al, be);
-              if (q0 + j < a.nq && v <= thr_s[q0 + j]) append_candidate(a, v, pos, q0 + j);
+              const bool pass = v <= th[jj];
+              const uint32_t ballot = __ballot_sync(0xffffffffu, pass);
+              if (ballot) {
+                if (nbuf + 32 > (uint32_t)EPI_BUF) flush();
+                if (pass)
+                  buf[nbuf + __popc(ballot & ((1u << lane) - 1u))] =
+                      make_uint4(q0 + j, __float_as_uint(v), (uint32_t)pos, 0u);
+                nbuf += __popc(ballot);
+              }
             }
           }
         }
@@ -332,11 +382,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
       tc_fence_before();
       mbar_arrive(tempty + ab);
     }
+    __syncwarp();
+    if (a.mode == MODE_FILTER && nbuf) flush();
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
@@ -347,19 +399,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_scan_f16(const TcArgs t) {
 
 // Shared memory the tensor scan needs for nq queries (thresholds included).
 size_t tc_scan_smem(uint32_t nq) {
-  return 1024 + (size_t)STAGES * STAGE_BYTES + 128 + (size_t)nq * sizeof(float);
+  return 1024 + (size_t)STAGES * STAGE_BYTES + 128 + 4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) *
+                                                                                     sizeof(float);
 }
 
 // Largest query count one tensor-scan launch takes (thresholds in shared memory).
 uint32_t tc_scan_max_queries() { return 4096; }
 
-// Launch the tensor scan of a.count virtual rows against a.nq FP16 queries in
-// q16 ([qtiles*bn][kpad]). Returns a CUDA error from the launch.
-cudaError_t launch_tc_scan(const ScanArgs &a, const __half *q16, uint32_t kpad, uint32_t bn, int sms,
-                           cudaStream_t st) {
+// Launch the tensor scan of a.count virtual rows against a.nq FP16 queries:
+// rows_map describes the shard's rows ([rows][dims] FP16, box 64 x 1,
+// 128-byte swizzle), query_map the FP16 queries ([qtiles*bn][kpad], box
+// 64 x bn). Returns a CUDA error from the launch.
+cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, const CUtensorMap &query_map,
+                           uint32_t kpad, uint32_t bn, int sms, cudaStream_t st) {
   TcArgs t;
   t.a = a;
-  t.q16 = q16;
   t.kpad = kpad;
   t.kblocks = kpad / 64;
   t.bn = bn;
@@ -371,7 +425,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const __half *q16, uint32_t kpad, 
   if (e != cudaSuccess) return e;
   const uint64_t ntiles = t.rtiles * t.qtiles;
   const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
-  tc_scan_f16<<<grid, NTHREADS, smem, st>>>(t);
+  tc_scan_f16<<<grid, NTHREADS, smem, st>>>(rows_map, query_map, t);
   return cudaGetLastError();
 }
 

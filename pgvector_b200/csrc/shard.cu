@@ -5,6 +5,8 @@
 // CPU repair steps removed: selection, exact rescoring and ordering all run
 // on the device, and the only host decisions are buffer sizes (a candidate
 // list that overflows its capacity is grown and the chunk re-scanned).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -161,6 +163,34 @@ struct StageClock {
 
 void counted(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// 2-D FP16 tensor [outer][inner] (row pitch in bytes) read in boxes of
+// box_rows x 64 elements with the 128-byte swizzle tcgen05 operands use.
+bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                    uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
 constexpr uint64_t kSampleRows = 32768;    // sample size of the bound
 constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
@@ -182,6 +212,8 @@ struct AnnB200Shard {
   DeviceBuffer cand;    // candidate lists
   DeviceBuffer big;     // survivor sort scratch of the rare large case
   uint32_t *hflags = nullptr;  // pinned: flags readback
+  CUtensorMap rows_map;        // FP16 rows for the tensor scan's gather
+  bool rows_map_ok = false;
 };
 
 extern "C" const char *AnnB200LastError(void) { return g_error.c_str(); }
@@ -275,6 +307,9 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "shard upload");
+  // the tensor scan gathers 128-byte row pieces by TMA (row pitch a multiple of 16 bytes)
+  s->rows_map_ok = dtype == DT_F16 && dims % 8 == 0 && rows > 0 && rows < (1ull << 31) &&
+                   encode_f16_map(&s->rows_map, v.codes, dims, rows, v.row_bytes, 1);
   return OK;
 }
 
@@ -326,7 +361,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const bool bits = v.dtype == DT_BIT;
   const bool window = flags & ANNB200_WINDOW;
   const uint64_t n = rows ? nrows : v.rows;
-  const bool tc = v.dtype == DT_F16 && !(flags & ANNB200_FORCE_SIMT) && v.dims % 8 == 0 && nq >= 16;
+  const bool tc = v.dtype == DT_F16 && sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
   const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
@@ -395,8 +430,11 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.cnt = cnt;
   a.flags = dflags;
 
+  CUtensorMap query_map;
+  if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+    return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   auto scan = [&](void) -> cudaError_t {
-    if (tc) return launch_tc_scan(a, qs.q16, kpad, bn, sh->sms, st);
+    if (tc) return launch_tc_scan(a, sh->rows_map, query_map, kpad, bn, sh->sms, st);
     launch_simt_scan(a, st);
     return cudaGetLastError();
   };

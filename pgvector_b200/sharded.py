@@ -1,0 +1,57 @@
+"""Row-sharded search across ranks (one process per GPU).
+
+The reference spreads an index over GPUs as contiguous row-range shards and
+tree-merges the per-shard top-k lists on the host (shard placement
+ann/server/cuvs.c:2845-2862, AnnIndexTreeMerge
+ann/server/indexfile.c:3235-3258). Here each rank owns one contiguous range,
+searches it on its GPU, and the per-rank lists are combined by one NCCL
+all-gather followed by the on-device merge (AnnB200MergeTopk) -- the only
+collective on the path.
+"""
+
+
+def shard_bounds(rows, world, align=32):
+    """Row boundaries of `world` contiguous shards; inner boundaries are
+    multiples of `align` so each shard's slice of a u32 filter bitmap starts
+    on a word."""
+    b = [(rows * r // world) // align * align for r in range(world)] + [rows]
+    return b
+
+
+def bitmap_slice(words, lo, hi):
+    """The words covering rows [lo, hi) (lo a multiple of 32) and the bit count."""
+    return words[lo // 32:(hi + 31) // 32], hi - lo
+
+
+def gather_lists(dist_t, ids_t, count_t, group=None):
+    """All-gather every rank's [nq][k] results into [world][nq][k] tensors
+    (rank-major, the layout AnnB200MergeTopk takes)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    out = []
+    for t in (dist_t, ids_t, count_t):
+        t = t.contiguous()
+        if dist.get_backend(group) == 'nccl':
+            buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(buf, t, group=group)
+        else:
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t, group=group)
+            buf = torch.stack(parts)
+        out.append(buf)
+    return out
+
+
+def search_sharded(shard, queries, k, metric, rows, group=None, merge=None):
+    """Search this rank's shard and merge all ranks' results; every rank
+    returns the merged (dist, id, count). `merge` defaults to the device
+    merge; `rows` is this rank's candidate list (or None for all rows)."""
+    import torch.distributed as dist
+    d, i, c = shard.search(queries, k, metric, rows=rows)
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return d, i, c
+    gd, gi, gc = gather_lists(d, i, c, group)
+    if merge is None:
+        from . import merge_topk as merge
+    return merge(gd, gi, gc, k)

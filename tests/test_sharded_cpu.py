@@ -1,0 +1,97 @@
+"""The multi-GPU path's host logic on CPU: two gloo ranks shard a corpus by
+row range, search their shard (the CPU oracle stands in for the GPU scan),
+all-gather the per-rank lists in the layout the device merge takes, merge,
+and must equal one search over the whole corpus."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+from pgvector_b200 import sharded, synth
+
+ROWS, DIMS, NQ, K = 5000, 24, 6, 40
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(('127.0.0.1', 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+class OracleShard:
+    """Stand-in for pgvector_b200.Shard on a CPU rank: same search contract
+    (global ids = first_id + row, [nq][k] tensors)."""
+
+    def __init__(self, x, first_id):
+        self.x, self.first = x, first_id
+
+    def search(self, queries, k, metric, rows=None):
+        ids = None if rows is None else rows.numpy().view(np.uint32)
+        d, i, c, s = oracle.search(oracle.F32, DIMS, self.x, queries.numpy(), k, metric, ids=ids, threads=1)
+        i = np.where(i >= 0, i + self.first, -1)
+        return torch.from_numpy(d), torch.from_numpy(i), torch.from_numpy(c.astype(np.int32))
+
+
+def merge_host(gd, gi, gc, k):
+    """Sorted union of the gathered lists by (distance, id): the device
+    merge's contract, in numpy."""
+    world, nq, cap = gd.shape
+    od = np.full((nq, k), np.inf)
+    oi = np.full((nq, k), -1, dtype=np.int64)
+    oc = np.zeros(nq, dtype=np.int32)
+    for q in range(nq):
+        entries = sorted((float(gd[r, q, j]), int(gi[r, q, j])) for r in range(world) for j in range(int(gc[r, q])))
+        entries = entries[:k]
+        oc[q] = len(entries)
+        for j, (d, i) in enumerate(entries):
+            od[q, j], oi[q, j] = d, i
+    return torch.from_numpy(od), torch.from_numpy(oi), torch.from_numpy(oc)
+
+
+def worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    torch.distributed.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        x = synth.mixture(ROWS, DIMS, 10, seed=31)
+        q = torch.from_numpy(synth.mixture_queries(NQ, DIMS, 10, seed=31))
+        words, _ = synth.bitmap(ROWS, 0.3, seed=31)
+        b = sharded.shard_bounds(ROWS, world)
+        lo, hi = b[rank], b[rank + 1]
+        w, nbits = sharded.bitmap_slice(words, lo, hi)
+        bits = np.unpackbits(w.view(np.uint8), bitorder='little')[:nbits]
+        rows = torch.from_numpy(np.nonzero(bits)[0].astype(np.uint32).view(np.int32))
+        shard = OracleShard(x[lo:hi], lo)
+        d, i, c = sharded.search_sharded(shard, q, K, 0, rows, merge=merge_host)
+        out[rank] = (d.numpy(), i.numpy(), c.numpy())
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize('world', [2])
+def test_two_rank_sharded_search_equals_whole(world):
+    ctx = mp.get_context('spawn')
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    mp.start_processes(worker, args=(world, free_port(), out), nprocs=world, join=True, start_method='spawn')
+    x = synth.mixture(ROWS, DIMS, 10, seed=31)
+    q = synth.mixture_queries(NQ, DIMS, 10, seed=31)
+    _, ids = synth.bitmap(ROWS, 0.3, seed=31)
+    od, oi, oc, _ = oracle.search(oracle.F32, DIMS, x, q, K, 0, ids=ids)
+    for r in range(world):
+        d, i, c = out[r]
+        assert np.array_equal(c, oc.astype(np.int32))
+        assert np.array_equal(i, oi) and np.array_equal(d, od)
+
+
+def test_shard_bounds_word_aligned():
+    for rows in (1, 31, 32, 1000, 10_000_000):
+        for world in (1, 2, 3, 4, 8):
+            b = sharded.shard_bounds(rows, world)
+            assert b[0] == 0 and b[-1] == rows and all(x % 32 == 0 for x in b[:-1])
+            assert all(b0 <= b1 for b0, b1 in zip(b, b[1:]))
