@@ -275,9 +275,9 @@ def main():
     for _ in range(args.warmup):
         step(queries, my_words)
     barrier()
-    stage_ms = (ctypes.c_double * 8)()
-    stage_calls = (ctypes.c_ulonglong * 8)()
-    lib.AnnB200StageTimes(stage_ms, stage_calls, 8, 1)
+    stage_ms = (ctypes.c_double * 9)()
+    stage_calls = (ctypes.c_ulonglong * 9)()
+    lib.AnnB200StageTimes(stage_ms, stage_calls, 9, 1)
     launches0 = lib.AnnB200LaunchCount()
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
@@ -293,7 +293,7 @@ def main():
     barrier()
     clock_info = clocks.stop() if clocks else None
     launches = lib.AnnB200LaunchCount() - launches0
-    lib.AnnB200StageTimes(stage_ms, stage_calls, 8, 0)
+    lib.AnnB200StageTimes(stage_ms, stage_calls, 9, 0)
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = args.steps * args.batch / (ms / 1e3)
     result = out
@@ -351,7 +351,8 @@ def main():
                 'hbm_achieved_gbs': bytes_alg / (filt_ms * 1e-3) / 1e9, 'hbm_peak_gbs': hbm,
                 'hbm_frac': bytes_alg / (filt_ms * 1e-3) / 1e9 / hbm,
                 'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(
-                    ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge'])}}
+                    ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge',
+                     'gather'])}}
 
     # ---- correctness spot check against the CPU oracle (single GPU)
     verified = None

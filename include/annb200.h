@@ -161,10 +161,12 @@ unsigned long long AnnB200LaunchCount(void);
  * reference's ANN_KERNEL_TIMING, ann/server/cuvs.c:6999-7060). Stages, in
  * order: 0 query preparation, 1 sample scan, 2 sample bound, 3 filter scan,
  * 4 tighten, 5 finalize (exact rescoring and ordering), 6 bitmap expansion,
- * 7 merge. Fills up to n entries of ms (milliseconds) and calls; reset
- * clears the totals. Returns the number of stages, or 0 when timing is off.
+ * 7 merge, 8 candidate-row gather (copies rows for the tensor scan; its time
+ * is also inside stages 1 and 3). Fills up to n entries of ms (milliseconds)
+ * and calls; reset clears the totals. Returns the number of stages, or 0
+ * when timing is off.
  */
-#define ANNB200_STAGES 8
+#define ANNB200_STAGES 9
 int			AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset);
 
 #ifdef __cplusplus

@@ -6,13 +6,14 @@
 // persistent CTA per SM walks (128-row, BN-query) tiles, BN <= 256:
 //
 //   warp 0     TMA producer: per 64-dimension k-block (one pipeline stage of
-//              4), each lane issues one cp.async.bulk.tensor tile::gather4
-//              that gathers 4 of the tile's 128 candidate rows (128 bytes
-//              each) by row id, and lane 0 one tiled load of the BN x 64
-//              FP16 query block; both land in the 128-byte-swizzled K-major
+//              4), one thread issues two tiled cp.async.bulk.tensor loads --
+//              the 128 x 64 block of candidate rows and the BN x 64 block of
+//              FP16 queries -- which land in the 128-byte-swizzled K-major
 //              layout tcgen05 reads and complete on the stage's mbarrier.
-//              Row ids of the next tile are fetched while the current one
-//              streams.
+//              Candidate rows are contiguous: a shard's own rows when every
+//              row is scanned, else a staging copy that gather_rows filled
+//              (TMA's per-row tile::gather4 is request-rate bound at about
+//              13 GB/s an SM, a plain coalesced copy is not).
 //   warp 1     one thread issues tcgen05.mma.cta_group::1.kind::f16
 //              (M=128, N=BN, K=16) into an FP32 accumulator in tensor memory,
 //              and tcgen05.commit frees each stage and publishes each tile.
@@ -20,8 +21,10 @@
 //              (warp w reads TMEM lanes 32*(w%4)..+31), applies the per-row
 //              affine map to the v-domain score and either stores it (sample
 //              matrix) or appends (v, row) when v passes the query's
-//              threshold. Two accumulators (2 x 256 columns) let the epilogue
-//              of tile t overlap the MMAs of tile t+1.
+//              threshold: the 32 compares of a column chunk form a bitmask
+//              first, and only a chunk with a passing score in the warp takes
+//              the staging path. Two accumulators (2 x 256 columns) let the
+//              epilogue of tile t overlap the MMAs of tile t+1.
 //
 // Every wait is bounded (4 s of %globaltimer); a wait that runs out sets
 // FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are drained and
@@ -47,6 +50,7 @@ constexpr unsigned long long kWaitNs = 4000000000ull;
 
 struct TcArgs {
   ScanArgs a;
+  int64_t a_row0;      // row of the A tensor map holding virtual row 0
   uint32_t kpad;       // halves per query row, multiple of 64
   uint32_t kblocks;    // kpad / 64
   uint32_t bn;         // queries per tile, multiple of 32, <= 256
@@ -99,17 +103,6 @@ __device__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abo
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
-}
-
-// Four rows (row coordinates r0..r3) x 64 FP16 columns from column x of the
-// row tensor, 128 bytes a row, swizzled, into dst; completes on bar.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t r0, int32_t r1,
-                                            int32_t r2, int32_t r3, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
-      : "memory");
 }
 
 // A (box rows) x 64 tile at (x, y) of a 2-D tensor into dst; completes on bar.
@@ -223,43 +216,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // lane g gathers tile rows 4g..4g+3; invalid slots (past the candidate
-    // list) re-read a valid row and are ignored by the epilogue
-    auto tile_ids = [&](uint64_t tile, int32_t (&r)[4]) {
-      const uint64_t rt = tile / t.qtiles;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        uint64_t vi = rt * BM + lane * 4 + i;
-        if (vi >= a.count) vi = a.count - 1;
-        const uint64_t pos = a.base + vi * a.stride;
-        r[i] = (int32_t)(a.ids ? (uint64_t)__ldg(a.ids + pos) : pos);
-      }
-    };
-    const uint32_t tx_bytes = (uint32_t)A_BYTES + t.bn * 128u;
-    uint64_t it = 0;
-    bool ok = true;
-    int32_t cur[4], nxt[4];
-    if (blockIdx.x < ntiles) tile_ids(blockIdx.x, cur);
-    for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const uint32_t qt = (uint32_t)(tile % t.qtiles);
-      if (tile + gridDim.x < ntiles) tile_ids(tile + gridDim.x, nxt);
-      for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
-        const uint32_t s = (uint32_t)(it % STAGES);
-        const uint32_t ph = (uint32_t)((it / STAGES) & 1);
-        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
+    if (lane == 0) {
+      const uint32_t tx_bytes = (uint32_t)A_BYTES + t.bn * 128u;
+      uint64_t it = 0;
+      bool ok = true;
+      for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const uint64_t rt = tile / t.qtiles;
+        const uint32_t qt = (uint32_t)(tile % t.qtiles);
+        const int32_t arow = (int32_t)(t.a_row0 + (int64_t)rt * BM);
+        for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
+          const uint32_t s = (uint32_t)(it % STAGES);
+          const uint32_t ph = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(empty + s, ph ^ 1, abort, a.flags)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          mbar_expect_tx(full + s, tx_bytes);
+          tma_load_2d(sa, &rows_map, (int32_t)(kb * 64), arow, full + s);
+          tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), full + s);
         }
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        if (lane == 0) mbar_expect_tx(full + s, tx_bytes);
-        __syncwarp();
-        tma_gather4(sa + lane * 512, &rows_map, (int32_t)(kb * 64), cur[0], cur[1], cur[2], cur[3], full + s);
-        if (lane == 0) tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), full + s);
       }
-#pragma unroll
-      for (int i = 0; i < 4; i++) cur[i] = nxt[i];
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -358,24 +337,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         } else {
           const float4 *tq = reinterpret_cast<const float4 *>(thr_s + q0);
+          uint32_t m = 0;
 #pragma unroll
           for (int j4 = 0; j4 < 8; j4++) {
             const float4 t4 = tq[j4];
             const float th[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-              const int j = j4 * 4 + jj;
-              const float v = fmaf(__uint_as_float(r[j]), al, be);
-              const bool pass = v <= th[jj];
-              const uint32_t ballot = __ballot_sync(0xffffffffu, pass);
-              if (ballot) {
-                if (nbuf + 32 > (uint32_t)EPI_BUF) flush();
-                if (pass)
-                  buf[nbuf + __popc(ballot & ((1u << lane) - 1u))] =
-                      make_uint4(q0 + j, __float_as_uint(v), (uint32_t)pos, 0u);
-                nbuf += __popc(ballot);
-              }
-            }
+            for (int jj = 0; jj < 4; jj++)
+              m |= (uint32_t)(fmaf(__uint_as_float(r[j4 * 4 + jj]), al, be) <= th[jj]) << (j4 * 4 + jj);
+          }
+          // rare path: each round every lane stages its lowest passing column
+          while (__any_sync(0xffffffffu, m != 0)) {
+            const bool has = m != 0;
+            const int j = has ? __ffs(m) - 1 : 0;
+            m &= m - 1;
+            float v = 0.0f;
+#pragma unroll
+            for (int jj = 0; jj < 32; jj++) v = (jj == j) ? __uint_as_float(r[jj]) : v;
+            v = fmaf(v, al, be);
+            const uint32_t ballot = __ballot_sync(0xffffffffu, has);
+            if (nbuf + 32 > (uint32_t)EPI_BUF) flush();
+            if (has)
+              buf[nbuf + __popc(ballot & ((1u << lane) - 1u))] =
+                  make_uint4(q0 + j, __float_as_uint(v), (uint32_t)pos, 0u);
+            nbuf += __popc(ballot);
           }
         }
       }
@@ -395,7 +380,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
+// Copy candidate rows (virtual row i = candidate position base + i*stride,
+// row id ids[pos] or pos) to consecutive rows of out: one warp a row,
+// 16-byte coalesced loads and stores (row_bytes a multiple of 16).
+__global__ void __launch_bounds__(256) gather_rows(const uint8_t *codes, uint64_t row_bytes, const uint32_t *ids,
+                                                   uint64_t base, uint64_t stride, uint64_t count, uint8_t *out) {
+  const uint64_t i = (uint64_t)blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (i >= count) return;
+  const uint64_t pos = base + i * stride;
+  const uint64_t id = ids ? (uint64_t)__ldg(ids + pos) : pos;
+  const uint4 *src = reinterpret_cast<const uint4 *>(codes + id * row_bytes);
+  uint4 *dst = reinterpret_cast<uint4 *>(out + i * row_bytes);
+  const uint32_t units = (uint32_t)(row_bytes / 16);
+  uint4 v[4];
+  for (uint32_t u0 = 0; u0 < units; u0 += 128) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t u = u0 + k * 32 + lane;
+      if (u < units) v[k] = __ldg(src + u);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t u = u0 + k * 32 + lane;
+      if (u < units) dst[u] = v[k];
+    }
+  }
+}
+
 }  // namespace
+
+void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, const uint32_t *ids, uint64_t base, uint64_t stride,
+                        uint64_t count, uint8_t *out, cudaStream_t st) {
+  if (count) gather_rows<<<(unsigned)((count + 7) / 8), 256, 0, st>>>(codes, row_bytes, ids, base, stride, count, out);
+}
 
 // Shared memory the tensor scan needs for nq queries (thresholds included).
 size_t tc_scan_smem(uint32_t nq) {
@@ -407,13 +425,16 @@ size_t tc_scan_smem(uint32_t nq) {
 uint32_t tc_scan_max_queries() { return 4096; }
 
 // Launch the tensor scan of a.count virtual rows against a.nq FP16 queries:
-// rows_map describes the shard's rows ([rows][dims] FP16, box 64 x 1,
-// 128-byte swizzle), query_map the FP16 queries ([qtiles*bn][kpad], box
-// 64 x bn). Returns a CUDA error from the launch.
-cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, const CUtensorMap &query_map,
-                           uint32_t kpad, uint32_t bn, int sms, cudaStream_t st) {
+// rows_map describes contiguous FP16 rows ([rows][dims], box 64 x 128,
+// 128-byte swizzle) whose row a_row0 is virtual row 0 -- the shard itself
+// or a staging copy of gathered candidates; query_map the FP16 queries
+// ([qtiles*bn][kpad], box 64 x bn). The epilogue still reads per-row norms
+// through a.ids / a.base / a.stride. Returns a CUDA error from the launch.
+cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
+                           const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st) {
   TcArgs t;
   t.a = a;
+  t.a_row0 = a_row0;
   t.kpad = kpad;
   t.kblocks = kpad / 64;
   t.bn = bn;

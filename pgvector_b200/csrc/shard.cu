@@ -113,7 +113,7 @@ struct Carver {
 
 // ---- launch counting and stage timing (ANN_B200_KERNEL_TIMING=1)
 std::atomic<unsigned long long> g_launches{0};
-enum Stage { ST_PREP, ST_SAMPLE, ST_BOUND, ST_FILTER, ST_TIGHTEN, ST_FINAL, ST_BITMAP, ST_MERGE, ST_COUNT };
+enum Stage { ST_PREP, ST_SAMPLE, ST_BOUND, ST_FILTER, ST_TIGHTEN, ST_FINAL, ST_BITMAP, ST_MERGE, ST_GATHER, ST_COUNT };
 std::mutex g_stage_mu;
 double g_stage_ms[ST_COUNT];
 unsigned long long g_stage_calls[ST_COUNT];
@@ -191,6 +191,8 @@ bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+constexpr uint64_t kStagingBytes = 2ull << 30;
+constexpr uint64_t BM_ROWS = 128;  // gathered rows a tensor-scan chunk may stage
 constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
 constexpr uint64_t kSampleRows = 32768;    // sample size of the bound
 constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
@@ -212,8 +214,9 @@ struct AnnB200Shard {
   DeviceBuffer cand;    // candidate lists
   DeviceBuffer big;     // survivor sort scratch of the rare large case
   uint32_t *hflags = nullptr;  // pinned: flags readback
-  CUtensorMap rows_map;        // FP16 rows for the tensor scan's gather
+  CUtensorMap rows_map;        // the shard's FP16 rows, box 64 x 128, for the tensor scan
   bool rows_map_ok = false;
+  DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
 };
 
 extern "C" const char *AnnB200LastError(void) { return g_error.c_str(); }
@@ -240,6 +243,7 @@ extern "C" void AnnB200ShardDestroy(AnnB200Shard *s) {
     s->ws.release();
     s->cand.release();
     s->big.release();
+    s->staging.release();
   }
   delete s;
 }
@@ -309,7 +313,7 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   if (e != cudaSuccess) return cuda_fail(e, "shard upload");
   // the tensor scan gathers 128-byte row pieces by TMA (row pitch a multiple of 16 bytes)
   s->rows_map_ok = dtype == DT_F16 && dims % 8 == 0 && rows > 0 && rows < (1ull << 31) &&
-                   encode_f16_map(&s->rows_map, v.codes, dims, rows, v.row_bytes, 1);
+                   encode_f16_map(&s->rows_map, v.codes, dims, rows, v.row_bytes, 128);
   return OK;
 }
 
@@ -433,9 +437,32 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   CUtensorMap query_map;
   if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
-  auto scan = [&](void) -> cudaError_t {
-    if (tc) return launch_tc_scan(a, sh->rows_map, query_map, kpad, bn, sh->sms, st);
+  // one scan launch (plus the candidate-row gather it needs), timed as `stage`
+  auto scan = [&](int stage) -> cudaError_t {
+    if (tc) {
+      if (!a.ids && a.stride == 1) {  // contiguous rows of the shard itself
+        int hk = clock.begin(stage);
+        cudaError_t e = launch_tc_scan(a, sh->rows_map, (int64_t)a.base, query_map, kpad, bn, sh->sms, st);
+        clock.end(hk);
+        return e;
+      }
+      // gather the candidates into the staging copy, then scan it contiguously
+      cudaError_t e = sh->staging.reserve(a.count * v.row_bytes);
+      if (e != cudaSuccess) return e;
+      int hs = clock.begin(ST_GATHER);
+      launch_gather_rows(v.codes, v.row_bytes, a.ids, a.base, a.stride, a.count, (uint8_t *)sh->staging.p, st);
+      clock.end(hs);
+      counted(1);
+      CUtensorMap staged;
+      if (!encode_f16_map(&staged, sh->staging.p, v.dims, a.count, v.row_bytes, 128)) return cudaErrorInvalidValue;
+      int hk = clock.begin(stage);
+      e = launch_tc_scan(a, staged, 0, query_map, kpad, bn, sh->sms, st);
+      clock.end(hk);
+      return e;
+    }
+    int hk = clock.begin(stage);
     launch_simt_scan(a, st);
+    clock.end(hk);
     return cudaGetLastError();
   };
 
@@ -466,9 +493,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       a.stride = stride;
       a.mat = mat;
       a.mat_ld = S;
-      h = clock.begin(ST_SAMPLE);
-      CK(scan(), "sample scan");
-      clock.end(h);
+      CK(scan(ST_SAMPLE), "sample scan");
       h = clock.begin(ST_BOUND);
       launch_kth_bound(mat, S, S, nq, k, metric, window, qs, st);
       clock.end(h);
@@ -488,15 +513,14 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
         double room = (double)seen * (double)cap / (4.0 * (double)k);
         len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)room));
       }
+      if (tc && rows) len = std::min<uint64_t>(len, std::max<uint64_t>(BM_ROWS, kStagingBytes / v.row_bytes));
       CK(cudaMemcpyAsync(snap, cnt, nq * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st), "snapshot");
       for (;;) {
         a.count = len;
         a.base = start;
         a.cand = (uint2 *)sh->cand.p;
         a.cap = cap;
-        h = clock.begin(ST_FILTER);
-        CK(scan(), "filter scan");
-        clock.end(h);
+        CK(scan(ST_FILTER), "filter scan");
         counted(1);
         CK(cudaMemcpyAsync(sh->hflags, dflags, 16, cudaMemcpyDeviceToHost, st), "flags");
         CK(cudaStreamSynchronize(st), "filter scan");
@@ -653,7 +677,7 @@ extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(
 
 extern "C" int AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset) {
   std::lock_guard<std::mutex> lock(g_stage_mu);
-  for (uint32_t i = 0; i < n && i < ST_COUNT; i++) {
+  for (uint32_t i = 0; i < n && i < (uint32_t)ST_COUNT; i++) {
     if (ms) ms[i] = g_stage_ms[i];
     if (calls) calls[i] = g_stage_calls[i];
   }
