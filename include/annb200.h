@@ -128,6 +128,20 @@ int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
 						  int32_t *status, void *stream);
 
 /*
+ * The approximate score matrix the scan prunes with (the reference's
+ * score-matrix route, score_mma_* / AnnBlackwellScore,
+ * ann/server/blackwell.c:289-525,1066-1110): out [nq][n] FP32 approximate
+ * distances of every candidate row to every query -- Euclidean distance
+ * squared for L2, -dot for IP, 1 - cosine, Hamming -- n = nrows, or the
+ * shard's rows when rows is NULL; nq <= 4096. err (optional, device FP64
+ * [nq]) receives each query's bound on |approximate - exact| in the same
+ * domain. Synchronous.
+ */
+int			AnnB200ScoreMatrix(AnnB200Shard *shard, const void *queries, uint32_t nq,
+							   const uint32_t *rows, uint64_t nrows, uint32_t metric,
+							   uint32_t flags, float *out, double *err, void *stream);
+
+/*
  * Merge nlists per-shard result sets into one per query, on the device.
  * Inputs: device [nlists][nq][list_cap] distances/ids and [nlists][nq]
  * counts, each list sorted by (distance, id) with disjoint ids (the layout an

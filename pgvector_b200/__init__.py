@@ -98,6 +98,19 @@ class Shard:
                                    _ptr(status), _stream(stream)))
         return dist, ids, count
 
+    def score_matrix(self, queries, metric, rows=None, force_simt=False, stream=None):
+        """Approximate distances [nq][n] (squared for L2) and each query's
+        error bound, as the scan computes them."""
+        import torch
+        nq = int(queries.shape[0])
+        n = int(rows.shape[0]) if rows is not None else self.rows
+        out = torch.empty((nq, max(n, 1)), dtype=torch.float32, device=queries.device)
+        err = torch.empty((nq,), dtype=torch.float64, device=queries.device)
+        check(load().AnnB200ScoreMatrix(self._handle, _ptr(queries), nq, _ptr(rows), n if rows is not None else 0,
+                                        int(metric), FORCE_SIMT if force_simt else 0, _ptr(out), _ptr(err),
+                                        _stream(stream)))
+        return out[:, :n], err
+
 
 def merge_topk(dist, ids, counts, k, window=False, out_cap=None, stream=None):
     """Merge [nlists][nq][list_cap] per-shard results on the device."""

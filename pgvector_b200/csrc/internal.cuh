@@ -323,6 +323,7 @@ cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t 
                          double *out_dist, int64_t *out_id, uint32_t *out_count, uint32_t *flags,
                          cudaStream_t st);
 uint32_t bitmap_blocks(uint64_t nbits);
+void launch_v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, const QueryState &qs, cudaStream_t st);
 void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,
                         unsigned long long *total, cudaStream_t st);
 

@@ -16,6 +16,8 @@
 // dimension order. Every operation is an explicit round-to-nearest intrinsic
 // so no multiply-add is fused, which makes each distance identical to the
 // CPU's bit for bit.
+#include <algorithm>
+
 #include "internal.cuh"
 
 namespace annb200 {
@@ -103,70 +105,162 @@ __device__ uint32_t block_radix_select(KeyAt key_at, uint32_t n, uint32_t k, uin
 
 // ---------------------------------------------------------------- exact distances
 
-// The reference CPU worker's distance of one decoded row (see file header).
+// Raw storage of 8 consecutive dimensions of a row, per format: loaded first,
+// decoded later, so a thread keeps many loads in flight.
+template <int DT> struct Raw8 { uint4 w; };
+template <> struct Raw8<DT_F32> { float4 a, b; };
+template <> struct Raw8<DT_E4M3> { uint2 w; };
+template <> struct Raw8<DT_NVFP4> { uint32_t w; uint32_t sc; };
+
+template <int DT>
+__device__ __forceinline__ void load_raw8(const ShardView &s, const uint8_t *row, uint64_t id, uint32_t d0,
+                                          Raw8<DT> &r) {
+  if (DT == DT_F32) {
+    Raw8<DT_F32> &x = reinterpret_cast<Raw8<DT_F32> &>(r);
+    const float *f = reinterpret_cast<const float *>(row) + d0;
+    if ((s.row_bytes & 15) == 0 && d0 + 8 <= s.dims) {
+      x.a = __ldg(reinterpret_cast<const float4 *>(f));
+      x.b = __ldg(reinterpret_cast<const float4 *>(f + 4));
+    } else {
+      float t[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) t[j] = d0 + j < s.dims ? __ldg(f + j) : 0.0f;
+      x.a = make_float4(t[0], t[1], t[2], t[3]);
+      x.b = make_float4(t[4], t[5], t[6], t[7]);
+    }
+  } else if (DT == DT_F16) {
+    Raw8<DT_F16> &x = reinterpret_cast<Raw8<DT_F16> &>(r);
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(row) + d0;
+    if ((s.row_bytes & 15) == 0 && d0 + 8 <= s.dims) x.w = __ldg(reinterpret_cast<const uint4 *>(h));
+    else {
+      uint32_t t[4] = {0, 0, 0, 0};
+      for (int j = 0; j < 8; j++)
+        if (d0 + j < s.dims) t[j / 2] |= (uint32_t)__ldg(h + j) << (16 * (j & 1));
+      x.w = make_uint4(t[0], t[1], t[2], t[3]);
+    }
+  } else if (DT == DT_E4M3) {
+    reinterpret_cast<Raw8<DT_E4M3> &>(r).w = __ldg(reinterpret_cast<const uint2 *>(row + d0));
+  } else {
+    Raw8<DT_NVFP4> &x = reinterpret_cast<Raw8<DT_NVFP4> &>(r);
+    x.w = __ldg(reinterpret_cast<const uint32_t *>(row + d0 / 2));
+    x.sc = __ldg(s.bscales + id * s.bblocks + d0 / 16);
+  }
+}
+
+// Decode like decode8 (the FP32 values the reference would score).
+template <int DT>
+__device__ __forceinline__ void decode_raw8(const Raw8<DT> &r, float rs, float v[8]) {
+  if (DT == DT_F32) {
+    const Raw8<DT_F32> &x = reinterpret_cast<const Raw8<DT_F32> &>(r);
+    v[0] = x.a.x; v[1] = x.a.y; v[2] = x.a.z; v[3] = x.a.w;
+    v[4] = x.b.x; v[5] = x.b.y; v[6] = x.b.z; v[7] = x.b.w;
+  } else if (DT == DT_F16) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&reinterpret_cast<const Raw8<DT_F16> &>(r).w);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else if (DT == DT_E4M3) {
+    const uint2 w = reinterpret_cast<const Raw8<DT_E4M3> &>(r).w;
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fmul_rn(e4m3_value(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu), rs);
+  } else {
+    const Raw8<DT_NVFP4> &x = reinterpret_cast<const Raw8<DT_NVFP4> &>(r);
+    const float bs = __fmul_rn(e4m3_value(x.sc), rs);
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fmul_rn(e2m1_value((x.w >> (4 * j)) & 0xfu), bs);
+  }
+}
+
+// The reference CPU worker's distance of one decoded row (see file header),
+// with the row streamed in batches of 64 dimensions: the next batch's loads
+// are issued before the current batch is summed, and the sums keep the
+// reference's exact operation order.
 template <int DT>
 __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q, uint32_t metric,
                                  double qn2d) {
   const uint32_t dims = s.dims;
+  const uint8_t *row = s.codes + id * s.row_bytes;
   if (DT == DT_BIT) {
-    const uint8_t *row = s.codes + id * s.row_bytes;
     const uint8_t *qb = reinterpret_cast<const uint8_t *>(q);
     uint32_t d = 0;
     uint64_t b = 0;
-    if ((s.row_bytes & 3) == 0)
+    if ((s.row_bytes & 15) == 0)
+      for (; b < s.row_bytes; b += 16) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4 *>(row + b));
+        const uint4 y = *reinterpret_cast<const uint4 *>(qb + b);
+        d += __popc(x.x ^ y.x) + __popc(x.y ^ y.y) + __popc(x.z ^ y.z) + __popc(x.w ^ y.w);
+      }
+    else if ((s.row_bytes & 3) == 0)
       for (; b < s.row_bytes; b += 4)
         d += __popc(__ldg(reinterpret_cast<const uint32_t *>(row + b)) ^ *reinterpret_cast<const uint32_t *>(qb + b));
     for (; b < s.row_bytes; b++) d += __popc((uint32_t)(__ldg(row + b) ^ qb[b]));
     return (double)d;
   } else {
-    if (metric == M_L2) {
-      float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      float tail = 0.0f;
-      uint32_t d = 0;
-      float v[8];
-      for (; d + 8 <= dims; d += 8) {
-        decode8<DT>(s, id, d, v);
+    // 8-dimension groups a batch: 128 bytes of row per buffer
+    constexpr int G = DT == DT_F32 ? 4 : (DT == DT_F16 ? 8 : 16);
+    const float rs = (DT == DT_E4M3 || DT == DT_NVFP4) ? __ldg(s.rowscale + id) : 1.0f;
+    const uint32_t groups = (dims + 7) / 8;
+    Raw8<DT> bufA[G], bufB[G];
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float tail = 0.0f;
+    double dot = 0.0, nrm = 0.0;
+    auto load_batch = [&](uint32_t g0, Raw8<DT>(&buf)[G]) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          float diff = __fsub_rn(v[j], q[d + j]);
-          sums[j] = __fadd_rn(sums[j], __fmul_rn(diff, diff));
+      for (int g = 0; g < G; g++)
+        if (g0 + g < groups) load_raw8<DT>(s, row, id, (g0 + g) * 8, buf[g]);
+    };
+    auto sum_batch = [&](uint32_t g0, const Raw8<DT>(&buf)[G]) {
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const uint32_t d0 = (g0 + g) * 8;
+        if (d0 >= dims) break;
+        float v[8];
+        decode_raw8<DT>(buf[g], rs, v);
+        if (metric == M_L2) {
+          if (d0 + 8 <= dims) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              float diff = __fsub_rn(v[j], q[d0 + j]);
+              sums[j] = __fadd_rn(sums[j], __fmul_rn(diff, diff));
+            }
+          } else {
+            for (int j = 0; d0 + j < dims; j++) {
+              float diff = __fsub_rn(v[j], q[d0 + j]);
+              tail = __fadd_rn(tail, __fmul_rn(diff, diff));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            if (d0 + j < dims) {
+              double x = v[j], y = q[d0 + j];
+              dot = __dadd_rn(dot, __dmul_rn(x, y));
+              nrm = __dadd_rn(nrm, __dmul_rn(x, x));
+            }
+          }
         }
       }
-      if (d < dims) {
-        decode8<DT>(s, id, d, v);
-        for (int j = 0; d + j < dims; j++) {
-          float diff = __fsub_rn(v[j], q[d + j]);
-          tail = __fadd_rn(tail, __fmul_rn(diff, diff));
-        }
-      }
+    };
+    load_batch(0, bufA);
+    for (uint32_t g0 = 0; g0 < groups; g0 += 2 * G) {
+      if (g0 + G < groups) load_batch(g0 + G, bufB);
+      sum_batch(g0, bufA);
+      if (g0 + G >= groups) break;
+      if (g0 + 2 * G < groups) load_batch(g0 + 2 * G, bufA);
+      sum_batch(g0 + G, bufB);
+    }
+    if (metric == M_L2) {
       float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
       float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
       float total = __fadd_rn(__fadd_rn(tail, left), right);
       return __dsqrt_rn((double)total);
     }
-    double dot = 0.0, nrm = 0.0;
-    float v[8];
-    for (uint32_t d = 0; d < dims; d += 8) {
-      decode8<DT>(s, id, d, v);
-      for (int j = 0; j < 8 && d + j < dims; j++) {
-        double x = v[j], y = q[d + j];
-        dot = __dadd_rn(dot, __dmul_rn(x, y));
-        nrm = __dadd_rn(nrm, __dmul_rn(x, x));
-      }
-    }
     if (metric == M_IP) return -dot;
     double r = __ddiv_rn(dot, __dsqrt_rn(__dmul_rn(nrm, qn2d)));
     return __dsub_rn(1.0, fmax(-1.0, fmin(1.0, r)));
-  }
-}
-
-__device__ double exact_any(const ShardView &s, uint64_t id, const float *q, uint32_t metric, double qn2d) {
-  switch (s.dtype) {
-    case DT_F32: return exact_distance<DT_F32>(s, id, q, metric, qn2d);
-    case DT_F16: return exact_distance<DT_F16>(s, id, q, metric, qn2d);
-    case DT_E4M3: return exact_distance<DT_E4M3>(s, id, q, metric, qn2d);
-    case DT_NVFP4: return exact_distance<DT_NVFP4>(s, id, q, metric, qn2d);
-    default: return exact_distance<DT_BIT>(s, id, q, metric, qn2d);
   }
 }
 
@@ -479,6 +573,7 @@ __device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned lo
   }
 }
 
+template <int DT>
 __global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
   extern __shared__ uint8_t dyn[];
   unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
@@ -521,7 +616,7 @@ __global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
     if (i < m) {
       uint32_t p = e[i].y;
       uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
-      key[i] = double_key(exact_any(a.s, id, qv, a.metric, qn2d));
+      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d));
       pos[i] = p;
     } else {
       key[i] = ~0ull;
@@ -535,6 +630,7 @@ __global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
 
 // The same for one query whose survivors outgrew shared memory: rescoring and
 // sorting in a global scratch of p2 (key, pos) pairs.
+template <int DT>
 __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, unsigned long long *key, uint32_t *pos,
                                                    uint32_t p2) {
   const uint32_t m = a.big[q];
@@ -546,7 +642,7 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
     if (i < m) {
       uint32_t p = e[i].y;
       uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
-      key[i] = double_key(exact_any(a.s, id, qv, a.metric, qn2d));
+      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d));
       pos[i] = p;
     } else {
       key[i] = ~0ull;
@@ -556,6 +652,18 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
   __syncthreads();
   bitonic_sort(key, pos, p2);
   write_results(a, q, key, pos, m);
+}
+
+// ---------------------------------------------------------------- score matrix
+
+// v-domain scores -> approximate distances (squared distance for L2).
+__global__ void v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, QueryState qs) {
+  const uint32_t q = blockIdx.y;
+  const double qn2 = qs.qn2d[q], rnq = qs.rnq[q];
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float *p = m + (uint64_t)q * n + i;
+    *p = (float)v_to_dist(metric, (double)*p, qn2, rnq);
+  }
 }
 
 // ---------------------------------------------------------------- merge
@@ -758,17 +866,34 @@ static SelectArgs to_args(const SelectLaunch &l) {
 
 void launch_tighten(const SelectLaunch &l, cudaStream_t st) { tighten<<<l.nq, NT, 0, st>>>(to_args(l)); }
 
-cudaError_t launch_finalize(const SelectLaunch &l, cudaStream_t st) {
+template <int DT>
+static cudaError_t finalize_dt(const SelectLaunch &l, cudaStream_t st) {
   const size_t smem = (size_t)kSortCap * (8 + 4);
-  cudaError_t e = cudaFuncSetAttribute(finalize, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(finalize<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  finalize<<<l.nq, NT, smem, st>>>(to_args(l));
+  finalize<DT><<<l.nq, NT, smem, st>>>(to_args(l));
   return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const SelectLaunch &l, cudaStream_t st) {
+  switch (l.s.dtype) {
+    case DT_F32: return finalize_dt<DT_F32>(l, st);
+    case DT_F16: return finalize_dt<DT_F16>(l, st);
+    case DT_E4M3: return finalize_dt<DT_E4M3>(l, st);
+    case DT_NVFP4: return finalize_dt<DT_NVFP4>(l, st);
+    default: return finalize_dt<DT_BIT>(l, st);
+  }
 }
 
 void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,
                          cudaStream_t st) {
-  finalize_big<<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2);
+  switch (l.s.dtype) {
+    case DT_F32: finalize_big<DT_F32><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
+    case DT_F16: finalize_big<DT_F16><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
+    case DT_E4M3: finalize_big<DT_E4M3><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
+    case DT_NVFP4: finalize_big<DT_NVFP4><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
+    default: finalize_big<DT_BIT><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
+  }
 }
 
 cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,
@@ -781,6 +906,11 @@ cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t 
   if (e != cudaSuccess) return e;
   merge_lists<<<nq, NT, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+void launch_v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, const QueryState &qs, cudaStream_t st) {
+  dim3 grid((unsigned)std::min<uint64_t>((n + 255) / 256, 1024), nq);
+  v_to_distance<<<grid, 256, 0, st>>>(m, n, nq, metric, qs);
 }
 
 uint32_t bitmap_blocks(uint64_t nbits) {

@@ -193,6 +193,17 @@ bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
 
 constexpr uint64_t kStagingBytes = 2ull << 30;
 constexpr uint64_t BM_ROWS = 128;  // gathered rows a tensor-scan chunk may stage
+// Relative bound on the approximate dot product's accumulation error (times
+// sum |x_i q_i| <= ||x|| ||q||). Tensor scan: each tcgen05.mma (K=16) adds an
+// exactly formed FP16 product sum into the FP32 accumulator, so K/16 rounding
+// steps, each allowed 4 ulps (2^-21) of the magnitudes involved. CUDA-core
+// scan: one FP32 rounding per fused multiply-add, allowed 2 ulps each.
+double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims) {
+  if (bits) return 0.0;
+  if (tc) return ((double)kpad / 16.0 + 2.0) * std::ldexp(1.0, -21);
+  return (double)dims * std::ldexp(1.0, -22);
+}
+
 constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
 constexpr uint64_t kSampleRows = 32768;    // sample size of the bound
 constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
@@ -370,7 +381,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
   const uint32_t nq_pad = qtiles * bn;
-  const double gamma = bits ? 0.0 : (tc ? (double)kpad : (double)v.dims) * std::ldexp(1.0, -22);
+  const double gamma = scan_gamma(bits, tc, kpad, v.dims);
   const bool sample = k > 0 && n > kNoSampleRows;
   const uint64_t stride = sample ? std::max<uint64_t>(1, n / std::max<uint64_t>(kSampleRows, 8ull * k)) : 1;
   const uint64_t S = sample ? n / stride : 0;
@@ -687,4 +698,92 @@ extern "C" int AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t
       g_stage_calls[i] = 0;
     }
   return timing_on() ? ST_COUNT : 0;
+}
+
+extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows,
+                                  uint64_t nrows, uint32_t metric, uint32_t flags, float *out, double *err,
+                                  void *stream) {
+  if (!sh) return fail(INVALID, "shard is NULL");
+  const ShardView &v = sh->view;
+  if (v.dtype == DT_BIT ? metric != M_HAM : metric > M_COS)
+    return fail(UNSUPPORTED, "metric %u does not apply to storage format %u", metric, v.dtype);
+  const uint64_t n = rows ? nrows : v.rows;
+  if (nq == 0 || n == 0) return OK;
+  if (!queries || !out) return fail(INVALID, "NULL query or output pointer");
+  if (nq > tc_scan_max_queries()) return fail(UNSUPPORTED, "at most %u queries a call", tc_scan_max_queries());
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bits = v.dtype == DT_BIT;
+  const bool tc = v.dtype == DT_F16 && sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
+  const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
+  const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
+  const uint32_t nq_pad = tc ? (nq + bn - 1) / bn * bn : 0;
+  Carver c;
+  const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
+               o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
+               o_q16 = c.take<__half>((size_t)nq_pad * kpad), o_flags = c.take<uint32_t>(16);
+  CK(sh->ws.reserve(c.off), "workspace");
+  uint8_t *w = (uint8_t *)sh->ws.p;
+  QueryState qs;
+  qs.qn2 = (float *)(w + o_qn2);
+  qs.rnq = (float *)(w + o_rnq);
+  qs.qn2d = (double *)(w + o_qn2d);
+  qs.err = (double *)(w + o_err);
+  qs.thr = (float *)(w + o_thr);
+  qs.status = (int32_t *)(w + o_status);
+  qs.q16 = (__half *)(w + o_q16);
+  uint32_t *dflags = (uint32_t *)(w + o_flags);
+  CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
+  if (tc && nq_pad > nq)
+    CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
+  if (rows) {
+    launch_check_rows(rows, nrows, v.rows, dflags, st);
+    CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
+    CK(cudaStreamSynchronize(st), "row check");
+    if (sh->hflags[0] & FLAG_BAD_ROWS) return fail(INVALID, "candidate rows must be increasing and < rows");
+  }
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, scan_gamma(bits, tc, kpad, v.dims),
+                      sh->maxn2, qs, bits, st);
+  counted(1);
+  ScanArgs a{};
+  a.s = v;
+  a.ids = rows;
+  a.count = n;
+  a.base = 0;
+  a.stride = 1;
+  a.queries = (const float *)queries;
+  a.nq = nq;
+  a.metric = metric;
+  a.mode = MODE_MATRIX;
+  a.mat = out;
+  a.mat_ld = n;
+  a.flags = dflags;
+  if (tc) {
+    CUtensorMap query_map;
+    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+      return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
+    if (!rows) {
+      CK(launch_tc_scan(a, sh->rows_map, 0, query_map, kpad, bn, sh->sms, st), "score scan");
+    } else {
+      CK(sh->staging.reserve(n * v.row_bytes), "staging");
+      launch_gather_rows(v.codes, v.row_bytes, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
+      CUtensorMap staged;
+      if (!encode_f16_map(&staged, sh->staging.p, v.dims, n, v.row_bytes, 128))
+        return fail(BACKEND_ERROR, "tensor map of the staged rows could not be encoded");
+      CK(launch_tc_scan(a, staged, 0, query_map, kpad, bn, sh->sms, st), "score scan");
+      counted(1);
+    }
+  } else {
+    launch_simt_scan(a, st);
+    CK(cudaGetLastError(), "score scan");
+  }
+  counted(1);
+  launch_v_to_distance(out, n, nq, metric, qs, st);
+  counted(1);
+  if (err) CK(cudaMemcpyAsync(err, qs.err, nq * sizeof(double), cudaMemcpyDeviceToDevice, st), "err");
+  CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
+  CK(cudaStreamSynchronize(st), "score matrix");
+  if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
+  return OK;
 }

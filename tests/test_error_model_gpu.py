@@ -1,0 +1,61 @@
+"""The scan's approximate scores against exact arithmetic.
+
+Exactness of every search rests on one inequality: for each (row, query)
+pair, |approximate - exact| <= the per-query bound the library computes
+(scan_gamma and prep_queries). Pruning uses that bound as its margin, so a
+row whose exact distance can still reach the answer is never dropped. This
+test measures the inequality over millions of pairs on both scan paths,
+and requires the observed error to stay below half of the bound.
+"""
+import numpy as np
+import pytest
+
+from pgvector_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def exact(x64, q64, metric):
+    dot = q64 @ x64.T
+    if metric == 1:
+        return -dot
+    if metric == 2:
+        nx = (x64 * x64).sum(1)
+        nq = (q64 * q64).sum(1)
+        return 1 - np.clip(dot / np.sqrt(np.outer(nq, nx)), -1, 1)
+    return (q64 * q64).sum(1)[:, None] + (x64 * x64).sum(1)[None, :] - 2 * dot
+
+
+@pytest.mark.parametrize('metric', [2, 1, 0])
+@pytest.mark.parametrize('simt', [False, True])
+def test_bound_holds_on_f16_rows(cuda, metric, simt):
+    import torch
+    import pgvector_b200 as pb
+    n, d, nq = 20000, 768, 256
+    x = synth.mixture(n, d, 50, seed=40, normalize=(metric == 2)).astype(np.float16)
+    q = synth.mixture_queries(nq, d, 50, seed=40, normalize=(metric == 2))
+    q[: nq // 2] = q[: nq // 2].astype(np.float16).astype(np.float32)   # half the queries FP16-exact
+    shard = pb.Shard(pb.F16, d, torch.from_numpy(x.view(np.int16)).to(cuda))
+    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), metric, force_simt=simt)
+    approx = approx.cpu().numpy().astype(np.float64)
+    err = err.cpu().numpy()
+    ex = exact(x.astype(np.float64), q.astype(np.float64), metric)
+    diff = np.abs(approx - ex)
+    ratio = (diff / err[:, None]).max()
+    print('metric %d simt %s: max |approx - exact| = %.3g, max ratio to bound = %.4f'
+          % (metric, simt, diff.max(), ratio))
+    assert (diff <= err[:, None]).all()
+    assert ratio < 0.5
+
+
+def test_hamming_scores_are_exact(cuda):
+    import torch
+    import pgvector_b200 as pb
+    rows, proto = synth.bit_rows(5000, 1024, 64, seed=41)
+    rng = np.random.default_rng(41)
+    qs = rng.integers(0, 256, (64, 128), dtype=np.uint8)
+    shard = pb.Shard(pb.BIT, 1024, torch.from_numpy(rows).to(cuda))
+    approx, err = shard.score_matrix(torch.from_numpy(qs).to(cuda), pb.HAMMING)
+    ex = np.unpackbits(qs[:, None, :] ^ rows[None, :, :], axis=2).sum(2)
+    assert np.array_equal(approx.cpu().numpy(), ex.astype(np.float32))
+    assert (err.cpu().numpy() == 0).all()
