@@ -58,6 +58,7 @@ struct ShardView {
   const float *rowscale;    // E4M3 / NVFP4 row scales
   const float *n2;          // decoded squared norm, FP32
   const float *rn;          // 1/sqrt(n2), 0 for a zero row
+  const double *n2x;        // FP64 squared norm summed in dimension order (the reference's cosine norm)
   uint64_t row_bytes;
   uint64_t rows;
   uint32_t dims;
@@ -85,6 +86,16 @@ struct ScanArgs {
   uint32_t cap;
   uint32_t *flags;          // [0] Flag bits, [1] largest count seen (overflow)
 };
+
+// Row id of candidate position pos: ids[pos], or pos when there is no list.
+// A list entry past the shard is clamped to its last row, so a bad list can
+// never address memory outside the shard; check_rows flags such a list and
+// the search then fails with ANN_INVALID.
+__device__ __forceinline__ uint64_t cand_row(const uint32_t *ids, uint64_t pos, uint64_t rows) {
+  if (!ids) return pos;
+  const uint64_t id = __ldg(ids + pos);
+  return id < rows ? id : rows - 1;
+}
 
 // Append (v, position) to query q's candidate list; FILTER mode.
 __device__ __forceinline__ void append_candidate(const ScanArgs &a, float v, uint64_t pos, uint32_t q) {
@@ -280,6 +291,7 @@ __device__ __forceinline__ float threshold_v(uint32_t metric, double D, double e
 // Arguments of the per-query selection kernels (tighten, finalize).
 struct SelectLaunch {
   ShardView s;
+  const uint8_t *staged;    // candidate rows in position order (or NULL: read the shard)
   const uint32_t *ids;
   const float *queries;
   uint32_t nq, k, metric;
@@ -302,20 +314,21 @@ struct SelectLaunch {
 void launch_simt_scan(const ScanArgs &a, cudaStream_t st);
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);
-void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, const uint32_t *ids, uint64_t base, uint64_t stride,
-                        uint64_t count, uint8_t *out, cudaStream_t st);
+void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
+                        uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st);
 size_t tc_scan_smem(uint32_t nq);
 uint32_t tc_scan_max_queries();
-void launch_shard_stats(const ShardView &s, float *n2, float *rn, uint32_t *maxn2, cudaStream_t st);
+void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         cudaStream_t st);
+                         uint32_t *flags, cudaStream_t st);
 void launch_fill_thresholds(uint32_t nq, const QueryState &qs, cudaStream_t st);
 void launch_check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t *flags, cudaStream_t st);
 void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, uint32_t k, uint32_t metric,
                       int window, const QueryState &qs, cudaStream_t st);
 void launch_tighten(const SelectLaunch &l, cudaStream_t st);
-cudaError_t launch_finalize(const SelectLaunch &l, cudaStream_t st);
+void launch_survivors(const SelectLaunch &l, cudaStream_t st);
+cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t st);
 void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,
                          cudaStream_t st);
 cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,

@@ -24,7 +24,7 @@ __device__ __forceinline__ void emit(const ScanArgs &a, float v, uint64_t vi, ui
 template <int DT, int BN>
 __global__ void __launch_bounds__(256) simt_scan(const ScanArgs a) {
   constexpr int TN = BN / 16;
-  __shared__ float xs[BK][BM + 4];
+  __shared__ __align__(16) float xs[BK][BM + 4];
   __shared__ float qs[BK][BN + 4];
   const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
   const uint64_t vbase = (uint64_t)blockIdx.x * BM;
@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(256) simt_scan(const ScanArgs a) {
   const uint64_t lvi = vbase + lr;
   const bool lvalid = lvi < a.count;
   const uint64_t lpos = a.base + lvi * a.stride;
-  const uint64_t lid = lvalid ? (a.ids ? (uint64_t)__ldg(a.ids + lpos) : lpos) : 0;
+  const uint64_t lid = lvalid ? cand_row(a.ids, lpos, a.s.rows) : 0;
   const uint32_t dims = a.s.dims;
 
   float acc[4][TN];
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) simt_scan(const ScanArgs a) {
     uint64_t vi = vbase + ty * 4 + i;
     if (vi >= a.count) continue;
     uint64_t pos = a.base + vi * a.stride;
-    uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
+    uint64_t id = cand_row(a.ids, pos, a.s.rows);
     float al, be;
     row_affine(a.s, id, a.metric, 0, al, be);
 #pragma unroll
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256) simt_scan(const ScanArgs a) {
 template <int BN>
 __global__ void __launch_bounds__(256) simt_hamming(const ScanArgs a) {
   constexpr int TN = BN / 16;
-  __shared__ uint32_t xs[BK][BM + 4];
+  __shared__ __align__(16) uint32_t xs[BK][BM + 4];
   __shared__ uint32_t qs[BK][BN + 4];
   const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
   const uint64_t vbase = (uint64_t)blockIdx.x * BM;
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) simt_hamming(const ScanArgs a) {
   const uint64_t lvi = vbase + lr;
   const bool lvalid = lvi < a.count;
   const uint64_t lpos = a.base + lvi * a.stride;
-  const uint64_t lid = lvalid ? (a.ids ? (uint64_t)__ldg(a.ids + lpos) : lpos) : 0;
+  const uint64_t lid = lvalid ? cand_row(a.ids, lpos, a.s.rows) : 0;
   const uint8_t *lrow = a.s.codes + lid * rb;
   const uint8_t *qbytes = reinterpret_cast<const uint8_t *>(a.queries);
 

@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint64_t pos = a.base + vi * a.stride;
       float al = 0.0f, be = __int_as_float(0x7fc00000);  // invalid rows score NaN: never pass
       if (valid) {
-        const uint64_t id = a.ids ? (uint64_t)__ldg(a.ids + pos) : pos;
+        const uint64_t id = cand_row(a.ids, pos, a.s.rows);
         row_affine(a.s, id, a.metric, a.raw_scale, al, be);
       }
       const uint32_t taddr = tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16);
@@ -383,13 +383,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // Copy candidate rows (virtual row i = candidate position base + i*stride,
 // row id ids[pos] or pos) to consecutive rows of out: one warp a row,
 // 16-byte coalesced loads and stores (row_bytes a multiple of 16).
-__global__ void __launch_bounds__(256) gather_rows(const uint8_t *codes, uint64_t row_bytes, const uint32_t *ids,
-                                                   uint64_t base, uint64_t stride, uint64_t count, uint8_t *out) {
+__global__ void __launch_bounds__(256) gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows,
+                                                   const uint32_t *ids, uint64_t base, uint64_t stride, uint64_t count,
+                                                   uint8_t *out) {
   const uint64_t i = (uint64_t)blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (i >= count) return;
   const uint64_t pos = base + i * stride;
-  const uint64_t id = ids ? (uint64_t)__ldg(ids + pos) : pos;
+  const uint64_t id = cand_row(ids, pos, rows);
   const uint4 *src = reinterpret_cast<const uint4 *>(codes + id * row_bytes);
   uint4 *dst = reinterpret_cast<uint4 *>(out + i * row_bytes);
   const uint32_t units = (uint32_t)(row_bytes / 16);
@@ -410,9 +411,10 @@ __global__ void __launch_bounds__(256) gather_rows(const uint8_t *codes, uint64_
 
 }  // namespace
 
-void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, const uint32_t *ids, uint64_t base, uint64_t stride,
-                        uint64_t count, uint8_t *out, cudaStream_t st) {
-  if (count) gather_rows<<<(unsigned)((count + 7) / 8), 256, 0, st>>>(codes, row_bytes, ids, base, stride, count, out);
+void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
+                        uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st) {
+  if (count)
+    gather_rows<<<(unsigned)((count + 7) / 8), 256, 0, st>>>(codes, row_bytes, rows, ids, base, stride, count, out);
 }
 
 // Shared memory the tensor scan needs for nq queries (thresholds included).

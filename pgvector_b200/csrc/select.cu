@@ -24,7 +24,8 @@ namespace annb200 {
 
 namespace {
 
-constexpr int NT = 512;  // threads of the per-query selection kernels
+constexpr int NT = 512;  // threads of the per-query bound / tighten / merge kernels
+constexpr int NTF = 256; // threads of finalize (two blocks an SM at its register use)
 
 // ---------------------------------------------------------------- block helpers
 
@@ -180,9 +181,8 @@ __device__ __forceinline__ void decode_raw8(const Raw8<DT> &r, float rs, float v
 // reference's exact operation order.
 template <int DT>
 __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q, uint32_t metric,
-                                 double qn2d) {
+                                 double qn2d, const uint8_t *row) {
   const uint32_t dims = s.dims;
-  const uint8_t *row = s.codes + id * s.row_bytes;
   if (DT == DT_BIT) {
     const uint8_t *qb = reinterpret_cast<const uint8_t *>(q);
     uint32_t d = 0;
@@ -203,16 +203,17 @@ __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q
     constexpr int G = DT == DT_F32 ? 4 : (DT == DT_F16 ? 8 : 16);
     const float rs = (DT == DT_E4M3 || DT == DT_NVFP4) ? __ldg(s.rowscale + id) : 1.0f;
     const uint32_t groups = (dims + 7) / 8;
-    Raw8<DT> bufA[G], bufB[G];
+    // the whole row toward L2 first: every batch load below then hits L2
+    for (uint64_t b = 0; b < s.row_bytes; b += 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+    Raw8<DT> buf[G];
     float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float tail = 0.0f;
-    double dot = 0.0, nrm = 0.0;
-    auto load_batch = [&](uint32_t g0, Raw8<DT>(&buf)[G]) {
+    double dot = 0.0;
+    for (uint32_t g0 = 0; g0 < groups; g0 += G) {
 #pragma unroll
       for (int g = 0; g < G; g++)
         if (g0 + g < groups) load_raw8<DT>(s, row, id, (g0 + g) * 8, buf[g]);
-    };
-    auto sum_batch = [&](uint32_t g0, const Raw8<DT>(&buf)[G]) {
 #pragma unroll
       for (int g = 0; g < G; g++) {
         const uint32_t d0 = (g0 + g) * 8;
@@ -234,23 +235,10 @@ __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; j++) {
-            if (d0 + j < dims) {
-              double x = v[j], y = q[d0 + j];
-              dot = __dadd_rn(dot, __dmul_rn(x, y));
-              nrm = __dadd_rn(nrm, __dmul_rn(x, x));
-            }
-          }
+          for (int j = 0; j < 8; j++)
+            if (d0 + j < dims) dot = __dadd_rn(dot, __dmul_rn((double)v[j], (double)q[d0 + j]));
         }
       }
-    };
-    load_batch(0, bufA);
-    for (uint32_t g0 = 0; g0 < groups; g0 += 2 * G) {
-      if (g0 + G < groups) load_batch(g0 + G, bufB);
-      sum_batch(g0, bufA);
-      if (g0 + G >= groups) break;
-      if (g0 + 2 * G < groups) load_batch(g0 + 2 * G, bufA);
-      sum_batch(g0 + G, bufB);
     }
     if (metric == M_L2) {
       float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
@@ -259,6 +247,7 @@ __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q
       return __dsqrt_rn((double)total);
     }
     if (metric == M_IP) return -dot;
+    const double nrm = s.n2x[id];
     double r = __ddiv_rn(dot, __dsqrt_rn(__dmul_rn(nrm, qn2d)));
     return __dsub_rn(1.0, fmax(-1.0, fmin(1.0, r)));
   }
@@ -291,6 +280,24 @@ __global__ void shard_stats(ShardView s, float *n2, float *rn, uint32_t *maxn2) 
   }
 }
 
+// Per row, one thread: the FP64 squared norm of the decoded values summed in
+// dimension order -- exactly the norm the reference's cosine accumulates
+// (ann/server/cpu.c:118-126) -- so rescoring needs only the dot product.
+template <int DT>
+__global__ void exact_norms(ShardView s, double *n2x) {
+  const uint64_t row = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= s.rows) return;
+  double acc = 0.0;
+  float v[8];
+  for (uint32_t d = 0; d < s.dims; d += 8) {
+    decode8<DT>(s, row, d, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (d + j < s.dims) acc = __dadd_rn(acc, __dmul_rn((double)v[j], (double)v[j]));
+  }
+  n2x[row] = acc;
+}
+
 // ---------------------------------------------------------------- queries
 
 struct PrepArgs {
@@ -300,6 +307,7 @@ struct PrepArgs {
   double gamma;            // relative accumulation error of the approximate scan
   const uint32_t *maxn2;   // shard's largest squared row norm (float bits)
   QueryState qs;
+  uint32_t *flags;         // [5] counts invalid queries
 };
 
 // One block a query: validity, norms, the FP16 copy and the error bound
@@ -373,7 +381,9 @@ __global__ void prep_queries(PrepArgs p) {
   p.qs.qn2d[q] = qn;
   p.qs.qn2[q] = (float)qn;
   p.qs.rnq[q] = qn > 0.0 ? (float)(1.0 / sqrt(qn)) : 0.0f;
-  p.qs.status[q] = (bad || (p.metric == M_COS && qn == 0.0)) ? 1 : 0;
+  const int invalid = bad || (p.metric == M_COS && qn == 0.0);
+  p.qs.status[q] = invalid;
+  if (invalid) atomicAdd(p.flags + 5, 1u);
 }
 
 __global__ void prep_queries_bits(uint32_t nq, QueryState qs) {
@@ -439,6 +449,7 @@ __global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
 
 struct SelectArgs {
   ShardView s;
+  const uint8_t *staged;  // candidate rows in position order (or NULL: read the shard)
   const uint32_t *ids;
   const float *queries;
   uint32_t nq, k, metric;
@@ -567,22 +578,24 @@ __device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned lo
   const uint32_t n = s_n;
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
     uint32_t p = pos[i];
-    uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
+    uint64_t id = cand_row(a.ids, p, a.s.rows);
     a.out_dist[(uint64_t)q * a.out_cap + i] = key_double(key[i]);
     a.out_id[(uint64_t)q * a.out_cap + i] = a.first_id + (int64_t)id;
   }
 }
 
-template <int DT>
-__global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
-  extern __shared__ uint8_t dyn[];
-  unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
-  uint32_t *pos = reinterpret_cast<uint32_t *>(key + kSortCap);
+// Final pruning of each query's list: drop what the k-th approximate score
+// rules out; cnt[q] becomes the survivor count (or the query is left to the
+// large-sort path when more than kSortCap survive).
+__global__ void __launch_bounds__(NT) survivors(SelectArgs a) {
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t scratch[32];
   const uint32_t q = blockIdx.x;
   if (a.qs.status[q]) {
-    if (threadIdx.x == 0) a.out_count[q] = 0;
+    if (threadIdx.x == 0) {
+      a.cnt[q] = 0;
+      a.out_count[q] = 0;
+    }
     return;
   }
   const uint32_t c = a.cnt[q];
@@ -590,34 +603,210 @@ __global__ void __launch_bounds__(NT) finalize(SelectArgs a) {
     if (threadIdx.x == 0) {
       atomicOr(a.flags, FLAG_OVERFLOW);
       atomicMax(a.flags + 1, c);
+      a.cnt[q] = 0;
       a.out_count[q] = 0;
     }
     return;
   }
   float t;
   const uint32_t m = tighten_one(a, q, c, hist, scratch, &t);
-  if (m > (uint32_t)kSortCap) {
-    if (threadIdx.x == 0) {
-      a.cnt[q] = m;
+  if (threadIdx.x == 0) {
+    atomicAdd(a.flags + 3, c);   // statistics: candidates and survivors
+    atomicAdd(a.flags + 4, m);
+    if (m > (uint32_t)kSortCap) {
       a.big[q] = m;
       atomicOr(a.flags, FLAG_BIGSORT);
       atomicMax(a.flags + 2, m);
       a.out_count[q] = 0;
+      a.cnt[q] = 0;          // the large-sort path reads big[q]
+    } else {
+      a.cnt[q] = m;
     }
+  }
+}
+
+// Exact distance of every survivor, one thread a survivor with its own
+// (alignment-checked) row loads: the path for rows whose pitch is not a
+// multiple of 16 bytes.
+template <int DT>
+__global__ void __launch_bounds__(128) rescore_thread(SelectArgs a, unsigned long long *exact) {
+  const uint32_t q = blockIdx.y;
+  const uint32_t m = a.cnt[q];
+  const uint2 *e = a.cand + (uint64_t)q * a.cap;
+  const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
+                                                    (uint64_t)q * a.qbytes);
+  const double qn2d = a.qs.qn2d[q];
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < m; i += gridDim.x * blockDim.x) {
+    const uint32_t p = e[i].y;
+    const uint64_t id = cand_row(a.ids, p, a.s.rows);
+    const uint8_t *row = a.staged ? a.staged + (uint64_t)p * a.s.row_bytes : a.s.codes + id * a.s.row_bytes;
+    exact[(uint64_t)q * kSortCap + i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row));
+  }
+}
+
+// Exact distance of every survivor of every query. A warp owns 32 survivors
+// (one a lane) and streams their rows through shared memory 128 bytes at a
+// time: each load instruction reads 4 rows x 128 contiguous bytes (the rows
+// are random in HBM, so per-lane 16-byte loads of 32 different rows would
+// run at a fifth of this bandwidth); then every lane sums its own row's
+// chunk in the reference's exact operation order. Chunks are double
+// buffered. exact[q * kSortCap + i] receives ordered keys. Needs a row pitch
+// that is a multiple of 16 bytes (and 16-byte aligned rows).
+constexpr int RS_WARPS = 4;
+constexpr int RS_STRIDE = 144;  // bytes a staged row chunk: 128 + 16 of padding (bank-conflict free)
+
+template <int DT>
+__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact) {
+  __shared__ __align__(16) uint8_t stage[RS_WARPS][2][32 * RS_STRIDE];
+  const uint32_t q = blockIdx.y;
+  const uint32_t m = a.cnt[q];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t i0 = (blockIdx.x * RS_WARPS + warp) * 32;
+  if (i0 >= m) return;
+  const uint2 *e = a.cand + (uint64_t)q * a.cap;
+  const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
+                                                    (uint64_t)q * a.qbytes);
+  const ShardView &s = a.s;
+  const uint32_t i = i0 + lane;
+  const bool mine = i < m;
+  const uint32_t p = mine ? e[i].y : e[i0].y;
+  const uint64_t id = cand_row(a.ids, p, s.rows);
+  const uint8_t *row = a.staged ? a.staged + (uint64_t)p * s.row_bytes : s.codes + id * s.row_bytes;
+  const uint32_t chunks = (uint32_t)((s.row_bytes + 127) / 128);
+  // lane l loads, for t = 0..7, 16 bytes (segment l % 8) of warp row l / 8 + 4t
+  auto load_chunk = [&](uint32_t c, uint4 (&v)[8]) {
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+      const int r = lane / 8 + 4 * t;
+      const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)row, r));
+      const uint64_t off = (uint64_t)c * 128 + (lane % 8) * 16;
+      v[t] = off + 16 <= s.row_bytes ? __ldg(reinterpret_cast<const uint4 *>(src + off)) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto store_chunk = [&](int buf, const uint4 (&v)[8]) {
+#pragma unroll
+    for (int t = 0; t < 8; t++)
+      *reinterpret_cast<uint4 *>(&stage[warp][buf][(lane / 8 + 4 * t) * RS_STRIDE + (lane % 8) * 16]) = v[t];
+  };
+  const float rs = (DT == DT_E4M3 || DT == DT_NVFP4) ? __ldg(s.rowscale + id) : 1.0f;
+  float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float tail = 0.0f;
+  double dot = 0.0;
+  uint32_t ham = 0;
+  const uint32_t dims = s.dims;
+  const uint8_t *qb = reinterpret_cast<const uint8_t *>(qv);
+  uint4 v[8];
+  load_chunk(0, v);
+  for (uint32_t c = 0; c < chunks; c++) {
+    const int buf = c & 1;
+    store_chunk(buf, v);
+    __syncwarp();
+    if (c + 1 < chunks) load_chunk(c + 1, v);   // in flight while this chunk is summed
+    const uint8_t *mine_chunk = &stage[warp][buf][lane * RS_STRIDE];
+    if (DT == DT_BIT) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint64_t off = (uint64_t)c * 128 + u * 16;
+        if (off < s.row_bytes) {
+          const uint4 x = *reinterpret_cast<const uint4 *>(mine_chunk + u * 16);
+          const uint32_t *y = reinterpret_cast<const uint32_t *>(qb + off);
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int w = 0; w < 4; w++)
+            if (off + 4 * w < s.row_bytes) ham += __popc(xs[w] ^ y[w]);
+        }
+      }
+    } else {
+      constexpr uint32_t per = DT == DT_F32 ? 32 : (DT == DT_F16 ? 64 : (DT == DT_E4M3 ? 128 : 256));
+      const uint32_t d0 = c * per;
+#pragma unroll 1
+      for (uint32_t g = 0; g < per / 8; g++) {
+        const uint32_t d = d0 + g * 8;
+        if (d >= dims) break;
+        float x[8];
+        if (DT == DT_F32) {
+          const float4 a4 = *reinterpret_cast<const float4 *>(mine_chunk + g * 32);
+          const float4 b4 = *reinterpret_cast<const float4 *>(mine_chunk + g * 32 + 16);
+          x[0] = a4.x; x[1] = a4.y; x[2] = a4.z; x[3] = a4.w; x[4] = b4.x; x[5] = b4.y; x[6] = b4.z; x[7] = b4.w;
+        } else if (DT == DT_F16) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(mine_chunk + g * 16);
+          const __half2 *h = reinterpret_cast<const __half2 *>(&w);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            float2 f = __half22float2(h[j]);
+            x[2 * j] = f.x;
+            x[2 * j + 1] = f.y;
+          }
+        } else if (DT == DT_E4M3) {
+          const uint2 w = *reinterpret_cast<const uint2 *>(mine_chunk + g * 8);
+#pragma unroll
+          for (int j = 0; j < 8; j++) x[j] = __fmul_rn(e4m3_value(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu), rs);
+        } else {
+          const uint32_t w = *reinterpret_cast<const uint32_t *>(mine_chunk + g * 4);
+          const float bs = __fmul_rn(e4m3_value(__ldg(s.bscales + id * s.bblocks + d / 16)), rs);
+#pragma unroll
+          for (int j = 0; j < 8; j++) x[j] = __fmul_rn(e2m1_value((w >> (4 * j)) & 0xfu), bs);
+        }
+        if (a.metric == M_L2) {
+          if (d + 8 <= dims) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              float diff = __fsub_rn(x[j], qv[d + j]);
+              sums[j] = __fadd_rn(sums[j], __fmul_rn(diff, diff));
+            }
+          } else {
+            for (int j = 0; d + j < dims; j++) {
+              float diff = __fsub_rn(x[j], qv[d + j]);
+              tail = __fadd_rn(tail, __fmul_rn(diff, diff));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            if (d + j < dims) dot = __dadd_rn(dot, __dmul_rn((double)x[j], (double)qv[d + j]));
+        }
+      }
+    }
+    __syncwarp();
+  }
+  if (!mine) return;
+  double dist;
+  if (DT == DT_BIT) {
+    dist = (double)ham;
+  } else if (a.metric == M_L2) {
+    float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
+    float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
+    float total = __fadd_rn(__fadd_rn(tail, left), right);
+    dist = __dsqrt_rn((double)total);
+  } else if (a.metric == M_IP) {
+    dist = -dot;
+  } else {
+    const double r = __ddiv_rn(dot, __dsqrt_rn(__dmul_rn(s.n2x[id], a.qs.qn2d[q])));
+    dist = __dsub_rn(1.0, fmax(-1.0, fmin(1.0, r)));
+  }
+  exact[(uint64_t)q * kSortCap + i] = double_key(dist);
+}
+
+// Per query: sort the survivors by (exact distance, position) and write the
+// k best or the gathered window.
+__global__ void __launch_bounds__(NTF) order(SelectArgs a, const unsigned long long *exact) {
+  extern __shared__ uint8_t dyn[];
+  unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
+  uint32_t *pos = reinterpret_cast<uint32_t *>(key + kSortCap);
+  const uint32_t q = blockIdx.x;
+  if (a.qs.status[q] || a.big[q]) return;
+  const uint32_t m = a.cnt[q];
+  if (m == 0) {
+    if (threadIdx.x == 0) a.out_count[q] = 0;
     return;
   }
   uint32_t p2 = 1;
   while (p2 < m) p2 <<= 1;
   const uint2 *e = a.cand + (uint64_t)q * a.cap;
-  const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
-                                                    (uint64_t)q * a.qbytes);
-  const double qn2d = a.qs.qn2d[q];
   for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
     if (i < m) {
-      uint32_t p = e[i].y;
-      uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
-      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d));
-      pos[i] = p;
+      key[i] = exact[(uint64_t)q * kSortCap + i];
+      pos[i] = e[i].y;
     } else {
       key[i] = ~0ull;
       pos[i] = ~0u;
@@ -641,8 +830,9 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
   for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
     if (i < m) {
       uint32_t p = e[i].y;
-      uint64_t id = a.ids ? (uint64_t)a.ids[p] : (uint64_t)p;
-      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d));
+      uint64_t id = cand_row(a.ids, p, a.s.rows);
+      const uint8_t *row = a.staged ? a.staged + (uint64_t)p * a.s.row_bytes : a.s.codes + id * a.s.row_bytes;
+      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row));
       pos[i] = p;
     } else {
       key[i] = ~0ull;
@@ -821,25 +1011,38 @@ __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nb
 
 // ---------------------------------------------------------------- launchers
 
-void launch_shard_stats(const ShardView &s, float *n2, float *rn, uint32_t *maxn2, cudaStream_t st) {
+void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st) {
   if (s.rows == 0 || s.dtype == DT_BIT) return;
   dim3 grid((unsigned)((s.rows + 7) / 8));
+  dim3 gridx((unsigned)((s.rows + 127) / 128));
   switch (s.dtype) {
-    case DT_F32: shard_stats<DT_F32><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
-    case DT_F16: shard_stats<DT_F16><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
-    case DT_E4M3: shard_stats<DT_E4M3><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
-    case DT_NVFP4: shard_stats<DT_NVFP4><<<grid, 256, 0, st>>>(s, n2, rn, maxn2); break;
+    case DT_F32:
+      shard_stats<DT_F32><<<grid, 256, 0, st>>>(s, n2, rn, maxn2);
+      exact_norms<DT_F32><<<gridx, 128, 0, st>>>(s, n2x);
+      break;
+    case DT_F16:
+      shard_stats<DT_F16><<<grid, 256, 0, st>>>(s, n2, rn, maxn2);
+      exact_norms<DT_F16><<<gridx, 128, 0, st>>>(s, n2x);
+      break;
+    case DT_E4M3:
+      shard_stats<DT_E4M3><<<grid, 256, 0, st>>>(s, n2, rn, maxn2);
+      exact_norms<DT_E4M3><<<gridx, 128, 0, st>>>(s, n2x);
+      break;
+    case DT_NVFP4:
+      shard_stats<DT_NVFP4><<<grid, 256, 0, st>>>(s, n2, rn, maxn2);
+      exact_norms<DT_NVFP4><<<gridx, 128, 0, st>>>(s, n2x);
+      break;
   }
 }
 
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         cudaStream_t st) {
+                         uint32_t *flags, cudaStream_t st) {
   if (bits) {
     prep_queries_bits<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
     return;
   }
-  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, gamma, maxn2, qs};
+  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, gamma, maxn2, qs, flags};
   prep_queries<<<nq, 256, 0, st>>>(p);
 }
 
@@ -858,7 +1061,7 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
 }
 
 static SelectArgs to_args(const SelectLaunch &l) {
-  SelectArgs a{l.s,   l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
+  SelectArgs a{l.s,   l.staged, l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
                l.cnt, l.cand,  l.cap,     l.flags, l.big,    l.out_dist, l.out_id,    l.out_count, l.out_cap,
                l.first_id};
   return a;
@@ -866,23 +1069,36 @@ static SelectArgs to_args(const SelectLaunch &l) {
 
 void launch_tighten(const SelectLaunch &l, cudaStream_t st) { tighten<<<l.nq, NT, 0, st>>>(to_args(l)); }
 
-template <int DT>
-static cudaError_t finalize_dt(const SelectLaunch &l, cudaStream_t st) {
-  const size_t smem = (size_t)kSortCap * (8 + 4);
-  cudaError_t e = cudaFuncSetAttribute(finalize<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  finalize<DT><<<l.nq, NT, smem, st>>>(to_args(l));
-  return cudaGetLastError();
-}
+void launch_survivors(const SelectLaunch &l, cudaStream_t st) { survivors<<<l.nq, NT, 0, st>>>(to_args(l)); }
 
-cudaError_t launch_finalize(const SelectLaunch &l, cudaStream_t st) {
-  switch (l.s.dtype) {
-    case DT_F32: return finalize_dt<DT_F32>(l, st);
-    case DT_F16: return finalize_dt<DT_F16>(l, st);
-    case DT_E4M3: return finalize_dt<DT_E4M3>(l, st);
-    case DT_NVFP4: return finalize_dt<DT_NVFP4>(l, st);
-    default: return finalize_dt<DT_BIT>(l, st);
+// Exact rescoring of the survivors (flat grid) and the per-query ordering.
+cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t st) {
+  unsigned long long *ex = reinterpret_cast<unsigned long long *>(exact);
+  const SelectArgs a = to_args(l);
+  if (l.s.row_bytes % 16 != 0) {
+    const dim3 g(kSortCap / 128 / 4, l.nq);
+    switch (l.s.dtype) {
+      case DT_F32: rescore_thread<DT_F32><<<g, 128, 0, st>>>(a, ex); break;
+      case DT_F16: rescore_thread<DT_F16><<<g, 128, 0, st>>>(a, ex); break;
+      case DT_E4M3: rescore_thread<DT_E4M3><<<g, 128, 0, st>>>(a, ex); break;
+      case DT_NVFP4: rescore_thread<DT_NVFP4><<<g, 128, 0, st>>>(a, ex); break;
+      default: rescore_thread<DT_BIT><<<g, 128, 0, st>>>(a, ex); break;
+    }
+  } else {
+    const dim3 grid(kSortCap / (RS_WARPS * 32), l.nq);
+    switch (l.s.dtype) {
+      case DT_F32: rescore<DT_F32><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+      case DT_F16: rescore<DT_F16><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+      case DT_E4M3: rescore<DT_E4M3><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+      case DT_NVFP4: rescore<DT_NVFP4><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+      default: rescore<DT_BIT><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+    }
   }
+  const size_t smem = (size_t)kSortCap * (8 + 4);
+  cudaError_t e = cudaFuncSetAttribute(order, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  order<<<l.nq, NTF, smem, st>>>(a, ex);
+  return cudaGetLastError();
 }
 
 void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,

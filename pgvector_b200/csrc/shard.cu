@@ -118,6 +118,14 @@ std::mutex g_stage_mu;
 double g_stage_ms[ST_COUNT];
 unsigned long long g_stage_calls[ST_COUNT];
 
+bool debug_on() {
+  static const int on = [] {
+    const char *v = getenv("ANN_B200_DEBUG");
+    return v && *v && *v != '0';
+  }();
+  return on;
+}
+
 bool timing_on() {
   static const int on = [] {
     const char *v = getenv("ANN_B200_KERNEL_TIMING");
@@ -191,7 +199,6 @@ bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr uint64_t kStagingBytes = 2ull << 30;
 constexpr uint64_t BM_ROWS = 128;  // gathered rows a tensor-scan chunk may stage
 // Relative bound on the approximate dot product's accumulation error (times
 // sum |x_i q_i| <= ||x|| ||q||). Tensor scan: each tcgen05.mma (K=16) adds an
@@ -204,8 +211,9 @@ double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims) {
   return (double)dims * std::ldexp(1.0, -22);
 }
 
+constexpr uint64_t kChunkRows = 589824;     // most rows one gathered tensor-scan chunk covers
 constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
-constexpr uint64_t kSampleRows = 32768;    // sample size of the bound
+constexpr uint64_t kSampleRows = 16384;    // sample size of the bound
 constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
 
 }  // namespace
@@ -218,6 +226,7 @@ struct AnnB200Shard {
   void *owned[3] = {nullptr, nullptr, nullptr};
   float *n2 = nullptr;
   float *rn = nullptr;
+  double *n2x = nullptr;
   uint32_t *maxn2 = nullptr;
   uint64_t norm_rows = 0;     // capacity of n2 / rn
   std::mutex mu;
@@ -228,6 +237,8 @@ struct AnnB200Shard {
   CUtensorMap rows_map;        // the shard's FP16 rows, box 64 x 128, for the tensor scan
   bool rows_map_ok = false;
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
+  cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
+  cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
 };
 
 extern "C" const char *AnnB200LastError(void) { return g_error.c_str(); }
@@ -249,8 +260,12 @@ extern "C" void AnnB200ShardDestroy(AnnB200Shard *s) {
       if (p) cudaFree(p);
     if (s->n2) cudaFree(s->n2);
     if (s->rn) cudaFree(s->rn);
+    if (s->n2x) cudaFree(s->n2x);
     if (s->maxn2) cudaFree(s->maxn2);
     if (s->hflags) cudaFreeHost(s->hflags);
+    for (cudaEvent_t &e : s->ev)
+      if (e) cudaEventDestroy(e);
+    if (s->side) cudaStreamDestroy(s->side);
     s->ws.release();
     s->cand.release();
     s->big.release();
@@ -306,18 +321,22 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   if (e == cudaSuccess && dtype != DT_BIT && rows > s->norm_rows) {
     if (s->n2) cudaFree(s->n2);
     if (s->rn) cudaFree(s->rn);
+    if (s->n2x) cudaFree(s->n2x);
     s->n2 = s->rn = nullptr;
+    s->n2x = nullptr;
     s->norm_rows = 0;
     e = cudaMalloc(&s->n2, rows * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->rn, rows * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s->n2x, rows * sizeof(double));
     if (e == cudaSuccess) s->norm_rows = rows;
   }
   if (e == cudaSuccess) e = cudaMemsetAsync(s->maxn2, 0, 16, st);
   if (e == cudaSuccess) {
     v.n2 = s->n2;
     v.rn = s->rn;
-    launch_shard_stats(v, s->n2, s->rn, s->maxn2, st);
-    if (dtype != DT_BIT && rows) counted(1);
+    v.n2x = s->n2x;
+    launch_shard_stats(v, s->n2, s->rn, s->n2x, s->maxn2, st);
+    if (dtype != DT_BIT && rows) counted(2);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
@@ -340,6 +359,8 @@ extern "C" int AnnB200ShardCreate(int device, uint32_t dtype, uint32_t dims, uin
   cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, device);
   cudaError_t e = cudaMalloc(&s->maxn2, 16);
   if (e == cudaSuccess) e = cudaMallocHost(&s->hflags, 64);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking);
+  for (int i = 0; i < 5 && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&s->ev[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
     int r = cuda_fail(e, "shard");
     AnnB200ShardDestroy(s);
@@ -391,10 +412,11 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
                o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
                o_q16 = c.take<__half>((size_t)nq_pad * kpad), o_mat = c.take<float>((size_t)S * nq),
-               o_cnt = c.take<uint32_t>(nq), o_snap = c.take<uint32_t>(nq), o_flags = c.take<uint32_t>(16),
-               o_big = c.take<uint32_t>(nq);
+               o_cnt = c.take<uint32_t>(nq), o_thr0 = c.take<float>(nq), o_flags = c.take<uint32_t>(16),
+               o_big = c.take<uint32_t>(nq), o_exact = c.take<double>((size_t)nq * kSortCap);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
+  double *exact = (double *)(w + o_exact);
   QueryState qs;
   qs.qn2 = (float *)(w + o_qn2);
   qs.rnq = (float *)(w + o_rnq);
@@ -405,7 +427,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   qs.q16 = (__half *)(w + o_q16);
   float *mat = (float *)(w + o_mat);
   uint32_t *cnt = (uint32_t *)(w + o_cnt);
-  uint32_t *snap = (uint32_t *)(w + o_snap);
+  float *thr0 = (float *)(w + o_thr0);
   uint32_t *dflags = (uint32_t *)(w + o_flags);
   uint32_t *big = (uint32_t *)(w + o_big);
 
@@ -420,16 +442,12 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
   StageClock clock(st);
   if (rows) {
-    // the scans index rows by these ids: reject a bad list before any scan runs
+    // kernels clamp list entries to the shard; a bad list is reported at the end
     launch_check_rows(rows, nrows, v.rows, dflags, st);
     counted(1);
-    CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
-    CK(cudaStreamSynchronize(st), "row check");
-    if (sh->hflags[0] & FLAG_BAD_ROWS)
-      return fail(INVALID, "candidate rows must be increasing and < %llu", (unsigned long long)v.rows);
   }
   int h = clock.begin(ST_PREP);
-  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, st);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, dflags, st);
   clock.end(h);
   counted(1);
   CK(cudaGetLastError(), "query preparation");
@@ -448,33 +466,32 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   CUtensorMap query_map;
   if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
-  // one scan launch (plus the candidate-row gather it needs), timed as `stage`
-  auto scan = [&](int stage) -> cudaError_t {
-    if (tc) {
-      if (!a.ids && a.stride == 1) {  // contiguous rows of the shard itself
-        int hk = clock.begin(stage);
-        cudaError_t e = launch_tc_scan(a, sh->rows_map, (int64_t)a.base, query_map, kpad, bn, sh->sms, st);
-        clock.end(hk);
-        return e;
-      }
-      // gather the candidates into the staging copy, then scan it contiguously
-      cudaError_t e = sh->staging.reserve(a.count * v.row_bytes);
-      if (e != cudaSuccess) return e;
-      int hs = clock.begin(ST_GATHER);
-      launch_gather_rows(v.codes, v.row_bytes, a.ids, a.base, a.stride, a.count, (uint8_t *)sh->staging.p, st);
-      clock.end(hs);
-      counted(1);
-      CUtensorMap staged;
-      if (!encode_f16_map(&staged, sh->staging.p, v.dims, a.count, v.row_bytes, 128)) return cudaErrorInvalidValue;
-      int hk = clock.begin(stage);
-      e = launch_tc_scan(a, staged, 0, query_map, kpad, bn, sh->sms, st);
-      clock.end(hk);
-      return e;
-    }
+  // One scan launch timed as `stage`. Tensor path: rows come from the shard
+  // itself when the candidates are a contiguous run, else from `staged`
+  // (virtual row 0 at its first row, filled by gather_rows).
+  auto scan = [&](int stage, const void *staged) -> cudaError_t {
     int hk = clock.begin(stage);
-    launch_simt_scan(a, st);
+    cudaError_t e;
+    if (tc && !staged) {
+      e = launch_tc_scan(a, sh->rows_map, (int64_t)a.base, query_map, kpad, bn, sh->sms, st);
+    } else if (tc) {
+      CUtensorMap staged_map;
+      if (!encode_f16_map(&staged_map, staged, v.dims, a.count, v.row_bytes, 128)) return cudaErrorInvalidValue;
+      e = launch_tc_scan(a, staged_map, 0, query_map, kpad, bn, sh->sms, st);
+    } else {
+      launch_simt_scan(a, st);
+      e = cudaGetLastError();
+    }
     clock.end(hk);
-    return cudaGetLastError();
+    counted(1);
+    return e;
+  };
+  // gather candidate rows [base + i*stride] into `slot` on stream gst
+  auto gather = [&](uint64_t base, uint64_t stride, uint64_t count, void *slot, cudaStream_t gst) {
+    int hg = gst == st ? clock.begin(ST_GATHER) : -1;
+    launch_gather_rows(v.codes, v.row_bytes, v.rows, rows, base, stride, count, (uint8_t *)slot, gst);
+    clock.end(hg);
+    counted(1);
   };
 
   SelectLaunch sl{};
@@ -497,6 +514,9 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   sl.first_id = sh->first;
 
   if (k > 0 && n > 0) {
+    // staging: the pass's gathered candidate rows, then the sample's
+    if (tc && (rows || sample))
+      CK(sh->staging.reserve(((rows ? n : 0) + (sample ? S : 0)) * v.row_bytes), "staging");
     if (sample) {
       a.mode = MODE_MATRIX;
       a.count = S;
@@ -504,7 +524,13 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       a.stride = stride;
       a.mat = mat;
       a.mat_ld = S;
-      CK(scan(ST_SAMPLE), "sample scan");
+      const void *staged = nullptr;
+      if (tc && (rows || stride > 1)) {
+        uint8_t *sample_rows = (uint8_t *)sh->staging.p + (rows ? n * v.row_bytes : 0);
+        gather(0, stride, S, sample_rows, st);
+        staged = sample_rows;
+      }
+      CK(scan(ST_SAMPLE, staged), "sample scan");
       h = clock.begin(ST_BOUND);
       launch_kth_bound(mat, S, S, nq, k, metric, window, qs, st);
       clock.end(h);
@@ -514,69 +540,104 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       counted(1);
     }
     CK(cudaGetLastError(), "bound");
-    // filter scan in chunks sized so a chunk appends about cap/4 entries a query
-    uint64_t seen = sample ? S : n, start = 0;
+    // ---- filter pass, survivors, exact rescoring and ordering, enqueued with
+    // one host synchronisation at the end. Chunks of the filter pass are
+    // sized so each appends at most about cap/2 entries a query (tighten
+    // after each such capacity chunk); a tensor scan over a row list splits
+    // them into overlap chunks growing 3x from 64k rows, gathering chunk i+1
+    // on the side stream while chunk i is scanned (two staging slots). If a
+    // list overflowed, the whole pass runs again with larger lists.
+    CK(cudaMemcpyAsync(thr0, qs.thr, nq * sizeof(float), cudaMemcpyDeviceToDevice, st), "thresholds");
     a.mode = MODE_FILTER;
     a.stride = 1;
-    while (start < n) {
-      uint64_t len = n - start;
-      if (sample) {
-        double room = (double)seen * (double)cap / (4.0 * (double)k);
-        len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)room));
+    const bool staged_pass = tc && rows;
+    for (int attempt = 0;; attempt++) {
+      std::vector<std::pair<uint64_t, uint64_t>> chunks;
+      std::vector<char> tighten_after;
+      uint64_t seen = sample ? S : n;
+      for (uint64_t start = 0; start < n;) {
+        uint64_t len = n - start;
+        if (sample) {
+          double room = (double)seen * (double)cap / (2.0 * (double)k);
+          len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)room));
+        }
+        uint64_t piece = staged_pass ? std::min<uint64_t>(len, 65536) : len;
+        for (uint64_t off = 0; off < len;) {
+          uint64_t m = std::min(piece, len - off);
+          chunks.push_back({start + off, m});
+          tighten_after.push_back(0);
+          off += m;
+          piece = std::min<uint64_t>(piece * 3, kChunkRows);
+        }
+        tighten_after.back() = 1;
+        seen += len;
+        start += len;
       }
-      if (tc && rows) len = std::min<uint64_t>(len, std::max<uint64_t>(BM_ROWS, kStagingBytes / v.row_bytes));
-      CK(cudaMemcpyAsync(snap, cnt, nq * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st), "snapshot");
-      for (;;) {
-        a.count = len;
-        a.base = start;
-        a.cand = (uint2 *)sh->cand.p;
-        a.cap = cap;
-        CK(scan(ST_FILTER), "filter scan");
-        counted(1);
-        CK(cudaMemcpyAsync(sh->hflags, dflags, 16, cudaMemcpyDeviceToHost, st), "flags");
-        CK(cudaStreamSynchronize(st), "filter scan");
-        if (sh->hflags[0] & FLAG_BAD_ROWS) return fail(INVALID, "candidate rows must be increasing and < %llu",
-                                                       (unsigned long long)v.rows);
-        if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
-        if (!(sh->hflags[0] & FLAG_OVERFLOW)) break;
-        // grow the lists (keeping entries of earlier chunks) and re-scan this chunk
-        uint64_t need = std::max<uint64_t>(sh->hflags[1], (uint64_t)cap * 2);
-        uint32_t ncap = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(n, 1), need + need / 4);
-        if (ncap <= cap) ncap = cap + 1;
-        DeviceBuffer fresh;
-        CK(fresh.reserve((size_t)nq * ncap * sizeof(uint2)), "candidate lists");
-        CK(cudaMemcpy2DAsync(fresh.p, (size_t)ncap * sizeof(uint2), sh->cand.p, (size_t)cap * sizeof(uint2),
-                             (size_t)cap * sizeof(uint2), nq, cudaMemcpyDeviceToDevice, st),
-           "grow lists");
-        CK(cudaStreamSynchronize(st), "grow lists");
-        std::swap(sh->cand.p, fresh.p);
-        std::swap(sh->cand.n, fresh.n);
-        cap = ncap;
-        CK(cudaMemcpyAsync(cnt, snap, nq * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st), "restore");
-        CK(cudaMemsetAsync(dflags, 0, 8, st), "memset");
+      // the staging copy holds every candidate row of the pass at its
+      // position (exact rescoring reads survivors from it); the sample's
+      // copy sits after it
+      uint8_t *stage_base = nullptr;
+      if (staged_pass) {
+        stage_base = (uint8_t *)sh->staging.p;
+        // the side stream starts after everything queued so far
+        CK(cudaEventRecord(sh->ev[4], st), "event");
+        CK(cudaStreamWaitEvent(sh->side, sh->ev[4], 0), "event");
+        gather(chunks[0].first, 1, chunks[0].second, stage_base + chunks[0].first * v.row_bytes, sh->side);
+        CK(cudaEventRecord(sh->ev[0], sh->side), "event");
       }
-      seen += len;
-      start += len;
+      sl.staged = staged_pass ? stage_base : nullptr;
+      a.cand = (uint2 *)sh->cand.p;
+      a.cap = cap;
       sl.cand = (uint2 *)sh->cand.p;
       sl.cap = cap;
-      if (start < n) {
-        h = clock.begin(ST_TIGHTEN);
-        launch_tighten(sl, st);
-        clock.end(h);
-        counted(1);
+      for (size_t i = 0; i < chunks.size(); i++) {
+        const int cur = (int)(i & 1), nxt = (int)((i + 1) & 1);
+        if (staged_pass && i + 1 < chunks.size()) {
+          gather(chunks[i + 1].first, 1, chunks[i + 1].second, stage_base + chunks[i + 1].first * v.row_bytes,
+                 sh->side);
+          CK(cudaEventRecord(sh->ev[nxt], sh->side), "event");
+        }
+        if (staged_pass) CK(cudaStreamWaitEvent(st, sh->ev[cur], 0), "event");
+        a.count = chunks[i].second;
+        a.base = chunks[i].first;
+        CK(scan(ST_FILTER, staged_pass ? stage_base + chunks[i].first * v.row_bytes : nullptr), "filter scan");
+        if (i + 1 < chunks.size() && tighten_after[i]) {
+          h = clock.begin(ST_TIGHTEN);
+          launch_tighten(sl, st);
+          clock.end(h);
+          counted(1);
+        }
       }
+      h = clock.begin(ST_TIGHTEN);
+      launch_survivors(sl, st);
+      clock.end(h);
+      h = clock.begin(ST_FINAL);
+      CK(launch_finalize(sl, exact, st), "finalize");
+      clock.end(h);
+      counted(3);
+      CK(cudaMemcpyAsync(sh->hflags, dflags, 32, cudaMemcpyDeviceToHost, st), "flags");
+      CK(cudaStreamSynchronize(st), "search");
+      if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
+      if (!(sh->hflags[0] & FLAG_OVERFLOW)) break;
+      // run the pass again with lists sized for the largest count seen
+      uint64_t need = std::max<uint64_t>(sh->hflags[1], (uint64_t)cap * 2);
+      uint32_t ncap = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(n, 1), need + need / 4);
+      if (ncap <= cap) ncap = cap + 1;
+      cap = ncap;
+      CK(sh->cand.reserve((size_t)nq * cap * sizeof(uint2)), "candidate lists");
+      CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
+      CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
+      CK(cudaMemcpyAsync(qs.thr, thr0, nq * sizeof(float), cudaMemcpyDeviceToDevice, st), "thresholds");
+      CK(cudaMemsetAsync(dflags, 0, 8, st), "memset");
+      CK(cudaMemsetAsync(dflags + 2, 0, 12, st), "memset");
     }
-    sl.cand = (uint2 *)sh->cand.p;
-    sl.cap = cap;
-    h = clock.begin(ST_FINAL);
-    CK(launch_finalize(sl, st), "finalize");
-    clock.end(h);
-    counted(1);
-    CK(cudaMemcpyAsync(sh->hflags, dflags, 16, cudaMemcpyDeviceToHost, st), "flags");
-    CK(cudaStreamSynchronize(st), "finalize");
+    if (debug_on())
+      fprintf(stderr, "annb200: nq=%u n=%llu k=%u tensor=%d sample=%llu cap=%u candidates=%u survivors=%u\n", nq,
+              (unsigned long long)n, k, (int)tc, (unsigned long long)S, cap, sh->hflags[3], sh->hflags[4]);
     if (sh->hflags[0] & FLAG_BIGSORT) {
       std::vector<uint32_t> hbig(nq);
-      CK(cudaMemcpy(hbig.data(), big, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost), "big list");
+      CK(cudaMemcpyAsync(hbig.data(), big, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "big list");
+      CK(cudaStreamSynchronize(st), "big list");
       for (uint32_t q = 0; q < nq; q++) {
         if (!hbig[q]) continue;
         uint32_t p2 = 1;
@@ -586,20 +647,19 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
                             p2, st);
         counted(1);
         CK(cudaGetLastError(), "large sort");
+        CK(cudaStreamSynchronize(st), "large sort");
       }
-      CK(cudaStreamSynchronize(st), "large sort");
     }
-    if (sh->hflags[0] & FLAG_OVERFLOW) return fail(BACKEND_ERROR, "candidate list overflow after finalize");
     if (sh->hflags[0] & FLAG_OUT_CAP) return fail(INVALID, "window results exceed out_cap");
   } else {
     CK(cudaMemsetAsync(out_count, 0, nq * sizeof(uint32_t), st), "memset");
+    CK(cudaMemcpyAsync(sh->hflags, dflags, 32, cudaMemcpyDeviceToHost, st), "flags");
+    CK(cudaStreamSynchronize(st), "search");
   }
+  if (sh->hflags[0] & FLAG_BAD_ROWS)
+    return fail(INVALID, "candidate rows must be increasing and < %llu", (unsigned long long)v.rows);
   if (status) CK(cudaMemcpyAsync(status, qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToDevice, st), "status");
-  std::vector<int32_t> hs(nq);
-  CK(cudaMemcpyAsync(hs.data(), qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "status");
-  CK(cudaStreamSynchronize(st), "search");
-  for (uint32_t q = 0; q < nq; q++)
-    if (hs[q]) *any_invalid = true;
+  if (sh->hflags[5]) *any_invalid = true;   // queries prep_queries marked invalid
   return OK;
 }
 
@@ -737,14 +797,9 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
   if (tc && nq_pad > nq)
     CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
-  if (rows) {
-    launch_check_rows(rows, nrows, v.rows, dflags, st);
-    CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
-    CK(cudaStreamSynchronize(st), "row check");
-    if (sh->hflags[0] & FLAG_BAD_ROWS) return fail(INVALID, "candidate rows must be increasing and < rows");
-  }
+  if (rows) launch_check_rows(rows, nrows, v.rows, dflags, st);
   launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, scan_gamma(bits, tc, kpad, v.dims),
-                      sh->maxn2, qs, bits, st);
+                      sh->maxn2, qs, bits, dflags, st);
   counted(1);
   ScanArgs a{};
   a.s = v;
@@ -767,7 +822,7 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
       CK(launch_tc_scan(a, sh->rows_map, 0, query_map, kpad, bn, sh->sms, st), "score scan");
     } else {
       CK(sh->staging.reserve(n * v.row_bytes), "staging");
-      launch_gather_rows(v.codes, v.row_bytes, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
+      launch_gather_rows(v.codes, v.row_bytes, v.rows, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
       CUtensorMap staged;
       if (!encode_f16_map(&staged, sh->staging.p, v.dims, n, v.row_bytes, 128))
         return fail(BACKEND_ERROR, "tensor map of the staged rows could not be encoded");
@@ -785,5 +840,6 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   CK(cudaMemcpyAsync(sh->hflags, dflags, 4, cudaMemcpyDeviceToHost, st), "flags");
   CK(cudaStreamSynchronize(st), "score matrix");
   if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
+  if (sh->hflags[0] & FLAG_BAD_ROWS) return fail(INVALID, "candidate rows must be increasing and < rows");
   return OK;
 }
