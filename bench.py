@@ -331,26 +331,29 @@ def main():
                'd2h_bytes_per_step': int(hd.numel() * 8 + hi_.numel() * 8) if rank == 0 else 0,
                'ms_per_step': ems / args.steps}
 
-    # ---- roofline of the filter scan (stage 3)
+    # ---- roofline of the filter pass (stage 3: every tcgen05 scan launch of
+    # one step's filter pass, timed by the library's stage clock on its
+    # stream). Algorithmic work per pass: 2 * batch * candidate rows * dims
+    # FLOPs; algorithmic bytes: the candidate rows (dims * 2 B + 4 B row id)
+    # plus the FP16 query block.
     hbm, tf_burst, tf_sust, kind = peaks()
-    nf = max(int(stage_calls[3]), 1)
-    filt_ms = stage_ms[3] / nf
-    scans_per_step = nf / args.steps
-    flops = 2.0 * args.batch * (nrows_local / scans_per_step) * args.dims
-    achieved_tf = flops / (filt_ms * 1e-3) / 1e12
-    bytes_alg = (nrows_local / scans_per_step) * (args.dims * 2 + 4) + args.batch * args.dims * 2
+    pass_ms = stage_ms[3] / args.steps
+    flops = 2.0 * args.batch * nrows_local * args.dims
+    achieved_tf = flops / (pass_ms * 1e-3) / 1e12
+    bytes_alg = nrows_local * (args.dims * 2 + 4) + args.batch * args.dims * 2
     traffic = None
     tpath = os.path.join(ROOT, 'profiles', 'tc_scan_f16_config2.md')
     if os.path.exists(tpath):
         for line in open(tpath):
-            if line.startswith('traffic_bytes_per_full_launch:'):
-                traffic = float(line.split(':', 1)[1])
+            if line.startswith('traffic_bytes_per_row:'):
+                traffic = float(line.split(':', 1)[1]) * nrows_local
     roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
                 'frac': achieved_tf / tf_sust, 'traffic': traffic,
-                'kernel': 'tc_scan_f16 (filter pass)', 'peak_source': kind + ' bf16_tflops_sustained',
-                'kernel_ms': filt_ms, 'flops_per_launch': flops,
-                'hbm_achieved_gbs': bytes_alg / (filt_ms * 1e-3) / 1e9, 'hbm_peak_gbs': hbm,
-                'hbm_frac': bytes_alg / (filt_ms * 1e-3) / 1e9 / hbm,
+                'kernel': 'tc_scan_f16, filter pass (%d launches a step)' % round(stage_calls[3] / args.steps),
+                'peak_source': kind + ' bf16_tflops_sustained', 'pass_ms': pass_ms, 'flops_per_pass': flops,
+                'algorithmic_bytes_per_pass': bytes_alg,
+                'hbm_achieved_gbs': bytes_alg / (pass_ms * 1e-3) / 1e9, 'hbm_peak_gbs': hbm,
+                'hbm_frac': bytes_alg / (pass_ms * 1e-3) / 1e9 / hbm,
                 'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(
                     ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge',
                      'gather'])}}
