@@ -164,6 +164,23 @@ int			AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows,
 							  uint64_t *count, void *stream);
 
 /*
+ * AnnB200BitmapRows for callers that must not allocate device memory on their
+ * call path -- a worker serving from a device-memory budget it reserved at
+ * start-up, or a latency-critical caller that cannot afford the device
+ * synchronisation cudaMalloc / cudaFree bring. No counterpart in the
+ * reference. Same arguments and result as AnnB200BitmapRows, but its scratch
+ * (one offset per 32,768 bitmap bits and the row count) lives in a fixed
+ * 256 KB array in device memory that every GPU loading this library holds
+ * until exit, so it allocates nothing. Limit: nbits <= 2^31; larger bitmaps
+ * fail with ANN_INVALID. The first call on a device looks the array's
+ * address up on that device (make it before any stream capture). All calls
+ * share the array: calls running on a device at the same time (other
+ * streams or threads) race and must be serialised by the caller.
+ */
+int			AnnB200BitmapRowsStatic(const uint32_t *words, uint64_t nbits, uint32_t *rows,
+									uint64_t *count, void *stream);
+
+/*
  * Kernels this library has launched in this process (all devices). A caller
  * that times a region reads it before and after to count its launches.
  */

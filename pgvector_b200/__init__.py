@@ -134,6 +134,16 @@ def bitmap_rows(words, nbits, stream=None):
     return rows[:n.value]
 
 
+def bitmap_rows_static(words, nbits, rows, stream=None):
+    """bitmap_rows for callers that must not allocate device memory: writes
+    the row numbers into the caller's `rows` tensor (int32, >= nbits long)
+    using the library's fixed scratch array; returns the count. At most 2^31
+    rows; concurrent calls on one device must be serialised."""
+    n = ctypes.c_uint64()
+    check(load().AnnB200BitmapRowsStatic(_ptr(words), int(nbits), _ptr(rows), ctypes.byref(n), _stream(stream)))
+    return n.value
+
+
 def backend():
     """The AnnBackend vtable AnnB200Backend() returns."""
     return load().AnnB200Backend().contents
@@ -164,6 +174,6 @@ def search_gathered(jobs):
     return out
 
 
-__all__ = ['Shard', 'merge_topk', 'bitmap_rows', 'backend', 'search_gathered', 'device_count', 'load', 'check',
+__all__ = ['Shard', 'merge_topk', 'bitmap_rows', 'bitmap_rows_static', 'backend', 'search_gathered', 'device_count', 'load', 'check',
            'AnnB200Error', 'F32', 'F16', 'E4M3', 'NVFP4', 'BIT', 'L2', 'IP', 'COSINE', 'HAMMING', 'WINDOW',
            'FORCE_SIMT', 'OK', 'INVALID', 'UNSUPPORTED', 'NOMEM', 'BACKEND_ERROR']

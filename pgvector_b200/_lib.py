@@ -34,6 +34,7 @@ SIGNATURES = {
     'AnnB200MergeTopk': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
                                  c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p]),
     'AnnB200BitmapRows': (c_int, [c_void_p, c_uint64, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),
+    'AnnB200BitmapRowsStatic': (c_int, [c_void_p, c_uint64, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),
     'AnnB200Backend': (ctypes.POINTER(AnnBackend), []),
     'AnnB200LaunchCount': (ctypes.c_ulonglong, []),
     'AnnB200ScoreMatrix': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,

@@ -311,6 +311,10 @@ struct SelectLaunch {
 };
 
 // ---------------------------------------------------------------- launchers
+// Record the calling thread's error message (AnnB200LastError) and return status.
+int report_error(int status, const char *fmt, ...);
+// Count kernels launched by this library (AnnB200LaunchCount).
+void count_launches(unsigned long long n);
 void launch_simt_scan(const ScanArgs &a, cudaStream_t st);
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);

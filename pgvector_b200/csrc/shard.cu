@@ -241,6 +241,19 @@ struct AnnB200Shard {
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
 };
 
+namespace annb200 {
+int report_error(int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return status;
+}
+void count_launches(unsigned long long n) { counted(n); }
+}  // namespace annb200
+
 extern "C" const char *AnnB200LastError(void) { return g_error.c_str(); }
 
 extern "C" int AnnB200DeviceCount(void) {
