@@ -128,6 +128,32 @@ int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
 						  int32_t *status, void *stream);
 
 /*
+ * IVF list gather: exact k-nearest search of each query over the rows of the
+ * lists it probes -- the list scan of the reference's IVFFlat index
+ * (src/ivfscan.c:124-186: visit the probed lists, score every entry, order
+ * them), for a batch of queries at once.
+ *
+ * The shard holds its rows list-major: list l is rows
+ * list_offsets[l] .. list_offsets[l+1]-1 (device u64 [nlists+1],
+ * non-decreasing, last <= the shard's rows). probes is device u32
+ * [nq][nprobe]: each query's list numbers, distinct and < nlists (a query
+ * that breaks this gets status ANN_INVALID and no results). row_ids
+ * (optional, device int64 [rows]) gives each stored row's global id;
+ * without it the id is first_id + row. Results as AnnB200Search without
+ * ANNB200_WINDOW: min(k, rows in the probed lists) per query, sorted by
+ * (distance, id), distances bit-identical to the reference CPU worker's
+ * (L2 as sqrt of the eight-lane FP32 sum, inner product and cosine in
+ * FP64). Metrics L2, IP, cosine; every vector storage format. nlists <=
+ * 2^24, nprobe <= 4096. Synchronous.
+ */
+int			AnnB200SearchLists(AnnB200Shard *shard, const float *queries, uint32_t nq,
+							   const uint64_t *list_offsets, uint32_t nlists,
+							   const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids,
+							   uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap,
+							   double *out_dist, int64_t *out_id, uint32_t *out_count,
+							   int32_t *status, void *stream);
+
+/*
  * The approximate score matrix the scan prunes with (the reference's
  * score-matrix route, score_mma_* / AnnBlackwellScore,
  * ann/server/blackwell.c:289-525,1066-1110): out [nq][n] FP32 approximate

@@ -98,6 +98,25 @@ class Shard:
                                    _ptr(status), _stream(stream)))
         return dist, ids, count
 
+    def search_lists(self, queries, k, metric, offsets, probes, row_ids=None, stream=None, status=None):
+        """IVF list gather: each query's k nearest among the rows of the lists
+        it probes. offsets: int64 [nlists+1] row runs of the lists; probes:
+        int32 [nq][nprobe] list numbers; row_ids: optional int64 [rows] global
+        ids. Returns (dist, id, count) CUDA tensors like search()."""
+        import torch
+        nq = int(queries.shape[0])
+        nlists = int(offsets.shape[0]) - 1
+        nprobe = int(probes.shape[1]) if probes.dim() == 2 else 0
+        cap = max(int(k), 1)
+        dev = queries.device
+        dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
+        ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
+        count = torch.empty((nq,), dtype=torch.int32, device=dev)
+        check(load().AnnB200SearchLists(self._handle, _ptr(queries), nq, _ptr(offsets), nlists, _ptr(probes), nprobe,
+                                        _ptr(row_ids), int(k), int(metric), 0, cap, _ptr(dist), _ptr(ids),
+                                        _ptr(count), _ptr(status), _stream(stream)))
+        return dist, ids, count
+
     def score_matrix(self, queries, metric, rows=None, force_simt=False, stream=None):
         """Approximate distances [nq][n] (squared for L2) and each query's
         error bound, as the scan computes them."""

@@ -31,6 +31,9 @@ SIGNATURES = {
     'AnnB200ShardDestroy': (None, [c_void_p]),
     'AnnB200Search': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
                               c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    'AnnB200SearchLists': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, c_uint32,
+                                   c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                   c_void_p, c_void_p, c_void_p]),
     'AnnB200MergeTopk': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
                                  c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p]),
     'AnnB200BitmapRows': (c_int, [c_void_p, c_uint64, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),

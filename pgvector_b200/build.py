@@ -21,7 +21,7 @@ NVCC = os.path.join(CUDA_HOME, 'bin', 'nvcc')
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 NVCC_FLAGS = ARCH + ['-O3', '-lineinfo', '-std=c++17', '-Xcompiler', '-fPIC', '-I' + INCLUDE,
                      '--expt-relaxed-constexpr']
-CU_SOURCES = ['scan_simt.cu', 'scan_tc.cu', 'select.cu', 'shard.cu', 'bitmap_static.cu']
+CU_SOURCES = ['scan_simt.cu', 'scan_tc.cu', 'select.cu', 'shard.cu', 'ivf.cu', 'bitmap_static.cu']
 C_SOURCES = ['backend.c']
 
 

@@ -87,6 +87,26 @@ struct ScanArgs {
   uint32_t *flags;          // [0] Flag bits, [1] largest count seen (overflow)
 };
 
+// IVF list gather (ivf.cu): the shard holds lists l = 0..nlists-1 as row
+// runs [offsets[l], offsets[l+1]); probes [nq][nprobe] name each query's
+// lists. The plan arrays are device workspace.
+constexpr uint32_t kMaxProbes = 4096;
+constexpr uint32_t kMaxLists = 1u << 24;
+struct ListPlan {
+  const uint64_t *offsets;    // [nlists + 1]
+  uint32_t nlists;
+  uint64_t rows;              // shard rows
+  const uint32_t *probes;     // [nq][nprobe]
+  uint32_t nprobe, nq;
+  unsigned long long *lcount; // [nlists] queries probing each list
+  unsigned long long *lfill;  // [nlists] fill cursors
+  unsigned long long *qoff;   // [nlists + 1] start of each list's queries in qlist
+  uint32_t *qlist;            // [nq * nprobe] query numbers, list-major
+  unsigned long long *tiles;  // [nlists] work items of each list
+  unsigned long long *toff;   // [nlists + 1] prefix sums of tiles (toff[nlists] = items)
+  unsigned long long *bsum;   // [kMaxLists / 4096] prefix-sum block totals
+};
+
 // Row id of candidate position pos: ids[pos], or pos when there is no list.
 // A list entry past the shard is clamped to its last row, so a bad list can
 // never address memory outside the shard; check_rows flags such a list and
@@ -292,6 +312,7 @@ __device__ __forceinline__ float threshold_v(uint32_t metric, double D, double e
 struct SelectLaunch {
   ShardView s;
   const uint8_t *staged;    // candidate rows in position order (or NULL: read the shard)
+  const int64_t *row_ids;   // global id of each shard row (or NULL: first_id + row)
   const uint32_t *ids;
   const float *queries;
   uint32_t nq, k, metric;
@@ -316,6 +337,10 @@ int report_error(int status, const char *fmt, ...);
 // Count kernels launched by this library (AnnB200LaunchCount).
 void count_launches(unsigned long long n);
 void launch_simt_scan(const ScanArgs &a, cudaStream_t st);
+void launch_list_plan(const ListPlan &p, const QueryState &qs, uint32_t *flags, cudaStream_t st);
+void launch_list_items(const ListPlan &p, uint64_t limit, cudaStream_t st);
+void launch_simt_scan_lists(const ListPlan &p, uint64_t limit, const ScanArgs &a, int sms, cudaStream_t st);
+uint32_t list_plan_scan_launches(uint32_t nlists);
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);
 void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
@@ -333,8 +358,8 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
 void launch_tighten(const SelectLaunch &l, cudaStream_t st);
 void launch_survivors(const SelectLaunch &l, cudaStream_t st);
 cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t st);
-void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,
-                         cudaStream_t st);
+void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, unsigned long long *pos,
+                         uint32_t p2, cudaStream_t st);
 cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,
                          uint32_t nq, uint32_t list_cap, uint32_t k, int window, uint32_t out_cap,
                          double *out_dist, int64_t *out_id, uint32_t *out_count, uint32_t *flags,

@@ -450,6 +450,7 @@ __global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
 struct SelectArgs {
   ShardView s;
   const uint8_t *staged;  // candidate rows in position order (or NULL: read the shard)
+  const int64_t *row_ids; // global id of each shard row (or NULL: first_id + row)
   const uint32_t *ids;
   const float *queries;
   uint32_t nq, k, metric;
@@ -525,10 +526,11 @@ __global__ void __launch_bounds__(NT) tighten(SelectArgs a) {
   }
 }
 
-// Sort n (key, pos) pairs in shared or global memory, ascending by key then
-// pos (bitonic network over the next power of two; entries past n are
-// padding with the largest key).
-__device__ void bitonic_sort(unsigned long long *key, uint32_t *pos, uint32_t p2) {
+// Sort (key, gid) pairs in shared or global memory, ascending by key then by
+// gid -- the ordered global row id, so ties fall in row-id order (bitonic
+// network over the next power of two; entries past the count are padding
+// with the largest key).
+__device__ void bitonic_sort(unsigned long long *key, unsigned long long *pos, uint32_t p2) {
   for (uint32_t size = 2; size <= p2; size <<= 1) {
     for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
       for (uint32_t i = threadIdx.x; i < p2 / 2; i += blockDim.x) {
@@ -536,7 +538,7 @@ __device__ void bitonic_sort(unsigned long long *key, uint32_t *pos, uint32_t p2
         uint32_t hi = lo + stride;
         bool up = (lo & size) == 0;
         unsigned long long ka = key[lo], kb = key[hi];
-        uint32_t pa = pos[lo], pb = pos[hi];
+        unsigned long long pa = pos[lo], pb = pos[hi];
         bool greater = ka > kb || (ka == kb && pa > pb);
         if (greater == up) {
           key[lo] = kb;
@@ -550,9 +552,17 @@ __device__ void bitonic_sort(unsigned long long *key, uint32_t *pos, uint32_t p2
   }
 }
 
+// Global row id of candidate position p (row_ids map, else first_id + row),
+// as an unsigned key with the order of the signed id.
+__device__ __forceinline__ unsigned long long gid_key(const SelectArgs &a, uint32_t p) {
+  const uint64_t row = cand_row(a.ids, p, a.s.rows);
+  const int64_t g = a.row_ids ? a.row_ids[row] : a.first_id + (int64_t)row;
+  return (unsigned long long)g ^ 0x8000000000000000ull;
+}
+
 // Write a sorted survivor list: the k best, or the gathered window.
-__device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned long long *key, const uint32_t *pos,
-                              uint32_t m) {
+__device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned long long *key,
+                              const unsigned long long *gid, uint32_t m) {
   __shared__ uint32_t s_n;
   if (threadIdx.x == 0) {
     uint32_t n = m < a.k ? m : a.k;
@@ -577,10 +587,8 @@ __device__ void write_results(const SelectArgs &a, uint32_t q, const unsigned lo
   __syncthreads();
   const uint32_t n = s_n;
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-    uint32_t p = pos[i];
-    uint64_t id = cand_row(a.ids, p, a.s.rows);
     a.out_dist[(uint64_t)q * a.out_cap + i] = key_double(key[i]);
-    a.out_id[(uint64_t)q * a.out_cap + i] = a.first_id + (int64_t)id;
+    a.out_id[(uint64_t)q * a.out_cap + i] = (int64_t)(gid[i] ^ 0x8000000000000000ull);
   }
 }
 
@@ -787,12 +795,12 @@ __global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned 
   exact[(uint64_t)q * kSortCap + i] = double_key(dist);
 }
 
-// Per query: sort the survivors by (exact distance, position) and write the
-// k best or the gathered window.
+// Per query: sort the survivors by (exact distance, global row id) and write
+// the k best or the gathered window.
 __global__ void __launch_bounds__(NTF) order(SelectArgs a, const unsigned long long *exact) {
   extern __shared__ uint8_t dyn[];
   unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
-  uint32_t *pos = reinterpret_cast<uint32_t *>(key + kSortCap);
+  unsigned long long *pos = key + kSortCap;
   const uint32_t q = blockIdx.x;
   if (a.qs.status[q] || a.big[q]) return;
   const uint32_t m = a.cnt[q];
@@ -806,10 +814,10 @@ __global__ void __launch_bounds__(NTF) order(SelectArgs a, const unsigned long l
   for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
     if (i < m) {
       key[i] = exact[(uint64_t)q * kSortCap + i];
-      pos[i] = e[i].y;
+      pos[i] = gid_key(a, e[i].y);
     } else {
       key[i] = ~0ull;
-      pos[i] = ~0u;
+      pos[i] = ~0ull;
     }
   }
   __syncthreads();
@@ -818,10 +826,10 @@ __global__ void __launch_bounds__(NTF) order(SelectArgs a, const unsigned long l
 }
 
 // The same for one query whose survivors outgrew shared memory: rescoring and
-// sorting in a global scratch of p2 (key, pos) pairs.
+// sorting in a global scratch of p2 (key, gid) pairs.
 template <int DT>
-__global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, unsigned long long *key, uint32_t *pos,
-                                                   uint32_t p2) {
+__global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, unsigned long long *key,
+                                                   unsigned long long *pos, uint32_t p2) {
   const uint32_t m = a.big[q];
   const uint2 *e = a.cand + (uint64_t)q * a.cap;
   const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
@@ -833,10 +841,10 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
       uint64_t id = cand_row(a.ids, p, a.s.rows);
       const uint8_t *row = a.staged ? a.staged + (uint64_t)p * a.s.row_bytes : a.s.codes + id * a.s.row_bytes;
       key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row));
-      pos[i] = p;
+      pos[i] = gid_key(a, p);
     } else {
       key[i] = ~0ull;
-      pos[i] = ~0u;
+      pos[i] = ~0ull;
     }
   }
   __syncthreads();
@@ -1061,7 +1069,7 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
 }
 
 static SelectArgs to_args(const SelectLaunch &l) {
-  SelectArgs a{l.s,   l.staged, l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
+  SelectArgs a{l.s,   l.staged, l.row_ids, l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
                l.cnt, l.cand,  l.cap,     l.flags, l.big,    l.out_dist, l.out_id,    l.out_count, l.out_cap,
                l.first_id};
   return a;
@@ -1094,15 +1102,15 @@ cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t s
       default: rescore<DT_BIT><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
     }
   }
-  const size_t smem = (size_t)kSortCap * (8 + 4);
+  const size_t smem = (size_t)kSortCap * (8 + 8);
   cudaError_t e = cudaFuncSetAttribute(order, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   order<<<l.nq, NTF, smem, st>>>(a, ex);
   return cudaGetLastError();
 }
 
-void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, uint32_t *pos, uint32_t p2,
-                         cudaStream_t st) {
+void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, unsigned long long *pos,
+                         uint32_t p2, cudaStream_t st) {
   switch (l.s.dtype) {
     case DT_F32: finalize_big<DT_F32><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
     case DT_F16: finalize_big<DT_F16><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;

@@ -199,7 +199,6 @@ bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr uint64_t BM_ROWS = 128;  // gathered rows a tensor-scan chunk may stage
 // Relative bound on the approximate dot product's accumulation error (times
 // sum |x_i q_i| <= ||x|| ||q||). Tensor scan: each tcgen05.mma (K=16) adds an
 // exactly formed FP16 product sum into the FP32 accumulator, so K/16 rounding
@@ -401,6 +400,25 @@ extern "C" int AnnB200ShardAssign(AnnB200Shard *s, uint32_t dtype, uint32_t dims
 }
 
 namespace {
+
+// Queries whose survivors outgrew the shared-memory sort: rescored and sorted
+// one at a time in a global scratch.
+int big_sorts(AnnB200Shard *sh, const SelectLaunch &sl, const uint32_t *big, uint32_t nq, cudaStream_t st) {
+  std::vector<uint32_t> hbig(nq);
+  CK(cudaMemcpyAsync(hbig.data(), big, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "big list");
+  CK(cudaStreamSynchronize(st), "big list");
+  for (uint32_t q = 0; q < nq; q++) {
+    if (!hbig[q]) continue;
+    uint32_t p2 = 1;
+    while (p2 < hbig[q]) p2 <<= 1;
+    CK(sh->big.reserve((size_t)p2 * 16), "sort scratch");
+    launch_finalize_big(sl, q, (unsigned long long *)sh->big.p, (unsigned long long *)sh->big.p + p2, p2, st);
+    counted(1);
+    CK(cudaGetLastError(), "large sort");
+    CK(cudaStreamSynchronize(st), "large sort");
+  }
+  return OK;
+}
 
 // One search over queries [q0, q0+nq) (nq within one tensor-scan launch).
 int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows, uint64_t nrows,
@@ -648,20 +666,8 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       fprintf(stderr, "annb200: nq=%u n=%llu k=%u tensor=%d sample=%llu cap=%u candidates=%u survivors=%u\n", nq,
               (unsigned long long)n, k, (int)tc, (unsigned long long)S, cap, sh->hflags[3], sh->hflags[4]);
     if (sh->hflags[0] & FLAG_BIGSORT) {
-      std::vector<uint32_t> hbig(nq);
-      CK(cudaMemcpyAsync(hbig.data(), big, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "big list");
-      CK(cudaStreamSynchronize(st), "big list");
-      for (uint32_t q = 0; q < nq; q++) {
-        if (!hbig[q]) continue;
-        uint32_t p2 = 1;
-        while (p2 < hbig[q]) p2 <<= 1;
-        CK(sh->big.reserve((size_t)p2 * 12), "sort scratch");
-        launch_finalize_big(sl, q, (unsigned long long *)sh->big.p, (uint32_t *)((uint8_t *)sh->big.p + (size_t)p2 * 8),
-                            p2, st);
-        counted(1);
-        CK(cudaGetLastError(), "large sort");
-        CK(cudaStreamSynchronize(st), "large sort");
-      }
+      int r = big_sorts(sh, sl, big, nq, st);
+      if (r != OK) return r;
     }
     if (sh->hflags[0] & FLAG_OUT_CAP) return fail(INVALID, "window results exceed out_cap");
   } else {
@@ -703,6 +709,199 @@ extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq,
     if (r != OK) return r;
   }
   if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  return OK;
+}
+
+namespace {
+
+// One IVF search over queries [q0, q0+nq): plan (probe inversion), a sample
+// pass over the first S rows of every probed list with no threshold, the
+// bound from its k-th score, the full pass over the probed lists, then the
+// flat search's survivor selection, exact rescoring and ordering.
+int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *offsets,
+                       uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids, uint32_t k,
+                       uint32_t metric, uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
+                       int32_t *status, cudaStream_t st, bool *any_invalid) {
+  const ShardView &v = sh->view;
+  const double gamma = scan_gamma(false, false, 0, v.dims);
+  // sample rows a list: enough that nprobe lists give about 4k rows
+  const uint64_t want = (4ull * k + nprobe - 1) / std::max<uint32_t>(nprobe, 1);
+  const uint64_t S = std::max<uint64_t>(64, (want + 63) / 64 * 64);
+
+  Carver c;
+  const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
+               o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
+               o_cnt = c.take<uint32_t>(nq), o_flags = c.take<uint32_t>(16), o_big = c.take<uint32_t>(nq),
+               o_exact = c.take<double>((size_t)nq * kSortCap), o_lcount = c.take<uint64_t>(nlists),
+               o_lfill = c.take<uint64_t>(nlists), o_tiles = c.take<uint64_t>(nlists),
+               o_qoff = c.take<uint64_t>((size_t)nlists + 1), o_toff = c.take<uint64_t>((size_t)nlists + 1),
+               o_bsum = c.take<uint64_t>(kMaxLists / 4096), o_qlist = c.take<uint32_t>((size_t)nq * nprobe);
+  CK(sh->ws.reserve(c.off), "workspace");
+  uint8_t *w = (uint8_t *)sh->ws.p;
+  double *exact = (double *)(w + o_exact);
+  QueryState qs{};
+  qs.qn2 = (float *)(w + o_qn2);
+  qs.rnq = (float *)(w + o_rnq);
+  qs.qn2d = (double *)(w + o_qn2d);
+  qs.err = (double *)(w + o_err);
+  qs.thr = (float *)(w + o_thr);
+  qs.status = (int32_t *)(w + o_status);
+  uint32_t *cnt = (uint32_t *)(w + o_cnt);
+  uint32_t *dflags = (uint32_t *)(w + o_flags);
+  uint32_t *big = (uint32_t *)(w + o_big);
+  ListPlan p{};
+  p.offsets = offsets;
+  p.nlists = nlists;
+  p.rows = v.rows;
+  p.probes = probes;
+  p.nprobe = nprobe;
+  p.nq = nq;
+  p.lcount = (unsigned long long *)(w + o_lcount);
+  p.lfill = (unsigned long long *)(w + o_lfill);
+  p.tiles = (unsigned long long *)(w + o_tiles);
+  p.qoff = (unsigned long long *)(w + o_qoff);
+  p.toff = (unsigned long long *)(w + o_toff);
+  p.bsum = (unsigned long long *)(w + o_bsum);
+  p.qlist = (uint32_t *)(w + o_qlist);
+
+  uint32_t cap = (uint32_t)std::max<uint64_t>({kBaseCap, 8ull * k, (uint64_t)nprobe * S});
+  CK(sh->cand.reserve((size_t)nq * cap * sizeof(uint2)), "candidate lists");
+  CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
+  CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
+  CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
+  if (nlists) {
+    CK(cudaMemsetAsync(p.lcount, 0, (size_t)nlists * 8, st), "memset");
+    CK(cudaMemsetAsync(p.lfill, 0, (size_t)nlists * 8, st), "memset");
+  }
+  StageClock clock(st);
+  int h = clock.begin(ST_PREP);
+  launch_prep_queries(queries, nq, v.dims, metric, 0, 0, gamma, sh->maxn2, qs, 0, dflags, st);
+  launch_list_plan(p, qs, dflags, st);
+  clock.end(h);
+  counted(1 + (nlists ? 1 : 0) + 2 + list_plan_scan_launches(nlists));
+  CK(cudaGetLastError(), "list plan");
+
+  ScanArgs a{};
+  a.s = v;
+  a.queries = queries;
+  a.nq = nq;
+  a.metric = metric;
+  a.mode = MODE_FILTER;
+  a.thr = qs.thr;
+  a.cnt = cnt;
+  a.flags = dflags;
+
+  SelectLaunch sl{};
+  sl.s = v;
+  sl.row_ids = row_ids;
+  sl.queries = queries;
+  sl.nq = nq;
+  sl.k = k;
+  sl.metric = metric;
+  sl.qbytes = v.dims * 4;
+  sl.qs = qs;
+  sl.cnt = cnt;
+  sl.flags = dflags;
+  sl.big = big;
+  sl.out_dist = out_dist;
+  sl.out_id = out_id;
+  sl.out_count = out_count;
+  sl.out_cap = out_cap;
+  sl.first_id = sh->first;
+
+  auto pass = [&](int stage, uint64_t limit) -> cudaError_t {
+    int hk = clock.begin(stage);
+    launch_list_items(p, limit, st);
+    launch_simt_scan_lists(p, limit, a, sh->sms, st);
+    clock.end(hk);
+    counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1);
+    return cudaGetLastError();
+  };
+
+  for (;;) {
+    a.cand = (uint2 *)sh->cand.p;
+    a.cap = cap;
+    sl.cand = a.cand;
+    sl.cap = cap;
+    launch_fill_thresholds(nq, qs, st);
+    counted(1);
+    CK(pass(ST_SAMPLE, S), "sample pass");
+    h = clock.begin(ST_BOUND);
+    launch_tighten(sl, st);
+    CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
+    clock.end(h);
+    counted(1);
+    CK(pass(ST_FILTER, ~0ull), "list pass");
+    h = clock.begin(ST_TIGHTEN);
+    launch_survivors(sl, st);
+    clock.end(h);
+    h = clock.begin(ST_FINAL);
+    CK(launch_finalize(sl, exact, st), "finalize");
+    clock.end(h);
+    counted(3);
+    CK(cudaMemcpyAsync(sh->hflags, dflags, 32, cudaMemcpyDeviceToHost, st), "flags");
+    CK(cudaStreamSynchronize(st), "list search");
+    if (!(sh->hflags[0] & FLAG_OVERFLOW)) break;
+    uint64_t need = std::max<uint64_t>(sh->hflags[1], (uint64_t)cap * 2);
+    cap = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(v.rows, 1), need + need / 4);
+    CK(sh->cand.reserve((size_t)nq * cap * sizeof(uint2)), "candidate lists");
+    CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
+    CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
+    CK(cudaMemsetAsync(dflags, 0, 8, st), "memset");
+    CK(cudaMemsetAsync(dflags + 2, 0, 12, st), "memset");
+  }
+  if (debug_on())
+    fprintf(stderr, "annb200: lists nq=%u nlists=%u nprobe=%u k=%u sample=%llu cap=%u candidates=%u survivors=%u\n",
+            nq, nlists, nprobe, k, (unsigned long long)S, cap, sh->hflags[3], sh->hflags[4]);
+  if (sh->hflags[0] & FLAG_BIGSORT) {
+    int r = big_sorts(sh, sl, big, nq, st);
+    if (r != OK) return r;
+  }
+  if (sh->hflags[0] & FLAG_BAD_ROWS)
+    return fail(INVALID, "list offsets must be non-decreasing and <= %llu", (unsigned long long)v.rows);
+  if (status) CK(cudaMemcpyAsync(status, qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToDevice, st), "status");
+  if (sh->hflags[5]) *any_invalid = true;
+  return OK;
+}
+
+}  // namespace
+
+extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *list_offsets,
+                                  uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids,
+                                  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist,
+                                  int64_t *out_id, uint32_t *out_count, int32_t *status, void *stream) {
+  if (!sh) return fail(INVALID, "shard is NULL");
+  const ShardView &v = sh->view;
+  if (v.dtype == DT_BIT || metric > M_COS)
+    return fail(UNSUPPORTED, "list search takes L2, inner product or cosine over vector rows");
+  if (flags & ANNB200_WINDOW) return fail(UNSUPPORTED, "list search returns the strict top k only");
+  if (nq == 0) return OK;
+  if (!queries || !out_dist || !out_id || !out_count || !list_offsets || (nprobe && !probes))
+    return fail(INVALID, "NULL query, list, probe or result pointer");
+  if (out_cap < k) return fail(INVALID, "out_cap %u < k %u", out_cap, k);
+  if (nlists > kMaxLists) return fail(UNSUPPORTED, "more than %u lists", kMaxLists);
+  if (nprobe > kMaxProbes) return fail(UNSUPPORTED, "more than %u probes a query", kMaxProbes);
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t block = 4096;
+  bool any_invalid = false;
+  for (uint32_t q0 = 0; q0 < nq; q0 += block) {
+    const uint32_t m = std::min(block, nq - q0);
+    int r;
+    if (k == 0) {
+      CK(cudaMemsetAsync(out_count + q0, 0, m * sizeof(uint32_t), st), "memset");
+      r = OK;
+    } else {
+      r = search_lists_block(sh, queries + (uint64_t)q0 * v.dims, m, list_offsets, nlists, probes + (uint64_t)q0 * nprobe,
+                             nprobe, row_ids, k, metric, out_cap, out_dist + (uint64_t)q0 * out_cap,
+                             out_id + (uint64_t)q0 * out_cap, out_count + q0, status ? status + q0 : nullptr, st,
+                             &any_invalid);
+    }
+    if (r != OK) return r;
+  }
+  CK(cudaStreamSynchronize(st), "list search");
+  if (any_invalid) return fail(INVALID, "a query is not finite, has zero norm under cosine, or probes a bad list");
   return OK;
 }
 

@@ -62,6 +62,35 @@ def bitmap(n, selectivity, seed=0):
     return np.packbits(padded, bitorder='little').view(np.uint32), np.nonzero(bits)[0].astype(np.uint32)
 
 
+def ivf_corpus(n, d, nlists, zipf=1.1, sigma=0.1, seed=0, normalize=False):
+    """IVF-shaped corpus stored list-major: list sizes follow Zipf(zipf) over
+    a random list order, list l's rows are its centroid plus noise. Returns
+    (rows [n][d] f32, offsets u64 [nlists+1], centroids [nlists][d],
+    row_ids i64 [n]: a random permutation of 0..n-1, the rows' global ids)."""
+    rng = np.random.default_rng(seed)
+    cent = rng.standard_normal((nlists, d)).astype(np.float32)
+    w = 1.0 / np.arange(1, nlists + 1, dtype=np.float64) ** zipf
+    w = w[rng.permutation(nlists)]
+    sizes = np.floor(w / w.sum() * n).astype(np.int64)
+    sizes[np.argmax(sizes)] += n - sizes.sum()
+    lab = np.repeat(np.arange(nlists), sizes)
+    x = cent[lab] + sigma * rng.standard_normal((n, d)).astype(np.float32)
+    if normalize:
+        x /= np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-30)
+        cent = cent / np.maximum(np.linalg.norm(cent, axis=1, keepdims=True), 1e-30)
+    offsets = np.zeros(nlists + 1, dtype=np.uint64)
+    offsets[1:] = np.cumsum(sizes)
+    return x.astype(np.float32), offsets, cent, rng.permutation(n).astype(np.int64)
+
+
+def ivf_probes(queries, centroids, nprobe):
+    """Each query's nprobe nearest centroids (squared L2), nearest first."""
+    q = np.asarray(queries, dtype=np.float64)
+    c = np.asarray(centroids, dtype=np.float64)
+    d2 = (q * q).sum(1)[:, None] - 2.0 * q @ c.T + (c * c).sum(1)[None, :]
+    return np.argsort(d2, axis=1, kind='stable')[:, :nprobe].astype(np.uint32)
+
+
 # ---------------------------------------------------------------- torch (full size, on the GPU)
 
 def torch_mixture(n, d, centres, sigma=0.1, seed=0, normalize=False, dtype=None, device='cuda',

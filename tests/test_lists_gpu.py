@@ -1,0 +1,130 @@
+"""GPU parity of the IVF list gather (AnnB200SearchLists) against the oracle.
+
+The reference's IVFFlat scan visits each query's probed lists, scores every
+entry and orders them (src/ivfscan.c:124-186); oracle.search_lists restates
+it. Bar: bit-exact ids, counts and FP64 distances, ties ordered by global id,
+for every vector storage format and metric.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from pgvector_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(a, cuda):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    if a.dtype == np.uint64:
+        a = a.view(np.int64)
+    return torch.from_numpy(a).to(cuda)
+
+
+def encode(dtype, x):
+    if dtype == oracle.F32:
+        return x, None, None
+    if dtype == oracle.F16:
+        return synth.to_half_bits(x), None, None
+    if dtype == oracle.E4M3:
+        codes, rs = oracle.quantize_fp8(x)
+        return codes, None, rs
+    codes, bs, rs = oracle.quantize_nvfp4(x)
+    return codes, bs, rs
+
+
+def gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None, status=None):
+    import pgvector_b200 as pb
+    shard = pb.Shard(dtype, dims, to_dev(codes, cuda), None if bs is None else to_dev(bs, cuda),
+                     None if rs is None else to_dev(rs, cuda))
+    d, i, c = shard.search_lists(to_dev(q, cuda), k, metric, to_dev(offsets, cuda), to_dev(probes, cuda),
+                                 row_ids=None if row_ids is None else to_dev(row_ids, cuda), status=status)
+    return d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy()
+
+
+def assert_lists_same(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None):
+    od, oi, oc = oracle.search_lists(dtype, dims, codes, q, offsets, probes, k, metric, row_ids=row_ids,
+                                     block_scales=bs, row_scales=rs)
+    gd, gi, gc = gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids)
+    assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
+    for j in range(q.shape[0]):
+        c = int(oc[j])
+        assert np.array_equal(gi[j, :c], oi[j, :c]), (j, gi[j, :c][:10], oi[j, :c][:10])
+        assert np.array_equal(gd[j, :c], od[j, :c]), (j, gd[j, :c][:10], od[j, :c][:10])
+    return oc
+
+
+@pytest.mark.parametrize('dtype,metric', [(0, 0), (0, 1), (0, 2), (1, 2), (1, 0), (2, 1), (3, 0), (3, 2)])
+def test_list_gather_formats_and_metrics(cuda, dtype, metric):
+    dims = 96 if dtype != oracle.F32 else 37
+    x, offsets, cent, row_ids = synth.ivf_corpus(30000, dims, 128, seed=10 + dtype)
+    q = synth.mixture_queries(48, dims, 16, seed=11)
+    q = cent[np.arange(48) % 128] + 0.1 * q.astype(np.float32)
+    probes = synth.ivf_probes(q, cent, 8)
+    codes, bs, rs = encode(dtype, x)
+    assert_lists_same(cuda, dtype, dims, codes, bs, rs, q.astype(np.float32), offsets, probes, 20, metric, row_ids)
+
+
+def test_config4_shape_nvfp4_l2(cuda):
+    # config 4's format and probe pattern at a size the oracle finishes quickly:
+    # NVFP4 d=768, Zipf(1.1) list sizes, nprobe 64, k 100
+    x, offsets, cent, row_ids = synth.ivf_corpus(60000, 768, 1024, seed=20)
+    q = cent[np.random.default_rng(21).integers(0, 1024, 32)] + 0.1 * synth.mixture_queries(32, 768, 8, seed=21)
+    probes = synth.ivf_probes(q, cent, 64)
+    codes, bs, rs = oracle.quantize_nvfp4(x)
+    assert_lists_same(cuda, oracle.NVFP4, 768, codes, bs, rs, q.astype(np.float32), offsets, probes, 100, 0,
+                      row_ids)
+
+
+def test_ties_order_by_global_id_across_lists(cuda):
+    # the same vector stored in several lists under different global ids:
+    # equal distances must come out in id order whatever the storage order
+    rng = np.random.default_rng(30)
+    base = rng.standard_normal((50, 16)).astype(np.float32)
+    x = np.concatenate([base, base, base, base])          # 4 lists of 50 identical rows
+    offsets = np.array([0, 50, 100, 150, 200], dtype=np.uint64)
+    row_ids = rng.permutation(200).astype(np.int64) * 3 + 7
+    q = base[:6] + 0.01
+    probes = np.tile(np.array([3, 0, 2, 1], dtype=np.uint32), (6, 1))
+    for metric in (0, 1, 2):
+        assert_lists_same(cuda, oracle.F32, 16, x, None, None, q, offsets, probes, 30, metric, row_ids)
+    # without row_ids the ids are the storage rows
+    assert_lists_same(cuda, oracle.F32, 16, x, None, None, q, offsets, probes, 30, 0)
+
+
+def test_small_and_empty_lists_and_large_k(cuda):
+    # empty lists, lists shorter than k, and a k past the shared-memory sort
+    # (more than 4,096 survivors: the large-sort path)
+    x, offsets, cent, row_ids = synth.ivf_corpus(20000, 32, 64, zipf=1.6, seed=40)
+    sizes = np.diff(offsets.astype(np.int64))
+    offsets2 = offsets.copy()
+    offsets2[1:] = np.cumsum(np.where(np.arange(64) % 7 == 0, 0, sizes))   # every 7th list empty
+    n2 = int(offsets2[-1])
+    q = cent[:40] + 0.05
+    probes = synth.ivf_probes(q, cent, 5)
+    oc = assert_lists_same(cuda, oracle.F32, 32, x[:n2], None, None, q, offsets2, probes, 50, 0, row_ids[:n2])
+    assert (oc < 50).any()       # some queries probe fewer than k rows
+    assert_lists_same(cuda, oracle.F32, 32, x, None, None, q, offsets, probes, 5000, 0, row_ids)
+
+
+def test_bad_probes_are_invalid_queries(cuda):
+    import torch
+    import pgvector_b200 as pb
+    x, offsets, cent, _ = synth.ivf_corpus(5000, 16, 32, seed=50)
+    q = cent[:4] + 0.05
+    probes = synth.ivf_probes(q, cent, 4)
+    probes[1, 2] = probes[1, 0]      # a duplicate list
+    probes[2, 3] = 32                # a list past nlists
+    status = torch.zeros((4,), dtype=torch.int32, device=cuda)
+    with pytest.raises(pb.AnnB200Error):
+        gpu_lists(cuda, oracle.F32, 16, x, None, None, q, offsets, probes, 5, 0, status=status)
+    assert status.cpu().numpy().tolist() == [0, 1, 1, 0]
+    good = probes[[0, 3]]
+    od, oi, oc = oracle.search_lists(oracle.F32, 16, x, q[[0, 3]], offsets, good, 5, 0)
+    gd, gi, gc = gpu_lists(cuda, oracle.F32, 16, x, None, None, q[[0, 3]], offsets, good, 5, 0)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
