@@ -345,7 +345,6 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);
 void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
                         uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st);
-size_t tc_scan_smem(uint32_t nq);
 uint32_t tc_scan_max_queries();
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,

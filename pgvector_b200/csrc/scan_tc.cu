@@ -38,12 +38,10 @@ namespace annb200 {
 namespace {
 
 constexpr int BM = 128;
-constexpr int STAGES = 4;
 constexpr int MAXBN = 256;
 constexpr int A_BYTES = BM * 128;
 constexpr int B_BYTES = MAXBN * 128;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int NTHREADS = 192;
 constexpr int EPI_BUF = 256;      // staged appends a warp buffers before a flush
 constexpr int TMEM_COLS = 512;
 constexpr unsigned long long kWaitNs = 4000000000ull;
@@ -167,19 +165,129 @@ __device__ __forceinline__ uint32_t f16_idesc(uint32_t n) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__global__ void __launch_bounds__(NTHREADS, 1)
-    tc_scan_f16(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
-                const TcArgs t) {
+// Per storage format: pipeline stages, raw-code ring (quantized formats stage
+// their codes and convert them to FP16 in shared memory), threads.
+template <int Q> struct TcCfg;
+template <> struct TcCfg<DT_F16> {
+  static constexpr int STG = 4, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 192;
+};
+template <> struct TcCfg<DT_E4M3> {   // 64 one-byte codes a row a k-block
+  static constexpr int STG = 3, RSTG = 4, RAWB = BM * 64, RAW_X = 64, NT = 320;
+};
+template <> struct TcCfg<DT_NVFP4> {  // 64 nibbles (32 bytes) a row a k-block
+  static constexpr int STG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 320;
+};
+
+// Four E4M3 codes -> two FP16 pairs (exact: every E4M3 value is an FP16 value).
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t &o0, uint32_t &o1) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(o0), "=r"(o1)
+      : "r"(w));
+}
+// Eight E2M1 codes (low nibble first) -> four FP16 pairs, each times the
+// FP16 pair s: an E2M1 value (2 significant bits) times an E4M3 block scale
+// (4 bits) is exact in FP16, whose range holds 2^-10 .. 2688.
+__device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t s, uint32_t (&o)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t.reg .b32 h0, h1, h2, h3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h0, b0;\n\tcvt.rn.f16x2.e2m1x2 h1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h2, b2;\n\tcvt.rn.f16x2.e2m1x2 h3, b3;\n\t"
+      "mul.rn.f16x2 %0, h0, %5;\n\tmul.rn.f16x2 %1, h1, %5;\n\t"
+      "mul.rn.f16x2 %2, h2, %5;\n\tmul.rn.f16x2 %3, h3, %5;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w), "r"(s));
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r in a 128-row x 128-byte
+// K-major tile with the 128-byte swizzle (the layout TMA writes and the
+// tcgen05 descriptor reads): chunk index XOR (row mod 8).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// Convert one stage's raw codes (BM rows of RAW_X bytes, dense) into the
+// FP16 A tile (raw values: the row scale is applied in the epilogue). 128
+// converter threads; ct = converter thread, vrow0 = virtual row of tile row 0.
+template <int Q>
+__device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *raw, uint8_t *atile, uint32_t ct,
+                                              uint64_t vrow0, uint32_t kb) {
+  if (Q == DT_E4M3) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const uint32_t i = ct + 128 * u, r = i >> 2, c = i & 3;  // 16 codes: dims 16c .. 16c+15
+      const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + c * 16);
+      uint4 lo, hi;
+      e4m3x4_to_f16(w.x, lo.x, lo.y);
+      e4m3x4_to_f16(w.y, lo.z, lo.w);
+      e4m3x4_to_f16(w.z, hi.x, hi.y);
+      e4m3x4_to_f16(w.w, hi.z, hi.w);
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c)) = lo;
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c + 1)) = hi;
+    }
+  } else if (Q == DT_NVFP4) {
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const uint32_t i = ct + 128 * u, r = i >> 1, h = i & 1;  // 32 nibbles: dims 32h .. 32h+31
+      const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+      const uint64_t vi = vrow0 + r;
+      uint32_t sc[2] = {0u, 0u};
+      if (vi < a.count) {
+        const uint64_t id = cand_row(a.ids, a.base + vi * a.stride, a.s.rows);
+        const uint32_t b0 = kb * 4 + h * 2;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          if (b0 + j < a.s.bblocks) {
+            const uint32_t code = __ldg(a.s.bscales + id * a.s.bblocks + b0 + j);
+            uint32_t pair, unused;
+            e4m3x4_to_f16(code | (code << 8), pair, unused);
+            sc[j] = pair;
+          }
+        }
+      }
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        uint32_t o[4];
+        e2m1x8_to_f16(ws[j], sc[j >> 1], o);
+        *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
+// Wait (bounded) for the last load issued into each of n ring slots: no
+// bulk copy may still be writing this CTA's shared memory when it exits.
+__device__ void drain_ring(uint64_t *bars, int n, uint64_t issued) {
+  for (int s = 0; s < n; s++) {
+    if ((uint64_t)s >= issued) break;
+    const uint64_t last = issued - 1 - ((issued - 1 - s) % n);  // last iteration that used slot s
+    const uint32_t ph = (uint32_t)((last / n) & 1);
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bars + s, ph) && globaltimer() - t0 < kWaitNs) {
+    }
+  }
+}
+
+template <int Q>
+__global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
+    tc_scan(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
+            const TcArgs t) {
+  using C = TcCfg<Q>;
+  constexpr int STG = C::STG, RSTG = C::RSTG, RAWB = C::RAWB;
+  constexpr int RSTG1 = RSTG > 0 ? RSTG : 1;  // (the FP16 kernel has no raw ring)
+  constexpr bool QUANT = Q != DT_F16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  uint64_t *empty = full + STAGES;
-  uint64_t *tfull = empty + STAGES;
+  uint8_t *raw = smem + STG * STAGE_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);  // A (and B for FP16) ready
+  uint64_t *empty = full + STG;                                      // stage consumed by the MMAs
+  uint64_t *bfull = empty + STG;                                     // B ready (quantized formats)
+  uint64_t *rawfull = bfull + STG;
+  uint64_t *rawempty = rawfull + RSTG;
+  uint64_t *tfull = rawempty + RSTG;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile uint32_t *abort = tmem_slot + 1;
-  uint4 *stage_buf = reinterpret_cast<uint4 *>(smem + STAGES * STAGE_BYTES + 128);  // 4 warps x EPI_BUF
+  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 256);  // 4 warps x EPI_BUF
   float *thr_s = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);
 
   const ScanArgs &a = t.a;
@@ -187,9 +295,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint64_t ntiles = t.rtiles * t.qtiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
-      mbar_init(full + s, 1);
+    for (int s = 0; s < STG; s++) {
+      mbar_init(full + s, QUANT ? 4 : 1);
       mbar_init(empty + s, 1);
+      mbar_init(bfull + s, 1);
+    }
+    for (int r = 0; r < RSTG; r++) {
+      mbar_init(rawfull + r, 1);
+      mbar_init(rawempty + r, 4);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(tfull + b, 1);
@@ -201,7 +314,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   // query slots past nq (padding of the last query tile) get NaN: never pass
   if (a.mode == MODE_FILTER)
-    for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += NTHREADS)
+    for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += C::NT)
       thr_s[i] = i < a.nq ? a.thr[i] : __int_as_float(0x7fc00000);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -216,27 +329,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // FP16: rows and queries into the stage. Quantized: raw codes into the
+    // raw ring (the converters load the queries).
     if (lane == 0) {
-      const uint32_t tx_bytes = (uint32_t)A_BYTES + t.bn * 128u;
+      constexpr int RING = QUANT ? RSTG1 : STG;
+      uint64_t *ring_full = QUANT ? rawfull : full;
+      uint64_t *ring_empty = QUANT ? rawempty : empty;
+      const uint32_t tx_bytes = QUANT ? (uint32_t)RAWB : (uint32_t)A_BYTES + t.bn * 128u;
       uint64_t it = 0;
       bool ok = true;
       for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const uint64_t rt = tile / t.qtiles;
         const uint32_t qt = (uint32_t)(tile % t.qtiles);
         const int32_t arow = (int32_t)(t.a_row0 + (int64_t)rt * BM);
-        for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % STAGES);
-          const uint32_t ph = (uint32_t)((it / STAGES) & 1);
-          if (!mbar_wait(empty + s, ph ^ 1, abort, a.flags)) {
+        for (uint32_t kb = 0; kb < t.kblocks; kb++) {
+          const uint32_t s = (uint32_t)(it % RING);
+          const uint32_t ph = (uint32_t)((it / RING) & 1);
+          if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags)) {
             ok = false;
             break;
           }
-          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-          mbar_expect_tx(full + s, tx_bytes);
-          tma_load_2d(sa, &rows_map, (int32_t)(kb * 64), arow, full + s);
-          tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), full + s);
+          mbar_expect_tx(ring_full + s, tx_bytes);
+          if (QUANT) {
+            tma_load_2d(smem_u32(raw + s * RAWB), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
+          } else {
+            const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+            tma_load_2d(sa, &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+            tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), ring_full + s);
+          }
+          it++;
         }
       }
+      drain_ring(ring_full, RING, it);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -251,9 +375,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * 256;
         for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % STAGES);
-          const uint32_t ph = (uint32_t)((it / STAGES) & 1);
-          if (!mbar_wait(full + s, ph, abort, a.flags)) {
+          const uint32_t s = (uint32_t)(it % STG);
+          const uint32_t ph = (uint32_t)((it / STG) & 1);
+          if (!mbar_wait(full + s, ph, abort, a.flags) || (QUANT && !mbar_wait(bfull + s, ph, abort, a.flags))) {
             ok = false;
             break;
           }
@@ -273,6 +397,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitNs) {
       }
     }
+    __syncwarp();
+  } else if (QUANT && warp >= 6) {
+    // ------------------------------------------------------------ converters
+    // raw codes -> FP16 A tile; converter thread 0 also loads the stage's
+    // query block (B) once the MMAs have released the stage.
+    const uint32_t ct = threadIdx.x - 192;
+    uint64_t it = 0, bissued = 0;
+    bool ok = true;
+    for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const uint64_t rt = tile / t.qtiles;
+      const uint32_t qt = (uint32_t)(tile % t.qtiles);
+      for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
+        const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
+        const uint32_t r = (uint32_t)(it % RSTG1), rph = (uint32_t)((it / RSTG1) & 1);
+        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (ct == 0) {
+          mbar_expect_tx(bfull + s, t.bn * 128u);
+          tma_load_2d(smem_u32(smem + s * STAGE_BYTES + A_BYTES), &query_map, (int32_t)(kb * 64),
+                      (int32_t)(qt * t.bn), bfull + s);
+          bissued = it + 1;
+        }
+        got = mbar_wait(rawfull + r, rph, abort, a.flags);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        convert_stage<Q>(a, raw + r * RAWB, smem + s * STAGE_BYTES, ct, rt * BM, kb);
+        // generic-proxy stores -> visible to the tensor core's async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(rawempty + r);
+          mbar_arrive(full + s);
+        }
+      }
+    }
+    if (ct == 0) drain_ring(bfull, STG, bissued);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -417,21 +582,39 @@ void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows,
     gather_rows<<<(unsigned)((count + 7) / 8), 256, 0, st>>>(codes, row_bytes, rows, ids, base, stride, count, out);
 }
 
-// Shared memory the tensor scan needs for nq queries (thresholds included).
-size_t tc_scan_smem(uint32_t nq) {
-  return 1024 + (size_t)STAGES * STAGE_BYTES + 128 + 4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) *
-                                                                                     sizeof(float);
+// Shared memory the tensor scan of storage format q needs for nq queries
+// (thresholds included).
+template <int Q>
+size_t tc_scan_smem_t(uint32_t nq) {
+  return 1024 + (size_t)TcCfg<Q>::STG * STAGE_BYTES + (size_t)TcCfg<Q>::RSTG * TcCfg<Q>::RAWB + 256 +
+         4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) * sizeof(float);
 }
 
 // Largest query count one tensor-scan launch takes (thresholds in shared memory).
 uint32_t tc_scan_max_queries() { return 4096; }
 
-// Launch the tensor scan of a.count virtual rows against a.nq FP16 queries:
-// rows_map describes contiguous FP16 rows ([rows][dims], box 64 x 128,
-// 128-byte swizzle) whose row a_row0 is virtual row 0 -- the shard itself
-// or a staging copy of gathered candidates; query_map the FP16 queries
-// ([qtiles*bn][kpad], box 64 x bn). The epilogue still reads per-row norms
-// through a.ids / a.base / a.stride. Returns a CUDA error from the launch.
+template <int Q>
+cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_map, const TcArgs &t, int sms,
+                        cudaStream_t st) {
+  const size_t smem = tc_scan_smem_t<Q>(t.a.nq);
+  cudaError_t e = cudaFuncSetAttribute(tc_scan<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const uint64_t ntiles = t.rtiles * t.qtiles;
+  const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
+  tc_scan<Q><<<grid, TcCfg<Q>::NT, smem, st>>>(rows_map, query_map, t);
+  return cudaGetLastError();
+}
+
+// Launch the tensor scan of a.count virtual rows against a.nq FP16 queries.
+// rows_map describes contiguous rows whose row a_row0 is virtual row 0 --
+// the shard itself or a staging copy of gathered candidates: FP16
+// ([rows][dims], box 64 x 128, 128-byte swizzle), or the raw codes of an
+// E4M3 ([rows][dims] bytes, box 64 x 128) or NVFP4 shard ([rows][dims/2]
+// bytes, box 32 x 128), converted to FP16 in shared memory (a.raw_scale
+// must be set: scores are on the raw codes). query_map: the FP16 queries
+// ([qtiles*bn][kpad], box 64 x bn). The epilogue reads per-row norms and
+// scales through a.ids / a.base / a.stride. Returns a CUDA error from the
+// launch.
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st) {
   TcArgs t;
@@ -443,13 +626,12 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   t.qtiles = (a.nq + bn - 1) / bn;
   t.rtiles = (a.count + BM - 1) / BM;
   if (a.count == 0 || a.nq == 0) return cudaSuccess;
-  const size_t smem = tc_scan_smem(a.nq);
-  cudaError_t e = cudaFuncSetAttribute(tc_scan_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  const uint64_t ntiles = t.rtiles * t.qtiles;
-  const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
-  tc_scan_f16<<<grid, NTHREADS, smem, st>>>(rows_map, query_map, t);
-  return cudaGetLastError();
+  switch (a.s.dtype) {
+    case DT_F16: return launch_tc_t<DT_F16>(rows_map, query_map, t, sms, st);
+    case DT_E4M3: return launch_tc_t<DT_E4M3>(rows_map, query_map, t, sms, st);
+    case DT_NVFP4: return launch_tc_t<DT_NVFP4>(rows_map, query_map, t, sms, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace annb200

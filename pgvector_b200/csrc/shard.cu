@@ -199,6 +199,44 @@ bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Raw codes of a quantized shard as a 2-D byte tensor [outer][inner bytes]
+// (row pitch in bytes), read in unswizzled boxes of box_x bytes x 128 rows;
+// bytes past `inner` read as zero.
+bool encode_u8_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                   uint32_t box_x) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_x, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Formats the tensor scan reads (row pitch a multiple of 16 bytes, as TMA
+// needs): FP16 rows, and E4M3 / NVFP4 codes converted to FP16 on chip.
+bool tc_format(uint32_t dtype, uint32_t dims, uint64_t row_bytes) {
+  switch (dtype) {
+    case DT_F16: return dims % 8 == 0;
+    case DT_E4M3: return row_bytes % 16 == 0;
+    case DT_NVFP4: return row_bytes % 16 == 0;
+    default: return false;
+  }
+}
+
+// The tensor map the tensor scan reads `rows` rows of this format from.
+bool encode_rows_map(CUtensorMap *map, uint32_t dtype, const void *base, uint32_t dims, uint64_t rows,
+                     uint64_t pitch) {
+  switch (dtype) {
+    case DT_F16: return encode_f16_map(map, base, dims, rows, pitch, 128);
+    case DT_E4M3: return encode_u8_map(map, base, dims, rows, pitch, 64);
+    case DT_NVFP4: return encode_u8_map(map, base, (dims + 1) / 2, rows, pitch, 32);
+    default: return false;
+  }
+}
+
 // Relative bound on the approximate dot product's accumulation error (times
 // sum |x_i q_i| <= ||x|| ||q||). Tensor scan: each tcgen05.mma (K=16) adds an
 // exactly formed FP16 product sum into the FP32 accumulator, so K/16 rounding
@@ -354,8 +392,8 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "shard upload");
   // the tensor scan gathers 128-byte row pieces by TMA (row pitch a multiple of 16 bytes)
-  s->rows_map_ok = dtype == DT_F16 && dims % 8 == 0 && rows > 0 && rows < (1ull << 31) &&
-                   encode_f16_map(&s->rows_map, v.codes, dims, rows, v.row_bytes, 128);
+  s->rows_map_ok = tc_format(dtype, dims, v.row_bytes) && rows > 0 && rows < (1ull << 31) &&
+                   encode_rows_map(&s->rows_map, dtype, v.codes, dims, rows, v.row_bytes);
   return OK;
 }
 
@@ -428,7 +466,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const bool bits = v.dtype == DT_BIT;
   const bool window = flags & ANNB200_WINDOW;
   const uint64_t n = rows ? nrows : v.rows;
-  const bool tc = v.dtype == DT_F16 && sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
+  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
   const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
@@ -489,7 +527,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.queries = (const float *)queries;
   a.nq = nq;
   a.metric = metric;
-  a.raw_scale = 0;
+  a.raw_scale = tc && v.dtype != DT_F16;   // tensor scan of quantized rows: scores on raw codes
   a.thr = qs.thr;
   a.cnt = cnt;
   a.flags = dflags;
@@ -507,7 +545,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       e = launch_tc_scan(a, sh->rows_map, (int64_t)a.base, query_map, kpad, bn, sh->sms, st);
     } else if (tc) {
       CUtensorMap staged_map;
-      if (!encode_f16_map(&staged_map, staged, v.dims, a.count, v.row_bytes, 128)) return cudaErrorInvalidValue;
+      if (!encode_rows_map(&staged_map, v.dtype, staged, v.dims, a.count, v.row_bytes)) return cudaErrorInvalidValue;
       e = launch_tc_scan(a, staged_map, 0, query_map, kpad, bn, sh->sms, st);
     } else {
       launch_simt_scan(a, st);
@@ -987,7 +1025,7 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   std::lock_guard<std::mutex> lock(sh->mu);
   cudaStream_t st = (cudaStream_t)stream;
   const bool bits = v.dtype == DT_BIT;
-  const bool tc = v.dtype == DT_F16 && sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
+  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
   const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t nq_pad = tc ? (nq + bn - 1) / bn * bn : 0;
@@ -1026,6 +1064,7 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.mat = out;
   a.mat_ld = n;
   a.flags = dflags;
+  a.raw_scale = tc && v.dtype != DT_F16;
   if (tc) {
     CUtensorMap query_map;
     if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
@@ -1036,7 +1075,7 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
       CK(sh->staging.reserve(n * v.row_bytes), "staging");
       launch_gather_rows(v.codes, v.row_bytes, v.rows, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
       CUtensorMap staged;
-      if (!encode_f16_map(&staged, sh->staging.p, v.dims, n, v.row_bytes, 128))
+      if (!encode_rows_map(&staged, v.dtype, sh->staging.p, v.dims, n, v.row_bytes))
         return fail(BACKEND_ERROR, "tensor map of the staged rows could not be encoded");
       CK(launch_tc_scan(a, staged, 0, query_map, kpad, bn, sh->sms, st), "score scan");
       counted(1);

@@ -48,6 +48,39 @@ def test_bound_holds_on_f16_rows(cuda, metric, simt):
     assert ratio < 0.5
 
 
+@pytest.mark.parametrize('dtype,dims', [(2, 1024), (3, 768), (3, 224)])
+@pytest.mark.parametrize('metric', [1, 0, 2])
+@pytest.mark.parametrize('simt', [False, True])
+def test_bound_holds_on_quantized_rows(cuda, dtype, dims, metric, simt):
+    # exact: FP64 arithmetic on the rows decoded to FP32 as the reference
+    # decodes them (code x scale products rounded to FP32)
+    import torch
+    import oracle
+    import pgvector_b200 as pb
+    n, nq = 12000, 128
+    x = synth.mixture(n, dims, 40, seed=42 + dims)
+    q = synth.mixture_queries(nq, dims, 40, seed=42 + dims)
+    if dtype == oracle.E4M3:
+        codes, rs = oracle.quantize_fp8(x)
+        bs = None
+        shard = pb.Shard(pb.E4M3, dims, torch.from_numpy(codes).to(cuda), None, torch.from_numpy(rs).to(cuda))
+    else:
+        codes, bs, rs = oracle.quantize_nvfp4(x)
+        shard = pb.Shard(pb.NVFP4, dims, torch.from_numpy(codes).to(cuda), torch.from_numpy(bs).to(cuda),
+                         torch.from_numpy(rs).to(cuda))
+    dec = oracle.decode_rows(dtype, dims, codes, block_scales=bs, row_scales=rs).astype(np.float64)
+    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), metric, force_simt=simt)
+    approx = approx.cpu().numpy().astype(np.float64)
+    err = err.cpu().numpy()
+    ex = exact(dec, q.astype(np.float64), metric)
+    diff = np.abs(approx - ex)
+    ratio = (diff / err[:, None]).max()
+    print('dtype %d metric %d simt %s: max |approx - exact| = %.3g, max ratio to bound = %.4f'
+          % (dtype, metric, simt, diff.max(), ratio))
+    assert (diff <= err[:, None]).all()
+    assert ratio < 0.5
+
+
 def test_hamming_scores_are_exact(cuda):
     import torch
     import pgvector_b200 as pb

@@ -123,6 +123,25 @@ def test_nvfp4_l2_and_cosine(cuda):
     assert_same(cuda, oracle.NVFP4, 768, packed, q, 10, 2, bs=sc, rs=row)
 
 
+@pytest.mark.parametrize('dtype,dims', [(2, 1024), (2, 200), (3, 768), (3, 224)])
+@pytest.mark.parametrize('simt', [False, True])
+def test_quantized_tensor_and_simt_paths(cuda, dtype, dims, simt):
+    # the tensor scan converts E4M3 / NVFP4 codes to FP16 on chip; dims that
+    # end inside a 64-dimension k-block exercise the zero-filled tail and the
+    # block scales past the row's last block
+    x = synth.mixture(40000, dims, 128, seed=60 + dims)
+    q = synth.mixture_queries(48, dims, 128, seed=60 + dims)
+    if dtype == oracle.E4M3:
+        codes, rs = oracle.quantize_fp8(x)
+        bs = None
+    else:
+        codes, bs, rs = oracle.quantize_nvfp4(x)
+    _, ids = synth.bitmap(40000, 0.3, seed=61)
+    assert_same(cuda, dtype, dims, codes, q, 100, 1, bs=bs, rs=rs, force_simt=simt)
+    assert_same(cuda, dtype, dims, codes, q, 50, 0, ids=ids, bs=bs, rs=rs, force_simt=simt)
+    assert_same(cuda, dtype, dims, codes, q, 20, 2, ids=ids, bs=bs, rs=rs, window=True, force_simt=simt)
+
+
 def test_hamming_bit_exact_with_ties(cuda):
     rows, proto = synth.bit_rows(60000, 1024, 256, flip=0.05, seed=9)
     rng = np.random.default_rng(9)
