@@ -1,16 +1,23 @@
 #!/usr/bin/env python
 """Throughput of the exact gather-scan on BASELINE.json's config 2.
 
-Workload: cosine kNN over halfvec (FP16) rows, d=768, N=10M
-unit-normalised rows from a 1,000-centre Gaussian mixture, a uniform 10%
-row-filter bitmap (the scan gathers the ~1M surviving rows), batch 1,024
-queries, k=100. Data are seeded synthetic stand-ins generated on the GPU.
+Workload (configs[1], the default): cosine kNN over halfvec (FP16) rows,
+d=768, N=10M unit-normalised rows from a 1,000-centre Gaussian mixture, a
+uniform 10% row-filter bitmap (the scan gathers the ~1M surviving rows),
+batch 1,024 queries, k=100. Data are seeded synthetic stand-ins generated on
+the GPU.
 
 One step = one request: the filter bitmap is expanded to a row list on the
 device, the batch is scanned (tcgen05 FP16 scan, bound, filter, exact FP64
 rescoring), and with N GPUs the corpus is row-sharded: every rank scans its
 rows, the per-rank top-k lists are all-gathered over NCCL and merged on the
-device (strong scaling: the 10M-row corpus is fixed, N GPUs share it).
+device (strong scaling: the corpus is fixed, N GPUs share it).
+
+--config 3 / 4 measure the other GPU-sized configurations the same way (not
+the headline line): 3 = inner product over FP8-E4M3 rows with row scales,
+d=1024, N=100M from a 4,096-centre mixture, batch 1,024, k=500, no filter;
+4 = IVF list gather over NVFP4 rows, d=768, N=200M in 65,536 lists with
+Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, lists sharded by rank.
 
   value  queries/s with inputs resident in HBM (CUDA events, max over ranks)
   e2e    the same through the public API with pinned host buffers: queries
@@ -35,28 +42,45 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = 'QPS at batch 1024, k=100 (1/2/4/8 B200); achieved HBM GB/s vs peak'
-WORKLOAD = ('config 2: cosine kNN, halfvec (fp16) d=768, N=10M unit-normalised rows from a 1,000-centre '
-            'Gaussian mixture, uniform 10% row-filter bitmap, batch 1,024, k=100')
+WORKLOADS = {
+    2: 'config 2: cosine kNN, halfvec (fp16) d=768, N=10M unit-normalised rows from a 1,000-centre '
+       'Gaussian mixture, uniform 10% row-filter bitmap, batch 1,024, k=100',
+    3: 'config 3: inner-product kNN, FP8-E4M3 codes + per-row scale (absmax/448), d=1024, N=100M from a '
+       '4,096-centre Gaussian mixture, batch 1,024, k=500, row-sharded',
+    4: 'config 4: IVF gather-scan, NVFP4 (e2m1 + E4M3 scale per 16 + row scale), d=768, N=200M in 65,536 '
+       'lists with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, sharded by list',
+}
+DEFAULTS = {2: dict(rows=10_000_000, dims=768, batch=1024, k=100, centres=1000),
+            3: dict(rows=100_000_000, dims=1024, batch=1024, k=500, centres=4096),
+            4: dict(rows=200_000_000, dims=768, batch=4096, k=100, centres=65536)}
 
 
 def args_parse():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=40)
+    ap.add_argument('--steps', type=int, default=None, help='timed steps (default 300; 10 for configs 3/4)')
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--rows', type=int, default=10_000_000)
-    ap.add_argument('--dims', type=int, default=768)
-    ap.add_argument('--batch', type=int, default=1024)
-    ap.add_argument('--k', type=int, default=100)
-    ap.add_argument('--selectivity', type=float, default=0.1)
-    ap.add_argument('--centres', type=int, default=1000)
+    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4])
+    ap.add_argument('--rows', type=int, default=None)
+    ap.add_argument('--dims', type=int, default=None)
+    ap.add_argument('--batch', type=int, default=None)
+    ap.add_argument('--k', type=int, default=None)
+    ap.add_argument('--selectivity', type=float, default=0.1, help='config 2 row-filter bitmap density')
+    ap.add_argument('--centres', type=int, default=None, help='mixture centres (config 4: IVF lists)')
+    ap.add_argument('--nprobe', type=int, default=64)
     ap.add_argument('--seed', type=int, default=20261201)
     ap.add_argument('--cpu-seconds', type=float, default=12.0, help='bound of the CPU-baseline sample')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-e2e', action='store_true')
-    ap.add_argument('--verify', type=int, default=2, help='queries checked against the CPU oracle (N=1)')
-    return ap.parse_args()
+    ap.add_argument('--verify', type=int, default=2, help='queries checked against the CPU oracle')
+    args = ap.parse_args()
+    for key, val in DEFAULTS[args.config].items():
+        if getattr(args, key) is None:
+            setattr(args, key, val)
+    if args.steps is None:
+        args.steps = 300 if args.config == 2 else 10
+    return args
 
 
 def peaks():
@@ -126,32 +150,41 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU baseline (reference worker code)
 
+METRIC_CODE = {2: 2, 3: 1, 4: 0}   # cosine, inner product, L2
+
+
 def cpu_sample(args, rows, queries):
-    """A bounded sample of the workload on the host: `rows` candidate rows of
-    the config-2 distribution (FP16 values decoded to FP32 exactly) and
-    `queries` queries, numpy-generated from the same mixture."""
+    """A bounded host sample of the workload's distribution: `rows` rows
+    decoded to FP32 exactly as the device format stores them, and `queries`
+    queries (numpy, same mixture)."""
     import numpy as np
+    import oracle
     from pgvector_b200 import synth
-    x = synth.mixture(rows, args.dims, args.centres, seed=args.seed, normalize=True).astype(np.float16)
-    q = synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed, normalize=True)
-    return x.astype(np.float32), q.astype(np.float16).astype(np.float32)
+    if args.config == 2:
+        x = synth.mixture(rows, args.dims, args.centres, seed=args.seed, normalize=True).astype(np.float16)
+        q = synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed, normalize=True)
+        return x.astype(np.float32), q.astype(np.float16).astype(np.float32)
+    x = synth.mixture(rows, args.dims, args.centres, seed=args.seed)
+    q = synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed)
+    codes, scale = oracle.quantize_fp8(x)
+    return oracle.decode_rows(oracle.E4M3, args.dims, codes, row_scales=scale), q
 
 
-def cpu_run(x, q, k, threads, budget_s=None, count=None):
-    """Gathered cosine jobs through the reference's AnnGatheredExact
-    (oracle/_ref, ann/server/cpu.c:218-276) -- or the oracle's restatement
-    when the reference library is absent -- on `threads` host threads, for
-    budget_s seconds or exactly `count` queries; returns (queries done,
-    seconds, kind)."""
+def cpu_run(x, q, k, threads, metric, budget_s=None, count=None):
+    """Gathered jobs through the reference's AnnGatheredExact (oracle/_ref,
+    ann/server/cpu.c:218-276) -- or the oracle's restatement when the
+    reference library is absent -- on `threads` host threads, for budget_s
+    seconds or exactly `count` queries; returns (queries done, seconds,
+    kind)."""
     from concurrent.futures import ThreadPoolExecutor
     import oracle
     kind = 'reference' if oracle.ref_available() else 'port'
 
     def one(i):
         if kind == 'reference':
-            st, res = oracle.ref_gathered_exact(q[i % len(q)], x, k, 2)
+            oracle.ref_gathered_exact(q[i % len(q)], x, k, metric)
         else:
-            oracle.search(oracle.F32, x.shape[1], x, q[i % len(q)][None], k, 2, window=True, threads=1)
+            oracle.search(oracle.F32, x.shape[1], x, q[i % len(q)][None], k, metric, window=True, threads=1)
         return 1
 
     done, t0 = 0, time.perf_counter()
@@ -164,8 +197,68 @@ def cpu_run(x, q, k, threads, budget_s=None, count=None):
     return done, time.perf_counter() - t0, kind
 
 
+def ivf_cpu_sample(args, rows):
+    """Config 4 on the host: the oracle's IVF list gather (the reference's
+    IVF scan is PostgreSQL code, src/ivfscan.c:124-186, with no worker entry
+    point, so its C restatement is timed) over an NVFP4 corpus of `rows`
+    rows with the full configuration's mean list size (N/nlist) and nprobe,
+    so each query does the full-size amount of work."""
+    import numpy as np
+    import oracle
+    from pgvector_b200 import synth
+    nlists = max(args.nprobe, int(round(args.centres * rows / args.rows)))
+    x, offsets, cent, _ = synth.ivf_corpus(rows, args.dims, nlists, seed=args.seed)
+    codes, bs, rs = oracle.quantize_nvfp4(x)
+    rng = np.random.default_rng(args.seed + 5)
+    lab = rng.integers(0, nlists, 256)
+    q = (cent[lab] + 0.1 * rng.standard_normal((256, args.dims))).astype(np.float32)
+    probes = synth.ivf_probes(q, cent, args.nprobe)
+    return codes, bs, rs, offsets, q, probes
+
+
+def ivf_cpu_run(sample, args, threads, budget_s=None, count=None):
+    import oracle
+    codes, bs, rs, offsets, q, probes = sample
+    done, t0, i = 0, time.perf_counter(), 0
+    while (count is not None and done < count) or (count is None and time.perf_counter() - t0 < budget_s):
+        m = threads if count is None else min(threads, count - done)
+        sel = [(i + j) % len(q) for j in range(m)]
+        oracle.search_lists(oracle.NVFP4, args.dims, codes, q[sel], offsets, probes[sel], args.k, 0,
+                            block_scales=bs, row_scales=rs, threads=threads)
+        done += m
+        i += m
+    return done, time.perf_counter() - t0, 'port'
+
+
+_SAMPLES = {}
+
+
+def cpu_measure(args, threads, budget_s=None, count=None):
+    """(queries/s at full size, sample description, kind) of the host path."""
+    if args.config == 4:
+        rows = 200_000
+        if 4 not in _SAMPLES:
+            _SAMPLES[4] = ivf_cpu_sample(args, rows)
+        sample = _SAMPLES[4]
+        done, secs, kind = ivf_cpu_run(sample, args, threads, budget_s=budget_s, count=count)
+        desc = ('%d IVF queries (NVFP4 L2, k=%d, nprobe=%d over %d-row lists on average) in %.1f s on %d threads; '
+                'the per-query work equals the full configuration\'s' %
+                (done, args.k, args.nprobe, rows // max(1, len(sample[3]) - 1), secs, threads))
+        return done / secs, desc, kind
+    rows = 50_000 if args.config == 2 else 20_000
+    if args.config not in _SAMPLES:
+        _SAMPLES[args.config] = cpu_sample(args, rows, 64)
+    x, q = _SAMPLES[args.config]
+    done, secs, kind = cpu_run(x, q, args.k, threads, METRIC_CODE[args.config], budget_s=budget_s, count=count)
+    full = full_candidates(args)
+    desc = ('%d gathered jobs (metric %d, k=%d) over %d candidate rows of the config-%d distribution in %.1f s on '
+            '%d threads, scaled linearly to %d candidate rows' %
+            (done, METRIC_CODE[args.config], args.k, rows, args.config, secs, threads, full))
+    return done / secs * rows / full, desc, kind
+
+
 def full_candidates(args):
-    return int(round(args.rows * args.selectivity))
+    return int(round(args.rows * args.selectivity)) if args.config == 2 else args.rows
 
 
 def reference_arm(args):
@@ -173,32 +266,288 @@ def reference_arm(args):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sample_rows = 100_000
-    x, q = cpu_sample(args, sample_rows, 64)
     per_step = max(threads, 8)
-    scale = sample_rows / full_candidates(args)
     for _ in range(args.warmup):
-        cpu_run(x, q, args.k, threads, count=per_step)
-    total_q, total_s, kind = 0, 0.0, 'reference'
+        cpu_measure(args, threads, count=per_step)
+    rates, desc, kind = [], '', 'reference'
     for _ in range(args.steps):
-        done, secs, kind = cpu_run(x, q, args.k, threads, count=per_step)
-        total_q += done
-        total_s += secs
-    qps = total_q / total_s * scale
+        qps, desc, kind = cpu_measure(args, threads, count=per_step)
+        rates.append(qps)
+    qps = len(rates) / sum(1.0 / r for r in rates)
     line = {'metric': METRIC, 'value': qps, 'unit': 'queries/s', 'n_gpus': args.gpus, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': args.batch / qps * 1e3,
             'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f64',
-            'data': 'synthetic (seeded 1,000-centre Gaussian mixture, unit-normalised, FP16 values)',
-            'config': {'workload': WORKLOAD, 'global_batch': args.batch, 'rows': args.rows, 'dims': args.dims,
-                       'k': args.k, 'selectivity': args.selectivity, 'parallelism': 'host threads'},
+            'data': 'synthetic (seeded Gaussian mixture of the configuration)',
+            'config': {'workload': WORKLOADS[args.config], 'global_batch': args.batch, 'rows': args.rows,
+                       'dims': args.dims, 'k': args.k, 'parallelism': 'host threads'},
             'impl': 'reference',
             'cpu_baseline': {'value': qps, 'unit': 'queries/s', 'cores': threads, 'kind': kind,
-                             'sample': '%d queries a step x %d candidate rows (cosine, k=%d, gathered jobs via '
-                                       'AnnGatheredExact), time scaled linearly to %d candidate rows'
-                                       % (per_step, sample_rows, args.k, full_candidates(args))},
+                             'sample': '%d queries a step: %s' % (per_step, desc)},
             'e2e': {'value': qps, 'unit': 'queries/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    if args.config == 2:
+        line['config']['selectivity'] = args.selectivity
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------- workloads
+
+class Workload:
+    """One configuration on this rank: the shard, the batch's device inputs
+    (`inputs`: tensors copied from host memory each step in the end-to-end
+    loop) and one step of the public API over them."""
+    metric = 0
+    dtype = 'f16'
+    kernel = ''
+    bound = 'tensor'
+
+    def step(self, *inputs):
+        raise NotImplementedError
+
+
+def mixture_rows(args, dev, lo, hi, centres, fill, chunk=1 << 20, normalize=False, label_of=None):
+    """Rows lo..hi of the seeded global mixture, generated chunk by chunk
+    (per-chunk seeds: every rank draws the same global rows) and handed to
+    fill(a, b, float32 rows) -- row a..b of the local range."""
+    import torch
+    g = torch.Generator(device=dev)
+    for c0 in range(lo // chunk * chunk, hi, chunk):
+        g.manual_seed(args.seed * 1000003 + c0 // chunk)
+        m = min(chunk, args.rows - c0)
+        lab = (torch.randint(0, centres.shape[0], (m,), generator=g, device=dev) if label_of is None
+               else label_of(c0, m))
+        v = centres[lab] + 0.1 * torch.randn((m, args.dims), generator=g, device=dev)
+        if normalize:
+            v /= v.norm(dim=1, keepdim=True).clamp_min(1e-30)
+        a, b = max(c0, lo), min(c0 + m, hi)
+        fill(a - lo, b - lo, v[a - c0:b - c0])
+        del v, lab
+
+
+def build_config2(args, rank, world, dev):
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import sharded, synth
+    w = Workload()
+    bounds = sharded.shard_bounds(args.rows, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    centres = torch.randn((args.centres, args.dims), generator=g, device=dev)
+    codes = torch.empty((hi - lo, args.dims), dtype=torch.float16, device=dev)
+
+    def fill(a, b, v):
+        codes[a:b] = v.to(torch.float16)
+    mixture_rows(args, dev, lo, hi, centres, fill, normalize=True)
+    g.manual_seed(args.seed + 7919)
+    lab = torch.randint(0, args.centres, (args.batch,), generator=g, device=dev)
+    qv = centres[lab] + 0.1 * torch.randn((args.batch, args.dims), generator=g, device=dev)
+    qv /= qv.norm(dim=1, keepdim=True)
+    queries = qv.to(torch.float16).to(torch.float32).contiguous()       # halfvec query values
+    words = synth.torch_bitmap(args.rows, args.selectivity, seed=args.seed + 1, device=dev)
+    my_words, nbits = sharded.bitmap_slice(words, lo, hi)
+    w.inputs = [queries, my_words.contiguous()]
+    w.shard = pb.Shard(pb.F16, args.dims, codes, first_id=lo)
+    w.codes, w.lo, w.metric, w.dtype = codes, lo, pb.COSINE, 'f16'
+    w.kernel = 'tc_scan<F16>, filter pass'
+    w.data = 'synthetic (seeded 1,000-centre Gaussian mixture, unit-normalised, generated on the GPU)'
+    w.row_bytes = args.dims * 2 + 4                         # row + its id in the row list
+    w.profile = 'tc_scan_f16_config2.md'
+
+    def step(q, words_):
+        rows = pb.bitmap_rows(words_, nbits)
+        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.COSINE, rows)
+        return d, i, c, rows.numel()
+    w.step = step
+
+    def verify(result, nq):
+        import numpy as np
+        import oracle
+        rows_t = pb.bitmap_rows(w.inputs[1], nbits)
+        rows_np = rows_t.cpu().numpy().view(np.uint32).astype(np.int64)
+        h = codes[rows_t.long()].cpu().numpy().view(np.uint16)          # only the candidate rows
+        qn = queries[:nq].cpu().numpy()
+        od, oi, oc, _ = oracle.search(oracle.F16, args.dims, h, qn, args.k, 2)
+        return bool(np.array_equal(result[1][:nq].cpu().numpy(), rows_np[oi] + lo) and
+                    np.array_equal(result[0][:nq].cpu().numpy(), od))
+    w.verify = verify
+    del centres, qv, lab
+    return w
+
+
+def build_config3(args, rank, world, dev):
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import sharded, synth
+    w = Workload()
+    bounds = sharded.shard_bounds(args.rows, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    centres = torch.randn((args.centres, args.dims), generator=g, device=dev)
+    pad = (args.dims + 15) // 16 * 16
+    codes = torch.empty((hi - lo, pad), dtype=torch.uint8, device=dev)
+    scales = torch.empty((hi - lo,), dtype=torch.float32, device=dev)
+
+    def fill(a, b, v):
+        c, s = synth.torch_quantize_fp8(v)
+        codes[a:b] = c
+        scales[a:b] = s
+    mixture_rows(args, dev, lo, hi, centres, fill)
+    g.manual_seed(args.seed + 7919)
+    lab = torch.randint(0, args.centres, (args.batch,), generator=g, device=dev)
+    queries = (centres[lab] + 0.1 * torch.randn((args.batch, args.dims), generator=g, device=dev)).contiguous()
+    w.inputs = [queries]
+    w.shard = pb.Shard(pb.E4M3, args.dims, codes, None, scales, first_id=lo)
+    w.metric, w.dtype = pb.IP, 'e4m3->f16'
+    w.kernel = 'tc_scan<E4M3>, filter pass'
+    w.data = 'synthetic (seeded 4,096-centre Gaussian mixture, FP8-quantised on the GPU with the builder\'s rules)'
+    w.row_bytes = pad + 4                                   # codes + row scale
+    w.profile = 'tc_scan_e4m3_config3.md'
+
+    def step(q):
+        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.IP, None)
+        return d, i, c, hi - lo
+    w.step = step
+
+    def verify(result, nq):
+        return verify_by_rescoring(args, w, result, nq, codes, None, scales, oracle_dtype=2, lo=lo, hi=hi)
+    w.verify = verify
+    del centres
+    return w
+
+
+def build_config4(args, rank, world, dev):
+    import numpy as np
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import sharded, synth
+    w = Workload()
+    nlists = args.centres
+    rng = np.random.default_rng(args.seed + 3)
+    weights = 1.0 / np.arange(1, nlists + 1, dtype=np.float64) ** 1.1
+    weights = weights[rng.permutation(nlists)]
+    sizes = np.floor(weights / weights.sum() * args.rows).astype(np.int64)
+    sizes[np.argmax(sizes)] += args.rows - sizes.sum()
+    offsets = np.zeros(nlists + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum(sizes)
+    lb = [nlists * r // world for r in range(world + 1)]        # lists l0..l1 on this rank
+    l0, l1 = lb[rank], lb[rank + 1]
+    lo, hi = int(offsets[l0]), int(offsets[l1])
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    cent = torch.randn((nlists, args.dims), generator=g, device=dev)
+    doff = torch.from_numpy(offsets).to(dev)
+    blocks = (args.dims + 15) // 16
+    codes = torch.empty((hi - lo, blocks * 8), dtype=torch.uint8, device=dev)
+    bscales = torch.empty((hi - lo, blocks), dtype=torch.uint8, device=dev)
+    rscales = torch.empty((hi - lo,), dtype=torch.float32, device=dev)
+
+    def label_of(c0, m):
+        idx = torch.arange(c0, c0 + m, device=dev)
+        return torch.searchsorted(doff[1:], idx, right=True)
+
+    def fill(a, b, v):
+        p, s, r = synth.torch_quantize_nvfp4(v)
+        codes[a:b] = p
+        bscales[a:b] = s
+        rscales[a:b] = r
+    mixture_rows(args, dev, lo, hi, cent, fill, label_of=label_of)
+    # queries: the centre of a uniformly chosen list plus noise, so that a
+    # probe touches a list of the mean size (N / nlist rows) on average, the
+    # per-query gather the configuration's cost figures assume
+    g.manual_seed(args.seed + 7919)
+    qlab = torch.randint(0, nlists, (args.batch,), generator=g, device=dev)
+    queries = (cent[qlab] + 0.1 * torch.randn((args.batch, args.dims), generator=g, device=dev)).contiguous()
+    # coarse probe (outside the timed step): nprobe nearest centroids
+    d2 = (cent * cent).sum(1)[None, :] - 2.0 * queries @ cent.T
+    probes = torch.topk(d2, args.nprobe, dim=1, largest=False).indices
+    local = torch.where((probes >= l0) & (probes < l1), probes - l0, torch.full_like(probes, -1))
+    local = local.to(torch.int32).contiguous()                  # -1 = UINT32_MAX: padding
+    loc_off = torch.from_numpy(offsets[l0:l1 + 1] - offsets[l0]).to(dev)
+    w.inputs = [queries, local]
+    w.shard = pb.Shard(pb.NVFP4, args.dims, codes, bscales, rscales, first_id=lo)
+    w.metric, w.dtype, w.bound = pb.L2, 'nvfp4->f32', 'hbm'
+    w.kernel = 'simt_scan_lists<NVFP4>, list pass'
+    w.data = ('synthetic (seeded: %d list centres ~N(0,1), rows = centre + 0.1 noise, Zipf(1.1) list sizes, '
+              'NVFP4-quantised on the GPU with the builder\'s rules)' % nlists)
+    w.row_bytes = blocks * 8 + blocks + 4
+    w.profile = 'simt_scan_lists_config4.md'
+    # algorithmic bytes of a pass: every probed list's rows, read once
+    hit = torch.zeros(l1 - l0, dtype=torch.bool, device=dev)
+    lp = local[local >= 0].long()
+    hit[lp] = True
+    lsz = torch.from_numpy(sizes[l0:l1]).to(dev)
+    w.pass_rows = int(lsz[hit].sum().item())
+    pairs = int(torch.from_numpy(sizes[l0:l1]).to(dev)[lp].sum().item())
+    w.pass_flops = 2.0 * pairs * args.dims
+
+    def step(q, pr):
+        d, i, c = w.shard.search_lists(q, args.k, pb.L2, loc_off, pr)
+        if world > 1:
+            gd, gi, gc = sharded.gather_lists(d, i, c)
+            return pb.merge_topk(gd, gi, gc, args.k) + (w.pass_rows,)
+        return d, i, c, w.pass_rows
+    w.step = step
+
+    def verify(result, nq):
+        import oracle
+        qn = queries[:nq].cpu().numpy()
+        pr = local[:nq].cpu().numpy().view(np.uint32)
+        lists = sorted(set(int(x) for x in pr.ravel() if x != 0xffffffff))
+        # the probed lists only, re-packed list-major with their global ids
+        parts, new_off, ids = [], [0], []
+        for l in lists:
+            a, b = int(offsets[l0 + l] - lo), int(offsets[l0 + l + 1] - lo)
+            parts.append((a, b))
+            new_off.append(new_off[-1] + b - a)
+            ids.append(np.arange(a, b, dtype=np.int64) + lo)
+        sel = torch.cat([torch.arange(a, b, device=dev) for a, b in parts])
+        remap = {l: j for j, l in enumerate(lists)}
+        pr2 = np.array([[remap.get(int(x), 0xffffffff) for x in row] for row in pr], dtype=np.uint32)
+        od, oi, oc = oracle.search_lists(oracle.NVFP4, args.dims, codes[sel].cpu().numpy(), qn,
+                                         np.array(new_off, dtype=np.uint64), pr2, args.k, 0,
+                                         row_ids=np.concatenate(ids), block_scales=bscales[sel].cpu().numpy(),
+                                         row_scales=rscales[sel].cpu().numpy())
+        return bool(np.array_equal(result[1][:nq].cpu().numpy(), oi) and
+                    np.array_equal(result[0][:nq].cpu().numpy(), od))
+    w.verify = verify if world == 1 else (lambda result, nq: None)
+    del cent
+    return w
+
+
+def verify_by_rescoring(args, w, result, nq, codes, bscales, rscales, oracle_dtype, lo, hi):
+    """Size-independent check for shards too large for the oracle: the
+    returned rows' distances recomputed by the oracle equal the returned
+    ones bit for bit and are sorted by (distance, id), and no row of a
+    200,000-row random sample beats the k-th (single GPU)."""
+    import numpy as np
+    import torch
+    import oracle
+    if hi - lo != args.rows:
+        return None
+    ok = True
+    rng = np.random.default_rng(args.seed + 11)
+    sample = np.unique(rng.integers(0, hi - lo, 200_000))
+    for qi in range(nq):
+        q = w.inputs[0][qi:qi + 1].cpu().numpy()
+        ids = result[1][qi].cpu().numpy()
+        dist = result[0][qi].cpu().numpy()
+        rows = np.unique(np.concatenate([ids - lo, sample]))
+        rt = torch.from_numpy(rows).to(codes.device)
+        sub = codes[rt].cpu().numpy()
+        bs = None if bscales is None else bscales[rt].cpu().numpy()
+        rs = rscales[rt].cpu().numpy()
+        od, oi, oc, _ = oracle.search(oracle_dtype, args.dims, sub, q, len(rows), w.metric, block_scales=bs,
+                                      row_scales=rs)
+        exact = dict(zip(rows[oi[0][:oc[0]]].tolist(), od[0][:oc[0]].tolist()))
+        got = [exact[int(i - lo)] for i in ids]
+        ok &= bool(np.array_equal(np.array(got), dist))
+        ok &= all((dist[j], ids[j]) <= (dist[j + 1], ids[j + 1]) for j in range(len(ids) - 1))
+        kth = (dist[-1], ids[-1])
+        member = set((ids - lo).tolist())
+        ok &= all((d, int(r) + lo) >= kth for r, d in exact.items() if int(r) not in member)
+    return ok
 
 
 # ---------------------------------------------------------------- our arm
@@ -208,11 +557,9 @@ def main():
     if args.impl == 'reference':
         return reference_arm(args)
     os.environ.setdefault('ANN_B200_KERNEL_TIMING', '1')
-    import numpy as np
     import torch
     import torch.distributed as dist
     import pgvector_b200 as pb
-    from pgvector_b200 import sharded, synth
     from datetime import timedelta
 
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -223,42 +570,8 @@ def main():
     if world > 1:
         dist.init_process_group('nccl', timeout=timedelta(seconds=180), device_id=dev)
     lib = pb.load()
-
-    # ---- data: this rank's contiguous row range of the global corpus
-    bounds = sharded.shard_bounds(args.rows, world)
-    lo, hi = bounds[rank], bounds[rank + 1]
-    chunk = 1 << 20
-    codes = torch.empty((hi - lo, args.dims), dtype=torch.float16, device=dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(args.seed)
-    centres = torch.randn((args.centres, args.dims), generator=g, device=dev)
-    for c0 in range(lo // chunk * chunk, hi, chunk):
-        g.manual_seed(args.seed * 1000003 + c0 // chunk)
-        m = min(chunk, args.rows - c0)
-        lab = torch.randint(0, args.centres, (m,), generator=g, device=dev)
-        v = centres[lab] + 0.1 * torch.randn((m, args.dims), generator=g, device=dev)
-        v /= v.norm(dim=1, keepdim=True).clamp_min(1e-30)
-        a, b = max(c0, lo), min(c0 + m, hi)
-        codes[a - lo:b - lo] = v[a - c0:b - c0].to(torch.float16)
-        del v, lab
-    g.manual_seed(args.seed + 7919)
-    lab = torch.randint(0, args.centres, (args.batch,), generator=g, device=dev)
-    qv = centres[lab] + 0.1 * torch.randn((args.batch, args.dims), generator=g, device=dev)
-    qv /= qv.norm(dim=1, keepdim=True)
-    queries = qv.to(torch.float16).to(torch.float32).contiguous()       # halfvec query values
-    words = synth.torch_bitmap(args.rows, args.selectivity, seed=args.seed + 1, device=dev)
-    my_words, nbits = sharded.bitmap_slice(words, lo, hi)
-    my_words = my_words.contiguous()
-    del centres, qv, lab
+    w = {2: build_config2, 3: build_config3, 4: build_config4}[args.config](args, rank, world, dev)
     torch.cuda.synchronize()
-
-    shard = pb.Shard(pb.F16, args.dims, codes, first_id=lo)
-    k = args.k
-
-    def step(q, w):
-        rows = pb.bitmap_rows(w, nbits)
-        d, i, c = sharded.search_sharded(shard, q, k, pb.COSINE, rows)
-        return d, i, c, rows.numel()
 
     def barrier():
         if world > 1:
@@ -277,7 +590,7 @@ def main():
     if clocks:
         clocks.start()
     for _ in range(args.warmup):
-        step(queries, my_words)
+        w.step(*w.inputs)
     barrier()
     stage_ms = (ctypes.c_double * 9)()
     stage_calls = (ctypes.c_ulonglong * 9)()
@@ -288,7 +601,7 @@ def main():
     e0.record()
     nrows_local = 0
     for _ in range(args.steps):
-        out = step(queries, my_words)
+        out = w.step(*w.inputs)
         nrows_local = out[3]
     e1.record()
     barrier()
@@ -301,103 +614,99 @@ def main():
 
     # ---- end to end through the public API with host buffers
     e2e = None
+    k = args.k
     if not args.no_e2e:
-        hq = queries.cpu().pin_memory()
-        hw = my_words.cpu().pin_memory()
+        hin = [x.cpu().pin_memory() for x in w.inputs]
+        din = [torch.empty_like(x) for x in w.inputs]
         hd = torch.empty((args.batch, k), dtype=torch.float64).pin_memory()
         hi_ = torch.empty((args.batch, k), dtype=torch.int64).pin_memory()
-        dq = torch.empty_like(queries)
-        dw = torch.empty_like(my_words)
-        for _ in range(args.warmup):
-            dq.copy_(hq, non_blocking=True)
-            dw.copy_(hw, non_blocking=True)
-            d, i, c, _n = step(dq, dw)
+
+        def e2e_step():
+            for d_, h_ in zip(din, hin):
+                d_.copy_(h_, non_blocking=True)
+            d, i, c, _n = w.step(*din)
             hd.copy_(d[:, :k], non_blocking=True)
             hi_.copy_(i[:, :k], non_blocking=True)
+        for _ in range(args.warmup):
+            e2e_step()
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
         for _ in range(args.steps):
-            dq.copy_(hq, non_blocking=True)
-            dw.copy_(hw, non_blocking=True)
-            d, i, c, _n = step(dq, dw)
-            hd.copy_(d[:, :k], non_blocking=True)
-            hi_.copy_(i[:, :k], non_blocking=True)
+            e2e_step()
         f1.record()
         barrier()
         ems = max_over_ranks(f0.elapsed_time(f1))
         e2e = {'value': args.steps * args.batch / (ems / 1e3), 'unit': 'queries/s',
-               'h2d_bytes_per_step': int(hq.numel() * 4 + hw.numel() * 4),
+               'h2d_bytes_per_step': int(sum(h.numel() * h.element_size() for h in hin)),
                'd2h_bytes_per_step': int(hd.numel() * 8 + hi_.numel() * 8) if rank == 0 else 0,
                'ms_per_step': ems / args.steps}
 
-    # ---- roofline of the filter pass (stage 3: every tcgen05 scan launch of
-    # one step's filter pass, timed by the library's stage clock on its
+    # ---- roofline of the dominant pass (stage 3: every scan launch of one
+    # step's filter / list pass, timed by the library's stage clock on its
     # stream). Algorithmic work per pass: 2 * batch * candidate rows * dims
-    # FLOPs; algorithmic bytes: the candidate rows (dims * 2 B + 4 B row id)
-    # plus the FP16 query block.
+    # FLOPs (IVF: 2 * dims per probed (row, query) pair); algorithmic bytes:
+    # each candidate row once (codes, scales and its row id) plus the query
+    # block.
     hbm, tf_burst, tf_sust, kind = peaks()
     pass_ms = stage_ms[3] / args.steps
-    flops = 2.0 * args.batch * nrows_local * args.dims
+    if args.config == 4:
+        flops, bytes_alg = w.pass_flops, w.pass_rows * (w.row_bytes - 4) + args.batch * args.dims * 4
+    else:
+        flops = 2.0 * args.batch * nrows_local * args.dims
+        bytes_alg = nrows_local * w.row_bytes + args.batch * args.dims * 2
     achieved_tf = flops / (pass_ms * 1e-3) / 1e12
-    bytes_alg = nrows_local * (args.dims * 2 + 4) + args.batch * args.dims * 2
+    hbm_gbs = bytes_alg / (pass_ms * 1e-3) / 1e9
     traffic = None
-    tpath = os.path.join(ROOT, 'profiles', 'tc_scan_f16_config2.md')
+    tpath = os.path.join(ROOT, 'profiles', w.profile)
     if os.path.exists(tpath):
         for line in open(tpath):
             if line.startswith('traffic_bytes_per_row:'):
-                traffic = float(line.split(':', 1)[1]) * nrows_local
-    roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
-                'frac': achieved_tf / tf_sust, 'traffic': traffic,
-                'kernel': 'tc_scan_f16, filter pass (%d launches a step)' % round(stage_calls[3] / args.steps),
-                'peak_source': kind + ' bf16_tflops_sustained', 'pass_ms': pass_ms, 'flops_per_pass': flops,
-                'algorithmic_bytes_per_pass': bytes_alg,
-                'hbm_achieved_gbs': bytes_alg / (pass_ms * 1e-3) / 1e9, 'hbm_peak_gbs': hbm,
-                'hbm_frac': bytes_alg / (pass_ms * 1e-3) / 1e9 / hbm,
-                'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(
-                    ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge',
-                     'gather'])}}
+                traffic = float(line.split(':', 1)[1]) * (w.pass_rows if args.config == 4 else nrows_local)
+    stage_names = ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge', 'gather']
+    common = {'kernel': '%s (%d launches a step)' % (w.kernel, round(stage_calls[3] / args.steps)),
+              'pass_ms': pass_ms, 'flops_per_pass': flops, 'algorithmic_bytes_per_pass': bytes_alg,
+              'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(stage_names)}}
+    if w.bound == 'tensor':
+        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
+                    'frac': achieved_tf / tf_sust, 'traffic': traffic,
+                    'peak_source': kind + ' bf16_tflops_sustained',
+                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
+    else:
+        roofline = {'bound': 'hbm', 'achieved': hbm_gbs, 'peak': hbm, 'unit': 'GB/s', 'frac': hbm_gbs / hbm,
+                    'traffic': traffic, 'peak_source': kind + ' hbm_gbs', 'achieved_tflops': achieved_tf,
+                    **common}
 
-    # ---- correctness spot check against the CPU oracle (single GPU)
-    verified = None
-    if world == 1 and args.verify > 0:
-        import oracle
-        rows_t = pb.bitmap_rows(my_words, nbits)
-        rows_np = rows_t.cpu().numpy().view(np.uint32).astype(np.int64)
-        h = codes[rows_t.long()].cpu().numpy().view(np.uint16)          # only the candidate rows
-        qn = queries[:args.verify].cpu().numpy()
-        od, oi, oc, _ = oracle.search(oracle.F16, args.dims, h, qn, k, 2)
-        verified = bool(np.array_equal(result[1][:args.verify].cpu().numpy(), rows_np[oi] + lo) and
-                        np.array_equal(result[0][:args.verify].cpu().numpy(), od))
-        del h
+    # ---- correctness spot check against the CPU oracle
+    verified = w.verify(result, args.verify) if args.verify > 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        x, q = cpu_sample(args, 50_000, 64)
-        done, secs, ckind = cpu_run(x, q, k, threads, budget_s=args.cpu_seconds)
-        scale = 50_000 / full_candidates(args)
-        cpu = {'value': done / secs * scale, 'unit': 'queries/s', 'cores': threads, 'kind': ckind,
-               'sample': '%d cosine gathered jobs (k=%d) over %d candidate rows of the config-2 distribution '
-                         'in %.1f s on %d threads, scaled linearly to %d candidate rows'
-                         % (done, k, 50_000, secs, threads, full_candidates(args))}
+        qps, desc, ckind = cpu_measure(args, threads, budget_s=args.cpu_seconds)
+        cpu = {'value': qps, 'unit': 'queries/s', 'cores': threads, 'kind': ckind, 'sample': desc}
 
     if rank == 0:
+        cand = int(nrows_local) * world if args.config != 4 else None
+        cfg = {'workload': WORKLOADS[args.config], 'global_batch': args.batch, 'rows': args.rows, 'dims': args.dims,
+               'k': args.k}
+        if args.config == 2:
+            cfg['selectivity'] = args.selectivity
+        if args.config == 4:
+            cfg.update({'nlist': args.centres, 'nprobe': args.nprobe})
+        cfg['l2'] = 'inputs larger than L2 (%.2f GB of candidate rows a step on rank 0)' % (
+            (w.pass_rows if args.config == 4 else nrows_local) * w.row_bytes / 1e9)
+        if cand is not None:
+            cfg['candidate_rows'] = cand
+        cfg['parallelism'] = ('%s x%d, NCCL all-gather of top-k + device merge' % (
+            'list-sharded' if args.config == 4 else 'row-sharded', world) if world > 1 else 'single GPU')
         line = {'metric': METRIC, 'value': value, 'unit': 'queries/s', 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True,
-                'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f16',
-                'data': 'synthetic (seeded 1,000-centre Gaussian mixture, unit-normalised, generated on the GPU)',
-                'config': {'workload': WORKLOAD, 'global_batch': args.batch, 'rows': args.rows, 'dims': args.dims,
-                           'k': args.k, 'selectivity': args.selectivity,
-                           'candidate_rows': int(nrows_local) * world,
-                           'l2': 'inputs larger than L2 (%.2f GB of gathered rows a step)'
-                                 % (nrows_local * world * args.dims * 2 / 1e9),
-                           'parallelism': 'row-sharded x%d, NCCL all-gather of top-k + device merge' % world
-                           if world > 1 else 'single GPU'},
+                'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg,
                 'e2e': e2e, 'gpu_launches': int(launches), 'roofline': roofline, 'cpu_baseline': cpu,
                 'clocks': clock_info, 'verified_vs_oracle': verified}
         print(json.dumps(line), flush=True)
-    shard.close()
+    w.shard.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -137,7 +137,9 @@ int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
  * list_offsets[l] .. list_offsets[l+1]-1 (device u64 [nlists+1],
  * non-decreasing, last <= the shard's rows). probes is device u32
  * [nq][nprobe]: each query's list numbers, distinct and < nlists (a query
- * that breaks this gets status ANN_INVALID and no results). row_ids
+ * that breaks this gets status ANN_INVALID and no results); entries equal
+ * to UINT32_MAX are padding, for queries with fewer lists on this shard
+ * when the lists are sharded across GPUs. row_ids
  * (optional, device int64 [rows]) gives each stored row's global id;
  * without it the id is first_id + row. Results as AnnB200Search without
  * ANNB200_WINDOW: min(k, rows in the probed lists) per query, sorted by

@@ -91,6 +91,7 @@ struct ScanArgs {
 // runs [offsets[l], offsets[l+1]); probes [nq][nprobe] name each query's
 // lists. The plan arrays are device workspace.
 constexpr uint32_t kMaxProbes = 4096;
+constexpr uint32_t kNoProbe = 0xffffffffu;  // probe table padding
 constexpr uint32_t kMaxLists = 1u << 24;
 struct ListPlan {
   const uint64_t *offsets;    // [nlists + 1]
@@ -338,8 +339,9 @@ int report_error(int status, const char *fmt, ...);
 void count_launches(unsigned long long n);
 void launch_simt_scan(const ScanArgs &a, cudaStream_t st);
 void launch_list_plan(const ListPlan &p, const QueryState &qs, uint32_t *flags, cudaStream_t st);
-void launch_list_items(const ListPlan &p, uint64_t limit, cudaStream_t st);
-void launch_simt_scan_lists(const ListPlan &p, uint64_t limit, const ScanArgs &a, int sms, cudaStream_t st);
+void launch_list_items(const ListPlan &p, uint64_t rbegin, uint64_t rend, cudaStream_t st);
+void launch_simt_scan_lists(const ListPlan &p, uint64_t rbegin, uint64_t rend, const ScanArgs &a, int sms,
+                            cudaStream_t st);
 uint32_t list_plan_scan_launches(uint32_t nlists);
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);

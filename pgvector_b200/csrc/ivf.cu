@@ -126,6 +126,7 @@ __global__ void check_offsets(ListPlan p, uint32_t *flags) {
 
 // One block a query: a list number past nlists or a list probed twice makes
 // the query invalid (status 1); a valid query counts itself into its lists.
+// kNoProbe entries are padding (a query with fewer lists on this shard).
 // Duplicates show as equal neighbours once the query's probes are sorted.
 __global__ void __launch_bounds__(256) probe_count(ListPlan p, QueryState qs, uint32_t *flags) {
   __shared__ uint32_t s[kMaxProbes];
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(256) probe_count(ListPlan p, QueryState qs, ui
       __syncthreads();
     }
   for (uint32_t i = threadIdx.x; i < p.nprobe; i += blockDim.x)
-    if (s[i] >= p.nlists || (i + 1 < p.nprobe && s[i] == s[i + 1])) bad = 1;
+    if (s[i] != kNoProbe && (s[i] >= p.nlists || (i + 1 < p.nprobe && s[i] == s[i + 1]))) bad = 1;
   __syncthreads();
   if (bad) {
     if (threadIdx.x == 0) {
@@ -161,7 +162,8 @@ __global__ void __launch_bounds__(256) probe_count(ListPlan p, QueryState qs, ui
     return;
   }
   if (qs.status[q]) return;
-  for (uint32_t i = threadIdx.x; i < p.nprobe; i += blockDim.x) atomicAdd(p.lcount + pr[i], 1ull);
+  for (uint32_t i = threadIdx.x; i < p.nprobe; i += blockDim.x)
+    if (pr[i] != kNoProbe) atomicAdd(p.lcount + pr[i], 1ull);
 }
 
 __global__ void probe_fill(ListPlan p, QueryState qs) {
@@ -170,18 +172,29 @@ __global__ void probe_fill(ListPlan p, QueryState qs) {
   const uint32_t *pr = p.probes + (uint64_t)q * p.nprobe;
   for (uint32_t i = 0; i < p.nprobe; i++) {
     const uint32_t l = pr[i];
+    if (l == kNoProbe) continue;
     const unsigned long long slot = atomicAdd(p.lfill + l, 1ull);
     p.qlist[p.qoff[l] + slot] = q;
   }
 }
 
-// Work items of list l: row tiles (of its first `limit` rows) x query groups.
-__global__ void count_tiles(ListPlan p, uint64_t limit) {
-  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
-  if (l >= p.nlists) return;
+// Rows [lo + rbegin, lo + rend) of list l, clipped to the list.
+__device__ __forceinline__ void list_window(const ListPlan &p, uint32_t l, uint64_t rbegin, uint64_t rend,
+                                            uint64_t &b, uint64_t &e) {
   uint64_t lo, hi;
   list_range(p, l, lo, hi);
-  const uint64_t len = hi - lo < limit ? hi - lo : limit;
+  const uint64_t len = hi - lo;
+  b = lo + (rbegin < len ? rbegin : len);
+  e = lo + (rend < len ? rend : len);
+}
+
+// Work items of list l: row tiles of its rows [rbegin, rend) x query groups.
+__global__ void count_tiles(ListPlan p, uint64_t rbegin, uint64_t rend) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= p.nlists) return;
+  uint64_t b, e;
+  list_window(p, l, rbegin, rend, b, e);
+  const uint64_t len = e - b;
   const uint64_t groups = (p.lcount[l] + BQ - 1) / BQ;
   p.tiles[l] = (len + BM - 1) / BM * groups;
 }
@@ -200,7 +213,8 @@ __device__ __forceinline__ uint32_t find_list(const unsigned long long *toff, ui
 }
 
 template <int DT>
-__global__ void __launch_bounds__(256) simt_scan_lists(const ListPlan p, uint64_t limit, const ScanArgs a) {
+__global__ void __launch_bounds__(256) simt_scan_lists(const ListPlan p, uint64_t rbegin, uint64_t rend,
+                                                        const ScanArgs a) {
   __shared__ __align__(16) float xs[BK][BM + 4];
   __shared__ float qs[BK][BQ + 4];
   __shared__ uint32_t qidx[BQ];
@@ -216,8 +230,7 @@ __global__ void __launch_bounds__(256) simt_scan_lists(const ListPlan p, uint64_
     const uint64_t groups = (nql + BQ - 1) / BQ;
     const uint64_t g = t % groups, rt = t / groups;
     uint64_t lo, hi;
-    list_range(p, l, lo, hi);
-    if (hi - lo > limit) hi = lo + limit;
+    list_window(p, l, rbegin, rend, lo, hi);
     const uint64_t r0 = lo + rt * BM;
     const uint32_t nqt = (uint32_t)(nql - g * BQ < BQ ? nql - g * BQ : BQ);
     if (tid < BQ) qidx[tid] = tid < (int)nqt ? p.qlist[p.qoff[l] + g * BQ + tid] : 0u;
@@ -283,19 +296,20 @@ void launch_list_plan(const ListPlan &p, const QueryState &qs, uint32_t *flags, 
   probe_fill<<<(p.nq + 127) / 128, 128, 0, st>>>(p, qs);
 }
 
-// Items of a pass over the first `limit` rows of every probed list.
-void launch_list_items(const ListPlan &p, uint64_t limit, cudaStream_t st) {
-  if (p.nlists) count_tiles<<<(p.nlists + 255) / 256, 256, 0, st>>>(p, limit);
+// Items of a pass over rows [rbegin, rend) of every probed list.
+void launch_list_items(const ListPlan &p, uint64_t rbegin, uint64_t rend, cudaStream_t st) {
+  if (p.nlists) count_tiles<<<(p.nlists + 255) / 256, 256, 0, st>>>(p, rbegin, rend);
   exclusive_scan(p.tiles, p.nlists, p.toff, p.bsum, st);
 }
 
-void launch_simt_scan_lists(const ListPlan &p, uint64_t limit, const ScanArgs &a, int sms, cudaStream_t st) {
+void launch_simt_scan_lists(const ListPlan &p, uint64_t rbegin, uint64_t rend, const ScanArgs &a, int sms,
+                            cudaStream_t st) {
   const dim3 grid((unsigned)sms * 8);
   switch (a.s.dtype) {
-    case DT_F32: simt_scan_lists<DT_F32><<<grid, 256, 0, st>>>(p, limit, a); break;
-    case DT_F16: simt_scan_lists<DT_F16><<<grid, 256, 0, st>>>(p, limit, a); break;
-    case DT_E4M3: simt_scan_lists<DT_E4M3><<<grid, 256, 0, st>>>(p, limit, a); break;
-    case DT_NVFP4: simt_scan_lists<DT_NVFP4><<<grid, 256, 0, st>>>(p, limit, a); break;
+    case DT_F32: simt_scan_lists<DT_F32><<<grid, 256, 0, st>>>(p, rbegin, rend, a); break;
+    case DT_F16: simt_scan_lists<DT_F16><<<grid, 256, 0, st>>>(p, rbegin, rend, a); break;
+    case DT_E4M3: simt_scan_lists<DT_E4M3><<<grid, 256, 0, st>>>(p, rbegin, rend, a); break;
+    case DT_NVFP4: simt_scan_lists<DT_NVFP4><<<grid, 256, 0, st>>>(p, rbegin, rend, a); break;
     default: break;
   }
 }

@@ -752,19 +752,21 @@ extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq,
 
 namespace {
 
-// One IVF search over queries [q0, q0+nq): plan (probe inversion), a sample
-// pass over the first S rows of every probed list with no threshold, the
-// bound from its k-th score, the full pass over the probed lists, then the
-// flat search's survivor selection, exact rescoring and ordering.
+// One IVF search over queries [q0, q0+nq): plan (probe inversion), then the
+// probed lists' rows in windows of growing depth -- rows [0, S) of every
+// list (S >= k, so one list alone can supply a bound), then [S, 8S),
+// [8S, 64S) ... -- each window appending the rows that pass the current
+// thresholds and each followed by a tighten that lowers them from the k-th
+// candidate so far (a window appends about 7k rows a query once k rows of
+// its lists have been seen). Then the flat search's survivor selection,
+// exact rescoring and ordering.
 int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *offsets,
                        uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids, uint32_t k,
                        uint32_t metric, uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
                        int32_t *status, cudaStream_t st, bool *any_invalid) {
   const ShardView &v = sh->view;
   const double gamma = scan_gamma(false, false, 0, v.dims);
-  // sample rows a list: enough that nprobe lists give about 4k rows
-  const uint64_t want = (4ull * k + nprobe - 1) / std::max<uint32_t>(nprobe, 1);
-  const uint64_t S = std::max<uint64_t>(64, (want + 63) / 64 * 64);
+  const uint64_t S = std::max<uint64_t>(64, ((uint64_t)k + 63) / 64 * 64);
 
   Carver c;
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
@@ -802,6 +804,7 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   p.bsum = (unsigned long long *)(w + o_bsum);
   p.qlist = (uint32_t *)(w + o_qlist);
 
+  // the first window appends at most nprobe * S rows a query: it never overflows
   uint32_t cap = (uint32_t)std::max<uint64_t>({kBaseCap, 8ull * k, (uint64_t)nprobe * S});
   CK(sh->cand.reserve((size_t)nq * cap * sizeof(uint2)), "candidate lists");
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
@@ -847,10 +850,10 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   sl.out_cap = out_cap;
   sl.first_id = sh->first;
 
-  auto pass = [&](int stage, uint64_t limit) -> cudaError_t {
+  auto pass = [&](int stage, uint64_t rbegin, uint64_t rend) -> cudaError_t {
     int hk = clock.begin(stage);
-    launch_list_items(p, limit, st);
-    launch_simt_scan_lists(p, limit, a, sh->sms, st);
+    launch_list_items(p, rbegin, rend, st);
+    launch_simt_scan_lists(p, rbegin, rend, a, sh->sms, st);
     clock.end(hk);
     counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1);
     return cudaGetLastError();
@@ -863,13 +866,14 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
     sl.cap = cap;
     launch_fill_thresholds(nq, qs, st);
     counted(1);
-    CK(pass(ST_SAMPLE, S), "sample pass");
-    h = clock.begin(ST_BOUND);
-    launch_tighten(sl, st);
-    CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
-    clock.end(h);
-    counted(1);
-    CK(pass(ST_FILTER, ~0ull), "list pass");
+    for (uint64_t rb = 0, re = S;; rb = re, re = std::min<uint64_t>(re * 8, v.rows)) {
+      CK(pass(rb == 0 ? ST_SAMPLE : ST_FILTER, rb, re), "list pass");
+      if (re >= v.rows) break;
+      h = clock.begin(rb == 0 ? ST_BOUND : ST_TIGHTEN);
+      launch_tighten(sl, st);
+      clock.end(h);
+      counted(1);
+    }
     h = clock.begin(ST_TIGHTEN);
     launch_survivors(sl, st);
     clock.end(h);

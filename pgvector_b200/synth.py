@@ -138,3 +138,72 @@ def torch_bitmap(n, selectivity, seed=0, device='cuda'):
     w = (bits.view(nw, 32).to(torch.int64) << torch.arange(32, device=device, dtype=torch.int64)).sum(dim=1)
     # the same 32 bits as a signed int32 (two's complement)
     return torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+
+
+# ---------------------------------------------------------------- torch quantizers (builder semantics)
+#
+# The index builder's FP8 and NVFP4 quantizers (ann/builder/build_cuvs_index.py
+# :296-348) restated over torch tensors, so full-size corpora can be encoded
+# on the GPU; oracle.quantize_fp8 / quantize_nvfp4 are the C statements of
+# the same steps, and tests/test_oracle.py checks that both agree bit for bit.
+
+def _e4m3_table(device):
+    """Non-negative E4M3 magnitudes of codes 0..126, increasing."""
+    import torch
+    c = torch.arange(127, device=device)
+    e = (c >> 3).to(torch.float32)
+    m = (c & 7).to(torch.float32)
+    return torch.where(c < 8, m * 2.0 ** -9, (8.0 + m) * torch.exp2(e - 10.0)).to(torch.float32)
+
+
+def _nearest(table, x):
+    """Index of the nearest table entry (ties to the lower entry)."""
+    import torch
+    size = table.numel()
+    i = torch.searchsorted(table, x.contiguous()).clamp_(1, size - 1)
+    below, above = table[i - 1], table[i]
+    return torch.where((x - below) <= (above - x), i - 1, i)
+
+
+def torch_quantize_fp8(x):
+    """[n, d] float32 -> (codes uint8 [n, ceil(d/16)*16], row scales float32
+    [n]): scale = absmax/448, code = nearest E4M3 magnitude of |v/scale|
+    with the sign in bit 7."""
+    import torch
+    n, d = x.shape
+    pad = (d + 15) // 16 * 16
+    amax = x.abs().amax(dim=1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    v = x / scale[:, None]
+    code = _nearest(_e4m3_table(x.device), v.abs()).to(torch.uint8)
+    code = code | torch.where(v < 0, 0x80, 0).to(torch.uint8)
+    out = torch.zeros((n, pad), dtype=torch.uint8, device=x.device)
+    out[:, :d] = code
+    return out, scale
+
+
+def torch_quantize_nvfp4(x):
+    """[n, d] float32 -> (packed uint8 [n, blocks*8], block scale codes uint8
+    [n, blocks], row scales float32 [n]), blocks = ceil(d/16): row =
+    absmax/(6*448); a block's scale code is the smallest E4M3 entry >=
+    blockmax/(6*row) (at most 126); values are the nearest E2M1 magnitude of
+    min(|v/(table[code]*row)|, 6), sign in bit 3, even dimension low."""
+    import torch
+    n, d = x.shape
+    blocks = (d + 15) // 16
+    xp = torch.zeros((n, blocks * 16), dtype=torch.float32, device=x.device)
+    xp[:, :d] = x
+    amax = x.abs().amax(dim=1)
+    row = torch.where(amax > 0, amax / 2688.0, torch.ones_like(amax))
+    six = 6.0 * row
+    xb = xp.view(n, blocks, 16)
+    bmax = xb.abs().amax(dim=2)
+    table = _e4m3_table(x.device)
+    code = torch.searchsorted(table, (bmax / six[:, None]).contiguous()).clamp_(max=126)
+    scale = table[code] * row[:, None]
+    v = torch.where(scale[:, :, None] > 0, xb / scale[:, :, None], torch.zeros_like(xb))
+    e2m1 = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=torch.float32, device=x.device)
+    nib = _nearest(e2m1, v.abs().clamp(max=6.0)).to(torch.uint8) | torch.where(v < 0, 8, 0).to(torch.uint8)
+    nib = nib.view(n, blocks * 8, 2)
+    packed = nib[:, :, 0] | (nib[:, :, 1] << 4)
+    return packed.contiguous(), code.to(torch.uint8).contiguous(), row

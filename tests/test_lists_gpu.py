@@ -128,3 +128,27 @@ def test_bad_probes_are_invalid_queries(cuda):
     od, oi, oc = oracle.search_lists(oracle.F32, 16, x, q[[0, 3]], offsets, good, 5, 0)
     gd, gi, gc = gpu_lists(cuda, oracle.F32, 16, x, None, None, q[[0, 3]], offsets, good, 5, 0)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+def test_padding_probes_and_list_shards(cuda):
+    # lists sharded over two "ranks": each shard sees only its own lists, the
+    # others padded with UINT32_MAX; merging both shards' results gives the
+    # unsharded answer
+    import torch
+    import pgvector_b200 as pb
+    x, offsets, cent, row_ids = synth.ivf_corpus(30000, 48, 96, seed=70)
+    q = cent[np.arange(40) % 96] + 0.05
+    probes = synth.ivf_probes(q, cent, 10)
+    od, oi, oc = oracle.search_lists(oracle.F32, 48, x, q, offsets, probes, 25, 0, row_ids=row_ids)
+    parts = []
+    for l0, l1 in ((0, 50), (50, 96)):
+        lo, hi = int(offsets[l0]), int(offsets[l1])
+        local = np.where((probes >= l0) & (probes < l1), probes - l0, 0xffffffff).astype(np.uint32)
+        off = (offsets[l0:l1 + 1] - offsets[l0]).astype(np.uint64)
+        parts.append(gpu_lists(cuda, oracle.F32, 48, x[lo:hi], None, None, q, off, local, 25, 0, row_ids[lo:hi]))
+    gd = torch.from_numpy(np.stack([p[0] for p in parts])).to(cuda)
+    gi = torch.from_numpy(np.stack([p[1] for p in parts])).to(cuda)
+    gc = torch.from_numpy(np.stack([p[2] for p in parts]).astype(np.int32)).to(cuda)
+    md, mi, mc = pb.merge_topk(gd, gi, gc, 25)
+    assert np.array_equal(mc.cpu().numpy(), oc.astype(np.int32))
+    assert np.array_equal(mi.cpu().numpy(), oi) and np.array_equal(md.cpu().numpy(), od)

@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 
 import oracle
+from pgvector_b200 import synth
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
 
@@ -235,3 +236,19 @@ def test_tree_merge_golden_equals_sorted_union():
         union = sorted((float(np.float32(d)), int(key)) for _, key, d in lists)
         merged = g['merged%d' % t]
         assert [int(key) for key, _ in merged] == [key for _, key in union[:k]]
+
+
+@pytest.mark.parametrize('dims', [768, 37, 1024])
+def test_torch_quantizers_match_the_oracle(dims):
+    # the bench encodes full-size corpora on the GPU with the torch statement
+    # of the builder's quantizers; on the CPU both must agree bit for bit
+    import torch
+    x = synth.mixture(3000, dims, 20, seed=90 + dims)
+    x[5] = 0.0
+    x[7, :5] = [448.0, -1e-9, 3e-7, -6.0, 0.25]
+    codes, scale = oracle.quantize_fp8(x)
+    tc, ts = synth.torch_quantize_fp8(torch.from_numpy(x))
+    assert np.array_equal(tc.numpy(), codes) and np.array_equal(ts.numpy(), scale)
+    packed, sc, row = oracle.quantize_nvfp4(x)
+    tp, tsc, tr = synth.torch_quantize_nvfp4(torch.from_numpy(x))
+    assert np.array_equal(tp.numpy(), packed) and np.array_equal(tsc.numpy(), sc) and np.array_equal(tr.numpy(), row)
