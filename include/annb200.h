@@ -68,6 +68,10 @@ extern "C"
 								 * distance (ann/server/backend.h:45-50) */
 #define ANNB200_FORCE_SIMT 2u	/* score on CUDA cores even where the tcgen05
 								 * tensor-core scan applies */
+#define ANNB200_INDEX_L2 4u		/* L2 in the loaded-index form: the FP32
+								 * sqrtf of tail + (left + right) lane sums
+								 * (Distance, ann/server/indexfile.c:3133-3151)
+								 * instead of the gathered jobs' FP64 sqrt */
 
 typedef struct AnnB200Shard AnnB200Shard;
 
@@ -207,6 +211,36 @@ int			AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows,
  */
 int			AnnB200BitmapRowsStatic(const uint32_t *words, uint64_t nbits, uint32_t *rows,
 									uint64_t *count, void *stream);
+
+/*
+ * Loaded on-disk indexes (the worker's load_index / search_index,
+ * ann/server/backend.h:133-135). An AnnB200Index holds an index directory's
+ * FP32 rows (vectors.f32, ann/common/INDEX_FORMAT.md, row i = the i-th
+ * smallest key) resident on one device; AnnB200IndexSearch is the exact
+ * route of the reference's loaded-index search (AnnIndexExact + Offer +
+ * AnnIndexTreeMerge, ann/server/indexfile.c:3134-3258): per query the k
+ * rows of smallest FP32 L2 distance (Distance's own arithmetic, bit for
+ * bit), sorted by (distance, ordinal) -- key order is ordinal order, so this
+ * is the reference's (distance, key) order.
+ *
+ * AnnB200IndexCreate copies rows x dims host floats (an mmap of vectors.f32
+ * is fine) to `device` (-1: the next device round robin) and returns once
+ * the index is searchable.
+ *
+ * AnnB200IndexSearch takes host memory throughout: queries [nq][dims];
+ * ordinals (NULL: every row) a strictly increasing list of eligible rows,
+ * nordinals long; results [nq][k] distances and ordinals and counts [nq].
+ * Synchronous; safe to call from many threads at once (each thread stages
+ * through its own buffers). ANN_INVALID for a non-finite query or an
+ * ordinal list that is not increasing or runs past the rows.
+ */
+typedef struct AnnB200Index AnnB200Index;
+int			AnnB200IndexCreate(int device, uint32_t dims, uint64_t rows, const float *vectors,
+							   AnnB200Index **index);
+void		AnnB200IndexDestroy(AnnB200Index *index);
+int			AnnB200IndexSearch(AnnB200Index *index, const float *queries, uint32_t nq,
+							   const uint64_t *ordinals, uint64_t nordinals, uint32_t k,
+							   float *out_dist, uint64_t *out_ordinal, uint32_t *out_count);
 
 /*
  * Kernels this library has launched in this process (all devices). A caller

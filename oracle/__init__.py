@@ -36,6 +36,8 @@ def build(reference=None):
     subprocess.run(['make', '-s', '-C', HERE, 'all'], check=True)
     if os.path.isdir(os.path.join(ref, 'ann', 'server')):
         subprocess.run(['make', '-s', '-C', HERE, 'ref', 'REF=' + ref], check=True)
+        if os.path.exists(os.path.join(os.path.dirname(HERE), 'pgvector_b200', 'libannb200.so')):
+            subprocess.run(['make', '-s', '-C', HERE, 'worker', 'REF=' + ref], check=True)
 
 
 def lib():

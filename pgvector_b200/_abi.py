@@ -34,6 +34,26 @@ DEVICE_JOBS = ctypes.CFUNCTYPE(ctypes.c_uint64)
 LOST = ctypes.CFUNCTYPE(ctypes.c_char_p)
 
 
+class AnnIndexHit(ctypes.Structure):
+    _fields_ = [('key', ctypes.c_int64), ('distance', ctypes.c_float), ('ordinal', ctypes.c_uint64)]
+
+
+class AnnIndexJob(ctypes.Structure):
+    _fields_ = [('name', ctypes.c_char * 64), ('dimensions', ctypes.c_uint32), ('k', ctypes.c_uint32),
+                ('query', ctypes.POINTER(ctypes.c_float)), ('filter', ctypes.POINTER(ctypes.c_int64)),
+                ('nfilter', ctypes.c_uint32), ('filtered', ctypes.c_int),
+                ('ordinals', ctypes.POINTER(ctypes.c_uint64)), ('bitsets', ctypes.c_void_p),
+                ('deviceBitsets', ctypes.c_void_p), ('deviceRows', ctypes.c_void_p),
+                ('results', ctypes.POINTER(AnnIndexHit)), ('nresults', ctypes.c_uint32),
+                ('route', ctypes.c_uint32), ('status', ctypes.c_int),
+                ('exclude', ctypes.POINTER(ctypes.c_uint64)), ('nexclude', ctypes.c_uint32),
+                ('ownedOrdinals', ctypes.POINTER(ctypes.c_uint64))]
+
+
+LOAD_INDEX = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p)
+SEARCH_INDEX = ctypes.CFUNCTYPE(None, ctypes.POINTER(AnnIndexJob), ctypes.c_uint32)
+
+
 class AnnBackend(ctypes.Structure):
     _fields_ = [('name', ctypes.c_char_p), ('metrics', ctypes.c_uint32), ('filters', ctypes.c_uint32),
                 ('algorithm', ctypes.c_char_p), ('storage', ctypes.c_char_p), ('exact', ctypes.c_int),

@@ -56,6 +56,8 @@ typedef struct Lane
 	int64_t    *id;
 	uint32_t   *count;
 	size_t		resultCap;
+	uint32_t   *counts;			/* device: per-query counts of a batch */
+	size_t		countsBytes;
 	double	   *hostDist;		/* pinned result staging */
 	int64_t    *hostId;
 	size_t		hostCap;
@@ -291,6 +293,174 @@ GatheredJob(AnnGatheredJob *job)
 	job->nresults = count;
 	job->status = ANN_OK;
 	atomic_fetch_add(&DeviceJobs, 1);
+}
+
+/* ---------------------------------------------------------------- loaded indexes */
+
+#define INDEX_MAX_DEVICES 64
+
+struct AnnB200Index
+{
+	int			device;
+	uint32_t	dims;
+	uint64_t	rows;
+	AnnB200Shard *shard;		/* owns the device copy of the rows */
+};
+
+/* Per thread and device: staging for index searches on that device. */
+static _Thread_local Lane IndexLanes[INDEX_MAX_DEVICES];
+
+static Lane *
+LaneOn(int device)
+{
+	Lane	   *lane;
+
+	if (device < 0 || device >= INDEX_MAX_DEVICES)
+		return NULL;
+	lane = &IndexLanes[device];
+	if (cudaSetDevice(device) != cudaSuccess)
+		return NULL;
+	if (!lane->ready)
+	{
+		lane->device = device;
+		if (cudaStreamCreateWithFlags(&lane->stream, cudaStreamNonBlocking) != cudaSuccess)
+			return NULL;
+		lane->ready = 1;
+	}
+	return lane;
+}
+
+int
+AnnB200IndexCreate(int device, uint32_t dims, uint64_t rows, const float *vectors, AnnB200Index **out)
+{
+	AnnB200Index *ix;
+	int			devices = AnnB200DeviceCount();
+	int			prev = 0;
+	int			status;
+
+	if (out == NULL)
+		return ANN_INVALID;
+	*out = NULL;
+	if (dims == 0 || rows == 0 || rows > UINT32_MAX || vectors == NULL)
+		return ANN_INVALID;
+	if (devices <= 0)
+		return ANN_BACKEND_ERROR;
+	if (device < 0)
+		device = (int) (atomic_fetch_add(&NextLane, 1) % (unsigned) devices);
+	if (device >= devices || device >= INDEX_MAX_DEVICES)
+		return ANN_INVALID;
+	ix = calloc(1, sizeof(*ix));
+	if (ix == NULL)
+		return ANN_NOMEM;
+	ix->device = device;
+	ix->dims = dims;
+	ix->rows = rows;
+	cudaGetDevice(&prev);
+	status = AnnB200ShardCreate(device, ANNB200_F32, dims, rows, vectors, NULL, NULL, 0, ANNB200_SHARD_HOST,
+								NULL, &ix->shard);
+	cudaSetDevice(prev);
+	if (status != ANN_OK)
+	{
+		free(ix);
+		return status;
+	}
+	*out = ix;
+	return ANN_OK;
+}
+
+void
+AnnB200IndexDestroy(AnnB200Index *ix)
+{
+	if (ix == NULL)
+		return;
+	AnnB200ShardDestroy(ix->shard);
+	free(ix);
+}
+
+int
+AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const uint64_t *ordinals,
+				   uint64_t nordinals, uint32_t k, float *out_dist, uint64_t *out_ordinal, uint32_t *out_count)
+{
+	Lane	   *lane;
+	uint32_t   *rows = NULL;
+	uint32_t   *counts = NULL;
+	size_t		values,
+				results;
+	int			prev = 0;
+	int			status = ANN_OK;
+
+	if (ix == NULL || (nq && (queries == NULL || out_count == NULL)))
+		return ANN_INVALID;
+	if (nq == 0)
+		return ANN_OK;
+	if (k && (out_dist == NULL || out_ordinal == NULL))
+		return ANN_INVALID;
+	values = (size_t) nq * ix->dims;
+	if (!AllFinite(queries, values))
+		return ANN_INVALID;
+	for (uint64_t i = 0; ordinals && i < nordinals; i++)
+		if (ordinals[i] >= ix->rows || (i && ordinals[i] <= ordinals[i - 1]))
+			return ANN_INVALID;
+	memset(out_count, 0, sizeof(*out_count) * nq);
+	if (k == 0 || (ordinals && nordinals == 0))
+		return ANN_OK;
+	if (InjectLost())
+		return ANN_BACKEND_ERROR;
+	results = (size_t) nq * k;
+	cudaGetDevice(&prev);
+	lane = LaneOn(ix->device);
+	if (lane == NULL)
+	{
+		cudaSetDevice(prev);
+		return ANN_BACKEND_ERROR;
+	}
+	counts = malloc(sizeof(*counts) * nq);
+	if (ordinals)
+		rows = malloc(sizeof(*rows) * nordinals);
+	if (counts == NULL || (ordinals && rows == NULL) ||
+		!Grow((void **) &lane->query, &lane->queryBytes, values * sizeof(float)) ||
+		(ordinals && !Grow((void **) &lane->ids, &lane->idsBytes, nordinals * sizeof(uint32_t))) ||
+		!LaneResults(lane, results) ||
+		!Grow((void **) &lane->counts, &lane->countsBytes, nq * sizeof(uint32_t)))
+		status = ANN_NOMEM;
+	for (uint64_t i = 0; status == ANN_OK && ordinals && i < nordinals; i++)
+		rows[i] = (uint32_t) ordinals[i];
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(lane->query, queries, values * sizeof(float), cudaMemcpyHostToDevice,
+						 lane->stream) != cudaSuccess ||
+		 (ordinals && cudaMemcpyAsync(lane->ids, rows, nordinals * sizeof(uint32_t), cudaMemcpyHostToDevice,
+									  lane->stream) != cudaSuccess)))
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK)
+		status = AnnB200Search(ix->shard, lane->query, nq, ordinals ? lane->ids : NULL, ordinals ? nordinals : 0,
+							   k, ANNB200_L2, ANNB200_INDEX_L2, k, lane->dist, lane->id, lane->counts, NULL,
+							   lane->stream);
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(counts, lane->counts, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostDist, lane->dist, results * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, results * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK)
+	{
+		for (uint32_t q = 0; q < nq; q++)
+		{
+			out_count[q] = counts[q];
+			for (uint32_t i = 0; i < counts[q]; i++)
+			{
+				out_dist[(size_t) q * k + i] = (float) lane->hostDist[(size_t) q * k + i];
+				out_ordinal[(size_t) q * k + i] = (uint64_t) lane->hostId[(size_t) q * k + i];
+			}
+		}
+		atomic_fetch_add(&DeviceJobs, 1);
+	}
+	free(rows);
+	free(counts);
+	cudaSetDevice(prev);
+	return status;
 }
 
 static void

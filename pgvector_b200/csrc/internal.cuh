@@ -330,6 +330,7 @@ struct SelectLaunch {
   uint32_t *out_count;
   uint32_t out_cap;
   int64_t first_id;
+  int index_form;           // L2 distances in the loaded-index form (FP32 sqrtf)
 };
 
 // ---------------------------------------------------------------- launchers

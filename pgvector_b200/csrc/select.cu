@@ -175,13 +175,24 @@ __device__ __forceinline__ void decode_raw8(const Raw8<DT> &r, float rs, float v
   }
 }
 
+// Final L2 of the eight lane sums and the tail. Gathered jobs
+// (ann/server/cpu.c L2Squared): sqrt in FP64 of (tail + left) + right.
+// Loaded indexes (ann/server/indexfile.c Distance): sqrtf of
+// tail + (left + right), an FP32 distance.
+__device__ __forceinline__ double l2_finish(const float (&sums)[8], float tail, int index_form) {
+  const float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
+  const float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
+  if (index_form) return (double)__fsqrt_rn(__fadd_rn(tail, __fadd_rn(left, right)));
+  return __dsqrt_rn((double)__fadd_rn(__fadd_rn(tail, left), right));
+}
+
 // The reference CPU worker's distance of one decoded row (see file header),
 // with the row streamed in batches of 64 dimensions: the next batch's loads
 // are issued before the current batch is summed, and the sums keep the
 // reference's exact operation order.
 template <int DT>
 __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q, uint32_t metric,
-                                 double qn2d, const uint8_t *row) {
+                                 double qn2d, const uint8_t *row, int index_form) {
   const uint32_t dims = s.dims;
   if (DT == DT_BIT) {
     const uint8_t *qb = reinterpret_cast<const uint8_t *>(q);
@@ -240,12 +251,7 @@ __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q
         }
       }
     }
-    if (metric == M_L2) {
-      float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
-      float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
-      float total = __fadd_rn(__fadd_rn(tail, left), right);
-      return __dsqrt_rn((double)total);
-    }
+    if (metric == M_L2) return l2_finish(sums, tail, index_form);
     if (metric == M_IP) return -dot;
     const double nrm = s.n2x[id];
     double r = __ddiv_rn(dot, __dsqrt_rn(__dmul_rn(nrm, qn2d)));
@@ -467,6 +473,7 @@ struct SelectArgs {
   uint32_t *out_count;
   uint32_t out_cap;
   int64_t first_id;
+  int index_form;         // L2 distances in the loaded-index form (FP32 sqrtf)
 };
 
 // Lower a query's threshold with the k-th smallest v among its candidates and
@@ -648,7 +655,7 @@ __global__ void __launch_bounds__(128) rescore_thread(SelectArgs a, unsigned lon
     const uint32_t p = e[i].y;
     const uint64_t id = cand_row(a.ids, p, a.s.rows);
     const uint8_t *row = a.staged ? a.staged + (uint64_t)p * a.s.row_bytes : a.s.codes + id * a.s.row_bytes;
-    exact[(uint64_t)q * kSortCap + i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row));
+    exact[(uint64_t)q * kSortCap + i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row, a.index_form));
   }
 }
 
@@ -782,10 +789,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned 
   if (DT == DT_BIT) {
     dist = (double)ham;
   } else if (a.metric == M_L2) {
-    float left = __fadd_rn(__fadd_rn(sums[0], sums[1]), __fadd_rn(sums[2], sums[3]));
-    float right = __fadd_rn(__fadd_rn(sums[4], sums[5]), __fadd_rn(sums[6], sums[7]));
-    float total = __fadd_rn(__fadd_rn(tail, left), right);
-    dist = __dsqrt_rn((double)total);
+    dist = l2_finish(sums, tail, a.index_form);
   } else if (a.metric == M_IP) {
     dist = -dot;
   } else {
@@ -840,7 +844,7 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
       uint32_t p = e[i].y;
       uint64_t id = cand_row(a.ids, p, a.s.rows);
       const uint8_t *row = a.staged ? a.staged + (uint64_t)p * a.s.row_bytes : a.s.codes + id * a.s.row_bytes;
-      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row));
+      key[i] = double_key(exact_distance<DT>(a.s, id, qv, a.metric, qn2d, row, a.index_form));
       pos[i] = gid_key(a, p);
     } else {
       key[i] = ~0ull;
@@ -1071,7 +1075,7 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
 static SelectArgs to_args(const SelectLaunch &l) {
   SelectArgs a{l.s,   l.staged, l.row_ids, l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
                l.cnt, l.cand,  l.cap,     l.flags, l.big,    l.out_dist, l.out_id,    l.out_count, l.out_cap,
-               l.first_id};
+               l.first_id, l.index_form};
   return a;
 }
 

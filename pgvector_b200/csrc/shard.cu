@@ -581,6 +581,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   sl.out_count = out_count;
   sl.out_cap = out_cap;
   sl.first_id = sh->first;
+  sl.index_form = (flags & ANNB200_INDEX_L2) && metric == M_L2;
 
   if (k > 0 && n > 0) {
     // staging: the pass's gathered candidate rows, then the sample's

@@ -91,6 +91,29 @@ def ivf_probes(queries, centroids, nprobe):
     return np.argsort(d2, axis=1, kind='stable')[:, :nprobe].astype(np.uint32)
 
 
+def write_index_dir(directory, keys, vectors, shards=1):
+    """An index directory in the worker's documented format
+    (ann/common/INDEX_FORMAT.md, version 1): rows sorted by key into
+    keys.i64 and vectors.f32, and a manifest naming `shards` contiguous
+    graphless shards. Returns (sorted keys, rows in key order)."""
+    import os
+    order = np.argsort(np.asarray(keys, dtype=np.int64), kind='stable')
+    k = np.ascontiguousarray(np.asarray(keys, dtype=np.int64)[order])
+    v = np.ascontiguousarray(np.asarray(vectors, dtype=np.float32)[order])
+    n, d = v.shape
+    os.makedirs(directory, exist_ok=True)
+    k.astype('<i8').tofile(os.path.join(directory, 'keys.i64'))
+    v.astype('<f4').tofile(os.path.join(directory, 'vectors.f32'))
+    bounds = [n * i // shards for i in range(shards + 1)]
+    lines = ['pgvector-ann-index 1', 'dimensions %d' % d, 'rows %d' % n, 'metric l2', 'dtype float32',
+             'shards %d' % shards]
+    lines += ['shard %d %d %d -' % (i, bounds[i], bounds[i + 1] - bounds[i]) for i in range(shards)]
+    with open(os.path.join(directory, 'manifest.tmp'), 'w') as f:
+        f.write('\n'.join(lines) + '\n')
+    os.rename(os.path.join(directory, 'manifest.tmp'), os.path.join(directory, 'manifest'))
+    return k, v
+
+
 # ---------------------------------------------------------------- torch (full size, on the GPU)
 
 def torch_mixture(n, d, centres, sigma=0.1, seed=0, normalize=False, dtype=None, device='cuda',

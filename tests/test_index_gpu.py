@@ -1,0 +1,163 @@
+"""Loaded on-disk indexes: the b200 backend's load_index / search_index
+against the reference worker's own cpu backend on the same directory.
+
+Both backends are driven through the worker's backend vtable
+(ann/server/backend.h:114-151) in one process: the reference's cpu backend
+and index registry from oracle/_ref/libannref.so (compiled from the
+reference sources), and AnnB200WorkerBackend() from
+oracle/_ref/libannb200_worker.so (pgvector_b200/csrc/worker_index.c linked
+against that registry and libannb200.so, as the worker's build links it).
+Bar: every hit's key, FP32 distance (bit for bit) and ordinal, the counts,
+routes and statuses equal the cpu backend's (ann/server/cpu.c:298-407).
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from pgvector_b200 import _abi, synth
+
+pytestmark = pytest.mark.gpu
+
+WORKER_SO = os.path.join(os.path.dirname(oracle.REF_SO), 'libannb200_worker.so')
+
+
+@pytest.fixture(scope='module')
+def backends(cuda):
+    if not (os.path.exists(oracle.REF_SO) and os.path.exists(WORKER_SO)):
+        pytest.skip('reference worker library not built (make -C oracle ref worker)')
+    import pgvector_b200 as pb
+    pb.load()
+    ref = ctypes.CDLL(oracle.REF_SO, mode=ctypes.RTLD_GLOBAL)
+    ref.AnnCpuBackend.restype = ctypes.POINTER(_abi.AnnBackend)
+    worker = ctypes.CDLL(WORKER_SO, mode=ctypes.RTLD_GLOBAL)
+    worker.AnnB200WorkerBackend.restype = ctypes.POINTER(_abi.AnnBackend)
+    return ref.AnnCpuBackend().contents, worker.AnnB200WorkerBackend().contents
+
+
+def load(backend, name, directory):
+    return _abi.LOAD_INDEX(backend.load_index)(name.encode(), directory.encode())
+
+
+class Jobs:
+    """A batch of AnnIndexJob with the buffers they point at kept alive."""
+
+    def __init__(self):
+        self.specs = []
+
+    def add(self, name, query, k, keys=None, ordinals=None, exclude=None, dims=None):
+        self.specs.append(dict(name=name, query=np.ascontiguousarray(query, dtype=np.float32), k=k, keys=keys,
+                               ordinals=ordinals, exclude=exclude, dims=dims))
+        return self
+
+    def run(self, backend, rename=None):
+        n = len(self.specs)
+        jobs = (_abi.AnnIndexJob * n)()
+        keep = []
+        for job, s in zip(jobs, self.specs):
+            name = s['name'] if rename is None else rename.get(s['name'], s['name'])
+            job.name = name.encode()
+            job.dimensions = s['dims'] if s['dims'] is not None else s['query'].shape[0]
+            job.k = s['k']
+            job.query = s['query'].ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            res = (_abi.AnnIndexHit * max(s['k'], 1))()
+            job.results = res
+            keep += [s['query'], res]
+            if s['keys'] is not None:
+                arr = np.ascontiguousarray(s['keys'], dtype=np.int64)
+                job.filter = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
+                job.nfilter = len(arr)
+                job.filtered = 1
+                keep.append(arr)
+            if s['ordinals'] is not None:
+                arr = np.ascontiguousarray(s['ordinals'], dtype=np.uint64)
+                job.ordinals = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
+                job.nfilter = len(arr)
+                job.filtered = 1
+                keep.append(arr)
+            if s['exclude'] is not None:
+                arr = np.ascontiguousarray(s['exclude'], dtype=np.uint64)
+                job.exclude = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
+                job.nexclude = len(arr)
+                keep.append(arr)
+        _abi.SEARCH_INDEX(backend.search_index)(jobs, n)
+        out = []
+        for job in jobs:
+            hits = [(job.results[i].key, np.float32(job.results[i].distance).view(np.uint32).item(),
+                     job.results[i].ordinal) for i in range(job.nresults)]
+            out.append((job.status, job.route, hits))
+        del keep
+        return out
+
+
+def assert_same_as_cpu(backends, jobs, ref_name, ours_name):
+    cpu, ours = backends
+    want = jobs.run(cpu, rename={'IX': ref_name})
+    got = jobs.run(ours, rename={'IX': ours_name})
+    assert len(want) == len(got)
+    for i, (w, g) in enumerate(zip(want, got)):
+        assert g[0] == w[0], (i, 'status', g[0], w[0])
+        assert g[1] == w[1], (i, 'route', g[1], w[1])
+        assert g[2] == w[2], (i, g[2][:5], w[2][:5])
+    return want
+
+
+def test_unfiltered_batch_and_filters(backends, tmp_path):
+    rng = np.random.default_rng(7)
+    n, d = 30000, 96
+    x = synth.mixture(n, d, 60, seed=7)
+    keys = rng.choice(np.arange(-10 ** 9, 10 ** 9), n, replace=False)
+    skeys, rows = synth.write_index_dir(str(tmp_path / 'ix'), keys, x, shards=3)
+    cpu, ours = backends
+    assert load(cpu, 'cpu_a', str(tmp_path / 'ix')) == 0
+    assert load(ours, 'b200_a', str(tmp_path / 'ix')) == 0
+    q = synth.mixture_queries(48, d, 60, seed=8)
+    jobs = Jobs()
+    for i in range(40):                       # one unfiltered batch (tensor-path size), mixed k
+        jobs.add('IX', q[i], (10, 50, 100, 7)[i % 4])
+    sel = np.sort(rng.choice(skeys, 3000, replace=False))
+    missing = np.setdiff1d(rng.integers(-10 ** 9, 10 ** 9, 50), skeys)
+    jobs.add('IX', q[40], 25, keys=np.sort(np.concatenate([sel, missing])))       # key filter, some unknown
+    ords = np.sort(rng.choice(n, 500, replace=False))
+    jobs.add('IX', q[41], 30, ordinals=ords)                                        # ordinals given
+    jobs.add('IX', q[42], 30, ordinals=ords, exclude=ords[::3])                     # residual exclusions
+    jobs.add('IX', q[43], 50, keys=sel[:20])                                        # k past the eligible rows
+    jobs.add('IX', q[44], 10, keys=np.array([], dtype=np.int64))                    # empty filter
+    jobs.add('IX', q[45], 0)                                                        # k = 0
+    jobs.add('missing_index', q[46], 10)                                            # not loaded: ANN_STALE
+    jobs.add('IX', q[47][:90], 10, dims=90)                                         # dimension mismatch
+    want = assert_same_as_cpu(backends, jobs, 'cpu_a', 'b200_a')
+    assert want[0][0] == 0 and len(want[0][2]) == 10
+    assert want[-2][0] == 3            # ANN_STALE
+    assert want[-1][0] == 1            # ANN_INVALID
+
+
+def test_ties_and_duplicate_rows(backends, tmp_path):
+    # identical rows under different keys: equal FP32 distances order by key
+    rng = np.random.default_rng(9)
+    base = rng.standard_normal((100, 24)).astype(np.float32)
+    x = np.concatenate([base] * 30)
+    keys = rng.permutation(len(x)) * 7 - 5000
+    synth.write_index_dir(str(tmp_path / 'ties'), keys, x, shards=2)
+    cpu, ours = backends
+    assert load(cpu, 'cpu_t', str(tmp_path / 'ties')) == 0
+    assert load(ours, 'b200_t', str(tmp_path / 'ties')) == 0
+    jobs = Jobs()
+    for i in range(20):
+        jobs.add('IX', base[i] + 1e-3 * i, 45)
+    jobs.add('IX', base[3], 61, ordinals=np.arange(0, len(x), 2))
+    assert_same_as_cpu(backends, jobs, 'cpu_t', 'b200_t')
+
+
+def test_odd_dimensions_and_single_query(backends, tmp_path):
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((5000, 37)).astype(np.float32) * 3
+    keys = np.arange(5000) * 3 + 1
+    synth.write_index_dir(str(tmp_path / 'odd'), keys, x, shards=1)
+    cpu, ours = backends
+    assert load(cpu, 'cpu_o', str(tmp_path / 'odd')) == 0
+    assert load(ours, 'b200_o', str(tmp_path / 'odd')) == 0
+    jobs = Jobs().add('IX', rng.standard_normal(37), 17)
+    assert_same_as_cpu(backends, jobs, 'cpu_o', 'b200_o')
