@@ -276,6 +276,7 @@ struct AnnB200Shard {
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
+  int pair_clusters = -1;      // CTA pairs of the pair scan that fit at once (-1: not asked yet)
 };
 
 namespace annb200 {
@@ -439,6 +440,16 @@ extern "C" int AnnB200ShardAssign(AnnB200Shard *s, uint32_t dtype, uint32_t dims
 
 namespace {
 
+// CTA pairs the pair scan can keep resident on the shard's device (asked
+// once; 0 turns the pair scan off, as does ANN_B200_NO_PAIR=1).
+int pair_clusters(AnnB200Shard *sh) {
+  if (sh->pair_clusters < 0) {
+    const char *off = getenv("ANN_B200_NO_PAIR");
+    sh->pair_clusters = (off && *off && *off != '0') ? 0 : tc_scan_pair_clusters(tc_scan_max_queries());
+  }
+  return sh->pair_clusters;
+}
+
 // Queries whose survivors outgrew the shared-memory sort: rescored and sorted
 // one at a time in a global scratch.
 int big_sorts(AnnB200Shard *sh, const SelectLaunch &sl, const uint32_t *big, uint32_t nq, cudaStream_t st) {
@@ -532,21 +543,33 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.cnt = cnt;
   a.flags = dflags;
 
-  CUtensorMap query_map;
+  // FP16 batches of 256+ queries run on CTA pairs (M=256 tiles; each CTA
+  // loads half of a 256-query block), others on single CTAs
+  const bool pair = tc && bn == 256 && v.dtype == DT_F16 && pair_clusters(sh) > 0;
+  // the query block as single CTAs read it (box bn) and as CTA pairs do (box 128)
+  CUtensorMap query_map, query_half;
   if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+    return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
+  if (pair && !encode_f16_map(&query_half, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, 128))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   // One scan launch timed as `stage`. Tensor path: rows come from the shard
   // itself when the candidates are a contiguous run, else from `staged`
-  // (virtual row 0 at its first row, filled by gather_rows).
+  // (virtual row 0 at its first row, filled by gather_rows); FP16 row lists
+  // are gathered by the scan itself. CTA pairs take contiguous runs only.
+  auto tc_launch = [&](const CUtensorMap &rows_map, int64_t row0) -> cudaError_t {
+    return pair && !a.ids && a.stride == 1
+               ? launch_tc_scan_pair(a, rows_map, row0, query_half, kpad, pair_clusters(sh), st)
+               : launch_tc_scan(a, rows_map, row0, query_map, kpad, bn, sh->sms, st);
+  };
   auto scan = [&](int stage, const void *staged) -> cudaError_t {
     int hk = clock.begin(stage);
     cudaError_t e;
     if (tc && !staged) {
-      e = launch_tc_scan(a, sh->rows_map, (int64_t)a.base, query_map, kpad, bn, sh->sms, st);
+      e = tc_launch(sh->rows_map, (int64_t)a.base);
     } else if (tc) {
       CUtensorMap staged_map;
       if (!encode_rows_map(&staged_map, v.dtype, staged, v.dims, a.count, v.row_bytes)) return cudaErrorInvalidValue;
-      e = launch_tc_scan(a, staged_map, 0, query_map, kpad, bn, sh->sms, st);
+      e = tc_launch(staged_map, 0);
     } else {
       launch_simt_scan(a, st);
       e = cudaGetLastError();
@@ -583,9 +606,12 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   sl.first_id = sh->first;
   sl.index_form = (flags & ANNB200_INDEX_L2) && metric == M_L2;
 
+  // FP16 candidate rows are gathered by the tensor scan itself; quantized
+  // rows are copied to a contiguous staging buffer its TMA reads
+  const bool stage_rows = tc && v.dtype != DT_F16;
   if (k > 0 && n > 0) {
     // staging: the pass's gathered candidate rows, then the sample's
-    if (tc && (rows || sample))
+    if (stage_rows && (rows || sample))
       CK(sh->staging.reserve(((rows ? n : 0) + (sample ? S : 0)) * v.row_bytes), "staging");
     if (sample) {
       a.mode = MODE_MATRIX;
@@ -595,7 +621,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       a.mat = mat;
       a.mat_ld = S;
       const void *staged = nullptr;
-      if (tc && (rows || stride > 1)) {
+      if (stage_rows && (rows || stride > 1)) {
         uint8_t *sample_rows = (uint8_t *)sh->staging.p + (rows ? n * v.row_bytes : 0);
         gather(0, stride, S, sample_rows, st);
         staged = sample_rows;
@@ -620,7 +646,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     CK(cudaMemcpyAsync(thr0, qs.thr, nq * sizeof(float), cudaMemcpyDeviceToDevice, st), "thresholds");
     a.mode = MODE_FILTER;
     a.stride = 1;
-    const bool staged_pass = tc && rows;
+    const bool staged_pass = stage_rows && rows;
     for (int attempt = 0;; attempt++) {
       std::vector<std::pair<uint64_t, uint64_t>> chunks;
       std::vector<char> tighten_after;
@@ -1071,18 +1097,24 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.flags = dflags;
   a.raw_scale = tc && v.dtype != DT_F16;
   if (tc) {
-    CUtensorMap query_map;
-    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+    const bool pair = bn == 256 && v.dtype == DT_F16 && pair_clusters(sh) > 0;
+    CUtensorMap query_map, query_half;
+    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn) ||
+        (pair && !encode_f16_map(&query_half, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, 128)))
       return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
-    if (!rows) {
-      CK(launch_tc_scan(a, sh->rows_map, 0, query_map, kpad, bn, sh->sms, st), "score scan");
+    auto tc_launch = [&](const CUtensorMap &rows_map) -> cudaError_t {
+      return pair && !a.ids ? launch_tc_scan_pair(a, rows_map, 0, query_half, kpad, pair_clusters(sh), st)
+                            : launch_tc_scan(a, rows_map, 0, query_map, kpad, bn, sh->sms, st);
+    };
+    if (!rows || v.dtype == DT_F16) {
+      CK(tc_launch(sh->rows_map), "score scan");   // FP16 row lists: gathered by the scan
     } else {
       CK(sh->staging.reserve(n * v.row_bytes), "staging");
       launch_gather_rows(v.codes, v.row_bytes, v.rows, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
       CUtensorMap staged;
       if (!encode_rows_map(&staged, v.dtype, sh->staging.p, v.dims, n, v.row_bytes))
         return fail(BACKEND_ERROR, "tensor map of the staged rows could not be encoded");
-      CK(launch_tc_scan(a, staged, 0, query_map, kpad, bn, sh->sms, st), "score scan");
+      CK(tc_launch(staged), "score scan");
       counted(1);
     }
   } else {

@@ -86,6 +86,20 @@ def test_f16_tensor_path(cuda, metric):
     assert_same(cuda, oracle.F16, 768, h, q, 100, metric, ids=ids)
 
 
+@pytest.mark.parametrize('pair', [True, False])
+def test_f16_cta_pair_and_single_cta_scans(cuda, pair, monkeypatch):
+    # batches of 256+ FP16 queries scan on CTA pairs (tcgen05 cta_group::2);
+    # ANN_B200_NO_PAIR=1, read when a shard first searches, keeps single CTAs.
+    # Rows not a multiple of the 256-row pair tile; a padded last query tile.
+    if not pair:
+        monkeypatch.setenv('ANN_B200_NO_PAIR', '1')
+    x = synth.mixture(70001, 256, 200, seed=12, normalize=True)
+    h = synth.to_half_bits(x)
+    q = synth.mixture_queries(520, 256, 200, seed=12, normalize=True)
+    assert_same(cuda, oracle.F16, 256, h, q, 64, 2)
+    assert_same(cuda, oracle.F16, 256, h, q[:256], 10, 0, window=True)
+
+
 def test_f16_simt_path_matches(cuda):
     x = synth.mixture(20000, 96, 30, seed=5, normalize=True)
     h = synth.to_half_bits(x)
