@@ -349,9 +349,6 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
 void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
                         uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st);
 uint32_t tc_scan_max_queries();
-cudaError_t launch_tc_scan_pair(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
-                                const CUtensorMap &query_map, uint32_t kpad, int clusters, cudaStream_t st);
-int tc_scan_pair_clusters(uint32_t nq);
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,

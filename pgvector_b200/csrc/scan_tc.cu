@@ -10,10 +10,18 @@
 //              the 128 x 64 block of candidate rows and the BN x 64 block of
 //              FP16 queries -- which land in the 128-byte-swizzled K-major
 //              layout tcgen05 reads and complete on the stage's mbarrier.
-//              Candidate rows are contiguous: a shard's own rows when every
-//              row is scanned, else a staging copy that gather_rows filled
-//              (TMA's per-row tile::gather4 is request-rate bound at about
-//              13 GB/s an SM, a plain coalesced copy is not).
+//              Contiguous candidate rows (a whole shard, a staged copy) come
+//              this way.
+//   warps 6-9  (FP16 row lists and strided samples) gather: 16-byte
+//              cp.async copies of the named rows straight from the shard into
+//              the swizzled A tiles (8 lanes a row), completing on the stage
+//              barrier through cp.async.mbarrier.arrive.noinc, with the next
+//              tile's rows prefetched into L2; A and B then have separate
+//              rings (6 x 16 KB of rows, 3 x 32 KB of queries). TMA's per-row
+//              tile::gather4 was measured request-rate bound at about 13 GB/s
+//              an SM; these copies sustain ~920 TFLOP/s of scan.
+//   warps 6-9  (E4M3 / NVFP4 rows) converters: the raw codes arrive by TMA
+//              in a ring of their own and are converted to FP16 A tiles.
 //   warp 1     one thread issues tcgen05.mma.cta_group::1.kind::f16
 //              (M=128, N=BN, K=16) into an FP32 accumulator in tensor memory,
 //              and tcgen05.commit frees each stage and publishes each tile.
@@ -256,21 +264,30 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
 
 // Per storage format: pipeline stages, raw-code ring (quantized formats stage
 // their codes and convert them to FP16 in shared memory), threads.
+// STG stages hold an A tile and a B tile each; the gathered-FP16 kernel
+// instead keeps STG A tiles and BSTG B tiles in separate rings.
 template <int Q> struct TcCfg;
 template <> struct TcCfg<DT_F16> {
-  static constexpr int STG = 4, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 192;
+  static constexpr int STG = 4, BSTG = 4, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 192;
+  static constexpr int RING = STG * STAGE_BYTES;
 };
 template <> struct TcCfg<DT_E4M3> {   // 64 one-byte codes a row a k-block
-  static constexpr int STG = 3, RSTG = 4, RAWB = BM * 64, RAW_X = 64, NT = 320;
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 64, RAW_X = 64, NT = 320;
+  static constexpr int RING = STG * STAGE_BYTES;
 };
 template <> struct TcCfg<DT_NVFP4> {  // 64 nibbles (32 bytes) a row a k-block
-  static constexpr int STG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 320;
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 320;
+  static constexpr int RING = STG * STAGE_BYTES;
 };
 // FP16 rows named by a candidate list (or a strided sample): 4 gather warps
-// copy them from the shard into the A tile, TMA loads only the queries.
+// copy them from the shard into the A tiles, TMA loads only the queries.
+// Gathered rows come from random HBM locations and take far longer to land
+// than the L2-resident query block, so the A ring is twice as deep (6 x 16 KB)
+// as the B ring (3 x 32 KB).
 constexpr int GF16 = 0x10 | DT_F16;
 template <> struct TcCfg<GF16> {
-  static constexpr int STG = 4, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 320;
+  static constexpr int STG = 6, BSTG = 3, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 320;
+  static constexpr int RING = STG * A_BYTES + BSTG * B_BYTES;
 };
 
 // 16 bytes global -> shared, bypassing L1; n = 0 writes zeros and reads nothing.
@@ -371,17 +388,23 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
     tc_scan(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
             const TcArgs t) {
   using C = TcCfg<Q>;
-  constexpr int STG = C::STG, RSTG = C::RSTG, RAWB = C::RAWB;
+  constexpr int STG = C::STG, BSTG = C::BSTG, RSTG = C::RSTG, RAWB = C::RAWB;
   constexpr int RSTG1 = RSTG > 0 ? RSTG : 1;  // (the FP16 kernels have no raw ring)
   constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4;
   constexpr bool GATHER = Q == GF16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *raw = smem + STG * STAGE_BYTES;
+  // A and B tiles of stage s (separate rings for the gathered kernel)
+  auto a_tile = [&](uint32_t s) { return smem + (GATHER ? s * A_BYTES : s * STAGE_BYTES); };
+  auto b_tile = [&](uint32_t s) {
+    return GATHER ? smem + STG * A_BYTES + s * B_BYTES : smem + s * STAGE_BYTES + A_BYTES;
+  };
+  uint8_t *raw = smem + C::RING;
   uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);  // A (and B for FP16) ready
-  uint64_t *empty = full + STG;                                      // stage consumed by the MMAs
-  uint64_t *bfull = empty + STG;                                     // B ready (quantized formats)
-  uint64_t *rawfull = bfull + STG;
+  uint64_t *empty = full + STG;                                      // A stage consumed by the MMAs
+  uint64_t *bfull = empty + STG;                                     // B ready (quantized, gathered)
+  uint64_t *bempty = bfull + STG;                                    // B stage consumed (gathered)
+  uint64_t *rawfull = bempty + STG;
   uint64_t *rawempty = rawfull + RSTG;
   uint64_t *tfull = rawempty + RSTG;
   uint64_t *tempty = tfull + 2;
@@ -397,9 +420,10 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STG; s++) {
-      mbar_init(full + s, QUANT ? 4 : (GATHER ? 128 + 1 : 1));
+      mbar_init(full + s, QUANT ? 4 : (GATHER ? 128 : 1));
       mbar_init(empty + s, 1);
       mbar_init(bfull + s, 1);
+      mbar_init(bempty + s, 1);
     }
     for (int r = 0; r < RSTG; r++) {
       mbar_init(rawfull + r, 1);
@@ -434,9 +458,9 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
     // only). Quantized: raw codes into the raw ring (the converters load the
     // queries).
     if (lane == 0) {
-      constexpr int RING = QUANT ? RSTG1 : STG;
-      uint64_t *ring_full = QUANT ? rawfull : full;
-      uint64_t *ring_empty = QUANT ? rawempty : empty;
+      constexpr int RING = QUANT ? RSTG1 : (GATHER ? BSTG : STG);
+      uint64_t *ring_full = QUANT ? rawfull : (GATHER ? bfull : full);
+      uint64_t *ring_empty = QUANT ? rawempty : (GATHER ? bempty : empty);
       const uint32_t tx_bytes = QUANT ? (uint32_t)RAWB : (GATHER ? 0u : (uint32_t)A_BYTES) + t.bn * 128u;
       uint64_t it = 0;
       bool ok = true;
@@ -455,9 +479,8 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           if (QUANT) {
             tma_load_2d(smem_u32(raw + s * RAWB), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
           } else {
-            const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-            if (!GATHER) tma_load_2d(sa, &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
-            tma_load_2d(sa + A_BYTES, &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), ring_full + s);
+            if (!GATHER) tma_load_2d(smem_u32(a_tile(s)), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+            tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), ring_full + s);
           }
           it++;
         }
@@ -479,17 +502,22 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
           const uint32_t s = (uint32_t)(it % STG);
           const uint32_t ph = (uint32_t)((it / STG) & 1);
-          if (!mbar_wait(full + s, ph, abort, a.flags) || (QUANT && !mbar_wait(bfull + s, ph, abort, a.flags))) {
+          // the B tile: same stage index, or its own ring (gathered kernel)
+          const uint32_t s_b = GATHER ? (uint32_t)(it % BSTG) : s;
+          const uint32_t ph_b = GATHER ? (uint32_t)((it / BSTG) & 1) : ph;
+          if (!mbar_wait(full + s, ph, abort, a.flags) ||
+              ((QUANT || GATHER) && !mbar_wait(bfull + s_b, ph_b, abort, a.flags))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sa = smem_u32(a_tile(s));
+          const uint32_t sb = smem_u32(b_tile(s_b));
 #pragma unroll
           for (uint32_t kk = 0; kk < 4; kk++)
             tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
           tc_commit(empty + s);
+          if (GATHER) tc_commit(bempty + s_b);
         }
         if (ok) tc_commit(tfull + ab);
       }
@@ -520,8 +548,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         }
         if (ct == 0) {
           mbar_expect_tx(bfull + s, t.bn * 128u);
-          tma_load_2d(smem_u32(smem + s * STAGE_BYTES + A_BYTES), &query_map, (int32_t)(kb * 64),
-                      (int32_t)(qt * t.bn), bfull + s);
+          tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), bfull + s);
           bissued = it + 1;
         }
         got = mbar_wait(rawfull + r, rph, abort, a.flags);
@@ -529,7 +556,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           ok = false;
           break;
         }
-        convert_stage<Q>(a, raw + r * RAWB, smem + s * STAGE_BYTES, ct, rt * BM, kb);
+        convert_stage<Q>(a, raw + r * RAWB, a_tile(s), ct, rt * BM, kb);
         // generic-proxy stores -> visible to the tensor core's async proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -547,7 +574,9 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
     // tile: 8 lanes a row (its 128 bytes of the k-block), 16 rows a pass,
     // 16-byte cp.async each; each thread's copies arrive on the stage barrier
     // when they land (cp.async.mbarrier.arrive.noinc). Rows past the
-    // candidates are zero-filled.
+    // candidates are zero-filled. Each thread also asks L2 for one whole row
+    // of this CTA's next tile (cp.async.bulk.prefetch.L2), so that tile's
+    // copies are served from L2 instead of random HBM accesses.
     const uint32_t gt = threadIdx.x - 192;
     const uint32_t c = gt & 7, r0 = gt >> 3;
     const uint64_t rb = a.s.row_bytes;
@@ -564,6 +593,14 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         const uint64_t id = val[j] ? cand_row(a.ids, a.base + vi * a.stride, a.s.rows) : 0;
         src[j] = a.s.codes + id * rb;
       }
+      const uint64_t next = tile + gridDim.x;
+      if (next < ntiles) {
+        const uint64_t vn = (next / t.qtiles) * BM + gt;
+        if (vn < a.count) {
+          const uint8_t *row = a.s.codes + cand_row(a.ids, a.base + vn * a.stride, a.s.rows) * rb;
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row), "r"((uint32_t)rb) : "memory");
+        }
+      }
       for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
         const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
         const bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
@@ -571,7 +608,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           ok = false;
           break;
         }
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t sa = smem_u32(a_tile(s));
         const uint64_t off = (uint64_t)kb * 128 + c * 16;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -609,251 +646,6 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
-                 : "memory");
-  }
-}
-
-// ---------------------------------------------------------------- CTA-pair scan
-//
-// The FP16 scan on pairs of CTAs (a cluster of two on neighbouring SMs) with
-// tcgen05.mma.cta_group::2: one M=256, N=256 MMA reads rows 0-127 of the
-// tile from the first CTA's shared memory and rows 128-255 from the
-// second's, and queries 0-127 from the first and 128-255 from the second.
-// Each CTA therefore loads a 128-row block and half of the 256-query block
-// per k-block (32 KB instead of 48 KB for the same FLOPs), which leaves room
-// for six stages, and holds its own 128 accumulator rows in its tensor
-// memory (double buffered). The first CTA of the pair (rank 0) owns the
-// stage barriers the TMA loads of both complete on, issues the MMAs, and
-// commits them to both CTAs' barriers; both epilogues report a drained
-// accumulator to rank 0. All waits are bounded as in tc_scan.
-constexpr int PAIR_STG = 6;
-constexpr int PAIR_A = 128 * 128;            // this CTA's 128 rows x 64 halves
-constexpr int PAIR_B = 128 * 128;            // this CTA's 128 queries x 64 halves
-constexpr int PAIR_STAGE = PAIR_A + PAIR_B;
-constexpr int PAIR_NT = 192;
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_count() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-// Shared-memory address (cluster window) of the same variable in CTA `rank`.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *flags) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (;;) {
-    for (int i = 0; i < 32; i++)
-      if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*abort) return false;
-    if (globaltimer() - t0 > kWaitNs) {
-      *abort = 1;
-      atomicOr(flags, FLAG_TIMEOUT);
-      return false;
-    }
-  }
-}
-// Arrive on a barrier given by its cluster-window address (either CTA).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
-}
-// A 2-D tile into this CTA's shared memory, completing on a barrier of
-// either CTA of the pair (cluster-window address).
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y,
-                                                 uint32_t bar_caddr) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_caddr)
-      : "memory");
-}
-__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Completion of this thread's MMAs arrives on the barrier at the same offset
-// in both CTAs of the pair.
-__device__ __forceinline__ void tc_commit_pair_both(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"((unsigned short)3)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit_pair_local(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__global__ void __launch_bounds__(PAIR_NT, 1)
-    tc_scan_pair(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
-                 const TcArgs t) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + PAIR_STG * PAIR_STAGE);  // rank 0: both CTAs' loads
-  uint64_t *empty = full + PAIR_STG;                                            // both: MMAs done with a stage
-  uint64_t *tfull = empty + PAIR_STG;                                           // both: accumulator ready
-  uint64_t *tempty = tfull + 2;                                                 // rank 0: both epilogues done
-  uint64_t *drain = tempty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-  volatile uint32_t *abort = tmem_slot + 1;
-  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 256);
-  float *thr_s = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);
-
-  const ScanArgs &a = t.a;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const uint32_t pair = cluster_id(), npairs = cluster_count();
-  const uint64_t ntiles = t.rtiles * t.qtiles;  // rtiles of 256 rows; t.bn = 256
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < PAIR_STG; s++) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
-    }
-    for (int b = 0; b < 2; b++) {
-      mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, 2 * 128);
-    }
-    mbar_init(drain, 1);
-    *abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (a.mode == MODE_FILTER)
-    for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += PAIR_NT)
-      thr_s[i] = i < a.nq ? a.thr[i] : __int_as_float(0x7fc00000);
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA signal
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (both CTAs)
-    if (lane == 0) {
-      uint64_t it = 0;
-      bool ok = true;
-      for (uint64_t tile = pair; tile < ntiles && ok; tile += npairs) {
-        const uint64_t rt = tile / t.qtiles;
-        const uint32_t qt = (uint32_t)(tile % t.qtiles);
-        const int32_t arow = (int32_t)(t.a_row0 + (int64_t)rt * 256 + (int64_t)rank * 128);
-        const int32_t brow = (int32_t)(qt * 256 + rank * 128);
-        for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % PAIR_STG);
-          const uint32_t ph = (uint32_t)((it / PAIR_STG) & 1);
-          if (!mbar_wait_cluster(empty + s, ph ^ 1, abort, a.flags)) {
-            ok = false;
-            break;
-          }
-          const uint32_t bar = map_to_rank(smem_u32(full + s), 0);
-          if (rank == 0) mbar_expect_tx(full + s, 2u * PAIR_STAGE);
-          const uint32_t sa = smem_u32(smem + s * PAIR_STAGE);
-          tma_load_2d_pair(sa, &rows_map, (int32_t)(kb * 64), arow, bar);
-          tma_load_2d_pair(sa + PAIR_A, &query_map, (int32_t)(kb * 64), brow, bar);
-        }
-      }
-      // rank 0's stage barriers complete only when both CTAs' loads landed
-      if (rank == 0) drain_ring(full, PAIR_STG, it);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (rank 0)
-    if (lane == 0 && rank == 0) {
-      const uint32_t idesc = (1u << 4) | ((256u >> 3) << 17) | ((256u >> 4) << 24);  // F32 acc, N=256, M=256
-      uint64_t it = 0, tc = 0;
-      bool ok = true;
-      for (uint64_t tile = pair; tile < ntiles && ok; tile += npairs, tc++) {
-        const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
-        if (!mbar_wait_cluster(tempty + ab, (use & 1) ^ 1, abort, a.flags)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * 256;
-        for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % PAIR_STG);
-          const uint32_t ph = (uint32_t)((it / PAIR_STG) & 1);
-          if (!mbar_wait_cluster(full + s, ph, abort, a.flags)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * PAIR_STAGE);
-          const uint32_t sb = sa + PAIR_A;
-#pragma unroll
-          for (uint32_t kk = 0; kk < 4; kk++)
-            tc_mma_pair(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
-          tc_commit_pair_both(empty + s);
-        }
-        if (ok) tc_commit_pair_both(tfull + ab);
-      }
-      tc_commit_pair_local(drain);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitNs) {
-      }
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ epilogue (both CTAs)
-    Appender app{a, stage_buf + (warp - 2) * EPI_BUF, 0, lane};
-    const int quad = warp & 3;
-    uint64_t tc = 0;
-    for (uint64_t tile = pair; tile < ntiles; tile += npairs, tc++) {
-      const uint64_t rt = tile / t.qtiles;
-      const uint32_t qt = (uint32_t)(tile % t.qtiles);
-      const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
-      bool got = mbar_wait_cluster(tfull + ab, use & 1, abort, a.flags);
-      if (!__all_sync(0xffffffffu, got)) break;
-      tc_fence_after();
-      epilogue_rows(a, tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16),
-                    rt * 256 + rank * 128 + quad * 32 + lane, qt * 256, 256, thr_s, app);
-      tc_fence_before();
-      mbar_arrive_cluster(map_to_rank(smem_u32(tempty + ab), 0));
-    }
-    __syncwarp();
-    if (a.mode == MODE_FILTER && app.n) app.flush();
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();  // rank 0's MMAs have drained and both epilogues are done with tensor memory
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
   }
 }
@@ -899,7 +691,7 @@ void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows,
 // (thresholds included).
 template <int Q>
 size_t tc_scan_smem_t(uint32_t nq) {
-  return 1024 + (size_t)TcCfg<Q>::STG * STAGE_BYTES + (size_t)TcCfg<Q>::RSTG * TcCfg<Q>::RAWB + 256 +
+  return 1024 + (size_t)TcCfg<Q>::RING + (size_t)TcCfg<Q>::RSTG * TcCfg<Q>::RAWB + 256 +
          4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) * sizeof(float);
 }
 
@@ -916,74 +708,6 @@ cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_ma
   const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
   tc_scan<Q><<<grid, TcCfg<Q>::NT, smem, st>>>(rows_map, query_map, t);
   return cudaGetLastError();
-}
-
-// Shared memory of the CTA-pair scan (thresholds for nq queries included).
-size_t tc_scan_pair_smem(uint32_t nq) {
-  return 1024 + (size_t)PAIR_STG * PAIR_STAGE + 256 + 4 * EPI_BUF * sizeof(uint4) +
-         (size_t)((nq + 255) / 256 * 256) * sizeof(float);
-}
-
-// The CTA-pair FP16 scan: as launch_tc_scan with bn = 256, but query_map's
-// box is 64 x 128 (each CTA loads half the query block) and row tiles hold
-// 256 rows. `clusters` is the number of pairs the grid holds (at most the
-// number that fit on the device at once).
-cudaError_t launch_tc_scan_pair(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
-                                const CUtensorMap &query_map, uint32_t kpad, int clusters, cudaStream_t st) {
-  TcArgs t;
-  t.a = a;
-  t.a_row0 = a_row0;
-  t.kpad = kpad;
-  t.kblocks = kpad / 64;
-  t.bn = 256;
-  t.qtiles = (a.nq + 255) / 256;
-  t.rtiles = (a.count + 255) / 256;
-  if (a.count == 0 || a.nq == 0) return cudaSuccess;
-  const size_t smem = tc_scan_pair_smem(a.nq);
-  cudaError_t e = cudaFuncSetAttribute(tc_scan_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  const uint64_t ntiles = t.rtiles * t.qtiles;
-  const unsigned pairs = (unsigned)(ntiles < (uint64_t)clusters ? ntiles : (uint64_t)clusters);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(PAIR_NT);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, tc_scan_pair, rows_map, query_map, t);
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
-}
-
-// Pairs of the CTA-pair scan that fit on the current device at once (0 if
-// clusters of two cannot be placed).
-int tc_scan_pair_clusters(uint32_t nq) {
-  const size_t smem = tc_scan_pair_smem(nq);
-  if (cudaFuncSetAttribute(tc_scan_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(PAIR_NT);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, tc_scan_pair, &cfg) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return n;
 }
 
 // Launch the tensor scan of a.count virtual rows against a.nq FP16 queries.

@@ -276,7 +276,6 @@ struct AnnB200Shard {
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
-  int pair_clusters = -1;      // CTA pairs of the pair scan that fit at once (-1: not asked yet)
 };
 
 namespace annb200 {
@@ -440,16 +439,6 @@ extern "C" int AnnB200ShardAssign(AnnB200Shard *s, uint32_t dtype, uint32_t dims
 
 namespace {
 
-// CTA pairs the pair scan can keep resident on the shard's device (asked
-// once; 0 turns the pair scan off, as does ANN_B200_NO_PAIR=1).
-int pair_clusters(AnnB200Shard *sh) {
-  if (sh->pair_clusters < 0) {
-    const char *off = getenv("ANN_B200_NO_PAIR");
-    sh->pair_clusters = (off && *off && *off != '0') ? 0 : tc_scan_pair_clusters(tc_scan_max_queries());
-  }
-  return sh->pair_clusters;
-}
-
 // Queries whose survivors outgrew the shared-memory sort: rescored and sorted
 // one at a time in a global scratch.
 int big_sorts(AnnB200Shard *sh, const SelectLaunch &sl, const uint32_t *big, uint32_t nq, cudaStream_t st) {
@@ -543,23 +532,15 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.cnt = cnt;
   a.flags = dflags;
 
-  // FP16 batches of 256+ queries run on CTA pairs (M=256 tiles; each CTA
-  // loads half of a 256-query block), others on single CTAs
-  const bool pair = tc && bn == 256 && v.dtype == DT_F16 && pair_clusters(sh) > 0;
-  // the query block as single CTAs read it (box bn) and as CTA pairs do (box 128)
-  CUtensorMap query_map, query_half;
+  CUtensorMap query_map;
   if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
-    return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
-  if (pair && !encode_f16_map(&query_half, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, 128))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   // One scan launch timed as `stage`. Tensor path: rows come from the shard
   // itself when the candidates are a contiguous run, else from `staged`
   // (virtual row 0 at its first row, filled by gather_rows); FP16 row lists
-  // are gathered by the scan itself. CTA pairs take contiguous runs only.
+  // are gathered by the scan itself.
   auto tc_launch = [&](const CUtensorMap &rows_map, int64_t row0) -> cudaError_t {
-    return pair && !a.ids && a.stride == 1
-               ? launch_tc_scan_pair(a, rows_map, row0, query_half, kpad, pair_clusters(sh), st)
-               : launch_tc_scan(a, rows_map, row0, query_map, kpad, bn, sh->sms, st);
+    return launch_tc_scan(a, rows_map, row0, query_map, kpad, bn, sh->sms, st);
   };
   auto scan = [&](int stage, const void *staged) -> cudaError_t {
     int hk = clock.begin(stage);
@@ -1097,14 +1078,11 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.flags = dflags;
   a.raw_scale = tc && v.dtype != DT_F16;
   if (tc) {
-    const bool pair = bn == 256 && v.dtype == DT_F16 && pair_clusters(sh) > 0;
-    CUtensorMap query_map, query_half;
-    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn) ||
-        (pair && !encode_f16_map(&query_half, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, 128)))
+    CUtensorMap query_map;
+    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
       return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
     auto tc_launch = [&](const CUtensorMap &rows_map) -> cudaError_t {
-      return pair && !a.ids ? launch_tc_scan_pair(a, rows_map, 0, query_half, kpad, pair_clusters(sh), st)
-                            : launch_tc_scan(a, rows_map, 0, query_map, kpad, bn, sh->sms, st);
+      return launch_tc_scan(a, rows_map, 0, query_map, kpad, bn, sh->sms, st);
     };
     if (!rows || v.dtype == DT_F16) {
       CK(tc_launch(sh->rows_map), "score scan");   // FP16 row lists: gathered by the scan

@@ -86,18 +86,18 @@ def test_f16_tensor_path(cuda, metric):
     assert_same(cuda, oracle.F16, 768, h, q, 100, metric, ids=ids)
 
 
-@pytest.mark.parametrize('pair', [True, False])
-def test_f16_cta_pair_and_single_cta_scans(cuda, pair, monkeypatch):
-    # batches of 256+ FP16 queries scan on CTA pairs (tcgen05 cta_group::2);
-    # ANN_B200_NO_PAIR=1, read when a shard first searches, keeps single CTAs.
-    # Rows not a multiple of the 256-row pair tile; a padded last query tile.
-    if not pair:
-        monkeypatch.setenv('ANN_B200_NO_PAIR', '1')
+def test_f16_gathered_and_contiguous_scans(cuda):
+    # batches of 256+ FP16 queries: contiguous rows read by TMA, row lists
+    # gathered by the scan's own copy warps; rows not a multiple of the tile,
+    # a padded last query tile
     x = synth.mixture(70001, 256, 200, seed=12, normalize=True)
     h = synth.to_half_bits(x)
     q = synth.mixture_queries(520, 256, 200, seed=12, normalize=True)
+    _, ids = synth.bitmap(70001, 0.55, seed=13)
     assert_same(cuda, oracle.F16, 256, h, q, 64, 2)
+    assert_same(cuda, oracle.F16, 256, h, q, 40, 1, ids=ids)
     assert_same(cuda, oracle.F16, 256, h, q[:256], 10, 0, window=True)
+    assert_same(cuda, oracle.F16, 256, h, q[:300], 25, 0, ids=ids[::3], window=True)
 
 
 def test_f16_simt_path_matches(cuda):
