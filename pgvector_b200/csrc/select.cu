@@ -671,13 +671,9 @@ constexpr int RS_WARPS = 4;
 constexpr int RS_STRIDE = 144;  // bytes a staged row chunk: 128 + 16 of padding (bank-conflict free)
 
 template <int DT>
-__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact) {
-  __shared__ __align__(16) uint8_t stage[RS_WARPS][2][32 * RS_STRIDE];
-  const uint32_t q = blockIdx.y;
-  const uint32_t m = a.cnt[q];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t i0 = (blockIdx.x * RS_WARPS + warp) * 32;
-  if (i0 >= m) return;
+__device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, uint32_t q, uint32_t m, uint32_t i0,
+                              uint8_t (*stage)[32 * RS_STRIDE]) {
+  const int lane = threadIdx.x & 31;
   const uint2 *e = a.cand + (uint64_t)q * a.cap;
   const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
                                                     (uint64_t)q * a.qbytes);
@@ -701,7 +697,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned 
   auto store_chunk = [&](int buf, const uint4 (&v)[8]) {
 #pragma unroll
     for (int t = 0; t < 8; t++)
-      *reinterpret_cast<uint4 *>(&stage[warp][buf][(lane / 8 + 4 * t) * RS_STRIDE + (lane % 8) * 16]) = v[t];
+      *reinterpret_cast<uint4 *>(&stage[buf][(lane / 8 + 4 * t) * RS_STRIDE + (lane % 8) * 16]) = v[t];
   };
   const float rs = (DT == DT_E4M3 || DT == DT_NVFP4) ? __ldg(s.rowscale + id) : 1.0f;
   float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -717,7 +713,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned 
     store_chunk(buf, v);
     __syncwarp();
     if (c + 1 < chunks) load_chunk(c + 1, v);   // in flight while this chunk is summed
-    const uint8_t *mine_chunk = &stage[warp][buf][lane * RS_STRIDE];
+    const uint8_t *mine_chunk = &stage[buf][lane * RS_STRIDE];
     if (DT == DT_BIT) {
 #pragma unroll
       for (int u = 0; u < 8; u++) {
@@ -797,6 +793,19 @@ __global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned 
     dist = __dsub_rn(1.0, fmax(-1.0, fmin(1.0, r)));
   }
   exact[(uint64_t)q * kSortCap + i] = double_key(dist);
+}
+
+// A few blocks a query, each warp taking 32 survivors at a time: most
+// queries keep about k survivors, so a grid sized for the largest possible
+// count (4,096) would be mostly blocks with nothing to do.
+template <int DT>
+__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact) {
+  __shared__ __align__(16) uint8_t stage[RS_WARPS][2][32 * RS_STRIDE];
+  const uint32_t q = blockIdx.y;
+  const uint32_t m = a.cnt[q];
+  const int warp = threadIdx.x >> 5;
+  for (uint32_t i0 = (blockIdx.x * RS_WARPS + warp) * 32; i0 < m; i0 += gridDim.x * RS_WARPS * 32)
+    rescore_group<DT>(a, exact, q, m, i0, stage[warp]);
 }
 
 // Per query: sort the survivors by (exact distance, global row id) and write
@@ -1088,7 +1097,7 @@ cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t s
   unsigned long long *ex = reinterpret_cast<unsigned long long *>(exact);
   const SelectArgs a = to_args(l);
   if (l.s.row_bytes % 16 != 0) {
-    const dim3 g(kSortCap / 128 / 4, l.nq);
+    const dim3 g(2, l.nq);
     switch (l.s.dtype) {
       case DT_F32: rescore_thread<DT_F32><<<g, 128, 0, st>>>(a, ex); break;
       case DT_F16: rescore_thread<DT_F16><<<g, 128, 0, st>>>(a, ex); break;
@@ -1097,7 +1106,7 @@ cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t s
       default: rescore_thread<DT_BIT><<<g, 128, 0, st>>>(a, ex); break;
     }
   } else {
-    const dim3 grid(kSortCap / (RS_WARPS * 32), l.nq);
+    const dim3 grid(2, l.nq);
     switch (l.s.dtype) {
       case DT_F32: rescore<DT_F32><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
       case DT_F16: rescore<DT_F16><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
