@@ -98,7 +98,8 @@ class Shard:
                                    _ptr(status), _stream(stream)))
         return dist, ids, count
 
-    def search_lists(self, queries, k, metric, offsets, probes, row_ids=None, stream=None, status=None):
+    def search_lists(self, queries, k, metric, offsets, probes, row_ids=None, stream=None, status=None,
+                     force_simt=False):
         """IVF list gather: each query's k nearest among the rows of the lists
         it probes. offsets: int64 [nlists+1] row runs of the lists; probes:
         int32 [nq][nprobe] list numbers; row_ids: optional int64 [rows] global
@@ -113,7 +114,8 @@ class Shard:
         ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
         count = torch.empty((nq,), dtype=torch.int32, device=dev)
         check(load().AnnB200SearchLists(self._handle, _ptr(queries), nq, _ptr(offsets), nlists, _ptr(probes), nprobe,
-                                        _ptr(row_ids), int(k), int(metric), 0, cap, _ptr(dist), _ptr(ids),
+                                        _ptr(row_ids), int(k), int(metric), FORCE_SIMT if force_simt else 0, cap,
+                                        _ptr(dist), _ptr(ids),
                                         _ptr(count), _ptr(status), _stream(stream)))
         return dist, ids, count
 

@@ -106,7 +106,38 @@ struct ListPlan {
   unsigned long long *tiles;  // [nlists] work items of each list
   unsigned long long *toff;   // [nlists + 1] prefix sums of tiles (toff[nlists] = items)
   unsigned long long *bsum;   // [kMaxLists / 4096] prefix-sum block totals
+  uint32_t bm, bq;            // rows and queries of a work item (the scan kernel's tile)
 };
+
+// Row range [lo, hi) of list l, clamped to the shard; bad offsets (decreasing,
+// or past the shard) are flagged by check_offsets and read as empty here.
+__device__ __forceinline__ void list_range(const ListPlan &p, uint32_t l, uint64_t &lo, uint64_t &hi) {
+  lo = p.offsets[l];
+  hi = p.offsets[l + 1];
+  if (hi > p.rows) hi = p.rows;
+  if (lo > hi) lo = hi;
+}
+
+// Rows [lo + rbegin, lo + rend) of list l, clipped to the list.
+__device__ __forceinline__ void list_window(const ListPlan &p, uint32_t l, uint64_t rbegin, uint64_t rend,
+                                            uint64_t &b, uint64_t &e) {
+  uint64_t lo, hi;
+  list_range(p, l, lo, hi);
+  const uint64_t len = hi - lo;
+  b = lo + (rbegin < len ? rbegin : len);
+  e = lo + (rend < len ? rend : len);
+}
+
+// Largest l with toff[l] <= item (toff non-decreasing, toff[0] = 0).
+__device__ __forceinline__ uint32_t find_list(const unsigned long long *toff, uint32_t nlists, uint64_t item) {
+  uint32_t lo = 0, hi = nlists;  // toff[lo] <= item < toff[hi]
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (toff[mid] <= item) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
 
 // Row id of candidate position pos: ids[pos], or pos when there is no list.
 // A list entry past the shard is clamped to its last row, so a bad list can
@@ -349,6 +380,9 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
 void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
                         uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st);
 uint32_t tc_scan_max_queries();
+cudaError_t launch_tc_scan_lists(const ScanArgs &a, const ListPlan &p, uint64_t rbegin, uint64_t rend,
+                                 const CUtensorMap &rows_map, const CUtensorMap &scales_map, const __half *q16,
+                                 uint32_t kpad, int sms, cudaStream_t st);
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,

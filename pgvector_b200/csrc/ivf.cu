@@ -108,15 +108,6 @@ void exclusive_scan(const unsigned long long *in, uint64_t n, unsigned long long
 
 // ---------------------------------------------------------------- probe table
 
-// Row range [lo, hi) of list l, clamped to the shard; bad offsets (decreasing,
-// or past the shard) are flagged by check_offsets and read as empty here.
-__device__ __forceinline__ void list_range(const ListPlan &p, uint32_t l, uint64_t &lo, uint64_t &hi) {
-  lo = p.offsets[l];
-  hi = p.offsets[l + 1];
-  if (hi > p.rows) hi = p.rows;
-  if (lo > hi) lo = hi;
-}
-
 __global__ void check_offsets(ListPlan p, uint32_t *flags) {
   const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= p.nlists) return;
@@ -178,39 +169,19 @@ __global__ void probe_fill(ListPlan p, QueryState qs) {
   }
 }
 
-// Rows [lo + rbegin, lo + rend) of list l, clipped to the list.
-__device__ __forceinline__ void list_window(const ListPlan &p, uint32_t l, uint64_t rbegin, uint64_t rend,
-                                            uint64_t &b, uint64_t &e) {
-  uint64_t lo, hi;
-  list_range(p, l, lo, hi);
-  const uint64_t len = hi - lo;
-  b = lo + (rbegin < len ? rbegin : len);
-  e = lo + (rend < len ? rend : len);
-}
-
-// Work items of list l: row tiles of its rows [rbegin, rend) x query groups.
+// Work items of list l: row tiles (p.bm rows) of its rows [rbegin, rend) x
+// query groups (p.bq queries).
 __global__ void count_tiles(ListPlan p, uint64_t rbegin, uint64_t rend) {
   const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= p.nlists) return;
   uint64_t b, e;
   list_window(p, l, rbegin, rend, b, e);
   const uint64_t len = e - b;
-  const uint64_t groups = (p.lcount[l] + BQ - 1) / BQ;
-  p.tiles[l] = (len + BM - 1) / BM * groups;
+  const uint64_t groups = (p.lcount[l] + p.bq - 1) / p.bq;
+  p.tiles[l] = (len + p.bm - 1) / p.bm * groups;
 }
 
 // ---------------------------------------------------------------- list scan
-
-// Largest l with toff[l] <= item (toff non-decreasing, toff[0] = 0).
-__device__ __forceinline__ uint32_t find_list(const unsigned long long *toff, uint32_t nlists, uint64_t item) {
-  uint32_t lo = 0, hi = nlists;  // toff[lo] <= item < toff[hi]
-  while (hi - lo > 1) {
-    const uint32_t mid = (lo + hi) >> 1;
-    if (toff[mid] <= item) lo = mid;
-    else hi = mid;
-  }
-  return lo;
-}
 
 template <int DT>
 __global__ void __launch_bounds__(256) simt_scan_lists(const ListPlan p, uint64_t rbegin, uint64_t rend,
@@ -302,6 +273,7 @@ void launch_list_items(const ListPlan &p, uint64_t rbegin, uint64_t rend, cudaSt
   exclusive_scan(p.tiles, p.nlists, p.toff, p.bsum, st);
 }
 
+// (p.bm and p.bq must be 64 and 16: the items counted for this kernel.)
 void launch_simt_scan_lists(const ListPlan &p, uint64_t rbegin, uint64_t rend, const ScanArgs &a, int sms,
                             cudaStream_t st) {
   const dim3 grid((unsigned)sms * 8);

@@ -650,6 +650,369 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   }
 }
 
+// ---------------------------------------------------------------- IVF list scan on tensor cores
+//
+// The list gather of ivf.cu on tcgen05: a work item is a 128-row tile of a
+// probed list x up to 32 of the queries that probe the list (ListPlan with
+// bm = 128, bq = 32). The rows of a list are contiguous in the shard, so the
+// tile is one TMA box -- FP16 rows straight into the A tile, E4M3 / NVFP4
+// codes (and NVFP4's block scales, 16 bytes a row covering four k-blocks)
+// into a raw ring the converter warps turn into FP16. The group's queries
+// are gathered from the FP16 query copy by cp.async into a 32-row B tile.
+// One M=128, N=32 accumulator an item, double buffered (64 TMEM columns).
+// Each CTA walks a contiguous run of items and decodes them incrementally,
+// so list metadata, query numbers and thresholds are read once a list.
+constexpr int LQ = 32;                       // queries an item (MMA N)
+constexpr int L_STG = 6;
+constexpr int L_B = LQ * 128;                // B tile: 32 queries x 64 halves
+constexpr int L_STAGE = A_BYTES + L_B;       // 20 KB, a multiple of 1024
+constexpr int L_RSTG = 6;
+constexpr int L_CW = 8;                      // query-gather / converter warps (6 .. 6+L_CW-1)
+constexpr int L_NT = 192 + 32 * L_CW;
+constexpr int L_TMEM = 64;
+
+template <int Q> struct LCfg;
+template <> struct LCfg<DT_F16> { static constexpr int RAWB = 0, RAW_X = 0, SCB = 0; };
+template <> struct LCfg<DT_E4M3> { static constexpr int RAWB = BM * 64, RAW_X = 64, SCB = 0; };
+template <> struct LCfg<DT_NVFP4> { static constexpr int RAWB = BM * 32, RAW_X = 32, SCB = BM * 16; };
+
+struct ListTcArgs {
+  ScanArgs a;
+  ListPlan p;
+  uint64_t rbegin, rend;   // the window of each list's rows this launch scans
+  const __half *q16;       // FP16 queries [.][kpad]
+  uint32_t kpad, kblocks;
+};
+
+// Walks this CTA's run of items in order: list l, item t within it (row tile
+// t / groups, query group t % groups), with the list's window and queries.
+struct ItemCursor {
+  const ListPlan *p;
+  uint64_t rbegin, rend;
+  uint64_t item, end;
+  uint32_t l;
+  uint64_t t, tiles, groups, lo, hi, qoff;
+  uint32_t nql;
+  __device__ void load_list() {
+    tiles = p->tiles[l];
+    nql = (uint32_t)p->lcount[l];
+    groups = (nql + LQ - 1) / LQ;
+    list_window(*p, l, rbegin, rend, lo, hi);
+    qoff = p->qoff[l];
+  }
+  __device__ void start(uint64_t first, uint64_t last) {
+    item = first;
+    end = last;
+    if (item < end) {
+      l = find_list(p->toff, p->nlists, item);
+      t = item - p->toff[l];
+      load_list();
+    }
+  }
+  __device__ bool valid() const { return item < end; }
+  __device__ void next() {
+    ++item;
+    if (item >= end) return;
+    if (++t >= tiles) {
+      t = 0;
+      do {
+        ++l;
+      } while (l + 1 < p->nlists && p->tiles[l] == 0);
+      load_list();
+    }
+  }
+  __device__ uint64_t row0() const { return lo + (t / groups) * BM; }
+  __device__ uint32_t group() const { return (uint32_t)(t % groups); }
+  __device__ uint32_t nq_item() const {
+    const uint32_t g0 = group() * LQ;
+    return nql - g0 < (uint32_t)LQ ? nql - g0 : (uint32_t)LQ;
+  }
+};
+
+// NVFP4 rows of one stage: codes (128 rows x 32 bytes) and the rows' block
+// scales for this k-block's four blocks (at byte (kb % 4) * 4 of each row's
+// 16-byte scale box) -> FP16 A tile of raw values (row scale in the epilogue).
+// nth converter threads, ct the thread's index.
+template <int NTH>
+__device__ __forceinline__ void convert_nvfp4_box(const uint8_t *raw, const uint8_t *sbox, uint8_t *atile,
+                                                  uint32_t ct, uint32_t kb) {
+#pragma unroll
+  for (int u = 0; u < 256 / NTH; u++) {
+    const uint32_t i = ct + NTH * u, r = i >> 1, h = i & 1;  // 32 nibbles: dims 32h .. 32h+31
+    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+    uint32_t sc[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const uint32_t code = sbox[r * 16 + (kb & 3) * 4 + h * 2 + j];
+      uint32_t pair, unused;
+      e4m3x4_to_f16(code | (code << 8), pair, unused);
+      sc[j] = pair;
+    }
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint32_t o[4];
+      e2m1x8_to_f16(ws[j], sc[j >> 1], o);
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// E4M3 rows of one stage (128 rows x 64 codes) -> FP16 A tile of raw values.
+template <int NTH>
+__device__ __forceinline__ void convert_e4m3(const uint8_t *raw, uint8_t *atile, uint32_t ct) {
+#pragma unroll
+  for (int u = 0; u < 512 / NTH; u++) {
+    const uint32_t i = ct + NTH * u, r = i >> 2, c = i & 3;  // 16 codes: dims 16c .. 16c+15
+    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + c * 16);
+    uint4 lo, hi;
+    e4m3x4_to_f16(w.x, lo.x, lo.y);
+    e4m3x4_to_f16(w.y, lo.z, lo.w);
+    e4m3x4_to_f16(w.z, hi.x, hi.y);
+    e4m3x4_to_f16(w.w, hi.z, hi.w);
+    *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c)) = lo;
+    *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c + 1)) = hi;
+  }
+}
+
+template <int Q>
+__global__ void __launch_bounds__(L_NT, 1)
+    tc_scan_lists(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap scales_map,
+                  const ListTcArgs L) {
+  using C = LCfg<Q>;
+  constexpr bool QUANT = Q != DT_F16;
+  constexpr int RAWB = C::RAWB + C::SCB;     // raw codes + (NVFP4) scale box a raw stage
+  constexpr int RSTG = QUANT ? L_RSTG : 0;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *raw = smem + L_STG * L_STAGE;
+  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);
+  uint64_t *empty = full + L_STG;
+  uint64_t *rawfull = empty + L_STG;
+  uint64_t *rawempty = rawfull + L_RSTG;
+  uint64_t *tfull = rawempty + L_RSTG;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile uint32_t *abort = tmem_slot + 1;
+  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 256);  // 4 warps x EPI_BUF
+  float *gthr = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);                    // [4 warps][32]
+  uint32_t *gq = reinterpret_cast<uint32_t *>(gthr + 4 * LQ);                          // [4 warps][32]
+
+  const ScanArgs &a = L.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t items = L.p.toff[L.p.nlists];
+  const uint64_t per = (items + gridDim.x - 1) / gridDim.x;
+  const uint64_t first = blockIdx.x * per < items ? blockIdx.x * per : items;
+  const uint64_t last = first + per < items ? first + per : items;
+  ItemCursor cur{&L.p, L.rbegin, L.rend};
+  cur.start(first, last);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L_STG; s++) {
+      // B copies (one a thread) + (converter warps | A's TMA)
+      mbar_init(full + s, QUANT ? 32 * L_CW + L_CW : 32 * L_CW + 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int r = 0; r < L_RSTG; r++) {
+      mbar_init(rawfull + r, 1);
+      mbar_init(rawempty + r, L_CW);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(L_TMEM)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    // FP16: the row tile into the stage. Quantized: codes (+ scale box) into the raw ring.
+    if (lane == 0) {
+      constexpr int RING = QUANT ? L_RSTG : L_STG;
+      uint64_t *ring_full = QUANT ? rawfull : full;
+      uint64_t *ring_empty = QUANT ? rawempty : empty;
+      uint64_t it = 0;
+      bool ok = true;
+      for (; cur.valid() && ok; cur.next()) {
+        const int32_t arow = (int32_t)cur.row0();
+        for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
+          const uint32_t s = (uint32_t)(it % RING), ph = (uint32_t)((it / RING) & 1);
+          if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags)) {
+            ok = false;
+            break;
+          }
+          if (QUANT) {
+            mbar_expect_tx(ring_full + s, (uint32_t)RAWB);
+            uint8_t *dst = raw + s * RAWB;
+            tma_load_2d(smem_u32(dst), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
+            if (C::SCB)
+              tma_load_2d(smem_u32(dst + C::RAWB), &scales_map, (int32_t)((kb >> 2) * 16), arow, ring_full + s);
+          } else {
+            mbar_expect_tx(ring_full + s, (uint32_t)A_BYTES);
+            tma_load_2d(smem_u32(smem + s * L_STAGE), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+          }
+        }
+      }
+      drain_ring(ring_full, RING, it);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = f16_idesc(LQ);
+      uint64_t it = 0, tc = 0;
+      bool ok = true;
+      for (uint64_t item = first; item < last && ok; item++, tc++) {
+        const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
+        if (!mbar_wait(tempty + ab, (use & 1) ^ 1, abort, a.flags)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * LQ;
+        for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
+          const uint32_t s = (uint32_t)(it % L_STG), ph = (uint32_t)((it / L_STG) & 1);
+          if (!mbar_wait(full + s, ph, abort, a.flags)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * L_STAGE);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (uint32_t kk = 0; kk < 4; kk++)
+            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+          tc_commit(empty + s);
+        }
+        if (ok) tc_commit(tfull + ab);
+      }
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ query gather (+ conversion)
+    // B: the item's queries (row ct/8 of the tile, 16 bytes of the
+    // k-block a thread) by cp.async; rows past the group are zero-filled.
+    // Quantized formats: then the stage's codes into the FP16 A tile.
+    static_assert(L_CW == 8, "one B chunk a gather thread");
+    const uint32_t ct = threadIdx.x - 192;
+    const uint32_t c = ct & 7, rq = ct >> 3;
+    uint64_t it = 0;
+    bool ok = true;
+    for (; cur.valid() && ok; cur.next()) {
+      const uint32_t nqt = cur.nq_item();
+      const uint64_t qb = cur.qoff + (uint64_t)cur.group() * LQ;
+      const uint32_t n = rq < nqt ? 16u : 0u;
+      const __half *src = L.q16 + (uint64_t)(rq < nqt ? L.p.qlist[qb + rq] : 0u) * L.kpad;
+      for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
+        const uint32_t s = (uint32_t)(it % L_STG), ph = (uint32_t)((it / L_STG) & 1);
+        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        uint8_t *stage = smem + s * L_STAGE;
+        cp_async16(smem_u32(stage + A_BYTES) + sw128_offset(rq, c), src + kb * 64 + c * 8, n);
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(full + s)) : "memory");
+        if (QUANT) {
+          const uint32_t r = (uint32_t)(it % L_RSTG), rph = (uint32_t)((it / L_RSTG) & 1);
+          got = mbar_wait(rawfull + r, rph, abort, a.flags);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          const uint8_t *rs = raw + r * RAWB;
+          if (Q == DT_NVFP4) convert_nvfp4_box<32 * L_CW>(rs, rs + C::RAWB, stage, ct, kb);
+          else convert_e4m3<32 * L_CW>(rs, stage, ct);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(rawempty + r);
+            mbar_arrive(full + s);
+          }
+        }
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // A lane owns one row of the item; the group's query numbers and
+    // thresholds sit in this warp's table (reloaded when the group changes).
+    Appender app{a, stage_buf + (warp - 2) * EPI_BUF, 0, lane};
+    const int quad = warp & 3;
+    float *wthr = gthr + (warp - 2) * LQ;
+    uint32_t *wq = gq + (warp - 2) * LQ;
+    uint64_t tc = 0, tab = ~0ull;
+    for (; cur.valid(); cur.next(), tc++) {
+      const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
+      const uint32_t nqt = cur.nq_item();
+      const uint64_t qb = cur.qoff + (uint64_t)cur.group() * LQ;
+      if (qb != tab) {          // a new query group: its numbers and thresholds
+        __syncwarp();
+        const uint32_t qn = (uint32_t)lane < nqt ? L.p.qlist[qb + lane] : 0u;
+        wq[lane] = qn;
+        wthr[lane] = (uint32_t)lane < nqt ? a.thr[qn] : __int_as_float(0x7fc00000);
+        __syncwarp();
+        tab = qb;
+      }
+      bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint64_t row = cur.row0() + quad * 32 + lane;
+      const bool valid = row < cur.hi;
+      float al = 0.0f, be = __int_as_float(0x7fc00000);   // rows past the list never pass
+      if (valid) row_affine(a.s, row, a.metric, a.raw_scale, al, be);
+      uint32_t r[32];
+      TMEM_LD32(tmem_base + ab * LQ + ((uint32_t)(quad * 32) << 16), r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(tempty + ab);        // the scores are in registers: the accumulator is free
+      uint32_t m = 0;
+#pragma unroll
+      for (int j = 0; j < 32; j++) m |= (uint32_t)(fmaf(__uint_as_float(r[j]), al, be) <= wthr[j]) << j;
+      while (__any_sync(0xffffffffu, m != 0)) {
+        const bool has = m != 0;
+        const int j = has ? __ffs(m) - 1 : 0;
+        m &= m - 1;
+        float v = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 32; jj++) v = (jj == j) ? __uint_as_float(r[jj]) : v;
+        v = fmaf(v, al, be);
+        const uint32_t ballot = __ballot_sync(0xffffffffu, has);
+        if (app.n + 32 > (uint32_t)EPI_BUF) app.flush();
+        if (has)
+          app.buf[app.n + __popc(ballot & ((1u << lane) - 1u))] =
+              make_uint4(wq[j], __float_as_uint(v), (uint32_t)row, 0u);
+        app.n += __popc(ballot);
+      }
+    }
+    __syncwarp();
+    if (app.n) app.flush();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(L_TMEM)
+                 : "memory");
+  }
+}
+
 // Copy candidate rows (virtual row i = candidate position base + i*stride,
 // row id ids[pos] or pos) to consecutive rows of out: one warp a row,
 // 16-byte coalesced loads and stores (row_bytes a multiple of 16).
@@ -710,6 +1073,23 @@ cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_ma
   return cudaGetLastError();
 }
 
+template <int Q>
+size_t tc_scan_lists_smem() {
+  constexpr int RAWB = LCfg<Q>::RAWB + LCfg<Q>::SCB;
+  return 1024 + (size_t)L_STG * L_STAGE + (Q != DT_F16 ? (size_t)L_RSTG * RAWB : 0) + 256 +
+         4 * EPI_BUF * sizeof(uint4) + 2 * 4 * LQ * sizeof(uint32_t);
+}
+
+template <int Q>
+cudaError_t launch_lists_t(const CUtensorMap &rows_map, const CUtensorMap &scales_map, const ListTcArgs &L, int sms,
+                           cudaStream_t st) {
+  const size_t smem = tc_scan_lists_smem<Q>();
+  cudaError_t e = cudaFuncSetAttribute(tc_scan_lists<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  tc_scan_lists<Q><<<sms, L_NT, smem, st>>>(rows_map, scales_map, L);
+  return cudaGetLastError();
+}
+
 // Launch the tensor scan of a.count virtual rows against a.nq FP16 queries.
 // FP16 rows named by a candidate list or a strided sample (a.ids set, or
 // a.stride > 1) are gathered from the shard by the kernel itself (rows_map
@@ -739,6 +1119,30 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
                                       : launch_tc_t<DT_F16>(rows_map, query_map, t, sms, st);
     case DT_E4M3: return launch_tc_t<DT_E4M3>(rows_map, query_map, t, sms, st);
     case DT_NVFP4: return launch_tc_t<DT_NVFP4>(rows_map, query_map, t, sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// The IVF list scan on tensor cores over the items launch_list_items counted
+// with p.bm = 128 and p.bq = 32 (rows [rbegin, rend) of every probed list).
+// rows_map: the shard's rows as launch_tc_scan reads contiguous runs of them;
+// scales_map (NVFP4 only): the block scales [rows][bblocks] as bytes, box 16 x
+// 128. q16: the FP16 queries [.][kpad] prep_queries wrote.
+cudaError_t launch_tc_scan_lists(const ScanArgs &a, const ListPlan &p, uint64_t rbegin, uint64_t rend,
+                                 const CUtensorMap &rows_map, const CUtensorMap &scales_map, const __half *q16,
+                                 uint32_t kpad, int sms, cudaStream_t st) {
+  ListTcArgs L;
+  L.a = a;
+  L.p = p;
+  L.rbegin = rbegin;
+  L.rend = rend;
+  L.q16 = q16;
+  L.kpad = kpad;
+  L.kblocks = kpad / 64;
+  switch (a.s.dtype) {
+    case DT_F16: return launch_lists_t<DT_F16>(rows_map, scales_map, L, sms, st);
+    case DT_E4M3: return launch_lists_t<DT_E4M3>(rows_map, scales_map, L, sms, st);
+    case DT_NVFP4: return launch_lists_t<DT_NVFP4>(rows_map, scales_map, L, sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -273,6 +273,8 @@ struct AnnB200Shard {
   uint32_t *hflags = nullptr;  // pinned: flags readback
   CUtensorMap rows_map;        // the shard's FP16 rows, box 64 x 128, for the tensor scan
   bool rows_map_ok = false;
+  CUtensorMap scales_map;      // NVFP4 block scales [rows][bblocks], box 16 x 128 (IVF tensor scan)
+  bool scales_map_ok = false;
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
@@ -394,6 +396,10 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   // the tensor scan gathers 128-byte row pieces by TMA (row pitch a multiple of 16 bytes)
   s->rows_map_ok = tc_format(dtype, dims, v.row_bytes) && rows > 0 && rows < (1ull << 31) &&
                    encode_rows_map(&s->rows_map, dtype, v.codes, dims, rows, v.row_bytes);
+  // the IVF tensor scan reads NVFP4 block scales by TMA: 16 bytes (four
+  // k-blocks) a row a box, so the scale pitch must be a multiple of 16
+  s->scales_map_ok = s->rows_map_ok && dtype == DT_NVFP4 && v.bblocks % 16 == 0 &&
+                     encode_u8_map(&s->scales_map, v.bscales, v.bblocks, rows, v.bblocks, 16);
   return OK;
 }
 
@@ -770,10 +776,14 @@ namespace {
 // exact rescoring and ordering.
 int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *offsets,
                        uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids, uint32_t k,
-                       uint32_t metric, uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
-                       int32_t *status, cudaStream_t st, bool *any_invalid) {
+                       uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                       uint32_t *out_count, int32_t *status, cudaStream_t st, bool *any_invalid) {
   const ShardView &v = sh->view;
-  const double gamma = scan_gamma(false, false, 0, v.dims);
+  // tensor cores when the rows can be read by TMA (and NVFP4's scales too)
+  const bool tc = !(flags & ANNB200_FORCE_SIMT) && sh->rows_map_ok &&
+                  (v.dtype != DT_NVFP4 || sh->scales_map_ok);
+  const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
+  const double gamma = scan_gamma(false, tc, kpad, v.dims);
   const uint64_t S = std::max<uint64_t>(64, ((uint64_t)k + 63) / 64 * 64);
 
   Carver c;
@@ -783,7 +793,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
                o_exact = c.take<double>((size_t)nq * kSortCap), o_lcount = c.take<uint64_t>(nlists),
                o_lfill = c.take<uint64_t>(nlists), o_tiles = c.take<uint64_t>(nlists),
                o_qoff = c.take<uint64_t>((size_t)nlists + 1), o_toff = c.take<uint64_t>((size_t)nlists + 1),
-               o_bsum = c.take<uint64_t>(kMaxLists / 4096), o_qlist = c.take<uint32_t>((size_t)nq * nprobe);
+               o_bsum = c.take<uint64_t>(kMaxLists / 4096), o_qlist = c.take<uint32_t>((size_t)nq * nprobe),
+               o_q16 = c.take<__half>((size_t)nq * kpad);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
   double *exact = (double *)(w + o_exact);
@@ -794,6 +805,7 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   qs.err = (double *)(w + o_err);
   qs.thr = (float *)(w + o_thr);
   qs.status = (int32_t *)(w + o_status);
+  qs.q16 = (__half *)(w + o_q16);
   uint32_t *cnt = (uint32_t *)(w + o_cnt);
   uint32_t *dflags = (uint32_t *)(w + o_flags);
   uint32_t *big = (uint32_t *)(w + o_big);
@@ -811,6 +823,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   p.toff = (unsigned long long *)(w + o_toff);
   p.bsum = (unsigned long long *)(w + o_bsum);
   p.qlist = (uint32_t *)(w + o_qlist);
+  p.bm = tc ? 128 : 64;   // an item: 128 rows x 32 queries on tensor cores, 64 x 16 on CUDA cores
+  p.bq = tc ? 32 : 16;
 
   // the first window appends at most nprobe * S rows a query: it never overflows
   uint32_t cap = (uint32_t)std::max<uint64_t>({kBaseCap, 8ull * k, (uint64_t)nprobe * S});
@@ -824,7 +838,7 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   }
   StageClock clock(st);
   int h = clock.begin(ST_PREP);
-  launch_prep_queries(queries, nq, v.dims, metric, 0, 0, gamma, sh->maxn2, qs, 0, dflags, st);
+  launch_prep_queries(queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, 0, dflags, st);
   launch_list_plan(p, qs, dflags, st);
   clock.end(h);
   counted(1 + (nlists ? 1 : 0) + 2 + list_plan_scan_launches(nlists));
@@ -836,6 +850,7 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   a.nq = nq;
   a.metric = metric;
   a.mode = MODE_FILTER;
+  a.raw_scale = tc && v.dtype != DT_F16;   // tensor scan of quantized rows: scores on raw codes
   a.thr = qs.thr;
   a.cnt = cnt;
   a.flags = dflags;
@@ -861,10 +876,12 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   auto pass = [&](int stage, uint64_t rbegin, uint64_t rend) -> cudaError_t {
     int hk = clock.begin(stage);
     launch_list_items(p, rbegin, rend, st);
-    launch_simt_scan_lists(p, rbegin, rend, a, sh->sms, st);
+    cudaError_t e = cudaSuccess;
+    if (tc) e = launch_tc_scan_lists(a, p, rbegin, rend, sh->rows_map, sh->scales_map, qs.q16, kpad, sh->sms, st);
+    else launch_simt_scan_lists(p, rbegin, rend, a, sh->sms, st);
     clock.end(hk);
     counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1);
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
   };
 
   for (;;) {
@@ -944,7 +961,7 @@ extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32
       r = OK;
     } else {
       r = search_lists_block(sh, queries + (uint64_t)q0 * v.dims, m, list_offsets, nlists, probes + (uint64_t)q0 * nprobe,
-                             nprobe, row_ids, k, metric, out_cap, out_dist + (uint64_t)q0 * out_cap,
+                             nprobe, row_ids, k, metric, flags, out_cap, out_dist + (uint64_t)q0 * out_cap,
                              out_id + (uint64_t)q0 * out_cap, out_count + q0, status ? status + q0 : nullptr, st,
                              &any_invalid);
     }

@@ -38,19 +38,23 @@ def encode(dtype, x):
     return codes, bs, rs
 
 
-def gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None, status=None):
+def gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None, status=None,
+              force_simt=False):
     import pgvector_b200 as pb
     shard = pb.Shard(dtype, dims, to_dev(codes, cuda), None if bs is None else to_dev(bs, cuda),
                      None if rs is None else to_dev(rs, cuda))
     d, i, c = shard.search_lists(to_dev(q, cuda), k, metric, to_dev(offsets, cuda), to_dev(probes, cuda),
-                                 row_ids=None if row_ids is None else to_dev(row_ids, cuda), status=status)
+                                 row_ids=None if row_ids is None else to_dev(row_ids, cuda), status=status,
+                                 force_simt=force_simt)
     return d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy()
 
 
-def assert_lists_same(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None):
+def assert_lists_same(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None,
+                      force_simt=False):
     od, oi, oc = oracle.search_lists(dtype, dims, codes, q, offsets, probes, k, metric, row_ids=row_ids,
                                      block_scales=bs, row_scales=rs)
-    gd, gi, gc = gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids)
+    gd, gi, gc = gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids,
+                           force_simt=force_simt)
     assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
     for j in range(q.shape[0]):
         c = int(oc[j])
@@ -59,18 +63,25 @@ def assert_lists_same(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, m
     return oc
 
 
-@pytest.mark.parametrize('dtype,metric', [(0, 0), (0, 1), (0, 2), (1, 2), (1, 0), (2, 1), (3, 0), (3, 2)])
-def test_list_gather_formats_and_metrics(cuda, dtype, metric):
-    dims = 96 if dtype != oracle.F32 else 37
+@pytest.mark.parametrize('dtype,dims,metric', [(0, 37, 0), (0, 37, 1), (0, 37, 2), (1, 96, 2), (1, 96, 0),
+                                               (1, 200, 1), (2, 96, 1), (2, 200, 0), (3, 96, 0), (3, 256, 0),
+                                               (3, 512, 2)])
+@pytest.mark.parametrize('simt', [False, True])
+def test_list_gather_formats_and_metrics(cuda, dtype, dims, metric, simt):
+    # tensor cores for FP16 / E4M3 rows and NVFP4 rows whose scale rows are
+    # a multiple of 16 bytes (dims % 256 == 0); CUDA cores otherwise and
+    # with ANNB200_FORCE_SIMT
     x, offsets, cent, row_ids = synth.ivf_corpus(30000, dims, 128, seed=10 + dtype)
     q = synth.mixture_queries(48, dims, 16, seed=11)
     q = cent[np.arange(48) % 128] + 0.1 * q.astype(np.float32)
     probes = synth.ivf_probes(q, cent, 8)
     codes, bs, rs = encode(dtype, x)
-    assert_lists_same(cuda, dtype, dims, codes, bs, rs, q.astype(np.float32), offsets, probes, 20, metric, row_ids)
+    assert_lists_same(cuda, dtype, dims, codes, bs, rs, q.astype(np.float32), offsets, probes, 20, metric, row_ids,
+                      force_simt=simt)
 
 
-def test_config4_shape_nvfp4_l2(cuda):
+@pytest.mark.parametrize('simt', [False, True])
+def test_config4_shape_nvfp4_l2(cuda, simt):
     # config 4's format and probe pattern at a size the oracle finishes quickly:
     # NVFP4 d=768, Zipf(1.1) list sizes, nprobe 64, k 100
     x, offsets, cent, row_ids = synth.ivf_corpus(60000, 768, 1024, seed=20)
@@ -78,38 +89,42 @@ def test_config4_shape_nvfp4_l2(cuda):
     probes = synth.ivf_probes(q, cent, 64)
     codes, bs, rs = oracle.quantize_nvfp4(x)
     assert_lists_same(cuda, oracle.NVFP4, 768, codes, bs, rs, q.astype(np.float32), offsets, probes, 100, 0,
-                      row_ids)
+                      row_ids, force_simt=simt)
 
 
-def test_ties_order_by_global_id_across_lists(cuda):
+@pytest.mark.parametrize('dtype', [0, 1])
+def test_ties_order_by_global_id_across_lists(cuda, dtype):
     # the same vector stored in several lists under different global ids:
     # equal distances must come out in id order whatever the storage order
     rng = np.random.default_rng(30)
     base = rng.standard_normal((50, 16)).astype(np.float32)
     x = np.concatenate([base, base, base, base])          # 4 lists of 50 identical rows
+    codes, bs, rs = encode(dtype, x)
     offsets = np.array([0, 50, 100, 150, 200], dtype=np.uint64)
     row_ids = rng.permutation(200).astype(np.int64) * 3 + 7
     q = base[:6] + 0.01
     probes = np.tile(np.array([3, 0, 2, 1], dtype=np.uint32), (6, 1))
     for metric in (0, 1, 2):
-        assert_lists_same(cuda, oracle.F32, 16, x, None, None, q, offsets, probes, 30, metric, row_ids)
+        assert_lists_same(cuda, dtype, 16, codes, bs, rs, q, offsets, probes, 30, metric, row_ids)
     # without row_ids the ids are the storage rows
-    assert_lists_same(cuda, oracle.F32, 16, x, None, None, q, offsets, probes, 30, 0)
+    assert_lists_same(cuda, dtype, 16, codes, bs, rs, q, offsets, probes, 30, 0)
 
 
-def test_small_and_empty_lists_and_large_k(cuda):
+@pytest.mark.parametrize('dtype', [0, 1])
+def test_small_and_empty_lists_and_large_k(cuda, dtype):
     # empty lists, lists shorter than k, and a k past the shared-memory sort
     # (more than 4,096 survivors: the large-sort path)
     x, offsets, cent, row_ids = synth.ivf_corpus(20000, 32, 64, zipf=1.6, seed=40)
+    codes, bs, rs = encode(dtype, x)
     sizes = np.diff(offsets.astype(np.int64))
     offsets2 = offsets.copy()
     offsets2[1:] = np.cumsum(np.where(np.arange(64) % 7 == 0, 0, sizes))   # every 7th list empty
     n2 = int(offsets2[-1])
     q = cent[:40] + 0.05
     probes = synth.ivf_probes(q, cent, 5)
-    oc = assert_lists_same(cuda, oracle.F32, 32, x[:n2], None, None, q, offsets2, probes, 50, 0, row_ids[:n2])
+    oc = assert_lists_same(cuda, dtype, 32, codes[:n2], None, None, q, offsets2, probes, 50, 0, row_ids[:n2])
     assert (oc < 50).any()       # some queries probe fewer than k rows
-    assert_lists_same(cuda, oracle.F32, 32, x, None, None, q, offsets, probes, 5000, 0, row_ids)
+    assert_lists_same(cuda, dtype, 32, codes, None, None, q, offsets, probes, 5000, 0, row_ids)
 
 
 def test_bad_probes_are_invalid_queries(cuda):
@@ -130,22 +145,24 @@ def test_bad_probes_are_invalid_queries(cuda):
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
 
 
-def test_padding_probes_and_list_shards(cuda):
+@pytest.mark.parametrize('dtype', [0, 1])
+def test_padding_probes_and_list_shards(cuda, dtype):
     # lists sharded over two "ranks": each shard sees only its own lists, the
     # others padded with UINT32_MAX; merging both shards' results gives the
     # unsharded answer
     import torch
     import pgvector_b200 as pb
     x, offsets, cent, row_ids = synth.ivf_corpus(30000, 48, 96, seed=70)
+    x, _, _ = encode(dtype, x)
     q = cent[np.arange(40) % 96] + 0.05
     probes = synth.ivf_probes(q, cent, 10)
-    od, oi, oc = oracle.search_lists(oracle.F32, 48, x, q, offsets, probes, 25, 0, row_ids=row_ids)
+    od, oi, oc = oracle.search_lists(dtype, 48, x, q, offsets, probes, 25, 0, row_ids=row_ids)
     parts = []
     for l0, l1 in ((0, 50), (50, 96)):
         lo, hi = int(offsets[l0]), int(offsets[l1])
         local = np.where((probes >= l0) & (probes < l1), probes - l0, 0xffffffff).astype(np.uint32)
         off = (offsets[l0:l1 + 1] - offsets[l0]).astype(np.uint64)
-        parts.append(gpu_lists(cuda, oracle.F32, 48, x[lo:hi], None, None, q, off, local, 25, 0, row_ids[lo:hi]))
+        parts.append(gpu_lists(cuda, dtype, 48, x[lo:hi], None, None, q, off, local, 25, 0, row_ids[lo:hi]))
     gd = torch.from_numpy(np.stack([p[0] for p in parts])).to(cuda)
     gi = torch.from_numpy(np.stack([p[1] for p in parts])).to(cuda)
     gc = torch.from_numpy(np.stack([p[2] for p in parts]).astype(np.int32)).to(cuda)
