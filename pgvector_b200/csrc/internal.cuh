@@ -107,6 +107,8 @@ struct ListPlan {
   unsigned long long *toff;   // [nlists + 1] prefix sums of tiles (toff[nlists] = items)
   unsigned long long *bsum;   // [kMaxLists / 4096] prefix-sum block totals
   uint32_t bm, bq;            // rows and queries of a work item (the scan kernel's tile)
+  uint32_t *nzl;              // [nlists] the lists with work items, in order (tensor scan; or NULL)
+  unsigned long long *nzoff;  // [nlists + 1] their prefix counts (nzoff[nlists] = how many)
 };
 
 // Row range [lo, hi) of list l, clamped to the shard; bad offsets (decreasing,

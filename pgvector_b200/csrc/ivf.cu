@@ -181,6 +181,16 @@ __global__ void count_tiles(ListPlan p, uint64_t rbegin, uint64_t rend) {
   p.tiles[l] = (len + p.bm - 1) / p.bm * groups;
 }
 
+__global__ void flag_nonempty(ListPlan p) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l < p.nlists) p.lfill[l] = p.tiles[l] > 0 ? 1ull : 0ull;
+}
+
+__global__ void scatter_nonempty(ListPlan p) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l < p.nlists && p.tiles[l] > 0) p.nzl[p.nzoff[l]] = l;
+}
+
 // ---------------------------------------------------------------- list scan
 
 template <int DT>
@@ -268,9 +278,16 @@ void launch_list_plan(const ListPlan &p, const QueryState &qs, uint32_t *flags, 
 }
 
 // Items of a pass over rows [rbegin, rend) of every probed list.
+// With p.nzl set, also the compact list of lists that have work items
+// (flags in lfill, free once the probe table is inverted).
 void launch_list_items(const ListPlan &p, uint64_t rbegin, uint64_t rend, cudaStream_t st) {
   if (p.nlists) count_tiles<<<(p.nlists + 255) / 256, 256, 0, st>>>(p, rbegin, rend);
   exclusive_scan(p.tiles, p.nlists, p.toff, p.bsum, st);
+  if (p.nzl) {
+    if (p.nlists) flag_nonempty<<<(p.nlists + 255) / 256, 256, 0, st>>>(p);
+    exclusive_scan(p.lfill, p.nlists, p.nzoff, p.bsum, st);
+    if (p.nlists) scatter_nonempty<<<(p.nlists + 255) / 256, 256, 0, st>>>(p);
+  }
 }
 
 // (p.bm and p.bq must be 64 and 16: the items counted for this kernel.)

@@ -663,18 +663,20 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 // Each CTA walks a contiguous run of items and decodes them incrementally,
 // so list metadata, query numbers and thresholds are read once a list.
 constexpr int LQ = 32;                       // queries an item (MMA N)
-constexpr int L_STG = 6;
 constexpr int L_B = LQ * 128;                // B tile: 32 queries x 64 halves
 constexpr int L_STAGE = A_BYTES + L_B;       // 20 KB, a multiple of 1024
-constexpr int L_RSTG = 6;
 constexpr int L_CW = 8;                      // query-gather / converter warps (6 .. 6+L_CW-1)
 constexpr int L_NT = 192 + 32 * L_CW;
 constexpr int L_TMEM = 64;
 
+// STG converted stages (A + B); RSTG raw stages of codes in flight from HBM
+// (quantized formats: the deep ring that covers HBM latency).
 template <int Q> struct LCfg;
-template <> struct LCfg<DT_F16> { static constexpr int RAWB = 0, RAW_X = 0, SCB = 0; };
-template <> struct LCfg<DT_E4M3> { static constexpr int RAWB = BM * 64, RAW_X = 64, SCB = 0; };
-template <> struct LCfg<DT_NVFP4> { static constexpr int RAWB = BM * 32, RAW_X = 32, SCB = BM * 16; };
+template <> struct LCfg<DT_F16> { static constexpr int STG = 9, RSTG = 0, RAWB = 0, RAW_X = 0, SCB = 0; };
+template <> struct LCfg<DT_E4M3> { static constexpr int STG = 4, RSTG = 12, RAWB = BM * 64, RAW_X = 64, SCB = 0; };
+template <> struct LCfg<DT_NVFP4> {
+  static constexpr int STG = 4, RSTG = 16, RAWB = BM * 32, RAW_X = 32, SCB = BM * 16;
+};
 
 struct ListTcArgs {
   ScanArgs a;
@@ -686,27 +688,57 @@ struct ListTcArgs {
 
 // Walks this CTA's run of items in order: list l, item t within it (row tile
 // t / groups, query group t % groups), with the list's window and queries.
+// Lists come from the compact list of lists with items (p.nzl), and the next
+// list's metadata is requested while the current list is worked on, so a
+// list change costs no memory round trip.
 struct ItemCursor {
   const ListPlan *p;
   uint64_t rbegin, rend;
-  uint64_t item, end;
-  uint32_t l;
+  uint64_t item, end, ci, nci;
+  uint32_t l, nql;
   uint64_t t, tiles, groups, lo, hi, qoff;
-  uint32_t nql;
-  __device__ void load_list() {
-    tiles = p->tiles[l];
-    nql = (uint32_t)p->lcount[l];
+  // the next list (loads in flight)
+  uint32_t nl;
+  unsigned long long ntiles, nlcount, noff0, noff1, nqoff;
+  __device__ void set_list(uint32_t list, unsigned long long tl, unsigned long long lc, unsigned long long o0,
+                           unsigned long long o1, unsigned long long qo) {
+    l = list;
+    tiles = tl;
+    nql = (uint32_t)lc;
     groups = (nql + LQ - 1) / LQ;
-    list_window(*p, l, rbegin, rend, lo, hi);
-    qoff = p->qoff[l];
+    uint64_t h = o1 < p->rows ? o1 : p->rows;   // list_range's clamping
+    uint64_t b = o0 < h ? o0 : h;
+    const uint64_t len = h - b;
+    lo = b + (rbegin < len ? rbegin : len);
+    hi = b + (rend < len ? rend : len);
+    qoff = qo;
+  }
+  __device__ void fetch_next() {
+    if (ci + 1 < nci) {
+      nl = p->nzl[ci + 1];
+      ntiles = p->tiles[nl];
+      nlcount = p->lcount[nl];
+      noff0 = p->offsets[nl];
+      noff1 = p->offsets[nl + 1];
+      nqoff = p->qoff[nl];
+    }
   }
   __device__ void start(uint64_t first, uint64_t last) {
     item = first;
     end = last;
+    nci = p->nzoff[p->nlists];
     if (item < end) {
-      l = find_list(p->toff, p->nlists, item);
-      t = item - p->toff[l];
-      load_list();
+      uint64_t a = 0, b = nci;   // toff[nzl[a]] <= item < toff[nzl[b]] (or b = nci)
+      while (b - a > 1) {
+        const uint64_t mid = (a + b) >> 1;
+        if (p->toff[p->nzl[mid]] <= item) a = mid;
+        else b = mid;
+      }
+      ci = a;
+      const uint32_t list = p->nzl[ci];
+      set_list(list, p->tiles[list], p->lcount[list], p->offsets[list], p->offsets[list + 1], p->qoff[list]);
+      t = item - p->toff[list];
+      fetch_next();
     }
   }
   __device__ bool valid() const { return item < end; }
@@ -715,10 +747,9 @@ struct ItemCursor {
     if (item >= end) return;
     if (++t >= tiles) {
       t = 0;
-      do {
-        ++l;
-      } while (l + 1 < p->nlists && p->tiles[l] == 0);
-      load_list();
+      ++ci;
+      set_list(nl, ntiles, nlcount, noff0, noff1, nqoff);
+      fetch_next();
     }
   }
   __device__ uint64_t row0() const { return lo + (t / groups) * BM; }
@@ -726,6 +757,20 @@ struct ItemCursor {
   __device__ uint32_t nq_item() const {
     const uint32_t g0 = group() * LQ;
     return nql - g0 < (uint32_t)LQ ? nql - g0 : (uint32_t)LQ;
+  }
+  __device__ uint64_t qbase() const { return qoff + (uint64_t)group() * LQ; }
+  // The query group of the next item: false if this is the run's last item.
+  __device__ bool peek_group(uint64_t &qb, uint32_t &nqt) const {
+    if (item + 1 >= end) return false;
+    if (t + 1 < tiles) {
+      const uint32_t g = (uint32_t)((t + 1) % groups);
+      qb = qoff + (uint64_t)g * LQ;
+      nqt = nql - g * LQ < (uint32_t)LQ ? nql - g * LQ : (uint32_t)LQ;
+    } else {
+      qb = nqoff;
+      nqt = nlcount < (unsigned long long)LQ ? (uint32_t)nlcount : (uint32_t)LQ;
+    }
+    return true;
   }
 };
 
@@ -782,7 +827,8 @@ __global__ void __launch_bounds__(L_NT, 1)
   using C = LCfg<Q>;
   constexpr bool QUANT = Q != DT_F16;
   constexpr int RAWB = C::RAWB + C::SCB;     // raw codes + (NVFP4) scale box a raw stage
-  constexpr int RSTG = QUANT ? L_RSTG : 0;
+  constexpr int L_STG = C::STG, L_RSTG = C::RSTG > 0 ? C::RSTG : 1;
+  constexpr int RSTG = C::RSTG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *raw = smem + L_STG * L_STAGE;
@@ -795,7 +841,7 @@ __global__ void __launch_bounds__(L_NT, 1)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile uint32_t *abort = tmem_slot + 1;
-  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 256);  // 4 warps x EPI_BUF
+  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 512);  // 4 warps x EPI_BUF
   float *gthr = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);                    // [4 warps][32]
   uint32_t *gq = reinterpret_cast<uint32_t *>(gthr + 4 * LQ);                          // [4 warps][32]
 
@@ -814,7 +860,7 @@ __global__ void __launch_bounds__(L_NT, 1)
       mbar_init(full + s, QUANT ? 32 * L_CW + L_CW : 32 * L_CW + 1);
       mbar_init(empty + s, 1);
     }
-    for (int r = 0; r < L_RSTG; r++) {
+    for (int r = 0; r < RSTG; r++) {
       mbar_init(rawfull + r, 1);
       mbar_init(rawempty + r, L_CW);
     }
@@ -912,11 +958,22 @@ __global__ void __launch_bounds__(L_NT, 1)
     const uint32_t c = ct & 7, rq = ct >> 3;
     uint64_t it = 0;
     bool ok = true;
+    uint64_t pf_qb = ~0ull;      // the next item's query number, requested one item ahead
+    uint32_t pf_q = 0;
     for (; cur.valid() && ok; cur.next()) {
       const uint32_t nqt = cur.nq_item();
-      const uint64_t qb = cur.qoff + (uint64_t)cur.group() * LQ;
+      const uint64_t qb = cur.qbase();
       const uint32_t n = rq < nqt ? 16u : 0u;
-      const __half *src = L.q16 + (uint64_t)(rq < nqt ? L.p.qlist[qb + rq] : 0u) * L.kpad;
+      const uint32_t qn = rq < nqt ? (qb == pf_qb ? pf_q : L.p.qlist[qb + rq]) : 0u;
+      const __half *src = L.q16 + (uint64_t)qn * L.kpad;
+      {
+        uint64_t nqb;
+        uint32_t nnqt;
+        if (cur.peek_group(nqb, nnqt) && nqb != qb) {
+          pf_qb = nqb;
+          pf_q = rq < nnqt ? L.p.qlist[nqb + rq] : 0u;
+        }
+      }
       for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
         const uint32_t s = (uint32_t)(it % L_STG), ph = (uint32_t)((it / L_STG) & 1);
         bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
@@ -957,17 +1014,40 @@ __global__ void __launch_bounds__(L_NT, 1)
     float *wthr = gthr + (warp - 2) * LQ;
     uint32_t *wq = gq + (warp - 2) * LQ;
     uint64_t tc = 0, tab = ~0ull;
+    // the next group's query number and threshold, requested one item ahead
+    uint64_t pf_qb = ~0ull;
+    uint32_t pf_q = 0, pf_nqt = 0;
+    float pf_t = 0.0f;
     for (; cur.valid(); cur.next(), tc++) {
       const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
       const uint32_t nqt = cur.nq_item();
-      const uint64_t qb = cur.qoff + (uint64_t)cur.group() * LQ;
+      const uint64_t qb = cur.qbase();
       if (qb != tab) {          // a new query group: its numbers and thresholds
         __syncwarp();
-        const uint32_t qn = (uint32_t)lane < nqt ? L.p.qlist[qb + lane] : 0u;
+        uint32_t qn;
+        float th;
+        if (qb == pf_qb) {
+          qn = pf_q;
+          th = pf_t;
+        } else {
+          qn = (uint32_t)lane < nqt ? L.p.qlist[qb + lane] : 0u;
+          th = (uint32_t)lane < nqt ? a.thr[qn] : __int_as_float(0x7fc00000);
+        }
         wq[lane] = qn;
-        wthr[lane] = (uint32_t)lane < nqt ? a.thr[qn] : __int_as_float(0x7fc00000);
+        wthr[lane] = th;
         __syncwarp();
         tab = qb;
+      }
+      bool pf_new = false;
+      {
+        uint64_t nqb;
+        uint32_t nnqt;
+        if (cur.peek_group(nqb, nnqt) && nqb != qb && nqb != pf_qb) {
+          pf_qb = nqb;
+          pf_nqt = nnqt;
+          pf_q = (uint32_t)lane < nnqt ? L.p.qlist[nqb + lane] : 0u;
+          pf_new = true;
+        }
       }
       bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
       if (!__all_sync(0xffffffffu, got)) break;
@@ -984,6 +1064,7 @@ __global__ void __launch_bounds__(L_NT, 1)
       uint32_t m = 0;
 #pragma unroll
       for (int j = 0; j < 32; j++) m |= (uint32_t)(fmaf(__uint_as_float(r[j]), al, be) <= wthr[j]) << j;
+      if (pf_new) pf_t = (uint32_t)lane < pf_nqt ? a.thr[pf_q] : __int_as_float(0x7fc00000);
       while (__any_sync(0xffffffffu, m != 0)) {
         const bool has = m != 0;
         const int j = has ? __ffs(m) - 1 : 0;
@@ -1076,7 +1157,7 @@ cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_ma
 template <int Q>
 size_t tc_scan_lists_smem() {
   constexpr int RAWB = LCfg<Q>::RAWB + LCfg<Q>::SCB;
-  return 1024 + (size_t)L_STG * L_STAGE + (Q != DT_F16 ? (size_t)L_RSTG * RAWB : 0) + 256 +
+  return 1024 + (size_t)LCfg<Q>::STG * L_STAGE + (size_t)LCfg<Q>::RSTG * RAWB + 512 +
          4 * EPI_BUF * sizeof(uint4) + 2 * 4 * LQ * sizeof(uint32_t);
 }
 

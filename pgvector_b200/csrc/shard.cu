@@ -794,7 +794,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
                o_lfill = c.take<uint64_t>(nlists), o_tiles = c.take<uint64_t>(nlists),
                o_qoff = c.take<uint64_t>((size_t)nlists + 1), o_toff = c.take<uint64_t>((size_t)nlists + 1),
                o_bsum = c.take<uint64_t>(kMaxLists / 4096), o_qlist = c.take<uint32_t>((size_t)nq * nprobe),
-               o_q16 = c.take<__half>((size_t)nq * kpad);
+               o_q16 = c.take<__half>((size_t)nq * kpad), o_nzl = c.take<uint32_t>(tc ? nlists : 0),
+               o_nzoff = c.take<uint64_t>(tc ? (size_t)nlists + 1 : 0);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
   double *exact = (double *)(w + o_exact);
@@ -825,6 +826,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   p.qlist = (uint32_t *)(w + o_qlist);
   p.bm = tc ? 128 : 64;   // an item: 128 rows x 32 queries on tensor cores, 64 x 16 on CUDA cores
   p.bq = tc ? 32 : 16;
+  p.nzl = tc ? (uint32_t *)(w + o_nzl) : nullptr;
+  p.nzoff = tc ? (unsigned long long *)(w + o_nzoff) : nullptr;
 
   // the first window appends at most nprobe * S rows a query: it never overflows
   uint32_t cap = (uint32_t)std::max<uint64_t>({kBaseCap, 8ull * k, (uint64_t)nprobe * S});
@@ -880,7 +883,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
     if (tc) e = launch_tc_scan_lists(a, p, rbegin, rend, sh->rows_map, sh->scales_map, qs.q16, kpad, sh->sms, st);
     else launch_simt_scan_lists(p, rbegin, rend, a, sh->sms, st);
     clock.end(hk);
-    counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1);
+    counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1 +
+            (tc ? (nlists ? 2 : 0) + list_plan_scan_launches(nlists) : 0));
     return e != cudaSuccess ? e : cudaGetLastError();
   };
 
