@@ -664,18 +664,24 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 // so list metadata, query numbers and thresholds are read once a list.
 constexpr int LQ = 32;                       // queries an item (MMA N)
 constexpr int L_B = LQ * 128;                // B tile: 32 queries x 64 halves
-constexpr int L_STAGE = A_BYTES + L_B;       // 20 KB, a multiple of 1024
-constexpr int L_CW = 8;                      // query-gather / converter warps (6 .. 6+L_CW-1)
-constexpr int L_NT = 192 + 32 * L_CW;
+constexpr int L_CW = 8;                      // converter warps (6 .. 13)
+constexpr int L_BW = 6 + L_CW;               // the query-gather warp
+constexpr int L_NT = 32 * (L_BW + 1);
 constexpr int L_TMEM = 64;
+constexpr int L_BAR = 1024;                  // barrier region bytes
 
-// STG converted stages (A + B); RSTG raw stages of codes in flight from HBM
-// (quantized formats: the deep ring that covers HBM latency).
+// STG A stages (converted FP16 row tiles); BSTG query tiles, gathered up to
+// BSTG k-blocks ahead so their L2 latency stays hidden; RSTG raw stages of
+// codes in flight from HBM (quantized formats).
 template <int Q> struct LCfg;
-template <> struct LCfg<DT_F16> { static constexpr int STG = 9, RSTG = 0, RAWB = 0, RAW_X = 0, SCB = 0; };
-template <> struct LCfg<DT_E4M3> { static constexpr int STG = 4, RSTG = 12, RAWB = BM * 64, RAW_X = 64, SCB = 0; };
+template <> struct LCfg<DT_F16> {
+  static constexpr int STG = 8, BSTG = 16, RSTG = 0, RAWB = 0, RAW_X = 0, SCB = 0;
+};
+template <> struct LCfg<DT_E4M3> {
+  static constexpr int STG = 4, BSTG = 16, RSTG = 9, RAWB = BM * 64, RAW_X = 64, SCB = 0;
+};
 template <> struct LCfg<DT_NVFP4> {
-  static constexpr int STG = 4, RSTG = 16, RAWB = BM * 32, RAW_X = 32, SCB = BM * 16;
+  static constexpr int STG = 4, BSTG = 16, RSTG = 12, RAWB = BM * 32, RAW_X = 32, SCB = BM * 16;
 };
 
 struct ListTcArgs {
@@ -827,23 +833,25 @@ __global__ void __launch_bounds__(L_NT, 1)
   using C = LCfg<Q>;
   constexpr bool QUANT = Q != DT_F16;
   constexpr int RAWB = C::RAWB + C::SCB;     // raw codes + (NVFP4) scale box a raw stage
-  constexpr int L_STG = C::STG, L_RSTG = C::RSTG > 0 ? C::RSTG : 1;
-  constexpr int RSTG = C::RSTG;
+  constexpr int STG = C::STG, BSTG = C::BSTG, RSTG = C::RSTG, RSTG1 = RSTG > 0 ? RSTG : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *raw = smem + L_STG * L_STAGE;
-  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);
-  uint64_t *empty = full + L_STG;
-  uint64_t *rawfull = empty + L_STG;
-  uint64_t *rawempty = rawfull + L_RSTG;
-  uint64_t *tfull = rawempty + L_RSTG;
+  uint8_t *btiles = smem + STG * A_BYTES;
+  uint8_t *raw = btiles + BSTG * L_B;
+  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);   // A tile ready
+  uint64_t *empty = full + STG;                                        // A stage consumed
+  uint64_t *bfull = empty + STG;                                       // query tile landed
+  uint64_t *bempty = bfull + BSTG;                                     // query tile consumed
+  uint64_t *rawfull = bempty + BSTG;
+  uint64_t *rawempty = rawfull + RSTG1;
+  uint64_t *tfull = rawempty + RSTG1;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile uint32_t *abort = tmem_slot + 1;
-  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 512);  // 4 warps x EPI_BUF
-  float *gthr = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);                    // [4 warps][32]
-  uint32_t *gq = reinterpret_cast<uint32_t *>(gthr + 4 * LQ);                          // [4 warps][32]
+  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + L_BAR);  // 4 warps x EPI_BUF
+  float *gthr = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);                      // [4 warps][32]
+  uint32_t *gq = reinterpret_cast<uint32_t *>(gthr + 4 * LQ);                            // [4 warps][32]
 
   const ScanArgs &a = L.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -855,10 +863,13 @@ __global__ void __launch_bounds__(L_NT, 1)
   cur.start(first, last);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < L_STG; s++) {
-      // B copies (one a thread) + (converter warps | A's TMA)
-      mbar_init(full + s, QUANT ? 32 * L_CW + L_CW : 32 * L_CW + 1);
+    for (int s = 0; s < STG; s++) {
+      mbar_init(full + s, QUANT ? L_CW : 1);   // converter warps | the A tile's TMA
       mbar_init(empty + s, 1);
+    }
+    for (int s = 0; s < BSTG; s++) {
+      mbar_init(bfull + s, 32);                // the gather warp's copies
+      mbar_init(bempty + s, 1);
     }
     for (int r = 0; r < RSTG; r++) {
       mbar_init(rawfull + r, 1);
@@ -885,9 +896,9 @@ __global__ void __launch_bounds__(L_NT, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // FP16: the row tile into the stage. Quantized: codes (+ scale box) into the raw ring.
+    // FP16: the row tile into the A stage. Quantized: codes (+ scale box) into the raw ring.
     if (lane == 0) {
-      constexpr int RING = QUANT ? L_RSTG : L_STG;
+      constexpr int RING = QUANT ? RSTG1 : STG;
       uint64_t *ring_full = QUANT ? rawfull : full;
       uint64_t *ring_empty = QUANT ? rawempty : empty;
       uint64_t it = 0;
@@ -908,7 +919,7 @@ __global__ void __launch_bounds__(L_NT, 1)
               tma_load_2d(smem_u32(dst + C::RAWB), &scales_map, (int32_t)((kb >> 2) * 16), arow, ring_full + s);
           } else {
             mbar_expect_tx(ring_full + s, (uint32_t)A_BYTES);
-            tma_load_2d(smem_u32(smem + s * L_STAGE), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+            tma_load_2d(smem_u32(smem + s * A_BYTES), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
           }
         }
       }
@@ -927,18 +938,20 @@ __global__ void __launch_bounds__(L_NT, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * LQ;
         for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % L_STG), ph = (uint32_t)((it / L_STG) & 1);
-          if (!mbar_wait(full + s, ph, abort, a.flags)) {
+          const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
+          const uint32_t sb = (uint32_t)(it % BSTG), phb = (uint32_t)((it / BSTG) & 1);
+          if (!mbar_wait(full + s, ph, abort, a.flags) || !mbar_wait(bfull + sb, phb, abort, a.flags)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * L_STAGE);
-          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sa = smem_u32(smem + s * A_BYTES);
+          const uint32_t sbq = smem_u32(btiles + sb * L_B);
 #pragma unroll
           for (uint32_t kk = 0; kk < 4; kk++)
-            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sbq + kk * 32), idesc, (kb | kk) != 0);
           tc_commit(empty + s);
+          tc_commit(bempty + sb);
         }
         if (ok) tc_commit(tfull + ab);
       }
@@ -948,52 +961,63 @@ __global__ void __launch_bounds__(L_NT, 1)
       }
     }
     __syncwarp();
-  } else if (warp >= 6) {
-    // ------------------------------------------------------------ query gather (+ conversion)
-    // B: the item's queries (row ct/8 of the tile, 16 bytes of the
-    // k-block a thread) by cp.async; rows past the group are zero-filled.
-    // Quantized formats: then the stage's codes into the FP16 A tile.
-    static_assert(L_CW == 8, "one B chunk a gather thread");
-    const uint32_t ct = threadIdx.x - 192;
-    const uint32_t c = ct & 7, rq = ct >> 3;
-    uint64_t it = 0;
-    bool ok = true;
-    uint64_t pf_qb = ~0ull;      // the next item's query number, requested one item ahead
+  } else if (warp == L_BW) {
+    // ------------------------------------------------------------ query gather
+    // Lane j copies query j of the item's group (its 128 bytes of the
+    // k-block) into the B ring by cp.async, up to BSTG k-blocks ahead of the
+    // MMAs; rows past the group are zero-filled.
+    uint64_t it = 0, pf_qb = ~0ull;
     uint32_t pf_q = 0;
+    bool ok = true;
     for (; cur.valid() && ok; cur.next()) {
       const uint32_t nqt = cur.nq_item();
       const uint64_t qb = cur.qbase();
-      const uint32_t n = rq < nqt ? 16u : 0u;
-      const uint32_t qn = rq < nqt ? (qb == pf_qb ? pf_q : L.p.qlist[qb + rq]) : 0u;
+      const uint32_t qn = (uint32_t)lane < nqt ? (qb == pf_qb ? pf_q : L.p.qlist[qb + lane]) : 0u;
+      const uint32_t n = (uint32_t)lane < nqt ? 16u : 0u;
       const __half *src = L.q16 + (uint64_t)qn * L.kpad;
       {
         uint64_t nqb;
         uint32_t nnqt;
         if (cur.peek_group(nqb, nnqt) && nqb != qb) {
           pf_qb = nqb;
-          pf_q = rq < nnqt ? L.p.qlist[nqb + rq] : 0u;
+          pf_q = (uint32_t)lane < nnqt ? L.p.qlist[nqb + lane] : 0u;
         }
       }
       for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
-        const uint32_t s = (uint32_t)(it % L_STG), ph = (uint32_t)((it / L_STG) & 1);
-        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        const uint32_t sb = (uint32_t)(it % BSTG), ph = (uint32_t)((it / BSTG) & 1);
+        const bool got = mbar_wait(bempty + sb, ph ^ 1, abort, a.flags);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        uint8_t *stage = smem + s * L_STAGE;
-        cp_async16(smem_u32(stage + A_BYTES) + sw128_offset(rq, c), src + kb * 64 + c * 8, n);
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(full + s)) : "memory");
-        if (QUANT) {
-          const uint32_t r = (uint32_t)(it % L_RSTG), rph = (uint32_t)((it / L_RSTG) & 1);
-          got = mbar_wait(rawfull + r, rph, abort, a.flags);
+        const uint32_t dst = smem_u32(btiles + sb * L_B);
+#pragma unroll
+        for (uint32_t c = 0; c < 8; c++) cp_async16(dst + sw128_offset(lane, c), src + kb * 64 + c * 8, n);
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bfull + sb)) : "memory");
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ converters (quantized formats)
+    if (QUANT) {
+      const uint32_t ct = threadIdx.x - 192;
+      uint64_t it = 0;
+      bool ok = true;
+      for (; cur.valid() && ok; cur.next()) {
+        for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
+          const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
+          const uint32_t r = (uint32_t)(it % RSTG1), rph = (uint32_t)((it / RSTG1) & 1);
+          bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+          if (got) got = mbar_wait(rawfull + r, rph, abort, a.flags);
           if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
           }
           const uint8_t *rs = raw + r * RAWB;
-          if (Q == DT_NVFP4) convert_nvfp4_box<32 * L_CW>(rs, rs + C::RAWB, stage, ct, kb);
-          else convert_e4m3<32 * L_CW>(rs, stage, ct);
+          uint8_t *atile = smem + s * A_BYTES;
+          if (Q == DT_NVFP4) convert_nvfp4_box<32 * L_CW>(rs, rs + C::RAWB, atile, ct, kb);
+          else convert_e4m3<32 * L_CW>(rs, atile, ct);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
@@ -1003,7 +1027,6 @@ __global__ void __launch_bounds__(L_NT, 1)
         }
       }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -1156,8 +1179,8 @@ cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_ma
 
 template <int Q>
 size_t tc_scan_lists_smem() {
-  constexpr int RAWB = LCfg<Q>::RAWB + LCfg<Q>::SCB;
-  return 1024 + (size_t)LCfg<Q>::STG * L_STAGE + (size_t)LCfg<Q>::RSTG * RAWB + 512 +
+  using C = LCfg<Q>;
+  return 1024 + (size_t)C::STG * A_BYTES + (size_t)C::BSTG * L_B + (size_t)C::RSTG * (C::RAWB + C::SCB) + L_BAR +
          4 * EPI_BUF * sizeof(uint4) + 2 * 4 * LQ * sizeof(uint32_t);
 }
 
