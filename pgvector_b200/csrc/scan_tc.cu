@@ -655,9 +655,9 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 // The list gather of ivf.cu on tcgen05: a work item is a 128-row tile of a
 // probed list x up to 32 of the queries that probe the list (ListPlan with
 // bm = 128, bq = 32). The rows of a list are contiguous in the shard, so the
-// tile is one TMA box -- FP16 rows straight into the A tile, E4M3 / NVFP4
-// codes (and NVFP4's block scales, 16 bytes a row covering four k-blocks)
-// into a raw ring the converter warps turn into FP16. The group's queries
+// tile is one TMA box a k-block -- FP16 rows straight into the A tile, E4M3 /
+// NVFP4 codes 128 bytes of each row at a time (and NVFP4's block scales for
+// those bytes) into a raw ring the converter warps turn into FP16. The group's queries
 // are gathered from the FP16 query copy by cp.async into a 32-row B tile.
 // One M=128, N=32 accumulator an item, double buffered (64 TMEM columns).
 // Each CTA walks a contiguous run of items and decodes them incrementally,
@@ -671,17 +671,22 @@ constexpr int L_TMEM = 64;
 constexpr int L_BAR = 1024;                  // barrier region bytes
 
 // STG A stages (converted FP16 row tiles); BSTG query tiles, gathered up to
-// BSTG k-blocks ahead so their L2 latency stays hidden; RSTG raw stages of
-// codes in flight from HBM (quantized formats).
+// BSTG k-blocks ahead so their L2 latency stays hidden; RSTG raw segments of
+// codes in flight from HBM (quantized formats). A raw segment is 128 bytes
+// of each of the tile's 128 rows (one TMA box, 128-byte swizzle) and covers
+// SEGK k-blocks; NVFP4 adds the 16 block-scale bytes of those k-blocks
+// (SCB). Whole 128-byte row pieces keep the TMA request count per byte low:
+// 32-byte boxes a k-block cost four times the requests and left the copy
+// engine, not HBM, the limit.
 template <int Q> struct LCfg;
 template <> struct LCfg<DT_F16> {
-  static constexpr int STG = 8, BSTG = 16, RSTG = 0, RAWB = 0, RAW_X = 0, SCB = 0;
+  static constexpr int STG = 8, BSTG = 16, RSTG = 0, RAWB = 0, SEGK = 1, SCB = 0;
 };
 template <> struct LCfg<DT_E4M3> {
-  static constexpr int STG = 4, BSTG = 16, RSTG = 9, RAWB = BM * 64, RAW_X = 64, SCB = 0;
+  static constexpr int STG = 4, BSTG = 16, RSTG = 4, RAWB = BM * 128, SEGK = 2, SCB = 0;
 };
 template <> struct LCfg<DT_NVFP4> {
-  static constexpr int STG = 4, BSTG = 16, RSTG = 12, RAWB = BM * 32, RAW_X = 32, SCB = BM * 16;
+  static constexpr int STG = 4, BSTG = 16, RSTG = 4, RAWB = BM * 128, SEGK = 4, SCB = BM * 16;
 };
 
 struct ListTcArgs {
@@ -780,21 +785,24 @@ struct ItemCursor {
   }
 };
 
-// NVFP4 rows of one stage: codes (128 rows x 32 bytes) and the rows' block
-// scales for this k-block's four blocks (at byte (kb % 4) * 4 of each row's
-// 16-byte scale box) -> FP16 A tile of raw values (row scale in the epilogue).
-// nth converter threads, ct the thread's index.
+// NVFP4 k-block q of a raw segment: codes (128 rows x 128 bytes, 128-byte
+// swizzle; the k-block is 16-byte chunks 2q and 2q+1 of each row) and the
+// rows' block scales (16 bytes a row, the k-block's four at byte 4q) -> FP16
+// A tile of raw values (row scale in the epilogue). nth converter threads, ct
+// the thread's index. Unit i is row r, half h with the eight lanes of a
+// quarter warp on eight consecutive rows, so the swizzle spreads their 16-byte
+// reads over all banks.
 template <int NTH>
-__device__ __forceinline__ void convert_nvfp4_box(const uint8_t *raw, const uint8_t *sbox, uint8_t *atile,
-                                                  uint32_t ct, uint32_t kb) {
+__device__ __forceinline__ void convert_nvfp4_seg(const uint8_t *raw, const uint8_t *sbox, uint8_t *atile,
+                                                  uint32_t ct, uint32_t q) {
 #pragma unroll
   for (int u = 0; u < 256 / NTH; u++) {
-    const uint32_t i = ct + NTH * u, r = i >> 1, h = i & 1;  // 32 nibbles: dims 32h .. 32h+31
-    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+    const uint32_t i = ct + NTH * u, h = (i >> 3) & 1, r = (i & 7) | ((i >> 4) << 3);  // dims 32h .. 32h+31
+    const uint4 w = *reinterpret_cast<const uint4 *>(raw + sw128_offset(r, 2 * q + h));
     uint32_t sc[2];
 #pragma unroll
     for (int j = 0; j < 2; j++) {
-      const uint32_t code = sbox[r * 16 + (kb & 3) * 4 + h * 2 + j];
+      const uint32_t code = sbox[r * 16 + q * 4 + h * 2 + j];
       uint32_t pair, unused;
       e4m3x4_to_f16(code | (code << 8), pair, unused);
       sc[j] = pair;
@@ -809,13 +817,15 @@ __device__ __forceinline__ void convert_nvfp4_box(const uint8_t *raw, const uint
   }
 }
 
-// E4M3 rows of one stage (128 rows x 64 codes) -> FP16 A tile of raw values.
+// E4M3 k-block q of a raw segment (128 rows x 128 codes, 128-byte swizzle;
+// the k-block is chunks 4q .. 4q+3) -> FP16 A tile of raw values. Unit i is
+// row r, chunk c, a quarter warp on eight consecutive rows.
 template <int NTH>
-__device__ __forceinline__ void convert_e4m3(const uint8_t *raw, uint8_t *atile, uint32_t ct) {
+__device__ __forceinline__ void convert_e4m3_seg(const uint8_t *raw, uint8_t *atile, uint32_t ct, uint32_t q) {
 #pragma unroll
   for (int u = 0; u < 512 / NTH; u++) {
-    const uint32_t i = ct + NTH * u, r = i >> 2, c = i & 3;  // 16 codes: dims 16c .. 16c+15
-    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + c * 16);
+    const uint32_t i = ct + NTH * u, c = (i >> 3) & 3, r = (i & 7) | ((i >> 5) << 3);  // dims 16c .. 16c+15
+    const uint4 w = *reinterpret_cast<const uint4 *>(raw + sw128_offset(r, 4 * q + c));
     uint4 lo, hi;
     e4m3x4_to_f16(w.x, lo.x, lo.y);
     e4m3x4_to_f16(w.y, lo.z, lo.w);
@@ -896,16 +906,19 @@ __global__ void __launch_bounds__(L_NT, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // FP16: the row tile into the A stage. Quantized: codes (+ scale box) into the raw ring.
+    // FP16: the row tile a k-block into the A stage. Quantized: a raw
+    // segment (128 bytes of every row, SEGK k-blocks, + NVFP4 scale box)
+    // into the raw ring.
     if (lane == 0) {
       constexpr int RING = QUANT ? RSTG1 : STG;
       uint64_t *ring_full = QUANT ? rawfull : full;
       uint64_t *ring_empty = QUANT ? rawempty : empty;
+      const uint32_t steps = QUANT ? (L.kblocks + C::SEGK - 1) / C::SEGK : L.kblocks;
       uint64_t it = 0;
       bool ok = true;
       for (; cur.valid() && ok; cur.next()) {
         const int32_t arow = (int32_t)cur.row0();
-        for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
+        for (uint32_t kb = 0; kb < steps; kb++, it++) {
           const uint32_t s = (uint32_t)(it % RING), ph = (uint32_t)((it / RING) & 1);
           if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags)) {
             ok = false;
@@ -914,9 +927,9 @@ __global__ void __launch_bounds__(L_NT, 1)
           if (QUANT) {
             mbar_expect_tx(ring_full + s, (uint32_t)RAWB);
             uint8_t *dst = raw + s * RAWB;
-            tma_load_2d(smem_u32(dst), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
+            tma_load_2d(smem_u32(dst), &rows_map, (int32_t)(kb * 128), arow, ring_full + s);
             if (C::SCB)
-              tma_load_2d(smem_u32(dst + C::RAWB), &scales_map, (int32_t)((kb >> 2) * 16), arow, ring_full + s);
+              tma_load_2d(smem_u32(dst + C::RAWB), &scales_map, (int32_t)(kb * 16), arow, ring_full + s);
           } else {
             mbar_expect_tx(ring_full + s, (uint32_t)A_BYTES);
             tma_load_2d(smem_u32(smem + s * A_BYTES), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
@@ -1002,12 +1015,14 @@ __global__ void __launch_bounds__(L_NT, 1)
     // ------------------------------------------------------------ converters (quantized formats)
     if (QUANT) {
       const uint32_t ct = threadIdx.x - 192;
-      uint64_t it = 0;
+      uint64_t it = 0, seg = 0;   // A stages, raw segments
       bool ok = true;
       for (; cur.valid() && ok; cur.next()) {
         for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
           const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
-          const uint32_t r = (uint32_t)(it % RSTG1), rph = (uint32_t)((it / RSTG1) & 1);
+          const uint32_t r = (uint32_t)(seg % RSTG1), rph = (uint32_t)((seg / RSTG1) & 1);
+          const uint32_t q = kb % C::SEGK;
+          const bool seg_end = q == C::SEGK - 1 || kb + 1 == L.kblocks;
           bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
           if (got) got = mbar_wait(rawfull + r, rph, abort, a.flags);
           if (!__all_sync(0xffffffffu, got)) {
@@ -1016,14 +1031,15 @@ __global__ void __launch_bounds__(L_NT, 1)
           }
           const uint8_t *rs = raw + r * RAWB;
           uint8_t *atile = smem + s * A_BYTES;
-          if (Q == DT_NVFP4) convert_nvfp4_box<32 * L_CW>(rs, rs + C::RAWB, atile, ct, kb);
-          else convert_e4m3<32 * L_CW>(rs, atile, ct);
+          if (Q == DT_NVFP4) convert_nvfp4_seg<32 * L_CW>(rs, rs + C::RAWB, atile, ct, q);
+          else convert_e4m3_seg<32 * L_CW>(rs, atile, ct, q);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(rawempty + r);
+            if (seg_end) mbar_arrive(rawempty + r);
             mbar_arrive(full + s);
           }
+          seg += seg_end;
         }
       }
     }
@@ -1229,9 +1245,10 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
 
 // The IVF list scan on tensor cores over the items launch_list_items counted
 // with p.bm = 128 and p.bq = 32 (rows [rbegin, rend) of every probed list).
-// rows_map: the shard's rows as launch_tc_scan reads contiguous runs of them;
-// scales_map (NVFP4 only): the block scales [rows][bblocks] as bytes, box 16 x
-// 128. q16: the FP16 queries [.][kpad] prep_queries wrote.
+// rows_map: FP16 rows as launch_tc_scan reads contiguous runs of them
+// (box 64 x 128, 128-byte swizzle), or the E4M3 / NVFP4 codes as bytes in
+// boxes of 128 x 128 with the 128-byte swizzle; scales_map (NVFP4 only): the
+// block scales [rows][bblocks] as bytes, box 16 x 128. q16: the FP16 queries [.][kpad] prep_queries wrote.
 cudaError_t launch_tc_scan_lists(const ScanArgs &a, const ListPlan &p, uint64_t rbegin, uint64_t rend,
                                  const CUtensorMap &rows_map, const CUtensorMap &scales_map, const __half *q16,
                                  uint32_t kpad, int sms, cudaStream_t st) {

@@ -215,6 +215,21 @@ bool encode_u8_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Raw codes [outer][inner bytes] in boxes of 128 bytes x 128 rows with the
+// 128-byte swizzle (the IVF tensor scan's raw segments); bytes past `inner`
+// read as zero.
+bool encode_u8_seg_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Formats the tensor scan reads (row pitch a multiple of 16 bytes, as TMA
 // needs): FP16 rows, and E4M3 / NVFP4 codes converted to FP16 on chip.
 bool tc_format(uint32_t dtype, uint32_t dims, uint64_t row_bytes) {
@@ -275,6 +290,8 @@ struct AnnB200Shard {
   bool rows_map_ok = false;
   CUtensorMap scales_map;      // NVFP4 block scales [rows][bblocks], box 16 x 128 (IVF tensor scan)
   bool scales_map_ok = false;
+  CUtensorMap seg_map;         // E4M3 / NVFP4 codes, 128-byte swizzled boxes 128 x 128 (IVF tensor scan)
+  bool seg_map_ok = false;
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
@@ -400,6 +417,10 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   // k-blocks) a row a box, so the scale pitch must be a multiple of 16
   s->scales_map_ok = s->rows_map_ok && dtype == DT_NVFP4 && v.bblocks % 16 == 0 &&
                      encode_u8_map(&s->scales_map, v.bscales, v.bblocks, rows, v.bblocks, 16);
+  // and quantized codes in 128-byte row pieces (128 bytes = 2 E4M3 / 4 NVFP4 k-blocks)
+  s->seg_map_ok = s->rows_map_ok && (dtype == DT_E4M3 || dtype == DT_NVFP4) &&
+                  encode_u8_seg_map(&s->seg_map, v.codes, dtype == DT_E4M3 ? dims : (dims + 1) / 2, rows,
+                                    v.row_bytes);
   return OK;
 }
 
@@ -781,7 +802,7 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   const ShardView &v = sh->view;
   // tensor cores when the rows can be read by TMA (and NVFP4's scales too)
   const bool tc = !(flags & ANNB200_FORCE_SIMT) && sh->rows_map_ok &&
-                  (v.dtype != DT_NVFP4 || sh->scales_map_ok);
+                  (v.dtype == DT_F16 || sh->seg_map_ok) && (v.dtype != DT_NVFP4 || sh->scales_map_ok);
   const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
   const double gamma = scan_gamma(false, tc, kpad, v.dims);
   const uint64_t S = std::max<uint64_t>(64, ((uint64_t)k + 63) / 64 * 64);
@@ -880,7 +901,9 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
     int hk = clock.begin(stage);
     launch_list_items(p, rbegin, rend, st);
     cudaError_t e = cudaSuccess;
-    if (tc) e = launch_tc_scan_lists(a, p, rbegin, rend, sh->rows_map, sh->scales_map, qs.q16, kpad, sh->sms, st);
+    if (tc)
+      e = launch_tc_scan_lists(a, p, rbegin, rend, v.dtype == DT_F16 ? sh->rows_map : sh->seg_map, sh->scales_map,
+                               qs.q16, kpad, sh->sms, st);
     else launch_simt_scan_lists(p, rbegin, rend, a, sh->sms, st);
     clock.end(hk);
     counted((nlists ? 1 : 0) + list_plan_scan_launches(nlists) + 1 +
