@@ -13,11 +13,14 @@ rescoring), and with N GPUs the corpus is row-sharded: every rank scans its
 rows, the per-rank top-k lists are all-gathered over NCCL and merged on the
 device (strong scaling: the corpus is fixed, N GPUs share it).
 
---config 3 / 4 measure the other GPU-sized configurations the same way (not
-the headline line): 3 = inner product over FP8-E4M3 rows with row scales,
-d=1024, N=100M from a 4,096-centre mixture, batch 1,024, k=500, no filter;
-4 = IVF list gather over NVFP4 rows, d=768, N=200M in 65,536 lists with
-Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, lists sharded by rank.
+--config 3 / 4 / 5 measure the other GPU-sized configurations the same way
+(not the headline line): 3 = inner product over FP8-E4M3 rows with row
+scales, d=1024, N=100M from a 4,096-centre mixture, batch 1,024, k=500, no
+filter; 4 = IVF list gather over NVFP4 rows, d=768, N=200M in 65,536 lists
+with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, lists sharded by
+rank; 5 = Hamming over 1,024-bit rows, N=1B (128 GB: one B200 holds it)
+XOR-perturbed from 65,536 random prototypes at a 5% flip rate, batch 1,024,
+k=100, row-sharded.
 
   value  queries/s with inputs resident in HBM (CUDA events, max over ranks)
   e2e    the same through the public API with pinned host buffers: queries
@@ -49,19 +52,22 @@ WORKLOADS = {
        '4,096-centre Gaussian mixture, batch 1,024, k=500, row-sharded',
     4: 'config 4: IVF gather-scan, NVFP4 (e2m1 + E4M3 scale per 16 + row scale), d=768, N=200M in 65,536 '
        'lists with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, sharded by list',
+    5: 'config 5: Hamming kNN on 1,024-bit vectors, N=1B rows XOR-perturbed from 65,536 Bernoulli(0.5) '
+       'prototypes at a 5% flip rate, batch 1,024, k=100, row-sharded; integer distances, ties by row id',
 }
 DEFAULTS = {2: dict(rows=10_000_000, dims=768, batch=1024, k=100, centres=1000),
             3: dict(rows=100_000_000, dims=1024, batch=1024, k=500, centres=4096),
-            4: dict(rows=200_000_000, dims=768, batch=4096, k=100, centres=65536)}
+            4: dict(rows=200_000_000, dims=768, batch=4096, k=100, centres=65536),
+            5: dict(rows=1_000_000_000, dims=1024, batch=1024, k=100, centres=65536)}
 
 
 def args_parse():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=None, help='timed steps (default 300; 10 for configs 3/4)')
+    ap.add_argument('--steps', type=int, default=None, help='timed steps (default 300; 10 for configs 3/4, 5 for 5)')
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4])
+    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument('--rows', type=int, default=None)
     ap.add_argument('--dims', type=int, default=None)
     ap.add_argument('--batch', type=int, default=None)
@@ -79,7 +85,7 @@ def args_parse():
         if getattr(args, key) is None:
             setattr(args, key, val)
     if args.steps is None:
-        args.steps = 300 if args.config == 2 else 10
+        args.steps = {2: 300, 5: 5}.get(args.config, 10)
     return args
 
 
@@ -150,16 +156,21 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU baseline (reference worker code)
 
-METRIC_CODE = {2: 2, 3: 1, 4: 0}   # cosine, inner product, L2
+METRIC_CODE = {2: 2, 3: 1, 4: 0, 5: 3}   # cosine, inner product, L2, Hamming
 
 
 def cpu_sample(args, rows, queries):
     """A bounded host sample of the workload's distribution: `rows` rows
-    decoded to FP32 exactly as the device format stores them, and `queries`
-    queries (numpy, same mixture)."""
+    decoded to FP32 exactly as the device format stores them (config 5: the
+    bit rows themselves), and `queries` queries (numpy, same mixture)."""
     import numpy as np
     import oracle
     from pgvector_b200 import synth
+    if args.config == 5:
+        x, proto = synth.bit_rows(rows, args.dims, args.centres, flip=0.05, seed=args.seed)
+        rng = np.random.default_rng(args.seed + 7919)
+        flips = np.packbits(rng.random((queries, args.dims)) < 0.05, axis=1, bitorder='little')
+        return x, proto[rng.integers(0, args.centres, queries)] ^ flips
     if args.config == 2:
         x = synth.mixture(rows, args.dims, args.centres, seed=args.seed, normalize=True).astype(np.float16)
         q = synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed, normalize=True)
@@ -180,8 +191,13 @@ def cpu_run(x, q, k, threads, metric, budget_s=None, count=None):
     import oracle
     kind = 'reference' if oracle.ref_available() else 'port'
 
+    if metric == 3:       # bit vectors: no worker entry point scores them; the oracle's restatement
+        kind = 'port'
+
     def one(i):
-        if kind == 'reference':
+        if metric == 3:
+            oracle.search(oracle.BIT, x.shape[1] * 8, x, q[i % len(q)][None], k, metric, threads=1)
+        elif kind == 'reference':
             oracle.ref_gathered_exact(q[i % len(q)], x, k, metric)
         else:
             oracle.search(oracle.F32, x.shape[1], x, q[i % len(q)][None], k, metric, window=True, threads=1)
@@ -245,7 +261,7 @@ def cpu_measure(args, threads, budget_s=None, count=None):
                 'the per-query work equals the full configuration\'s' %
                 (done, args.k, args.nprobe, rows // max(1, len(sample[3]) - 1), secs, threads))
         return done / secs, desc, kind
-    rows = 50_000 if args.config == 2 else 20_000
+    rows = {2: 50_000, 5: 200_000}.get(args.config, 20_000)
     if args.config not in _SAMPLES:
         _SAMPLES[args.config] = cpu_sample(args, rows, 64)
     x, q = _SAMPLES[args.config]
@@ -300,6 +316,7 @@ class Workload:
     dtype = 'f16'
     kernel = ''
     bound = 'tensor'
+    ops = 'f16'         # tensor-core operand type of the dominant kernel
 
     def step(self, *inputs):
         raise NotImplementedError
@@ -516,6 +533,56 @@ def build_config4(args, rank, world, dev):
     return w
 
 
+def build_config5(args, rank, world, dev):
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import sharded
+    w = Workload()
+    bounds = sharded.shard_bounds(args.rows, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    nb = args.dims // 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    proto = torch.randint(0, 256, (args.centres, nb), generator=g, device=dev, dtype=torch.uint8)
+    weights = torch.tensor([1, 2, 4, 8, 16, 32, 64, 128], dtype=torch.int32, device=dev)   # bit i of a byte
+
+    def perturbed(m, gen):
+        # prototype rows XOR Bernoulli(0.05) bits, packed least significant bit first
+        lab = torch.randint(0, args.centres, (m,), generator=gen, device=dev)
+        flips = torch.rand((m, nb, 8), generator=gen, device=dev) < 0.05
+        return proto[lab] ^ (flips.to(torch.int32) * weights).sum(dim=2).to(torch.uint8)
+    codes = torch.empty((hi - lo, nb), dtype=torch.uint8, device=dev)
+    chunk = 1 << 18
+    for c0 in range(lo // chunk * chunk, hi, chunk):      # per-chunk seeds: every rank draws the same rows
+        g.manual_seed(args.seed * 1000003 + c0 // chunk)
+        m = min(chunk, args.rows - c0)
+        v = perturbed(m, g)
+        a, b = max(c0, lo), min(c0 + m, hi)
+        codes[a - lo:b - lo] = v[a - c0:b - c0]
+        del v
+    g.manual_seed(args.seed + 7919)
+    queries = perturbed(args.batch, g).contiguous()
+    w.inputs = [queries]
+    w.shard = pb.Shard(pb.BIT, args.dims, codes, first_id=lo)
+    w.metric, w.dtype = pb.HAMMING, 'bit->int8 (+-1), s32 accumulate'
+    w.kernel = 'tc_scan<BIT> (kind::i8), filter pass'
+    w.data = ('synthetic (seeded: 65,536 uniform random 1,024-bit prototypes, rows = prototype XOR Bernoulli(0.05) '
+              'bits, generated on the GPU)')
+    w.row_bytes = nb
+    w.profile = 'tc_scan_bit_config5.md'
+    w.ops = 'int8'
+
+    def step(q):
+        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.HAMMING, None)
+        return d, i, c, hi - lo
+    w.step = step
+
+    def verify(result, nq):
+        return verify_by_rescoring(args, w, result, nq, codes, None, None, oracle_dtype=4, lo=lo, hi=hi)
+    w.verify = verify
+    return w
+
+
 def verify_by_rescoring(args, w, result, nq, codes, bscales, rscales, oracle_dtype, lo, hi):
     """Size-independent check for shards too large for the oracle: the
     returned rows' distances recomputed by the oracle equal the returned
@@ -537,7 +604,7 @@ def verify_by_rescoring(args, w, result, nq, codes, bscales, rscales, oracle_dty
         rt = torch.from_numpy(rows).to(codes.device)
         sub = codes[rt].cpu().numpy()
         bs = None if bscales is None else bscales[rt].cpu().numpy()
-        rs = rscales[rt].cpu().numpy()
+        rs = None if rscales is None else rscales[rt].cpu().numpy()
         od, oi, oc, _ = oracle.search(oracle_dtype, args.dims, sub, q, len(rows), w.metric, block_scales=bs,
                                       row_scales=rs)
         exact = dict(zip(rows[oi[0][:oc[0]]].tolist(), od[0][:oc[0]].tolist()))
@@ -570,7 +637,7 @@ def main():
     if world > 1:
         dist.init_process_group('nccl', timeout=timedelta(seconds=180), device_id=dev)
     lib = pb.load()
-    w = {2: build_config2, 3: build_config3, 4: build_config4}[args.config](args, rank, world, dev)
+    w = {2: build_config2, 3: build_config3, 4: build_config4, 5: build_config5}[args.config](args, rank, world, dev)
     torch.cuda.synchronize()
 
     def barrier():
@@ -654,7 +721,7 @@ def main():
         flops, bytes_alg = w.pass_flops, w.pass_rows * (w.row_bytes - 4) + args.batch * args.dims * 4
     else:
         flops = 2.0 * args.batch * nrows_local * args.dims
-        bytes_alg = nrows_local * w.row_bytes + args.batch * args.dims * 2
+        bytes_alg = nrows_local * w.row_bytes + args.batch * args.dims * (1 if w.ops == 'int8' else 2)
     achieved_tf = flops / (pass_ms * 1e-3) / 1e12
     hbm_gbs = bytes_alg / (pass_ms * 1e-3) / 1e9
     traffic = None
@@ -667,7 +734,14 @@ def main():
     common = {'kernel': '%s (%d launches a step)' % (w.kernel, round(stage_calls[3] / args.steps)),
               'pass_ms': pass_ms, 'flops_per_pass': flops, 'algorithmic_bytes_per_pass': bytes_alg,
               'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(stage_names)}}
-    if w.bound == 'tensor':
+    if w.bound == 'tensor' and w.ops == 'int8':
+        # dense int8 runs at twice the bf16 rate on B200: the measured
+        # sustained bf16 figure doubled is the denominator
+        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': 2 * tf_sust, 'unit': 'TOP/s (int8)',
+                    'frac': achieved_tf / (2 * tf_sust), 'traffic': traffic,
+                    'peak_source': kind + ' bf16_tflops_sustained x 2 (int8 dense rate)',
+                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
+    elif w.bound == 'tensor':
         roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
                     'frac': achieved_tf / tf_sust, 'traffic': traffic,
                     'peak_source': kind + ' bf16_tflops_sustained',

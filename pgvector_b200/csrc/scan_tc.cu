@@ -57,8 +57,8 @@ constexpr unsigned long long kWaitNs = 4000000000ull;
 struct TcArgs {
   ScanArgs a;
   int64_t a_row0;      // row of the A tensor map holding virtual row 0
-  uint32_t kpad;       // halves per query row, multiple of 64
-  uint32_t kblocks;    // kpad / 64
+  uint32_t kpad;       // elements per query row: halves (multiple of 64) or, bit vectors, int8 (of 128)
+  uint32_t kblocks;    // 128-byte k-blocks a row: kpad / 64, or kpad / 128 for bit vectors
   uint32_t bn;         // queries per tile, multiple of 32, <= 256
   uint32_t qtiles;
   uint64_t rtiles;
@@ -141,6 +141,16 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
       : "memory");
 }
 
+// Signed 8-bit A and B, 32-bit integer accumulator (the +-1 expansion of bit vectors).
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor of a K-major operand tile in the 128-byte
 // swizzle layout: rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked
 // along M/N (stride byte offset 1024), start address advanced 32 bytes per
@@ -156,6 +166,13 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // Instruction descriptor: FP16 A and B, FP32 accumulator, both K-major.
 __device__ __forceinline__ uint32_t f16_idesc(uint32_t n) {
   return (1u << 4)                  // D format F32
+         | ((n >> 3) << 17)         // N / 8
+         | ((uint32_t)(BM >> 4) << 24);  // M / 16
+}
+// kind::i8: signed 8-bit A and B (both the same type), S32 accumulator, both K-major.
+__device__ __forceinline__ uint32_t i8_idesc(uint32_t n) {
+  return (2u << 4)                  // D format S32
+         | (1u << 7) | (1u << 10)   // A, B signed 8-bit
          | ((n >> 3) << 17)         // N / 8
          | ((uint32_t)(BM >> 4) << 24);  // M / 16
 }
@@ -207,12 +224,23 @@ struct Appender {
   }
 };
 
+// Score of an accumulator word: the FP32 dot product, or for bit vectors
+// (nbits bits a row, +-1 expansion, S32 dot product d) the Hamming distance
+// (nbits - d) / 2, exact in FP32.
+template <int Q>
+__device__ __forceinline__ float acc_score(uint32_t r, int32_t nbits) {
+  if (Q == DT_BIT) return (float)(nbits - (int32_t)r) * 0.5f;
+  return __uint_as_float(r);
+}
+
 // One warp's 32 accumulator rows (TMEM lanes at taddr; this lane's virtual
 // row vi) against queries q_base .. q_base+bn-1: the score matrix, or the
 // threshold filter -- the 32 compares of a column chunk form a bitmask first
 // and only a chunk with a passing score in the warp takes the staging path.
+template <int Q>
 __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr, uint64_t vi, uint32_t q_base,
                                               uint32_t bn, const float *thr_s, Appender &app) {
+  const int32_t nbits = (int32_t)(a.s.row_bytes * 8);
   const bool valid = vi < a.count;
   const uint64_t pos = a.base + vi * a.stride;
   float al = 0.0f, be = __int_as_float(0x7fc00000);  // invalid rows score NaN: never pass
@@ -229,7 +257,7 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
       if (valid) {
 #pragma unroll
         for (int j = 0; j < 32; j++)
-          if (q0 + j < a.nq) a.mat[(uint64_t)(q0 + j) * a.mat_ld + vi] = fmaf(__uint_as_float(r[j]), al, be);
+          if (q0 + j < a.nq) a.mat[(uint64_t)(q0 + j) * a.mat_ld + vi] = fmaf(acc_score<Q>(r[j], nbits), al, be);
       }
     } else {
       const float4 *tq = reinterpret_cast<const float4 *>(thr_s + q0);
@@ -240,7 +268,7 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
         const float th[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
         for (int jj = 0; jj < 4; jj++)
-          m |= (uint32_t)(fmaf(__uint_as_float(r[j4 * 4 + jj]), al, be) <= th[jj]) << (j4 * 4 + jj);
+          m |= (uint32_t)(fmaf(acc_score<Q>(r[j4 * 4 + jj], nbits), al, be) <= th[jj]) << (j4 * 4 + jj);
       }
       // rare path: each round every lane stages its lowest passing column
       while (__any_sync(0xffffffffu, m != 0)) {
@@ -249,7 +277,7 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
         m &= m - 1;
         float v = 0.0f;
 #pragma unroll
-        for (int jj = 0; jj < 32; jj++) v = (jj == j) ? __uint_as_float(r[jj]) : v;
+        for (int jj = 0; jj < 32; jj++) v = (jj == j) ? acc_score<Q>(r[jj], nbits) : v;
         v = fmaf(v, al, be);
         const uint32_t ballot = __ballot_sync(0xffffffffu, has);
         if (app.n + 32 > (uint32_t)EPI_BUF) app.flush();
@@ -277,6 +305,10 @@ template <> struct TcCfg<DT_E4M3> {   // 64 one-byte codes a row a k-block
 };
 template <> struct TcCfg<DT_NVFP4> {  // 64 nibbles (32 bytes) a row a k-block
   static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 320;
+  static constexpr int RING = STG * STAGE_BYTES;
+};
+template <> struct TcCfg<DT_BIT> {    // 128 bits (16 bytes) a row a k-block -> 128 int8
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 16, RAW_X = 16, NT = 320;
   static constexpr int RING = STG * STAGE_BYTES;
 };
 // FP16 rows named by a candidate list (or a strided sample): 4 gather warps
@@ -367,6 +399,25 @@ __device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *
         *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
+  } else if (Q == DT_BIT) {
+    // 128 bits a row -> 128 int8: bit b of the k-block's 16 bytes (byte b/8,
+    // bit b%8 from the least significant) is element b, +1 if clear, -1 if
+    // set. A nibble times 0x00204081 puts its bit i at bit 8i (the other
+    // products land at positions that are not multiples of 8, with no
+    // carries), so each nibble becomes four bytes of 0 / 1, then of 1 / -1.
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const uint32_t i = ct + 128 * u, r = i >> 2, w = i & 3;  // bits 32w .. 32w+31
+      const uint32_t x = *reinterpret_cast<const uint32_t *>(raw + r * 16 + w * 4);
+      uint32_t o[8];
+#pragma unroll
+      for (int n = 0; n < 8; n++) {
+        const uint32_t m = (((x >> (4 * n)) & 0xfu) * 0x00204081u) & 0x01010101u;
+        o[n] = (m * 0xffu) | 0x01010101u;
+      }
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * w)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * w + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
   }
 }
 
@@ -390,8 +441,9 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   using C = TcCfg<Q>;
   constexpr int STG = C::STG, BSTG = C::BSTG, RSTG = C::RSTG, RAWB = C::RAWB;
   constexpr int RSTG1 = RSTG > 0 ? RSTG : 1;  // (the FP16 kernels have no raw ring)
-  constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4;
+  constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4 || Q == DT_BIT;
   constexpr bool GATHER = Q == GF16;
+  constexpr int32_t QX = Q == DT_BIT ? 128 : 64;   // query elements a k-block (128 bytes)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // A and B tiles of stage s (separate rings for the gathered kernel)
@@ -480,7 +532,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
             tma_load_2d(smem_u32(raw + s * RAWB), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
           } else {
             if (!GATHER) tma_load_2d(smem_u32(a_tile(s)), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
-            tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), ring_full + s);
+            tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * QX), (int32_t)(qt * t.bn), ring_full + s);
           }
           it++;
         }
@@ -491,7 +543,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = f16_idesc(t.bn);
+      const uint32_t idesc = Q == DT_BIT ? i8_idesc(t.bn) : f16_idesc(t.bn);
       uint64_t it = 0, tc = 0;
       bool ok = true;
       for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
@@ -514,8 +566,12 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           const uint32_t sa = smem_u32(a_tile(s));
           const uint32_t sb = smem_u32(b_tile(s_b));
 #pragma unroll
-          for (uint32_t kk = 0; kk < 4; kk++)
-            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+          for (uint32_t kk = 0; kk < 4; kk++) {   // K = 16 halves or 32 int8: 32 bytes an MMA
+            if (Q == DT_BIT)
+              tc_mma_i8(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+            else
+              tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+          }
           tc_commit(empty + s);
           if (GATHER) tc_commit(bempty + s_b);
         }
@@ -548,7 +604,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         }
         if (ct == 0) {
           mbar_expect_tx(bfull + s, t.bn * 128u);
-          tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * 64), (int32_t)(qt * t.bn), bfull + s);
+          tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * QX), (int32_t)(qt * t.bn), bfull + s);
           bissued = it + 1;
         }
         got = mbar_wait(rawfull + r, rph, abort, a.flags);
@@ -632,8 +688,8 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      epilogue_rows(a, tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16), rt * BM + quad * 32 + lane,
-                    qt * t.bn, t.bn, thr_s, app);
+      epilogue_rows<Q>(a, tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16), rt * BM + quad * 32 + lane,
+                       qt * t.bn, t.bn, thr_s, app);
       tc_fence_before();
       mbar_arrive(tempty + ab);
     }
@@ -1219,7 +1275,11 @@ cudaError_t launch_lists_t(const CUtensorMap &rows_map, const CUtensorMap &scale
 // E4M3 ([rows][dims] bytes, box 64 x 128) or NVFP4 shard ([rows][dims/2]
 // bytes, box 32 x 128), converted to FP16 in shared memory (a.raw_scale
 // must be set: scores are on the raw codes). query_map: the FP16 queries
-// ([qtiles*bn][kpad], box 64 x bn). The epilogue reads per-row norms and
+// ([qtiles*bn][kpad], box 64 x bn). Bit vectors ([rows][row_bytes], box 16
+// x 128, row_bytes a multiple of 16) are expanded to +-1 int8 on chip and
+// scored by kind::i8 MMAs against query_map = the int8 query expansion
+// ([qtiles*bn][kpad] bytes, box 128 x bn, 128-byte swizzle); their scores
+// are exact Hamming distances. The epilogue reads per-row norms and
 // scales through a.ids / a.base / a.stride. Returns a CUDA error from the
 // launch.
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
@@ -1228,7 +1288,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   t.a = a;
   t.a_row0 = a_row0;
   t.kpad = kpad;
-  t.kblocks = kpad / 64;
+  t.kblocks = a.s.dtype == DT_BIT ? kpad / 128 : kpad / 64;
   t.bn = bn;
   t.qtiles = (a.nq + bn - 1) / bn;
   t.rtiles = (a.count + BM - 1) / BM;
@@ -1239,6 +1299,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
                                       : launch_tc_t<DT_F16>(rows_map, query_map, t, sms, st);
     case DT_E4M3: return launch_tc_t<DT_E4M3>(rows_map, query_map, t, sms, st);
     case DT_NVFP4: return launch_tc_t<DT_NVFP4>(rows_map, query_map, t, sms, st);
+    case DT_BIT: return launch_tc_t<DT_BIT>(rows_map, query_map, t, sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -402,6 +402,20 @@ __global__ void prep_queries_bits(uint32_t nq, QueryState qs) {
   qs.status[q] = 0;
 }
 
+// Bit-vector queries -> the tensor scan's int8 block [q][kpad]: element b
+// (byte b/8 of the row, bit b%8 from the least significant) is -1 if the bit
+// is set, +1 if clear, 0 past the row's bytes -- the expansion the scan
+// applies to the rows, so the S32 dot product is nbits - 2 x Hamming.
+__global__ void expand_query_bits(const uint8_t *q, uint32_t row_bytes, uint32_t kpad, int8_t *out) {
+  const uint64_t qi = blockIdx.x;
+  for (uint32_t b = threadIdx.x; b < kpad; b += blockDim.x) {
+    const uint32_t byte = b >> 3;
+    int8_t v = 0;
+    if (byte < row_bytes) v = ((q[qi * row_bytes + byte] >> (b & 7)) & 1u) ? (int8_t)-1 : (int8_t)1;
+    out[qi * kpad + b] = v;
+  }
+}
+
 // Threshold for queries without a sample bound: +inf (everything eligible).
 __global__ void fill_thresholds(uint32_t nq, QueryState qs) {
   uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1061,6 +1075,9 @@ void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint3
                          uint32_t *flags, cudaStream_t st) {
   if (bits) {
     prep_queries_bits<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
+    if (use_q16 && nq)
+      expand_query_bits<<<nq, 256, 0, st>>>(reinterpret_cast<const uint8_t *>(queries), (dims + 7) / 8, kpad,
+                                            reinterpret_cast<int8_t *>(qs.q16));
     return;
   }
   PrepArgs p{queries, nq, dims, metric, kpad, use_q16, gamma, maxn2, qs, flags};

@@ -215,15 +215,16 @@ bool encode_u8_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Raw codes [outer][inner bytes] in boxes of 128 bytes x 128 rows with the
-// 128-byte swizzle (the IVF tensor scan's raw segments); bytes past `inner`
-// read as zero.
-bool encode_u8_seg_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch) {
+// A byte tensor [outer][inner] in boxes of 128 bytes x box_rows rows with
+// the 128-byte swizzle (the IVF tensor scan's raw segments, box_rows = 128;
+// the int8 query block of bit vectors); bytes past `inner` read as zero.
+bool encode_u8_seg_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                       uint32_t box_rows = 128) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {pitch};
-  cuuint32_t box[2] = {128, 128};
+  cuuint32_t box[2] = {128, box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -237,6 +238,7 @@ bool tc_format(uint32_t dtype, uint32_t dims, uint64_t row_bytes) {
     case DT_F16: return dims % 8 == 0;
     case DT_E4M3: return row_bytes % 16 == 0;
     case DT_NVFP4: return row_bytes % 16 == 0;
+    case DT_BIT: return row_bytes % 16 == 0;
     default: return false;
   }
 }
@@ -248,8 +250,23 @@ bool encode_rows_map(CUtensorMap *map, uint32_t dtype, const void *base, uint32_
     case DT_F16: return encode_f16_map(map, base, dims, rows, pitch, 128);
     case DT_E4M3: return encode_u8_map(map, base, dims, rows, pitch, 64);
     case DT_NVFP4: return encode_u8_map(map, base, (dims + 1) / 2, rows, pitch, 32);
+    case DT_BIT: return encode_u8_map(map, base, ((uint64_t)dims + 7) / 8, rows, pitch, 16);
     default: return false;
   }
+}
+
+// The tensor scan's query block: elements a query row (FP16 halves, a
+// multiple of 64; for bit vectors the +-1 int8 expansion of the row's bits,
+// a multiple of 128), bytes an element, and the block's tensor map
+// (128-byte boxes of bn rows, 128-byte swizzle) over nq_pad rows.
+uint32_t tc_kpad(const ShardView &v) {
+  return v.dtype == DT_BIT ? (uint32_t)((v.row_bytes * 8 + 127) / 128 * 128) : (v.dims + 63) / 64 * 64;
+}
+size_t tc_qelem(const ShardView &v) { return v.dtype == DT_BIT ? 1 : 2; }
+bool encode_query_map(CUtensorMap *map, const ShardView &v, const void *q, uint32_t kpad, uint32_t nq_pad,
+                      uint32_t bn) {
+  if (v.dtype == DT_BIT) return encode_u8_seg_map(map, q, kpad, nq_pad, kpad, bn);
+  return encode_f16_map(map, q, kpad, nq_pad, (uint64_t)kpad * 2, bn);
 }
 
 // Relative bound on the approximate dot product's accumulation error (times
@@ -494,7 +511,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const bool window = flags & ANNB200_WINDOW;
   const uint64_t n = rows ? nrows : v.rows;
   const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
-  const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
+  const uint32_t kpad = tc ? tc_kpad(v) : 0;
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
   const uint32_t nq_pad = qtiles * bn;
@@ -535,7 +552,9 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
   CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
   if (tc && nq_pad > nq)
-    CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
+    CK(cudaMemsetAsync((uint8_t *)qs.q16 + (size_t)nq * kpad * tc_qelem(v), 0,
+                       (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
+       "memset");
   StageClock clock(st);
   if (rows) {
     // kernels clamp list entries to the shard; a bad list is reported at the end
@@ -545,7 +564,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   int h = clock.begin(ST_PREP);
   launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, dflags, st);
   clock.end(h);
-  counted(1);
+  counted(bits && tc ? 2 : 1);
   CK(cudaGetLastError(), "query preparation");
 
   ScanArgs a{};
@@ -554,13 +573,13 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.queries = (const float *)queries;
   a.nq = nq;
   a.metric = metric;
-  a.raw_scale = tc && v.dtype != DT_F16;   // tensor scan of quantized rows: scores on raw codes
+  a.raw_scale = tc && v.dtype != DT_F16 && !bits;   // tensor scan of quantized rows: scores on raw codes
   a.thr = qs.thr;
   a.cnt = cnt;
   a.flags = dflags;
 
   CUtensorMap query_map;
-  if (tc && !encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+  if (tc && !encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   // One scan launch timed as `stage`. Tensor path: rows come from the shard
   // itself when the candidates are a contiguous run, else from `staged`
@@ -1082,7 +1101,7 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   cudaStream_t st = (cudaStream_t)stream;
   const bool bits = v.dtype == DT_BIT;
   const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
-  const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
+  const uint32_t kpad = tc ? tc_kpad(v) : 0;
   const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
   const uint32_t nq_pad = tc ? (nq + bn - 1) / bn * bn : 0;
   Carver c;
@@ -1102,11 +1121,13 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   uint32_t *dflags = (uint32_t *)(w + o_flags);
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
   if (tc && nq_pad > nq)
-    CK(cudaMemsetAsync(qs.q16 + (size_t)nq * kpad, 0, (size_t)(nq_pad - nq) * kpad * sizeof(__half), st), "memset");
+    CK(cudaMemsetAsync((uint8_t *)qs.q16 + (size_t)nq * kpad * tc_qelem(v), 0,
+                       (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
+       "memset");
   if (rows) launch_check_rows(rows, nrows, v.rows, dflags, st);
   launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, scan_gamma(bits, tc, kpad, v.dims),
                       sh->maxn2, qs, bits, dflags, st);
-  counted(1);
+  counted(bits && tc ? 2 : 1);
   ScanArgs a{};
   a.s = v;
   a.ids = rows;
@@ -1120,10 +1141,10 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.mat = out;
   a.mat_ld = n;
   a.flags = dflags;
-  a.raw_scale = tc && v.dtype != DT_F16;
+  a.raw_scale = tc && v.dtype != DT_F16 && !bits;
   if (tc) {
     CUtensorMap query_map;
-    if (!encode_f16_map(&query_map, qs.q16, kpad, nq_pad, (uint64_t)kpad * 2, bn))
+    if (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn))
       return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
     auto tc_launch = [&](const CUtensorMap &rows_map) -> cudaError_t {
       return launch_tc_scan(a, rows_map, 0, query_map, kpad, bn, sh->sms, st);

@@ -164,6 +164,30 @@ def test_hamming_bit_exact_with_ties(cuda):
     assert_same(cuda, oracle.BIT, 1024, rows[:500], qs[:4], 7, 3)
 
 
+@pytest.mark.parametrize('dims', [1024, 512, 128, 1000, 136])
+@pytest.mark.parametrize('simt', [False, True])
+def test_hamming_tensor_and_simt_paths(cuda, dims, simt):
+    # rows whose byte pitch is a multiple of 16 (1024, 512, 128 bits) are
+    # expanded to +-1 int8 and scored by kind::i8 MMAs (exact S32 dot
+    # products); 1000 and 136 bits (125 and 17 bytes) stay on CUDA cores.
+    # Whole shard, a row list (staged rows), window mode, duplicated rows
+    # (ties ordered by row id) and a k past the shared-memory sort.
+    rows, proto = synth.bit_rows(50000, dims, 64, flip=0.05, seed=dims)
+    rows[7000:7300] = rows[123]
+    rng = np.random.default_rng(dims)
+    nb = rows.shape[1]
+    qs = proto[rng.integers(0, 64, 40)] ^ np.packbits(rng.random((40, nb * 8)) < 0.05, axis=1,
+                                                      bitorder='little')[:, :nb]
+    if dims % 8:
+        qs[:, -1] &= (1 << (dims % 8)) - 1       # the row's padding bits are zero, as the rows'
+    qs[3] = rows[123]
+    _, ids = synth.bitmap(50000, 0.3, seed=dims + 1)
+    assert_same(cuda, oracle.BIT, dims, rows, qs, 100, 3, force_simt=simt)
+    assert_same(cuda, oracle.BIT, dims, rows, qs, 20, 3, ids=ids, force_simt=simt)
+    assert_same(cuda, oracle.BIT, dims, rows, qs[:16], 10, 3, ids=ids[:3000], window=True, force_simt=simt)
+    assert_same(cuda, oracle.BIT, dims, rows, qs[:16], 5000, 3, force_simt=simt)
+
+
 # ---------------------------------------------------------------- edge cases
 
 def test_edge_k_values(cuda):
