@@ -485,11 +485,11 @@ def build_config4(args, rank, world, dev):
     w.inputs = [queries, local]
     w.shard = pb.Shard(pb.NVFP4, args.dims, codes, bscales, rscales, first_id=lo)
     w.metric, w.dtype, w.bound = pb.L2, 'nvfp4->f32', 'hbm'
-    w.kernel = 'simt_scan_lists<NVFP4>, list pass'
+    w.kernel = 'tc_scan_lists<NVFP4>, list pass'
     w.data = ('synthetic (seeded: %d list centres ~N(0,1), rows = centre + 0.1 noise, Zipf(1.1) list sizes, '
               'NVFP4-quantised on the GPU with the builder\'s rules)' % nlists)
     w.row_bytes = blocks * 8 + blocks + 4
-    w.profile = 'simt_scan_lists_config4.md'
+    w.profile = 'tc_scan_lists_nvfp4_config4.md'
     # algorithmic bytes of a pass: every probed list's rows, read once
     hit = torch.zeros(l1 - l0, dtype=torch.bool, device=dev)
     lp = local[local >= 0].long()
