@@ -291,7 +291,12 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
 }
 
 // Per storage format: pipeline stages, raw-code ring (quantized formats stage
-// their codes and convert them to FP16 in shared memory), threads.
+// their codes and convert them to FP16 -- bit vectors to int8 -- in shared
+// memory), threads. Quantized formats run CONV_WARPS converter warps: with 4,
+// a k-block's conversion (about 770 cycles) nearly matched its MMAs (about
+// 850 at the sustained rate) and the MMAs waited on it 30% of the time.
+constexpr int CONV_WARPS = 8;
+constexpr int CONV_THREADS = 32 * CONV_WARPS;
 // STG stages hold an A tile and a B tile each; the gathered-FP16 kernel
 // instead keeps STG A tiles and BSTG B tiles in separate rings.
 template <int Q> struct TcCfg;
@@ -300,15 +305,15 @@ template <> struct TcCfg<DT_F16> {
   static constexpr int RING = STG * STAGE_BYTES;
 };
 template <> struct TcCfg<DT_E4M3> {   // 64 one-byte codes a row a k-block
-  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 64, RAW_X = 64, NT = 320;
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 64, RAW_X = 64, NT = 192 + 32 * CONV_WARPS;
   static constexpr int RING = STG * STAGE_BYTES;
 };
 template <> struct TcCfg<DT_NVFP4> {  // 64 nibbles (32 bytes) a row a k-block
-  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 320;
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 32, RAW_X = 32, NT = 192 + 32 * CONV_WARPS;
   static constexpr int RING = STG * STAGE_BYTES;
 };
 template <> struct TcCfg<DT_BIT> {    // 128 bits (16 bytes) a row a k-block -> 128 int8
-  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 16, RAW_X = 16, NT = 320;
+  static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 16, RAW_X = 16, NT = 192 + 32 * CONV_WARPS;
   static constexpr int RING = STG * STAGE_BYTES;
 };
 // FP16 rows named by a candidate list (or a strided sample): 4 gather warps
@@ -354,14 +359,14 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) { retur
 
 // Convert one stage's raw codes (BM rows of RAW_X bytes, dense) into the
 // FP16 A tile (raw values: the row scale is applied in the epilogue). 128
-// converter threads; ct = converter thread, vrow0 = virtual row of tile row 0.
+// converter threads (CONV_THREADS); ct = converter thread, vrow0 = virtual row of tile row 0.
 template <int Q>
 __device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *raw, uint8_t *atile, uint32_t ct,
                                               uint64_t vrow0, uint32_t kb) {
   if (Q == DT_E4M3) {
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const uint32_t i = ct + 128 * u, r = i >> 2, c = i & 3;  // 16 codes: dims 16c .. 16c+15
+    for (int u = 0; u < 512 / CONV_THREADS; u++) {
+      const uint32_t i = ct + CONV_THREADS * u, r = i >> 2, c = i & 3;  // 16 codes: dims 16c .. 16c+15
       const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + c * 16);
       uint4 lo, hi;
       e4m3x4_to_f16(w.x, lo.x, lo.y);
@@ -373,8 +378,8 @@ __device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *
     }
   } else if (Q == DT_NVFP4) {
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const uint32_t i = ct + 128 * u, r = i >> 1, h = i & 1;  // 32 nibbles: dims 32h .. 32h+31
+    for (int u = 0; u < 256 / CONV_THREADS; u++) {
+      const uint32_t i = ct + CONV_THREADS * u, r = i >> 1, h = i & 1;  // 32 nibbles: dims 32h .. 32h+31
       const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
       const uint64_t vi = vrow0 + r;
       uint32_t sc[2] = {0u, 0u};
@@ -406,8 +411,8 @@ __device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *
     // products land at positions that are not multiples of 8, with no
     // carries), so each nibble becomes four bytes of 0 / 1, then of 1 / -1.
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const uint32_t i = ct + 128 * u, r = i >> 2, w = i & 3;  // bits 32w .. 32w+31
+    for (int u = 0; u < 512 / CONV_THREADS; u++) {
+      const uint32_t i = ct + CONV_THREADS * u, r = i >> 2, w = i & 3;  // bits 32w .. 32w+31
       const uint32_t x = *reinterpret_cast<const uint32_t *>(raw + r * 16 + w * 4);
       uint32_t o[8];
 #pragma unroll
@@ -472,14 +477,14 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STG; s++) {
-      mbar_init(full + s, QUANT ? 4 : (GATHER ? 128 : 1));
+      mbar_init(full + s, QUANT ? CONV_WARPS : (GATHER ? 128 : 1));
       mbar_init(empty + s, 1);
       mbar_init(bfull + s, 1);
       mbar_init(bempty + s, 1);
     }
     for (int r = 0; r < RSTG; r++) {
       mbar_init(rawfull + r, 1);
-      mbar_init(rawempty + r, 4);
+      mbar_init(rawempty + r, CONV_WARPS);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(tfull + b, 1);
