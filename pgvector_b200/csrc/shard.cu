@@ -683,6 +683,13 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
         if (sample) {
           double room = (double)seen * (double)cap / (2.0 * (double)k);
           len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)room));
+          if (start == 0) {
+            // head window: its rows pass the sample's bound at about k/S of
+            // them, the rows after the tighten at about k/(S + head); head =
+            // sqrt(S n) - S minimises the appends of the two
+            const double head = std::sqrt((double)S * (double)n) - (double)S;
+            len = std::min<uint64_t>(len, std::max<uint64_t>(65536, (uint64_t)head / 128 * 128));
+          }
         }
         uint64_t piece = staged_pass ? std::min<uint64_t>(len, 65536) : len;
         for (uint64_t off = 0; off < len;) {
