@@ -180,7 +180,9 @@ int			AnnB200ScoreMatrix(AnnB200Shard *shard, const void *queries, uint32_t nq,
  * all-gather of AnnB200Search outputs produces). Output as AnnB200Search:
  * the k best by (distance, id), or with ANNB200_WINDOW every entry within
  * the gathered tolerance of the merged k-th distance. nlists * list_cap must
- * not exceed 4096.
+ * not exceed 4096. Without ANNB200_WINDOW the merge is only enqueued on
+ * stream (results are ready when the stream reaches it); with it the call
+ * waits for the merge, to report a window larger than out_cap.
  */
 int			AnnB200MergeTopk(const double *dist, const int64_t *ids, const uint32_t *counts,
 							 uint32_t nlists, uint32_t nq, uint32_t list_cap, uint32_t k,

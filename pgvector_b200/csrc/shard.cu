@@ -1044,6 +1044,9 @@ extern "C" int AnnB200MergeTopk(const double *dist, const int64_t *ids, const ui
      "merge");
   clock.end(h);
   counted(1);
+  // only a window can outgrow out_cap (k <= out_cap was checked): without
+  // one the merge stays queued on the stream, with no host round trip
+  if (!(flags & ANNB200_WINDOW)) return OK;
   uint32_t hf = 0;
   CK(cudaMemcpyAsync(&hf, fl.p, 4, cudaMemcpyDeviceToHost, st), "merge flags");
   CK(cudaStreamSynchronize(st), "merge");

@@ -25,21 +25,26 @@ def bitmap_slice(words, lo, hi):
 
 def gather_lists(dist_t, ids_t, count_t, group=None):
     """All-gather every rank's [nq][k] results into [world][nq][k] tensors
-    (rank-major, the layout AnnB200MergeTopk takes)."""
+    (rank-major, the layout AnnB200MergeTopk takes). The three result tensors
+    travel packed in one byte buffer: one collective a step."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
-    out = []
-    for t in (dist_t, ids_t, count_t):
-        t = t.contiguous()
-        if dist.get_backend(group) == 'nccl':
-            buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-            dist.all_gather_into_tensor(buf, t, group=group)
-        else:
-            parts = [torch.empty_like(t) for _ in range(world)]
-            dist.all_gather(parts, t, group=group)
-            buf = torch.stack(parts)
-        out.append(buf)
+    parts = [t.contiguous() for t in (dist_t, ids_t, count_t)]
+    flat = [p.reshape(-1).view(torch.uint8) for p in parts]
+    send = torch.cat(flat)
+    if dist.get_backend(group) == 'nccl':
+        buf = torch.empty((world, send.numel()), dtype=torch.uint8, device=send.device)
+        dist.all_gather_into_tensor(buf, send, group=group)
+    else:
+        chunks = [torch.empty_like(send) for _ in range(world)]
+        dist.all_gather(chunks, send, group=group)
+        buf = torch.stack(chunks)
+    out, off = [], 0
+    for p, f in zip(parts, flat):
+        n = f.numel()
+        out.append(buf[:, off:off + n].contiguous().view(p.dtype).view((world,) + tuple(p.shape)))
+        off += n
     return out
 
 
