@@ -713,42 +713,61 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
 
 // ---------------------------------------------------------------- IVF list scan on tensor cores
 //
-// The list gather of ivf.cu on tcgen05: a work item is a 128-row tile of a
-// probed list x up to 32 of the queries that probe the list (ListPlan with
-// bm = 128, bq = 32). The rows of a list are contiguous in the shard, so the
-// tile is one TMA box a k-block -- FP16 rows straight into the A tile, E4M3 /
-// NVFP4 codes 128 bytes of each row at a time (and NVFP4's block scales for
-// those bytes) into a raw ring the converter warps turn into FP16. The group's queries
-// are gathered from the FP16 query copy by cp.async into a 32-row B tile.
-// One M=128, N=32 accumulator an item, double buffered (64 TMEM columns).
+// The list gather of ivf.cu on tcgen05. A work item is a 256-row tile of a
+// probed list x up to 64 of the queries that probe the list (ListPlan with
+// bm = 256, bq = 64). Rows are the MMA's N operand and queries its M
+// operand (M = 64, N = 256, K = 16): an IVF list has few queries (about 4 in
+// config 4), and a tcgen05.mma costs some 70-80 cycles to issue whatever its
+// shape, so 256 rows an instruction (about 100 cycles of math at M = 64)
+// keep the tensor core ahead of HBM where 128 rows x 32 queries did not.
+// The rows of a list are contiguous in the shard: FP16 rows come by TMA
+// straight into the row (B) tile, E4M3 / NVFP4 codes 128 bytes of each row
+// at a time (and NVFP4's block scales for those bytes) into a raw ring the
+// converter warps turn into FP16. The group's queries are gathered from the
+// FP16 query copy by cp.async into the query (A) tile; rows of the tile past
+// the group are left as they are (their accumulator rows are never read).
+// The accumulator is 64 x 256 FP32, double buffered (all 512 TMEM
+// columns); query m of the group sits in TMEM lane (m % 16) + 32 (m / 16),
+// so epilogue warp w reads queries 16 (w % 4) .. +15 in its lanes 0-15.
 // Each CTA walks a contiguous run of items and decodes them incrementally,
 // so list metadata, query numbers and thresholds are read once a list.
-constexpr int LQ = 32;                       // queries an item (MMA N)
-constexpr int L_B = LQ * 128;                // B tile: 32 queries x 64 halves
+constexpr int LQ = 64;                       // queries an item (MMA M)
+constexpr int LR = 256;                      // rows an item (MMA N)
+constexpr int LA_BYTES = LQ * 128;           // query tile a k-block: 64 x 64 halves
+constexpr int LB_BYTES = LR * 128;           // row tile a k-block: 256 x 64 halves
 constexpr int L_CW = 8;                      // converter warps (6 .. 13)
-constexpr int L_BW = 6 + L_CW;               // the query-gather warp
-constexpr int L_NT = 32 * (L_BW + 1);
-constexpr int L_TMEM = 64;
+constexpr int L_QW = 6 + L_CW;               // the query-gather warp
+constexpr int L_NT = 32 * (L_QW + 1);
+constexpr int L_TMEM = 512;                  // 2 accumulators x 256 columns
 constexpr int L_BAR = 1024;                  // barrier region bytes
 
-// STG A stages (converted FP16 row tiles); BSTG query tiles, gathered up to
-// BSTG k-blocks ahead so their L2 latency stays hidden; RSTG raw segments of
-// codes in flight from HBM (quantized formats). A raw segment is 128 bytes
-// of each of the tile's 128 rows (one TMA box, 128-byte swizzle) and covers
-// SEGK k-blocks; NVFP4 adds the 16 block-scale bytes of those k-blocks
-// (SCB). Whole 128-byte row pieces keep the TMA request count per byte low:
-// 32-byte boxes a k-block cost four times the requests and left the copy
-// engine, not HBM, the limit.
+// BSTG row (B) stages of converted (or TMA-loaded FP16) rows; ASTG query (A)
+// stages, gathered up to ASTG k-blocks ahead so their L2 latency stays
+// hidden; RSTG raw segments of codes in flight from HBM (quantized formats).
+// A raw segment is 128 bytes of each of the tile's 256 rows (two TMA boxes
+// of 128 rows, 128-byte swizzle) and covers SEGK k-blocks; NVFP4 adds the 16
+// block-scale bytes of those k-blocks (SCB). Whole 128-byte row pieces keep
+// the TMA request count per byte low.
 template <int Q> struct LCfg;
 template <> struct LCfg<DT_F16> {
-  static constexpr int STG = 8, BSTG = 16, RSTG = 0, RAWB = 0, SEGK = 1, SCB = 0;
+  static constexpr int BSTG = 4, ASTG = 6, RSTG = 0, RAWB = 0, SEGK = 1, SCB = 0;
 };
 template <> struct LCfg<DT_E4M3> {
-  static constexpr int STG = 4, BSTG = 16, RSTG = 4, RAWB = BM * 128, SEGK = 2, SCB = 0;
+  static constexpr int BSTG = 2, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 2, SCB = 0;
 };
 template <> struct LCfg<DT_NVFP4> {
-  static constexpr int STG = 4, BSTG = 16, RSTG = 4, RAWB = BM * 128, SEGK = 4, SCB = BM * 16;
+  static constexpr int BSTG = 2, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 4, SCB = LR * 16;
 };
+
+// Accumulator rows of a group of g queries: the group fills nqq = ceil(g/16)
+// TMEM lane quarters (query j in row j), and groups of up to 32 queries are
+// repeated rep = 4 / nqq times (copy c of query j in row j + 16 nqq c), so
+// that every epilogue warp has queries to score and each copy's warps share
+// the item's 256 rows: the MMA's cost is the same for any M-row content.
+__device__ __forceinline__ void group_layout(uint32_t g, uint32_t &nqq, uint32_t &rep) {
+  nqq = (g + 15) / 16;
+  rep = nqq == 1 ? 4u : (nqq == 2 ? 2u : 1u);
+}
 
 struct ListTcArgs {
   ScanArgs a;
@@ -757,6 +776,11 @@ struct ListTcArgs {
   const __half *q16;       // FP16 queries [.][kpad]
   uint32_t kpad, kblocks;
 };
+
+// Instruction descriptor: FP16 A and B, FP32 accumulator, both K-major, M x N.
+__device__ __forceinline__ uint32_t f16_idesc_mn(uint32_t m, uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
 
 // Walks this CTA's run of items in order: list l, item t within it (row tile
 // t / groups, query group t % groups), with the list's window and queries.
@@ -824,7 +848,7 @@ struct ItemCursor {
       fetch_next();
     }
   }
-  __device__ uint64_t row0() const { return lo + (t / groups) * BM; }
+  __device__ uint64_t row0() const { return lo + (t / groups) * LR; }
   __device__ uint32_t group() const { return (uint32_t)(t % groups); }
   __device__ uint32_t nq_item() const {
     const uint32_t g0 = group() * LQ;
@@ -846,18 +870,18 @@ struct ItemCursor {
   }
 };
 
-// NVFP4 k-block q of a raw segment: codes (128 rows x 128 bytes, 128-byte
+// NVFP4 k-block q of a raw segment: codes (256 rows x 128 bytes, 128-byte
 // swizzle; the k-block is 16-byte chunks 2q and 2q+1 of each row) and the
 // rows' block scales (16 bytes a row, the k-block's four at byte 4q) -> FP16
-// A tile of raw values (row scale in the epilogue). nth converter threads, ct
-// the thread's index. Unit i is row r, half h with the eight lanes of a
+// row tile of raw values (row scale in the epilogue). nth converter threads,
+// ct the thread's index. Unit i is row r, half h with the eight lanes of a
 // quarter warp on eight consecutive rows, so the swizzle spreads their 16-byte
 // reads over all banks.
 template <int NTH>
-__device__ __forceinline__ void convert_nvfp4_seg(const uint8_t *raw, const uint8_t *sbox, uint8_t *atile,
+__device__ __forceinline__ void convert_nvfp4_seg(const uint8_t *raw, const uint8_t *sbox, uint8_t *btile,
                                                   uint32_t ct, uint32_t q) {
 #pragma unroll
-  for (int u = 0; u < 256 / NTH; u++) {
+  for (int u = 0; u < 2 * LR / NTH; u++) {
     const uint32_t i = ct + NTH * u, h = (i >> 3) & 1, r = (i & 7) | ((i >> 4) << 3);  // dims 32h .. 32h+31
     const uint4 w = *reinterpret_cast<const uint4 *>(raw + sw128_offset(r, 2 * q + h));
     uint32_t sc[2];
@@ -873,18 +897,18 @@ __device__ __forceinline__ void convert_nvfp4_seg(const uint8_t *raw, const uint
     for (int j = 0; j < 4; j++) {
       uint32_t o[4];
       e2m1x8_to_f16(ws[j], sc[j >> 1], o);
-      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4 *>(btile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
 
-// E4M3 k-block q of a raw segment (128 rows x 128 codes, 128-byte swizzle;
-// the k-block is chunks 4q .. 4q+3) -> FP16 A tile of raw values. Unit i is
-// row r, chunk c, a quarter warp on eight consecutive rows.
+// E4M3 k-block q of a raw segment (256 rows x 128 codes, 128-byte swizzle;
+// the k-block is chunks 4q .. 4q+3) -> FP16 row tile of raw values. Unit i
+// is row r, chunk c, a quarter warp on eight consecutive rows.
 template <int NTH>
-__device__ __forceinline__ void convert_e4m3_seg(const uint8_t *raw, uint8_t *atile, uint32_t ct, uint32_t q) {
+__device__ __forceinline__ void convert_e4m3_seg(const uint8_t *raw, uint8_t *btile, uint32_t ct, uint32_t q) {
 #pragma unroll
-  for (int u = 0; u < 512 / NTH; u++) {
+  for (int u = 0; u < 4 * LR / NTH; u++) {
     const uint32_t i = ct + NTH * u, c = (i >> 3) & 3, r = (i & 7) | ((i >> 5) << 3);  // dims 16c .. 16c+15
     const uint4 w = *reinterpret_cast<const uint4 *>(raw + sw128_offset(r, 4 * q + c));
     uint4 lo, hi;
@@ -892,8 +916,8 @@ __device__ __forceinline__ void convert_e4m3_seg(const uint8_t *raw, uint8_t *at
     e4m3x4_to_f16(w.y, lo.z, lo.w);
     e4m3x4_to_f16(w.z, hi.x, hi.y);
     e4m3x4_to_f16(w.w, hi.z, hi.w);
-    *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c)) = lo;
-    *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 2 * c + 1)) = hi;
+    *reinterpret_cast<uint4 *>(btile + sw128_offset(r, 2 * c)) = lo;
+    *reinterpret_cast<uint4 *>(btile + sw128_offset(r, 2 * c + 1)) = hi;
   }
 }
 
@@ -903,26 +927,25 @@ __global__ void __launch_bounds__(L_NT, 1)
                   const ListTcArgs L) {
   using C = LCfg<Q>;
   constexpr bool QUANT = Q != DT_F16;
-  constexpr int RAWB = C::RAWB + C::SCB;     // raw codes + (NVFP4) scale box a raw stage
-  constexpr int STG = C::STG, BSTG = C::BSTG, RSTG = C::RSTG, RSTG1 = RSTG > 0 ? RSTG : 1;
+  constexpr int RAWS = C::RAWB + C::SCB;     // raw codes + (NVFP4) scale box a raw segment
+  constexpr int BSTG = C::BSTG, ASTG = C::ASTG, RSTG = C::RSTG, RSTG1 = RSTG > 0 ? RSTG : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *btiles = smem + STG * A_BYTES;
-  uint8_t *raw = btiles + BSTG * L_B;
-  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);   // A tile ready
-  uint64_t *empty = full + STG;                                        // A stage consumed
-  uint64_t *bfull = empty + STG;                                       // query tile landed
-  uint64_t *bempty = bfull + BSTG;                                     // query tile consumed
-  uint64_t *rawfull = bempty + BSTG;
+  uint8_t *qtiles = smem + BSTG * LB_BYTES;
+  uint8_t *raw = qtiles + ASTG * LA_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWS);   // row tile ready
+  uint64_t *empty = full + BSTG;                                       // row stage consumed
+  uint64_t *afull = empty + BSTG;                                      // query tile landed
+  uint64_t *aempty = afull + ASTG;                                     // query stage consumed
+  uint64_t *rawfull = aempty + ASTG;
   uint64_t *rawempty = rawfull + RSTG1;
   uint64_t *tfull = rawempty + RSTG1;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile uint32_t *abort = tmem_slot + 1;
-  uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + L_BAR);  // 4 warps x EPI_BUF
-  float *gthr = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);                      // [4 warps][32]
-  uint32_t *gq = reinterpret_cast<uint32_t *>(gthr + 4 * LQ);                            // [4 warps][32]
+  float2 *affine = reinterpret_cast<float2 *>(reinterpret_cast<uint8_t *>(full) + L_BAR);  // [2][LR] (alpha, beta)
+  volatile uint32_t *epi_ok = reinterpret_cast<volatile uint32_t *>(affine + 2 * LR);     // [2][4 warps]
 
   const ScanArgs &a = L.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -934,13 +957,13 @@ __global__ void __launch_bounds__(L_NT, 1)
   cur.start(first, last);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STG; s++) {
-      mbar_init(full + s, QUANT ? L_CW : 1);   // converter warps | the A tile's TMA
+    for (int s = 0; s < BSTG; s++) {
+      mbar_init(full + s, QUANT ? L_CW : 1);   // converter warps | the row tile's TMA
       mbar_init(empty + s, 1);
     }
-    for (int s = 0; s < BSTG; s++) {
-      mbar_init(bfull + s, 32);                // the gather warp's copies
-      mbar_init(bempty + s, 1);
+    for (int s = 0; s < ASTG; s++) {
+      mbar_init(afull + s, 32);                // the gather warp's copies
+      mbar_init(aempty + s, 1);
     }
     for (int r = 0; r < RSTG; r++) {
       mbar_init(rawfull + r, 1);
@@ -967,18 +990,19 @@ __global__ void __launch_bounds__(L_NT, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // FP16: the row tile a k-block into the A stage. Quantized: a raw
-    // segment (128 bytes of every row, SEGK k-blocks, + NVFP4 scale box)
-    // into the raw ring.
+    // FP16: a k-block of the tile's 256 rows (two 128-row boxes) into the row
+    // stage. Quantized: a raw segment (128 bytes of every row, SEGK k-blocks,
+    // + NVFP4 scale boxes) into the raw ring.
     if (lane == 0) {
-      constexpr int RING = QUANT ? RSTG1 : STG;
+      constexpr int RING = QUANT ? RSTG1 : BSTG;
+      constexpr int HALF = 128 * 128;   // bytes of a 128-row box (codes or FP16 rows)
       uint64_t *ring_full = QUANT ? rawfull : full;
       uint64_t *ring_empty = QUANT ? rawempty : empty;
       const uint32_t steps = QUANT ? (L.kblocks + C::SEGK - 1) / C::SEGK : L.kblocks;
       uint64_t it = 0;
       bool ok = true;
       for (; cur.valid() && ok; cur.next()) {
-        const int32_t arow = (int32_t)cur.row0();
+        const int32_t row = (int32_t)cur.row0();
         for (uint32_t kb = 0; kb < steps; kb++, it++) {
           const uint32_t s = (uint32_t)(it % RING), ph = (uint32_t)((it / RING) & 1);
           if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags)) {
@@ -986,14 +1010,19 @@ __global__ void __launch_bounds__(L_NT, 1)
             break;
           }
           if (QUANT) {
-            mbar_expect_tx(ring_full + s, (uint32_t)RAWB);
-            uint8_t *dst = raw + s * RAWB;
-            tma_load_2d(smem_u32(dst), &rows_map, (int32_t)(kb * 128), arow, ring_full + s);
-            if (C::SCB)
-              tma_load_2d(smem_u32(dst + C::RAWB), &scales_map, (int32_t)(kb * 16), arow, ring_full + s);
+            mbar_expect_tx(ring_full + s, (uint32_t)RAWS);
+            uint8_t *dst = raw + s * RAWS;
+            for (int h = 0; h < 2; h++) {
+              tma_load_2d(smem_u32(dst + h * HALF), &rows_map, (int32_t)(kb * 128), row + 128 * h, ring_full + s);
+              if (C::SCB)
+                tma_load_2d(smem_u32(dst + C::RAWB + h * 128 * 16), &scales_map, (int32_t)(kb * 16), row + 128 * h,
+                            ring_full + s);
+            }
           } else {
-            mbar_expect_tx(ring_full + s, (uint32_t)A_BYTES);
-            tma_load_2d(smem_u32(smem + s * A_BYTES), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+            mbar_expect_tx(ring_full + s, (uint32_t)LB_BYTES);
+            uint8_t *dst = smem + s * LB_BYTES;
+            for (int h = 0; h < 2; h++)
+              tma_load_2d(smem_u32(dst + h * HALF), &rows_map, (int32_t)(kb * 64), row + 128 * h, ring_full + s);
           }
         }
       }
@@ -1003,29 +1032,29 @@ __global__ void __launch_bounds__(L_NT, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = f16_idesc(LQ);
+      const uint32_t idesc = f16_idesc_mn(LQ, LR);
       uint64_t it = 0, tc = 0;
       bool ok = true;
       for (uint64_t item = first; item < last && ok; item++, tc++) {
         const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
         if (!mbar_wait(tempty + ab, (use & 1) ^ 1, abort, a.flags)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * LQ;
+        const uint32_t d_tmem = tmem_base + ab * LR;
         for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
-          const uint32_t sb = (uint32_t)(it % BSTG), phb = (uint32_t)((it / BSTG) & 1);
-          if (!mbar_wait(full + s, ph, abort, a.flags) || !mbar_wait(bfull + sb, phb, abort, a.flags)) {
+          const uint32_t s = (uint32_t)(it % BSTG), ph = (uint32_t)((it / BSTG) & 1);
+          const uint32_t sq = (uint32_t)(it % ASTG), phq = (uint32_t)((it / ASTG) & 1);
+          if (!mbar_wait(full + s, ph, abort, a.flags) || !mbar_wait(afull + sq, phq, abort, a.flags)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * A_BYTES);
-          const uint32_t sbq = smem_u32(btiles + sb * L_B);
+          const uint32_t sa = smem_u32(qtiles + sq * LA_BYTES);   // queries: A (M = 64)
+          const uint32_t sb = smem_u32(smem + s * LB_BYTES);      // rows: B (N = 256)
 #pragma unroll
           for (uint32_t kk = 0; kk < 4; kk++)
-            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sbq + kk * 32), idesc, (kb | kk) != 0);
+            tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
           tc_commit(empty + s);
-          tc_commit(bempty + sb);
+          tc_commit(aempty + sq);
         }
         if (ok) tc_commit(tfull + ab);
       }
@@ -1035,39 +1064,60 @@ __global__ void __launch_bounds__(L_NT, 1)
       }
     }
     __syncwarp();
-  } else if (warp == L_BW) {
+  } else if (warp == L_QW) {
     // ------------------------------------------------------------ query gather
-    // Lane j copies query j of the item's group (its 128 bytes of the
-    // k-block) into the B ring by cp.async, up to BSTG k-blocks ahead of the
-    // MMAs; rows past the group are zero-filled.
+    // Lane j copies queries j and j + 32 of the item's group (their 128 bytes
+    // of the k-block) into the query ring by cp.async, into the accumulator
+    // rows group_layout gives, up to ASTG k-blocks ahead of the MMAs; rows
+    // the group does not use are not written.
     uint64_t it = 0, pf_qb = ~0ull;
-    uint32_t pf_q = 0;
+    uint32_t pf_q[2] = {0u, 0u};
     bool ok = true;
     for (; cur.valid() && ok; cur.next()) {
       const uint32_t nqt = cur.nq_item();
       const uint64_t qb = cur.qbase();
-      const uint32_t qn = (uint32_t)lane < nqt ? (qb == pf_qb ? pf_q : L.p.qlist[qb + lane]) : 0u;
-      const uint32_t n = (uint32_t)lane < nqt ? 16u : 0u;
-      const __half *src = L.q16 + (uint64_t)qn * L.kpad;
+      uint32_t nqq, rep;
+      group_layout(nqt, nqq, rep);
+      const __half *src[2];
+      uint32_t n[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const uint32_t j = (uint32_t)lane + 32u * h;
+        const uint32_t qn = j < nqt ? (qb == pf_qb ? pf_q[h] : L.p.qlist[qb + j]) : 0u;
+        n[h] = j < nqt ? 16u : 0u;
+        src[h] = L.q16 + (uint64_t)qn * L.kpad;
+      }
       {
         uint64_t nqb;
         uint32_t nnqt;
         if (cur.peek_group(nqb, nnqt) && nqb != qb) {
           pf_qb = nqb;
-          pf_q = (uint32_t)lane < nnqt ? L.p.qlist[nqb + lane] : 0u;
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const uint32_t j = (uint32_t)lane + 32u * h;
+            pf_q[h] = j < nnqt ? L.p.qlist[nqb + j] : 0u;
+          }
         }
       }
       for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
-        const uint32_t sb = (uint32_t)(it % BSTG), ph = (uint32_t)((it / BSTG) & 1);
-        const bool got = mbar_wait(bempty + sb, ph ^ 1, abort, a.flags);
+        const uint32_t sq = (uint32_t)(it % ASTG), ph = (uint32_t)((it / ASTG) & 1);
+        const bool got = mbar_wait(aempty + sq, ph ^ 1, abort, a.flags);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        const uint32_t dst = smem_u32(btiles + sb * L_B);
+        const uint32_t dst = smem_u32(qtiles + sq * LA_BYTES);
 #pragma unroll
-        for (uint32_t c = 0; c < 8; c++) cp_async16(dst + sw128_offset(lane, c), src + kb * 64 + c * 8, n);
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bfull + sb)) : "memory");
+        for (int h = 0; h < 2; h++)
+          if (n[h]) {
+            const uint32_t j = (uint32_t)lane + 32u * h;
+            for (uint32_t cp = 0; cp < rep; cp++) {
+              const uint32_t m = j + 16u * nqq * cp;   // accumulator row of copy cp
+#pragma unroll
+              for (uint32_t c = 0; c < 8; c++) cp_async16(dst + sw128_offset(m, c), src[h] + kb * 64 + c * 8, 16u);
+            }
+          }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(afull + sq)) : "memory");
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -1076,11 +1126,11 @@ __global__ void __launch_bounds__(L_NT, 1)
     // ------------------------------------------------------------ converters (quantized formats)
     if (QUANT) {
       const uint32_t ct = threadIdx.x - 192;
-      uint64_t it = 0, seg = 0;   // A stages, raw segments
+      uint64_t it = 0, seg = 0;   // row stages, raw segments
       bool ok = true;
       for (; cur.valid() && ok; cur.next()) {
         for (uint32_t kb = 0; kb < L.kblocks; kb++, it++) {
-          const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
+          const uint32_t s = (uint32_t)(it % BSTG), ph = (uint32_t)((it / BSTG) & 1);
           const uint32_t r = (uint32_t)(seg % RSTG1), rph = (uint32_t)((seg / RSTG1) & 1);
           const uint32_t q = kb % C::SEGK;
           const bool seg_end = q == C::SEGK - 1 || kb + 1 == L.kblocks;
@@ -1090,10 +1140,10 @@ __global__ void __launch_bounds__(L_NT, 1)
             ok = false;
             break;
           }
-          const uint8_t *rs = raw + r * RAWB;
-          uint8_t *atile = smem + s * A_BYTES;
-          if (Q == DT_NVFP4) convert_nvfp4_seg<32 * L_CW>(rs, rs + C::RAWB, atile, ct, q);
-          else convert_e4m3_seg<32 * L_CW>(rs, atile, ct, q);
+          const uint8_t *rs = raw + r * RAWS;
+          uint8_t *btile = smem + s * LB_BYTES;
+          if (Q == DT_NVFP4) convert_nvfp4_seg<32 * L_CW>(rs, rs + C::RAWB, btile, ct, q);
+          else convert_e4m3_seg<32 * L_CW>(rs, btile, ct, q);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
@@ -1107,82 +1157,107 @@ __global__ void __launch_bounds__(L_NT, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    // A lane owns one row of the item; the group's query numbers and
-    // thresholds sit in this warp's table (reloaded when the group changes).
-    Appender app{a, stage_buf + (warp - 2) * EPI_BUF, 0, lane};
+    // Accumulator row m sits in TMEM lane (m % 16) + 32 (m / 16), so warp w
+    // reads rows 16 (w % 4) .. +15: with group_layout's rows, copy
+    // (w % 4) / nqq of queries 16 ((w % 4) % nqq) .. +15 of the group, and the
+    // copy's share of the item's 256 rows. A lane scores its query against
+    // those rows, 32 accumulator columns at a time, then reserves one block of candidate slots for all
+    // its passing rows of the item (one atomicAdd, whose round trip would
+    // otherwise be paid a chunk) and writes them in column order, re-reading
+    // from TMEM only the chunks that have some. The rows'
+    // alpha and beta (row scale, norm) are staged once an item in shared
+    // memory by all 128 epilogue threads (two rows each, double buffered,
+    // named barrier 1). The four warps also post whether their wait for the
+    // accumulator ended in time before that barrier, so all of them leave the
+    // loop at the same item and none is left at the barrier.
     const int quad = warp & 3;
-    float *wthr = gthr + (warp - 2) * LQ;
-    uint32_t *wq = gq + (warp - 2) * LQ;
+    const uint32_t et = threadIdx.x - 64;                 // epilogue thread 0..127
+    uint32_t qn = 0, c_lo = 0, c_hi = 0;   // this lane's query; this warp's 32-row chunks of the item
+    float th = __int_as_float(0x7fc00000);
     uint64_t tc = 0, tab = ~0ull;
-    // the next group's query number and threshold, requested one item ahead
-    uint64_t pf_qb = ~0ull;
-    uint32_t pf_q = 0, pf_nqt = 0;
-    float pf_t = 0.0f;
     for (; cur.valid(); cur.next(), tc++) {
       const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
       const uint32_t nqt = cur.nq_item();
       const uint64_t qb = cur.qbase();
-      if (qb != tab) {          // a new query group: its numbers and thresholds
-        __syncwarp();
-        uint32_t qn;
-        float th;
-        if (qb == pf_qb) {
-          qn = pf_q;
-          th = pf_t;
-        } else {
-          qn = (uint32_t)lane < nqt ? L.p.qlist[qb + lane] : 0u;
-          th = (uint32_t)lane < nqt ? a.thr[qn] : __int_as_float(0x7fc00000);
-        }
-        wq[lane] = qn;
-        wthr[lane] = th;
-        __syncwarp();
+      if (qb != tab) {          // a new query group: this lane's query, its threshold, the warp's rows
+        uint32_t nqq, rep;
+        group_layout(nqt, nqq, rep);
+        const bool active = (uint32_t)quad < nqq * rep;
+        const uint32_t jq = 16u * ((uint32_t)quad % nqq) + (uint32_t)lane;
+        const bool mine = active && lane < 16 && jq < nqt;
+        qn = mine ? L.p.qlist[qb + jq] : 0u;
+        th = mine ? a.thr[qn] : __int_as_float(0x7fc00000);
+        const uint32_t per = (uint32_t)(LR / 32) / rep;
+        c_lo = active ? ((uint32_t)quad / nqq) * per : 0u;
+        c_hi = active ? c_lo + per : 0u;
         tab = qb;
       }
-      bool pf_new = false;
-      {
-        uint64_t nqb;
-        uint32_t nnqt;
-        if (cur.peek_group(nqb, nnqt) && nqb != qb && nqb != pf_qb) {
-          pf_qb = nqb;
-          pf_nqt = nnqt;
-          pf_q = (uint32_t)lane < nnqt ? L.p.qlist[nqb + lane] : 0u;
-          pf_new = true;
+      // the item's rows: alpha, beta into affine[tc & 1] (rows past the list never pass)
+      const uint64_t row0 = cur.row0();
+      float2 *aff = affine + (tc & 1) * LR;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const uint64_t row = row0 + et + 128u * h;
+        float al = 0.0f, be = __int_as_float(0x7fc00000);
+        if (row < cur.hi) row_affine(a.s, row, a.metric, a.raw_scale, al, be);
+        aff[et + 128u * h] = make_float2(al, be);
+      }
+      const bool got = __all_sync(0xffffffffu, mbar_wait(tfull + ab, use & 1, abort, a.flags));
+      if (lane == 0) epi_ok[(tc & 1) * 4 + (warp - 2)] = got ? 1u : 0u;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const volatile uint32_t *ok4 = epi_ok + (tc & 1) * 4;
+      if (!(ok4[0] & ok4[1] & ok4[2] & ok4[3])) break;
+      tc_fence_after();
+      const uint32_t acc = tmem_base + ab * LR + ((uint32_t)(quad * 32) << 16);
+      // pass 1: the passing rows of each 32-column chunk, and their count
+      uint32_t mk[LR / 32], total = 0;
+#pragma unroll 1
+      for (uint32_t c = c_lo; c < c_hi; c++) {
+        uint32_t r[32];
+        TMEM_LD32(acc + c * 32, r);
+        tmem_ld_wait();
+        uint32_t msk = 0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const float2 f = aff[c * 32 + j];
+          msk |= (uint32_t)(fmaf(__uint_as_float(r[j]), f.x, f.y) <= th) << j;
+        }
+        mk[c] = msk;
+        total += (uint32_t)__popc(msk);
+      }
+      // pass 2 (only where some row passed): one block of candidate slots a
+      // lane, then the passing rows of each chunk, re-read from TMEM
+      if (__any_sync(0xffffffffu, total != 0)) {
+        const uint32_t base = total ? atomicAdd(a.cnt + qn, total) : 0u;
+        uint2 *cand = a.cand + (uint64_t)qn * a.cap;
+        uint32_t done = 0;
+#pragma unroll 1
+        for (uint32_t c = c_lo; c < c_hi; c++) {
+          if (!__any_sync(0xffffffffu, mk[c] != 0)) continue;
+          uint32_t r[32];
+          TMEM_LD32(acc + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            if ((mk[c] >> j) & 1u) {
+              const uint32_t slot = base + done + (uint32_t)__popc(mk[c] & ((1u << j) - 1u));
+              const float2 f = aff[c * 32 + j];
+              if (slot < a.cap) {
+                cand[slot] = make_uint2(__float_as_uint(fmaf(__uint_as_float(r[j]), f.x, f.y)),
+                                        (uint32_t)(row0 + c * 32 + j));
+              } else {
+                atomicOr(a.flags, FLAG_OVERFLOW);
+                atomicMax(a.flags + 1, slot + 1);
+              }
+            }
+          }
+          done += (uint32_t)__popc(mk[c]);
         }
       }
-      bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
-      if (!__all_sync(0xffffffffu, got)) break;
-      tc_fence_after();
-      const uint64_t row = cur.row0() + quad * 32 + lane;
-      const bool valid = row < cur.hi;
-      float al = 0.0f, be = __int_as_float(0x7fc00000);   // rows past the list never pass
-      if (valid) row_affine(a.s, row, a.metric, a.raw_scale, al, be);
-      uint32_t r[32];
-      TMEM_LD32(tmem_base + ab * LQ + ((uint32_t)(quad * 32) << 16), r);
-      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(tempty + ab);        // the scores are in registers: the accumulator is free
-      uint32_t m = 0;
-#pragma unroll
-      for (int j = 0; j < 32; j++) m |= (uint32_t)(fmaf(__uint_as_float(r[j]), al, be) <= wthr[j]) << j;
-      if (pf_new) pf_t = (uint32_t)lane < pf_nqt ? a.thr[pf_q] : __int_as_float(0x7fc00000);
-      while (__any_sync(0xffffffffu, m != 0)) {
-        const bool has = m != 0;
-        const int j = has ? __ffs(m) - 1 : 0;
-        m &= m - 1;
-        float v = 0.0f;
-#pragma unroll
-        for (int jj = 0; jj < 32; jj++) v = (jj == j) ? __uint_as_float(r[jj]) : v;
-        v = fmaf(v, al, be);
-        const uint32_t ballot = __ballot_sync(0xffffffffu, has);
-        if (app.n + 32 > (uint32_t)EPI_BUF) app.flush();
-        if (has)
-          app.buf[app.n + __popc(ballot & ((1u << lane) - 1u))] =
-              make_uint4(wq[j], __float_as_uint(v), (uint32_t)row, 0u);
-        app.n += __popc(ballot);
-      }
+      mbar_arrive(tempty + ab);        // every column read: the accumulator is free
     }
     __syncwarp();
-    if (app.n) app.flush();
   }
 
   tc_fence_before();
@@ -1257,8 +1332,8 @@ cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_ma
 template <int Q>
 size_t tc_scan_lists_smem() {
   using C = LCfg<Q>;
-  return 1024 + (size_t)C::STG * A_BYTES + (size_t)C::BSTG * L_B + (size_t)C::RSTG * (C::RAWB + C::SCB) + L_BAR +
-         4 * EPI_BUF * sizeof(uint4) + 2 * 4 * LQ * sizeof(uint32_t);
+  return 1024 + (size_t)C::BSTG * LB_BYTES + (size_t)C::ASTG * LA_BYTES + (size_t)C::RSTG * (C::RAWB + C::SCB) +
+         L_BAR + 2 * LR * sizeof(float2) + 2 * 4 * sizeof(uint32_t);
 }
 
 template <int Q>
@@ -1310,7 +1385,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
 }
 
 // The IVF list scan on tensor cores over the items launch_list_items counted
-// with p.bm = 128 and p.bq = 32 (rows [rbegin, rend) of every probed list).
+// with p.bm = 256 and p.bq = 64 (rows [rbegin, rend) of every probed list).
 // rows_map: FP16 rows as launch_tc_scan reads contiguous runs of them
 // (box 64 x 128, 128-byte swizzle), or the E4M3 / NVFP4 codes as bytes in
 // boxes of 128 x 128 with the 128-byte swizzle; scales_map (NVFP4 only): the

@@ -831,7 +831,11 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
                   (v.dtype == DT_F16 || sh->seg_map_ok) && (v.dtype != DT_NVFP4 || sh->scales_map_ok);
   const uint32_t kpad = tc ? (v.dims + 63) / 64 * 64 : 0;
   const double gamma = scan_gamma(false, tc, kpad, v.dims);
-  const uint64_t S = std::max<uint64_t>(64, ((uint64_t)k + 63) / 64 * 64);
+  // first window: k rows a list rounded up to the item's row tile (256 rows
+  // on tensor cores, 64 on CUDA cores), so every later window (x8) starts on
+  // a tile boundary
+  const uint64_t tile = tc ? 256 : 64;
+  const uint64_t S = std::max<uint64_t>(tile, ((uint64_t)k + tile - 1) / tile * tile);
 
   Carver c;
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
@@ -871,8 +875,8 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
   p.toff = (unsigned long long *)(w + o_toff);
   p.bsum = (unsigned long long *)(w + o_bsum);
   p.qlist = (uint32_t *)(w + o_qlist);
-  p.bm = tc ? 128 : 64;   // an item: 128 rows x 32 queries on tensor cores, 64 x 16 on CUDA cores
-  p.bq = tc ? 32 : 16;
+  p.bm = tc ? 256 : 64;   // an item: 256 rows x 64 queries on tensor cores, 64 x 16 on CUDA cores
+  p.bq = tc ? 64 : 16;
   p.nzl = tc ? (uint32_t *)(w + o_nzl) : nullptr;
   p.nzoff = tc ? (unsigned long long *)(w + o_nzoff) : nullptr;
 
