@@ -753,10 +753,10 @@ template <> struct LCfg<DT_F16> {
   static constexpr int BSTG = 4, ASTG = 6, RSTG = 0, RAWB = 0, SEGK = 1, SCB = 0;
 };
 template <> struct LCfg<DT_E4M3> {
-  static constexpr int BSTG = 2, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 2, SCB = 0;
+  static constexpr int BSTG = 3, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 2, SCB = 0;
 };
 template <> struct LCfg<DT_NVFP4> {
-  static constexpr int BSTG = 2, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 4, SCB = LR * 16;
+  static constexpr int BSTG = 3, ASTG = 6, RSTG = 2, RAWB = LR * 128, SEGK = 4, SCB = LR * 16;
 };
 
 // Accumulator rows of a group of g queries: the group fills nqq = ceil(g/16)
