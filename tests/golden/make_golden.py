@@ -1,6 +1,6 @@
 """Regenerate the golden fixtures in tests/golden/ from the reference itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference REFERENCE_TREE]   (default: $ANN_REFERENCE)
 
 quant.npz     the reference builder's quantize_fp8 / quantize_nvfp4
               (ann/builder/build_cuvs_index.py:314-348), imported from the
