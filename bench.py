@@ -17,8 +17,8 @@ device (strong scaling: the corpus is fixed, N GPUs share it).
 (not the headline line): 3 = inner product over FP8-E4M3 rows with row
 scales, d=1024, N=100M from a 4,096-centre mixture, batch 1,024, k=500, no
 filter; 4 = IVF list gather over NVFP4 rows, d=768, N=200M in 65,536 lists
-with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, lists sharded by
-rank; 5 = Hamming over 1,024-bit rows, N=1B (128 GB: one B200 holds it)
+with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, rows sharded by
+rank with lists cut at the boundaries; 5 = Hamming over 1,024-bit rows, N=1B (128 GB: one B200 holds it)
 XOR-perturbed from 65,536 random prototypes at a 5% flip rate, batch 1,024,
 k=100, row-sharded.
 
@@ -51,7 +51,8 @@ WORKLOADS = {
     3: 'config 3: inner-product kNN, FP8-E4M3 codes + per-row scale (absmax/448), d=1024, N=100M from a '
        '4,096-centre Gaussian mixture, batch 1,024, k=500, row-sharded',
     4: 'config 4: IVF gather-scan, NVFP4 (e2m1 + E4M3 scale per 16 + row scale), d=768, N=200M in 65,536 '
-       'lists with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, sharded by list',
+       'lists with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, sharded by row range (lists cut at '
+       'rank boundaries)',
     5: 'config 5: Hamming kNN on 1,024-bit vectors, N=1B rows XOR-perturbed from 65,536 Bernoulli(0.5) '
        'prototypes at a 5% flip rate, batch 1,024, k=100, row-sharded; integer distances, ties by row id',
 }
@@ -448,9 +449,16 @@ def build_config4(args, rank, world, dev):
     sizes[np.argmax(sizes)] += args.rows - sizes.sum()
     offsets = np.zeros(nlists + 1, dtype=np.int64)
     offsets[1:] = np.cumsum(sizes)
-    lb = [nlists * r // world for r in range(world + 1)]        # lists l0..l1 on this rank
-    l0, l1 = lb[rank], lb[rank + 1]
-    lo, hi = int(offsets[l0]), int(offsets[l1])
+    # rows lo..hi of the list-major storage on this rank: equal shares of the
+    # rows, lists cut at the boundaries (Zipf sizes put 27M of the 200M rows
+    # in one list, so shares of whole lists cannot balance). The rank's lists
+    # are l0..l1-1, each clipped to its rows; a list on two ranks is searched
+    # on both and the device merge joins them.
+    bounds = sharded.shard_bounds(args.rows, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    l0 = int(np.searchsorted(offsets, lo, side='right')) - 1
+    l1 = max(l0 + 1, int(np.searchsorted(offsets, hi, side='left')))
+    loc_np = np.clip(offsets[l0:l1 + 1], lo, hi) - lo
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed)
     cent = torch.randn((nlists, args.dims), generator=g, device=dev)
@@ -481,7 +489,7 @@ def build_config4(args, rank, world, dev):
     probes = torch.topk(d2, args.nprobe, dim=1, largest=False).indices
     local = torch.where((probes >= l0) & (probes < l1), probes - l0, torch.full_like(probes, -1))
     local = local.to(torch.int32).contiguous()                  # -1 = UINT32_MAX: padding
-    loc_off = torch.from_numpy(offsets[l0:l1 + 1] - offsets[l0]).to(dev)
+    loc_off = torch.from_numpy(loc_np).to(dev)
     w.inputs = [queries, local]
     w.shard = pb.Shard(pb.NVFP4, args.dims, codes, bscales, rscales, first_id=lo)
     w.metric, w.dtype, w.bound = pb.L2, 'nvfp4->f32', 'hbm'
@@ -494,9 +502,9 @@ def build_config4(args, rank, world, dev):
     hit = torch.zeros(l1 - l0, dtype=torch.bool, device=dev)
     lp = local[local >= 0].long()
     hit[lp] = True
-    lsz = torch.from_numpy(sizes[l0:l1]).to(dev)
+    lsz = torch.from_numpy(np.diff(loc_np)).to(dev)
     w.pass_rows = int(lsz[hit].sum().item())
-    pairs = int(torch.from_numpy(sizes[l0:l1]).to(dev)[lp].sum().item())
+    pairs = int(lsz[lp].sum().item())
     w.pass_flops = 2.0 * pairs * args.dims
 
     def step(q, pr):
@@ -515,7 +523,7 @@ def build_config4(args, rank, world, dev):
         # the probed lists only, re-packed list-major with their global ids
         parts, new_off, ids = [], [0], []
         for l in lists:
-            a, b = int(offsets[l0 + l] - lo), int(offsets[l0 + l + 1] - lo)
+            a, b = int(loc_np[l]), int(loc_np[l + 1])
             parts.append((a, b))
             new_off.append(new_off[-1] + b - a)
             ids.append(np.arange(a, b, dtype=np.int64) + lo)
@@ -773,7 +781,8 @@ def main():
         if cand is not None:
             cfg['candidate_rows'] = cand
         cfg['parallelism'] = ('%s x%d, NCCL all-gather of top-k + device merge' % (
-            'list-sharded' if args.config == 4 else 'row-sharded', world) if world > 1 else 'single GPU')
+            'row-sharded (IVF lists cut at rank boundaries)' if args.config == 4 else 'row-sharded', world)
+            if world > 1 else 'single GPU')
         line = {'metric': METRIC, 'value': value, 'unit': 'queries/s', 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True,
                 'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg,
