@@ -454,11 +454,7 @@ def build_config4(args, rank, world, dev):
     # in one list, so shares of whole lists cannot balance). The rank's lists
     # are l0..l1-1, each clipped to its rows; a list on two ranks is searched
     # on both and the device merge joins them.
-    bounds = sharded.shard_bounds(args.rows, world)
-    lo, hi = bounds[rank], bounds[rank + 1]
-    l0 = int(np.searchsorted(offsets, lo, side='right')) - 1
-    l1 = max(l0 + 1, int(np.searchsorted(offsets, hi, side='left')))
-    loc_np = np.clip(offsets[l0:l1 + 1], lo, hi) - lo
+    lo, hi, l0, l1, loc_np = sharded.ivf_shard(offsets, world, rank)
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed)
     cent = torch.randn((nlists, args.dims), generator=g, device=dev)

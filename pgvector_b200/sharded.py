@@ -18,6 +18,32 @@ def shard_bounds(rows, world, align=32):
     return b
 
 
+def ivf_shard(offsets, world, rank, align=32):
+    """This rank's share of a list-major IVF shard (offsets: the nlists + 1
+    row offsets of its lists): rows [lo, hi) in equal shares, the lists
+    l0 .. l1-1 that meet them, and those lists' offsets clipped to the range
+    (local, from 0). Lists are cut at the boundaries, so one very large list
+    does not unbalance the ranks; a list held by two ranks is searched on
+    both and the merge joins the halves. Returns (lo, hi, l0, l1, local
+    offsets as int64 numpy)."""
+    import numpy as np
+    offsets = np.asarray(offsets, dtype=np.int64)
+    b = shard_bounds(int(offsets[-1]), world, align)
+    lo, hi = b[rank], b[rank + 1]
+    l0 = int(np.searchsorted(offsets, lo, side='right')) - 1
+    l1 = max(l0 + 1, int(np.searchsorted(offsets, hi, side='left')))
+    return lo, hi, l0, l1, np.clip(offsets[l0:l1 + 1], lo, hi) - lo
+
+
+def local_probes(probes, l0, l1):
+    """A probe table ([nq][nprobe] global list numbers, numpy) in a rank's
+    list numbering: lists l0 .. l1-1 become 0 .. l1-l0-1, the others
+    padding (UINT32_MAX)."""
+    import numpy as np
+    p = np.asarray(probes).astype(np.int64)
+    return np.where((p >= l0) & (p < l1), p - l0, 0xffffffff).astype(np.uint32)
+
+
 def bitmap_slice(words, lo, hi):
     """The words covering rows [lo, hi) (lo a multiple of 32) and the bit count."""
     return words[lo // 32:(hi + 31) // 32], hi - lo

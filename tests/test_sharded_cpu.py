@@ -1,7 +1,9 @@
 """The multi-GPU path's host logic on CPU: two gloo ranks shard a corpus by
 row range, search their shard (the CPU oracle stands in for the GPU scan),
 all-gather the per-rank lists in the layout the device merge takes, merge,
-and must equal one search over the whole corpus."""
+and must equal one search over the whole corpus -- for the flat search over
+a filter bitmap and for the IVF list search with lists cut at the rank
+boundaries."""
 import os
 import socket
 
@@ -87,6 +89,70 @@ def test_two_rank_sharded_search_equals_whole(world):
         d, i, c = out[r]
         assert np.array_equal(c, oc.astype(np.int32))
         assert np.array_equal(i, oi) and np.array_equal(d, od)
+
+
+IVF_ROWS, IVF_DIMS, IVF_LISTS, IVF_NQ, IVF_K, IVF_PROBE = 20000, 16, 24, 8, 30, 6
+
+
+def ivf_case():
+    # Zipf(1.6) list sizes: a few large lists, which the row split must cut
+    x, offsets, cent, row_ids = synth.ivf_corpus(IVF_ROWS, IVF_DIMS, IVF_LISTS, zipf=1.6, seed=41)
+    q = (cent[np.arange(IVF_NQ) % IVF_LISTS] + 0.05).astype(np.float32)
+    probes = synth.ivf_probes(q, cent, IVF_PROBE)
+    return x, offsets, row_ids, q, probes
+
+
+def ivf_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    torch.distributed.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        x, offsets, row_ids, q, probes = ivf_case()
+        lo, hi, l0, l1, loc = sharded.ivf_shard(offsets, world, rank)
+        lp = sharded.local_probes(probes, l0, l1)
+        d, i, c = oracle.search_lists(oracle.F32, IVF_DIMS, x[lo:hi], q, loc.astype(np.uint64), lp, IVF_K, 0,
+                                      row_ids=row_ids[lo:hi], threads=1)
+        gd, gi, gc = sharded.gather_lists(torch.from_numpy(d), torch.from_numpy(i),
+                                          torch.from_numpy(c.astype(np.int32)))
+        md, mi, mc = merge_host(gd.numpy(), gi.numpy(), gc.numpy(), IVF_K)
+        out[rank] = (md.numpy(), mi.numpy(), mc.numpy(), hi - lo, l1 - l0)
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize('world', [2])
+def test_ivf_row_range_shards_equal_whole(world):
+    # each rank holds equal rows of the list-major storage with lists cut at
+    # the boundaries; its probes name only the lists it holds (the others are
+    # padding); merging the ranks' lists gives the unsharded IVF search
+    ctx = mp.get_context('spawn')
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    mp.start_processes(ivf_worker, args=(world, free_port(), out), nprocs=world, join=True, start_method='spawn')
+    x, offsets, row_ids, q, probes = ivf_case()
+    od, oi, oc = oracle.search_lists(oracle.F32, IVF_DIMS, x, q, offsets, probes, IVF_K, 0, row_ids=row_ids)
+    assert sum(out[r][3] for r in range(world)) == IVF_ROWS
+    assert sum(out[r][4] for r in range(world)) > IVF_LISTS       # some list is cut
+    for r in range(world):
+        d, i, c = out[r][:3]
+        assert np.array_equal(c, oc.astype(np.int32))
+        for j in range(IVF_NQ):
+            n = int(oc[j])
+            assert np.array_equal(i[j, :n], oi[j, :n]) and np.array_equal(d[j, :n], od[j, :n])
+
+
+def test_ivf_shard_tables():
+    x, offsets, row_ids, q, probes = ivf_case()
+    sizes = np.diff(offsets.astype(np.int64))
+    for world in (1, 2, 3, 8):
+        tot = np.zeros(IVF_LISTS, dtype=np.int64)
+        for r in range(world):
+            lo, hi, l0, l1, loc = sharded.ivf_shard(offsets, world, r)
+            assert loc[0] == 0 and loc[-1] == hi - lo and (np.diff(loc) >= 0).all()
+            tot[l0:l1] += np.diff(loc)
+            lp = sharded.local_probes(probes, l0, l1)
+            held = (probes >= l0) & (probes < l1)
+            assert (lp[held] == probes[held] - l0).all() and (lp[~held] == 0xffffffff).all()
+        assert (tot == sizes).all()
 
 
 def test_shard_bounds_word_aligned():
