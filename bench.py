@@ -46,6 +46,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = 'QPS at batch 1024, k=100 (1/2/4/8 B200); achieved HBM GB/s vs peak'
 WORKLOADS = {
+    1: 'config 1: exact L2 kNN, fp32, d=128, N=100,000 rows from a 100-centre Gaussian mixture (centres ~N(0,1), '
+       'sigma 0.1), 1,000 queries drawn the same way, k=10, no filter (the reference worker\'s CPU-runnable case)',
     2: 'config 2: cosine kNN, halfvec (fp16) d=768, N=10M unit-normalised rows from a 1,000-centre '
        'Gaussian mixture, uniform 10% row-filter bitmap, batch 1,024, k=100',
     3: 'config 3: inner-product kNN, FP8-E4M3 codes + per-row scale (absmax/448), d=1024, N=100M from a '
@@ -56,7 +58,8 @@ WORKLOADS = {
     5: 'config 5: Hamming kNN on 1,024-bit vectors, N=1B rows XOR-perturbed from 65,536 Bernoulli(0.5) '
        'prototypes at a 5% flip rate, batch 1,024, k=100, row-sharded; integer distances, ties by row id',
 }
-DEFAULTS = {2: dict(rows=10_000_000, dims=768, batch=1024, k=100, centres=1000),
+DEFAULTS = {1: dict(rows=100_000, dims=128, batch=1000, k=10, centres=100),
+            2: dict(rows=10_000_000, dims=768, batch=1024, k=100, centres=1000),
             3: dict(rows=100_000_000, dims=1024, batch=1024, k=500, centres=4096),
             4: dict(rows=200_000_000, dims=768, batch=4096, k=100, centres=65536),
             5: dict(rows=1_000_000_000, dims=1024, batch=1024, k=100, centres=65536)}
@@ -68,7 +71,7 @@ def args_parse():
     ap.add_argument('--steps', type=int, default=None, help='timed steps (default 300; 10 for configs 3/4, 5 for 5)')
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument('--config', type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument('--rows', type=int, default=None)
     ap.add_argument('--dims', type=int, default=None)
     ap.add_argument('--batch', type=int, default=None)
@@ -86,7 +89,7 @@ def args_parse():
         if getattr(args, key) is None:
             setattr(args, key, val)
     if args.steps is None:
-        args.steps = {2: 300, 5: 5}.get(args.config, 10)
+        args.steps = {1: 300, 2: 300, 5: 5}.get(args.config, 10)
     return args
 
 
@@ -157,7 +160,7 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU baseline (reference worker code)
 
-METRIC_CODE = {2: 2, 3: 1, 4: 0, 5: 3}   # cosine, inner product, L2, Hamming
+METRIC_CODE = {1: 0, 2: 2, 3: 1, 4: 0, 5: 3}   # L2, cosine, inner product, L2, Hamming
 
 
 def cpu_sample(args, rows, queries):
@@ -172,6 +175,9 @@ def cpu_sample(args, rows, queries):
         rng = np.random.default_rng(args.seed + 7919)
         flips = np.packbits(rng.random((queries, args.dims)) < 0.05, axis=1, bitorder='little')
         return x, proto[rng.integers(0, args.centres, queries)] ^ flips
+    if args.config == 1:
+        return (synth.mixture(rows, args.dims, args.centres, seed=args.seed),
+                synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed))
     if args.config == 2:
         x = synth.mixture(rows, args.dims, args.centres, seed=args.seed, normalize=True).astype(np.float16)
         q = synth.mixture_queries(queries, args.dims, args.centres, seed=args.seed, normalize=True)
@@ -262,7 +268,7 @@ def cpu_measure(args, threads, budget_s=None, count=None):
                 'the per-query work equals the full configuration\'s' %
                 (done, args.k, args.nprobe, rows // max(1, len(sample[3]) - 1), secs, threads))
         return done / secs, desc, kind
-    rows = {2: 50_000, 5: 200_000}.get(args.config, 20_000)
+    rows = {1: args.rows, 2: 50_000, 5: 200_000}.get(args.config, 20_000)   # config 1: the whole corpus
     if args.config not in _SAMPLES:
         _SAMPLES[args.config] = cpu_sample(args, rows, 64)
     x, q = _SAMPLES[args.config]
@@ -340,6 +346,45 @@ def mixture_rows(args, dev, lo, hi, centres, fill, chunk=1 << 20, normalize=Fals
         a, b = max(c0, lo), min(c0 + m, hi)
         fill(a - lo, b - lo, v[a - c0:b - c0])
         del v, lab
+
+
+def build_config1(args, rank, world, dev):
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import sharded, synth
+    w = Workload()
+    bounds = sharded.shard_bounds(args.rows, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    x = synth.mixture(args.rows, args.dims, args.centres, seed=args.seed)      # the CPU sample's rows
+    codes = torch.from_numpy(x[lo:hi]).to(dev)
+    queries = torch.from_numpy(synth.mixture_queries(args.batch, args.dims, args.centres, seed=args.seed)).to(dev)
+    w.inputs = [queries]
+    w.shard = pb.Shard(pb.F32, args.dims, codes, first_id=lo)
+    w.metric, w.dtype, w.bound = pb.L2, 'f32', 'fp32'
+    w.kernel = 'simt_scan<F32> (CUDA cores), filter pass'
+    w.data = 'synthetic (seeded 100-centre Gaussian mixture, sigma 0.1, the same rows as the CPU baseline)'
+    w.row_bytes = args.dims * 4
+    w.profile = 'none'
+    # the corpus (51 MB) fits in L2: every step first overwrites a buffer
+    # twice L2's size, and that time is part of the step
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    w.l2 = 'inputs fit in L2 (%.0f MB): a 256 MB buffer is written before every step, its time included' % (
+        (hi - lo) * args.dims * 4 / 1e6)
+
+    def step(q):
+        flush.fill_(1)
+        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.L2, None)
+        return d, i, c, hi - lo
+    w.step = step
+
+    def verify(result, nq):
+        import numpy as np
+        import oracle
+        od, oi, oc, _ = oracle.search(oracle.F32, args.dims, x, queries[:nq].cpu().numpy(), args.k, 0)
+        return bool(np.array_equal(result[1][:nq].cpu().numpy(), oi) and
+                    np.array_equal(result[0][:nq].cpu().numpy(), od))
+    w.verify = verify if world == 1 else (lambda result, nq: None)
+    return w
 
 
 def build_config2(args, rank, world, dev):
@@ -641,7 +686,8 @@ def main():
     if world > 1:
         dist.init_process_group('nccl', timeout=timedelta(seconds=180), device_id=dev)
     lib = pb.load()
-    w = {2: build_config2, 3: build_config3, 4: build_config4, 5: build_config5}[args.config](args, rank, world, dev)
+    w = {1: build_config1, 2: build_config2, 3: build_config3, 4: build_config4,
+         5: build_config5}[args.config](args, rank, world, dev)
     torch.cuda.synchronize()
 
     def barrier():
@@ -745,6 +791,15 @@ def main():
                     'frac': achieved_tf / (2 * tf_sust), 'traffic': traffic,
                     'peak_source': kind + ' bf16_tflops_sustained x 2 (int8 dense rate)',
                     'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
+    elif w.bound == 'fp32':
+        # FP32 rows are scored on CUDA cores; no measured FP32 figure exists,
+        # so the denominator is the nominal FMA rate at the maximum SM clock
+        mhz = (clock_info or {}).get('sm_max_mhz') or 1965.0
+        fp32 = torch.cuda.get_device_properties(dev).multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+        roofline = {'bound': 'fp32', 'achieved': achieved_tf, 'peak': fp32, 'unit': 'TFLOP/s',
+                    'frac': achieved_tf / fp32, 'traffic': traffic,
+                    'peak_source': 'nominal FP32 FMA rate (SMs x 128 lanes x 2 x max SM clock)',
+                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
     elif w.bound == 'tensor':
         roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
                     'frac': achieved_tf / tf_sust, 'traffic': traffic,
@@ -772,7 +827,7 @@ def main():
             cfg['selectivity'] = args.selectivity
         if args.config == 4:
             cfg.update({'nlist': args.centres, 'nprobe': args.nprobe})
-        cfg['l2'] = 'inputs larger than L2 (%.2f GB of candidate rows a step on rank 0)' % (
+        cfg['l2'] = getattr(w, 'l2', None) or 'inputs larger than L2 (%.2f GB of candidate rows a step on rank 0)' % (
             (w.pass_rows if args.config == 4 else nrows_local) * w.row_bytes / 1e9)
         if cand is not None:
             cfg['candidate_rows'] = cand
