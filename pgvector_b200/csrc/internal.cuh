@@ -377,8 +377,10 @@ void launch_list_items(const ListPlan &p, uint64_t rbegin, uint64_t rend, cudaSt
 void launch_simt_scan_lists(const ListPlan &p, uint64_t rbegin, uint64_t rend, const ScanArgs &a, int sms,
                             cudaStream_t st);
 uint32_t list_plan_scan_launches(uint32_t nlists);
+// query_lo_map: the low BF16 halves of the queries (FP32 rows only, else NULL).
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
-                           const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st);
+                           const CUtensorMap &query_map, const CUtensorMap *query_lo_map, uint32_t kpad, uint32_t bn,
+                           int sms, cudaStream_t st);
 void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows, const uint32_t *ids, uint64_t base,
                         uint64_t stride, uint64_t count, uint8_t *out, cudaStream_t st);
 uint32_t tc_scan_max_queries();
@@ -386,9 +388,11 @@ cudaError_t launch_tc_scan_lists(const ScanArgs &a, const ListPlan &p, uint64_t 
                                  const CUtensorMap &rows_map, const CUtensorMap &scales_map, const __half *q16,
                                  uint32_t kpad, int sms, cudaStream_t st);
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
+// lo_off: FP32 rows on tensor cores -- q16 receives the queries' BF16 high
+// halves and, lo_off elements further, their low halves (0: an FP16 copy).
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         uint32_t *flags, cudaStream_t st);
+                         uint32_t *flags, cudaStream_t st, uint64_t lo_off = 0);
 void launch_fill_thresholds(uint32_t nq, const QueryState &qs, cudaStream_t st);
 void launch_check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t *flags, cudaStream_t st);
 void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, uint32_t k, uint32_t metric,

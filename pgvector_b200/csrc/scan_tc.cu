@@ -38,6 +38,7 @@
 // FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are drained and
 // tensor memory is freed before the kernel returns.
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include "internal.cuh"
 
@@ -166,6 +167,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // Instruction descriptor: FP16 A and B, FP32 accumulator, both K-major.
 __device__ __forceinline__ uint32_t f16_idesc(uint32_t n) {
   return (1u << 4)                  // D format F32
+         | ((n >> 3) << 17)         // N / 8
+         | ((uint32_t)(BM >> 4) << 24);  // M / 16
+}
+// BF16 A and B (both the same type), FP32 accumulator, both K-major: the
+// split FP32 scan.
+__device__ __forceinline__ uint32_t bf16_idesc(uint32_t n) {
+  return (1u << 4)                  // D format F32
+         | (1u << 7) | (1u << 10)   // A, B BF16
          | ((n >> 3) << 17)         // N / 8
          | ((uint32_t)(BM >> 4) << 24);  // M / 16
 }
@@ -316,6 +325,15 @@ template <> struct TcCfg<DT_BIT> {    // 128 bits (16 bytes) a row a k-block -> 
   static constexpr int STG = 3, BSTG = 3, RSTG = 4, RAWB = BM * 16, RAW_X = 16, NT = 192 + 32 * CONV_WARPS;
   static constexpr int RING = STG * STAGE_BYTES;
 };
+// FP32 rows: 64 floats (256 bytes) a row a k-block, split into two BF16
+// tiles (hi = RN(x), lo = RN(x - hi)) against the query's two BF16 halves;
+// a stage holds A hi, A lo, B hi, B lo with at most 128 queries a tile.
+constexpr int F32_BN = 128;
+constexpr int F32_STAGE = 2 * A_BYTES + 2 * F32_BN * 128;
+template <> struct TcCfg<DT_F32> {
+  static constexpr int STG = 2, BSTG = 2, RSTG = 2, RAWB = BM * 256, RAW_X = 64, NT = 192 + 32 * CONV_WARPS;
+  static constexpr int RING = STG * F32_STAGE;
+};
 // FP16 rows named by a candidate list (or a strided sample): 4 gather warps
 // copy them from the shard into the A tiles, TMA loads only the queries.
 // Gathered rows come from random HBM locations and take far longer to land
@@ -404,6 +422,28 @@ __device__ __forceinline__ void convert_stage(const ScanArgs &a, const uint8_t *
         *reinterpret_cast<uint4 *>(atile + sw128_offset(r, 4 * h + j)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
+  } else if (Q == DT_F32) {
+    // 64 floats a row -> a BF16 tile of hi = RN(x) and, A_BYTES further, one
+    // of lo = RN(x - hi) (x - hi is exact in FP32). Unit i: 8 floats of row
+    // r (16-byte chunk c of both tiles).
+#pragma unroll
+    for (int u = 0; u < 1024 / CONV_THREADS; u++) {
+      const uint32_t i = ct + CONV_THREADS * u, r = i >> 3, c = i & 7;
+      const float4 p0 = *reinterpret_cast<const float4 *>(raw + r * 256 + c * 32);
+      const float4 p1 = *reinterpret_cast<const float4 *>(raw + r * 256 + c * 32 + 16);
+      const float x[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(x[2 * j]), h1 = __float2bfloat16_rn(x[2 * j + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(x[2 * j] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(x[2 * j + 1] - __bfloat162float(h1));
+        hw[j] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+        lw[j] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+      }
+      *reinterpret_cast<uint4 *>(atile + sw128_offset(r, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4 *>(atile + A_BYTES + sw128_offset(r, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
   } else if (Q == DT_BIT) {
     // 128 bits a row -> 128 int8: bit b of the k-block's 16 bytes (byte b/8,
     // bit b%8 from the least significant) is element b, +1 if clear, -1 if
@@ -442,19 +482,22 @@ __device__ void drain_ring(uint64_t *bars, int n, uint64_t issued) {
 template <int Q>
 __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
     tc_scan(const __grid_constant__ CUtensorMap rows_map, const __grid_constant__ CUtensorMap query_map,
-            const TcArgs t) {
+            const __grid_constant__ CUtensorMap query_lo_map, const TcArgs t) {
   using C = TcCfg<Q>;
   constexpr int STG = C::STG, BSTG = C::BSTG, RSTG = C::RSTG, RAWB = C::RAWB;
   constexpr int RSTG1 = RSTG > 0 ? RSTG : 1;  // (the FP16 kernels have no raw ring)
-  constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4 || Q == DT_BIT;
+  constexpr bool SPLIT = Q == DT_F32;         // two BF16 halves of rows and queries, three MMAs a K step
+  constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4 || Q == DT_BIT || SPLIT;
+  constexpr int STAGE = SPLIT ? F32_STAGE : STAGE_BYTES;
   constexpr bool GATHER = Q == GF16;
   constexpr int32_t QX = Q == DT_BIT ? 128 : 64;   // query elements a k-block (128 bytes)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // A and B tiles of stage s (separate rings for the gathered kernel)
-  auto a_tile = [&](uint32_t s) { return smem + (GATHER ? s * A_BYTES : s * STAGE_BYTES); };
+  // (split FP32: A hi, A lo, B hi, B lo; the lo tiles follow their hi tiles)
+  auto a_tile = [&](uint32_t s) { return smem + (GATHER ? s * A_BYTES : s * STAGE); };
   auto b_tile = [&](uint32_t s) {
-    return GATHER ? smem + STG * A_BYTES + s * B_BYTES : smem + s * STAGE_BYTES + A_BYTES;
+    return GATHER ? smem + STG * A_BYTES + s * B_BYTES : smem + s * STAGE + (SPLIT ? 2 : 1) * A_BYTES;
   };
   uint8_t *raw = smem + C::RING;
   uint64_t *full = reinterpret_cast<uint64_t *>(raw + RSTG * RAWB);  // A (and B for FP16) ready
@@ -548,7 +591,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = Q == DT_BIT ? i8_idesc(t.bn) : f16_idesc(t.bn);
+      const uint32_t idesc = Q == DT_BIT ? i8_idesc(t.bn) : (SPLIT ? bf16_idesc(t.bn) : f16_idesc(t.bn));
       uint64_t it = 0, tc = 0;
       bool ok = true;
       for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
@@ -572,10 +615,16 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           const uint32_t sb = smem_u32(b_tile(s_b));
 #pragma unroll
           for (uint32_t kk = 0; kk < 4; kk++) {   // K = 16 halves or 32 int8: 32 bytes an MMA
-            if (Q == DT_BIT)
+            if (Q == DT_BIT) {
               tc_mma_i8(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
-            else
+            } else if (SPLIT) {   // hi.hi + hi.lo + lo.hi (lo.lo is left to the error bound)
+              const uint32_t sal = sa + A_BYTES, sbl = sb + F32_BN * 128;
               tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+              tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sbl + kk * 32), idesc, 1u);
+              tc_mma_f16(d_tmem, sw128_desc(sal + kk * 32), sw128_desc(sb + kk * 32), idesc, 1u);
+            } else {
+              tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+            }
           }
           tc_commit(empty + s);
           if (GATHER) tc_commit(bempty + s_b);
@@ -608,8 +657,11 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           break;
         }
         if (ct == 0) {
-          mbar_expect_tx(bfull + s, t.bn * 128u);
+          mbar_expect_tx(bfull + s, (SPLIT ? 2u : 1u) * t.bn * 128u);
           tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * QX), (int32_t)(qt * t.bn), bfull + s);
+          if (SPLIT)
+            tma_load_2d(smem_u32(b_tile(s) + F32_BN * 128), &query_lo_map, (int32_t)(kb * QX), (int32_t)(qt * t.bn),
+                        bfull + s);
           bissued = it + 1;
         }
         got = mbar_wait(rawfull + r, rph, abort, a.flags);
@@ -1318,14 +1370,15 @@ size_t tc_scan_smem_t(uint32_t nq) {
 uint32_t tc_scan_max_queries() { return 4096; }
 
 template <int Q>
-cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_map, const TcArgs &t, int sms,
+cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_map, const CUtensorMap &query_lo_map,
+                        const TcArgs &t, int sms,
                         cudaStream_t st) {
   const size_t smem = tc_scan_smem_t<Q>(t.a.nq);
   cudaError_t e = cudaFuncSetAttribute(tc_scan<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const uint64_t ntiles = t.rtiles * t.qtiles;
   const unsigned grid = (unsigned)(ntiles < (uint64_t)sms ? ntiles : (uint64_t)sms);
-  tc_scan<Q><<<grid, TcCfg<Q>::NT, smem, st>>>(rows_map, query_map, t);
+  tc_scan<Q><<<grid, TcCfg<Q>::NT, smem, st>>>(rows_map, query_map, query_lo_map, t);
   return cudaGetLastError();
 }
 
@@ -1355,7 +1408,11 @@ cudaError_t launch_lists_t(const CUtensorMap &rows_map, const CUtensorMap &scale
 // E4M3 ([rows][dims] bytes, box 64 x 128) or NVFP4 shard ([rows][dims/2]
 // bytes, box 32 x 128), converted to FP16 in shared memory (a.raw_scale
 // must be set: scores are on the raw codes). query_map: the FP16 queries
-// ([qtiles*bn][kpad], box 64 x bn). Bit vectors ([rows][row_bytes], box 16
+// ([qtiles*bn][kpad], box 64 x bn). FP32 rows ([rows][dims] floats, box 64 x
+// 128 unswizzled, dims a multiple of 4) are split on chip into two BF16
+// tiles, hi = RN(x) and lo = RN(x - hi), and scored by three BF16 MMAs a K
+// step (hi.hi + hi.lo + lo.hi) against query_map and *query_lo_map, the
+// queries' two BF16 halves (bn <= 128). Bit vectors ([rows][row_bytes], box 16
 // x 128, row_bytes a multiple of 16) are expanded to +-1 int8 on chip and
 // scored by kind::i8 MMAs against query_map = the int8 query expansion
 // ([qtiles*bn][kpad] bytes, box 128 x bn, 128-byte swizzle); their scores
@@ -1363,7 +1420,9 @@ cudaError_t launch_lists_t(const CUtensorMap &rows_map, const CUtensorMap &scale
 // scales through a.ids / a.base / a.stride. Returns a CUDA error from the
 // launch.
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
-                           const CUtensorMap &query_map, uint32_t kpad, uint32_t bn, int sms, cudaStream_t st) {
+                           const CUtensorMap &query_map, const CUtensorMap *query_lo_map, uint32_t kpad, uint32_t bn,
+                           int sms, cudaStream_t st) {
+  const CUtensorMap &qlo = query_lo_map ? *query_lo_map : query_map;
   TcArgs t;
   t.a = a;
   t.a_row0 = a_row0;
@@ -1375,11 +1434,14 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   if (a.count == 0 || a.nq == 0) return cudaSuccess;
   switch (a.s.dtype) {
     case DT_F16:
-      return (a.ids || a.stride != 1) ? launch_tc_t<GF16>(rows_map, query_map, t, sms, st)
-                                      : launch_tc_t<DT_F16>(rows_map, query_map, t, sms, st);
-    case DT_E4M3: return launch_tc_t<DT_E4M3>(rows_map, query_map, t, sms, st);
-    case DT_NVFP4: return launch_tc_t<DT_NVFP4>(rows_map, query_map, t, sms, st);
-    case DT_BIT: return launch_tc_t<DT_BIT>(rows_map, query_map, t, sms, st);
+      return (a.ids || a.stride != 1) ? launch_tc_t<GF16>(rows_map, query_map, qlo, t, sms, st)
+                                      : launch_tc_t<DT_F16>(rows_map, query_map, qlo, t, sms, st);
+    case DT_E4M3: return launch_tc_t<DT_E4M3>(rows_map, query_map, qlo, t, sms, st);
+    case DT_NVFP4: return launch_tc_t<DT_NVFP4>(rows_map, query_map, qlo, t, sms, st);
+    case DT_BIT: return launch_tc_t<DT_BIT>(rows_map, query_map, qlo, t, sms, st);
+    case DT_F32:
+      if (!query_lo_map || bn > (uint32_t)F32_BN) return cudaErrorInvalidValue;
+      return launch_tc_t<DT_F32>(rows_map, query_map, qlo, t, sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -18,6 +18,8 @@
 // CPU's bit for bit.
 #include <algorithm>
 
+#include <cuda_bf16.h>
+
 #include "internal.cuh"
 
 namespace annb200 {
@@ -310,6 +312,7 @@ struct PrepArgs {
   const float *queries;
   uint32_t nq, dims, metric, kpad;
   int use_q16;
+  uint64_t lo_off;         // FP32 rows: the queries' low BF16 halves start lo_off elements after q16 (0: FP16 copy)
   double gamma;            // relative accumulation error of the approximate scan
   const uint32_t *maxn2;   // shard's largest squared row norm (float bits)
   QueryState qs;
@@ -324,15 +327,28 @@ struct PrepArgs {
 __global__ void prep_queries(PrepArgs p) {
   const uint32_t q = blockIdx.x;
   const float *qv = p.queries + (uint64_t)q * p.dims;
-  __shared__ double red[3][32];
+  __shared__ double red[4][32];
   __shared__ int bad;
   if (threadIdx.x == 0) bad = 0;
   __syncthreads();
-  double r2 = 0.0, t2 = 0.0, n2 = 0.0;
+  double r2 = 0.0, t2 = 0.0, n2 = 0.0, l2 = 0.0;
   for (uint32_t d = threadIdx.x; d < p.kpad || d < p.dims; d += blockDim.x) {
     float x = d < p.dims ? qv[d] : 0.0f;
     if (d < p.dims && !isfinite(x)) bad = 1;
-    if (p.use_q16 && d < p.kpad) {
+    if (p.use_q16 && d < p.kpad && p.lo_off) {
+      // two BF16 halves: hi = RN(x), lo = RN(x - hi); the scan sees hi + lo
+      const __nv_bfloat16 h = __float2bfloat16_rn(x);
+      const float hf = __bfloat162float(h);
+      const __nv_bfloat16 l = __float2bfloat16_rn(x - hf);
+      const float lf = __bfloat162float(l);
+      uint16_t *q16 = reinterpret_cast<uint16_t *>(p.qs.q16);
+      q16[(uint64_t)q * p.kpad + d] = __bfloat16_as_ushort(h);
+      q16[p.lo_off + (uint64_t)q * p.kpad + d] = __bfloat16_as_ushort(l);
+      const double s = (double)hf + (double)lf;
+      t2 += s * s;
+      r2 += ((double)x - s) * ((double)x - s);
+      l2 += (double)lf * (double)lf;
+    } else if (p.use_q16 && d < p.kpad) {
       __half h = __float2half_rn(x);
       p.qs.q16[(uint64_t)q * p.kpad + d] = h;
       double hx = (double)__half2float(h);
@@ -347,19 +363,22 @@ __global__ void prep_queries(PrepArgs p) {
     r2 += __shfl_xor_sync(0xffffffffu, r2, o);
     t2 += __shfl_xor_sync(0xffffffffu, t2, o);
     n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+    l2 += __shfl_xor_sync(0xffffffffu, l2, o);
   }
   if (lane == 0) {
     red[0][warp] = r2;
     red[1][warp] = t2;
     red[2][warp] = n2;
+    red[3][warp] = l2;
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
-  r2 = t2 = n2 = 0.0;
+  r2 = t2 = n2 = l2 = 0.0;
   for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
     r2 += red[0][w];
     t2 += red[1][w];
     n2 += red[2][w];
+    l2 += red[3][w];
   }
   // the reference's query norm: FP64, dimension order (cpu.c:96-101)
   double qn = 0.0;
@@ -369,17 +388,28 @@ __global__ void prep_queries(PrepArgs p) {
     r2 = 0.0;
   }
   const double mx2 = (double)__uint_as_float(*p.maxn2);
-  const double mx = sqrt(mx2), qnorm = sqrt(n2), tnorm = sqrt(t2), rnorm = sqrt(r2);
+  const double mx = sqrt(mx2), qnorm = sqrt(n2), tnorm = sqrt(t2), rnorm = sqrt(r2), lnorm = sqrt(l2);
   const double eps = 1.0 / 1048576.0;  // 2^-20
+  // FP32 rows split into BF16 halves X' = hi + lo, |x - X'| <= 2^-16 |x| +
+  // 2^-134 and |lo| <= 2^-8 |x| + 2^-134 an element; the scan computes
+  // X'.Q' - lo_x.lo_q: |x.q - that| <= ||x|| ||r_q|| (in rnorm) + (2^-16 ||x||
+  // + 2^-134 sqrt(d)) ||Q'|| + (2^-8 ||x|| + 2^-134 sqrt(d)) ||lo_q||, plus
+  // 2^-126 for each of the 3 kpad products in case the tensor core flushes a
+  // subnormal product. Zero for the FP16 copy. (Cosine over FP32 rows is
+  // scored on CUDA cores: these absolute terms would scale with 1/||x||.)
+  const double sd = sqrt((double)p.kpad);
+  const double esplit =
+      p.lo_off ? ldexp(1.0, -16) * tnorm + ldexp(1.0, -8) * lnorm + ldexp(1.0, -134) * sd * (tnorm + lnorm) : 0.0;
+  const double etiny = p.lo_off ? 3.0 * p.kpad * ldexp(1.0, -126) : 0.0;
   double err;
   switch (p.metric) {
     case M_L2: {
-      double edot = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm;
+      double edot = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm + mx * esplit + etiny;
       double span = (mx + qnorm) * (mx + qnorm);
       err = 2.0 * edot + eps * (mx2 + n2 + mx * qnorm) + ((double)p.dims / 8.0 + 8.0) * 1.2e-7 * span;
       break;
     }
-    case M_IP: err = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm; break;
+    case M_IP: err = p.gamma * mx * tnorm + mx * rnorm + eps * mx * qnorm + mx * esplit + etiny; break;
     case M_COS: err = qnorm > 0.0 ? p.gamma * tnorm / qnorm + rnorm / qnorm + 2.0 * eps : 0.0; break;
     default: err = 0.0; break;
   }
@@ -1072,7 +1102,7 @@ void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, u
 
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         uint32_t *flags, cudaStream_t st) {
+                         uint32_t *flags, cudaStream_t st, uint64_t lo_off) {
   if (bits) {
     prep_queries_bits<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
     if (use_q16 && nq)
@@ -1080,7 +1110,7 @@ void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint3
                                             reinterpret_cast<int8_t *>(qs.q16));
     return;
   }
-  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, gamma, maxn2, qs, flags};
+  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, lo_off, gamma, maxn2, qs, flags};
   prep_queries<<<nq, 256, 0, st>>>(p);
 }
 

@@ -186,6 +186,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D FP16 tensor [outer][inner] (row pitch in bytes) read in boxes of
 // box_rows x 64 elements with the 128-byte swizzle tcgen05 operands use.
+// FP32 rows [outer][inner] in unswizzled boxes of 64 floats x 128 rows (the
+// split FP32 tensor scan's raw stage).
+bool encode_f32_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_f16_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch,
                     uint32_t box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
@@ -235,6 +249,7 @@ bool encode_u8_seg_map(CUtensorMap *map, const void *base, uint64_t inner, uint6
 // needs): FP16 rows, and E4M3 / NVFP4 codes converted to FP16 on chip.
 bool tc_format(uint32_t dtype, uint32_t dims, uint64_t row_bytes) {
   switch (dtype) {
+    case DT_F32: return row_bytes % 16 == 0;
     case DT_F16: return dims % 8 == 0;
     case DT_E4M3: return row_bytes % 16 == 0;
     case DT_NVFP4: return row_bytes % 16 == 0;
@@ -247,6 +262,7 @@ bool tc_format(uint32_t dtype, uint32_t dims, uint64_t row_bytes) {
 bool encode_rows_map(CUtensorMap *map, uint32_t dtype, const void *base, uint32_t dims, uint64_t rows,
                      uint64_t pitch) {
   switch (dtype) {
+    case DT_F32: return encode_f32_map(map, base, dims, rows, pitch);
     case DT_F16: return encode_f16_map(map, base, dims, rows, pitch, 128);
     case DT_E4M3: return encode_u8_map(map, base, dims, rows, pitch, 64);
     case DT_NVFP4: return encode_u8_map(map, base, (dims + 1) / 2, rows, pitch, 32);
@@ -263,6 +279,14 @@ uint32_t tc_kpad(const ShardView &v) {
   return v.dtype == DT_BIT ? (uint32_t)((v.row_bytes * 8 + 127) / 128 * 128) : (v.dims + 63) / 64 * 64;
 }
 size_t tc_qelem(const ShardView &v) { return v.dtype == DT_BIT ? 1 : 2; }
+// Queries a tensor-scan tile: at most 128 for FP32 rows (four tiles a stage).
+uint32_t tc_bn(const ShardView &v, uint32_t nq) {
+  return std::min<uint32_t>(v.dtype == DT_F32 ? 128 : 256, (nq + 31) / 32 * 32);
+}
+// Whether the tensor scan serves this shard and metric: FP32 rows only for
+// L2 and inner product (their split's bound has absolute terms a cosine
+// would divide by the row's norm).
+bool tc_metric(const ShardView &v, uint32_t metric) { return v.dtype != DT_F32 || metric != M_COS; }
 bool encode_query_map(CUtensorMap *map, const ShardView &v, const void *q, uint32_t kpad, uint32_t nq_pad,
                       uint32_t bn) {
   if (v.dtype == DT_BIT) return encode_u8_seg_map(map, q, kpad, nq_pad, kpad, bn);
@@ -274,8 +298,9 @@ bool encode_query_map(CUtensorMap *map, const ShardView &v, const void *q, uint3
 // exactly formed FP16 product sum into the FP32 accumulator, so K/16 rounding
 // steps, each allowed 4 ulps (2^-21) of the magnitudes involved. CUDA-core
 // scan: one FP32 rounding per fused multiply-add, allowed 2 ulps each.
-double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims) {
+double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims, bool split = false) {
   if (bits) return 0.0;
+  if (tc && split) return (3.0 * kpad / 16.0 + 2.0) * std::ldexp(1.0, -21);   // three MMAs a K step
   if (tc) return ((double)kpad / 16.0 + 2.0) * std::ldexp(1.0, -21);
   return (double)dims * std::ldexp(1.0, -22);
 }
@@ -510,12 +535,14 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const bool bits = v.dtype == DT_BIT;
   const bool window = flags & ANNB200_WINDOW;
   const uint64_t n = rows ? nrows : v.rows;
-  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
+  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16 && tc_metric(v, metric);
+  const bool split = tc && v.dtype == DT_F32;   // FP32 rows: BF16 halves of rows and queries
   const uint32_t kpad = tc ? tc_kpad(v) : 0;
-  const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
+  const uint32_t bn = tc ? tc_bn(v, nq) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
   const uint32_t nq_pad = qtiles * bn;
-  const double gamma = scan_gamma(bits, tc, kpad, v.dims);
+  const uint64_t lo_off = split ? (uint64_t)nq_pad * kpad : 0;   // the low halves' block
+  const double gamma = scan_gamma(bits, tc, kpad, v.dims, split);
   const bool sample = k > 0 && n > kNoSampleRows;
   const uint64_t stride = sample ? std::max<uint64_t>(1, n / std::max<uint64_t>(kSampleRows, 8ull * k)) : 1;
   const uint64_t S = sample ? n / stride : 0;
@@ -524,7 +551,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   Carver c;
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
                o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
-               o_q16 = c.take<__half>((size_t)nq_pad * kpad), o_mat = c.take<float>((size_t)S * nq),
+               o_q16 = c.take<__half>((size_t)nq_pad * kpad * (split ? 2 : 1)), o_mat = c.take<float>((size_t)S * nq),
                o_cnt = c.take<uint32_t>(nq), o_thr0 = c.take<float>(nq), o_flags = c.take<uint32_t>(16),
                o_big = c.take<uint32_t>(nq), o_exact = c.take<double>((size_t)nq * kSortCap);
   CK(sh->ws.reserve(c.off), "workspace");
@@ -552,9 +579,10 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
   CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
   if (tc && nq_pad > nq)
-    CK(cudaMemsetAsync((uint8_t *)qs.q16 + (size_t)nq * kpad * tc_qelem(v), 0,
-                       (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
-       "memset");
+    for (int half = 0; half < (split ? 2 : 1); half++)   // padding query rows (of both halves) score zero
+      CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)half * lo_off + (size_t)nq * kpad) * tc_qelem(v), 0,
+                         (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
+         "memset");
   StageClock clock(st);
   if (rows) {
     // kernels clamp list entries to the shard; a bad list is reported at the end
@@ -562,7 +590,8 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     counted(1);
   }
   int h = clock.begin(ST_PREP);
-  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, dflags, st);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, dflags, st,
+                      lo_off);
   clock.end(h);
   counted(bits && tc ? 2 : 1);
   CK(cudaGetLastError(), "query preparation");
@@ -573,20 +602,21 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.queries = (const float *)queries;
   a.nq = nq;
   a.metric = metric;
-  a.raw_scale = tc && v.dtype != DT_F16 && !bits;   // tensor scan of quantized rows: scores on raw codes
+  a.raw_scale = tc && (v.dtype == DT_E4M3 || v.dtype == DT_NVFP4);   // scores on raw codes
   a.thr = qs.thr;
   a.cnt = cnt;
   a.flags = dflags;
 
-  CUtensorMap query_map;
-  if (tc && !encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn))
+  CUtensorMap query_map, query_lo_map;
+  if (tc && (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
+             (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn))))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   // One scan launch timed as `stage`. Tensor path: rows come from the shard
   // itself when the candidates are a contiguous run, else from `staged`
   // (virtual row 0 at its first row, filled by gather_rows); FP16 row lists
   // are gathered by the scan itself.
   auto tc_launch = [&](const CUtensorMap &rows_map, int64_t row0) -> cudaError_t {
-    return launch_tc_scan(a, rows_map, row0, query_map, kpad, bn, sh->sms, st);
+    return launch_tc_scan(a, rows_map, row0, query_map, split ? &query_lo_map : nullptr, kpad, bn, sh->sms, st);
   };
   auto scan = [&](int stage, const void *staged) -> cudaError_t {
     int hk = clock.begin(stage);
@@ -1114,14 +1144,16 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   std::lock_guard<std::mutex> lock(sh->mu);
   cudaStream_t st = (cudaStream_t)stream;
   const bool bits = v.dtype == DT_BIT;
-  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16;
+  const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16 && tc_metric(v, metric);
+  const bool split = tc && v.dtype == DT_F32;   // FP32 rows: BF16 halves of rows and queries
   const uint32_t kpad = tc ? tc_kpad(v) : 0;
-  const uint32_t bn = tc ? std::min<uint32_t>(256, (nq + 31) / 32 * 32) : 0;
+  const uint32_t bn = tc ? tc_bn(v, nq) : 0;
   const uint32_t nq_pad = tc ? (nq + bn - 1) / bn * bn : 0;
+  const uint64_t lo_off = split ? (uint64_t)nq_pad * kpad : 0;
   Carver c;
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
                o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
-               o_q16 = c.take<__half>((size_t)nq_pad * kpad), o_flags = c.take<uint32_t>(16);
+               o_q16 = c.take<__half>((size_t)nq_pad * kpad * (split ? 2 : 1)), o_flags = c.take<uint32_t>(16);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
   QueryState qs;
@@ -1135,12 +1167,13 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   uint32_t *dflags = (uint32_t *)(w + o_flags);
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
   if (tc && nq_pad > nq)
-    CK(cudaMemsetAsync((uint8_t *)qs.q16 + (size_t)nq * kpad * tc_qelem(v), 0,
-                       (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
-       "memset");
+    for (int half = 0; half < (split ? 2 : 1); half++)
+      CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)half * lo_off + (size_t)nq * kpad) * tc_qelem(v), 0,
+                         (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
+         "memset");
   if (rows) launch_check_rows(rows, nrows, v.rows, dflags, st);
-  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, scan_gamma(bits, tc, kpad, v.dims),
-                      sh->maxn2, qs, bits, dflags, st);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc,
+                      scan_gamma(bits, tc, kpad, v.dims, split), sh->maxn2, qs, bits, dflags, st, lo_off);
   counted(bits && tc ? 2 : 1);
   ScanArgs a{};
   a.s = v;
@@ -1155,13 +1188,14 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.mat = out;
   a.mat_ld = n;
   a.flags = dflags;
-  a.raw_scale = tc && v.dtype != DT_F16 && !bits;
+  a.raw_scale = tc && (v.dtype == DT_E4M3 || v.dtype == DT_NVFP4);
   if (tc) {
-    CUtensorMap query_map;
-    if (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn))
+    CUtensorMap query_map, query_lo_map;
+    if (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
+        (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn)))
       return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
     auto tc_launch = [&](const CUtensorMap &rows_map) -> cudaError_t {
-      return launch_tc_scan(a, rows_map, 0, query_map, kpad, bn, sh->sms, st);
+      return launch_tc_scan(a, rows_map, 0, query_map, split ? &query_lo_map : nullptr, kpad, bn, sh->sms, st);
     };
     if (!rows || v.dtype == DT_F16) {
       CK(tc_launch(sh->rows_map), "score scan");   // FP16 row lists: gathered by the scan

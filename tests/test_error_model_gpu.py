@@ -92,3 +92,34 @@ def test_hamming_scores_are_exact(cuda):
     ex = np.unpackbits(qs[:, None, :] ^ rows[None, :, :], axis=2).sum(2)
     assert np.array_equal(approx.cpu().numpy(), ex.astype(np.float32))
     assert (err.cpu().numpy() == 0).all()
+
+
+@pytest.mark.parametrize('dims', [128, 200])
+@pytest.mark.parametrize('metric', [1, 0, 2])
+@pytest.mark.parametrize('simt', [False, True])
+def test_bound_holds_on_f32_rows(cuda, dims, metric, simt):
+    # FP32 rows on tensor cores are split into two BF16 halves (L2 and inner
+    # product; cosine scores on CUDA cores); columns scaled over many binades
+    # and a few subnormal elements exercise the split's relative and absolute
+    # terms
+    import torch
+    import pgvector_b200 as pb
+    n, nq = 12000, 128
+    x = synth.mixture(n, dims, 40, seed=44 + dims)
+    q = synth.mixture_queries(nq, dims, 40, seed=44 + dims)
+    scale = np.ones(dims, dtype=np.float32)
+    scale[::7] = 1e-6
+    scale[3::11] = 300.0
+    x *= scale
+    x[::97, 5] = np.float32(1e-40)
+    shard = pb.Shard(pb.F32, dims, torch.from_numpy(x).to(cuda))
+    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), metric, force_simt=simt)
+    approx = approx.cpu().numpy().astype(np.float64)
+    err = err.cpu().numpy()
+    ex = exact(x.astype(np.float64), q.astype(np.float64), metric)
+    diff = np.abs(approx - ex)
+    ratio = (diff / err[:, None]).max()
+    print('f32 dims %d metric %d simt %s: max |approx - exact| = %.3g, max ratio to bound = %.4f'
+          % (dims, metric, simt, diff.max(), ratio))
+    assert (diff <= err[:, None]).all()
+    assert ratio < 0.5

@@ -156,6 +156,26 @@ def test_quantized_tensor_and_simt_paths(cuda, dtype, dims, simt):
     assert_same(cuda, dtype, dims, codes, q, 20, 2, ids=ids, bs=bs, rs=rs, window=True, force_simt=simt)
 
 
+@pytest.mark.parametrize('dims', [128, 200, 36, 37])
+@pytest.mark.parametrize('simt', [False, True])
+def test_f32_split_tensor_and_simt_paths(cuda, dims, simt):
+    # FP32 rows whose pitch is a multiple of 16 bytes (dims % 4 == 0) score on
+    # tensor cores as two BF16 halves (hi.hi + hi.lo + lo.hi) for L2 and inner
+    # product; cosine, 37 dims and ANNB200_FORCE_SIMT use CUDA cores. Whole
+    # shard, a row list (staged rows), window mode, and columns over many
+    # binades with a few subnormal elements.
+    x = synth.mixture(30000, dims, 64, seed=80 + dims)
+    q = synth.mixture_queries(40, dims, 64, seed=80 + dims)
+    x[:, ::5] *= np.float32(1e-5)
+    x[::101, 1] = np.float32(2e-40)
+    x[7000:7200] = x[55]                          # duplicates: ties ordered by row id
+    _, ids = synth.bitmap(30000, 0.3, seed=81)
+    for metric in (0, 1, 2):
+        assert_same(cuda, oracle.F32, dims, x, q, 50, metric, force_simt=simt)
+    assert_same(cuda, oracle.F32, dims, x, q, 20, 0, ids=ids, force_simt=simt)
+    assert_same(cuda, oracle.F32, dims, x, q[:16], 10, 1, ids=ids[:3000], window=True, force_simt=simt)
+
+
 def test_hamming_bit_exact_with_ties(cuda):
     rows, proto = synth.bit_rows(60000, 1024, 256, flip=0.05, seed=9)
     rng = np.random.default_rng(9)
