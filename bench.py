@@ -16,9 +16,10 @@ device (strong scaling: the corpus is fixed, N GPUs share it).
 --config 3 / 4 / 5 measure the other GPU-sized configurations the same way
 (not the headline line): 3 = inner product over FP8-E4M3 rows with row
 scales, d=1024, N=100M from a 4,096-centre mixture, batch 1,024, k=500, no
-filter; 4 = IVF list gather over NVFP4 rows, d=768, N=200M in 65,536 lists
-with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2, rows sharded by
-rank with lists cut at the boundaries; 5 = Hamming over 1,024-bit rows, N=1B (128 GB: one B200 holds it)
+filter; 4 = IVF search over NVFP4 rows, d=768, N=200M in 65,536 lists
+with Zipf(1.1) sizes, nprobe=64, batch 4,096, k=100, L2 (each step probes the
+FP32 centres, then gathers the probed lists), rows sharded by rank with lists
+cut at the boundaries; 5 = Hamming over 1,024-bit rows, N=1B (128 GB: one B200 holds it)
 XOR-perturbed from 65,536 random prototypes at a 5% flip rate, batch 1,024,
 k=100, row-sharded.
 
@@ -525,13 +526,17 @@ def build_config4(args, rank, world, dev):
     g.manual_seed(args.seed + 7919)
     qlab = torch.randint(0, nlists, (args.batch,), generator=g, device=dev)
     queries = (cent[qlab] + 0.1 * torch.randn((args.batch, args.dims), generator=g, device=dev)).contiguous()
-    # coarse probe (outside the timed step): nprobe nearest centroids
-    d2 = (cent * cent).sum(1)[None, :] - 2.0 * queries @ cent.T
-    probes = torch.topk(d2, args.nprobe, dim=1, largest=False).indices
-    local = torch.where((probes >= l0) & (probes < l1), probes - l0, torch.full_like(probes, -1))
-    local = local.to(torch.int32).contiguous()                  # -1 = UINT32_MAX: padding
+    # coarse probe, part of every step: the nprobe nearest centres of each
+    # query (an exact search of the FP32 centres, AnnB200ProbeLists), then
+    # this rank's lists renumbered and the others padding (-1 = UINT32_MAX)
+    centres = pb.Shard(pb.F32, args.dims, cent.contiguous())
+
+    def rank_probes(q):
+        pr = centres.probe_lists(q, args.nprobe, pb.L2)
+        return torch.where((pr >= l0) & (pr < l1), pr - l0, torch.full_like(pr, -1)).contiguous()
+    local = rank_probes(queries)
     loc_off = torch.from_numpy(loc_np).to(dev)
-    w.inputs = [queries, local]
+    w.inputs = [queries]
     w.shard = pb.Shard(pb.NVFP4, args.dims, codes, bscales, rscales, first_id=lo)
     w.metric, w.dtype, w.bound = pb.L2, 'nvfp4->f32', 'hbm'
     w.kernel = 'tc_scan_lists<NVFP4>, list pass'
@@ -548,8 +553,8 @@ def build_config4(args, rank, world, dev):
     pairs = int(lsz[lp].sum().item())
     w.pass_flops = 2.0 * pairs * args.dims
 
-    def step(q, pr):
-        d, i, c = w.shard.search_lists(q, args.k, pb.L2, loc_off, pr)
+    def step(q):
+        d, i, c = w.shard.search_lists(q, args.k, pb.L2, loc_off, rank_probes(q))
         if world > 1:
             gd, gi, gc = sharded.gather_lists(d, i, c)
             return pb.merge_topk(gd, gi, gc, args.k) + (w.pass_rows,)
@@ -709,9 +714,9 @@ def main():
     for _ in range(args.warmup):
         w.step(*w.inputs)
     barrier()
-    stage_ms = (ctypes.c_double * 9)()
-    stage_calls = (ctypes.c_ulonglong * 9)()
-    lib.AnnB200StageTimes(stage_ms, stage_calls, 9, 1)
+    stage_ms = (ctypes.c_double * 10)()
+    stage_calls = (ctypes.c_ulonglong * 10)()
+    lib.AnnB200StageTimes(stage_ms, stage_calls, 10, 1)
     launches0 = lib.AnnB200LaunchCount()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -724,7 +729,7 @@ def main():
     barrier()
     clock_info = clocks.stop() if clocks else None
     launches = lib.AnnB200LaunchCount() - launches0
-    lib.AnnB200StageTimes(stage_ms, stage_calls, 9, 0)
+    lib.AnnB200StageTimes(stage_ms, stage_calls, 10, 0)
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = args.steps * args.batch / (ms / 1e3)
     result = out
@@ -780,7 +785,8 @@ def main():
         for line in open(tpath):
             if line.startswith('traffic_bytes_per_row:'):
                 traffic = float(line.split(':', 1)[1]) * (w.pass_rows if args.config == 4 else nrows_local)
-    stage_names = ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge', 'gather']
+    stage_names = ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge', 'gather',
+                   'probe']
     common = {'kernel': '%s (%d launches a step)' % (w.kernel, round(stage_calls[3] / args.steps)),
               'pass_ms': pass_ms, 'flops_per_pass': flops, 'algorithmic_bytes_per_pass': bytes_alg,
               'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(stage_names)}}

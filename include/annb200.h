@@ -160,6 +160,22 @@ int			AnnB200SearchLists(AnnB200Shard *shard, const float *queries, uint32_t nq,
 							   int32_t *status, void *stream);
 
 /*
+ * IVF coarse probe: each query's nprobe nearest list centroids -- the list
+ * selection of the reference's IVFFlat scan (GetScanLists,
+ * src/ivfscan.c:48-122: score every centroid, keep the nprobe nearest). The
+ * centroids are a shard (row l = list l's centre; FP32 as the index stores
+ * them, or any vector format); probes (device u32 [nq][nprobe]) receives the
+ * list numbers (row - first_id) ordered by (exact distance, list number),
+ * UINT32_MAX past the number of lists -- the probe table AnnB200SearchLists
+ * takes. Where the reference's heap leaves the choice among lists at an
+ * exactly equal distance open, the lower list number is kept. Metrics L2,
+ * IP, cosine; nprobe <= 4096. Synchronous.
+ */
+int			AnnB200ProbeLists(AnnB200Shard *centroids, const float *queries, uint32_t nq,
+							  uint32_t nprobe, uint32_t metric, uint32_t *probes, int32_t *status,
+							  void *stream);
+
+/*
  * The approximate score matrix the scan prunes with (the reference's
  * score-matrix route, score_mma_* / AnnBlackwellScore,
  * ann/server/blackwell.c:289-525,1066-1110): out [nq][n] FP32 approximate
@@ -257,11 +273,12 @@ unsigned long long AnnB200LaunchCount(void);
  * order: 0 query preparation, 1 sample scan, 2 sample bound, 3 filter scan,
  * 4 tighten, 5 finalize (exact rescoring and ordering), 6 bitmap expansion,
  * 7 merge, 8 candidate-row gather (copies rows for the tensor scan; its time
- * is also inside stages 1 and 3). Fills up to n entries of ms (milliseconds)
- * and calls; reset clears the totals. Returns the number of stages, or 0
- * when timing is off.
+ * is also inside stages 1 and 3), 9 coarse probe (AnnB200ProbeLists: its
+ * centroid search's stages are all counted here). Fills up to n entries of
+ * ms (milliseconds) and calls; reset clears the totals. Returns the number
+ * of stages, or 0 when timing is off.
  */
-#define ANNB200_STAGES 9
+#define ANNB200_STAGES 10
 int			AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset);
 
 #ifdef __cplusplus

@@ -119,6 +119,19 @@ class Shard:
                                         _ptr(count), _ptr(status), _stream(stream)))
         return dist, ids, count
 
+    def probe_lists(self, queries, nprobe, metric, stream=None, status=None):
+        """IVF coarse probe on a shard of list centroids (row l = list l's
+        centre): each query's nprobe nearest lists as an int32 [nq][nprobe]
+        CUDA tensor of u32 list numbers (-1 = UINT32_MAX past the number of
+        lists), ordered by (distance, list) -- the probe table search_lists
+        takes."""
+        import torch
+        nq = int(queries.shape[0])
+        probes = torch.empty((nq, max(int(nprobe), 1)), dtype=torch.int32, device=queries.device)
+        check(load().AnnB200ProbeLists(self._handle, _ptr(queries), nq, int(nprobe), int(metric), _ptr(probes),
+                                       _ptr(status), _stream(stream)))
+        return probes
+
     def score_matrix(self, queries, metric, rows=None, force_simt=False, stream=None):
         """Approximate distances [nq][n] (squared for L2) and each query's
         error bound, as the scan computes them."""

@@ -34,6 +34,7 @@ SIGNATURES = {
     'AnnB200SearchLists': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, c_uint32,
                                    c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_void_p]),
+    'AnnB200ProbeLists': (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
     'AnnB200IndexCreate': (c_int, [ctypes.c_int, c_uint32, c_uint64, c_void_p, ctypes.POINTER(c_void_p)]),
     'AnnB200IndexDestroy': (None, [c_void_p]),
     'AnnB200IndexSearch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_void_p, c_void_p,

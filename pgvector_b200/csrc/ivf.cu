@@ -266,7 +266,23 @@ __global__ void __launch_bounds__(256) simt_scan_lists(const ListPlan p, uint64_
   }
 }
 
+// Probe table from a centroid search's results: entry j of query q is the
+// list (id - first) of its j-th nearest centroid, UINT32_MAX past the count.
+__global__ void probe_table(const int64_t *ids, const uint32_t *counts, uint32_t nq, uint32_t nprobe, int64_t first,
+                            uint32_t *probes) {
+  const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (uint64_t)nq * nprobe) return;
+  const uint32_t q = (uint32_t)(i / nprobe), j = (uint32_t)(i % nprobe);
+  probes[i] = j < counts[q] ? (uint32_t)(ids[i] - first) : kNoProbe;
+}
+
 }  // namespace
+
+void launch_probe_table(const int64_t *ids, const uint32_t *counts, uint32_t nq, uint32_t nprobe, int64_t first,
+                        uint32_t *probes, cudaStream_t st) {
+  const uint64_t n = (uint64_t)nq * nprobe;
+  if (n) probe_table<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, counts, nq, nprobe, first, probes);
+}
 
 // Invert the probe table: lcount, qoff, qlist (queries of each list). Marks
 // queries with bad probes invalid and flags bad offsets.

@@ -113,7 +113,11 @@ struct Carver {
 
 // ---- launch counting and stage timing (ANN_B200_KERNEL_TIMING=1)
 std::atomic<unsigned long long> g_launches{0};
-enum Stage { ST_PREP, ST_SAMPLE, ST_BOUND, ST_FILTER, ST_TIGHTEN, ST_FINAL, ST_BITMAP, ST_MERGE, ST_GATHER, ST_COUNT };
+enum Stage { ST_PREP, ST_SAMPLE, ST_BOUND, ST_FILTER, ST_TIGHTEN, ST_FINAL, ST_BITMAP, ST_MERGE, ST_GATHER, ST_PROBE,
+             ST_COUNT };
+// A call that books every stage of the work it runs to one stage (the
+// coarse probe's centroid search) sets this for its duration.
+thread_local int g_stage_override = -1;
 std::mutex g_stage_mu;
 double g_stage_ms[ST_COUNT];
 unsigned long long g_stage_calls[ST_COUNT];
@@ -143,6 +147,7 @@ struct StageClock {
   explicit StageClock(cudaStream_t s) : st(s), on(timing_on()) {}
   int begin(int stage) {
     if (!on) return -1;
+    if (g_stage_override >= 0) stage = g_stage_override;
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
@@ -838,6 +843,41 @@ extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq,
     if (r != OK) return r;
   }
   if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  return OK;
+}
+
+// The coarse probe: each query's nprobe nearest centroids, as a search of
+// the centroid shard with k = nprobe (exact distances, ties by list number),
+// then the results' ids as list numbers. Scratch for those results is a
+// buffer of this host thread on this device, so the shard's lock is taken
+// only by the search.
+extern "C" int AnnB200ProbeLists(AnnB200Shard *centroids, const float *queries, uint32_t nq, uint32_t nprobe,
+                                 uint32_t metric, uint32_t *probes, int32_t *status, void *stream) {
+  if (!centroids) return fail(INVALID, "centroid shard is NULL");
+  if (nq == 0) return OK;
+  if (!queries || !probes) return fail(INVALID, "NULL query or probe pointer");
+  if (nprobe == 0 || nprobe > kMaxProbes) return fail(UNSUPPORTED, "nprobe %u outside 1 .. %u", nprobe, kMaxProbes);
+  if (centroids->view.dtype == DT_BIT || metric > M_COS)
+    return fail(UNSUPPORTED, "coarse probe takes vector centroids and metric L2, IP or cosine");
+  DeviceGuard g(centroids->device);
+  static thread_local DeviceBuffer scratch[64];
+  if (centroids->device < 0 || centroids->device >= 64) return fail(UNSUPPORTED, "device %d", centroids->device);
+  DeviceBuffer &w = scratch[centroids->device];
+  const size_t pairs = (size_t)nq * nprobe;
+  CK(w.reserve(pairs * (sizeof(double) + sizeof(int64_t)) + (size_t)nq * sizeof(uint32_t)), "probe scratch");
+  double *dist = (double *)w.p;
+  int64_t *ids = (int64_t *)(dist + pairs);
+  uint32_t *counts = (uint32_t *)(ids + pairs);
+  g_stage_override = ST_PROBE;
+  int r = AnnB200Search(centroids, queries, nq, nullptr, 0, nprobe, metric, 0, nprobe, dist, ids, counts, status,
+                        stream);
+  g_stage_override = -1;
+  if (r != OK) return r;
+  launch_probe_table(ids, counts, nq, nprobe, centroids->first, probes, (cudaStream_t)stream);
+  counted(1);
+  CK(cudaGetLastError(), "probe table");
+  // the scratch is reused by this thread's next call, on whatever stream
+  CK(cudaStreamSynchronize((cudaStream_t)stream), "probe table");
   return OK;
 }
 

@@ -169,3 +169,57 @@ def test_padding_probes_and_list_shards(cuda, dtype):
     md, mi, mc = pb.merge_topk(gd, gi, gc, 25)
     assert np.array_equal(mc.cpu().numpy(), oc.astype(np.int32))
     assert np.array_equal(mi.cpu().numpy(), oi) and np.array_equal(md.cpu().numpy(), od)
+
+
+def oracle_probes(dtype, dims, centres, q, nprobe, metric):
+    # the nprobe nearest centroids by (exact distance, list number), padding past the lists
+    od, oi, oc, _ = oracle.search(dtype, dims, centres, q, nprobe, metric)
+    want = np.full((q.shape[0], nprobe), 0xffffffff, dtype=np.uint32)
+    for j in range(q.shape[0]):
+        want[j, :oc[j]] = oi[j, :oc[j]]
+    return want
+
+
+@pytest.mark.parametrize('dtype', [0, 1])
+@pytest.mark.parametrize('nq', [48, 8])
+def test_coarse_probe_matches_oracle(cuda, dtype, nq):
+    # the coarse probe (src/ivfscan.c:48-122) as an exact search of the
+    # centroids: 48 queries take the tensor scan (FP32 centres as two BF16
+    # halves, or FP16), 8 the CUDA-core scan; a duplicated centre makes an
+    # exact tie at the boundary (the lower list number is kept)
+    import pgvector_b200 as pb
+    rng = np.random.default_rng(90 + dtype)
+    cent = rng.standard_normal((3000, 64)).astype(np.float32)
+    cent[100] = cent[7]
+    q = (cent[rng.integers(0, 3000, nq)] + 0.3 * rng.standard_normal((nq, 64))).astype(np.float32)
+    q[0] = cent[7] + np.float32(0.01)
+    codes, _, _ = encode(dtype, cent)
+    shard = pb.Shard(dtype, 64, to_dev(codes, cuda))
+    qd = to_dev(q, cuda)
+    for metric in (0, 1, 2):
+        for nprobe in (1, 16, 64):
+            got = shard.probe_lists(qd, nprobe, metric).cpu().numpy().view(np.uint32)
+            assert np.array_equal(got, oracle_probes(dtype, 64, codes, q, nprobe, metric)), (metric, nprobe)
+    few = pb.Shard(dtype, 64, to_dev(codes[:10], cuda))           # fewer lists than probes: padding
+    got = few.probe_lists(qd, 16, 0).cpu().numpy().view(np.uint32)
+    assert np.array_equal(got, oracle_probes(dtype, 64, codes[:10], q, 16, 0))
+    assert (got[:, 10:] == 0xffffffff).all()
+
+
+def test_probe_then_list_scan_end_to_end(cuda):
+    # queries -> coarse probe on the FP32 centres -> list scan: equals the
+    # oracle's list scan over the oracle's probes
+    import pgvector_b200 as pb
+    x, offsets, cent, row_ids = synth.ivf_corpus(40000, 96, 256, seed=95)
+    q = (cent[np.random.default_rng(96).integers(0, 256, 40)] + 0.05).astype(np.float32)
+    codes = synth.to_half_bits(x)
+    centres = pb.Shard(pb.F32, 96, to_dev(cent.astype(np.float32), cuda))
+    rows = pb.Shard(pb.F16, 96, to_dev(codes, cuda))
+    qd = to_dev(q, cuda)
+    probes = centres.probe_lists(qd, 12, 0)
+    d, i, c = rows.search_lists(qd, 30, 0, to_dev(offsets, cuda), probes, row_ids=to_dev(row_ids, cuda))
+    want = oracle_probes(0, 96, cent.astype(np.float32), q, 12, 0)
+    assert np.array_equal(probes.cpu().numpy().view(np.uint32), want)
+    od, oi, oc = oracle.search_lists(oracle.F16, 96, codes, q, offsets, want, 30, 0, row_ids=row_ids)
+    assert np.array_equal(c.cpu().numpy(), oc.astype(np.int32))
+    assert np.array_equal(i.cpu().numpy(), oi) and np.array_equal(d.cpu().numpy(), od)
