@@ -712,6 +712,33 @@ __global__ void __launch_bounds__(128) rescore_thread(SelectArgs a, unsigned lon
 // buffered. exact[q * kSortCap + i] receives ordered keys. Needs a row pitch
 // that is a multiple of 16 bytes (and 16-byte aligned rows).
 constexpr int RS_WARPS = 4;
+
+// Four E4M3 codes -> their values (exact: every E4M3 value is an FP16 value).
+__device__ __forceinline__ void e4m3x4_values(uint32_t w, float (&v)[4]) {
+  uint32_t o0, o1;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(o0), "=r"(o1)
+      : "r"(w));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&o0));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&o1));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+// Eight E2M1 codes (low nibble first) -> their values (exact in FP16).
+__device__ __forceinline__ void e2m1x8_values(uint32_t w, float (&v)[8]) {
+  uint32_t o[4];
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&o[j]));
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
 constexpr int RS_STRIDE = 144;  // bytes a staged row chunk: 128 + 16 of padding (bank-conflict free)
 
 template <int DT>
@@ -750,6 +777,8 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
   uint32_t ham = 0;
   const uint32_t dims = s.dims;
   const uint8_t *qb = reinterpret_cast<const uint8_t *>(qv);
+  const bool qvec = (reinterpret_cast<uintptr_t>(qv) & 15u) == 0;   // the query read 16 bytes at a time
+  float bs = 0.0f;                                                   // NVFP4: the current 16-dim block's scale
   uint4 v[8];
   load_chunk(0, v);
   for (uint32_t c = 0; c < chunks; c++) {
@@ -793,32 +822,51 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
             x[2 * j + 1] = f.y;
           }
         } else if (DT == DT_E4M3) {
+          // code values by the hardware conversion, then the reference's FP32 product with the row scale
           const uint2 w = *reinterpret_cast<const uint2 *>(mine_chunk + g * 8);
+          float lo[4], hi[4];
+          e4m3x4_values(w.x, lo);
+          e4m3x4_values(w.y, hi);
 #pragma unroll
-          for (int j = 0; j < 8; j++) x[j] = __fmul_rn(e4m3_value(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu), rs);
+          for (int j = 0; j < 4; j++) {
+            x[j] = __fmul_rn(lo[j], rs);
+            x[4 + j] = __fmul_rn(hi[j], rs);
+          }
         } else {
           const uint32_t w = *reinterpret_cast<const uint32_t *>(mine_chunk + g * 4);
-          const float bs = __fmul_rn(e4m3_value(__ldg(s.bscales + id * s.bblocks + d / 16)), rs);
+          if ((d & 15u) == 0) bs = __fmul_rn(e4m3_value(__ldg(s.bscales + id * s.bblocks + d / 16)), rs);
+          float e[8];
+          e2m1x8_values(w, e);
 #pragma unroll
-          for (int j = 0; j < 8; j++) x[j] = __fmul_rn(e2m1_value((w >> (4 * j)) & 0xfu), bs);
+          for (int j = 0; j < 8; j++) x[j] = __fmul_rn(e[j], bs);
+        }
+        float qx[8];
+        if (qvec && d + 8 <= dims) {
+          const float4 q0 = *reinterpret_cast<const float4 *>(qv + d);
+          const float4 q1 = *reinterpret_cast<const float4 *>(qv + d + 4);
+          qx[0] = q0.x; qx[1] = q0.y; qx[2] = q0.z; qx[3] = q0.w;
+          qx[4] = q1.x; qx[5] = q1.y; qx[6] = q1.z; qx[7] = q1.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) qx[j] = d + j < dims ? qv[d + j] : 0.0f;
         }
         if (a.metric == M_L2) {
           if (d + 8 <= dims) {
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-              float diff = __fsub_rn(x[j], qv[d + j]);
+              float diff = __fsub_rn(x[j], qx[j]);
               sums[j] = __fadd_rn(sums[j], __fmul_rn(diff, diff));
             }
           } else {
             for (int j = 0; d + j < dims; j++) {
-              float diff = __fsub_rn(x[j], qv[d + j]);
+              float diff = __fsub_rn(x[j], qx[j]);
               tail = __fadd_rn(tail, __fmul_rn(diff, diff));
             }
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 8; j++)
-            if (d + j < dims) dot = __dadd_rn(dot, __dmul_rn((double)x[j], (double)qv[d + j]));
+            if (d + j < dims) dot = __dadd_rn(dot, __dmul_rn((double)x[j], (double)qx[j]));
         }
       }
     }
