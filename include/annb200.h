@@ -261,6 +261,47 @@ int			AnnB200IndexSearch(AnnB200Index *index, const float *queries, uint32_t nq,
 							   float *out_dist, uint64_t *out_ordinal, uint32_t *out_count);
 
 /*
+ * A loaded index served from its quantized copy (manifest line
+ * "quant fp8|nvfp4": vectors.e4m3 or vectors.nvfp4 + scales.e4m3, and
+ * rowscale.f32, ann/common/INDEX_FORMAT.md; mapped by AnnIndexFileOpen,
+ * ann/server/indexfile.c:2492-2507), for indexes whose FP32 rows do not fit
+ * on the device. The codes and scales of each index shard go to the device
+ * as one shard (AnnBlackwellUpload, ann/server/blackwell.c:961-1064, with
+ * no repacking: the tensor-core scan reads the file's layout); the FP32 rows
+ * (vectors.f32) stay in host memory, borrowed until AnnB200IndexDestroy.
+ *
+ * dtype ANNB200_E4M3 or ANNB200_NVFP4; block_scales NVFP4 only; nshards
+ * index shards of shard_rows[s] consecutive rows (nshards 0: one shard).
+ * AnnB200IndexSearch on such an index is the reference's quantized scan
+ * route (SearchGather, ann/server/cuvs.c:4585-4930): in each index shard
+ * the min(k + slack, eligible) rows nearest to the query by the exact L2
+ * distance of the decoded rows (ties by ordinal), slack = max(quant_slack,
+ * k * slack_ratio / 100) (GatherSlack, ann/server/cuvs.c:4286-4296); their
+ * FP32 rows re-scored on the device as the reference re-scores them
+ * (ExactDistance, ann/server/cuvs.c:2930-2942); the best k of all shards by
+ * (distance, ordinal). Like the reference's, the answer is the exact one
+ * whenever the true k nearest are among each shard's candidates.
+ */
+int			AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype,
+									const void *codes, const void *block_scales,
+									const float *row_scales, const float *vectors,
+									uint32_t nshards, const uint64_t *shard_rows,
+									uint32_t quant_slack, uint32_t slack_ratio,
+									AnnB200Index **index);
+
+/*
+ * The FP32 re-score of gathered candidate rows (device memory, current
+ * device): out[q][j] = ExactDistance of rows[q][j] to queries[q]
+ * (ann/server/cuvs.c:2930-2942: differences and squares in FP64 summed in
+ * dimension order, the square root rounded to FP32) for j < counts[q]
+ * (counts NULL: all stride). queries [nq][dims], rows [nq][stride][dims],
+ * out [nq][stride] FP32. Asynchronous on stream.
+ */
+int			AnnB200RescoreRows(const float *queries, uint32_t nq, uint32_t dims,
+							   const float *rows, uint32_t stride, const uint32_t *counts,
+							   float *out, void *stream);
+
+/*
  * Kernels this library has launched in this process (all devices). A caller
  * that times a region reads it before and after to count its launches.
  */

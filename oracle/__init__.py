@@ -133,6 +133,61 @@ def decode_rows(dtype, dims, codes, block_scales=None, row_scales=None, first=0,
     return out
 
 
+def exact_distance_f64(rows, query):
+    """The reference's FP32 re-score of a quantized scan's candidates
+    (ExactDistance, ann/server/cuvs.c:2930-2942): each difference and square
+    in FP64, summed in dimension order (cumsum adds in order), the FP64
+    square root rounded to FP32. Pinned by construction: the reference keeps
+    this function static in its GPU backend, which does not build here."""
+    delta = np.asarray(rows, dtype=np.float32).astype(np.float64) - \
+        np.asarray(query, dtype=np.float32).astype(np.float64)
+    sq = delta * delta
+    if sq.shape[-1] == 0:
+        return np.zeros(sq.shape[:-1], dtype=np.float32)
+    return np.sqrt(np.cumsum(sq, axis=-1)[..., -1]).astype(np.float32)
+
+
+def quant_index_search(dtype, vectors, codes, queries, k, bounds, ordinals=None, block_scales=None,
+                       row_scales=None, quant_slack=256, slack_ratio=100):
+    """The reference's quantized scan route for a loaded index (SearchGather,
+    ann/server/cuvs.c:4585-4930): per index shard [bounds[s], bounds[s+1]),
+    the min(k + slack, eligible) rows nearest by the exact L2 distance of the
+    decoded rows (slack = max(quant_slack, k * slack_ratio / 100), GatherSlack
+    cuvs.c:4286-4296; this restatement breaks ties by ordinal), re-scored by
+    exact_distance_f64 of their FP32 rows; the k best over all shards by
+    (distance, ordinal), which is the per-shard (distance, key) sort cut at k
+    and tree-merged (cuvs.c:4919-4930). Returns per query a list of
+    (ordinal, FP32 distance)."""
+    queries = np.ascontiguousarray(queries, dtype=np.float32)
+    dims = queries.shape[1]
+    want = k + max(quant_slack, k * slack_ratio // 100)
+    out = []
+    for q in queries:
+        cand = []
+        for s in range(len(bounds) - 1):
+            lo, hi = int(bounds[s]), int(bounds[s + 1])
+            if ordinals is None:
+                local = np.arange(hi - lo, dtype=np.uint32)
+            else:
+                o = np.asarray(ordinals, dtype=np.uint64)
+                local = (o[(o >= lo) & (o < hi)] - lo).astype(np.uint32)
+            kk = min(want, len(local))
+            if kk == 0 or k == 0:
+                continue
+            bs = None if block_scales is None else block_scales[lo:hi]
+            _, ids, cnt, _ = search(dtype, dims, codes[lo:hi], q[None], kk, 0, ids=local, block_scales=bs,
+                                    row_scales=row_scales[lo:hi], threads=1)
+            cand += [lo + int(i) for i in ids[0, :cnt[0]]]
+        cand = np.array(cand, dtype=np.int64)
+        if len(cand) == 0:
+            out.append([])
+            continue
+        dist = exact_distance_f64(vectors[cand], q)
+        order = np.lexsort((cand, dist))[:k]
+        out.append([(int(cand[i]), dist[i]) for i in order])
+    return out
+
+
 def quantize_fp8(vectors):
     v = np.ascontiguousarray(vectors, dtype=np.float32)
     rows, dims = v.shape

@@ -36,6 +36,11 @@ SIGNATURES = {
                                    c_void_p, c_void_p, c_void_p]),
     'AnnB200ProbeLists': (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
     'AnnB200IndexCreate': (c_int, [ctypes.c_int, c_uint32, c_uint64, c_void_p, ctypes.POINTER(c_void_p)]),
+    'AnnB200IndexCreateQuant': (c_int, [ctypes.c_int, c_uint32, c_uint64, c_uint32, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_uint32, c_void_p, c_uint32, c_uint32,
+                                        ctypes.POINTER(c_void_p)]),
+    'AnnB200RescoreRows': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_void_p, c_void_p,
+                                   c_void_p]),
     'AnnB200IndexDestroy': (None, [c_void_p]),
     'AnnB200IndexSearch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_void_p, c_void_p,
                                    c_void_p]),

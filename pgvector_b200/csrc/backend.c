@@ -61,6 +61,19 @@ typedef struct Lane
 	double	   *hostDist;		/* pinned result staging */
 	int64_t    *hostId;
 	size_t		hostCap;
+	/* a quantized index's FP32 re-score */
+	float	   *stage;			/* device: gathered candidate rows */
+	size_t		stageBytes;
+	float	   *hostStage;		/* pinned */
+	size_t		hostStageBytes;
+	float	   *rescored;		/* device: their FP32 distances */
+	size_t		rescoredBytes;
+	float	   *hostRescored;	/* pinned */
+	size_t		hostRescoredBytes;
+	uint32_t   *candCounts;		/* device: candidates a query */
+	size_t		candCountsBytes;
+	uint32_t   *hostCandCounts; /* pinned */
+	size_t		hostCandCountsBytes;
 } Lane;
 
 static _Thread_local Lane LaneState;
@@ -304,7 +317,16 @@ struct AnnB200Index
 	int			device;
 	uint32_t	dims;
 	uint64_t	rows;
-	AnnB200Shard *shard;		/* owns the device copy of the rows */
+	AnnB200Shard *shard;		/* owns the device copy of the FP32 rows
+								 * (NULL for an index served from its
+								 * quantized copy) */
+	/* an index served from its quantized copy */
+	uint32_t	nshards;
+	AnnB200Shard **shards;		/* per index shard: its codes on the device */
+	uint64_t   *bounds;			/* nshards + 1 row bounds */
+	const float *vectors;		/* host FP32 rows (borrowed) */
+	uint32_t	quantSlack;
+	uint32_t	slackRatio;
 };
 
 /* Per thread and device: staging for index searches on that device. */
@@ -374,7 +396,297 @@ AnnB200IndexDestroy(AnnB200Index *ix)
 	if (ix == NULL)
 		return;
 	AnnB200ShardDestroy(ix->shard);
+	for (uint32_t s = 0; ix->shards && s < ix->nshards; s++)
+		AnnB200ShardDestroy(ix->shards[s]);
+	free(ix->shards);
+	free(ix->bounds);
 	free(ix);
+}
+
+int
+AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype, const void *codes,
+						const void *block_scales, const float *row_scales, const float *vectors, uint32_t nshards,
+						const uint64_t *shard_rows, uint32_t quant_slack, uint32_t slack_ratio, AnnB200Index **out)
+{
+	AnnB200Index *ix;
+	int			devices = AnnB200DeviceCount();
+	int			prev = 0;
+	int			status = ANN_OK;
+	uint64_t	blocks = (dims + 15) / 16;
+	uint64_t	rowBytes = blocks * (dtype == ANNB200_NVFP4 ? 8 : 16);
+	uint64_t	total = 0;
+
+	if (out == NULL)
+		return ANN_INVALID;
+	*out = NULL;
+	if (dims == 0 || rows == 0 || rows > UINT32_MAX || codes == NULL || row_scales == NULL || vectors == NULL ||
+		(dtype != ANNB200_E4M3 && dtype != ANNB200_NVFP4) || (dtype == ANNB200_NVFP4 && block_scales == NULL) ||
+		(nshards && shard_rows == NULL))
+		return ANN_INVALID;
+	for (uint32_t s = 0; s < nshards; s++)
+	{
+		if (shard_rows[s] == 0)
+			return ANN_INVALID;
+		total += shard_rows[s];
+	}
+	if (nshards && total != rows)
+		return ANN_INVALID;
+	if (devices <= 0)
+		return ANN_BACKEND_ERROR;
+	if (device < 0)
+		device = (int) (atomic_fetch_add(&NextLane, 1) % (unsigned) devices);
+	if (device >= devices || device >= INDEX_MAX_DEVICES)
+		return ANN_INVALID;
+	ix = calloc(1, sizeof(*ix));
+	if (ix == NULL)
+		return ANN_NOMEM;
+	ix->device = device;
+	ix->dims = dims;
+	ix->rows = rows;
+	ix->vectors = vectors;
+	ix->quantSlack = quant_slack;
+	ix->slackRatio = slack_ratio;
+	ix->nshards = nshards ? nshards : 1;
+	ix->shards = calloc(ix->nshards, sizeof(*ix->shards));
+	ix->bounds = calloc(ix->nshards + 1, sizeof(*ix->bounds));
+	if (ix->shards == NULL || ix->bounds == NULL)
+	{
+		AnnB200IndexDestroy(ix);
+		return ANN_NOMEM;
+	}
+	for (uint32_t s = 0; s < ix->nshards; s++)
+		ix->bounds[s + 1] = ix->bounds[s] + (nshards ? shard_rows[s] : rows);
+	cudaGetDevice(&prev);
+	for (uint32_t s = 0; status == ANN_OK && s < ix->nshards; s++)
+	{
+		uint64_t	first = ix->bounds[s];
+
+		status = AnnB200ShardCreate(device, dtype, dims, ix->bounds[s + 1] - first,
+									(const uint8_t *) codes + first * rowBytes,
+									block_scales ? (const uint8_t *) block_scales + first * blocks : NULL,
+									row_scales + first, (int64_t) first, ANNB200_SHARD_HOST, NULL, &ix->shards[s]);
+	}
+	cudaSetDevice(prev);
+	if (status != ANN_OK)
+	{
+		AnnB200IndexDestroy(ix);
+		return status;
+	}
+	*out = ix;
+	return ANN_OK;
+}
+
+/* The slice of sorted `ordinals` in [lo, hi). */
+static void
+Slice(const uint64_t *ordinals, uint64_t n, uint64_t lo, uint64_t hi, uint64_t *start, uint64_t *len)
+{
+	uint64_t	a = 0,
+				b = n;
+
+	while (a < b)
+	{
+		uint64_t	m = a + (b - a) / 2;
+
+		if (ordinals[m] < lo)
+			a = m + 1;
+		else
+			b = m;
+	}
+	*start = a;
+	b = n;
+	while (a < b)
+	{
+		uint64_t	m = a + (b - a) / 2;
+
+		if (ordinals[m] < hi)
+			a = m + 1;
+		else
+			b = m;
+	}
+	*len = a - *start;
+}
+
+static int
+KeyCompare(const void *a, const void *b)
+{
+	uint64_t	x = *(const uint64_t *) a,
+				y = *(const uint64_t *) b;
+
+	return x < y ? -1 : x > y;
+}
+
+#define QUANT_STAGE_BYTES ((size_t) 256 << 20)	/* gathered FP32 rows a chunk */
+
+/*
+ * AnnB200IndexSearch on an index served from its quantized copy: the
+ * reference's quantized scan route (SearchGather, ann/server/cuvs.c:
+ * 4585-4930). Per index shard, the exact search of the codes picks the
+ * min(k + slack, eligible) candidates (slack as GatherSlack, cuvs.c:
+ * 4286-4296); their FP32 rows are copied from host memory into pinned
+ * staging and re-scored on the device (ExactDistance, cuvs.c:2930-2942);
+ * the k best of all shards' candidates by (distance, ordinal) -- the
+ * reference's per-shard (distance, key) sort, cut at k, and tree merge
+ * (cuvs.c:4919-4930) keep the same k, key order being ordinal order.
+ * Queries are on the device (lane->query); results go to host memory.
+ */
+static int
+QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals, uint64_t nordinals, uint32_t k,
+			float *out_dist, uint64_t *out_ordinal, uint32_t *out_count)
+{
+	uint32_t	S = ix->nshards;
+	uint32_t	dims = ix->dims;
+	uint64_t	ratio = (uint64_t) k * ix->slackRatio / 100;
+	uint64_t	want = (uint64_t) k + (ratio > ix->quantSlack ? ratio : ix->quantSlack);
+	uint64_t   *start = calloc(S, sizeof(uint64_t));
+	uint64_t   *elig = calloc(S, sizeof(uint64_t));
+	uint64_t   *want_s = calloc(S, sizeof(uint64_t));
+	uint64_t   *off = calloc(S, sizeof(uint64_t));
+	uint32_t   *local = NULL;
+	uint32_t   *counts = NULL;
+	uint64_t   *cand = NULL;
+	uint64_t   *keys = NULL;
+	uint64_t	C = 0;
+	size_t		m;
+	int			status = ANN_OK;
+
+	if (start == NULL || elig == NULL || want_s == NULL || off == NULL)
+		status = ANN_NOMEM;
+	for (uint32_t s = 0; status == ANN_OK && s < S; s++)
+	{
+		if (ordinals)
+			Slice(ordinals, nordinals, ix->bounds[s], ix->bounds[s + 1], &start[s], &elig[s]);
+		else
+			elig[s] = ix->bounds[s + 1] - ix->bounds[s];
+		want_s[s] = want < elig[s] ? want : elig[s];
+		off[s] = C;
+		C += want_s[s];
+	}
+	if (status == ANN_OK && C == 0)
+		goto done;
+	if (status == ANN_OK && C > UINT32_MAX / 2)
+		status = ANN_UNSUPPORTED;
+	m = QUANT_STAGE_BYTES / ((size_t) C * dims * sizeof(float) + 1);
+	if (m == 0)
+		m = 1;
+	if (m > nq)
+		m = nq;
+
+	/* eligible rows of each shard, as shard-local row numbers */
+	if (status == ANN_OK && ordinals)
+	{
+		local = malloc(sizeof(*local) * nordinals);
+		if (local == NULL ||
+			!Grow((void **) &lane->ids, &lane->idsBytes, nordinals * sizeof(uint32_t)))
+			status = ANN_NOMEM;
+		for (uint32_t s = 0; status == ANN_OK && s < S; s++)
+			for (uint64_t i = start[s]; i < start[s] + elig[s]; i++)
+				local[i] = (uint32_t) (ordinals[i] - ix->bounds[s]);
+		if (status == ANN_OK &&
+			cudaMemcpyAsync(lane->ids, local, nordinals * sizeof(uint32_t), cudaMemcpyHostToDevice,
+							lane->stream) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+	}
+	if (status == ANN_OK)
+	{
+		counts = malloc(sizeof(*counts) * S * m);
+		cand = malloc(sizeof(*cand) * m * C);
+		keys = malloc(sizeof(*keys) * C);
+		if (counts == NULL || cand == NULL || keys == NULL || !LaneResults(lane, m * C) ||
+			!Grow((void **) &lane->counts, &lane->countsBytes, S * m * sizeof(uint32_t)) ||
+			!Grow((void **) &lane->stage, &lane->stageBytes, m * C * dims * sizeof(float)) ||
+			!GrowHost((void **) &lane->hostStage, &lane->hostStageBytes, m * C * dims * sizeof(float)) ||
+			!Grow((void **) &lane->rescored, &lane->rescoredBytes, m * C * sizeof(float)) ||
+			!GrowHost((void **) &lane->hostRescored, &lane->hostRescoredBytes, m * C * sizeof(float)) ||
+			!Grow((void **) &lane->candCounts, &lane->candCountsBytes, m * sizeof(uint32_t)) ||
+			!GrowHost((void **) &lane->hostCandCounts, &lane->hostCandCountsBytes, m * sizeof(uint32_t)))
+			status = ANN_NOMEM;
+	}
+	for (uint32_t q0 = 0; status == ANN_OK && q0 < nq; q0 += (uint32_t) m)
+	{
+		uint32_t	mm = nq - q0 < m ? nq - q0 : (uint32_t) m;
+		const float *q = lane->query + (size_t) q0 * dims;
+
+		/* candidates: each shard's nearest by the codes' exact distance */
+		for (uint32_t s = 0; status == ANN_OK && s < S; s++)
+			if (want_s[s])
+				status = AnnB200Search(ix->shards[s], q, mm, ordinals ? lane->ids + start[s] : NULL,
+									   ordinals ? elig[s] : 0, (uint32_t) want_s[s], ANNB200_L2, 0,
+									   (uint32_t) want_s[s], lane->dist + m * off[s], lane->id + m * off[s],
+									   lane->counts + (size_t) s * m, NULL, lane->stream);
+		if (status == ANN_OK &&
+			(cudaMemcpyAsync(lane->hostId, lane->id, m * C * sizeof(int64_t), cudaMemcpyDeviceToHost,
+							 lane->stream) != cudaSuccess ||
+			 cudaMemcpyAsync(counts, lane->counts, S * m * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+							 lane->stream) != cudaSuccess ||
+			 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+			status = ANN_BACKEND_ERROR;
+		if (status != ANN_OK)
+			break;
+
+		/* their FP32 rows, from host memory */
+		for (uint32_t i = 0; i < mm; i++)
+		{
+			uint32_t	pos = 0;
+
+			for (uint32_t s = 0; s < S; s++)
+				for (uint32_t j = 0; want_s[s] && j < counts[(size_t) s * m + i]; j++)
+				{
+					uint64_t	ord = (uint64_t) lane->hostId[m * off[s] + (size_t) i * want_s[s] + j];
+
+					memcpy(lane->hostStage + ((size_t) i * C + pos) * dims, ix->vectors + ord * dims,
+						   sizeof(float) * dims);
+					cand[(size_t) i * C + pos++] = ord;
+				}
+			lane->hostCandCounts[i] = pos;
+		}
+		if (cudaMemcpyAsync(lane->stage, lane->hostStage, (size_t) mm * C * dims * sizeof(float),
+							cudaMemcpyHostToDevice, lane->stream) != cudaSuccess ||
+			cudaMemcpyAsync(lane->candCounts, lane->hostCandCounts, mm * sizeof(uint32_t), cudaMemcpyHostToDevice,
+							lane->stream) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+		if (status == ANN_OK)
+			status = AnnB200RescoreRows(q, mm, dims, lane->stage, (uint32_t) C, lane->candCounts, lane->rescored,
+										lane->stream);
+		if (status == ANN_OK &&
+			(cudaMemcpyAsync(lane->hostRescored, lane->rescored, (size_t) mm * C * sizeof(float),
+							 cudaMemcpyDeviceToHost, lane->stream) != cudaSuccess ||
+			 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+			status = ANN_BACKEND_ERROR;
+
+		/* the best k by (distance, ordinal): distances are >= 0, so their bits order them */
+		for (uint32_t i = 0; status == ANN_OK && i < mm; i++)
+		{
+			uint32_t	n = lane->hostCandCounts[i];
+			uint32_t	r = n < k ? n : k;
+
+			for (uint32_t j = 0; j < n; j++)
+			{
+				uint32_t	bits;
+
+				memcpy(&bits, &lane->hostRescored[(size_t) i * C + j], sizeof(bits));
+				keys[j] = (uint64_t) bits << 32 | cand[(size_t) i * C + j];
+			}
+			qsort(keys, n, sizeof(*keys), KeyCompare);
+			for (uint32_t j = 0; j < r; j++)
+			{
+				uint32_t	bits = (uint32_t) (keys[j] >> 32);
+
+				memcpy(&out_dist[(size_t) (q0 + i) * k + j], &bits, sizeof(bits));
+				out_ordinal[(size_t) (q0 + i) * k + j] = keys[j] & 0xffffffffu;
+			}
+			out_count[q0 + i] = r;
+		}
+	}
+done:
+	free(start);
+	free(elig);
+	free(want_s);
+	free(off);
+	free(local);
+	free(counts);
+	free(cand);
+	free(keys);
+	return status;
 }
 
 int
@@ -413,6 +725,21 @@ AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const ui
 	{
 		cudaSetDevice(prev);
 		return ANN_BACKEND_ERROR;
+	}
+	if (ix->shard == NULL)
+	{
+		/* served from the quantized copy */
+		if (!Grow((void **) &lane->query, &lane->queryBytes, values * sizeof(float)))
+			status = ANN_NOMEM;
+		else if (cudaMemcpyAsync(lane->query, queries, values * sizeof(float), cudaMemcpyHostToDevice,
+								 lane->stream) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+		if (status == ANN_OK)
+			status = QuantSearch(ix, lane, nq, ordinals, nordinals, k, out_dist, out_ordinal, out_count);
+		if (status == ANN_OK)
+			atomic_fetch_add(&DeviceJobs, 1);
+		cudaSetDevice(prev);
+		return status;
 	}
 	counts = malloc(sizeof(*counts) * nq);
 	if (ordinals)

@@ -380,6 +380,9 @@ uint32_t list_plan_scan_launches(uint32_t nlists);
 // ids/counts of a centroid search (out_cap = nprobe) -> u32 probe table.
 void launch_probe_table(const int64_t *ids, const uint32_t *counts, uint32_t nq, uint32_t nprobe, int64_t first,
                         uint32_t *probes, cudaStream_t st);
+// FP32 re-score (FP64 sum in dimension order) of gathered candidate rows.
+void launch_rescore_rows(const float *queries, uint32_t nq, uint32_t dims, const float *rows, uint32_t stride,
+                         const uint32_t *counts, float *out, cudaStream_t st);
 // query_lo_map: the low BF16 halves of the queries (FP32 rows only, else NULL).
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, const CUtensorMap *query_lo_map, uint32_t kpad, uint32_t bn,

@@ -261,6 +261,43 @@ __device__ double exact_distance(const ShardView &s, uint64_t id, const float *q
   }
 }
 
+// FP32 re-score of a quantized scan's candidates, as the reference's
+// loaded-index scan route does it on the host (ExactDistance,
+// ann/server/cuvs.c:2930-2942): each difference and square in FP64, summed
+// in dimension order, the FP64 square root rounded to FP32. One thread a
+// candidate row; rows [nq][stride][dims], only the first counts[q] of a
+// query's stride are read and written.
+__global__ void __launch_bounds__(256) rescore_rows(const float *__restrict__ queries, uint32_t nq, uint32_t dims,
+                                                    const float *__restrict__ rows, uint32_t stride,
+                                                    const uint32_t *__restrict__ counts, float *__restrict__ out,
+                                                    int vec4) {
+  const uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)nq * stride) return;
+  const uint32_t q = (uint32_t)(t / stride), j = (uint32_t)(t % stride);
+  if (counts && j >= counts[q]) return;
+  const float *x = rows + t * dims;
+  const float *v = queries + (uint64_t)q * dims;
+  double sum = 0.0;
+  uint32_t d = 0;
+  if (vec4)
+    for (; d < dims; d += 4) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(x + d));
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(v + d));
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const double delta = __dsub_rn((double)av[i], (double)bv[i]);
+        sum = __dadd_rn(sum, __dmul_rn(delta, delta));
+      }
+    }
+  for (; d < dims; d++) {
+    const double delta = __dsub_rn((double)__ldg(x + d), (double)__ldg(v + d));
+    sum = __dadd_rn(sum, __dmul_rn(delta, delta));
+  }
+  out[t] = __double2float_rn(__dsqrt_rn(sum));
+}
+
+
 // ---------------------------------------------------------------- shard stats
 
 // Per row: FP64 squared norm of the decoded values -> n2 (FP32) and
@@ -1123,6 +1160,15 @@ __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nb
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
+
+void launch_rescore_rows(const float *queries, uint32_t nq, uint32_t dims, const float *rows, uint32_t stride,
+                         const uint32_t *counts, float *out, cudaStream_t st) {
+  const uint64_t n = (uint64_t)nq * stride;
+  // 16-byte loads where every row and query starts on a 16-byte boundary
+  const int vec4 = (dims & 3) == 0 && (((uintptr_t)queries | (uintptr_t)rows) & 15) == 0;
+  if (n)
+    rescore_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(queries, nq, dims, rows, stride, counts, out, vec4);
+}
 
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st) {
   if (s.rows == 0 || s.dtype == DT_BIT) return;

@@ -13,9 +13,13 @@
  *
  *   load_index     registers the directory like the cpu backend and copies
  *                  its FP32 rows (vectors.f32) to a GPU (AnnB200IndexCreate,
- *                  round robin over the devices); the device copy hangs off
- *                  file->device and is freed by the registry's
- *                  AnnIndexDeviceDestroy hook when the index is unloaded.
+ *                  round robin over the devices); where they do not fit and
+ *                  the directory has a quantized copy, that copy instead
+ *                  (AnnB200IndexCreateQuant: the reference's quantized scan
+ *                  route, file->quantActive set as the reference's backend
+ *                  sets it). The device copy hangs off file->device and is
+ *                  freed by the registry's AnnIndexDeviceDestroy hook when
+ *                  the index is unloaded.
  *   search_index   per job: drop excluded rows (AnnIndexJobDropExcluded),
  *                  resolve the index (ANN_STALE if not loaded, ANN_INVALID on
  *                  a dimension mismatch), map a key filter to ordinals
@@ -25,7 +29,8 @@
  *                  queries); filtered jobs run one at a time over their
  *                  ordinals. Hits carry the key of their ordinal and the
  *                  reference's FP32 distance; route is set as the cpu backend
- *                  sets it (cpu.c:394).
+ *                  sets it (cpu.c:394), or as the quantized scan route sets
+ *                  it (ANN_ROUTE_EXACT, cuvs.c:4927).
  */
 #define _GNU_SOURCE
 #include <pthread.h>
@@ -45,6 +50,53 @@ DestroyDevice(void *device)
 	AnnB200IndexDestroy((AnnB200Index *) device);
 }
 
+/*
+ * The device copy of a directory with a quantized copy ("quant fp8|nvfp4")
+ * while the worker scans quantized copies (--quantized-scan, on by
+ * default): its codes, per index shard, with the FP32 rows left in the
+ * mapped vectors.f32 for re-scoring (AnnB200IndexCreateQuant).
+ */
+static AnnStatus
+CreateQuant(const AnnIndexFile *file, AnnB200Index **index)
+{
+	uint64_t	rows[ANN_INDEX_MAX_SHARDS];
+	uint32_t	nshards = file->nshards;
+
+	for (uint32_t s = 0; s < nshards; s++)
+		rows[s] = file->shards[s].rows;
+	return (AnnStatus) AnnB200IndexCreateQuant(-1, file->dimensions, file->rows,
+											   file->quant == ANN_QUANT_NVFP4 ? ANNB200_NVFP4 : ANNB200_E4M3,
+											   file->quantData, file->quantScales, file->rowScales, file->vectors,
+											   nshards, nshards ? rows : NULL, AnnIndexConfig.quant_slack,
+											   AnnIndexConfig.slack_ratio, index);
+}
+
+/*
+ * Which copy a loaded index searches on the device: its FP32 rows (exact)
+ * where they fit, else its quantized copy when it has one and quantized
+ * scans are on. ANN_B200_INDEX_COPY=fp32 or =quant chooses instead.
+ */
+static AnnStatus
+CreateDevice(AnnIndexFile *file, AnnB200Index **index)
+{
+	const char *copy = getenv("ANN_B200_INDEX_COPY");
+	int			quant = file->quant != ANN_QUANT_NONE && AnnIndexConfig.quantized_scan;
+	AnnStatus	status;
+
+	file->quantActive = 0;
+	if (quant && copy && strcmp(copy, "quant") == 0)
+		status = CreateQuant(file, index);
+	else
+	{
+		status = (AnnStatus) AnnB200IndexCreate(-1, file->dimensions, file->rows, file->vectors, index);
+		if (status != ANN_NOMEM || !quant || (copy && strcmp(copy, "fp32") == 0))
+			return status;
+		status = CreateQuant(file, index);
+	}
+	file->quantActive = status == ANN_OK;
+	return status;
+}
+
 static AnnStatus
 LoadIndex(const char *name, const char *directory)
 {
@@ -55,7 +107,7 @@ LoadIndex(const char *name, const char *directory)
 	if (status != ANN_OK)
 		return status;
 	AnnIndexDeviceDestroy = DestroyDevice;
-	status = (AnnStatus) AnnB200IndexCreate(-1, file->dimensions, file->rows, file->vectors, &index);
+	status = CreateDevice(file, &index);
 	if (status != ANN_OK)
 	{
 		AnnIndexFileClose(file);
@@ -74,6 +126,9 @@ LoadIndex(const char *name, const char *directory)
 static void
 Finish(AnnIndexJob *job, const AnnIndexFile *file, const float *dist, const uint64_t *ordinal, uint32_t n)
 {
+	/* the quantized scan route answers as an exact scan (cuvs.c:4927) */
+	int			quant = file->quantActive;
+
 	if (n > job->k)
 		n = job->k;
 	for (uint32_t i = 0; i < n; i++)
@@ -83,8 +138,20 @@ Finish(AnnIndexJob *job, const AnnIndexFile *file, const float *dist, const uint
 		job->results[i].ordinal = ordinal[i];
 	}
 	job->nresults = n;
-	job->route = job->filtered ? ANN_ROUTE_EXACT : ANN_ROUTE_ANN;
+	job->route = job->filtered || quant ? ANN_ROUTE_EXACT : ANN_ROUTE_ANN;
 	job->status = ANN_OK;
+}
+
+/*
+ * Whether job i joins the batch of job `first`: unfiltered, on the same
+ * index, and, on an index served from its quantized copy, with the same k
+ * (the number of candidates each query re-scores follows from its own k).
+ */
+static int
+SameBatch(AnnIndexJob *jobs, AnnIndexFile **files, const char *done, uint32_t first, uint32_t i)
+{
+	return files[i] == files[first] && !jobs[i].filtered && !done[i] &&
+		(!files[first]->quantActive || jobs[i].k == jobs[first].k);
 }
 
 /* Unfiltered jobs [first..] on `file`: one batch of queries, k = the largest. */
@@ -103,7 +170,7 @@ SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t fi
 	int			status;
 
 	for (uint32_t i = first; i < count; i++)
-		if (files[i] == file && !jobs[i].filtered && !done[i])
+		if (SameBatch(jobs, files, done, first, i))
 		{
 			n++;
 			if (jobs[i].k > kmax)
@@ -115,14 +182,14 @@ SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t fi
 	counts = malloc(sizeof(uint32_t) * n);
 	status = queries && dist && ordinal && counts ? ANN_OK : ANN_NOMEM;
 	for (uint32_t i = first; status == ANN_OK && i < count; i++)
-		if (files[i] == file && !jobs[i].filtered && !done[i])
+		if (SameBatch(jobs, files, done, first, i))
 			memcpy(queries + (size_t) g++ * dims, jobs[i].query, sizeof(float) * dims);
 	if (status == ANN_OK)
 		status = AnnB200IndexSearch((AnnB200Index *) file->device, queries, n, NULL, 0, kmax, dist, ordinal,
 									counts);
 	g = 0;
 	for (uint32_t i = first; i < count; i++)
-		if (files[i] == file && !jobs[i].filtered && !done[i])
+		if (SameBatch(jobs, files, done, first, i))
 		{
 			done[i] = 1;
 			if (status == ANN_OK)

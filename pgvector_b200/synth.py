@@ -91,11 +91,15 @@ def ivf_probes(queries, centroids, nprobe):
     return np.argsort(d2, axis=1, kind='stable')[:, :nprobe].astype(np.uint32)
 
 
-def write_index_dir(directory, keys, vectors, shards=1):
+def write_index_dir(directory, keys, vectors, shards=1, quant=None):
     """An index directory in the worker's documented format
     (ann/common/INDEX_FORMAT.md, version 1): rows sorted by key into
     keys.i64 and vectors.f32, and a manifest naming `shards` contiguous
-    graphless shards. Returns (sorted keys, rows in key order)."""
+    graphless shards. `quant` adds a quantized copy of the rows (given in
+    the same order as `vectors`): ('fp8', codes, row_scales) writes
+    vectors.e4m3, ('nvfp4', codes, block_scales, row_scales) vectors.nvfp4
+    and scales.e4m3, both rowscale.f32 and the manifest's quant line.
+    Returns (sorted keys, rows in key order)."""
     import os
     order = np.argsort(np.asarray(keys, dtype=np.int64), kind='stable')
     k = np.ascontiguousarray(np.asarray(keys, dtype=np.int64)[order])
@@ -108,6 +112,21 @@ def write_index_dir(directory, keys, vectors, shards=1):
     lines = ['pgvector-ann-index 1', 'dimensions %d' % d, 'rows %d' % n, 'metric l2', 'dtype float32',
              'shards %d' % shards]
     lines += ['shard %d %d %d -' % (i, bounds[i], bounds[i + 1] - bounds[i]) for i in range(shards)]
+    if quant is not None:
+        kind = quant[0]
+        if kind == 'fp8':
+            np.ascontiguousarray(np.asarray(quant[1], dtype=np.uint8)[order]).tofile(
+                os.path.join(directory, 'vectors.e4m3'))
+        elif kind == 'nvfp4':
+            np.ascontiguousarray(np.asarray(quant[1], dtype=np.uint8)[order]).tofile(
+                os.path.join(directory, 'vectors.nvfp4'))
+            np.ascontiguousarray(np.asarray(quant[2], dtype=np.uint8)[order]).tofile(
+                os.path.join(directory, 'scales.e4m3'))
+        else:
+            raise ValueError('quant must be fp8 or nvfp4')
+        np.ascontiguousarray(np.asarray(quant[-1], dtype=np.float32)[order]).astype('<f4').tofile(
+            os.path.join(directory, 'rowscale.f32'))
+        lines.append('quant %s' % kind)
     with open(os.path.join(directory, 'manifest.tmp'), 'w') as f:
         f.write('\n'.join(lines) + '\n')
     os.rename(os.path.join(directory, 'manifest.tmp'), os.path.join(directory, 'manifest'))

@@ -106,3 +106,28 @@ def test_simulated_device_loss_reported_without_a_gpu():
     status, reason = out.stdout.strip().split(' ', 1)
     assert int(status) == pb.BACKEND_ERROR
     assert 'GPU context lost (simulated' in reason
+
+
+def test_quantized_index_arguments_checked_on_host():
+    # AnnB200IndexCreateQuant / AnnB200RescoreRows refuse bad arguments
+    # before touching a device
+    lib = pb.load()
+    out = ctypes.c_void_p()
+    codes = np.zeros((4, 16), np.uint8)
+    scales = np.zeros((4, 1), np.uint8)
+    rs = np.ones(4, np.float32)
+    v = np.zeros((4, 16), np.float32)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    rows = (ctypes.c_uint64 * 2)(3, 2)
+    cases = [
+        (0, 0, 4, pb.NVFP4, P(codes), P(scales), P(rs), P(v), 0, None),      # dims 0
+        (0, 16, 4, pb.F16, P(codes), P(scales), P(rs), P(v), 0, None),       # not a quantized format
+        (0, 16, 4, pb.NVFP4, P(codes), None, P(rs), P(v), 0, None),          # NVFP4 without block scales
+        (0, 16, 4, pb.E4M3, P(codes), None, P(rs), None, 0, None),           # no FP32 rows
+        (0, 16, 4, pb.E4M3, P(codes), None, P(rs), P(v), 2, rows),           # shards cover 5 rows, not 4
+    ]
+    for i, c in enumerate(cases):
+        st = lib.AnnB200IndexCreateQuant(*c[:8], c[8], c[9], 256, 100, ctypes.byref(out))
+        assert st == pb.INVALID and not out.value, i
+    assert lib.AnnB200RescoreRows(None, 0, 4, None, 8, None, None, None) == 0   # nothing to do
+    assert lib.AnnB200RescoreRows(None, 2, 4, None, 8, None, None, None) == pb.INVALID

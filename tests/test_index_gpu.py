@@ -161,3 +161,109 @@ def test_odd_dimensions_and_single_query(backends, tmp_path):
     assert load(ours, 'b200_o', str(tmp_path / 'odd')) == 0
     jobs = Jobs().add('IX', rng.standard_normal(37), 17)
     assert_same_as_cpu(backends, jobs, 'cpu_o', 'b200_o')
+
+
+def test_rescore_rows_kernel(cuda):
+    # AnnB200RescoreRows against the restated ExactDistance
+    # (ann/server/cuvs.c:2930-2942), over the 16-byte and the scalar loads
+    import torch
+    import pgvector_b200 as pb
+    lib = pb.load()
+    rng = np.random.default_rng(13)
+    for d, shift in ((64, 0), (64, 1), (37, 0), (3, 0)):
+        nq, stride = 5, 40
+        q = (rng.standard_normal((nq, d)) * 3).astype(np.float32)
+        rows = (rng.standard_normal((nq, stride, d)) * 10 ** rng.uniform(-2, 2, (nq, stride, 1))).astype(np.float32)
+        counts = np.array([40, 0, 17, 1, 39], dtype=np.uint32)
+        qd = torch.from_numpy(q).to(cuda)
+        flat = torch.zeros(nq * stride * d + shift, dtype=torch.float32, device=cuda)
+        flat[shift:] = torch.from_numpy(rows.ravel()).to(cuda)
+        cd = torch.from_numpy(counts.view(np.int32)).to(cuda)
+        out = torch.full((nq, stride), -1.0, dtype=torch.float32, device=cuda)
+        st = lib.AnnB200RescoreRows(ctypes.c_void_p(qd.data_ptr()), nq, d,
+                                    ctypes.c_void_p(flat.data_ptr() + 4 * shift), stride,
+                                    ctypes.c_void_p(cd.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert st == 0
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for i in range(nq):
+            c = int(counts[i])
+            want = oracle.exact_distance_f64(rows[i, :c], q[i])
+            assert np.array_equal(got[i, :c].view(np.uint32), want.view(np.uint32)), (d, shift, i)
+            assert np.all(got[i, c:] == -1.0)
+
+
+def _eligible(skeys, spec):
+    """A job's eligible ordinals as the worker resolves them (None: all)."""
+    if spec.get('keys') is not None:
+        pos = np.searchsorted(skeys, spec['keys'])
+        ok = (pos < len(skeys)) & (skeys[np.minimum(pos, len(skeys) - 1)] == spec['keys'])
+        elig = pos[ok].astype(np.uint64)
+    elif spec.get('ordinals') is not None:
+        elig = np.asarray(spec['ordinals'], dtype=np.uint64)
+    else:
+        return None
+    if spec.get('exclude') is not None:
+        elig = np.setdiff1d(elig, np.asarray(spec['exclude'], dtype=np.uint64))
+    return elig
+
+
+@pytest.mark.parametrize('kind,d', [('fp8', 96), ('nvfp4', 96), ('nvfp4', 72)])
+def test_quantized_copy_route(backends, tmp_path, monkeypatch, kind, d):
+    # an index served from its quantized copy: the reference's quantized scan
+    # route (SearchGather, ann/server/cuvs.c:4585-4930) against its
+    # restatement (oracle.quant_index_search), bit for bit, and its recall
+    # against the cpu backend's exact answer
+    rng = np.random.default_rng(21)
+    n = 24000
+    x = synth.mixture(n, d, 60, seed=21)
+    keys = rng.choice(np.arange(-10 ** 9, 10 ** 9), n, replace=False)
+    order = np.argsort(keys, kind='stable')
+    if kind == 'fp8':
+        codes, rs = oracle.quantize_fp8(x)
+        quant, bs, dt = ('fp8', codes, rs), None, oracle.E4M3
+    else:
+        codes, bs, rs = oracle.quantize_nvfp4(x)
+        quant, dt = ('nvfp4', codes, bs, rs), oracle.NVFP4
+    directory = str(tmp_path / ('q_%s_%d' % (kind, d)))
+    skeys, xs = synth.write_index_dir(directory, keys, x, shards=3, quant=quant)
+    cs, rss, bss = codes[order], rs[order], None if bs is None else bs[order]
+    bounds = [n * i // 3 for i in range(4)]
+    cpu, ours = backends
+    ref_name, our_name = 'cpu_q_%s_%d' % (kind, d), 'b200_q_%s_%d' % (kind, d)
+    assert load(cpu, ref_name, directory) == 0
+    monkeypatch.setenv('ANN_B200_INDEX_COPY', 'quant')
+    assert load(ours, our_name, directory) == 0
+    q = synth.mixture_queries(48, d, 60, seed=22)
+    jobs = Jobs()
+    for i in range(32):                              # one tensor-path batch at k = 10
+        jobs.add('IX', q[i], 10)
+    for i in range(32, 40):                          # a small batch at k = 100
+        jobs.add('IX', q[i], 100)
+    sel = np.sort(rng.choice(skeys, 3000, replace=False))
+    missing = np.setdiff1d(rng.integers(-10 ** 9, 10 ** 9, 50), skeys)
+    jobs.add('IX', q[40], 25, keys=np.sort(np.concatenate([sel, missing])))
+    ords = np.sort(rng.choice(n, 500, replace=False))
+    jobs.add('IX', q[41], 30, ordinals=ords)
+    jobs.add('IX', q[42], 30, ordinals=ords, exclude=ords[::3])
+    jobs.add('IX', q[43], 50, keys=sel[:20])         # k past the eligible rows
+    jobs.add('IX', q[44], 10, keys=np.array([], dtype=np.int64))
+    jobs.add('IX', q[45], 0)
+    jobs.add('IX', q[46], 300)                       # k + slack = 600 candidates a shard
+    got = jobs.run(ours, rename={'IX': our_name})
+    exact = jobs.run(cpu, rename={'IX': ref_name})
+    found = total = 0
+    for i, (spec, g, e) in enumerate(zip(jobs.specs, got, exact)):
+        elig = _eligible(skeys, spec)
+        want = oracle.quant_index_search(dt, xs, cs, spec['query'][None], spec['k'], bounds, ordinals=elig,
+                                         block_scales=bss, row_scales=rss)[0]
+        hits = [(int(skeys[o]), dist.view(np.uint32).item(), o) for o, dist in want]
+        assert g[0] == 0, (i, 'status', g[0])
+        assert g[1] == 2, (i, 'route', g[1])                        # ANN_ROUTE_EXACT
+        assert g[2] == hits, (i, g[2][:4], hits[:4])
+        found += len({h[0] for h in g[2]} & {h[0] for h in e[2]})
+        total += len(e[2])
+    recall = found / total
+    print('%s d=%d recall against the exact FP32 answer: %.4f' % (kind, d, recall))
+    assert recall >= 0.97
