@@ -33,12 +33,31 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
+#include <unistd.h>
 
 static atomic_ullong DeviceJobs;
 static atomic_uint NextLane;
 static atomic_int LostSimulated;
 static char LostReason[256];
 static pthread_mutex_t LostLock = PTHREAD_MUTEX_INITIALIZER;
+
+/* Staging of one chunk of a quantized index search's candidate rows. */
+typedef struct QuantSlot
+{
+	float	   *stage;			/* device: gathered candidate rows */
+	size_t		stageBytes;
+	float	   *hostStage;		/* pinned */
+	size_t		hostStageBytes;
+	float	   *rescored;		/* device: their FP32 distances */
+	size_t		rescoredBytes;
+	float	   *hostRescored;	/* pinned */
+	size_t		hostRescoredBytes;
+	uint32_t   *candCounts;		/* device: candidates a query */
+	size_t		candCountsBytes;
+	uint32_t   *hostCandCounts; /* pinned */
+	size_t		hostCandCountsBytes;
+} QuantSlot;
 
 typedef struct Lane
 {
@@ -61,19 +80,11 @@ typedef struct Lane
 	double	   *hostDist;		/* pinned result staging */
 	int64_t    *hostId;
 	size_t		hostCap;
-	/* a quantized index's FP32 re-score */
-	float	   *stage;			/* device: gathered candidate rows */
-	size_t		stageBytes;
-	float	   *hostStage;		/* pinned */
-	size_t		hostStageBytes;
-	float	   *rescored;		/* device: their FP32 distances */
-	size_t		rescoredBytes;
-	float	   *hostRescored;	/* pinned */
-	size_t		hostRescoredBytes;
-	uint32_t   *candCounts;		/* device: candidates a query */
-	size_t		candCountsBytes;
-	uint32_t   *hostCandCounts; /* pinned */
-	size_t		hostCandCountsBytes;
+	/* a quantized index's FP32 re-score: two chunks of queries in flight */
+	int			rescoreReady;
+	cudaStream_t rescoreStream;
+	cudaEvent_t rescoreDone[2];
+	QuantSlot	slot[2];
 } Lane;
 
 static _Thread_local Lane LaneState;
@@ -506,6 +517,53 @@ Slice(const uint64_t *ordinals, uint64_t n, uint64_t lo, uint64_t hi, uint64_t *
 	*len = a - *start;
 }
 
+/* Reorder a[0..n) so that a[0..r) holds its r smallest keys (any order): quickselect. */
+static void
+SelectSmallest(uint64_t *a, uint32_t n, uint32_t r)
+{
+	uint32_t	lo = 0,
+				hi = n;
+
+	if (r == 0 || r >= n)
+		return;
+	while (hi - lo > 1)
+	{
+		uint64_t	x = a[lo],
+					y = a[lo + (hi - lo) / 2],
+					z = a[hi - 1];
+		uint64_t	pivot = x < y ? (y < z ? y : (x < z ? z : x)) : (x < z ? x : (y < z ? z : y));
+		uint32_t	i = lo,
+					j = lo,
+					e = hi;
+
+		/* three-way partition: [lo, i) < pivot, [i, e) == pivot, [e, hi) > pivot */
+		while (j < e)
+		{
+			uint64_t	v = a[j];
+
+			if (v < pivot)
+			{
+				a[j] = a[i];
+				a[i++] = v;
+				j++;
+			}
+			else if (v > pivot)
+			{
+				a[j] = a[--e];
+				a[e] = v;
+			}
+			else
+				j++;
+		}
+		if (r <= i)
+			hi = i;
+		else if (r <= e)
+			return;
+		else
+			lo = e;
+	}
+}
+
 static int
 KeyCompare(const void *a, const void *b)
 {
@@ -515,7 +573,107 @@ KeyCompare(const void *a, const void *b)
 	return x < y ? -1 : x > y;
 }
 
-#define QUANT_STAGE_BYTES ((size_t) 256 << 20)	/* gathered FP32 rows a chunk */
+static double
+NowMs(void)
+{
+	struct timespec ts;
+
+	clock_gettime(CLOCK_MONOTONIC, &ts);
+	return ts.tv_sec * 1e3 + ts.tv_nsec / 1e6;
+}
+
+/* One share of a chunk's candidate-row copies (queries [begin, end)). */
+typedef struct GatherTask
+{
+	const AnnB200Index *ix;
+	Lane	   *lane;
+	QuantSlot  *slot;			/* where the rows go */
+	const uint32_t *counts;		/* per shard and query: candidates found */
+	uint64_t   *cand;			/* out: each query's candidate ordinals */
+	const uint64_t *want;
+	const uint64_t *off;
+	size_t		m;
+	uint64_t	C;
+	uint32_t	begin;
+	uint32_t	end;
+} GatherTask;
+
+static void *
+GatherRows(void *arg)
+{
+	GatherTask *t = arg;
+	const AnnB200Index *ix = t->ix;
+	Lane	   *lane = t->lane;
+	QuantSlot  *slot = t->slot;
+	uint32_t	dims = ix->dims;
+
+	for (uint32_t i = t->begin; i < t->end; i++)
+	{
+		uint32_t	pos = 0;
+
+		for (uint32_t s = 0; s < ix->nshards; s++)
+			for (uint32_t j = 0; t->want[s] && j < t->counts[(size_t) s * t->m + i]; j++)
+			{
+				uint64_t	ord = (uint64_t) lane->hostId[t->m * t->off[s] + (size_t) i * t->want[s] + j];
+
+				memcpy(slot->hostStage + ((size_t) i * t->C + pos) * dims, ix->vectors + ord * dims,
+					   sizeof(float) * dims);
+				t->cand[(size_t) i * t->C + pos++] = ord;
+			}
+		slot->hostCandCounts[i] = pos;
+	}
+	return NULL;
+}
+
+#define GATHER_MAX_THREADS 32
+
+/*
+ * Copy the candidates' FP32 rows of queries [0, mm) into pinned staging:
+ * scattered row reads from host memory, split over threads by query
+ * (ANN_B200_GATHER_THREADS, default the online CPUs up to 16).
+ */
+static void
+GatherAll(const AnnB200Index *ix, Lane *lane, QuantSlot *slot, const uint32_t *counts, uint64_t *cand,
+		  const uint64_t *want, const uint64_t *off, size_t m, uint64_t C, uint32_t mm)
+{
+	GatherTask	task[GATHER_MAX_THREADS];
+	pthread_t	tid[GATHER_MAX_THREADS];
+	int			started[GATHER_MAX_THREADS] = {0};
+	long		threads = EnvLong("ANN_B200_GATHER_THREADS", 0);
+	uint64_t	bytes = (uint64_t) mm * C * ix->dims * sizeof(float);
+
+	if (threads <= 0)
+	{
+		threads = sysconf(_SC_NPROCESSORS_ONLN);
+		if (threads > 16)
+			threads = 16;
+	}
+	if (threads > GATHER_MAX_THREADS)
+		threads = GATHER_MAX_THREADS;
+	/* about 4 MB of rows a thread at least */
+	if ((uint64_t) threads > bytes / (4u << 20) + 1)
+		threads = (long) (bytes / (4u << 20) + 1);
+	if (threads > (long) mm)
+		threads = mm;
+	if (threads < 1)
+		threads = 1;
+	for (long t = 0; t < threads; t++)
+	{
+		task[t] = (GatherTask) {ix, lane, slot, counts, cand, want, off, m, C,
+			(uint32_t) ((uint64_t) mm * t / threads), (uint32_t) ((uint64_t) mm * (t + 1) / threads)};
+		if (t > 0)
+			started[t] = pthread_create(&tid[t], NULL, GatherRows, &task[t]) == 0;
+	}
+	GatherRows(&task[0]);
+	for (long t = 1; t < threads; t++)
+	{
+		if (started[t])
+			pthread_join(tid[t], NULL);
+		else
+			GatherRows(&task[t]);	/* no thread: copy this share here */
+	}
+}
+
 
 /*
  * AnnB200IndexSearch on an index served from its quantized copy: the
@@ -528,6 +686,9 @@ KeyCompare(const void *a, const void *b)
  * reference's per-shard (distance, key) sort, cut at k, and tree merge
  * (cuvs.c:4919-4930) keep the same k, key order being ordinal order.
  * Queries are on the device (lane->query); results go to host memory.
+ * Queries run in chunks whose candidate rows fill one staging slot
+ * (ANN_B200_QUANT_STAGE_MB, default 256 MB); the host copies one chunk's
+ * rows while the device re-scores the previous chunk's.
  */
 static int
 QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals, uint64_t nordinals, uint32_t k,
@@ -543,11 +704,14 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 	uint64_t   *off = calloc(S, sizeof(uint64_t));
 	uint32_t   *local = NULL;
 	uint32_t   *counts = NULL;
-	uint64_t   *cand = NULL;
+	uint64_t   *cand[2] = {NULL, NULL};
 	uint64_t   *keys = NULL;
 	uint64_t	C = 0;
 	size_t		m;
+	uint32_t	chunks;
 	int			status = ANN_OK;
+	int			debug = EnvLong("ANN_B200_DEBUG", 0) > 0;
+	size_t		stage = (size_t) EnvLong("ANN_B200_QUANT_STAGE_MB", 256) << 20;
 
 	if (start == NULL || elig == NULL || want_s == NULL || off == NULL)
 		status = ANN_NOMEM;
@@ -565,7 +729,7 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 		goto done;
 	if (status == ANN_OK && C > UINT32_MAX / 2)
 		status = ANN_UNSUPPORTED;
-	m = QUANT_STAGE_BYTES / ((size_t) C * dims * sizeof(float) + 1);
+	m = stage / ((size_t) C * dims * sizeof(float) + 1);
 	if (m == 0)
 		m = 1;
 	if (m > nq)
@@ -586,97 +750,148 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 							lane->stream) != cudaSuccess)
 			status = ANN_BACKEND_ERROR;
 	}
+	if (status == ANN_OK && !lane->rescoreReady)
+	{
+		if (cudaStreamCreateWithFlags(&lane->rescoreStream, cudaStreamNonBlocking) != cudaSuccess ||
+			cudaEventCreateWithFlags(&lane->rescoreDone[0], cudaEventDisableTiming) != cudaSuccess ||
+			cudaEventCreateWithFlags(&lane->rescoreDone[1], cudaEventDisableTiming) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+		else
+			lane->rescoreReady = 1;
+	}
 	if (status == ANN_OK)
 	{
 		counts = malloc(sizeof(*counts) * S * m);
-		cand = malloc(sizeof(*cand) * m * C);
+		cand[0] = malloc(sizeof(uint64_t) * m * C);
+		cand[1] = malloc(sizeof(uint64_t) * m * C);
 		keys = malloc(sizeof(*keys) * C);
-		if (counts == NULL || cand == NULL || keys == NULL || !LaneResults(lane, m * C) ||
-			!Grow((void **) &lane->counts, &lane->countsBytes, S * m * sizeof(uint32_t)) ||
-			!Grow((void **) &lane->stage, &lane->stageBytes, m * C * dims * sizeof(float)) ||
-			!GrowHost((void **) &lane->hostStage, &lane->hostStageBytes, m * C * dims * sizeof(float)) ||
-			!Grow((void **) &lane->rescored, &lane->rescoredBytes, m * C * sizeof(float)) ||
-			!GrowHost((void **) &lane->hostRescored, &lane->hostRescoredBytes, m * C * sizeof(float)) ||
-			!Grow((void **) &lane->candCounts, &lane->candCountsBytes, m * sizeof(uint32_t)) ||
-			!GrowHost((void **) &lane->hostCandCounts, &lane->hostCandCountsBytes, m * sizeof(uint32_t)))
+		if (counts == NULL || cand[0] == NULL || cand[1] == NULL || keys == NULL || !LaneResults(lane, m * C) ||
+			!Grow((void **) &lane->counts, &lane->countsBytes, S * m * sizeof(uint32_t)))
 			status = ANN_NOMEM;
+		for (int h = 0; status == ANN_OK && h < 2; h++)
+		{
+			QuantSlot  *sl = &lane->slot[h];
+
+			if (!Grow((void **) &sl->stage, &sl->stageBytes, m * C * dims * sizeof(float)) ||
+				!GrowHost((void **) &sl->hostStage, &sl->hostStageBytes, m * C * dims * sizeof(float)) ||
+				!Grow((void **) &sl->rescored, &sl->rescoredBytes, m * C * sizeof(float)) ||
+				!GrowHost((void **) &sl->hostRescored, &sl->hostRescoredBytes, m * C * sizeof(float)) ||
+				!Grow((void **) &sl->candCounts, &sl->candCountsBytes, m * sizeof(uint32_t)) ||
+				!GrowHost((void **) &sl->hostCandCounts, &sl->hostCandCountsBytes, m * sizeof(uint32_t)))
+				status = ANN_NOMEM;
+		}
 	}
-	for (uint32_t q0 = 0; status == ANN_OK && q0 < nq; q0 += (uint32_t) m)
+
+	/*
+	 * Chunk c: its candidates (the codes' search) and their row copies on
+	 * this thread while the device copies in and re-scores chunk c - 1 on
+	 * the re-score stream; then chunk c - 1's best k, then chunk c's
+	 * re-score queued. The slots alternate.
+	 */
+	chunks = (uint32_t) ((nq + m - 1) / m);
+	for (uint32_t c = 0; status == ANN_OK && c <= chunks; c++)
 	{
-		uint32_t	mm = nq - q0 < m ? nq - q0 : (uint32_t) m;
-		const float *q = lane->query + (size_t) q0 * dims;
+		double		t0 = NowMs(),
+					t1 = t0,
+					t2 = t0,
+					t3;
 
-		/* candidates: each shard's nearest by the codes' exact distance */
-		for (uint32_t s = 0; status == ANN_OK && s < S; s++)
-			if (want_s[s])
-				status = AnnB200Search(ix->shards[s], q, mm, ordinals ? lane->ids + start[s] : NULL,
-									   ordinals ? elig[s] : 0, (uint32_t) want_s[s], ANNB200_L2, 0,
-									   (uint32_t) want_s[s], lane->dist + m * off[s], lane->id + m * off[s],
-									   lane->counts + (size_t) s * m, NULL, lane->stream);
-		if (status == ANN_OK &&
-			(cudaMemcpyAsync(lane->hostId, lane->id, m * C * sizeof(int64_t), cudaMemcpyDeviceToHost,
-							 lane->stream) != cudaSuccess ||
-			 cudaMemcpyAsync(counts, lane->counts, S * m * sizeof(uint32_t), cudaMemcpyDeviceToHost,
-							 lane->stream) != cudaSuccess ||
-			 cudaStreamSynchronize(lane->stream) != cudaSuccess))
-			status = ANN_BACKEND_ERROR;
-		if (status != ANN_OK)
-			break;
-
-		/* their FP32 rows, from host memory */
-		for (uint32_t i = 0; i < mm; i++)
+		if (c < chunks)
 		{
-			uint32_t	pos = 0;
+			uint32_t	q0 = (uint32_t) (c * m);
+			uint32_t	mm = nq - q0 < m ? nq - q0 : (uint32_t) m;
+			const float *q = lane->query + (size_t) q0 * dims;
 
-			for (uint32_t s = 0; s < S; s++)
-				for (uint32_t j = 0; want_s[s] && j < counts[(size_t) s * m + i]; j++)
+			/* candidates: each shard's nearest by the codes' exact distance */
+			for (uint32_t s = 0; status == ANN_OK && s < S; s++)
+				if (want_s[s])
+					status = AnnB200Search(ix->shards[s], q, mm, ordinals ? lane->ids + start[s] : NULL,
+										   ordinals ? elig[s] : 0, (uint32_t) want_s[s], ANNB200_L2, 0,
+										   (uint32_t) want_s[s], lane->dist + m * off[s], lane->id + m * off[s],
+										   lane->counts + (size_t) s * m, NULL, lane->stream);
+			if (status == ANN_OK &&
+				(cudaMemcpyAsync(lane->hostId, lane->id, m * C * sizeof(int64_t), cudaMemcpyDeviceToHost,
+								 lane->stream) != cudaSuccess ||
+				 cudaMemcpyAsync(counts, lane->counts, S * m * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+								 lane->stream) != cudaSuccess ||
+				 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+				status = ANN_BACKEND_ERROR;
+			if (status != ANN_OK)
+				break;
+
+			/* their FP32 rows, from host memory */
+			t1 = NowMs();
+			GatherAll(ix, lane, &lane->slot[c & 1], counts, cand[c & 1], want_s, off, m, C, mm);
+			t2 = NowMs();
+		}
+		if (c > 0)
+		{
+			uint32_t	p0 = (uint32_t) ((c - 1) * m);
+			uint32_t	pm = nq - p0 < m ? nq - p0 : (uint32_t) m;
+			QuantSlot  *sl = &lane->slot[(c - 1) & 1];
+			const uint64_t *cd = cand[(c - 1) & 1];
+
+			if (cudaEventSynchronize(lane->rescoreDone[(c - 1) & 1]) != cudaSuccess)
+			{
+				status = ANN_BACKEND_ERROR;
+				break;
+			}
+
+			/* the best k by (distance, ordinal): distances are >= 0, so their bits order them */
+			for (uint32_t i = 0; i < pm; i++)
+			{
+				uint32_t	n = sl->hostCandCounts[i];
+				uint32_t	r = n < k ? n : k;
+
+				for (uint32_t j = 0; j < n; j++)
 				{
-					uint64_t	ord = (uint64_t) lane->hostId[m * off[s] + (size_t) i * want_s[s] + j];
+					uint32_t	bits;
 
-					memcpy(lane->hostStage + ((size_t) i * C + pos) * dims, ix->vectors + ord * dims,
-						   sizeof(float) * dims);
-					cand[(size_t) i * C + pos++] = ord;
+					memcpy(&bits, &sl->hostRescored[(size_t) i * C + j], sizeof(bits));
+					keys[j] = (uint64_t) bits << 32 | cd[(size_t) i * C + j];
 				}
-			lane->hostCandCounts[i] = pos;
-		}
-		if (cudaMemcpyAsync(lane->stage, lane->hostStage, (size_t) mm * C * dims * sizeof(float),
-							cudaMemcpyHostToDevice, lane->stream) != cudaSuccess ||
-			cudaMemcpyAsync(lane->candCounts, lane->hostCandCounts, mm * sizeof(uint32_t), cudaMemcpyHostToDevice,
-							lane->stream) != cudaSuccess)
-			status = ANN_BACKEND_ERROR;
-		if (status == ANN_OK)
-			status = AnnB200RescoreRows(q, mm, dims, lane->stage, (uint32_t) C, lane->candCounts, lane->rescored,
-										lane->stream);
-		if (status == ANN_OK &&
-			(cudaMemcpyAsync(lane->hostRescored, lane->rescored, (size_t) mm * C * sizeof(float),
-							 cudaMemcpyDeviceToHost, lane->stream) != cudaSuccess ||
-			 cudaStreamSynchronize(lane->stream) != cudaSuccess))
-			status = ANN_BACKEND_ERROR;
+				SelectSmallest(keys, n, r);
+				qsort(keys, r, sizeof(*keys), KeyCompare);
+				for (uint32_t j = 0; j < r; j++)
+				{
+					uint32_t	bits = (uint32_t) (keys[j] >> 32);
 
-		/* the best k by (distance, ordinal): distances are >= 0, so their bits order them */
-		for (uint32_t i = 0; status == ANN_OK && i < mm; i++)
+					memcpy(&out_dist[(size_t) (p0 + i) * k + j], &bits, sizeof(bits));
+					out_ordinal[(size_t) (p0 + i) * k + j] = keys[j] & 0xffffffffu;
+				}
+				out_count[p0 + i] = r;
+			}
+		}
+		t3 = NowMs();
+		if (c < chunks)
 		{
-			uint32_t	n = lane->hostCandCounts[i];
-			uint32_t	r = n < k ? n : k;
+			uint32_t	q0 = (uint32_t) (c * m);
+			uint32_t	mm = nq - q0 < m ? nq - q0 : (uint32_t) m;
+			QuantSlot  *sl = &lane->slot[c & 1];
+			cudaStream_t rs = lane->rescoreStream;
 
-			for (uint32_t j = 0; j < n; j++)
-			{
-				uint32_t	bits;
-
-				memcpy(&bits, &lane->hostRescored[(size_t) i * C + j], sizeof(bits));
-				keys[j] = (uint64_t) bits << 32 | cand[(size_t) i * C + j];
-			}
-			qsort(keys, n, sizeof(*keys), KeyCompare);
-			for (uint32_t j = 0; j < r; j++)
-			{
-				uint32_t	bits = (uint32_t) (keys[j] >> 32);
-
-				memcpy(&out_dist[(size_t) (q0 + i) * k + j], &bits, sizeof(bits));
-				out_ordinal[(size_t) (q0 + i) * k + j] = keys[j] & 0xffffffffu;
-			}
-			out_count[q0 + i] = r;
+			if (cudaMemcpyAsync(sl->stage, sl->hostStage, (size_t) mm * C * dims * sizeof(float),
+								cudaMemcpyHostToDevice, rs) != cudaSuccess ||
+				cudaMemcpyAsync(sl->candCounts, sl->hostCandCounts, mm * sizeof(uint32_t), cudaMemcpyHostToDevice,
+								rs) != cudaSuccess)
+				status = ANN_BACKEND_ERROR;
+			if (status == ANN_OK)
+				status = AnnB200RescoreRows(lane->query + (size_t) q0 * dims, mm, dims, sl->stage, (uint32_t) C,
+											sl->candCounts, sl->rescored, rs);
+			if (status == ANN_OK &&
+				(cudaMemcpyAsync(sl->hostRescored, sl->rescored, (size_t) mm * C * sizeof(float),
+								 cudaMemcpyDeviceToHost, rs) != cudaSuccess ||
+				 cudaEventRecord(lane->rescoreDone[c & 1], rs) != cudaSuccess))
+				status = ANN_BACKEND_ERROR;
 		}
+		if (debug)
+			fprintf(stderr, "annb200 quantized index: chunk %u of %u, %llu candidates a query: search %.2f ms, "
+					"row copies %.2f ms, re-score wait and best k %.2f ms\n", c, chunks, (unsigned long long) C,
+					t1 - t0, t2 - t1, t3 - t2);
 	}
+	/* nothing of this call stays queued on the lane's buffers */
+	if (lane->rescoreReady && cudaStreamSynchronize(lane->rescoreStream) != cudaSuccess && status == ANN_OK)
+		status = ANN_BACKEND_ERROR;
 done:
 	free(start);
 	free(elig);
@@ -684,7 +899,8 @@ done:
 	free(off);
 	free(local);
 	free(counts);
-	free(cand);
+	free(cand[0]);
+	free(cand[1]);
 	free(keys);
 	return status;
 }

@@ -234,6 +234,10 @@ def test_quantized_copy_route(backends, tmp_path, monkeypatch, kind, d):
     ref_name, our_name = 'cpu_q_%s_%d' % (kind, d), 'b200_q_%s_%d' % (kind, d)
     assert load(cpu, ref_name, directory) == 0
     monkeypatch.setenv('ANN_B200_INDEX_COPY', 'quant')
+    # 8 MB of staged rows a chunk: the 32-query batch runs as two chunks
+    # (27 queries on the tensor-core scan, then 5), the second one's rows
+    # copied while the first is re-scored
+    monkeypatch.setenv('ANN_B200_QUANT_STAGE_MB', '8')
     assert load(ours, our_name, directory) == 0
     q = synth.mixture_queries(48, d, 60, seed=22)
     jobs = Jobs()
