@@ -31,6 +31,13 @@
  *                           ann/server/cuvs.c:3446-3455, on the device.
  *   AnnB200BitmapRows()     filter bitmap to eligible row list, the expand_*
  *                           kernels of ann/server/cuvs.c:1910-1968.
+ *   AnnB200IndexCreate/Search  a loaded index's exact search (the worker's
+ *                           load_index / search_index, cpu.c:286-407);
+ *                           AnnB200IndexCreateQuant the same from the
+ *                           directory's quantized copy (the quantized scan
+ *                           route, ann/server/cuvs.c:4585-4930), with
+ *                           AnnB200RescoreRows its FP32 re-score
+ *                           (ExactDistance, cuvs.c:2930-2942).
  */
 #ifndef ANNB200_H
 #define ANNB200_H
