@@ -309,6 +309,47 @@ int			AnnB200RescoreRows(const float *queries, uint32_t nq, uint32_t dims,
 							   float *out, void *stream);
 
 /*
+ * Typed gathered jobs: the worker's gathered job (ops 7/10, AnnGatheredJob
+ * and AnnGatheredExact semantics, ann/server/backend.h:45-62,
+ * ann/server/cpu.c:218-276) for rows in any storage format above and a batch
+ * of queries, the additive typed op the reference's protocol leaves room for
+ * ("new operations get new numbers", ann/server/PROTOCOL.md:118-120): PG
+ * callers with halfvec, FP8, NVFP4 or bit rows send them as they are instead
+ * of converting them to FP32.
+ *
+ * Host memory throughout. Per job: rows x row-bytes codes (and scales) in
+ * `dtype`'s format; queries FP32 [nq][dims], or packed bits
+ * [nq][ceil(dims/8)] for Hamming (bit rows and Hamming go together). Each
+ * query's results are every row within d_k + 1e-3*|d_k| + 1e-6 of its k-th
+ * distance, sorted by (distance, row): distances[q*cap + i], ids[q*cap + i],
+ * nresults[q]. status: ANN_INVALID for a bad combination, a missing scale
+ * array, a non-finite query or row value (NaN codes included), a zero query
+ * under cosine, or a window larger than cap (cap >= rows always has room);
+ * k = 0 or rows = 0 give no results and ANN_OK. Synchronous; thread-safe
+ * like search_gathered (each thread stages through its own buffers).
+ */
+typedef struct AnnB200TypedJob
+{
+	uint32_t	dtype;			/* ANNB200_F32 .. ANNB200_BIT */
+	uint32_t	metric;			/* ANNB200_L2 .. ANNB200_HAMMING */
+	uint32_t	dimensions;
+	uint32_t	rows;
+	uint32_t	nq;				/* queries in the batch */
+	uint32_t	k;
+	uint32_t	cap;			/* result room a query */
+	uint32_t	reserved;		/* 0 */
+	const void *queries;
+	const void *codes;
+	const void *block_scales;	/* NVFP4 only */
+	const float *row_scales;	/* E4M3 and NVFP4 */
+	double	   *distances;		/* [nq][cap] */
+	uint32_t   *ids;			/* [nq][cap] row numbers */
+	uint32_t   *nresults;		/* [nq] */
+	int			status;			/* AnnStatus */
+} AnnB200TypedJob;
+int			AnnB200SearchTyped(AnnB200TypedJob *jobs, uint32_t n);
+
+/*
  * Kernels this library has launched in this process (all devices). A caller
  * that times a region reads it before and after to count its launches.
  */

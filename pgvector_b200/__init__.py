@@ -208,6 +208,46 @@ def search_gathered(jobs):
     return out
 
 
-__all__ = ['Shard', 'merge_topk', 'bitmap_rows', 'bitmap_rows_static', 'backend', 'search_gathered', 'device_count', 'load', 'check',
+def search_typed(jobs):
+    """Typed gathered jobs (AnnB200SearchTyped): jobs are dicts with dtype,
+    metric, queries (float32 [nq, dims], or packed-bit uint8 [nq, bytes] for
+    Hamming), codes (the rows in dtype's format: float32, float16 / int16
+    bits, or uint8 codes [rows, row-bytes]), dims, k, and block_scales /
+    row_scales where the format has them; cap defaults to the rows. Returns
+    per job (status, [[(row, distance), ...] per query])."""
+    lib = load()
+    n = len(jobs)
+    arr = (_abi.AnnB200TypedJob * n)()
+    keep = []
+    caps = []
+    for i, j in enumerate(jobs):
+        q = np.ascontiguousarray(j['queries'])
+        c = np.ascontiguousarray(j['codes'])
+        nq, rows = q.shape[0], c.shape[0]
+        cap = int(j.get('cap', max(rows, 1)))
+        dist = np.zeros(max(nq * cap, 1), np.float64)
+        ids = np.zeros(max(nq * cap, 1), np.uint32)
+        cnt = np.zeros(max(nq, 1), np.uint32)
+        bs = None if j.get('block_scales') is None else np.ascontiguousarray(j['block_scales'], dtype=np.uint8)
+        rs = None if j.get('row_scales') is None else np.ascontiguousarray(j['row_scales'], dtype=np.float32)
+        keep += [q, c, dist, ids, cnt, bs, rs]
+        a = arr[i]
+        a.dtype, a.metric, a.dimensions, a.rows = int(j['dtype']), int(j['metric']), int(j['dims']), rows
+        a.nq, a.k, a.cap = nq, int(j['k']), cap
+        a.queries, a.codes = q.ctypes.data, c.ctypes.data
+        a.block_scales = None if bs is None else bs.ctypes.data
+        a.row_scales = None if rs is None else rs.ctypes.data
+        a.distances, a.ids, a.nresults = dist.ctypes.data, ids.ctypes.data, cnt.ctypes.data
+        caps.append((nq, cap, dist, ids, cnt))
+    lib.AnnB200SearchTyped(arr, n)
+    out = []
+    for i, (nq, cap, dist, ids, cnt) in enumerate(caps):
+        out.append((arr[i].status, [[(int(ids[q * cap + r]), float(dist[q * cap + r])) for r in range(cnt[q])]
+                                    for q in range(nq)]))
+    del keep
+    return out
+
+
+__all__ = ['Shard', 'search_typed', 'merge_topk', 'bitmap_rows', 'bitmap_rows_static', 'backend', 'search_gathered', 'device_count', 'load', 'check',
            'AnnB200Error', 'F32', 'F16', 'E4M3', 'NVFP4', 'BIT', 'L2', 'IP', 'COSINE', 'HAMMING', 'WINDOW',
            'FORCE_SIMT', 'OK', 'INVALID', 'UNSUPPORTED', 'NOMEM', 'BACKEND_ERROR']

@@ -18,6 +18,16 @@ class AnnGatheredJob(ctypes.Structure):
                 ('nresults', ctypes.c_uint32), ('status', ctypes.c_int)]
 
 
+class AnnB200TypedJob(ctypes.Structure):
+    """AnnB200TypedJob of annb200.h: one typed gathered job."""
+    _fields_ = [('dtype', ctypes.c_uint32), ('metric', ctypes.c_uint32), ('dimensions', ctypes.c_uint32),
+                ('rows', ctypes.c_uint32), ('nq', ctypes.c_uint32), ('k', ctypes.c_uint32),
+                ('cap', ctypes.c_uint32), ('reserved', ctypes.c_uint32), ('queries', ctypes.c_void_p),
+                ('codes', ctypes.c_void_p), ('block_scales', ctypes.c_void_p), ('row_scales', ctypes.c_void_p),
+                ('distances', ctypes.c_void_p), ('ids', ctypes.c_void_p), ('nresults', ctypes.c_void_p),
+                ('status', ctypes.c_int)]
+
+
 class AnnIndex(ctypes.Structure):
     _fields_ = [('generation', ctypes.c_uint64), ('rows', ctypes.c_uint32), ('dimensions', ctypes.c_uint32),
                 ('vectors', ctypes.POINTER(ctypes.c_float)), ('backend_state', ctypes.c_void_p)]

@@ -77,6 +77,10 @@ typedef struct Lane
 	size_t		resultCap;
 	uint32_t   *counts;			/* device: per-query counts of a batch */
 	size_t		countsBytes;
+	uint8_t    *scales;			/* device: a typed job's NVFP4 block scales */
+	size_t		scalesBytes;
+	float	   *rowScales;		/* device: a typed job's row scales */
+	size_t		rowScalesBytes;
 	double	   *hostDist;		/* pinned result staging */
 	int64_t    *hostId;
 	size_t		hostCap;
@@ -1004,6 +1008,199 @@ AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const ui
 	free(counts);
 	cudaSetDevice(prev);
 	return status;
+}
+
+/* Bytes a row takes in a storage format. */
+static size_t
+TypedRowBytes(uint32_t dtype, uint32_t dims)
+{
+	switch (dtype)
+	{
+		case ANNB200_F32:
+			return (size_t) dims * 4;
+		case ANNB200_F16:
+			return (size_t) dims * 2;
+		case ANNB200_E4M3:
+			return (size_t) (dims + 15) / 16 * 16;
+		case ANNB200_NVFP4:
+			return (size_t) (dims + 15) / 16 * 8;
+		default:
+			return (size_t) (dims + 7) / 8;
+	}
+}
+
+/*
+ * Whether a typed job's queries and rows hold only values the reference's
+ * arithmetic scores: finite FP32 / FP16 values, no E4M3 NaN code (E4M3 has
+ * no infinity; E2M1 has neither), finite row scales, and a query of nonzero
+ * norm under cosine.
+ */
+static int
+TypedValid(const AnnB200TypedJob *job)
+{
+	uint32_t	dims = job->dimensions;
+	size_t		rb = TypedRowBytes(job->dtype, dims);
+
+	if (job->metric != ANNB200_HAMMING)
+		for (uint32_t q = 0; q < job->nq; q++)
+		{
+			const float *v = (const float *) job->queries + (size_t) q * dims;
+			double		norm = 0;
+
+			if (!AllFinite(v, dims))
+				return 0;
+			for (uint32_t d = 0; d < dims; d++)
+				norm += (double) v[d] * v[d];
+			if (job->metric == ANNB200_COSINE && norm == 0)
+				return 0;
+		}
+	for (uint32_t r = 0; r < job->rows; r++)
+	{
+		const uint8_t *row = (const uint8_t *) job->codes + (size_t) r * rb;
+
+		switch (job->dtype)
+		{
+			case ANNB200_F32:
+				if (!AllFinite((const float *) row, dims))
+					return 0;
+				break;
+			case ANNB200_F16:
+				for (uint32_t d = 0; d < dims; d++)
+				{
+					uint16_t	h;
+
+					memcpy(&h, row + 2 * (size_t) d, 2);
+					if ((h & 0x7c00) == 0x7c00)
+						return 0;
+				}
+				break;
+			case ANNB200_E4M3:
+				for (uint32_t d = 0; d < dims; d++)
+					if ((row[d] & 0x7f) == 0x7f)
+						return 0;
+				break;
+			case ANNB200_NVFP4:
+				for (uint32_t b = 0; b < (dims + 15) / 16; b++)
+					if ((((const uint8_t *) job->block_scales)[(size_t) r * ((dims + 15) / 16) + b] & 0x7f) == 0x7f)
+						return 0;
+				break;
+			default:
+				break;
+		}
+		if ((job->dtype == ANNB200_E4M3 || job->dtype == ANNB200_NVFP4) && !isfinite(job->row_scales[r]))
+			return 0;
+	}
+	return 1;
+}
+
+/*
+ * One typed gathered job: rows of any storage format and a batch of
+ * queries, each query with the gathered job's results (AnnGatheredExact
+ * semantics, ann/server/cpu.c:218-276, over the rows decoded as the
+ * shard search decodes them).
+ */
+static int
+TypedJob(AnnB200TypedJob *job)
+{
+	Lane	   *lane;
+	uint32_t	dims = job->dimensions;
+	int			hamming = job->metric == ANNB200_HAMMING;
+	size_t		rb,
+				qb,
+				blocks,
+				results;
+	int			status;
+
+	for (uint32_t q = 0; job->nresults && q < job->nq; q++)
+		job->nresults[q] = 0;
+	if (job->dtype > ANNB200_BIT || job->metric > ANNB200_HAMMING || (job->dtype == ANNB200_BIT) != hamming ||
+		dims == 0 || dims > (hamming ? 65536u : ANN_MAX_DIM) || job->reserved != 0)
+		return ANN_INVALID;
+	if (job->nq == 0 || job->k == 0 || job->rows == 0)
+		return ANN_OK;
+	if (job->queries == NULL || job->codes == NULL || job->nresults == NULL || job->distances == NULL ||
+		job->ids == NULL || job->cap == 0 ||
+		(job->dtype == ANNB200_NVFP4 && job->block_scales == NULL) ||
+		((job->dtype == ANNB200_E4M3 || job->dtype == ANNB200_NVFP4) && job->row_scales == NULL))
+		return ANN_INVALID;
+	if (!TypedValid(job))
+		return ANN_INVALID;
+	if (InjectLost())
+		return ANN_BACKEND_ERROR;
+	lane = LaneGet();
+	if (lane == NULL)
+		return ANN_BACKEND_ERROR;
+	rb = TypedRowBytes(job->dtype, dims);
+	qb = hamming ? (size_t) (dims + 7) / 8 : (size_t) dims * 4;
+	blocks = (dims + 15) / 16;
+	results = (size_t) job->nq * job->cap;
+	if (!Grow(&lane->rows, &lane->rowsBytes, (size_t) job->rows * rb) ||
+		!Grow((void **) &lane->query, &lane->queryBytes, (size_t) job->nq * qb) ||
+		(job->dtype == ANNB200_NVFP4 &&
+		 !Grow((void **) &lane->scales, &lane->scalesBytes, (size_t) job->rows * blocks)) ||
+		((job->dtype == ANNB200_E4M3 || job->dtype == ANNB200_NVFP4) &&
+		 !Grow((void **) &lane->rowScales, &lane->rowScalesBytes, (size_t) job->rows * sizeof(float))) ||
+		!Grow((void **) &lane->counts, &lane->countsBytes, (size_t) job->nq * sizeof(uint32_t)) ||
+		!LaneResults(lane, results))
+		return ANN_NOMEM;
+	if (cudaMemcpyAsync(lane->rows, job->codes, (size_t) job->rows * rb, cudaMemcpyHostToDevice,
+						lane->stream) != cudaSuccess ||
+		cudaMemcpyAsync(lane->query, job->queries, (size_t) job->nq * qb, cudaMemcpyHostToDevice,
+						lane->stream) != cudaSuccess ||
+		(job->dtype == ANNB200_NVFP4 &&
+		 cudaMemcpyAsync(lane->scales, job->block_scales, (size_t) job->rows * blocks, cudaMemcpyHostToDevice,
+						 lane->stream) != cudaSuccess) ||
+		((job->dtype == ANNB200_E4M3 || job->dtype == ANNB200_NVFP4) &&
+		 cudaMemcpyAsync(lane->rowScales, job->row_scales, (size_t) job->rows * sizeof(float),
+						 cudaMemcpyHostToDevice, lane->stream) != cudaSuccess))
+		return ANN_BACKEND_ERROR;
+	{
+		const void *bs = job->dtype == ANNB200_NVFP4 ? lane->scales : NULL;
+		const float *rs = job->dtype == ANNB200_E4M3 || job->dtype == ANNB200_NVFP4 ? lane->rowScales : NULL;
+
+		if (lane->shard == NULL)
+			status = AnnB200ShardCreate(lane->device, job->dtype, dims, job->rows, lane->rows, bs, rs, 0, 0,
+										lane->stream, &lane->shard);
+		else
+			status = AnnB200ShardAssign(lane->shard, job->dtype, dims, job->rows, lane->rows, bs, rs, 0,
+										lane->stream);
+	}
+	if (status == ANN_OK)
+		status = AnnB200Search(lane->shard, lane->query, job->nq, NULL, 0, job->k, job->metric, ANNB200_WINDOW,
+							   job->cap, lane->dist, lane->id, lane->counts, NULL, lane->stream);
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(job->nresults, lane->counts, (size_t) job->nq * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostDist, lane->dist, results * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, results * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status != ANN_OK)
+	{
+		for (uint32_t q = 0; q < job->nq; q++)
+			job->nresults[q] = 0;
+		return status;
+	}
+	for (uint32_t q = 0; q < job->nq; q++)
+		for (uint32_t i = 0; i < job->nresults[q]; i++)
+		{
+			job->distances[(size_t) q * job->cap + i] = lane->hostDist[(size_t) q * job->cap + i];
+			job->ids[(size_t) q * job->cap + i] = (uint32_t) lane->hostId[(size_t) q * job->cap + i];
+		}
+	atomic_fetch_add(&DeviceJobs, 1);
+	return ANN_OK;
+}
+
+int
+AnnB200SearchTyped(AnnB200TypedJob *jobs, uint32_t n)
+{
+	if (n && jobs == NULL)
+		return ANN_INVALID;
+	for (uint32_t i = 0; i < n; i++)
+		jobs[i].status = TypedJob(&jobs[i]);
+	return ANN_OK;
 }
 
 static void

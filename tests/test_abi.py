@@ -131,3 +131,34 @@ def test_quantized_index_arguments_checked_on_host():
         assert st == pb.INVALID and not out.value, i
     assert lib.AnnB200RescoreRows(None, 0, 4, None, 8, None, None, None) == 0   # nothing to do
     assert lib.AnnB200RescoreRows(None, 2, 4, None, 8, None, None, None) == pb.INVALID
+
+
+def test_typed_jobs_checked_on_host():
+    # AnnB200SearchTyped refuses bad jobs before touching a device
+    q = np.ones((2, 4), np.float32)
+    rows = np.ones((3, 4), np.float32)
+    bad_q = q.copy()
+    bad_q[1, 2] = np.nan
+    e4 = np.zeros((3, 16), np.uint8)
+    e4_nan = e4.copy()
+    e4_nan[2, 1] = 0xff
+    half_inf = np.full((3, 4), 0x7c00, np.uint16)
+    cases = [
+        dict(dtype=pb.F32, metric=3, dims=4, k=1, queries=q, codes=rows),                 # Hamming on floats
+        dict(dtype=pb.BIT, metric=0, dims=32, k=1, queries=np.zeros((1, 4), np.uint8),
+             codes=np.zeros((3, 4), np.uint8)),                                            # bits without Hamming
+        dict(dtype=pb.F32, metric=0, dims=4, k=1, queries=bad_q, codes=rows),             # non-finite query
+        dict(dtype=pb.F32, metric=2, dims=4, k=1, queries=np.zeros((1, 4), np.float32), codes=rows),
+        dict(dtype=pb.E4M3, metric=1, dims=4, k=1, queries=q, codes=e4),                  # no row scales
+        dict(dtype=pb.E4M3, metric=1, dims=4, k=1, queries=q, codes=e4_nan, row_scales=np.ones(3, np.float32)),
+        dict(dtype=pb.F16, metric=0, dims=4, k=1, queries=q, codes=half_inf),             # infinite halves
+        dict(dtype=pb.NVFP4, metric=0, dims=4, k=1, queries=q, codes=np.zeros((3, 8), np.uint8),
+             row_scales=np.ones(3, np.float32)),                                           # no block scales
+        dict(dtype=9, metric=0, dims=4, k=1, queries=q, codes=rows),
+    ]
+    got = pb.search_typed(cases)
+    assert [s for s, _ in got] == [pb.INVALID] * len(cases)
+    # nothing to do: OK without a device
+    got = pb.search_typed([dict(dtype=pb.F32, metric=0, dims=4, k=0, queries=q, codes=rows),
+                           dict(dtype=pb.F32, metric=0, dims=4, k=3, queries=q, codes=rows[:0])])
+    assert got == [(0, [[], []]), (0, [[], []])]

@@ -324,3 +324,43 @@ def test_backend_in_memory_index(cuda):
             assert [res[j].id for j in range(n.value)] == list(i[0, :c[0]])
             assert [res[j].distance for j in range(n.value)] == list(d[0, :c[0]])
     b.destroy(ctypes.byref(index))
+
+
+# ---------------------------------------------------------------- typed gathered jobs
+
+def test_typed_gathered_jobs(cuda):
+    # AnnB200SearchTyped: host rows in every storage format, a batch of
+    # queries each, window results equal to the oracle's window search
+    import pgvector_b200 as pb
+    d = 96
+    x = synth.mixture(3000, d, 30, seed=31)
+    q = synth.mixture_queries(24, d, 30, seed=32)
+    h = synth.to_half_bits(x)
+    c8, r8 = oracle.quantize_fp8(x)
+    c4, b4, r4 = oracle.quantize_nvfp4(x)
+    bits, proto = synth.bit_rows(3000, 256, 16, flip=0.05, seed=33)
+    qb = bits[np.random.default_rng(34).integers(0, 3000, 20)].copy()
+    cases = [
+        (oracle.F32, 0, x, q, None, None, 10, d),
+        (oracle.F32, 2, x, q[:1], None, None, 7, d),            # one query (CUDA cores)
+        (oracle.F16, 2, h, q, None, None, 100, d),              # halfvec cosine, a tensor-core batch
+        (oracle.E4M3, 1, c8, q, None, r8, 50, d),
+        (oracle.NVFP4, 0, c4, q[:5], b4, r4, 20, d),
+        (oracle.BIT, 3, bits, qb, None, None, 30, 256),         # Hamming: ties kept in the window
+    ]
+    jobs = [dict(dtype=dt, metric=m, dims=dims, k=k, queries=qs, codes=codes, block_scales=bs, row_scales=rs)
+            for dt, m, codes, qs, bs, rs, k, dims in cases]
+    for run in range(2):                                        # the lane's buffers reused
+        got = pb.search_typed(jobs)
+        for (dt, m, codes, qs, bs, rs, k, dims), (status, res) in zip(cases, got):
+            od, oi, oc, os_ = oracle.search(dt, dims, codes, qs, k, m, block_scales=bs, row_scales=rs,
+                                            window=True, cap=codes.shape[0])
+            assert status == 0 and (os_ == 0).all()
+            for qi in range(qs.shape[0]):
+                want = [(int(oi[qi, r]), float(od[qi, r])) for r in range(oc[qi])]
+                assert res[qi] == want, (dt, m, qi, res[qi][:4], want[:4])
+    # a window that outgrows cap, and the rows' duplicates under Hamming
+    dup = np.repeat(bits[:10], 50, axis=0)
+    st, res = pb.search_typed([dict(dtype=oracle.BIT, metric=3, dims=256, k=1, queries=bits[:1], codes=dup,
+                                    cap=10)])[0]
+    assert st == pb.INVALID and res == [[]]
