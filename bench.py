@@ -58,12 +58,17 @@ WORKLOADS = {
        'rank boundaries)',
     5: 'config 5: Hamming kNN on 1,024-bit vectors, N=1B rows XOR-perturbed from 65,536 Bernoulli(0.5) '
        'prototypes at a 5% flip rate, batch 1,024, k=100, row-sharded; integer distances, ties by row id',
+    6: 'config 6 (loaded index from its quantized copy): L2 kNN through AnnB200IndexSearch with host buffers, '
+       'd=768, N=2M FP32 rows from a 1,000-centre Gaussian mixture (sigma 0.3) with their NVFP4 copy on the '
+       'device in 3 index shards, the FP32 rows in host memory; batch 1,024, k=100, quant_slack 256, '
+       'slack_ratio 100',
 }
 DEFAULTS = {1: dict(rows=100_000, dims=128, batch=1000, k=10, centres=100),
             2: dict(rows=10_000_000, dims=768, batch=1024, k=100, centres=1000),
             3: dict(rows=100_000_000, dims=1024, batch=1024, k=500, centres=4096),
             4: dict(rows=200_000_000, dims=768, batch=4096, k=100, centres=65536),
-            5: dict(rows=1_000_000_000, dims=1024, batch=1024, k=100, centres=65536)}
+            5: dict(rows=1_000_000_000, dims=1024, batch=1024, k=100, centres=65536),
+            6: dict(rows=2_000_000, dims=768, batch=1024, k=100, centres=1000)}
 
 
 def args_parse():
@@ -72,7 +77,7 @@ def args_parse():
     ap.add_argument('--steps', type=int, default=None, help='timed steps (default 300; 10 for configs 3/4, 5 for 5)')
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument('--config', type=int, default=2, choices=[1, 2, 3, 4, 5, 6])
     ap.add_argument('--rows', type=int, default=None)
     ap.add_argument('--dims', type=int, default=None)
     ap.add_argument('--batch', type=int, default=None)
@@ -288,6 +293,10 @@ def full_candidates(args):
 def reference_arm(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
+        return 0
+    if args.config == 6:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'the reference serves quantized copies only from '
+                          'its cuVS / Blackwell GPU backend, which does not build without cuVS'}), flush=True)
         return 0
     threads = os.cpu_count() or 1
     per_step = max(threads, 8)
@@ -673,10 +682,89 @@ def verify_by_rescoring(args, w, result, nq, codes, bscales, rscales, oracle_dty
 
 # ---------------------------------------------------------------- our arm
 
+def index_quant_bench(args):
+    """Config 6: a loaded index served from its NVFP4 copy (the reference's
+    quantized scan route) through the host-memory API, beside the same index
+    served from its FP32 rows on the device. One step = one synchronous
+    AnnB200IndexSearch of the batch, timed by the host clock around the call
+    (its inputs and results are host memory, so this is the end-to-end
+    figure); every copy and kernel of the route is inside it."""
+    import ctypes
+    import numpy as np
+    import torch
+    import pgvector_b200 as pb
+    from pgvector_b200 import synth
+    if int(os.environ.get('RANK', '0')) != 0:
+        return 0
+    torch.cuda.set_device(0)
+    lib = pb.load()
+    n, d, nq, k = args.rows, args.dims, args.batch, args.k
+    blocks = (d + 15) // 16
+    xh = np.empty((n, d), np.float32)
+    codes = np.empty((n, blocks * 8), np.uint8)
+    bs = np.empty((n, blocks), np.uint8)
+    rs = np.empty(n, np.float32)
+    chunk = 1 << 18
+    x = synth.torch_mixture(n, d, args.centres, sigma=0.3, seed=args.seed, dtype=torch.float32)
+    for lo in range(0, n, chunk):
+        c, b, r = synth.torch_quantize_nvfp4(x[lo:lo + chunk])
+        hi = lo + c.shape[0]
+        codes[lo:hi], bs[lo:hi], rs[lo:hi] = c.cpu().numpy(), b.cpu().numpy(), r.cpu().numpy()
+        xh[lo:hi] = x[lo:hi].cpu().numpy()
+    del x
+    torch.cuda.empty_cache()
+    q = synth.torch_mixture_queries(nq, d, args.centres, sigma=0.3, seed=args.seed + 1).cpu().numpy()
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    quant, exact = ctypes.c_void_p(), ctypes.c_void_p()
+    shards = (ctypes.c_uint64 * 3)(n // 3, n // 3, n - 2 * (n // 3))
+    pb.check(lib.AnnB200IndexCreateQuant(0, d, n, pb.NVFP4, P(codes), P(bs), P(rs), P(xh), 3, shards, 256, 100,
+                                         ctypes.byref(quant)))
+    pb.check(lib.AnnB200IndexCreate(0, d, n, P(xh), ctypes.byref(exact)))
+    out = {}
+    for name, ix in (('quant', quant), ('fp32', exact)):
+        dist = np.zeros((nq, k), np.float32)
+        ords = np.zeros((nq, k), np.uint64)
+        cnt = np.zeros(nq, np.uint32)
+        for _ in range(args.warmup):
+            pb.check(lib.AnnB200IndexSearch(ix, P(q), nq, None, 0, k, P(dist), P(ords), P(cnt)))
+        clocks = ClockSampler(0)
+        clocks.start()
+        launches0 = lib.AnnB200LaunchCount()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            pb.check(lib.AnnB200IndexSearch(ix, P(q), nq, None, 0, k, P(dist), P(ords), P(cnt)))
+        secs = time.perf_counter() - t0
+        launches = lib.AnnB200LaunchCount() - launches0
+        out[name] = (nq * args.steps / secs, secs / args.steps * 1e3, ords.copy(), launches, clocks.stop())
+    lib.AnnB200IndexDestroy(quant)
+    lib.AnnB200IndexDestroy(exact)
+    qps, ms, ords, launches, clock_info = out['quant']
+    recall = float(np.mean([len(set(ords[i].tolist()) & set(out['fp32'][2][i].tolist())) / k for i in range(nq)]))
+    cands = 3 * (k + max(256, k))                    # per query: k + slack in each of the 3 shards
+    line = {'metric': 'QPS at batch %d, k=%d, loaded index served from its NVFP4 copy' % (nq, k),
+            'value': qps, 'unit': 'queries/s', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded Gaussian mixture on the GPU, quantized there, held in host memory)',
+            'config': {'workload': WORKLOADS[6], 'global_batch': nq, 'rows': n, 'dims': d, 'k': k,
+                       'parallelism': 'single GPU + host copy threads',
+                       'timing': 'host clock around the synchronous call (end to end)'},
+            'e2e': {'value': qps, 'unit': 'queries/s', 'h2d_bytes_per_step': nq * d * 4 * (1 + cands),
+                    'd2h_bytes_per_step': nq * (cands * 12 + k * 12)},
+            'roofline': None,
+            'roofline_note': 'bound by the candidates\' FP32 rows crossing from host memory '
+                             '(%.0f MB a batch)' % (nq * cands * d * 4 / 1e6),
+            'cpu_baseline': None, 'gpu_launches': launches, 'clocks': clock_info,
+            'fp32_route_qps': out['fp32'][0], 'recall_vs_fp32_route': recall}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = args_parse()
     if args.impl == 'reference':
         return reference_arm(args)
+    if args.config == 6:
+        return index_quant_bench(args)
     os.environ.setdefault('ANN_B200_KERNEL_TIMING', '1')
     import torch
     import torch.distributed as dist
