@@ -739,6 +739,26 @@ def index_quant_bench(args):
     lib.AnnB200IndexDestroy(quant)
     lib.AnnB200IndexDestroy(exact)
     qps, ms, ords, launches, clock_info = out['quant']
+
+    # CPU baseline: the oracle's restatement of the route (the reference has
+    # no CPU implementation of it) on a bounded sample of the batch, all host
+    # threads; its answers checked against the device's
+    cpu, verified = None, None
+    if not args.no_cpu_baseline:
+        import oracle
+        threads = os.cpu_count() or 1
+        bounds = [0, n // 3, 2 * (n // 3), n]
+        done, t0, agree = 0, time.perf_counter(), True
+        while done < nq and (done < 2 or time.perf_counter() - t0 < args.cpu_seconds):
+            got = oracle.quant_index_search(oracle.NVFP4, xh, codes, q[done:done + 1], k, bounds, block_scales=bs,
+                                            row_scales=rs, threads=threads)[0]
+            agree = agree and [o for o, _ in got] == [int(o) for o in ords[done][:len(got)]]
+            done += 1
+        secs = time.perf_counter() - t0
+        cpu = {'value': done / secs, 'unit': 'queries/s', 'cores': threads, 'kind': 'port',
+               'sample': '%d queries of the batch through oracle.quant_index_search (3 shard searches of the '
+                         'NVFP4 codes + FP64 re-score of the candidates) in %.1f s' % (done, secs)}
+        verified = agree
     recall = float(np.mean([len(set(ords[i].tolist()) & set(out['fp32'][2][i].tolist())) / k for i in range(nq)]))
     cands = 3 * (k + max(256, k))                    # per query: k + slack in each of the 3 shards
     line = {'metric': 'QPS at batch %d, k=%d, loaded index served from its NVFP4 copy' % (nq, k),
@@ -753,8 +773,8 @@ def index_quant_bench(args):
             'roofline': None,
             'roofline_note': 'bound by the candidates\' FP32 rows crossing from host memory '
                              '(%.0f MB a batch)' % (nq * cands * d * 4 / 1e6),
-            'cpu_baseline': None, 'gpu_launches': launches, 'clocks': clock_info,
-            'fp32_route_qps': out['fp32'][0], 'recall_vs_fp32_route': recall}
+            'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clock_info,
+            'fp32_route_qps': out['fp32'][0], 'recall_vs_fp32_route': recall, 'verified_vs_oracle': verified}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -148,7 +148,7 @@ def exact_distance_f64(rows, query):
 
 
 def quant_index_search(dtype, vectors, codes, queries, k, bounds, ordinals=None, block_scales=None,
-                       row_scales=None, quant_slack=256, slack_ratio=100):
+                       row_scales=None, quant_slack=256, slack_ratio=100, threads=1):
     """The reference's quantized scan route for a loaded index (SearchGather,
     ann/server/cuvs.c:4585-4930): per index shard [bounds[s], bounds[s+1]),
     the min(k + slack, eligible) rows nearest by the exact L2 distance of the
@@ -176,7 +176,7 @@ def quant_index_search(dtype, vectors, codes, queries, k, bounds, ordinals=None,
                 continue
             bs = None if block_scales is None else block_scales[lo:hi]
             _, ids, cnt, _ = search(dtype, dims, codes[lo:hi], q[None], kk, 0, ids=local, block_scales=bs,
-                                    row_scales=row_scales[lo:hi], threads=1)
+                                    row_scales=row_scales[lo:hi], threads=threads)
             cand += [lo + int(i) for i in ids[0, :cnt[0]]]
         cand = np.array(cand, dtype=np.int64)
         if len(cand) == 0:
