@@ -749,7 +749,7 @@ def index_quant_bench(args):
         threads = os.cpu_count() or 1
         bounds = [0, n // 3, 2 * (n // 3), n]
         done, t0, agree = 0, time.perf_counter(), True
-        while done < nq and (done < 2 or time.perf_counter() - t0 < args.cpu_seconds):
+        while done < nq and (done < 1 or time.perf_counter() - t0 < args.cpu_seconds):
             got = oracle.quant_index_search(oracle.NVFP4, xh, codes, q[done:done + 1], k, bounds, block_scales=bs,
                                             row_scales=rs, threads=threads)[0]
             agree = agree and [o for o, _ in got] == [int(o) for o in ords[done][:len(got)]]
