@@ -271,3 +271,58 @@ def test_quantized_copy_route(backends, tmp_path, monkeypatch, kind, d):
     recall = found / total
     print('%s d=%d recall against the exact FP32 answer: %.4f' % (kind, d, recall))
     assert recall >= 0.97
+
+
+def test_quantized_index_and_typed_jobs_from_threads(cuda):
+    # the worker calls from many lane threads at once: each thread stages
+    # through its own buffers, searches of one shard take turns on its lock,
+    # and every thread's answers equal the one-thread answers
+    import threading
+    import pgvector_b200 as pb
+    lib = pb.load()
+    n, d = 20000, 64
+    x = synth.mixture(n, d, 40, seed=41)
+    q = synth.mixture_queries(64, d, 40, seed=42)
+    codes, bs, rs = oracle.quantize_nvfp4(x)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ix = ctypes.c_void_p()
+    shard_rows = (ctypes.c_uint64 * 2)(12000, 8000)
+    assert lib.AnnB200IndexCreateQuant(0, d, n, pb.NVFP4, P(codes), P(bs), P(rs), P(x), 2, shard_rows, 64, 100,
+                                       ctypes.byref(ix)) == 0
+
+    def index_search(part, k):
+        qs = np.ascontiguousarray(q[part * 16:(part + 1) * 16])
+        dist = np.zeros((16, k), np.float32)
+        ords = np.zeros((16, k), np.uint64)
+        cnt = np.zeros(16, np.uint32)
+        assert lib.AnnB200IndexSearch(ix, P(qs), 16, None, 0, k, P(dist), P(ords), P(cnt)) == 0
+        return dist.view(np.uint32).tolist(), ords.tolist(), cnt.tolist()
+
+    h = synth.to_half_bits(x)
+
+    def typed(part):
+        return pb.search_typed([dict(dtype=pb.F16, metric=pb.L2, dims=d, k=5 + part, codes=h[part::4],
+                                     queries=q[part * 16:(part + 1) * 16])])
+
+    try:
+        want = [(index_search(p, 10 + p), typed(p)) for p in range(4)]
+        got = [None] * 4
+        errors = []
+
+        def run(p):
+            try:
+                for _ in range(3):
+                    got[p] = (index_search(p, 10 + p), typed(p))
+                    assert got[p] == want[p]
+            except Exception as e:              # surfaced below, with the thread's part
+                errors.append((p, repr(e)))
+
+        threads = [threading.Thread(target=run, args=(p,)) for p in range(4)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(300)
+        assert not errors, errors
+        assert got == want
+    finally:
+        lib.AnnB200IndexDestroy(ix)
