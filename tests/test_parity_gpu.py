@@ -364,3 +364,31 @@ def test_typed_gathered_jobs(cuda):
     st, res = pb.search_typed([dict(dtype=oracle.BIT, metric=3, dims=256, k=1, queries=bits[:1], codes=dup,
                                     cap=10)])[0]
     assert st == pb.INVALID and res == [[]]
+
+
+def test_typed_gathered_jobs_odd_shapes(cuda):
+    # row pitches the tensor-core scan cannot read (CUDA-core path), padded
+    # FP8 rows, odd NVFP4 block counts, a k past the rows, and a query batch
+    # split into several jobs
+    import pgvector_b200 as pb
+    rng = np.random.default_rng(51)
+    cases = []
+    for d in (37, 20, 72):
+        x = synth.mixture(700, d, 9, seed=d)
+        q = synth.mixture_queries(18, d, 9, seed=d + 1)
+        cases.append((oracle.F16, 0, synth.to_half_bits(x), q, None, None, 12, d))
+        c8, r8 = oracle.quantize_fp8(x)
+        cases.append((oracle.E4M3, 2, c8, q, None, r8, 5, d))
+        c4, b4, r4 = oracle.quantize_nvfp4(x)
+        cases.append((oracle.NVFP4, 1, c4, q, b4, r4, 900, d))   # k past the 700 rows
+    bits = np.packbits(rng.random((500, 1000)) < 0.5, axis=1, bitorder='little')
+    cases.append((oracle.BIT, 3, bits, bits[rng.integers(0, 500, 17)], None, None, 8, 1000))
+    jobs = [dict(dtype=dt, metric=m, dims=dims, k=k, queries=qs, codes=codes, block_scales=bs, row_scales=rs)
+            for dt, m, codes, qs, bs, rs, k, dims in cases]
+    got = pb.search_typed(jobs)
+    for (dt, m, codes, qs, bs, rs, k, dims), (status, res) in zip(cases, got):
+        od, oi, oc, os_ = oracle.search(dt, dims, codes, qs, k, m, block_scales=bs, row_scales=rs, window=True,
+                                        cap=codes.shape[0])
+        assert status == 0 and (os_ == 0).all()
+        for qi in range(qs.shape[0]):
+            assert res[qi] == [(int(oi[qi, r]), float(od[qi, r])) for r in range(oc[qi])], (dt, dims, qi)
