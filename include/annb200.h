@@ -288,6 +288,9 @@ int			AnnB200IndexSearch(AnnB200Index *index, const float *queries, uint32_t nq,
  * (ExactDistance, ann/server/cuvs.c:2930-2942); the best k of all shards by
  * (distance, ordinal). Like the reference's, the answer is the exact one
  * whenever the true k nearest are among each shard's candidates.
+ * The FP32 rows' pages are registered for the device to read the
+ * candidates' rows in place (ANN_B200_QUANT_MAPPED=0 turns this off); where
+ * registration fails, the rows are copied through pinned staging.
  */
 int			AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype,
 									const void *codes, const void *block_scales,
@@ -307,6 +310,17 @@ int			AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t
 int			AnnB200RescoreRows(const float *queries, uint32_t nq, uint32_t dims,
 							   const float *rows, uint32_t stride, const uint32_t *counts,
 							   float *out, void *stream);
+
+/*
+ * The same re-score with the rows fetched by ordinal: out[q][j] =
+ * ExactDistance of rows[ords[q][j]] to queries[q]. rows is any array the
+ * device can read: device memory, or host memory registered and mapped for
+ * the device (the quantized index route reads vectors.f32 this way where
+ * the mapping can be registered). ords [nq][stride] u64, device.
+ */
+int			AnnB200RescoreGather(const float *queries, uint32_t nq, uint32_t dims,
+								 const float *rows, const uint64_t *ords, uint32_t stride,
+								 const uint32_t *counts, float *out, void *stream);
 
 /*
  * Typed gathered jobs: the worker's gathered job (ops 7/10, AnnGatheredJob

@@ -41,6 +41,8 @@ SIGNATURES = {
                                         ctypes.POINTER(c_void_p)]),
     'AnnB200RescoreRows': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_void_p, c_void_p,
                                    c_void_p]),
+    'AnnB200RescoreGather': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
+                                     c_void_p, c_void_p]),
     'AnnB200IndexDestroy': (None, [c_void_p]),
     'AnnB200SearchTyped': (c_int, [c_void_p, c_uint32]),
     'AnnB200IndexSearch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_void_p, c_void_p,

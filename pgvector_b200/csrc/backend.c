@@ -57,6 +57,8 @@ typedef struct QuantSlot
 	size_t		candCountsBytes;
 	uint32_t   *hostCandCounts; /* pinned */
 	size_t		hostCandCountsBytes;
+	uint64_t   *ords;			/* device: candidate ordinals (mapped rows) */
+	size_t		ordsBytes;
 } QuantSlot;
 
 typedef struct Lane
@@ -340,6 +342,9 @@ struct AnnB200Index
 	AnnB200Shard **shards;		/* per index shard: its codes on the device */
 	uint64_t   *bounds;			/* nshards + 1 row bounds */
 	const float *vectors;		/* host FP32 rows (borrowed) */
+	const float *mapped;		/* the same rows as the device reads them, when
+								 * their pages could be registered; else NULL */
+	void	   *registered;		/* start of the registered pages */
 	uint32_t	quantSlack;
 	uint32_t	slackRatio;
 };
@@ -413,9 +418,54 @@ AnnB200IndexDestroy(AnnB200Index *ix)
 	AnnB200ShardDestroy(ix->shard);
 	for (uint32_t s = 0; ix->shards && s < ix->nshards; s++)
 		AnnB200ShardDestroy(ix->shards[s]);
+	if (ix->registered)
+	{
+		cudaSetDevice(ix->device);
+		cudaHostUnregister(ix->registered);
+	}
 	free(ix->shards);
 	free(ix->bounds);
 	free(ix);
+}
+
+/*
+ * Register the pages of a quantized index's FP32 rows for the device to read
+ * them in place (read-only where the driver supports it, as a read-only file
+ * mapping needs). Where that fails the rows are copied through pinned
+ * staging instead; nothing else changes.
+ */
+static void
+MapRows(AnnB200Index *ix)
+{
+	long		page = sysconf(_SC_PAGESIZE);
+	uintptr_t	start = (uintptr_t) ix->vectors;
+	uintptr_t	base = start & ~((uintptr_t) page - 1);
+	uintptr_t	end = start + (uintptr_t) ix->rows * ix->dims * sizeof(float);
+	size_t		len = (size_t) ((end - base + (uintptr_t) page - 1) & ~((uintptr_t) page - 1));
+	unsigned	flags = cudaHostRegisterMapped | cudaHostRegisterPortable;
+	void	   *dev = NULL;
+
+	if (cudaSetDevice(ix->device) != cudaSuccess)
+		return;
+	if (cudaHostRegister((void *) base, len, flags | cudaHostRegisterReadOnly) != cudaSuccess)
+	{
+		(void) cudaGetLastError();
+		if (cudaHostRegister((void *) base, len, flags) != cudaSuccess)
+		{
+			(void) cudaGetLastError();
+			return;
+		}
+	}
+	if (cudaHostGetDevicePointer(&dev, (void *) base, 0) != cudaSuccess || dev == NULL)
+	{
+		(void) cudaGetLastError();
+		cudaHostUnregister((void *) base);
+		return;
+	}
+	ix->registered = (void *) base;
+	ix->mapped = (const float *) ((const char *) dev + (start - base));
+	if (EnvLong("ANN_B200_DEBUG", 0) > 0)
+		fprintf(stderr, "annb200 quantized index: FP32 rows read in place (%zu bytes registered)\n", len);
 }
 
 int
@@ -481,6 +531,8 @@ AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype
 									block_scales ? (const uint8_t *) block_scales + first * blocks : NULL,
 									row_scales + first, (int64_t) first, ANNB200_SHARD_HOST, NULL, &ix->shards[s]);
 	}
+	if (status == ANN_OK && EnvLong("ANN_B200_QUANT_MAPPED", 1) != 0)
+		MapRows(ix);
 	cudaSetDevice(prev);
 	if (status != ANN_OK)
 	{
@@ -627,6 +679,22 @@ GatherRows(void *arg)
 		slot->hostCandCounts[i] = pos;
 	}
 	return NULL;
+}
+
+/* Each query's candidate ordinals, shard after shard, without their rows. */
+static void
+ListCandidates(const AnnB200Index *ix, Lane *lane, QuantSlot *slot, const uint32_t *counts, uint64_t *cand,
+			   const uint64_t *want, const uint64_t *off, size_t m, uint64_t C, uint32_t mm)
+{
+	for (uint32_t i = 0; i < mm; i++)
+	{
+		uint32_t	pos = 0;
+
+		for (uint32_t s = 0; s < ix->nshards; s++)
+			for (uint32_t j = 0; want[s] && j < counts[(size_t) s * m + i]; j++)
+				cand[(size_t) i * C + pos++] = (uint64_t) lane->hostId[m * off[s] + (size_t) i * want[s] + j];
+		slot->hostCandCounts[i] = pos;
+	}
 }
 
 #define GATHER_MAX_THREADS 32
@@ -776,8 +844,9 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 		{
 			QuantSlot  *sl = &lane->slot[h];
 
-			if (!Grow((void **) &sl->stage, &sl->stageBytes, m * C * dims * sizeof(float)) ||
-				!GrowHost((void **) &sl->hostStage, &sl->hostStageBytes, m * C * dims * sizeof(float)) ||
+			if ((ix->mapped ? !Grow((void **) &sl->ords, &sl->ordsBytes, m * C * sizeof(uint64_t)) :
+				 (!Grow((void **) &sl->stage, &sl->stageBytes, m * C * dims * sizeof(float)) ||
+				  !GrowHost((void **) &sl->hostStage, &sl->hostStageBytes, m * C * dims * sizeof(float)))) ||
 				!Grow((void **) &sl->rescored, &sl->rescoredBytes, m * C * sizeof(float)) ||
 				!GrowHost((void **) &sl->hostRescored, &sl->hostRescoredBytes, m * C * sizeof(float)) ||
 				!Grow((void **) &sl->candCounts, &sl->candCountsBytes, m * sizeof(uint32_t)) ||
@@ -823,9 +892,13 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 			if (status != ANN_OK)
 				break;
 
-			/* their FP32 rows, from host memory */
+			/* their FP32 rows, from host memory (or only their ordinals, when
+			 * the device reads the rows in place) */
 			t1 = NowMs();
-			GatherAll(ix, lane, &lane->slot[c & 1], counts, cand[c & 1], want_s, off, m, C, mm);
+			if (ix->mapped)
+				ListCandidates(ix, lane, &lane->slot[c & 1], counts, cand[c & 1], want_s, off, m, C, mm);
+			else
+				GatherAll(ix, lane, &lane->slot[c & 1], counts, cand[c & 1], want_s, off, m, C, mm);
 			t2 = NowMs();
 		}
 		if (c > 0)
@@ -874,12 +947,18 @@ QuantSearch(AnnB200Index *ix, Lane *lane, uint32_t nq, const uint64_t *ordinals,
 			QuantSlot  *sl = &lane->slot[c & 1];
 			cudaStream_t rs = lane->rescoreStream;
 
-			if (cudaMemcpyAsync(sl->stage, sl->hostStage, (size_t) mm * C * dims * sizeof(float),
-								cudaMemcpyHostToDevice, rs) != cudaSuccess ||
+			if ((ix->mapped ?
+				 cudaMemcpyAsync(sl->ords, cand[c & 1], (size_t) mm * C * sizeof(uint64_t), cudaMemcpyHostToDevice,
+								 rs) :
+				 cudaMemcpyAsync(sl->stage, sl->hostStage, (size_t) mm * C * dims * sizeof(float),
+								 cudaMemcpyHostToDevice, rs)) != cudaSuccess ||
 				cudaMemcpyAsync(sl->candCounts, sl->hostCandCounts, mm * sizeof(uint32_t), cudaMemcpyHostToDevice,
 								rs) != cudaSuccess)
 				status = ANN_BACKEND_ERROR;
-			if (status == ANN_OK)
+			if (status == ANN_OK && ix->mapped)
+				status = AnnB200RescoreGather(lane->query + (size_t) q0 * dims, mm, dims, ix->mapped, sl->ords,
+											  (uint32_t) C, sl->candCounts, sl->rescored, rs);
+			else if (status == ANN_OK)
 				status = AnnB200RescoreRows(lane->query + (size_t) q0 * dims, mm, dims, sl->stage, (uint32_t) C,
 											sl->candCounts, sl->rescored, rs);
 			if (status == ANN_OK &&

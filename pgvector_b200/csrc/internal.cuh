@@ -383,6 +383,10 @@ void launch_probe_table(const int64_t *ids, const uint32_t *counts, uint32_t nq,
 // FP32 re-score (FP64 sum in dimension order) of gathered candidate rows.
 void launch_rescore_rows(const float *queries, uint32_t nq, uint32_t dims, const float *rows, uint32_t stride,
                          const uint32_t *counts, float *out, cudaStream_t st);
+// The same, each candidate's row fetched by ordinal (rows: device-readable).
+void launch_rescore_gather(const float *queries, uint32_t nq, uint32_t dims, const float *rows,
+                           const uint64_t *ords, uint32_t stride, const uint32_t *counts, float *out,
+                           cudaStream_t st);
 // query_lo_map: the low BF16 halves of the queries (FP32 rows only, else NULL).
 cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64_t a_row0,
                            const CUtensorMap &query_map, const CUtensorMap *query_lo_map, uint32_t kpad, uint32_t bn,

@@ -1157,6 +1157,47 @@ __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nb
   }
 }
 
+// The same re-score with each candidate's row fetched by ordinal from a row
+// array the device reads directly (device memory, or host memory mapped for
+// the device): one warp a candidate, its row staged through shared memory in
+// 128-byte reads, the sum formed by lane 0 in dimension order.
+constexpr int RG_WARPS = 8, RG_CHUNK = 512;
+
+__global__ void __launch_bounds__(RG_WARPS * 32) rescore_gather(const float *__restrict__ queries, uint32_t nq,
+                                                                uint32_t dims, const float *__restrict__ rows,
+                                                                const uint64_t *__restrict__ ords, uint32_t stride,
+                                                                const uint32_t *__restrict__ counts,
+                                                                float *__restrict__ out) {
+  __shared__ float buf[RG_WARPS][RG_CHUNK];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t w = (uint64_t)blockIdx.x * RG_WARPS + warp;
+  if (w >= (uint64_t)nq * stride) return;                  // whole warps leave together
+  const uint32_t q = (uint32_t)(w / stride), j = (uint32_t)(w % stride);
+  if (counts && j >= counts[q]) return;
+  const float *x = rows + ords[w] * (uint64_t)dims;
+  const float *v = queries + (uint64_t)q * dims;
+  double sum = 0.0;
+  for (uint32_t d0 = 0; d0 < dims; d0 += RG_CHUNK) {
+    const uint32_t n = min((uint32_t)RG_CHUNK, dims - d0);
+    float r[RG_CHUNK / 32];
+#pragma unroll
+    for (int t = 0; t < RG_CHUNK / 32; t++) {
+      const uint32_t i = lane + 32u * t;
+      r[t] = i < n ? x[d0 + i] : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < RG_CHUNK / 32; t++) buf[warp][lane + 32 * t] = r[t];
+    __syncwarp();
+    if (lane == 0)
+      for (uint32_t t = 0; t < n; t++) {
+        const double delta = __dsub_rn((double)buf[warp][t], (double)__ldg(v + d0 + t));
+        sum = __dadd_rn(sum, __dmul_rn(delta, delta));
+      }
+    __syncwarp();
+  }
+  if (lane == 0) out[w] = __double2float_rn(__dsqrt_rn(sum));
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
@@ -1168,6 +1209,15 @@ void launch_rescore_rows(const float *queries, uint32_t nq, uint32_t dims, const
   const int vec4 = (dims & 3) == 0 && (((uintptr_t)queries | (uintptr_t)rows) & 15) == 0;
   if (n)
     rescore_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(queries, nq, dims, rows, stride, counts, out, vec4);
+}
+
+void launch_rescore_gather(const float *queries, uint32_t nq, uint32_t dims, const float *rows,
+                           const uint64_t *ords, uint32_t stride, const uint32_t *counts, float *out,
+                           cudaStream_t st) {
+  const uint64_t n = (uint64_t)nq * stride;
+  if (n)
+    rescore_gather<<<(unsigned)((n + RG_WARPS - 1) / RG_WARPS), RG_WARPS * 32, 0, st>>>(queries, nq, dims, rows, ords,
+                                                                                        stride, counts, out);
 }
 
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st) {

@@ -1141,6 +1141,20 @@ extern "C" int AnnB200RescoreRows(const float *queries, uint32_t nq, uint32_t di
   return OK;
 }
 
+extern "C" int AnnB200RescoreGather(const float *queries, uint32_t nq, uint32_t dims, const float *rows,
+                                    const uint64_t *ords, uint32_t stride, const uint32_t *counts, float *out,
+                                    void *stream) {
+  if (nq == 0 || stride == 0) return OK;
+  if (!queries || !rows || !ords || !out) return fail(INVALID, "NULL pointer");
+  if (dims == 0) return fail(INVALID, "dimensions 0");
+  if ((uint64_t)nq * stride > 0xffffffffull) return fail(INVALID, "more than 2^32 candidates");
+  cudaStream_t st = (cudaStream_t)stream;
+  launch_rescore_gather(queries, nq, dims, rows, ords, stride, counts, out, st);
+  CK(cudaGetLastError(), "rescore gather");
+  counted(1);
+  return OK;
+}
+
 extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint64_t *count,
                                  void *stream) {
   if (!count) return fail(INVALID, "count pointer is NULL");

@@ -326,3 +326,70 @@ def test_quantized_index_and_typed_jobs_from_threads(cuda):
         assert got == want
     finally:
         lib.AnnB200IndexDestroy(ix)
+
+
+def test_rescore_gather_kernel(cuda):
+    # AnnB200RescoreGather: rows fetched by ordinal, the restated ExactDistance
+    import torch
+    import pgvector_b200 as pb
+    lib = pb.load()
+    rng = np.random.default_rng(17)
+    for d in (768, 37, 1100):                   # one, a partial, and three row chunks
+        n, nq, stride = 3000, 4, 50
+        x = (rng.standard_normal((n, d)) * 10 ** rng.uniform(-2, 2, (n, 1))).astype(np.float32)
+        q = rng.standard_normal((nq, d)).astype(np.float32)
+        ords = rng.integers(0, n, (nq, stride)).astype(np.uint64)
+        counts = np.array([50, 0, 23, 1], dtype=np.uint32)
+        xd, qd = torch.from_numpy(x).to(cuda), torch.from_numpy(q).to(cuda)
+        od = torch.from_numpy(ords.view(np.int64)).to(cuda)
+        cd = torch.from_numpy(counts.view(np.int32)).to(cuda)
+        out = torch.full((nq, stride), -1.0, dtype=torch.float32, device=cuda)
+        assert lib.AnnB200RescoreGather(ctypes.c_void_p(qd.data_ptr()), nq, d, ctypes.c_void_p(xd.data_ptr()),
+                                        ctypes.c_void_p(od.data_ptr()), stride, ctypes.c_void_p(cd.data_ptr()),
+                                        ctypes.c_void_p(out.data_ptr()),
+                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for i in range(nq):
+            c = int(counts[i])
+            want = oracle.exact_distance_f64(x[ords[i, :c].astype(np.int64)], q[i])
+            assert np.array_equal(got[i, :c].view(np.uint32), want.view(np.uint32)), (d, i)
+            assert np.all(got[i, c:] == -1.0)
+
+
+@pytest.mark.parametrize('mapped', ['1', '0'])
+def test_quantized_index_rows_in_place_or_copied(cuda, monkeypatch, capfd, mapped):
+    # the quantized route with the FP32 rows read in place by the device
+    # (registered host memory) and copied through staging: both equal the
+    # restated route
+    import pgvector_b200 as pb
+    lib = pb.load()
+    n, d = 30000, 128
+    x = synth.mixture(n, d, 50, seed=61)
+    q = synth.mixture_queries(40, d, 50, seed=62)
+    codes, rs = oracle.quantize_fp8(x)
+    monkeypatch.setenv('ANN_B200_QUANT_MAPPED', mapped)
+    monkeypatch.setenv('ANN_B200_DEBUG', '1')
+    monkeypatch.setenv('ANN_B200_QUANT_STAGE_MB', '16')     # several chunks
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ix = ctypes.c_void_p()
+    shard_rows = (ctypes.c_uint64 * 3)(10000, 15000, 5000)
+    assert lib.AnnB200IndexCreateQuant(0, d, n, pb.E4M3, P(codes), None, P(rs), P(x), 3, shard_rows, 32, 150,
+                                       ctypes.byref(ix)) == 0
+    try:
+        assert ('read in place' in capfd.readouterr().err) == (mapped == '1')
+        ords_f = np.sort(np.random.default_rng(63).choice(n, 4000, replace=False)).astype(np.uint64)
+        for k, filt in ((10, None), (40, ords_f)):
+            dist = np.zeros((40, k), np.float32)
+            ords = np.zeros((40, k), np.uint64)
+            cnt = np.zeros(40, np.uint32)
+            assert lib.AnnB200IndexSearch(ix, P(q), 40, None if filt is None else P(filt),
+                                          0 if filt is None else len(filt), k, P(dist), P(ords), P(cnt)) == 0
+            want = oracle.quant_index_search(oracle.E4M3, x, codes, q, k, [0, 10000, 25000, n], ordinals=filt,
+                                             row_scales=rs, quant_slack=32, slack_ratio=150, threads=8)
+            for i in range(40):
+                assert cnt[i] == len(want[i])
+                assert [int(o) for o in ords[i, :cnt[i]]] == [o for o, _ in want[i]], (k, i)
+                assert dist[i, :cnt[i]].view(np.uint32).tolist() == [w.view(np.uint32).item() for _, w in want[i]]
+    finally:
+        lib.AnnB200IndexDestroy(ix)
