@@ -42,6 +42,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -120,16 +122,24 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.lines = []
+        self.skip = 0
 
-    def start(self):
+    def start(self, wait_s=10.0):
+        """Start sampling and wait (up to wait_s) for the first reading, so
+        that nvidia-smi's own start-up stays outside any timed region."""
         try:
             self.proc = subprocess.Popen(['nvidia-smi', '--query-gpu=' + self.FIELDS, '--format=csv,noheader,nounits',
-                                          '-i', str(self.gpu), '-lms', '200'], stdout=subprocess.PIPE,
+                                          '-i', str(self.gpu), '-lms', '100'], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
             self.proc = None
+            return
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < wait_s and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.skip = len(self.lines)      # readings before the measured region starts
 
     def _read(self):
         for line in self.proc.stdout:
@@ -146,7 +156,7 @@ class ClockSampler:
         self.thread.join(2)
         sm, mx, reasons = [], None, set()
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for line in self.lines:
+        for line in self.lines[self.skip:]:
             parts = [p.strip() for p in line.split(',')]
             if len(parts) < 9:
                 continue
@@ -387,13 +397,11 @@ def build_config1(args, rank, world, dev):
         return d, i, c, hi - lo
     w.step = step
 
-    def verify(result, nq):
-        import numpy as np
+    def local_oracle(nq):
         import oracle
-        od, oi, oc, _ = oracle.search(oracle.F32, args.dims, x, queries[:nq].cpu().numpy(), args.k, 0)
-        return bool(np.array_equal(result[1][:nq].cpu().numpy(), oi) and
-                    np.array_equal(result[0][:nq].cpu().numpy(), od))
-    w.verify = verify if world == 1 else (lambda result, nq: None)
+        od, oi, oc, _ = oracle.search(oracle.F32, args.dims, x[lo:hi], queries[:nq].cpu().numpy(), args.k, 0)
+        return od, oi + lo, oc
+    w.local_oracle = local_oracle
     return w
 
 
@@ -433,17 +441,16 @@ def build_config2(args, rank, world, dev):
         return d, i, c, rows.numel()
     w.step = step
 
-    def verify(result, nq):
+    def local_oracle(nq):
+        # the oracle over this rank's candidate rows only, with global ids
         import numpy as np
         import oracle
         rows_t = pb.bitmap_rows(w.inputs[1], nbits)
         rows_np = rows_t.cpu().numpy().view(np.uint32).astype(np.int64)
-        h = codes[rows_t.long()].cpu().numpy().view(np.uint16)          # only the candidate rows
-        qn = queries[:nq].cpu().numpy()
-        od, oi, oc, _ = oracle.search(oracle.F16, args.dims, h, qn, args.k, 2)
-        return bool(np.array_equal(result[1][:nq].cpu().numpy(), rows_np[oi] + lo) and
-                    np.array_equal(result[0][:nq].cpu().numpy(), od))
-    w.verify = verify
+        h = codes[rows_t.long()].cpu().numpy().view(np.uint16)
+        od, oi, oc, _ = oracle.search(oracle.F16, args.dims, h, queries[:nq].cpu().numpy(), args.k, 2)
+        return od, np.where(oi >= 0, rows_np[np.maximum(oi, 0)] + lo, -1), oc
+    w.local_oracle = local_oracle
     del centres, qv, lab
     return w
 
@@ -483,9 +490,9 @@ def build_config3(args, rank, world, dev):
         return d, i, c, hi - lo
     w.step = step
 
-    def verify(result, nq):
-        return verify_by_rescoring(args, w, result, nq, codes, None, scales, oracle_dtype=2, lo=lo, hi=hi)
-    w.verify = verify
+    def local_rescore(result, nq):
+        return rescore_local(args, w, result, nq, codes, None, scales, oracle_dtype=2, lo=lo, hi=hi, world=world)
+    w.local_rescore = local_rescore
     del centres
     return w
 
@@ -570,11 +577,15 @@ def build_config4(args, rank, world, dev):
         return d, i, c, w.pass_rows
     w.step = step
 
-    def verify(result, nq):
+    def local_oracle(nq):
+        # the oracle over the lists this rank holds (its share of each), with global ids
         import oracle
         qn = queries[:nq].cpu().numpy()
         pr = local[:nq].cpu().numpy().view(np.uint32)
         lists = sorted(set(int(x) for x in pr.ravel() if x != 0xffffffff))
+        if not lists:
+            return (np.full((nq, args.k), np.inf), np.full((nq, args.k), -1, dtype=np.int64),
+                    np.zeros(nq, dtype=np.uint32))
         # the probed lists only, re-packed list-major with their global ids
         parts, new_off, ids = [], [0], []
         for l in lists:
@@ -589,9 +600,8 @@ def build_config4(args, rank, world, dev):
                                          np.array(new_off, dtype=np.uint64), pr2, args.k, 0,
                                          row_ids=np.concatenate(ids), block_scales=bscales[sel].cpu().numpy(),
                                          row_scales=rscales[sel].cpu().numpy())
-        return bool(np.array_equal(result[1][:nq].cpu().numpy(), oi) and
-                    np.array_equal(result[0][:nq].cpu().numpy(), od))
-    w.verify = verify if world == 1 else (lambda result, nq: None)
+        return od, oi, oc
+    w.local_oracle = local_oracle
     del cent
     return w
 
@@ -640,44 +650,122 @@ def build_config5(args, rank, world, dev):
         return d, i, c, hi - lo
     w.step = step
 
-    def verify(result, nq):
-        return verify_by_rescoring(args, w, result, nq, codes, None, None, oracle_dtype=4, lo=lo, hi=hi)
-    w.verify = verify
+    def local_rescore(result, nq):
+        return rescore_local(args, w, result, nq, codes, None, None, oracle_dtype=4, lo=lo, hi=hi, world=world)
+    w.local_rescore = local_rescore
     return w
 
 
-def verify_by_rescoring(args, w, result, nq, codes, bscales, rscales, oracle_dtype, lo, hi):
-    """Size-independent check for shards too large for the oracle: the
-    returned rows' distances recomputed by the oracle equal the returned
-    ones bit for bit and are sorted by (distance, id), and no row of a
-    200,000-row random sample beats the k-th (single GPU)."""
+def rescore_local(args, w, result, nq, codes, bscales, rscales, oracle_dtype, lo, hi, world):
+    """This rank's half of the size-independent check for shards too large
+    for the oracle (configs 3 and 5): per checked query, the oracle's exact
+    distance of every returned row this rank holds, and of a random sample
+    of this rank's rows (200,000 rows over all ranks). The check itself
+    (check_rescored) runs on rank 0 over every rank's part."""
     import numpy as np
     import torch
     import oracle
-    if hi - lo != args.rows:
-        return None
-    ok = True
-    rng = np.random.default_rng(args.seed + 11)
-    sample = np.unique(rng.integers(0, hi - lo, 200_000))
+    rng = np.random.default_rng(args.seed + 11 + lo)
+    sample = np.unique(rng.integers(0, hi - lo, max(1, 200_000 // world)))
+    parts = []
     for qi in range(nq):
         q = w.inputs[0][qi:qi + 1].cpu().numpy()
-        ids = result[1][qi].cpu().numpy()
-        dist = result[0][qi].cpu().numpy()
-        rows = np.unique(np.concatenate([ids - lo, sample]))
+        n = int(result[2][qi].item())
+        ids = result[1][qi, :n].cpu().numpy()
+        mine = ids[(ids >= lo) & (ids < hi)] - lo
+        rows = np.unique(np.concatenate([mine, sample])).astype(np.int64)
         rt = torch.from_numpy(rows).to(codes.device)
         sub = codes[rt].cpu().numpy()
         bs = None if bscales is None else bscales[rt].cpu().numpy()
         rs = None if rscales is None else rscales[rt].cpu().numpy()
         od, oi, oc, _ = oracle.search(oracle_dtype, args.dims, sub, q, len(rows), w.metric, block_scales=bs,
                                       row_scales=rs)
-        exact = dict(zip(rows[oi[0][:oc[0]]].tolist(), od[0][:oc[0]].tolist()))
-        got = [exact[int(i - lo)] for i in ids]
-        ok &= bool(np.array_equal(np.array(got), dist))
-        ok &= all((dist[j], ids[j]) <= (dist[j + 1], ids[j + 1]) for j in range(len(ids) - 1))
+        exact = dict(zip((rows[oi[0][:oc[0]]] + lo).tolist(), od[0][:oc[0]].tolist()))
+        mine_set = set((mine + lo).tolist())
+        parts.append({'returned': {r: d for r, d in exact.items() if r in mine_set},
+                      'sample': [(d, r) for r, d in exact.items()]})
+    return parts
+
+
+def check_rescored(result, parts, nq):
+    """Rank 0: every returned row's distance equals the oracle's exact one
+    (bit for bit), the rows are sorted by (distance, id), and no sampled row
+    of any rank beats the k-th returned one."""
+    import numpy as np
+    ok = True
+    for qi in range(nq):
+        n = int(result[2][qi].item())
+        ids = result[1][qi, :n].cpu().numpy().tolist()
+        dist = result[0][qi, :n].cpu().numpy().tolist()
+        exact, sample = {}, []
+        for p in parts:
+            exact.update(p[qi]['returned'])
+            sample.extend(p[qi]['sample'])
+        ok &= n > 0 and all(i in exact for i in ids)
+        if not ok:
+            return False
+        ok &= bool(np.array_equal(np.array([exact[i] for i in ids]), np.array(dist)))
+        ok &= all((dist[j], ids[j]) <= (dist[j + 1], ids[j + 1]) for j in range(n - 1))
         kth = (dist[-1], ids[-1])
-        member = set((ids - lo).tolist())
-        ok &= all((d, int(r) + lo) >= kth for r, d in exact.items() if int(r) not in member)
-    return ok
+        member = set(ids)
+        ok &= all((d, r) >= kth for d, r in sample if r not in member)
+    return bool(ok)
+
+
+def merge_reference_lists(lists, k):
+    """The oracle's answer for the whole corpus from every rank's oracle
+    answer over its own rows: lists = [(dist [nq][cap], global id [nq][cap],
+    count [nq])] per rank; per query the k smallest (distance, id) pairs of
+    their union -- the host tree merge of per-shard lists the reference does
+    (AnnIndexTreeMerge, ann/server/indexfile.c:3235-3258), written in numpy
+    as the checker, independent of the device merge."""
+    nq = len(lists[0][2])
+    out = []
+    for q in range(nq):
+        entries = []
+        for d, i, c in lists:
+            n = int(c[q])
+            entries.extend(zip(np.asarray(d)[q, :n].tolist(), np.asarray(i)[q, :n].tolist()))
+        entries.sort()
+        out.append(entries[:k])
+    return out
+
+
+def check_global(result, lists, nq, k):
+    """Rank 0: the merged device answer (dist, id, count) equals, bit for
+    bit, the merge of every rank's oracle list."""
+    want = merge_reference_lists(lists, k)
+    d = np.asarray(result[0][:nq].cpu())
+    i = np.asarray(result[1][:nq].cpu())
+    c = np.asarray(result[2][:nq].cpu())
+    for q in range(nq):
+        n = int(c[q])
+        if n != len(want[q]) or list(zip(d[q, :n].tolist(), i[q, :n].tolist())) != want[q]:
+            return False
+    return True
+
+
+def gather_objects(obj, world):
+    """Every rank's `obj` on every rank (a collective all ranks enter)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def verify(w, result, nq, world, rank, k):
+    """The multi-rank correctness check: each rank answers the checked
+    queries with the CPU oracle over the rows it holds (or rescores the
+    returned rows and a sample, for shards too large for the oracle); rank 0
+    checks the merged device answer against all of them. None on the other
+    ranks."""
+    if hasattr(w, 'local_oracle'):
+        lists = gather_objects(w.local_oracle(nq), world)
+        return check_global(result, lists, nq, k) if rank == 0 else None
+    parts = gather_objects(w.local_rescore(result, nq), world)
+    return check_rescored(result, [p for p in parts], nq) if rank == 0 else None
 
 
 # ---------------------------------------------------------------- our arm
@@ -895,39 +983,38 @@ def main():
                 traffic = float(line.split(':', 1)[1]) * (w.pass_rows if args.config == 4 else nrows_local)
     stage_names = ['prep', 'sample_scan', 'bound', 'filter_scan', 'tighten', 'finalize', 'bitmap', 'merge', 'gather',
                    'probe']
+    stages = {n: round(stage_ms[j] / args.steps, 4) for j, n in enumerate(stage_names) if stage_calls[j]}
+    # The tensor denominator: the measured burst cuBLAS figure for a timed
+    # region shorter than a second (clocks stay at their maximum), the
+    # sustained one (under the power cap) for a longer region.
+    region_s = ms / 1e3
+    burst = region_s < 1.0
+    tf_peak = tf_burst if burst else tf_sust
+    tf_src = '%s bf16_tflops%s (timed region %.2f s)' % (kind, '' if burst else '_sustained', region_s)
     common = {'kernel': '%s (%d launches a step)' % (w.kernel, round(stage_calls[3] / args.steps)),
-              'pass_ms': pass_ms, 'flops_per_pass': flops, 'algorithmic_bytes_per_pass': bytes_alg,
-              'stage_ms_per_step': {n: stage_ms[j] / args.steps for j, n in enumerate(stage_names)}}
+              'pass_ms': round(pass_ms, 4), 'flops_per_pass': flops, 'algorithmic_bytes_per_pass': bytes_alg}
     if w.bound == 'tensor' and w.ops == 'int8':
-        # dense int8 runs at twice the bf16 rate on B200: the measured
-        # sustained bf16 figure doubled is the denominator
-        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': 2 * tf_sust, 'unit': 'TOP/s (int8)',
-                    'frac': achieved_tf / (2 * tf_sust), 'traffic': traffic,
-                    'peak_source': kind + ' bf16_tflops_sustained x 2 (int8 dense rate)',
-                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
-    elif w.bound == 'fp32':
-        # FP32 rows are scored on CUDA cores; no measured FP32 figure exists,
-        # so the denominator is the nominal FMA rate at the maximum SM clock
-        mhz = (clock_info or {}).get('sm_max_mhz') or 1965.0
-        fp32 = torch.cuda.get_device_properties(dev).multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
-        roofline = {'bound': 'fp32', 'achieved': achieved_tf, 'peak': fp32, 'unit': 'TFLOP/s',
-                    'frac': achieved_tf / fp32, 'traffic': traffic,
-                    'peak_source': 'nominal FP32 FMA rate (SMs x 128 lanes x 2 x max SM clock)',
-                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
+        # dense int8 runs at twice the bf16 rate on B200: the measured bf16
+        # figure doubled is the denominator
+        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': 2 * tf_peak, 'unit': 'TOP/s (int8)',
+                    'frac': achieved_tf / (2 * tf_peak), 'traffic': traffic,
+                    'peak_source': tf_src + ' x 2 (int8 dense rate)',
+                    'frac_of_sustained': achieved_tf / (2 * tf_sust), 'hbm_frac': hbm_gbs / hbm, **common}
     elif w.bound == 'tensor':
-        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_sust, 'unit': 'TFLOP/s',
-                    'frac': achieved_tf / tf_sust, 'traffic': traffic,
-                    'peak_source': kind + ' bf16_tflops_sustained',
-                    'hbm_achieved_gbs': hbm_gbs, 'hbm_peak_gbs': hbm, 'hbm_frac': hbm_gbs / hbm, **common}
+        roofline = {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tf_peak, 'unit': 'TFLOP/s',
+                    'frac': achieved_tf / tf_peak, 'traffic': traffic, 'peak_source': tf_src,
+                    'frac_of_sustained': achieved_tf / tf_sust, 'hbm_frac': hbm_gbs / hbm, **common}
         if args.config == 1:   # achieved counts the algorithmic FLOPs; the split runs three MMAs for each
             roofline['mma_flops_per_algorithmic_flop'] = 3
+        if w.ops == 'e4m3':    # FP8 operands: the dense FP8 rate is twice bf16's
+            roofline['frac_of_fp8_dense'] = achieved_tf / (2 * tf_peak)
     else:
         roofline = {'bound': 'hbm', 'achieved': hbm_gbs, 'peak': hbm, 'unit': 'GB/s', 'frac': hbm_gbs / hbm,
                     'traffic': traffic, 'peak_source': kind + ' hbm_gbs', 'achieved_tflops': achieved_tf,
                     **common}
 
     # ---- correctness spot check against the CPU oracle
-    verified = w.verify(result, args.verify) if args.verify > 0 else None
+    verified = verify(w, result, args.verify, world, rank, args.k) if args.verify > 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -950,11 +1037,14 @@ def main():
         cfg['parallelism'] = ('%s x%d, NCCL all-gather of top-k + device merge' % (
             'row-sharded (IVF lists cut at rank boundaries)' if args.config == 4 else 'row-sharded', world)
             if world > 1 else 'single GPU')
+        # the per-step stage times and the check close the line, so that a
+        # reader keeping only its end still has them
         line = {'metric': METRIC, 'value': value, 'unit': 'queries/s', 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True,
                 'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg,
                 'e2e': e2e, 'gpu_launches': int(launches), 'roofline': roofline, 'cpu_baseline': cpu,
-                'clocks': clock_info, 'verified_vs_oracle': verified}
+                'clocks': clock_info, 'verified_vs_oracle': verified, 'timed_steps': args.steps,
+                'stage_ms_per_step': stages}
         print(json.dumps(line), flush=True)
     w.shard.close()
     if world > 1:

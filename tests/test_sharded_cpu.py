@@ -161,3 +161,63 @@ def test_shard_bounds_word_aligned():
             b = sharded.shard_bounds(rows, world)
             assert b[0] == 0 and b[-1] == rows and all(x % 32 == 0 for x in b[:-1])
             assert all(b0 <= b1 for b0, b1 in zip(b, b[1:]))
+
+
+def check_worker(rank, world, port, out):
+    # bench.py's multi-rank check: each rank answers with the oracle over its
+    # own rows; rank 0 holds every rank's list and judges merged answers
+    import bench
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    torch.distributed.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        x = synth.mixture(ROWS, DIMS, 10, seed=37)
+        q = synth.mixture_queries(NQ, DIMS, 10, seed=37)
+        b = sharded.shard_bounds(ROWS, world)
+        lo, hi = b[rank], b[rank + 1]
+        d, i, c, _ = oracle.search(oracle.F32, DIMS, x[lo:hi], q, K, 0, threads=1)
+        lists = bench.gather_objects((d, np.where(i >= 0, i + lo, -1), c), world)
+        if rank == 0:
+            out['lists'] = lists
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_multi_rank_check_catches_bad_merges():
+    import bench
+    world = 2
+    ctx = mp.get_context('spawn')
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    mp.start_processes(check_worker, args=(world, free_port(), out), nprocs=world, join=True, start_method='spawn')
+    lists = out['lists']
+    gd = np.stack([l[0] for l in lists])
+    gi = np.stack([l[1] for l in lists])
+    gc = np.stack([l[2].astype(np.int32) for l in lists])
+    good = merge_host(gd, gi, gc, K)
+    assert bench.check_global(good, lists, NQ, K)
+    # and it is the whole corpus's answer
+    x = synth.mixture(ROWS, DIMS, 10, seed=37)
+    q = synth.mixture_queries(NQ, DIMS, 10, seed=37)
+    od, oi, oc, _ = oracle.search(oracle.F32, DIMS, x, q, K, 0)
+    assert np.array_equal(good[1].numpy(), oi) and np.array_equal(good[0].numpy(), od)
+    # a merge that dropped rank 1's list
+    dropped = merge_host(gd[:1], gi[:1], gc[:1], K)
+    assert not bench.check_global(dropped, lists, NQ, K)
+    # a merge that swapped two neighbours of one query's list
+    d, i, c = (t.clone() for t in good)
+    d[2, [3, 4]] = d[2, [4, 3]]
+    i[2, [3, 4]] = i[2, [4, 3]]
+    assert not bench.check_global((d, i, c), lists, NQ, K)
+    # a merge that concatenated the ranks' lists without ordering them
+    cat_d = np.concatenate([gd[1], gd[0]], axis=1)[:, :K]
+    cat_i = np.concatenate([gi[1], gi[0]], axis=1)[:, :K]
+    bad = (torch.from_numpy(cat_d), torch.from_numpy(cat_i), torch.full((NQ,), K, dtype=torch.int32))
+    assert not bench.check_global(bad, lists, NQ, K)
+    # the rank-0 rescoring check rejects a returned row whose distance is off
+    part = [{'returned': {int(good[1][0, j]): float(good[0][0, j]) for j in range(K)},
+             'sample': [(float(gd[1][0, j]), int(gi[1][0, j])) for j in range(K)]}]
+    one = tuple(t[:1] for t in good)
+    assert bench.check_rescored(one, [part], 1)
+    off = tuple(t.clone() for t in one)
+    off[0][0, 5] = np.nextafter(float(off[0][0, 5]), np.inf)
+    assert not bench.check_rescored(off, [part], 1)
