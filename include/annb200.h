@@ -289,8 +289,11 @@ int			AnnB200IndexSearch(AnnB200Index *index, const float *queries, uint32_t nq,
  * (distance, ordinal). Like the reference's, the answer is the exact one
  * whenever the true k nearest are among each shard's candidates.
  * The FP32 rows' pages are registered for the device to read the
- * candidates' rows in place (ANN_B200_QUANT_MAPPED=0 turns this off); where
- * registration fails, the rows are copied through pinned staging.
+ * candidates' rows in place (ANN_B200_QUANT_MAPPED=0 turns this off) when
+ * they take at most ANN_B200_QUANT_MAP_MAX_MB megabytes (default: a quarter
+ * of physical memory, since registered pages stay locked for the index's
+ * life); above that, or where registration fails, the candidates' rows are
+ * copied through pinned staging.
  */
 int			AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype,
 									const void *codes, const void *block_scales,

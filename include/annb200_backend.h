@@ -9,9 +9,10 @@
  * backend.h is included first (it defines ANN_BACKEND_H), its definitions
  * are used instead and only the constructor below is added.
  *
- * Integration: declare AnnB200Backend() in backend.h
- * beside AnnCpuBackend(), add "--backend b200" to worker.c's selection
- * (ann/server/worker.c:267-279) and link -lannb200.
+ * Integration: declare AnnB200Backend() (or AnnB200WorkerBackend(), which
+ * also serves loaded indexes) in backend.h beside AnnCpuBackend(), add
+ * "--backend b200" to worker.c's selection (ann/server/worker.c:267-279) and
+ * link -lannb200.
  */
 #ifndef ANNB200_BACKEND_H
 #define ANNB200_BACKEND_H
@@ -152,8 +153,10 @@ extern "C"
 /*
  * The B200 backend: "b200", metrics L2/IP/cosine (mask 7), exact. Gathered
  * jobs and in-memory index searches run on the calling thread's CUDA device
- * through AnnB200Search; loaded indexes are not served yet (load_index and
- * search_index are NULL, which the worker answers as unsupported).
+ * through AnnB200Search. Loaded on-disk indexes live in the worker's own
+ * registry, so this vtable leaves load_index and search_index NULL;
+ * AnnB200WorkerBackend(), compiled inside the worker's build
+ * (pgvector_b200/csrc/worker_index.c), is this vtable with them filled.
  */
 const AnnBackend *AnnB200Backend(void);
 

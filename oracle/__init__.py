@@ -32,7 +32,10 @@ u32, u64, i32, i64, f64 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32, ctyp
 
 def build(reference=None):
     """make -C oracle (and the reference library when its sources exist)."""
-    ref = reference or os.environ.get('ANN_REFERENCE', '/root/reference')
+    # the reference tree: ANN_REFERENCE, else a `reference` directory beside
+    # this repository
+    ref = reference or os.environ.get('ANN_REFERENCE') or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                       'reference')
     subprocess.run(['make', '-s', '-C', HERE, 'all'], check=True)
     if os.path.isdir(os.path.join(ref, 'ann', 'server')):
         subprocess.run(['make', '-s', '-C', HERE, 'ref', 'REF=' + ref], check=True)

@@ -5,9 +5,10 @@
  * 114-151): gathered jobs (ops 7/10; the cpu backend's SearchGathered,
  * ann/server/cpu.c:218-283) and in-memory index build/search/destroy (ops
  * 0-6; cpu.c:10-154) run on a CUDA device through AnnB200Search, which
- * returns the CPU worker's exact results. Loaded on-disk indexes are not
- * served by this backend yet (load_index / search_index are NULL, which the
- * worker answers as unsupported, ann/server/server.c:1952,3795).
+ * returns the CPU worker's exact results. Loaded on-disk indexes live in the
+ * worker's own registry, so their load_index / search_index are filled by
+ * AnnB200WorkerBackend() (worker_index.c, compiled inside the worker's
+ * build); this vtable leaves them NULL.
  *
  * Threading: the worker calls search_gathered from many lane threads at once
  * (ann/server/server.c:1541). Each thread keeps its own device context (a
@@ -420,8 +421,12 @@ AnnB200IndexDestroy(AnnB200Index *ix)
 		AnnB200ShardDestroy(ix->shards[s]);
 	if (ix->registered)
 	{
+		int			prev = 0;
+
+		cudaGetDevice(&prev);
 		cudaSetDevice(ix->device);
 		cudaHostUnregister(ix->registered);
+		cudaSetDevice(prev);
 	}
 	free(ix->shards);
 	free(ix->bounds);
@@ -429,10 +434,32 @@ AnnB200IndexDestroy(AnnB200Index *ix)
 }
 
 /*
+ * The most bytes of FP32 rows MapRows registers: ANN_B200_QUANT_MAP_MAX_MB,
+ * else a quarter of the machine's physical memory. Registering pins the
+ * pages for the index's whole life, so an index whose rows are larger (a
+ * mapped vectors.f32 of hundreds of GB) keeps the copy path instead of
+ * reading in and locking that much of the page cache.
+ */
+static uint64_t
+MapCapBytes(void)
+{
+	long		mb = EnvLong("ANN_B200_QUANT_MAP_MAX_MB", -1);
+	long		pages = sysconf(_SC_PHYS_PAGES);
+	long		page = sysconf(_SC_PAGESIZE);
+
+	if (mb >= 0)
+		return (uint64_t) mb << 20;
+	if (pages <= 0 || page <= 0)
+		return 0;
+	return (uint64_t) pages * (uint64_t) page / 4;
+}
+
+/*
  * Register the pages of a quantized index's FP32 rows for the device to read
  * them in place (read-only where the driver supports it, as a read-only file
- * mapping needs). Where that fails the rows are copied through pinned
- * staging instead; nothing else changes.
+ * mapping needs), when they are within MapCapBytes(). Where they are larger
+ * or registration fails the rows are copied through pinned staging instead;
+ * nothing else changes.
  */
 static void
 MapRows(AnnB200Index *ix)
@@ -444,7 +471,16 @@ MapRows(AnnB200Index *ix)
 	size_t		len = (size_t) ((end - base + (uintptr_t) page - 1) & ~((uintptr_t) page - 1));
 	unsigned	flags = cudaHostRegisterMapped | cudaHostRegisterPortable;
 	void	   *dev = NULL;
+	int			debug = EnvLong("ANN_B200_DEBUG", 0) > 0;
+	uint64_t	cap = MapCapBytes();
 
+	if ((uint64_t) len > cap)
+	{
+		if (debug)
+			fprintf(stderr, "annb200 quantized index: FP32 rows copied through pinned staging "
+					"(%zu bytes, above the %llu-byte registration cap)\n", len, (unsigned long long) cap);
+		return;
+	}
 	if (cudaSetDevice(ix->device) != cudaSuccess)
 		return;
 	if (cudaHostRegister((void *) base, len, flags | cudaHostRegisterReadOnly) != cudaSuccess)
@@ -453,6 +489,9 @@ MapRows(AnnB200Index *ix)
 		if (cudaHostRegister((void *) base, len, flags) != cudaSuccess)
 		{
 			(void) cudaGetLastError();
+			if (debug)
+				fprintf(stderr, "annb200 quantized index: FP32 rows copied through pinned staging "
+						"(registration failed)\n");
 			return;
 		}
 	}
@@ -460,11 +499,14 @@ MapRows(AnnB200Index *ix)
 	{
 		(void) cudaGetLastError();
 		cudaHostUnregister((void *) base);
+		if (debug)
+			fprintf(stderr, "annb200 quantized index: FP32 rows copied through pinned staging "
+					"(no device address)\n");
 		return;
 	}
 	ix->registered = (void *) base;
 	ix->mapped = (const float *) ((const char *) dev + (start - base));
-	if (EnvLong("ANN_B200_DEBUG", 0) > 0)
+	if (debug)
 		fprintf(stderr, "annb200 quantized index: FP32 rows read in place (%zu bytes registered)\n", len);
 }
 

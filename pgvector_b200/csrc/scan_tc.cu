@@ -34,11 +34,15 @@
 //              the staging path. Two accumulators (2 x 256 columns) let the
 //              epilogue of tile t overlap the MMAs of tile t+1.
 //
-// Every wait is bounded (4 s of %globaltimer); a wait that runs out sets
-// FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are drained and
-// tensor memory is freed before the kernel returns.
+// Every wait is bounded (4 s of %globaltimer; the pipeline waits of the flat
+// scan by ANN_B200_PIPELINE_WAIT_NS when a test sets it); a wait that runs
+// out sets FLAG_TIMEOUT, all roles leave their loops, in-flight MMAs are
+// drained, bulk copies still in flight are waited for and tensor memory is
+// freed before the kernel returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
+
+#include <cstdlib>
 
 #include "internal.cuh"
 
@@ -63,6 +67,7 @@ struct TcArgs {
   uint32_t bn;         // queries per tile, multiple of 32, <= 256
   uint32_t qtiles;
   uint64_t rtiles;
+  uint64_t wait_ns;    // limit of each pipeline wait (the drains keep kWaitNs)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -90,16 +95,17 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
-// Wait for the phase of `parity` to complete; false once the time limit
-// passes or another role has aborted.
-__device__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *flags) {
+// Wait for the phase of `parity` to complete; false once `limit_ns` passes
+// or another role has aborted.
+__device__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *flags,
+                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {
     for (int i = 0; i < 32; i++)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort = 1;
       atomicOr(flags, FLAG_TIMEOUT);
       return false;
@@ -571,7 +577,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         for (uint32_t kb = 0; kb < t.kblocks; kb++) {
           const uint32_t s = (uint32_t)(it % RING);
           const uint32_t ph = (uint32_t)((it / RING) & 1);
-          if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags)) {
+          if (!mbar_wait(ring_empty + s, ph ^ 1, abort, a.flags, t.wait_ns)) {
             ok = false;
             break;
           }
@@ -596,7 +602,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       bool ok = true;
       for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
         const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
-        if (!mbar_wait(tempty + ab, (use & 1) ^ 1, abort, a.flags)) break;
+        if (!mbar_wait(tempty + ab, (use & 1) ^ 1, abort, a.flags, t.wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * 256;
         for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
@@ -605,8 +611,8 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           // the B tile: same stage index, or its own ring (gathered kernel)
           const uint32_t s_b = GATHER ? (uint32_t)(it % BSTG) : s;
           const uint32_t ph_b = GATHER ? (uint32_t)((it / BSTG) & 1) : ph;
-          if (!mbar_wait(full + s, ph, abort, a.flags) ||
-              ((QUANT || GATHER) && !mbar_wait(bfull + s_b, ph_b, abort, a.flags))) {
+          if (!mbar_wait(full + s, ph, abort, a.flags, t.wait_ns) ||
+              ((QUANT || GATHER) && !mbar_wait(bfull + s_b, ph_b, abort, a.flags, t.wait_ns))) {
             ok = false;
             break;
           }
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
         const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
         const uint32_t r = (uint32_t)(it % RSTG1), rph = (uint32_t)((it / RSTG1) & 1);
-        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags, t.wait_ns);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -664,7 +670,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
                         bfull + s);
           bissued = it + 1;
         }
-        got = mbar_wait(rawfull + r, rph, abort, a.flags);
+        got = mbar_wait(rawfull + r, rph, abort, a.flags, t.wait_ns);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -716,7 +722,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       }
       for (uint32_t kb = 0; kb < t.kblocks; kb++, it++) {
         const uint32_t s = (uint32_t)(it % STG), ph = (uint32_t)((it / STG) & 1);
-        const bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags);
+        const bool got = mbar_wait(empty + s, ph ^ 1, abort, a.flags, t.wait_ns);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -742,7 +748,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       const uint64_t rt = tile / t.qtiles;
       const uint32_t qt = (uint32_t)(tile % t.qtiles);
       const uint32_t ab = (uint32_t)(tc & 1), use = (uint32_t)(tc >> 1);
-      bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags);
+      bool got = mbar_wait(tfull + ab, use & 1, abort, a.flags, t.wait_ns);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       epilogue_rows<Q>(a, tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16), rt * BM + quad * 32 + lane,
@@ -1369,6 +1375,19 @@ size_t tc_scan_smem_t(uint32_t nq) {
 // Largest query count one tensor-scan launch takes (thresholds in shared memory).
 uint32_t tc_scan_max_queries() { return 4096; }
 
+// The limit of each pipeline wait in the flat tensor scan: 4 s, or, for
+// tests of the time-out path, ANN_B200_PIPELINE_WAIT_NS (read at every
+// launch). A wait that runs out sets FLAG_TIMEOUT and the search fails with
+// ANN_BACKEND_ERROR; the drains that follow keep their 4 s.
+uint64_t pipeline_wait_ns() {
+  const char *v = getenv("ANN_B200_PIPELINE_WAIT_NS");
+  if (v && *v) {
+    const unsigned long long n = strtoull(v, nullptr, 10);
+    if (n > 0) return n;
+  }
+  return kWaitNs;
+}
+
 template <int Q>
 cudaError_t launch_tc_t(const CUtensorMap &rows_map, const CUtensorMap &query_map, const CUtensorMap &query_lo_map,
                         const TcArgs &t, int sms,
@@ -1431,6 +1450,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   t.bn = bn;
   t.qtiles = (a.nq + bn - 1) / bn;
   t.rtiles = (a.count + BM - 1) / BM;
+  t.wait_ns = pipeline_wait_ns();
   if (a.count == 0 || a.nq == 0) return cudaSuccess;
   switch (a.s.dtype) {
     case DT_F16:

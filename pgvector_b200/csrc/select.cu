@@ -1159,16 +1159,18 @@ __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nb
 
 // The same re-score with each candidate's row fetched by ordinal from a row
 // array the device reads directly (device memory, or host memory mapped for
-// the device): one warp a candidate, its row staged through shared memory in
-// 128-byte reads, the sum formed by lane 0 in dimension order.
-constexpr int RG_WARPS = 8, RG_CHUNK = 512;
+// the device): one warp a candidate, its row read in coalesced 128-byte
+// pieces; every lane forms its dimensions' FP64 squared differences into
+// shared memory, and lane 0 adds them in dimension order (the reference's
+// order, so the sum is bit-identical).
+constexpr int RG_WARPS = 8, RG_CHUNK = 256;
 
 __global__ void __launch_bounds__(RG_WARPS * 32) rescore_gather(const float *__restrict__ queries, uint32_t nq,
                                                                 uint32_t dims, const float *__restrict__ rows,
                                                                 const uint64_t *__restrict__ ords, uint32_t stride,
                                                                 const uint32_t *__restrict__ counts,
                                                                 float *__restrict__ out) {
-  __shared__ float buf[RG_WARPS][RG_CHUNK];
+  __shared__ double buf[RG_WARPS][RG_CHUNK];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t w = (uint64_t)blockIdx.x * RG_WARPS + warp;
   if (w >= (uint64_t)nq * stride) return;                  // whole warps leave together
@@ -1186,13 +1188,16 @@ __global__ void __launch_bounds__(RG_WARPS * 32) rescore_gather(const float *__r
       r[t] = i < n ? x[d0 + i] : 0.0f;
     }
 #pragma unroll
-    for (int t = 0; t < RG_CHUNK / 32; t++) buf[warp][lane + 32 * t] = r[t];
+    for (int t = 0; t < RG_CHUNK / 32; t++) {
+      const uint32_t i = lane + 32u * t;
+      if (i < n) {
+        const double delta = __dsub_rn((double)r[t], (double)__ldg(v + d0 + i));
+        buf[warp][i] = __dmul_rn(delta, delta);
+      }
+    }
     __syncwarp();
     if (lane == 0)
-      for (uint32_t t = 0; t < n; t++) {
-        const double delta = __dsub_rn((double)buf[warp][t], (double)__ldg(v + d0 + t));
-        sum = __dadd_rn(sum, __dmul_rn(delta, delta));
-      }
+      for (uint32_t t = 0; t < n; t++) sum = __dadd_rn(sum, buf[warp][t]);
     __syncwarp();
   }
   if (lane == 0) out[w] = __double2float_rn(__dsqrt_rn(sum));

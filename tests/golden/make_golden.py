@@ -51,7 +51,10 @@ def quant_inputs():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default=os.environ.get('ANN_REFERENCE', '/root/reference'))
+    beside = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))),
+                          'reference')
+    ap.add_argument('--reference', default=os.environ.get('ANN_REFERENCE') or beside,
+                    help='the reference tree (default: $ANN_REFERENCE, else `reference` beside this repository)')
     args = ap.parse_args()
     import oracle
     oracle.build(args.reference)

@@ -393,3 +393,53 @@ def test_quantized_index_rows_in_place_or_copied(cuda, monkeypatch, capfd, mappe
                 assert dist[i, :cnt[i]].view(np.uint32).tolist() == [w.view(np.uint32).item() for _, w in want[i]]
     finally:
         lib.AnnB200IndexDestroy(ix)
+
+
+def test_quantized_index_registration_cap_and_release(cuda, monkeypatch, capfd):
+    # the registration cap sends a large row array to the copy path; two
+    # indexes over one array: the second cannot register the pages again,
+    # copies instead and answers the same; once both are destroyed the pages
+    # register again (the first index released them)
+    import pgvector_b200 as pb
+    lib = pb.load()
+    n, d = 12000, 96
+    x = synth.mixture(n, d, 30, seed=71)
+    q = synth.mixture_queries(24, d, 30, seed=72)
+    codes, rs = oracle.quantize_fp8(x)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    monkeypatch.setenv('ANN_B200_DEBUG', '1')
+
+    def create():
+        ix = ctypes.c_void_p()
+        assert lib.AnnB200IndexCreateQuant(0, d, n, pb.E4M3, P(codes), None, P(rs), P(x), 0, None, 32, 100,
+                                           ctypes.byref(ix)) == 0
+        return ix, capfd.readouterr().err
+
+    def answer(ix):
+        dist = np.zeros((24, 10), np.float32)
+        ords = np.zeros((24, 10), np.uint64)
+        cnt = np.zeros(24, np.uint32)
+        assert lib.AnnB200IndexSearch(ix, P(q), 24, None, 0, 10, P(dist), P(ords), P(cnt)) == 0
+        return dist.view(np.uint32).tolist(), ords.tolist(), cnt.tolist()
+
+    monkeypatch.setenv('ANN_B200_QUANT_MAP_MAX_MB', '1')          # the rows take 4.6 MB
+    capped, err = create()
+    assert 'registration cap' in err and 'read in place' not in err
+    monkeypatch.delenv('ANN_B200_QUANT_MAP_MAX_MB')
+    first, err1 = create()
+    second, err2 = create()
+    try:
+        assert 'read in place' in err1
+        assert 'registration failed' in err2 and 'read in place' not in err2
+        a, b, c = answer(first), answer(second), answer(capped)
+        assert a == b == c
+        want = oracle.quant_index_search(oracle.E4M3, x, codes, q, 10, [0, n], row_scales=rs, quant_slack=32,
+                                         slack_ratio=100, threads=8)
+        assert a[1] == [[o for o, _ in w] + [0] * (10 - len(w)) for w in want]
+    finally:
+        lib.AnnB200IndexDestroy(first)
+        lib.AnnB200IndexDestroy(second)
+        lib.AnnB200IndexDestroy(capped)
+    third, err3 = create()
+    lib.AnnB200IndexDestroy(third)
+    assert 'read in place' in err3

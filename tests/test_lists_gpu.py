@@ -50,13 +50,17 @@ def gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, r
 
 
 def assert_lists_same(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids=None,
-                      force_simt=False):
-    od, oi, oc = oracle.search_lists(dtype, dims, codes, q, offsets, probes, k, metric, row_ids=row_ids,
+                      force_simt=False, check=None):
+    """The device answers the whole batch; the oracle answers the queries
+    `check` selects (all by default) and those must be equal."""
+    sel = np.arange(q.shape[0]) if check is None else np.asarray(check)
+    od, oi, oc = oracle.search_lists(dtype, dims, codes, q[sel], offsets, probes[sel], k, metric, row_ids=row_ids,
                                      block_scales=bs, row_scales=rs)
     gd, gi, gc = gpu_lists(cuda, dtype, dims, codes, bs, rs, q, offsets, probes, k, metric, row_ids,
                            force_simt=force_simt)
+    gd, gi, gc = gd[sel], gi[sel], gc[sel]
     assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
-    for j in range(q.shape[0]):
+    for j in range(len(sel)):
         c = int(oc[j])
         assert np.array_equal(gi[j, :c], oi[j, :c]), (j, gi[j, :c][:10], oi[j, :c][:10])
         assert np.array_equal(gd[j, :c], od[j, :c]), (j, gd[j, :c][:10], od[j, :c][:10])
@@ -90,6 +94,20 @@ def test_config4_shape_nvfp4_l2(cuda, simt):
     codes, bs, rs = oracle.quantize_nvfp4(x)
     assert_lists_same(cuda, oracle.NVFP4, 768, codes, bs, rs, q.astype(np.float32), offsets, probes, 100, 0,
                       row_ids, force_simt=simt)
+
+
+def test_config4_batch_4096_nvfp4_l2(cuda):
+    # config 4 at its batch, nprobe and k: NVFP4 d=768, 4,096 queries (64-query
+    # groups of the tensor list scan, many groups a list), Zipf(1.1) list
+    # sizes, nprobe 64, k 100; queries near uniformly chosen centres; the
+    # oracle checks every 8th query
+    x, offsets, cent, row_ids = synth.ivf_corpus(80000, 768, 512, seed=401)
+    rng = np.random.default_rng(402)
+    q = cent[rng.integers(0, 512, 4096)] + 0.1 * rng.standard_normal((4096, 768)).astype(np.float32)
+    probes = synth.ivf_probes(q, cent, 64)
+    codes, bs, rs = oracle.quantize_nvfp4(x)
+    assert_lists_same(cuda, oracle.NVFP4, 768, codes, bs, rs, q.astype(np.float32), offsets, probes, 100, 0,
+                      row_ids, check=np.arange(1, 4096, 8))
 
 
 @pytest.mark.parametrize('dtype', [0, 1])

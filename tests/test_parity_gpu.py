@@ -35,15 +35,19 @@ def gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, 
 
 
 def assert_same(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, rs=None, window=False,
-                force_simt=False):
+                force_simt=False, check=None):
+    """The device answers the whole batch; the oracle answers the queries
+    `check` selects (all of them by default) and those must be equal."""
     n = codes.shape[0] if ids is None else len(ids)
     cap = max(n, 1) if window else max(k, 1)
-    od, oi, oc, os_ = oracle.search(dtype, dims, codes, queries, k, metric, ids=ids, block_scales=bs,
+    sel = np.arange(queries.shape[0]) if check is None else np.asarray(check)
+    od, oi, oc, os_ = oracle.search(dtype, dims, codes, queries[sel], k, metric, ids=ids, block_scales=bs,
                                     row_scales=rs, window=window, cap=cap)
     assert (os_ == 0).all()
     gd, gi, gc = gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids, bs, rs, window, force_simt, cap)
+    gd, gi, gc = gd[sel], gi[sel], gc[sel]
     assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
-    for q in range(queries.shape[0]):
+    for q in range(len(sel)):
         c = int(oc[q])
         assert np.array_equal(gi[q, :c], oi[q, :c]), (q, gi[q, :c][:10], oi[q, :c][:10])
         assert np.array_equal(gd[q, :c], od[q, :c]), (q, gd[q, :c][:10], od[q, :c][:10])
@@ -392,3 +396,30 @@ def test_typed_gathered_jobs_odd_shapes(cuda):
         assert status == 0 and (os_ == 0).all()
         for qi in range(qs.shape[0]):
             assert res[qi] == [(int(oi[qi, r]), float(od[qi, r])) for r in range(oc[qi])], (dt, dims, qi)
+
+
+# ---------------------------------------------------------------- the benchmark configurations' batch and k
+
+def test_config3_batch_e4m3_ip_k500(cuda):
+    # config 3 at its batch and k on fewer rows: FP8-E4M3 rows with row
+    # scales, inner product, d=1024, 1,024 queries, k=500, whole shard and a
+    # 90% row list (both past the 32,768 rows below which no sample is taken)
+    # rows from a 64-centre mixture; the device answers all 1,024 queries
+    # (four 256-query tiles), the oracle checks every 8th (32 in each tile)
+    x = synth.mixture(40000, 1024, 64, seed=301)
+    q = synth.mixture_queries(1024, 1024, 64, seed=302)
+    codes, rs = oracle.quantize_fp8(x)
+    assert_same(cuda, oracle.E4M3, 1024, codes, q, 500, 1, rs=rs, check=np.arange(3, 1024, 8))
+    _, ids = synth.bitmap(40000, 0.9, seed=303)
+    assert_same(cuda, oracle.E4M3, 1024, codes, q, 500, 1, ids=ids, rs=rs, check=np.arange(5, 1024, 8))
+
+
+def test_config5_batch_hamming_1024_queries(cuda):
+    # config 5 at its batch and k: 1,024-bit rows XOR-perturbed (5%) from
+    # prototypes, 1,024 queries (four query tiles), k=100; integer distances
+    # with many ties, ordered by row id
+    rows, proto = synth.bit_rows(120000, 1024, 512, flip=0.05, seed=501)
+    rng = np.random.default_rng(502)
+    qs = proto[rng.integers(0, 512, 1024)] ^ np.packbits(rng.random((1024, 1024)) < 0.05, axis=1,
+                                                         bitorder='little')
+    assert_same(cuda, oracle.BIT, 1024, rows, qs, 100, 3)
