@@ -113,65 +113,107 @@ def peaks():
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+    """SM clock and throttle reasons sampled every 10 ms during a region,
+    read through NVML in a thread of this process (nvidia-smi's -lms loop
+    where NVML's Python binding is missing). Reading only: no setting of the
+    GPU is touched."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+    NAMES = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
 
     def __init__(self, gpu):
         self.gpu = gpu
         self.proc = None
+        self.nvml = None
+        self.samples = []         # (sm MHz, max MHz, set of reasons)
         self.lines = []
         self.skip = 0
+        self.running = False
 
     def start(self, wait_s=10.0):
         """Start sampling and wait (up to wait_s) for the first reading, so
-        that nvidia-smi's own start-up stays outside any timed region."""
+        that the sampler's own start-up stays outside any timed region; that
+        first reading is not counted."""
         try:
-            self.proc = subprocess.Popen(['nvidia-smi', '--query-gpu=' + self.FIELDS, '--format=csv,noheader,nounits',
-                                          '-i', str(self.gpu), '-lms', '100'], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = None
+            try:      # the CUDA device's own NVML handle, by PCI address (indices may differ)
+                import torch
+                pr = torch.cuda.get_device_properties(self.gpu)
+                bus = '%08x:%02x:%02x.0' % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                pass
+            if self.handle is None:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
+            self.running = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
         except Exception:
-            self.proc = None
-            return
+            self.nvml = None
+            try:
+                self.proc = subprocess.Popen(['nvidia-smi', '--query-gpu=' + self.FIELDS,
+                                              '--format=csv,noheader,nounits', '-i', str(self.gpu), '-lms', '20'],
+                                             stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.thread = threading.Thread(target=self._read, daemon=True)
+                self.thread.start()
+            except Exception:
+                self.proc = None
+                return
         t0 = time.perf_counter()
-        while not self.lines and time.perf_counter() - t0 < wait_s and self.proc.poll() is None:
-            time.sleep(0.02)
-        self.skip = len(self.lines)      # readings before the measured region starts
+        while not (self.samples or self.lines) and time.perf_counter() - t0 < wait_s:
+            time.sleep(0.005)
+        self.skip = max(len(self.samples), len(self.lines))
+
+    def _poll(self):
+        n = self.nvml
+        while self.running:
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                mx = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((float(sm), float(mx), {nm for nm, b in zip(self.NAMES, self.bits) if r & b}))
+            except Exception:
+                pass
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self):
-        if not self.proc:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(5)
-        except Exception:
-            self.proc.kill()
-        self.thread.join(2)
-        sm, mx, reasons = [], None, set()
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for line in self.lines[self.skip:]:
-            parts = [p.strip() for p in line.split(',')]
+            parts = [p.strip() for p in line.strip().split(',')]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                self.samples.append((float(parts[1]), float(parts[2]),
+                                     {nm for nm, v in zip(self.NAMES, parts[5:9]) if v.lower().startswith('active')}))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith('active'):
-                    reasons.add(name)
-        if not sm:
+
+    def stop(self):
+        if self.nvml is not None:
+            self.running = False
+            self.thread.join(2)
+        elif self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(2)
+        else:
             return None
-        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
-                'samples': len(sm)}
+        got = self.samples[self.skip:]
+        if not got:
+            return None
+        reasons = set()
+        for _, _, r in got:
+            reasons |= r
+        return {'sm_mhz': statistics.median(x[0] for x in got), 'sm_max_mhz': got[-1][1],
+                'reasons': sorted(reasons), 'samples': len(got), 'window': 'warm-up and timed region, 10 ms apart'}
 
 
 # ---------------------------------------------------------------- CPU baseline (reference worker code)
@@ -393,7 +435,7 @@ def build_config1(args, rank, world, dev):
 
     def step(q):
         flush.fill_(1)
-        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.L2, None)
+        d, i, c = w.shard.search_sharded(w.comm, q, args.k, pb.L2)
         return d, i, c, hi - lo
     w.step = step
 
@@ -437,7 +479,7 @@ def build_config2(args, rank, world, dev):
 
     def step(q, words_):
         rows = pb.bitmap_rows(words_, nbits)
-        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.COSINE, rows)
+        d, i, c = w.shard.search_sharded(w.comm, q, args.k, pb.COSINE, rows=rows)
         return d, i, c, rows.numel()
     w.step = step
 
@@ -486,7 +528,7 @@ def build_config3(args, rank, world, dev):
     w.profile = 'tc_scan_e4m3_config3.md'
 
     def step(q):
-        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.IP, None)
+        d, i, c = w.shard.search_sharded(w.comm, q, args.k, pb.IP)
         return d, i, c, hi - lo
     w.step = step
 
@@ -570,10 +612,7 @@ def build_config4(args, rank, world, dev):
     w.pass_flops = 2.0 * pairs * args.dims
 
     def step(q):
-        d, i, c = w.shard.search_lists(q, args.k, pb.L2, loc_off, rank_probes(q))
-        if world > 1:
-            gd, gi, gc = sharded.gather_lists(d, i, c)
-            return pb.merge_topk(gd, gi, gc, args.k) + (w.pass_rows,)
+        d, i, c = w.shard.search_lists_sharded(w.comm, q, args.k, pb.L2, loc_off, rank_probes(q))
         return d, i, c, w.pass_rows
     w.step = step
 
@@ -646,7 +685,7 @@ def build_config5(args, rank, world, dev):
     w.ops = 'int8'
 
     def step(q):
-        d, i, c = sharded.search_sharded(w.shard, q, args.k, pb.HAMMING, None)
+        d, i, c = w.shard.search_sharded(w.comm, q, args.k, pb.HAMMING)
         return d, i, c, hi - lo
     w.step = step
 
@@ -889,6 +928,10 @@ def main():
     lib = pb.load()
     w = {1: build_config1, 2: build_config2, 3: build_config3, 4: build_config4,
          5: build_config5}[args.config](args, rank, world, dev)
+    # N > 1: the library's own NCCL communicator carries the per-rank lists
+    # (AnnB200SearchSharded); torch.distributed only hands its id around
+    from pgvector_b200 import sharded
+    w.comm = sharded.comm_from_process_group(local) if world > 1 else None
     torch.cuda.synchronize()
 
     def barrier():
@@ -1047,6 +1090,8 @@ def main():
                 'stage_ms_per_step': stages}
         print(json.dumps(line), flush=True)
     w.shard.close()
+    if w.comm is not None:
+        w.comm.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -139,6 +139,61 @@ int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
 						  int32_t *status, void *stream);
 
 /*
+ * Row-sharded search across GPUs (one rank a GPU). The reference spreads a
+ * loaded index over the GPUs as row-range shards (placement
+ * ann/server/cuvs.c:2845-2862) and merges the per-shard top-k lists on the
+ * host (AnnIndexTreeMerge, ann/server/indexfile.c:3235-3258; MergeJob,
+ * ann/server/cuvs.c:3446-3455). Here the ranks exchange their lists with one
+ * NCCL all-gather and merge them on the device.
+ *
+ * Communicators: NCCL's C API, loaded at run time (libnccl.so.2; the copy
+ * the process already has, if any; ANN_B200_NCCL_LIBRARY names another).
+ * Several processes: one calls AnnB200CommId and hands the 128 bytes to the
+ * others, then each calls AnnB200CommCreate with its device and rank. One
+ * process over several devices (a worker with every GPU): AnnB200CommCreateAll
+ * fills comms[i] for devices[i]; each is then driven by its own thread.
+ * AnnB200CommDestroy releases one rank once every rank is done with the
+ * group; AnnB200CommAbort ends this rank's part at once (for a rank whose
+ * peers died or left: nothing of the group is waited for) and every later
+ * call on it fails. ANN_UNSUPPORTED without NCCL.
+ */
+#define ANNB200_COMM_ID_BYTES 128
+typedef struct AnnB200Comm AnnB200Comm;
+int			AnnB200CommId(void *id);
+int			AnnB200CommCreate(int device, int nranks, int rank, const void *id, AnnB200Comm **comm);
+int			AnnB200CommCreateAll(int ndev, const int *devices, AnnB200Comm **comms);
+void		AnnB200CommDestroy(AnnB200Comm *comm);
+void		AnnB200CommAbort(AnnB200Comm *comm);
+int			AnnB200CommRank(const AnnB200Comm *comm);
+int			AnnB200CommSize(const AnnB200Comm *comm);
+
+/*
+ * One rank of a row-sharded search: every rank of comm calls this at the same
+ * time with its own shard (its global ids first_id + row, disjoint from the
+ * other ranks'), its own candidate rows, and the same queries, nq, k, metric
+ * and flags. Arguments as AnnB200Search (strict top k only: ANNB200_WINDOW
+ * is unsupported); out_* receive, on every rank, the k best of all ranks'
+ * rows by (distance, id) -- the answer of one search over the union of the
+ * shards, bit for bit. comm NULL: AnnB200Search. nranks * k <= 4096, nq <=
+ * 32768.
+ *
+ * Each rank's search is enqueued on stream without a host round trip; one
+ * all-gather (per rank: a header with its status and flags, then its
+ * counts, distances and ids) and the device merge follow, then the one
+ * synchronisation. Every rank reads every rank's header, so all ranks
+ * succeed or fail together, and when a rank's candidate list overflowed
+ * they all search again synchronously and exchange once more; no rank
+ * leaves a collective the others enter. If the exchange does not finish
+ * within ANN_B200_COMM_TIMEOUT_MS (default 60,000: a peer that died or
+ * never called), the communicator is aborted and every later call on it
+ * fails with ANN_BACKEND_ERROR. Synchronous.
+ */
+int			AnnB200SearchSharded(AnnB200Shard *shard, AnnB200Comm *comm, const void *queries, uint32_t nq,
+								 const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric,
+								 uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+								 uint32_t *out_count, int32_t *status, void *stream);
+
+/*
  * IVF list gather: exact k-nearest search of each query over the rows of the
  * lists it probes -- the list scan of the reference's IVFFlat index
  * (src/ivfscan.c:124-186: visit the probed lists, score every entry, order
@@ -165,6 +220,22 @@ int			AnnB200SearchLists(AnnB200Shard *shard, const float *queries, uint32_t nq,
 							   uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap,
 							   double *out_dist, int64_t *out_id, uint32_t *out_count,
 							   int32_t *status, void *stream);
+
+/*
+ * One rank of a sharded IVF list search: AnnB200SearchLists over this
+ * rank's share of the list-major rows (each list it holds clipped to its
+ * rows, list numbers and probes in its own numbering, UINT32_MAX for lists
+ * it does not hold, global ids through row_ids or first_id), then the
+ * all-gather and device merge of AnnB200SearchSharded: every rank receives
+ * the k best over every rank's share of each query's probed lists. Same
+ * conditions as AnnB200SearchSharded.
+ */
+int			AnnB200SearchListsSharded(AnnB200Shard *shard, AnnB200Comm *comm, const float *queries,
+									  uint32_t nq, const uint64_t *list_offsets, uint32_t nlists,
+									  const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids,
+									  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap,
+									  double *out_dist, int64_t *out_id, uint32_t *out_count,
+									  int32_t *status, void *stream);
 
 /*
  * IVF coarse probe: each query's nprobe nearest list centroids -- the list

@@ -98,6 +98,47 @@ class Shard:
                                    _ptr(status), _stream(stream)))
         return dist, ids, count
 
+    def search_sharded(self, comm, queries, k, metric, rows=None, stream=None, status=None, force_simt=False):
+        """One rank of a row-sharded search (AnnB200SearchSharded): every rank
+        of `comm` calls this with its own shard and candidate rows and the
+        same queries; each gets the k best over all ranks' rows. Returns
+        (dist, id, count) CUDA tensors like search()."""
+        import torch
+        nq = int(queries.shape[0])
+        nrows = int(rows.shape[0]) if rows is not None else self.rows
+        cap = max(int(k), 1)
+        dev = queries.device
+        dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
+        ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
+        count = torch.empty((nq,), dtype=torch.int32, device=dev)
+        if rows is not None and rows.numel() == 0:
+            rows = torch.zeros((1,), dtype=torch.int32, device=dev)
+        check(load().AnnB200SearchSharded(self._handle, comm.handle if comm is not None else None, _ptr(queries), nq,
+                                          _ptr(rows), nrows if rows is not None else 0, int(k), int(metric),
+                                          FORCE_SIMT if force_simt else 0, cap, _ptr(dist), _ptr(ids), _ptr(count),
+                                          _ptr(status), _stream(stream)))
+        return dist, ids, count
+
+    def search_lists_sharded(self, comm, queries, k, metric, offsets, probes, row_ids=None, stream=None,
+                             status=None, force_simt=False):
+        """One rank of a sharded IVF list search (AnnB200SearchListsSharded):
+        this rank's share of the lists, then the exchange and merge."""
+        import torch
+        nq = int(queries.shape[0])
+        nlists = int(offsets.shape[0]) - 1
+        nprobe = int(probes.shape[1]) if probes.dim() == 2 else 0
+        cap = max(int(k), 1)
+        dev = queries.device
+        dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
+        ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
+        count = torch.empty((nq,), dtype=torch.int32, device=dev)
+        check(load().AnnB200SearchListsSharded(self._handle, comm.handle if comm is not None else None,
+                                               _ptr(queries), nq, _ptr(offsets), nlists, _ptr(probes), nprobe,
+                                               _ptr(row_ids), int(k), int(metric), FORCE_SIMT if force_simt else 0,
+                                               cap, _ptr(dist), _ptr(ids), _ptr(count), _ptr(status),
+                                               _stream(stream)))
+        return dist, ids, count
+
     def search_lists(self, queries, k, metric, offsets, probes, row_ids=None, stream=None, status=None,
                      force_simt=False):
         """IVF list gather: each query's k nearest among the rows of the lists
@@ -144,6 +185,41 @@ class Shard:
                                         int(metric), FORCE_SIMT if force_simt else 0, _ptr(out), _ptr(err),
                                         _stream(stream)))
         return out[:, :n], err
+
+
+class Comm:
+    """One rank's NCCL communicator in libannb200 (AnnB200CommCreate): the
+    all-gather of the row-sharded searches. comm_id: the 128 bytes
+    Comm.unique_id() returned on one rank, shared with all ranks."""
+
+    def __init__(self, device, nranks, rank, comm_id):
+        handle = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(comm_id), 128)
+        check(load().AnnB200CommCreate(int(device), int(nranks), int(rank), buf, ctypes.byref(handle)))
+        self.handle = handle
+        self.rank, self.nranks, self.device = int(rank), int(nranks), int(device)
+
+    @staticmethod
+    def unique_id():
+        buf = ctypes.create_string_buffer(128)
+        check(load().AnnB200CommId(buf))
+        return buf.raw
+
+    def abort(self):
+        """End this rank's part of the group at once (peers gone)."""
+        if getattr(self, 'handle', None):
+            load().AnnB200CommAbort(self.handle)
+
+    def close(self):
+        if getattr(self, 'handle', None):
+            load().AnnB200CommDestroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def merge_topk(dist, ids, counts, k, window=False, out_cap=None, stream=None):

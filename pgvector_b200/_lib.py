@@ -56,6 +56,18 @@ SIGNATURES = {
     'AnnB200ScoreMatrix': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
                                    c_void_p, c_void_p, c_void_p]),
     'AnnB200StageTimes': (c_int, [c_void_p, c_void_p, c_uint32, c_int]),
+    'AnnB200CommId': (c_int, [c_void_p]),
+    'AnnB200CommCreate': (c_int, [c_int, c_int, c_int, c_void_p, ctypes.POINTER(c_void_p)]),
+    'AnnB200CommCreateAll': (c_int, [c_int, c_void_p, c_void_p]),
+    'AnnB200CommDestroy': (None, [c_void_p]),
+    'AnnB200CommAbort': (None, [c_void_p]),
+    'AnnB200CommRank': (c_int, [c_void_p]),
+    'AnnB200CommSize': (c_int, [c_void_p]),
+    'AnnB200SearchListsSharded': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p,
+                                          c_uint32, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
+                                          c_void_p, c_void_p, c_void_p, c_void_p]),
+    'AnnB200SearchSharded': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
+                                     c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

@@ -21,7 +21,7 @@ NVCC = os.path.join(CUDA_HOME, 'bin', 'nvcc')
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 NVCC_FLAGS = ARCH + ['-O3', '-lineinfo', '-std=c++17', '-Xcompiler', '-fPIC', '-I' + INCLUDE,
                      '--expt-relaxed-constexpr']
-CU_SOURCES = ['scan_simt.cu', 'scan_tc.cu', 'select.cu', 'shard.cu', 'ivf.cu', 'bitmap_static.cu']
+CU_SOURCES = ['scan_simt.cu', 'scan_tc.cu', 'select.cu', 'shard.cu', 'ivf.cu', 'bitmap_static.cu', 'comm.cu']
 C_SOURCES = ['backend.c']
 
 
@@ -65,7 +65,7 @@ def build(verbose=False, force=False, ptxas_info=False):
             if verbose and out.strip():
                 print(out)
     if force or jobs or _stale(LIB, objects):
-        _run([NVCC] + ARCH + ['-shared', '-o', LIB] + objects + ['-lpthread'])
+        _run([NVCC] + ARCH + ['-shared', '-o', LIB] + objects + ['-lpthread', '-ldl'])
     return LIB
 
 

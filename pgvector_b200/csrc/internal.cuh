@@ -416,6 +416,12 @@ cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t 
                          uint32_t nq, uint32_t list_cap, uint32_t k, int window, uint32_t out_cap,
                          double *out_dist, int64_t *out_id, uint32_t *out_count, uint32_t *flags,
                          cudaStream_t st);
+// The non-window merge of sorted per-shard lists by rank (no sort), each
+// array's lists `*_stride` bytes apart; nlists * list_cap <= kSortCap.
+cudaError_t launch_merge_ranked(const void *dist, uint64_t dist_stride, const void *ids, uint64_t id_stride,
+                                const void *counts, uint64_t count_stride, uint32_t nlists, uint32_t nq,
+                                uint32_t list_cap, uint32_t k, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                                uint32_t *out_count, cudaStream_t st);
 uint32_t bitmap_blocks(uint64_t nbits);
 void launch_v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, const QueryState &qs, cudaStream_t st);
 void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,

@@ -994,6 +994,84 @@ __global__ void __launch_bounds__(NT) finalize_big(SelectArgs a, uint32_t q, uns
   write_results(a, q, key, pos, m);
 }
 
+// ---------------------------------------------------------------- rank merge
+
+// Lists of per-shard results, each sorted by (distance, id): list l of query
+// q has counts[l][q] entries at dist[l][q][..], ids[l][q][..], where list l
+// starts `*_stride` bytes after list l-1 (the [nlists][nq][cap] layout of
+// AnnB200MergeTopk, or the per-rank packets of the sharded search's
+// all-gather).
+struct RankMergeArgs {
+  const uint8_t *dist, *ids, *counts;
+  uint64_t dist_stride, id_stride, count_stride;
+  uint32_t nlists, nq, list_cap, k, out_cap;
+  double *out_dist;
+  int64_t *out_id;
+  uint32_t *out_count;
+};
+
+constexpr int RM_NT = 256;
+
+// (key, id, list) order: equal (distance, id) pairs -- which disjoint shards
+// never produce -- still get distinct ranks.
+__device__ __forceinline__ bool rank_before(unsigned long long ka, unsigned long long ia, uint32_t la,
+                                            unsigned long long kb, unsigned long long ib, uint32_t lb) {
+  return ka < kb || (ka == kb && (ia < ib || (ia == ib && la < lb)));
+}
+
+// Per query: each entry's place in the merged order is its position in its
+// own list plus, for every other list, how many of that list's entries come
+// before it (a binary search: the lists are sorted). Entries placed before k
+// are written there. No sort: one pass over the lists in shared memory.
+__global__ void __launch_bounds__(RM_NT) merge_ranked(RankMergeArgs a) {
+  extern __shared__ uint8_t dyn[];
+  unsigned long long *key = reinterpret_cast<unsigned long long *>(dyn);
+  unsigned long long *idk = key + kSortCap;
+  __shared__ uint32_t s_off[65];
+  const uint32_t q = blockIdx.x;
+  if (threadIdx.x == 0) {
+    uint32_t o = 0;
+    for (uint32_t l = 0; l < a.nlists; l++) {
+      s_off[l] = o;
+      const uint32_t c = reinterpret_cast<const uint32_t *>(a.counts + l * a.count_stride)[q];
+      o += c < a.list_cap ? c : a.list_cap;
+    }
+    s_off[a.nlists] = o;
+  }
+  __syncthreads();
+  const uint32_t total = s_off[a.nlists];
+  for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
+    uint32_t l = 0;
+    while (s_off[l + 1] <= i) l++;
+    const uint64_t src = (uint64_t)q * a.list_cap + (i - s_off[l]);
+    key[i] = double_key(reinterpret_cast<const double *>(a.dist + l * a.dist_stride)[src]);
+    idk[i] = (unsigned long long)reinterpret_cast<const int64_t *>(a.ids + l * a.id_stride)[src] ^
+             0x8000000000000000ull;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
+    uint32_t l = 0;
+    while (s_off[l + 1] <= i) l++;
+    const unsigned long long ki = key[i], ii = idk[i];
+    uint32_t rank = i - s_off[l];
+    for (uint32_t m = 0; m < a.nlists && rank < a.k; m++) {
+      if (m == l) continue;
+      uint32_t lo = s_off[m], hi = s_off[m + 1];   // first entry of list m not before entry i
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (rank_before(key[mid], idk[mid], m, ki, ii, l)) lo = mid + 1;
+        else hi = mid;
+      }
+      rank += lo - s_off[m];
+    }
+    if (rank < a.k) {
+      a.out_dist[(uint64_t)q * a.out_cap + rank] = key_double(ki);
+      a.out_id[(uint64_t)q * a.out_cap + rank] = (int64_t)(ii ^ 0x8000000000000000ull);
+    }
+  }
+  if (threadIdx.x == 0) a.out_count[q] = total < a.k ? total : a.k;
+}
+
 // ---------------------------------------------------------------- score matrix
 
 // v-domain scores -> approximate distances (squared distance for L2).
@@ -1327,6 +1405,20 @@ void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *
     case DT_NVFP4: finalize_big<DT_NVFP4><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
     default: finalize_big<DT_BIT><<<1, NT, 0, st>>>(to_args(l), q, key, pos, p2); break;
   }
+}
+
+cudaError_t launch_merge_ranked(const void *dist, uint64_t dist_stride, const void *ids, uint64_t id_stride,
+                                const void *counts, uint64_t count_stride, uint32_t nlists, uint32_t nq,
+                                uint32_t list_cap, uint32_t k, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                                uint32_t *out_count, cudaStream_t st) {
+  if (nq == 0) return cudaSuccess;
+  RankMergeArgs a{(const uint8_t *)dist, (const uint8_t *)ids, (const uint8_t *)counts, dist_stride, id_stride,
+                  count_stride, nlists, nq, list_cap, k, out_cap, out_dist, out_id, out_count};
+  const size_t smem = (size_t)kSortCap * 16;
+  cudaError_t e = cudaFuncSetAttribute(merge_ranked, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  merge_ranked<<<nq, RM_NT, smem, st>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_merge(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,

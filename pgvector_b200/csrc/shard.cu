@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "../../include/annb200.h"
+#include "comm.cuh"
 #include "internal.cuh"
 
 using namespace annb200;
@@ -138,39 +139,65 @@ bool timing_on() {
   return on;
 }
 
-// CUDA events around stages of one call, on the call's stream; read after
-// the call's own final synchronisation.
+// Recorded stage spans whose events have not been read yet. A call never
+// waits for its stage events: they are read once complete -- at the start of
+// a later call, or all of them (waiting) when AnnB200StageTimes reports --
+// so the timing adds no host synchronisation to the calls it times.
+struct Span {
+  int stage;
+  cudaEvent_t a, b;
+};
+std::vector<Span> g_pending;   // under g_stage_mu
+
+// Fold completed spans into the totals (all of them, waiting, when `wait`).
+void collect_spans(bool wait) {
+  std::lock_guard<std::mutex> lock(g_stage_mu);
+  size_t keep = 0;
+  for (size_t i = 0; i < g_pending.size(); i++) {
+    Span &sp = g_pending[i];
+    cudaError_t e = wait ? cudaEventSynchronize(sp.b) : cudaEventQuery(sp.b);
+    if (e == cudaErrorNotReady) {
+      g_pending[keep++] = sp;
+      continue;
+    }
+    float ms = 0;
+    if (e == cudaSuccess && cudaEventElapsedTime(&ms, sp.a, sp.b) == cudaSuccess) {
+      g_stage_ms[sp.stage] += ms;
+      g_stage_calls[sp.stage] += 1;
+    }
+    cudaGetLastError();
+    cudaEventDestroy(sp.a);
+    cudaEventDestroy(sp.b);
+  }
+  g_pending.resize(keep);
+}
+
+// CUDA events around stages of one call, on the call's stream; handed to
+// the pending list when the call returns.
 struct StageClock {
   cudaStream_t st;
   bool on;
-  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> spans;
-  explicit StageClock(cudaStream_t s) : st(s), on(timing_on()) {}
+  std::vector<Span> spans;
+  explicit StageClock(cudaStream_t s) : st(s), on(timing_on()) {
+    if (on) collect_spans(false);
+  }
   int begin(int stage) {
     if (!on) return -1;
     if (g_stage_override >= 0) stage = g_stage_override;
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    cudaEventRecord(a, st);
-    spans.push_back({stage, {a, b}});
+    Span sp{stage, nullptr, nullptr};
+    cudaEventCreate(&sp.a);
+    cudaEventCreate(&sp.b);
+    cudaEventRecord(sp.a, st);
+    spans.push_back(sp);
     return (int)spans.size() - 1;
   }
   void end(int h) {
-    if (h >= 0) cudaEventRecord(spans[h].second.second, st);
+    if (h >= 0) cudaEventRecord(spans[h].b, st);
   }
   ~StageClock() {
-    if (!on) return;
+    if (!on || spans.empty()) return;
     std::lock_guard<std::mutex> lock(g_stage_mu);
-    for (auto &sp : spans) {
-      float ms = 0;
-      if (cudaEventSynchronize(sp.second.second) == cudaSuccess &&
-          cudaEventElapsedTime(&ms, sp.second.first, sp.second.second) == cudaSuccess) {
-        g_stage_ms[sp.first] += ms;
-        g_stage_calls[sp.first] += 1;
-      }
-      cudaEventDestroy(sp.second.first);
-      cudaEventDestroy(sp.second.second);
-    }
+    g_pending.insert(g_pending.end(), spans.begin(), spans.end());
   }
 };
 
@@ -533,9 +560,16 @@ int big_sorts(AnnB200Shard *sh, const SelectLaunch &sl, const uint32_t *big, uin
 }
 
 // One search over queries [q0, q0+nq) (nq within one tensor-scan launch).
+//
+// defer_flags (device, 8 words) selects the deferred form the sharded search
+// uses: everything is enqueued on st with no host synchronisation, and the
+// search's flag words are copied to defer_flags when its kernels end; the
+// caller inspects them later and runs the search again synchronously if a
+// candidate list overflowed or a query needs the large sort.
 int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows, uint64_t nrows,
                  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
-                 uint32_t *out_count, int32_t *status, cudaStream_t st, bool *any_invalid) {
+                 uint32_t *out_count, int32_t *status, cudaStream_t st, bool *any_invalid,
+                 uint32_t *defer_flags = nullptr) {
   const ShardView &v = sh->view;
   const bool bits = v.dtype == DT_BIT;
   const bool window = flags & ANNB200_WINDOW;
@@ -780,6 +814,12 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
       CK(launch_finalize(sl, exact, st), "finalize");
       clock.end(h);
       counted(3);
+      if (defer_flags) {
+        CK(cudaMemcpyAsync(defer_flags, dflags, 32, cudaMemcpyDeviceToDevice, st), "flags");
+        if (status)
+          CK(cudaMemcpyAsync(status, qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToDevice, st), "status");
+        return OK;
+      }
       CK(cudaMemcpyAsync(sh->hflags, dflags, 32, cudaMemcpyDeviceToHost, st), "flags");
       CK(cudaStreamSynchronize(st), "search");
       if (sh->hflags[0] & FLAG_TIMEOUT) return fail(BACKEND_ERROR, "tensor scan pipeline timed out");
@@ -806,6 +846,12 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     if (sh->hflags[0] & FLAG_OUT_CAP) return fail(INVALID, "window results exceed out_cap");
   } else {
     CK(cudaMemsetAsync(out_count, 0, nq * sizeof(uint32_t), st), "memset");
+    if (defer_flags) {
+      CK(cudaMemcpyAsync(defer_flags, dflags, 32, cudaMemcpyDeviceToDevice, st), "flags");
+      if (status)
+        CK(cudaMemcpyAsync(status, qs.status, nq * sizeof(int32_t), cudaMemcpyDeviceToDevice, st), "status");
+      return OK;
+    }
     CK(cudaMemcpyAsync(sh->hflags, dflags, 32, cudaMemcpyDeviceToHost, st), "flags");
     CK(cudaStreamSynchronize(st), "search");
   }
@@ -844,6 +890,169 @@ extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq,
   }
   if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
   return OK;
+}
+
+// ---------------------------------------------------------------- row-sharded search over NCCL
+//
+// Every rank searches its own shard (global ids first_id + row) for the
+// same queries, then one all-gather moves each rank's packet -- a header
+// (its status and its search's flag words), its counts, distances and ids
+// -- to every rank, and each rank merges the lists on its device. The
+// search is enqueued without a host round trip (the deferred form of
+// search_block); the one synchronisation comes after the merge, when every
+// rank reads every rank's header. Because all ranks see the same headers,
+// they take the same decision: fail together, or -- when some rank's
+// candidate list overflowed or needs the large sort -- all search again
+// synchronously and exchange a second time. No rank ever leaves a
+// collective the others enter.
+
+namespace {
+
+constexpr uint32_t kShardBlocks = 8;                  // query blocks a sharded call (8 x 4,096 queries)
+constexpr size_t kHead = 16 + 32 * kShardBlocks;      // status word + 8 flag words a block
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+struct Packet {
+  size_t counts, dist, ids, bytes;
+  Packet(uint32_t nq, uint32_t k) {
+    counts = kHead;
+    dist = counts + align16((size_t)nq * 4);
+    ids = dist + (size_t)nq * k * 8;
+    bytes = align16(ids + (size_t)nq * k * 8);
+  }
+};
+
+// This rank's search of the queries into its packet: deferred (flags to the
+// header) or synchronous (overflow and large sorts handled here). Returns a
+// local status; the caller puts it in the header.
+int local_search(AnnB200Shard *sh, uint8_t *pk, const Packet &pl, const void *queries, uint32_t nq,
+                 const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags, int32_t *status,
+                 cudaStream_t st, bool deferred) {
+  const ShardView &v = sh->view;
+  const uint32_t block = tc_scan_max_queries();
+  const uint64_t qbytes = v.dtype == DT_BIT ? v.row_bytes : (uint64_t)v.dims * 4;
+  bool any_invalid = false;
+  for (uint32_t b = 0, q0 = 0; q0 < nq; q0 += block, b++) {
+    const uint32_t m = std::min(block, nq - q0);
+    int r = search_block(sh, (const uint8_t *)queries + q0 * qbytes, m, rows, nrows, k, metric, flags, k,
+                         (double *)(pk + pl.dist) + (uint64_t)q0 * k, (int64_t *)(pk + pl.ids) + (uint64_t)q0 * k,
+                         (uint32_t *)(pk + pl.counts) + q0, status ? status + q0 : nullptr, st, &any_invalid,
+                         deferred ? (uint32_t *)(pk + 16 + 32 * b) : nullptr);
+    if (r != OK) return r;
+  }
+  if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  return OK;
+}
+
+}  // namespace
+
+namespace {
+
+// The exchange both sharded searches share: `local(pk, deferred)` searches
+// this rank's shard into its packet (deferred: enqueued only, flags to the
+// header) and returns a local status; `local_ok` is this rank's argument
+// check. See AnnB200SearchSharded.
+template <typename Local>
+int sharded_exchange(AnnB200Shard *sh, AnnB200Comm *comm, int local, uint32_t nq, uint32_t k, uint32_t out_cap,
+                     double *out_dist, int64_t *out_id, uint32_t *out_count, cudaStream_t st, Local local_fn) {
+  if (nq == 0) return local;        // every rank sees the same nq: no exchange at all
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock_comm(comm->mu);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  const Packet pl(nq, k);
+  // without room for the exchange this rank cannot join it: the others end
+  // by the communicator's time limit
+  int r = comm_reserve(comm, pl.bytes, kHead);
+  if (r != OK) return r;
+  uint8_t *pk = (uint8_t *)comm->send;
+  const uint8_t *all = (const uint8_t *)comm->recv;
+  std::string local_msg;
+  for (int round = 0; round < 2; round++) {
+    CK(cudaMemsetAsync(pk, 0, pl.dist, st), "memset");       // header and counts
+    if (local == OK) {
+      local = local_fn(pk, pl, round == 0);
+      if (local != OK) CK(cudaMemsetAsync(pk, 0, pl.dist, st), "memset");
+    }
+    if (local != OK) local_msg = g_error;
+    *comm->host_status = local;
+    CK(cudaMemcpyAsync(pk, comm->host_status, 4, cudaMemcpyHostToDevice, st), "status");
+    StageClock clock(st);
+    int h = clock.begin(ST_MERGE);
+    r = comm_allgather(comm, pk, comm->recv, pl.bytes, st);
+    if (r != OK) return r;       // this rank's NCCL failed: the others end by the time limit
+    if (out_dist && out_id && out_count && out_cap >= k) {
+      CK(launch_merge_ranked(all + pl.dist, pl.bytes, all + pl.ids, pl.bytes, all + pl.counts, pl.bytes,
+                             (uint32_t)comm->nranks, nq, k, k, out_cap, out_dist, out_id, out_count, st),
+         "merge");
+      counted(1);
+    }
+    clock.end(h);
+    CK(cudaMemcpy2DAsync(comm->host_heads, kHead, all, pl.bytes, kHead, comm->nranks, cudaMemcpyDeviceToHost, st),
+       "headers");
+    r = comm_wait(comm, st);
+    if (r != OK) return r;
+    // every rank now holds every rank's header: the same decision everywhere
+    bool again = false, timeout = false, bad_rows = false, invalid_q = false;
+    int first_bad = OK, bad_rank = -1;
+    for (int rk = 0; rk < comm->nranks; rk++) {
+      const uint8_t *hd = comm->host_heads + (size_t)rk * kHead;
+      const int32_t rs = *(const int32_t *)hd;
+      if (rs != OK && first_bad == OK) {
+        first_bad = rs;
+        bad_rank = rk;
+      }
+      for (uint32_t b = 0; b < kShardBlocks; b++) {
+        const uint32_t *fw = (const uint32_t *)(hd + 16 + 32 * b);
+        if (round == 0 && (fw[0] & (FLAG_OVERFLOW | FLAG_BIGSORT))) again = true;
+        if (fw[0] & FLAG_TIMEOUT) timeout = true;
+        if (fw[0] & FLAG_BAD_ROWS) bad_rows = true;
+        if (fw[5]) invalid_q = true;
+      }
+    }
+    if (first_bad != OK) {
+      if (bad_rank == comm->rank) return fail(first_bad, "%s", local_msg.c_str());
+      return fail(first_bad, "rank %d of the sharded search failed", bad_rank);
+    }
+    if (timeout) return fail(BACKEND_ERROR, "tensor scan pipeline timed out on a rank of the sharded search");
+    if (bad_rows) return fail(INVALID, "candidate rows must be increasing and within each rank's shard");
+    if (invalid_q) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+    if (!again) return OK;
+  }
+  return OK;
+}
+
+}  // namespace
+
+extern "C" int AnnB200SearchSharded(AnnB200Shard *sh, AnnB200Comm *comm, const void *queries, uint32_t nq,
+                                    const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags,
+                                    uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
+                                    int32_t *status, void *stream) {
+  if (!comm)
+    return AnnB200Search(sh, queries, nq, rows, nrows, k, metric, flags, out_cap, out_dist, out_id, out_count, status,
+                         stream);
+  if (!sh) return fail(INVALID, "shard is NULL");
+  if (comm->device != sh->device)
+    return fail(INVALID, "the communicator's device %d is not the shard's %d", comm->device, sh->device);
+  // Checks that depend on this rank alone become its status: the rank still
+  // joins the exchange, and every rank returns the failure.
+  const ShardView &v = sh->view;
+  int local = OK;
+  if (flags & ANNB200_WINDOW) local = fail(UNSUPPORTED, "a sharded search returns the strict top k");
+  else if (v.dtype == DT_BIT ? metric != M_HAM : metric > M_COS)
+    local = fail(UNSUPPORTED, "metric %u does not apply to storage format %u", metric, v.dtype);
+  else if (!queries || !out_dist || !out_id || !out_count) local = fail(INVALID, "NULL query or result pointer");
+  else if (out_cap < k) local = fail(INVALID, "out_cap %u < k %u", out_cap, k);
+  else if (rows && nrows > v.rows) local = fail(INVALID, "more candidate rows than the shard holds");
+  else if ((uint64_t)comm->nranks * k > (uint64_t)kSortCap)
+    local = fail(UNSUPPORTED, "ranks x k must not exceed %d", kSortCap);
+  else if (nq > kShardBlocks * tc_scan_max_queries())
+    local = fail(UNSUPPORTED, "at most %u queries a sharded call", kShardBlocks * tc_scan_max_queries());
+  return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream,
+                          [&](uint8_t *pk, const Packet &pl, bool deferred) {
+                            return local_search(sh, pk, pl, queries, nq, rows, nrows, k, metric, flags, status,
+                                                (cudaStream_t)stream, deferred);
+                          });
 }
 
 // The coarse probe: each query's nprobe nearest centroids, as a search of
@@ -1060,11 +1269,12 @@ int search_lists_block(AnnB200Shard *sh, const float *queries, uint32_t nq, cons
 
 }  // namespace
 
-extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *list_offsets,
-                                  uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids,
-                                  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist,
-                                  int64_t *out_id, uint32_t *out_count, int32_t *status, void *stream) {
-  if (!sh) return fail(INVALID, "shard is NULL");
+namespace {
+
+// The argument checks of a list search (the shard's, the call's).
+int lists_check(const AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *list_offsets,
+                uint32_t nlists, const uint32_t *probes, uint32_t nprobe, uint32_t k, uint32_t metric, uint32_t flags,
+                uint32_t out_cap, const double *out_dist, const int64_t *out_id, const uint32_t *out_count) {
   const ShardView &v = sh->view;
   if (v.dtype == DT_BIT || metric > M_COS)
     return fail(UNSUPPORTED, "list search takes L2, inner product or cosine over vector rows");
@@ -1075,9 +1285,15 @@ extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32
   if (out_cap < k) return fail(INVALID, "out_cap %u < k %u", out_cap, k);
   if (nlists > kMaxLists) return fail(UNSUPPORTED, "more than %u lists", kMaxLists);
   if (nprobe > kMaxProbes) return fail(UNSUPPORTED, "more than %u probes a query", kMaxProbes);
-  DeviceGuard g(sh->device);
-  std::lock_guard<std::mutex> lock(sh->mu);
-  cudaStream_t st = (cudaStream_t)stream;
+  return OK;
+}
+
+// Every query's list search, in blocks of 4,096 queries (the shard's lock held).
+int search_lists_all(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *list_offsets,
+                     uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids, uint32_t k,
+                     uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                     uint32_t *out_count, int32_t *status, cudaStream_t st) {
+  const ShardView &v = sh->view;
   const uint32_t block = 4096;
   bool any_invalid = false;
   for (uint32_t q0 = 0; q0 < nq; q0 += block) {
@@ -1099,6 +1315,48 @@ extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32
   return OK;
 }
 
+}  // namespace
+
+extern "C" int AnnB200SearchLists(AnnB200Shard *sh, const float *queries, uint32_t nq, const uint64_t *list_offsets,
+                                  uint32_t nlists, const uint32_t *probes, uint32_t nprobe, const int64_t *row_ids,
+                                  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist,
+                                  int64_t *out_id, uint32_t *out_count, int32_t *status, void *stream) {
+  if (!sh) return fail(INVALID, "shard is NULL");
+  int r = lists_check(sh, queries, nq, list_offsets, nlists, probes, nprobe, k, metric, flags, out_cap, out_dist,
+                      out_id, out_count);
+  if (r != OK || nq == 0) return r;
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  return search_lists_all(sh, queries, nq, list_offsets, nlists, probes, nprobe, row_ids, k, metric, flags, out_cap,
+                          out_dist, out_id, out_count, status, (cudaStream_t)stream);
+}
+
+extern "C" int AnnB200SearchListsSharded(AnnB200Shard *sh, AnnB200Comm *comm, const float *queries, uint32_t nq,
+                                         const uint64_t *list_offsets, uint32_t nlists, const uint32_t *probes,
+                                         uint32_t nprobe, const int64_t *row_ids, uint32_t k, uint32_t metric,
+                                         uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+                                         uint32_t *out_count, int32_t *status, void *stream) {
+  if (!comm)
+    return AnnB200SearchLists(sh, queries, nq, list_offsets, nlists, probes, nprobe, row_ids, k, metric, flags, out_cap,
+                              out_dist, out_id, out_count, status, stream);
+  if (!sh) return fail(INVALID, "shard is NULL");
+  if (comm->device != sh->device)
+    return fail(INVALID, "the communicator's device %d is not the shard's %d", comm->device, sh->device);
+  int local = lists_check(sh, queries, nq, list_offsets, nlists, probes, nprobe, k, metric, flags, out_cap, out_dist,
+                          out_id, out_count);
+  if (local == OK && (uint64_t)comm->nranks * k > (uint64_t)kSortCap)
+    local = fail(UNSUPPORTED, "ranks x k must not exceed %d", kSortCap);
+  // the list search synchronises on its own (its windows): the exchange's
+  // header carries only its status
+  return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream,
+                          [&](uint8_t *pk, const Packet &pl, bool) {
+                            return search_lists_all(sh, queries, nq, list_offsets, nlists, probes, nprobe, row_ids, k,
+                                                    metric, flags, k, (double *)(pk + pl.dist),
+                                                    (int64_t *)(pk + pl.ids), (uint32_t *)(pk + pl.counts), status,
+                                                    (cudaStream_t)stream);
+                          });
+}
+
 extern "C" int AnnB200MergeTopk(const double *dist, const int64_t *ids, const uint32_t *counts, uint32_t nlists,
                                 uint32_t nq, uint32_t list_cap, uint32_t k, uint32_t flags, uint32_t out_cap,
                                 double *out_dist, int64_t *out_id, uint32_t *out_count, void *stream) {
@@ -1108,19 +1366,28 @@ extern "C" int AnnB200MergeTopk(const double *dist, const int64_t *ids, const ui
     return fail(UNSUPPORTED, "merge takes at most 64 lists and 4096 entries a query");
   if (!(flags & ANNB200_WINDOW) && out_cap < k) return fail(INVALID, "out_cap %u < k %u", out_cap, k);
   cudaStream_t st = (cudaStream_t)stream;
+  StageClock clock(st);
+  if (!(flags & ANNB200_WINDOW)) {
+    // the k best of sorted lists, by rank; queued on the stream with no host
+    // round trip (k <= out_cap was checked)
+    const uint64_t per = (uint64_t)nq * list_cap;
+    int h = clock.begin(ST_MERGE);
+    CK(launch_merge_ranked(dist, per * sizeof(double), ids, per * sizeof(int64_t), counts, (uint64_t)nq * 4, nlists,
+                           nq, list_cap, k, out_cap, out_dist, out_id, out_count, st),
+       "merge");
+    clock.end(h);
+    counted(1);
+    return OK;
+  }
   static thread_local DeviceBuffer fl;
   CK(fl.reserve(64), "merge flags");
   CK(cudaMemsetAsync(fl.p, 0, 16, st), "memset");
-  StageClock clock(st);
   int h = clock.begin(ST_MERGE);
   CK(launch_merge(dist, ids, counts, nlists, nq, list_cap, k, flags & ANNB200_WINDOW, out_cap, out_dist, out_id,
                   out_count, (uint32_t *)fl.p, st),
      "merge");
   clock.end(h);
   counted(1);
-  // only a window can outgrow out_cap (k <= out_cap was checked): without
-  // one the merge stays queued on the stream, with no host round trip
-  if (!(flags & ANNB200_WINDOW)) return OK;
   uint32_t hf = 0;
   CK(cudaMemcpyAsync(&hf, fl.p, 4, cudaMemcpyDeviceToHost, st), "merge flags");
   CK(cudaStreamSynchronize(st), "merge");
@@ -1183,6 +1450,7 @@ extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t
 extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(); }
 
 extern "C" int AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset) {
+  collect_spans(true);
   std::lock_guard<std::mutex> lock(g_stage_mu);
   for (uint32_t i = 0; i < n && i < (uint32_t)ST_COUNT; i++) {
     if (ms) ms[i] = g_stage_ms[i];

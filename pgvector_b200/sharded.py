@@ -5,8 +5,12 @@ tree-merges the per-shard top-k lists on the host (shard placement
 ann/server/cuvs.c:2845-2862, AnnIndexTreeMerge
 ann/server/indexfile.c:3235-3258). Here each rank owns one contiguous range,
 searches it on its GPU, and the per-rank lists are combined by one NCCL
-all-gather followed by the on-device merge (AnnB200MergeTopk) -- the only
-collective on the path.
+all-gather followed by the on-device merge -- the only collective on the
+path. The exchange lives in libannb200 (AnnB200SearchSharded, with its own
+NCCL communicator: comm_from_process_group); torch.distributed only carries
+the communicator's id from rank 0 to the others. gather_lists and
+search_sharded are the same exchange through torch.distributed, kept for
+the CPU (gloo) tests of the host logic.
 """
 
 
@@ -86,3 +90,16 @@ def search_sharded(shard, queries, k, metric, rows, group=None, merge=None):
     if merge is None:
         from . import merge_topk as merge
     return merge(gd, gi, gc, k)
+
+
+def comm_from_process_group(device, group=None):
+    """This rank's libannb200 NCCL communicator over the ranks of a
+    torch.distributed group: rank 0 makes the id, a broadcast hands it to
+    the others (the only use of torch.distributed here), and every rank
+    joins with its device."""
+    import torch.distributed as dist
+    from . import Comm
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    box = [Comm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0, group=group)
+    return Comm(device, world, rank, box[0])

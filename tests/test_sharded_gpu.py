@@ -1,0 +1,183 @@
+"""The row-sharded search through libannb200's own NCCL communicator
+(AnnB200SearchSharded / AnnB200SearchListsSharded): per-rank search, one
+all-gather of the ranks' packets, device merge -- against the oracle over
+the whole corpus, bit for bit.
+
+One GPU: a one-rank communicator runs the whole exchange (packet, NCCL
+all-gather, merge, header check), including the second round that follows a
+candidate-list overflow. Two GPUs (skipped with fewer): two processes, one a
+GPU, each holding half the rows; and a rank that never joins, whose peer's
+exchange ends with ANN_BACKEND_ERROR at the communicator's time limit (the
+communicator is aborted; no GPU faults). NVLS is off in these tests
+(NCCL_NVLS_ENABLE=0)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle
+from pgvector_b200 import sharded, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(a, dev):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    if a.dtype == np.uint64:
+        a = a.view(np.int64)
+    return torch.from_numpy(a).to(dev)
+
+
+def one_rank_comm(device=0):
+    import pgvector_b200 as pb
+    return pb.Comm(device, 1, 0, pb.Comm.unique_id())
+
+
+def same(got, want, nq):
+    gd, gi, gc = (t.cpu().numpy() for t in got)
+    od, oi, oc = want[:3]
+    assert np.array_equal(gc, oc.astype(gc.dtype))
+    for q in range(nq):
+        c = int(oc[q])
+        assert np.array_equal(gi[q, :c], oi[q, :c]), q
+        assert np.array_equal(gd[q, :c], od[q, :c]), q
+
+
+def test_one_rank_exchange_equals_oracle(cuda):
+    os.environ['NCCL_NVLS_ENABLE'] = '0'
+    import pgvector_b200 as pb
+    comm = one_rank_comm()
+    try:
+        # FP16 cosine over a filter row list (the headline workload's path)
+        x = synth.mixture(50000, 256, 40, seed=11, normalize=True)
+        h = synth.to_half_bits(x)
+        q = synth.mixture_queries(300, 256, 40, seed=12, normalize=True).astype(np.float16).astype(np.float32)
+        _, ids = synth.bitmap(50000, 0.5, seed=13)
+        shard = pb.Shard(pb.F16, 256, to_dev(h, cuda), first_id=1000)
+        got = shard.search_sharded(comm, to_dev(q, cuda), 50, pb.COSINE, rows=to_dev(ids, cuda))
+        od, oi, oc, _ = oracle.search(oracle.F16, 256, h, q, 50, 2, ids=ids)
+        same(got, (od, np.where(oi >= 0, oi + 1000, -1), oc), 300)
+        # bit rows, Hamming, whole shard
+        rows, proto = synth.bit_rows(40000, 512, 64, flip=0.05, seed=14)
+        qs = rows[np.arange(0, 40000, 997)][:40] ^ 1
+        bshard = pb.Shard(pb.BIT, 512, to_dev(rows, cuda))
+        same(bshard.search_sharded(comm, to_dev(qs, cuda), 100, pb.HAMMING), oracle.search(oracle.BIT, 512, rows, qs,
+                                                                                              100, 3), 40)
+        # heavy ties: 30,000 identical rows overflow the candidate lists and
+        # need the large sort -- the second, synchronous round
+        t = synth.mixture(36000, 64, 8, seed=15)
+        t[3000:33000] = t[7]
+        q2 = np.repeat(t[7:8], 20, axis=0) + np.float32(1e-3)
+        tshard = pb.Shard(pb.F32, 64, to_dev(t, cuda))
+        same(tshard.search_sharded(comm, to_dev(q2, cuda), 40, pb.L2), oracle.search(oracle.F32, 64, t, q2, 40, 0), 20)
+        # IVF lists
+        xi, offsets, cent, row_ids = synth.ivf_corpus(30000, 96, 64, seed=16)
+        qi = (cent[np.arange(48) % 64] + 0.05).astype(np.float32)
+        probes = synth.ivf_probes(qi, cent, 6)
+        hi_ = synth.to_half_bits(xi)
+        lshard = pb.Shard(pb.F16, 96, to_dev(hi_, cuda))
+        got = lshard.search_lists_sharded(comm, to_dev(qi, cuda), 20, pb.L2, to_dev(offsets, cuda),
+                                          to_dev(probes, cuda), row_ids=to_dev(row_ids, cuda))
+        same(got, oracle.search_lists(oracle.F16, 96, hi_, qi, offsets, probes, 20, 0, row_ids=row_ids), 48)
+        for s in (shard, bshard, tshard, lshard):
+            s.close()
+    finally:
+        comm.close()
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(('127.0.0.1', 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+ROWS, DIMS, NQ, K = 60000, 192, 200, 64
+
+
+def two_gpu_case():
+    x = synth.mixture(ROWS, DIMS, 30, seed=21, normalize=True)
+    h = synth.to_half_bits(x)
+    q = synth.mixture_queries(NQ, DIMS, 30, seed=22, normalize=True).astype(np.float16).astype(np.float32)
+    words, ids = synth.bitmap(ROWS, 0.4, seed=23)
+    return h, q, words, ids
+
+
+def two_gpu_worker(rank, world, port, out, missing):
+    import torch
+    import torch.distributed as dist
+    import pgvector_b200 as pb
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0',
+                      ANN_B200_COMM_TIMEOUT_MS='3000')
+    torch.cuda.set_device(rank)
+    dev = torch.device('cuda', rank)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    comm = None
+    try:
+        comm = sharded.comm_from_process_group(rank)
+        h, q, words, _ = two_gpu_case()
+        b = sharded.shard_bounds(ROWS, world)
+        lo, hi = b[rank], b[rank + 1]
+        w, nbits = sharded.bitmap_slice(words, lo, hi)
+        rows = pb.bitmap_rows(to_dev(w.view(np.int32), dev), nbits)
+        shard = pb.Shard(pb.F16, DIMS, to_dev(h[lo:hi], dev), first_id=lo)
+        qd = to_dev(q, dev)
+        if missing:
+            # rank 1 never joins the exchange (it stays idle, with nothing in
+            # flight); rank 0's call must end with an error at the time limit
+            if rank == 0:
+                try:
+                    shard.search_sharded(comm, qd, K, pb.COSINE, rows=rows)
+                    out[rank] = 'no error'
+                except pb.AnnB200Error as e:
+                    out[rank] = (e.status, str(e))
+            dist.barrier()
+        else:
+            d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=rows)
+            torch.cuda.synchronize()
+            out[rank] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+            dist.barrier()
+        shard.close()
+    finally:
+        if comm is not None:
+            if missing:
+                comm.abort()           # the group is gone: wait for none of it
+            comm.close()
+        dist.destroy_process_group()
+
+
+def run_two(missing):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs two GPUs')
+    ctx = mp.get_context('spawn')
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    mp.start_processes(two_gpu_worker, args=(2, free_port(), out, missing), nprocs=2, join=True,
+                       start_method='spawn')
+    return out
+
+
+def test_two_gpu_sharded_search_equals_whole(cuda):
+    out = run_two(False)
+    h, q, _, ids = two_gpu_case()
+    od, oi, oc, _ = oracle.search(oracle.F16, DIMS, h, q, K, 2, ids=ids)
+    for r in range(2):
+        d, i, c = out[r]
+        assert np.array_equal(c, oc.astype(c.dtype))
+        assert np.array_equal(i, oi) and np.array_equal(d, od)
+
+
+def test_two_gpu_missing_rank_times_out(cuda):
+    import pgvector_b200 as pb
+    out = run_two(True)
+    status, msg = out[0]
+    assert status == pb.BACKEND_ERROR and 'did not finish' in msg
