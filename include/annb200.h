@@ -292,6 +292,15 @@ int			AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows,
 							  uint64_t *count, void *stream);
 
 /*
+ * AnnB200BitmapRows with every row number offset by first_row: one shard's
+ * bitset (ann/server/indexfile.h:117-144, the per-shard bitsets of a cached
+ * filter) expanded into global row numbers (first_row + bit). first_row +
+ * nbits <= 2^32. Synchronous.
+ */
+int			AnnB200BitmapRowsFrom(const uint32_t *words, uint64_t nbits, uint32_t first_row, uint32_t *rows,
+								  uint64_t *count, void *stream);
+
+/*
  * AnnB200BitmapRows for callers that must not allocate device memory on their
  * call path -- a worker serving from a device-memory budget it reserved at
  * start-up, or a latency-critical caller that cannot afford the device
@@ -333,10 +342,58 @@ int			AnnB200BitmapRowsStatic(const uint32_t *words, uint64_t nbits, uint32_t *r
 typedef struct AnnB200Index AnnB200Index;
 int			AnnB200IndexCreate(int device, uint32_t dims, uint64_t rows, const float *vectors,
 							   AnnB200Index **index);
+
+/*
+ * The same index with its FP32 rows row-sharded over ndev devices, as the
+ * reference spreads an index's shards over its GPUs (placement
+ * ann/server/cuvs.c:2845-2862): part p holds rows [rows*p/ndev,
+ * rows*(p+1)/ndev) on devices[p] (distinct devices). AnnB200IndexSearch on
+ * it searches every part at once (one host thread a part), joins the
+ * parts' lists with one NCCL all-gather (AnnB200CommCreateAll,
+ * AnnB200SearchSharded) and a device merge, and returns the same answer as
+ * the unsharded index, bit for bit. Searches of one such index run one at a
+ * time (every part must enter the exchanges in the same order). ndev == 1
+ * is AnnB200IndexCreate. ANN_UNSUPPORTED without NCCL.
+ */
+int			AnnB200IndexCreateSharded(int ndev, const int *devices, uint32_t dims, uint64_t rows,
+									  const float *vectors, AnnB200Index **index);
 void		AnnB200IndexDestroy(AnnB200Index *index);
 int			AnnB200IndexSearch(AnnB200Index *index, const float *queries, uint32_t nq,
 							   const uint64_t *ordinals, uint64_t nordinals, uint32_t k,
 							   float *out_dist, uint64_t *out_ordinal, uint32_t *out_count);
+
+/*
+ * AnnB200IndexSearch with the eligible rows as per-shard bitsets: the cached
+ * filter forms the reference's server hands its backends (AnnIndexJob
+ * bitsets / deviceBitsets, ann/server/backend.h:85-96; AnnIndexBitmap,
+ * ann/server/indexfile.h:117-144). Shard s covers rows shard_first[s] ..
+ * shard_first[s] + shard_rows[s] - 1 (increasing, disjoint); bit r of
+ * bitsets[s] (word r/32, least significant bit first) marks row
+ * shard_first[s] + r eligible; a NULL bitset marks none. With
+ * ANNB200_BITSETS_DEVICE the bitsets are device memory on
+ * AnnB200IndexDevice(index) (kept there between searches); else host
+ * memory. Results as AnnB200IndexSearch. On an index with its FP32 rows on
+ * one device the bitsets are expanded on the device, with no ordinal list;
+ * other indexes take the rows as ordinals (device bitsets:
+ * ANN_UNSUPPORTED).
+ */
+#define ANNB200_BITSETS_DEVICE 1u
+int			AnnB200IndexSearchBitsets(AnnB200Index *index, const float *queries, uint32_t nq,
+									  uint32_t nshards, const uint32_t *const *bitsets,
+									  const uint64_t *shard_first, const uint64_t *shard_rows,
+									  uint32_t flags, uint32_t k, float *out_dist,
+									  uint64_t *out_ordinal, uint32_t *out_count);
+/* The device holding an index's FP32 rows, or -1 (row-sharded, quantized copy). */
+int			AnnB200IndexDevice(const AnnB200Index *index);
+/*
+ * Keep per-shard bitsets on that device (device[s]: shard s's copy, NULL
+ * for a NULL bitset) -- the reference's cached-bitmap upload hook
+ * (AnnIndexBitmapDevice.upload, ann/server/indexfile.h:147-165) -- and free
+ * them (its release hook). ANN_UNSUPPORTED where AnnB200IndexDevice is -1.
+ */
+int			AnnB200IndexKeepBitsets(AnnB200Index *index, uint32_t nshards, const uint32_t *const *bitsets,
+									const uint64_t *shard_rows, void **device);
+void		AnnB200IndexDropBitsets(AnnB200Index *index, uint32_t nshards, void **device);
 
 /*
  * A loaded index served from its quantized copy (manifest line

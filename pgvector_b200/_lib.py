@@ -44,12 +44,19 @@ SIGNATURES = {
     'AnnB200RescoreGather': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
                                      c_void_p, c_void_p]),
     'AnnB200IndexDestroy': (None, [c_void_p]),
+    'AnnB200IndexSearchBitsets': (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p,
+                                          c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
+    'AnnB200IndexDevice': (c_int, [c_void_p]),
+    'AnnB200IndexKeepBitsets': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p]),
+    'AnnB200IndexDropBitsets': (None, [c_void_p, c_uint32, c_void_p]),
+    'AnnB200IndexCreateSharded': (c_int, [c_int, c_void_p, c_uint32, c_uint64, c_void_p, ctypes.POINTER(c_void_p)]),
     'AnnB200SearchTyped': (c_int, [c_void_p, c_uint32]),
     'AnnB200IndexSearch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_void_p, c_void_p,
                                    c_void_p]),
     'AnnB200MergeTopk': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,
                                  c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p]),
     'AnnB200BitmapRows': (c_int, [c_void_p, c_uint64, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),
+    'AnnB200BitmapRowsFrom': (c_int, [c_void_p, c_uint64, c_uint32, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),
     'AnnB200BitmapRowsStatic': (c_int, [c_void_p, c_uint64, c_void_p, ctypes.POINTER(c_uint64), c_void_p]),
     'AnnB200Backend': (ctypes.POINTER(AnnBackend), []),
     'AnnB200LaunchCount': (ctypes.c_ulonglong, []),

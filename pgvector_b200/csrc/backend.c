@@ -348,6 +348,15 @@ struct AnnB200Index
 	void	   *registered;		/* start of the registered pages */
 	uint32_t	quantSlack;
 	uint32_t	slackRatio;
+	/* an index whose FP32 rows are row-sharded over several devices */
+	uint32_t	nparts;
+	AnnB200Shard **parts;		/* part p: rows partBounds[p] .. [p+1] */
+	uint64_t   *partBounds;
+	int		   *partDevices;
+	AnnB200Comm **comms;		/* one NCCL rank a part */
+	Lane	   *partLanes;		/* staging a part, used under searchLock */
+	pthread_mutex_t searchLock; /* one search at a time: every part enters
+								 * the same exchanges in the same order */
 };
 
 /* Per thread and device: staging for index searches on that device. */
@@ -371,6 +380,26 @@ LaneOn(int device)
 		lane->ready = 1;
 	}
 	return lane;
+}
+
+/* Free a lane's stream and buffers (a part's lane, owned by its index). */
+static void
+LaneRelease(Lane *lane)
+{
+	if (!lane->ready)
+		return;
+	cudaSetDevice(lane->device);
+	cudaStreamSynchronize(lane->stream);
+	cudaStreamDestroy(lane->stream);
+	cudaFree(lane->query);
+	cudaFree(lane->ids);
+	cudaFree(lane->dist);
+	cudaFree(lane->id);
+	cudaFree(lane->count);
+	cudaFree(lane->counts);
+	cudaFreeHost(lane->hostDist);
+	cudaFreeHost(lane->hostId);
+	memset(lane, 0, sizeof(*lane));
 }
 
 int
@@ -411,6 +440,76 @@ AnnB200IndexCreate(int device, uint32_t dims, uint64_t rows, const float *vector
 	return ANN_OK;
 }
 
+/*
+ * An index whose FP32 rows are row-sharded over several devices, as the
+ * reference spreads an index's shards over its GPUs (placement
+ * ann/server/cuvs.c:2845-2862): part p holds an equal share of the rows
+ * (global ordinals as its ids) on devices[p], and one NCCL rank a part
+ * (AnnB200CommCreateAll) joins the parts' lists in AnnB200IndexSearch.
+ * ndev == 1 is AnnB200IndexCreate on that device.
+ */
+int
+AnnB200IndexCreateSharded(int ndev, const int *devices, uint32_t dims, uint64_t rows, const float *vectors,
+						  AnnB200Index **out)
+{
+	AnnB200Index *ix;
+	int			prev = 0;
+	int			status = ANN_OK;
+
+	if (out == NULL)
+		return ANN_INVALID;
+	*out = NULL;
+	if (ndev < 1 || devices == NULL || dims == 0 || rows == 0 || vectors == NULL || (uint64_t) ndev > rows)
+		return ANN_INVALID;
+	if (ndev == 1)
+		return AnnB200IndexCreate(devices[0], dims, rows, vectors, out);
+	for (int i = 0; i < ndev; i++)
+		if (devices[i] < 0 || devices[i] >= AnnB200DeviceCount() || devices[i] >= INDEX_MAX_DEVICES)
+			return ANN_INVALID;
+	ix = calloc(1, sizeof(*ix));
+	if (ix == NULL)
+		return ANN_NOMEM;
+	ix->device = devices[0];
+	ix->dims = dims;
+	ix->rows = rows;
+	ix->nparts = (uint32_t) ndev;
+	pthread_mutex_init(&ix->searchLock, NULL);
+	ix->parts = calloc(ndev, sizeof(*ix->parts));
+	ix->partBounds = calloc(ndev + 1, sizeof(*ix->partBounds));
+	ix->partDevices = calloc(ndev, sizeof(*ix->partDevices));
+	ix->comms = calloc(ndev, sizeof(*ix->comms));
+	ix->partLanes = calloc(ndev, sizeof(*ix->partLanes));
+	if (!ix->parts || !ix->partBounds || !ix->partDevices || !ix->comms || !ix->partLanes)
+	{
+		AnnB200IndexDestroy(ix);
+		return ANN_NOMEM;
+	}
+	for (int p = 0; p < ndev; p++)
+	{
+		ix->partDevices[p] = devices[p];
+		ix->partBounds[p + 1] = rows * (uint64_t) (p + 1) / (uint64_t) ndev;
+	}
+	cudaGetDevice(&prev);
+	for (int p = 0; status == ANN_OK && p < ndev; p++)
+	{
+		uint64_t	lo = ix->partBounds[p];
+
+		status = AnnB200ShardCreate(devices[p], ANNB200_F32, dims, ix->partBounds[p + 1] - lo,
+									vectors + lo * dims, NULL, NULL, (int64_t) lo, ANNB200_SHARD_HOST, NULL,
+									&ix->parts[p]);
+	}
+	if (status == ANN_OK)
+		status = AnnB200CommCreateAll(ndev, devices, ix->comms);
+	cudaSetDevice(prev);
+	if (status != ANN_OK)
+	{
+		AnnB200IndexDestroy(ix);
+		return status;
+	}
+	*out = ix;
+	return ANN_OK;
+}
+
 void
 AnnB200IndexDestroy(AnnB200Index *ix)
 {
@@ -419,6 +518,22 @@ AnnB200IndexDestroy(AnnB200Index *ix)
 	AnnB200ShardDestroy(ix->shard);
 	for (uint32_t s = 0; ix->shards && s < ix->nshards; s++)
 		AnnB200ShardDestroy(ix->shards[s]);
+	for (uint32_t p = 0; p < ix->nparts; p++)
+	{
+		if (ix->parts)
+			AnnB200ShardDestroy(ix->parts[p]);
+		if (ix->comms)
+			AnnB200CommDestroy(ix->comms[p]);
+		if (ix->partLanes)
+			LaneRelease(&ix->partLanes[p]);
+	}
+	if (ix->nparts)
+		pthread_mutex_destroy(&ix->searchLock);
+	free(ix->parts);
+	free(ix->partBounds);
+	free(ix->partDevices);
+	free(ix->comms);
+	free(ix->partLanes);
 	if (ix->registered)
 	{
 		int			prev = 0;
@@ -1030,6 +1145,166 @@ done:
 	return status;
 }
 
+/* One part's share of a search on a row-sharded index. */
+typedef struct PartTask
+{
+	AnnB200Index *ix;
+	uint32_t	p;
+	const float *queries;
+	uint32_t	nq;
+	const uint64_t *ordinals;	/* the whole list (NULL: every row) */
+	uint64_t	start;			/* this part's slice of it */
+	uint64_t	n;
+	uint32_t	k;
+	int			status;
+} PartTask;
+
+/*
+ * Part p: its queries and eligible rows to its device, then its rank of
+ * the sharded search (AnnB200SearchSharded: local search, all-gather of
+ * the parts' lists, device merge). A part whose staging fails still joins
+ * the exchange (with NULL buffers, which it reports as its status), so
+ * the other parts never wait for it.
+ */
+static void *
+PartSearch(void *arg)
+{
+	PartTask   *t = arg;
+	AnnB200Index *ix = t->ix;
+	Lane	   *lane = &ix->partLanes[t->p];
+	size_t		values = (size_t) t->nq * ix->dims;
+	size_t		results = (size_t) t->nq * t->k;
+	int			ok;
+
+	cudaSetDevice(ix->partDevices[t->p]);
+	if (!lane->ready)
+	{
+		lane->device = ix->partDevices[t->p];
+		if (cudaStreamCreateWithFlags(&lane->stream, cudaStreamNonBlocking) != cudaSuccess)
+		{
+			t->status = ANN_BACKEND_ERROR;
+			return NULL;		/* no stream: cannot even join; the others time out */
+		}
+		lane->ready = 1;
+	}
+	ok = Grow((void **) &lane->query, &lane->queryBytes, values * sizeof(float)) &&
+		Grow((void **) &lane->ids, &lane->idsBytes, (t->n ? t->n : 1) * sizeof(uint32_t)) &&
+		LaneResults(lane, results) &&
+		Grow((void **) &lane->counts, &lane->countsBytes, t->nq * sizeof(uint32_t));
+	if (ok && cudaMemcpyAsync(lane->query, t->queries, values * sizeof(float), cudaMemcpyHostToDevice,
+							  lane->stream) != cudaSuccess)
+		ok = 0;
+	if (ok && t->ordinals && t->n)
+	{
+		uint32_t   *rows = malloc(sizeof(*rows) * t->n);
+		uint64_t	lo = ix->partBounds[t->p];
+
+		if (rows == NULL)
+			ok = 0;
+		for (uint64_t i = 0; ok && i < t->n; i++)
+			rows[i] = (uint32_t) (t->ordinals[t->start + i] - lo);
+		if (ok && (cudaMemcpyAsync(lane->ids, rows, t->n * sizeof(uint32_t), cudaMemcpyHostToDevice,
+								   lane->stream) != cudaSuccess ||
+				   cudaStreamSynchronize(lane->stream) != cudaSuccess))
+			ok = 0;
+		free(rows);
+	}
+	t->status = AnnB200SearchSharded(ix->parts[t->p], ix->comms[t->p], ok ? lane->query : NULL, t->nq,
+									 t->ordinals ? lane->ids : NULL, t->ordinals ? t->n : 0, t->k, ANNB200_L2,
+									 ANNB200_INDEX_L2, t->k, ok ? lane->dist : NULL, lane->id, lane->counts, NULL,
+									 lane->stream);
+	if (!ok && t->status == ANN_OK)
+		t->status = ANN_NOMEM;
+	return NULL;
+}
+
+/* AnnB200IndexSearch on a row-sharded index: every part at once, one thread a part. */
+static int
+PartedSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const uint64_t *ordinals, uint64_t nordinals,
+			 uint32_t k, float *out_dist, uint64_t *out_ordinal, uint32_t *out_count)
+{
+	uint32_t	P = ix->nparts;
+	PartTask   *task = calloc(P, sizeof(*task));
+	pthread_t  *tid = calloc(P, sizeof(*tid));
+	char	   *started = calloc(P, 1);
+	uint32_t   *counts = malloc(sizeof(*counts) * nq);
+	size_t		results = (size_t) nq * k;
+	int			status = ANN_OK;
+	int			prev = 0;
+
+	if (!task || !tid || !started || !counts)
+	{
+		free(task);
+		free(tid);
+		free(started);
+		free(counts);
+		return ANN_NOMEM;
+	}
+	cudaGetDevice(&prev);
+	pthread_mutex_lock(&ix->searchLock);
+	for (uint32_t p = 0; p < P; p++)
+	{
+		task[p] = (PartTask) {ix, p, queries, nq, ordinals, 0, 0, k, ANN_OK};
+		if (ordinals)
+			Slice(ordinals, nordinals, ix->partBounds[p], ix->partBounds[p + 1], &task[p].start, &task[p].n);
+	}
+	/* every part must enter the exchange: a part without a thread runs here, after the others started */
+	for (uint32_t p = 1; p < P; p++)
+		started[p] = pthread_create(&tid[p], NULL, PartSearch, &task[p]) == 0;
+	if (P > 1)
+	{
+		uint32_t	missing = 0;
+
+		for (uint32_t p = 1; p < P; p++)
+			missing += !started[p];
+		if (missing)
+		{
+			/* cannot run the parts together: abort the group rather than wait */
+			for (uint32_t p = 0; p < P; p++)
+				AnnB200CommAbort(ix->comms[p]);
+		}
+	}
+	PartSearch(&task[0]);
+	for (uint32_t p = 1; p < P; p++)
+		if (started[p])
+			pthread_join(tid[p], NULL);
+	for (uint32_t p = 0; p < P; p++)
+		if (task[p].status != ANN_OK && status == ANN_OK)
+			status = task[p].status;
+	if (status == ANN_OK)
+	{
+		Lane	   *lane = &ix->partLanes[0];
+
+		cudaSetDevice(ix->partDevices[0]);
+		if (cudaMemcpyAsync(counts, lane->counts, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+							lane->stream) != cudaSuccess ||
+			cudaMemcpyAsync(lane->hostDist, lane->dist, results * sizeof(double), cudaMemcpyDeviceToHost,
+							lane->stream) != cudaSuccess ||
+			cudaMemcpyAsync(lane->hostId, lane->id, results * sizeof(int64_t), cudaMemcpyDeviceToHost,
+							lane->stream) != cudaSuccess ||
+			cudaStreamSynchronize(lane->stream) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+		for (uint32_t q = 0; status == ANN_OK && q < nq; q++)
+		{
+			out_count[q] = counts[q];
+			for (uint32_t i = 0; i < counts[q]; i++)
+			{
+				out_dist[(size_t) q * k + i] = (float) lane->hostDist[(size_t) q * k + i];
+				out_ordinal[(size_t) q * k + i] = (uint64_t) lane->hostId[(size_t) q * k + i];
+			}
+		}
+	}
+	pthread_mutex_unlock(&ix->searchLock);
+	cudaSetDevice(prev);
+	free(task);
+	free(tid);
+	free(started);
+	free(counts);
+	if (status == ANN_OK)
+		atomic_fetch_add(&DeviceJobs, 1);
+	return status;
+}
+
 int
 AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const uint64_t *ordinals,
 				   uint64_t nordinals, uint32_t k, float *out_dist, uint64_t *out_ordinal, uint32_t *out_count)
@@ -1059,6 +1334,8 @@ AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const ui
 		return ANN_OK;
 	if (InjectLost())
 		return ANN_BACKEND_ERROR;
+	if (ix->nparts > 1)
+		return PartedSearch(ix, queries, nq, ordinals, nordinals, k, out_dist, out_ordinal, out_count);
 	results = (size_t) nq * k;
 	cudaGetDevice(&prev);
 	lane = LaneOn(ix->device);
@@ -1129,6 +1406,248 @@ AnnB200IndexSearch(AnnB200Index *ix, const float *queries, uint32_t nq, const ui
 	free(counts);
 	cudaSetDevice(prev);
 	return status;
+}
+
+/*
+ * The eligible rows of per-shard bitsets as sorted global ordinals, on the
+ * host (the forms whose search takes ordinals: a row-sharded index and one
+ * served from its quantized copy). Returns the count, or -1 without memory.
+ */
+static int64_t
+BitsetOrdinals(uint32_t nshards, const uint32_t *const *bitsets, const uint64_t *first, const uint64_t *rows,
+			   uint64_t **out)
+{
+	uint64_t	total = 0,
+				n = 0;
+
+	for (uint32_t s = 0; s < nshards; s++)
+		total += rows[s];
+	*out = malloc(sizeof(uint64_t) * (total ? total : 1));
+	if (*out == NULL)
+		return -1;
+	for (uint32_t s = 0; s < nshards; s++)
+		for (uint64_t w = 0; bitsets[s] && w < (rows[s] + 31) / 32; w++)
+		{
+			uint32_t	x = bitsets[s][w];
+
+			if ((w + 1) * 32 > rows[s])
+				x &= (uint32_t) ((1ull << (rows[s] - w * 32)) - 1);
+			while (x)
+			{
+				(*out)[n++] = first[s] + w * 32 + (uint64_t) __builtin_ctz(x);
+				x &= x - 1;
+			}
+		}
+	return (int64_t) n;
+}
+
+/*
+ * A loaded-index search whose eligible rows come as per-shard bitsets (the
+ * cached filter forms the reference's server hands its backends:
+ * AnnIndexJob.bitsets / deviceBitsets, ann/server/backend.h:85-96). On an
+ * index with its FP32 rows on one device the bitsets are expanded there
+ * (AnnB200BitmapRowsFrom: shard s's set bits become global row numbers
+ * first[s] + bit) and searched like an ordinal list; other indexes take
+ * the same rows as ordinals.
+ */
+int
+AnnB200IndexSearchBitsets(AnnB200Index *ix, const float *queries, uint32_t nq, uint32_t nshards,
+						  const uint32_t *const *bitsets, const uint64_t *shard_first, const uint64_t *shard_rows,
+						  uint32_t flags, uint32_t k, float *out_dist, uint64_t *out_ordinal, uint32_t *out_count)
+{
+	Lane	   *lane;
+	uint32_t   *counts = NULL;
+	size_t		values,
+				results;
+	uint64_t	total = 0,
+				maxWords = 0,
+				n = 0;
+	int			prev = 0;
+	int			status = ANN_OK;
+	int			onDevice = (flags & ANNB200_BITSETS_DEVICE) != 0;
+
+	if (ix == NULL || (nq && (queries == NULL || out_count == NULL)) || (nshards && (bitsets == NULL ||
+																		   shard_first == NULL ||
+																		   shard_rows == NULL)))
+		return ANN_INVALID;
+	if (nq == 0)
+		return ANN_OK;
+	if (k && (out_dist == NULL || out_ordinal == NULL))
+		return ANN_INVALID;
+	for (uint32_t s = 0; s < nshards; s++)
+	{
+		if (shard_first[s] + shard_rows[s] > ix->rows || (s && shard_first[s] < shard_first[s - 1] + shard_rows[s - 1]))
+			return ANN_INVALID;
+		total += shard_rows[s];
+		if ((shard_rows[s] + 31) / 32 > maxWords)
+			maxWords = (shard_rows[s] + 31) / 32;
+	}
+	values = (size_t) nq * ix->dims;
+	if (!AllFinite(queries, values))
+		return ANN_INVALID;
+	if (ix->shard == NULL || ix->nparts > 1)
+	{
+		uint64_t   *ords = NULL;
+		int64_t		m;
+
+		if (onDevice)
+			return ANN_UNSUPPORTED;
+		m = BitsetOrdinals(nshards, bitsets, shard_first, shard_rows, &ords);
+		if (m < 0)
+			return ANN_NOMEM;
+		status = AnnB200IndexSearch(ix, queries, nq, ords, (uint64_t) m, k, out_dist, out_ordinal, out_count);
+		free(ords);
+		return status;
+	}
+	memset(out_count, 0, sizeof(*out_count) * nq);
+	if (k == 0 || total == 0)
+		return ANN_OK;
+	if (InjectLost())
+		return ANN_BACKEND_ERROR;
+	results = (size_t) nq * k;
+	cudaGetDevice(&prev);
+	lane = LaneOn(ix->device);
+	if (lane == NULL)
+	{
+		cudaSetDevice(prev);
+		return ANN_BACKEND_ERROR;
+	}
+	counts = malloc(sizeof(*counts) * nq);
+	if (counts == NULL ||
+		!Grow((void **) &lane->query, &lane->queryBytes, values * sizeof(float)) ||
+		!Grow((void **) &lane->ids, &lane->idsBytes, total * sizeof(uint32_t)) ||
+		(!onDevice && !Grow((void **) &lane->rows, &lane->rowsBytes, maxWords * sizeof(uint32_t))) ||
+		!LaneResults(lane, results) ||
+		!Grow((void **) &lane->counts, &lane->countsBytes, nq * sizeof(uint32_t)))
+		status = ANN_NOMEM;
+	if (status == ANN_OK &&
+		cudaMemcpyAsync(lane->query, queries, values * sizeof(float), cudaMemcpyHostToDevice, lane->stream) !=
+		cudaSuccess)
+		status = ANN_BACKEND_ERROR;
+	for (uint32_t s = 0; status == ANN_OK && s < nshards; s++)
+	{
+		const uint32_t *words = bitsets[s];
+		uint64_t	found = 0;
+
+		if (words == NULL || shard_rows[s] == 0)
+			continue;
+		if (!onDevice)
+		{
+			if (cudaMemcpyAsync(lane->rows, words, (shard_rows[s] + 31) / 32 * sizeof(uint32_t),
+								cudaMemcpyHostToDevice, lane->stream) != cudaSuccess)
+			{
+				status = ANN_BACKEND_ERROR;
+				break;
+			}
+			words = lane->rows;
+		}
+		status = AnnB200BitmapRowsFrom(words, shard_rows[s], (uint32_t) shard_first[s], lane->ids + n, &found,
+									   lane->stream);
+		n += found;
+	}
+	if (status == ANN_OK && n)
+		status = AnnB200Search(ix->shard, lane->query, nq, lane->ids, n, k, ANNB200_L2, ANNB200_INDEX_L2, k,
+							   lane->dist, lane->id, lane->counts, NULL, lane->stream);
+	if (status == ANN_OK && n &&
+		(cudaMemcpyAsync(counts, lane->counts, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostDist, lane->dist, results * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, results * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK && n)
+	{
+		for (uint32_t q = 0; q < nq; q++)
+		{
+			out_count[q] = counts[q];
+			for (uint32_t i = 0; i < counts[q]; i++)
+			{
+				out_dist[(size_t) q * k + i] = (float) lane->hostDist[(size_t) q * k + i];
+				out_ordinal[(size_t) q * k + i] = (uint64_t) lane->hostId[(size_t) q * k + i];
+			}
+		}
+	}
+	if (status == ANN_OK)
+		atomic_fetch_add(&DeviceJobs, 1);
+	free(counts);
+	cudaSetDevice(prev);
+	return status;
+}
+
+/*
+ * Copy per-shard bitsets to the device of an index's FP32 rows, for
+ * AnnB200IndexSearchBitsets with ANNB200_BITSETS_DEVICE: device[s] receives
+ * shard s's copy (NULL for a NULL bitset). On failure nothing stays
+ * allocated.
+ */
+int
+AnnB200IndexKeepBitsets(AnnB200Index *ix, uint32_t nshards, const uint32_t *const *bitsets,
+						const uint64_t *shard_rows, void **device)
+{
+	int			prev = 0;
+	int			status = ANN_OK;
+
+	if (ix == NULL || device == NULL || (nshards && (bitsets == NULL || shard_rows == NULL)))
+		return ANN_INVALID;
+	if (AnnB200IndexDevice(ix) < 0)
+		return ANN_UNSUPPORTED;
+	cudaGetDevice(&prev);
+	cudaSetDevice(ix->device);
+	for (uint32_t s = 0; s < nshards; s++)
+		device[s] = NULL;
+	for (uint32_t s = 0; status == ANN_OK && s < nshards; s++)
+	{
+		size_t		bytes = (shard_rows[s] + 31) / 32 * sizeof(uint32_t);
+
+		if (bitsets[s] == NULL || bytes == 0)
+			continue;
+		if (cudaMalloc(&device[s], bytes) != cudaSuccess)
+		{
+			device[s] = NULL;
+			status = ANN_NOMEM;
+		}
+		else if (cudaMemcpy(device[s], bitsets[s], bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+	}
+	if (status != ANN_OK)
+	{
+		(void) cudaGetLastError();
+		AnnB200IndexDropBitsets(ix, nshards, device);
+	}
+	cudaSetDevice(prev);
+	return status;
+}
+
+/* Free what AnnB200IndexKeepBitsets kept. */
+void
+AnnB200IndexDropBitsets(AnnB200Index *ix, uint32_t nshards, void **device)
+{
+	int			prev = 0;
+
+	if (ix == NULL || device == NULL)
+		return;
+	cudaGetDevice(&prev);
+	cudaSetDevice(ix->device);
+	for (uint32_t s = 0; s < nshards; s++)
+	{
+		if (device[s])
+			cudaFree(device[s]);
+		device[s] = NULL;
+	}
+	cudaSetDevice(prev);
+}
+
+/*
+ * The device an index's FP32 rows live on, or -1 for an index that keeps
+ * them elsewhere (a row-sharded index, one served from its quantized copy):
+ * where a cached filter's bitsets may be kept for AnnB200IndexSearchBitsets.
+ */
+int
+AnnB200IndexDevice(const AnnB200Index *ix)
+{
+	return ix != NULL && ix->shard != NULL && ix->nparts <= 1 ? ix->device : -1;
 }
 
 /* Bytes a row takes in a storage format. */

@@ -36,6 +36,8 @@ struct Nccl {
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
   ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
   const char *(*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -63,12 +65,19 @@ const Nccl &nccl() {
     x.ok = sym(h, "ncclGetUniqueId", &x.GetUniqueId) && sym(h, "ncclCommInitRank", &x.CommInitRank) &&
            sym(h, "ncclCommInitAll", &x.CommInitAll) && sym(h, "ncclCommDestroy", &x.CommDestroy) &&
            sym(h, "ncclCommAbort", &x.CommAbort) && sym(h, "ncclCommGetAsyncError", &x.CommGetAsyncError) &&
-           sym(h, "ncclAllGather", &x.AllGather) && sym(h, "ncclGetErrorString", &x.GetErrorString);
+           sym(h, "ncclAllGather", &x.AllGather) && sym(h, "ncclGroupStart", &x.GroupStart) &&
+           sym(h, "ncclGroupEnd", &x.GroupEnd) && sym(h, "ncclGetErrorString", &x.GetErrorString);
     if (!x.ok) x.why = "libnccl.so.2 lacks an entry point this library calls";
     return x;
   }();
   return n;
 }
+
+// Connections between the ranks are made while the group is created, all
+// ranks present: NCCL otherwise makes them at a collective's first use,
+// inside the host call, where a rank whose peers never arrive would wait
+// for ever before any time limit could act. (Unless the caller chose.)
+void eager_connect() { setenv("NCCL_RUNTIME_CONNECT", "0", 0); }
 
 int nccl_fail(ncclResult_t r, const char *what) {
   return annb200::report_error(BACKEND_ERROR, "%s: %s", what, nccl().GetErrorString ? nccl().GetErrorString(r) : "");
@@ -117,6 +126,48 @@ AnnB200Comm *make_comm(int device, int rank, int nranks, ncclComm_t c) {
   return x;
 }
 
+// One small all-gather on every new rank while the whole group is there:
+// its connections are made and proven before any search relies on them.
+int warm_up(AnnB200Comm **comms, int n) {
+  cudaStream_t st[64] = {};
+  void *buf[64] = {};
+  int status = OK;
+  ncclResult_t r = ncclSuccess;
+  for (int i = 0; i < n && status == OK; i++) {
+    DevGuard g(comms[i]->device);
+    if (cudaStreamCreateWithFlags(&st[i], cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&buf[i], 16 * (size_t)(comms[i]->nranks + 1)) != cudaSuccess) {
+      cudaGetLastError();
+      status = annb200::report_error(NOMEM, "communicator warm-up buffers");
+    }
+  }
+  if (status == OK) {
+    if (n > 1) nccl().GroupStart();
+    for (int i = 0; i < n && r == ncclSuccess; i++) {
+      DevGuard g(comms[i]->device);
+      r = nccl().AllGather(buf[i], (uint8_t *)buf[i] + 16, 16, ncclUint8, comms[i]->nccl, st[i]);
+    }
+    if (n > 1) {
+      ncclResult_t e = nccl().GroupEnd();
+      if (r == ncclSuccess) r = e;
+    }
+    if (r != ncclSuccess) status = nccl_fail(r, "communicator warm-up");
+  }
+  for (int i = 0; i < n && status == OK; i++) {
+    DevGuard g(comms[i]->device);
+    status = annb200::comm_wait(comms[i], st[i]);
+  }
+  for (int i = 0; i < n; i++) {
+    DevGuard g(comms[i]->device);
+    if (st[i]) {
+      cudaStreamSynchronize(st[i]);
+      cudaStreamDestroy(st[i]);
+    }
+    if (buf[i]) cudaFree(buf[i]);
+  }
+  return status;
+}
+
 }  // namespace
 
 extern "C" int AnnB200CommId(void *id) {
@@ -139,13 +190,21 @@ extern "C" int AnnB200CommCreate(int device, int nranks, int rank, const void *i
   ncclUniqueId u;
   memcpy(&u, id, sizeof(u));
   ncclComm_t c = nullptr;
+  eager_connect();
   ncclResult_t r = nccl().CommInitRank(&c, nranks, u, rank);
   if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
-  *out = make_comm(device, rank, nranks, c);
-  if (!*out) {
-    nccl().CommDestroy(c);
+  AnnB200Comm *x = make_comm(device, rank, nranks, c);
+  if (!x) {
+    nccl().CommAbort(c);
     return annb200::report_error(NOMEM, "communicator");
   }
+  int status = warm_up(&x, 1);
+  if (status != OK) {
+    x->broken = true;
+    AnnB200CommDestroy(x);
+    return status;
+  }
+  *out = x;
   return OK;
 }
 
@@ -163,6 +222,7 @@ extern "C" int AnnB200CommCreateAll(int ndev, const int *devices, AnnB200Comm **
   if (!c) return annb200::report_error(NOMEM, "communicators");
   int prev = 0;
   cudaGetDevice(&prev);
+  eager_connect();
   ncclResult_t r = nccl().CommInitAll(c, ndev, devices);
   cudaSetDevice(prev);
   if (r != ncclSuccess) {
@@ -186,6 +246,15 @@ extern "C" int AnnB200CommCreateAll(int ndev, const int *devices, AnnB200Comm **
     return annb200::report_error(NOMEM, "communicator");
   }
   delete[] c;
+  status = ndev <= 64 ? warm_up(out, ndev) : OK;
+  if (status != OK) {
+    for (int i = 0; i < ndev; i++) {
+      if (out[i]) out[i]->broken = true;
+      AnnB200CommDestroy(out[i]);
+      out[i] = nullptr;
+    }
+    return status;
+  }
   return OK;
 }
 

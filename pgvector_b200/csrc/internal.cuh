@@ -425,6 +425,7 @@ cudaError_t launch_merge_ranked(const void *dist, uint64_t dist_stride, const vo
 uint32_t bitmap_blocks(uint64_t nbits);
 void launch_v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, const QueryState &qs, cudaStream_t st);
 void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,
-                        unsigned long long *total, cudaStream_t st);
+                        unsigned long long *total, cudaStream_t st,
+                        uint32_t base = 0);
 
 }  // namespace annb200

@@ -1216,7 +1216,7 @@ __global__ void bitmap_scan(uint32_t *blockcnt, uint32_t nblocks, unsigned long 
 }
 
 __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nbits, const uint32_t *blockoff,
-                             uint32_t *rows) {
+                             uint32_t *rows, uint32_t base) {
   __shared__ uint32_t scratch[32];
   uint64_t w = (uint64_t)blockIdx.x * BM_WORDS + threadIdx.x;
   uint32_t x = 0;
@@ -1230,7 +1230,7 @@ __global__ void bitmap_write(const uint32_t *words, uint64_t nwords, uint64_t nb
   uint32_t o = blockoff[blockIdx.x] + before;
   while (x) {
     uint32_t b = __ffs(x) - 1;
-    rows[o++] = (uint32_t)(w * 32 + b);
+    rows[o++] = base + (uint32_t)(w * 32 + b);
     x &= x - 1;
   }
 }
@@ -1444,13 +1444,13 @@ uint32_t bitmap_blocks(uint64_t nbits) {
 }
 
 void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,
-                        unsigned long long *total, cudaStream_t st) {
+                        unsigned long long *total, cudaStream_t st, uint32_t base) {
   uint64_t nwords = (nbits + 31) / 32;
   uint32_t nb = bitmap_blocks(nbits);
   if (nb == 0) return;
   bitmap_count<<<nb, BM_WORDS, 0, st>>>(words, nwords, nbits, blockcnt);
   bitmap_scan<<<1, 1024, 0, st>>>(blockcnt, nb, total);
-  bitmap_write<<<nb, BM_WORDS, 0, st>>>(words, nwords, nbits, blockcnt, rows);
+  bitmap_write<<<nb, BM_WORDS, 0, st>>>(words, nwords, nbits, blockcnt, rows, base);
 }
 
 }  // namespace annb200

@@ -1422,21 +1422,23 @@ extern "C" int AnnB200RescoreGather(const float *queries, uint32_t nq, uint32_t 
   return OK;
 }
 
-extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint64_t *count,
-                                 void *stream) {
+namespace {
+
+int bitmap_rows_at(const uint32_t *words, uint64_t nbits, uint32_t base, uint32_t *rows, uint64_t *count,
+                   cudaStream_t st) {
   if (!count) return fail(INVALID, "count pointer is NULL");
   *count = 0;
   if (nbits == 0) return OK;
   if (!words || !rows) return fail(INVALID, "NULL pointer");
-  if (nbits > 0xffffffffull) return fail(INVALID, "bitmap longer than 2^32 rows");
-  cudaStream_t st = (cudaStream_t)stream;
+  if (nbits > 0xffffffffull || (uint64_t)base + nbits > 0x100000000ull)
+    return fail(INVALID, "row numbers past 2^32");
   static thread_local DeviceBuffer scratch;
   const uint32_t nb = bitmap_blocks(nbits);
   CK(scratch.reserve(align256((size_t)nb * 4) + 8), "bitmap scratch");
   unsigned long long *total = (unsigned long long *)((uint8_t *)scratch.p + align256((size_t)nb * 4));
   StageClock clock(st);
   int h = clock.begin(ST_BITMAP);
-  launch_bitmap_rows(words, nbits, rows, (uint32_t *)scratch.p, total, st);
+  launch_bitmap_rows(words, nbits, rows, (uint32_t *)scratch.p, total, st, base);
   clock.end(h);
   counted(3);
   CK(cudaGetLastError(), "bitmap rows");
@@ -1445,6 +1447,18 @@ extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t
   CK(cudaStreamSynchronize(st), "bitmap rows");
   *count = found;
   return OK;
+}
+
+}  // namespace
+
+extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint64_t *count,
+                                 void *stream) {
+  return bitmap_rows_at(words, nbits, 0, rows, count, (cudaStream_t)stream);
+}
+
+extern "C" int AnnB200BitmapRowsFrom(const uint32_t *words, uint64_t nbits, uint32_t first_row, uint32_t *rows,
+                                     uint64_t *count, void *stream) {
+  return bitmap_rows_at(words, nbits, first_row, rows, count, (cudaStream_t)stream);
 }
 
 extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(); }

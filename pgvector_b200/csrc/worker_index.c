@@ -13,7 +13,11 @@
  *
  *   load_index     registers the directory like the cpu backend and copies
  *                  its FP32 rows (vectors.f32) to a GPU (AnnB200IndexCreate,
- *                  round robin over the devices); where they do not fit and
+ *                  round robin over the devices), or row-shards them over
+ *                  several GPUs (AnnB200IndexCreateSharded: one GPU's share
+ *                  each, lists joined by an NCCL all-gather and a device
+ *                  merge) when ANN_B200_INDEX_DEVICES asks for it or one
+ *                  GPU cannot hold them; where no GPU set holds them and
  *                  the directory has a quantized copy, that copy instead
  *                  (AnnB200IndexCreateQuant: the reference's quantized scan
  *                  route, file->quantActive set as the reference's backend
@@ -24,10 +28,12 @@
  *                  resolve the index (ANN_STALE if not loaded, ANN_INVALID on
  *                  a dimension mismatch), map a key filter to ordinals
  *                  (AnnIndexOrdinals, unless the server passed them), and run
- *                  the exact scan on the device. Unfiltered jobs on one index
- *                  run as one batch (the tensor-core scan applies from 16
- *                  queries); filtered jobs run one at a time over their
- *                  ordinals. Hits carry the key of their ordinal and the
+ *                  the exact scan on the device. Jobs on one index with the
+ *                  same filter arrays (or none) run as one batch (the
+ *                  tensor-core scan applies from 16 queries), over the
+ *                  cheapest filter form they carry: bitsets kept on the
+ *                  device, host bitsets expanded there, ordinals, or keys
+ *                  mapped to ordinals. Hits carry the key of their ordinal and the
  *                  reference's FP32 distance; route is set as the cpu backend
  *                  sets it (cpu.c:394), or as the quantized scan route sets
  *                  it (ANN_ROUTE_EXACT, cuvs.c:4927).
@@ -72,9 +78,43 @@ CreateQuant(const AnnIndexFile *file, AnnB200Index **index)
 }
 
 /*
+ * The FP32 rows on the devices: row-sharded over ANN_B200_INDEX_DEVICES
+ * devices when that is set above 1 (the reference spreads an index's shards
+ * over its GPUs, ann/server/cuvs.c:2845-2862); else on one device (round
+ * robin), and where they do not fit one device, over every visible device.
+ */
+static AnnStatus
+CreateRows(AnnIndexFile *file, AnnB200Index **index)
+{
+	const char *env = getenv("ANN_B200_INDEX_DEVICES");
+	int			devices = AnnB200DeviceCount();
+	int			want = env && *env ? atoi(env) : 1;
+	int			list[64];
+	AnnStatus	status;
+
+	if (want > devices)
+		want = devices;
+	if (want > 64)
+		want = 64;
+	if (want <= 1)
+	{
+		status = (AnnStatus) AnnB200IndexCreate(-1, file->dimensions, file->rows, file->vectors, index);
+		if (status != ANN_NOMEM || devices <= 1 || (env && *env))
+			return status;
+		want = devices < 64 ? devices : 64;
+	}
+	if ((uint64_t) want > file->rows)
+		want = (int) file->rows;
+	for (int d = 0; d < want; d++)
+		list[d] = d;
+	return (AnnStatus) AnnB200IndexCreateSharded(want, list, file->dimensions, file->rows, file->vectors, index);
+}
+
+/*
  * Which copy a loaded index searches on the device: its FP32 rows (exact)
- * where they fit, else its quantized copy when it has one and quantized
- * scans are on. ANN_B200_INDEX_COPY=fp32 or =quant chooses instead.
+ * where they fit (CreateRows), else its quantized copy when it has one and
+ * quantized scans are on. ANN_B200_INDEX_COPY=fp32 or =quant chooses
+ * instead.
  */
 static AnnStatus
 CreateDevice(AnnIndexFile *file, AnnB200Index **index)
@@ -88,7 +128,7 @@ CreateDevice(AnnIndexFile *file, AnnB200Index **index)
 		status = CreateQuant(file, index);
 	else
 	{
-		status = (AnnStatus) AnnB200IndexCreate(-1, file->dimensions, file->rows, file->vectors, index);
+		status = CreateRows(file, index);
 		if (status != ANN_NOMEM || !quant || (copy && strcmp(copy, "fp32") == 0))
 			return status;
 		status = CreateQuant(file, index);
@@ -143,20 +183,76 @@ Finish(AnnIndexJob *job, const AnnIndexFile *file, const float *dist, const uint
 }
 
 /*
- * Whether job i joins the batch of job `first`: unfiltered, on the same
- * index, and, on an index served from its quantized copy, with the same k
- * (the number of candidates each query re-scores follows from its own k).
+ * Whether job i joins the group of job `first`: one search of the group's
+ * queries at the largest k. Unfiltered jobs on one index group together;
+ * filtered jobs group when they share the same filter arrays -- the test
+ * the server uses for identical searches (SameSearch, ann/server/server.c:
+ * 1216-1225), and the lane batches same-filter jobs for one gather
+ * (ann/server/server.c:1311-1545; SearchGatherGroup, ann/server/cuvs.c:5407).
+ * On an index served from its quantized copy the group also needs one k
+ * (the candidates each query re-scores follow from its own k).
  */
 static int
-SameBatch(AnnIndexJob *jobs, AnnIndexFile **files, const char *done, uint32_t first, uint32_t i)
+SameGroup(AnnIndexJob *jobs, AnnIndexFile **files, const char *done, uint32_t first, uint32_t i)
 {
-	return files[i] == files[first] && !jobs[i].filtered && !done[i] &&
-		(!files[first]->quantActive || jobs[i].k == jobs[first].k);
+	const AnnIndexJob *a = &jobs[first],
+			   *b = &jobs[i];
+
+	if (done[i] || files[i] != files[first] || a->filtered != b->filtered)
+		return 0;
+	if (files[first]->quantActive && a->k != b->k)
+		return 0;
+	if (!a->filtered)
+		return 1;
+	return a->filter == b->filter && a->nfilter == b->nfilter && a->ordinals == b->ordinals &&
+		a->bitsets == b->bitsets && a->deviceBitsets == b->deviceBitsets && a->deviceRows == b->deviceRows;
 }
 
-/* Unfiltered jobs [first..] on `file`: one batch of queries, k = the largest. */
+/*
+ * The group's eligible rows into the search, in the cheapest form the job
+ * carries: bitsets kept on the device (nothing crosses), host bitsets (one
+ * bit a row crosses, expanded on the device), ordinals, or the filter's keys
+ * mapped to ordinals (AnnIndexOrdinals, as the cpu backend does).
+ */
+static int
+GroupSearch(AnnIndexFile *file, const AnnIndexJob *job, const float *queries, uint32_t n, uint32_t k, float *dist,
+			uint64_t *ordinal, uint32_t *counts)
+{
+	AnnB200Index *ix = (AnnB200Index *) file->device;
+	int			onDevice = AnnB200IndexDevice(ix) >= 0;
+	uint64_t	first[ANN_INDEX_MAX_SHARDS],
+				rows[ANN_INDEX_MAX_SHARDS];
+	uint64_t   *owned = NULL;
+	uint64_t	nords = job->nfilter;
+	int			status;
+
+	if (!job->filtered)
+		return AnnB200IndexSearch(ix, queries, n, NULL, 0, k, dist, ordinal, counts);
+	for (uint32_t s = 0; s < file->nshards; s++)
+	{
+		first[s] = file->shards[s].first;
+		rows[s] = file->shards[s].rows;
+	}
+	if (job->deviceBitsets && onDevice && file->nshards)
+		return AnnB200IndexSearchBitsets(ix, queries, n, file->nshards, (const uint32_t *const *) job->deviceBitsets,
+										 first, rows, ANNB200_BITSETS_DEVICE, k, dist, ordinal, counts);
+	if (job->bitsets && file->nshards && (onDevice || job->ordinals == NULL))
+		return AnnB200IndexSearchBitsets(ix, queries, n, file->nshards, (const uint32_t *const *) job->bitsets,
+										 first, rows, 0, k, dist, ordinal, counts);
+	if (job->ordinals)
+		return AnnB200IndexSearch(ix, queries, n, job->ordinals, job->nfilter, k, dist, ordinal, counts);
+	owned = malloc(sizeof(uint64_t) * (job->nfilter ? job->nfilter : 1));
+	if (owned == NULL)
+		return ANN_NOMEM;
+	nords = AnnIndexOrdinals(file, job->filter, job->nfilter, owned);
+	status = AnnB200IndexSearch(ix, queries, n, owned, nords, k, dist, ordinal, counts);
+	free(owned);
+	return status;
+}
+
+/* The jobs grouped with job `first`: one search of their queries at the largest k. */
 static void
-SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t first, char *done)
+SearchGroupOf(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t first, char *done)
 {
 	AnnIndexFile *file = files[first];
 	uint32_t	dims = file->dimensions;
@@ -170,7 +266,7 @@ SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t fi
 	int			status;
 
 	for (uint32_t i = first; i < count; i++)
-		if (SameBatch(jobs, files, done, first, i))
+		if (SameGroup(jobs, files, done, first, i))
 		{
 			n++;
 			if (jobs[i].k > kmax)
@@ -182,14 +278,13 @@ SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t fi
 	counts = malloc(sizeof(uint32_t) * n);
 	status = queries && dist && ordinal && counts ? ANN_OK : ANN_NOMEM;
 	for (uint32_t i = first; status == ANN_OK && i < count; i++)
-		if (SameBatch(jobs, files, done, first, i))
+		if (SameGroup(jobs, files, done, first, i))
 			memcpy(queries + (size_t) g++ * dims, jobs[i].query, sizeof(float) * dims);
 	if (status == ANN_OK)
-		status = AnnB200IndexSearch((AnnB200Index *) file->device, queries, n, NULL, 0, kmax, dist, ordinal,
-									counts);
+		status = GroupSearch(file, &jobs[first], queries, n, kmax, dist, ordinal, counts);
 	g = 0;
 	for (uint32_t i = first; i < count; i++)
-		if (SameBatch(jobs, files, done, first, i))
+		if (SameGroup(jobs, files, done, first, i))
 		{
 			done[i] = 1;
 			if (status == ANN_OK)
@@ -202,38 +297,6 @@ SearchBatch(AnnIndexJob *jobs, AnnIndexFile **files, uint32_t count, uint32_t fi
 	free(dist);
 	free(ordinal);
 	free(counts);
-}
-
-static void
-SearchFiltered(AnnIndexJob *job, AnnIndexFile *file)
-{
-	const uint64_t *ordinals = job->ordinals;
-	uint64_t	n = job->nfilter;
-	uint64_t   *owned = NULL;
-	float	   *dist = malloc(sizeof(float) * (job->k ? job->k : 1));
-	uint64_t   *ordinal = malloc(sizeof(uint64_t) * (job->k ? job->k : 1));
-	uint32_t	found = 0;
-	int			status = dist && ordinal ? ANN_OK : ANN_NOMEM;
-
-	if (status == ANN_OK && ordinals == NULL)
-	{
-		owned = malloc(sizeof(uint64_t) * (job->nfilter ? job->nfilter : 1));
-		if (owned == NULL)
-			status = ANN_NOMEM;
-		else
-			n = AnnIndexOrdinals(file, job->filter, job->nfilter, owned);
-		ordinals = owned;
-	}
-	if (status == ANN_OK)
-		status = AnnB200IndexSearch((AnnB200Index *) file->device, job->query, 1, ordinals, n, job->k, dist,
-									ordinal, &found);
-	if (status == ANN_OK)
-		Finish(job, file, dist, ordinal, found);
-	else
-		job->status = (AnnStatus) status;
-	free(owned);
-	free(dist);
-	free(ordinal);
 }
 
 static void
@@ -277,19 +340,77 @@ SearchIndex(AnnIndexJob *jobs, uint32_t count)
 		done[i] = 0;
 	}
 	for (uint32_t i = 0; i < count; i++)
-		if (!done[i] && !jobs[i].filtered)
-			SearchBatch(jobs, files, count, i, done);
-	for (uint32_t i = 0; i < count; i++)
 		if (!done[i])
-		{
-			SearchFiltered(&jobs[i], files[i]);
-			done[i] = 1;
-		}
+			SearchGroupOf(jobs, files, count, i, done);
 	for (uint32_t i = 0; i < count; i++)
 		if (files[i])
 			AnnIndexPut(files[i]);
 	free(files);
 	free(done);
+}
+
+/*
+ * Cached filter bitmaps (AnnIndexBitmapDevice, ann/server/indexfile.h:
+ * 147-165): keep each shard's bitset on the device of an index whose FP32
+ * rows live on one device, so a search over a cached filter copies nothing
+ * (AnnB200IndexSearchBitsets with ANNB200_BITSETS_DEVICE). Row lists are not
+ * kept: the device expands the bitsets per search. A failure leaves the
+ * bitmap on the per-query path, as the reference's hook does.
+ */
+static void
+UploadBitmap(AnnIndexFile *file, AnnIndexBitmap *bitmap)
+{
+	AnnB200Index *ix = (AnnB200Index *) file->device;
+	uint64_t	rows[ANN_INDEX_MAX_SHARDS];
+	void	  **device;
+	uint64_t	bytes = 0;
+
+	if (ix == NULL || AnnB200IndexDevice(ix) < 0 || bitmap->words == NULL || file->nshards == 0)
+		return;
+	device = calloc(file->nshards, sizeof(void *));
+	if (device == NULL)
+		return;
+	for (uint32_t s = 0; s < file->nshards; s++)
+	{
+		rows[s] = file->shards[s].rows;
+		bytes += (rows[s] + 31) / 32 * sizeof(uint32_t);
+	}
+	if (AnnB200IndexKeepBitsets(ix, file->nshards, (const uint32_t *const *) bitmap->bitsets, rows, device) != ANN_OK)
+	{
+		free(device);
+		return;
+	}
+	bitmap->device = device;
+	bitmap->deviceBytes = bytes;
+}
+
+static void
+ReleaseBitmap(AnnIndexFile *file, AnnIndexBitmap *bitmap)
+{
+	if (bitmap->device)
+	{
+		AnnB200IndexDropBitsets((AnnB200Index *) file->device, file->nshards, bitmap->device);
+		free(bitmap->device);
+	}
+	bitmap->device = NULL;
+	bitmap->deviceRows = NULL;
+	bitmap->deviceBytes = 0;
+}
+
+/*
+ * Whether a search for k results over every row should run as a scan of a
+ * cached row list instead of the backend's plain search (the server then
+ * turns a match-all predicate into a filtered search, ann/server/server.c:
+ * 3213-3218). Here the plain search already is the exact scan of every row,
+ * batched with the other unfiltered jobs, so building a row list only adds
+ * work: never.
+ */
+static int
+ScanPreferred(const struct AnnIndexFile *file, uint32_t k)
+{
+	(void) file;
+	(void) k;
+	return 0;
 }
 
 static AnnBackend WorkerBackend;
@@ -301,6 +422,9 @@ WorkerBackendInit(void)
 	WorkerBackend = *AnnB200Backend();
 	WorkerBackend.load_index = LoadIndex;
 	WorkerBackend.search_index = SearchIndex;
+	WorkerBackend.scan_preferred = ScanPreferred;
+	AnnIndexBitmapDevice.upload = UploadBitmap;
+	AnnIndexBitmapDevice.release = ReleaseBitmap;
 }
 
 const AnnBackend *AnnB200WorkerBackend(void);

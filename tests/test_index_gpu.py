@@ -47,15 +47,26 @@ class Jobs:
     def __init__(self):
         self.specs = []
 
-    def add(self, name, query, k, keys=None, ordinals=None, exclude=None, dims=None):
+    def add(self, name, query, k, keys=None, ordinals=None, exclude=None, dims=None, bitsets=None):
+        """keys / ordinals / bitsets: arrays shared by every job given the
+        same object (the server's same-filter jobs share their arrays);
+        bitsets: a list of per-shard uint32 words."""
         self.specs.append(dict(name=name, query=np.ascontiguousarray(query, dtype=np.float32), k=k, keys=keys,
-                               ordinals=ordinals, exclude=exclude, dims=dims))
+                               ordinals=ordinals, exclude=exclude, dims=dims, bitsets=bitsets))
         return self
 
     def run(self, backend, rename=None):
         n = len(self.specs)
         jobs = (_abi.AnnIndexJob * n)()
         keep = []
+        shared = {}
+
+        def arr_of(obj, dtype):
+            # one C array per Python object: jobs given the same array share its pointer
+            if id(obj) not in shared:
+                shared[id(obj)] = np.ascontiguousarray(obj, dtype=dtype)
+                keep.append(obj)
+            return shared[id(obj)]
         for job, s in zip(jobs, self.specs):
             name = s['name'] if rename is None else rename.get(s['name'], s['name'])
             job.name = name.encode()
@@ -66,17 +77,26 @@ class Jobs:
             job.results = res
             keep += [s['query'], res]
             if s['keys'] is not None:
-                arr = np.ascontiguousarray(s['keys'], dtype=np.int64)
+                arr = arr_of(s['keys'], np.int64)
                 job.filter = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
                 job.nfilter = len(arr)
                 job.filtered = 1
-                keep.append(arr)
             if s['ordinals'] is not None:
-                arr = np.ascontiguousarray(s['ordinals'], dtype=np.uint64)
+                arr = arr_of(s['ordinals'], np.uint64)
                 job.ordinals = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
                 job.nfilter = len(arr)
                 job.filtered = 1
-                keep.append(arr)
+            if s['bitsets'] is not None:
+                if id(s['bitsets']) not in shared:
+                    words = [np.ascontiguousarray(w, dtype=np.uint32) for w in s['bitsets']]
+                    ptrs = (ctypes.c_void_p * len(words))(*[w.ctypes.data for w in words])
+                    shared[id(s['bitsets'])] = ptrs
+                    keep += [words, ptrs, s['bitsets']]
+                job.bitsets = ctypes.cast(shared[id(s['bitsets'])], ctypes.c_void_p)
+                job.filtered = 1
+                if s['keys'] is None and s['ordinals'] is None:
+                    job.nfilter = sum(int(np.unpackbits(np.ascontiguousarray(w, dtype=np.uint32).view(np.uint8)).sum())
+                                      for w in s['bitsets'])
             if s['exclude'] is not None:
                 arr = np.ascontiguousarray(s['exclude'], dtype=np.uint64)
                 job.exclude = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
@@ -443,3 +463,102 @@ def test_quantized_index_registration_cap_and_release(cuda, monkeypatch, capfd):
     third, err3 = create()
     lib.AnnB200IndexDestroy(third)
     assert 'read in place' in err3
+
+
+def shard_bitsets(n, shards, ordinals):
+    """Per-shard bitsets (uint32 words, bit r of shard s = row first_s + r)
+    of a sorted ordinal list, over write_index_dir's shard bounds."""
+    bounds = [n * i // shards for i in range(shards + 1)]
+    out = []
+    for s in range(shards):
+        lo, hi = bounds[s], bounds[s + 1]
+        sel = ordinals[(ordinals >= lo) & (ordinals < hi)] - lo
+        bits = np.zeros(((hi - lo + 31) // 32) * 32, dtype=np.uint8)
+        bits[sel.astype(np.int64)] = 1
+        out.append(np.packbits(bits, bitorder='little').view(np.uint32))
+    return out, bounds
+
+
+def test_same_filter_groups_and_bitset_forms(backends, tmp_path):
+    # jobs sharing one filter's arrays run as one batched search (the
+    # tensor-core path from 16 queries); the filter's per-shard bitsets are
+    # expanded on the device instead of uploading ordinals; answers equal
+    # the cpu backend's, job by job
+    rng = np.random.default_rng(17)
+    n, d, shards = 40000, 64, 3
+    x = synth.mixture(n, d, 40, seed=17)
+    keys = rng.choice(np.arange(-10 ** 9, 10 ** 9), n, replace=False)
+    skeys, rows = synth.write_index_dir(str(tmp_path / 'grp'), keys, x, shards=shards)
+    cpu, ours = backends
+    assert load(cpu, 'cpu_g', str(tmp_path / 'grp')) == 0
+    assert load(ours, 'b200_g', str(tmp_path / 'grp')) == 0
+    q = synth.mixture_queries(80, d, 40, seed=18)
+    ords_a = np.sort(rng.choice(n, 9000, replace=False)).astype(np.uint64)
+    ords_b = np.sort(rng.choice(n, 700, replace=False)).astype(np.uint64)
+    keys_c = np.sort(rng.choice(skeys, 4000, replace=False))
+    bits_a, _ = shard_bitsets(n, shards, ords_a)
+    jobs = Jobs()
+    for i in range(24):                    # group 1: one ordinal array, with its bitsets
+        jobs.add('IX', q[i], (10, 40, 100)[i % 3], ordinals=ords_a, bitsets=bits_a)
+    for i in range(24, 44):                # group 2: one key array
+        jobs.add('IX', q[i], 25, keys=keys_c)
+    for i in range(44, 50):                # group 3: a small ordinal array, interleaved with unfiltered jobs
+        jobs.add('IX', q[i], 30, ordinals=ords_b)
+        jobs.add('IX', q[i + 20], 12)
+    jobs.add('IX', q[70], 30, ordinals=np.array(ords_b))   # same values, its own array: its own search
+    assert_same_as_cpu(backends, jobs, 'cpu_g', 'b200_g')
+    # bitsets alone (a filter the server keeps only as bitsets): the same
+    # answers as the ordinal list they encode
+    alone, listed = Jobs(), Jobs()
+    for i in range(20):
+        alone.add('IX', q[i], 33, bitsets=bits_a)
+        listed.add('IX', q[i], 33, ordinals=ords_a)
+    got = alone.run(ours, rename={'IX': 'b200_g'})
+    want = listed.run(ours, rename={'IX': 'b200_g'})
+    assert got == want and all(g[0] == 0 and len(g[2]) == 33 for g in got)
+
+
+def test_bitsets_kept_on_device(cuda):
+    # AnnB200IndexKeepBitsets / AnnB200IndexSearchBitsets(ANNB200_BITSETS_DEVICE):
+    # the cached-bitmap form kept on the device answers as the ordinal list,
+    # including shards with no bitset and shards whose rows are not a
+    # multiple of 32
+    import pgvector_b200 as pb
+    lib = pb.load()
+    rng = np.random.default_rng(19)
+    n, d, shards = 30001, 48, 4
+    x = synth.mixture(n, d, 30, seed=19)
+    q = synth.mixture_queries(40, d, 30, seed=20)
+    ords = np.sort(rng.choice(n, 6000, replace=False)).astype(np.uint64)
+    bits, bounds = shard_bitsets(n, shards, ords)
+    bits[2] = None
+    ords = ords[(ords < bounds[2]) | (ords >= bounds[3])]
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ix = ctypes.c_void_p()
+    assert lib.AnnB200IndexCreate(0, d, n, P(x), ctypes.byref(ix)) == 0
+    try:
+        assert lib.AnnB200IndexDevice(ix) == 0
+        first = np.array(bounds[:-1], dtype=np.uint64)
+        count = np.diff(np.array(bounds, dtype=np.uint64))
+        host = (ctypes.c_void_p * shards)(*[None if b is None else b.ctypes.data for b in bits])
+        dev = (ctypes.c_void_p * shards)()
+        assert lib.AnnB200IndexKeepBitsets(ix, shards, host, P(count), dev) == 0
+        assert dev[2] is None and all(dev[s] for s in (0, 1, 3))
+
+        def search(kind, k):
+            dist = np.zeros((40, k), np.float32)
+            o = np.zeros((40, k), np.uint64)
+            cnt = np.zeros(40, np.uint32)
+            if kind == 'ords':
+                st = lib.AnnB200IndexSearch(ix, P(q), 40, P(ords), len(ords), k, P(dist), P(o), P(cnt))
+            else:
+                st = lib.AnnB200IndexSearchBitsets(ix, P(q), 40, shards, dev if kind == 'device' else host, P(first),
+                                                   P(count), 1 if kind == 'device' else 0, k, P(dist), P(o), P(cnt))
+            assert st == 0
+            return dist.view(np.uint32).tolist(), o.tolist(), cnt.tolist()
+        for k in (10, 100):
+            assert search('device', k) == search('ords', k) == search('host', k)
+        lib.AnnB200IndexDropBitsets(ix, shards, dev)
+        assert all(dev[s] is None for s in range(shards))
+    finally:
+        lib.AnnB200IndexDestroy(ix)

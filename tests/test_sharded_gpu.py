@@ -181,3 +181,41 @@ def test_two_gpu_missing_rank_times_out(cuda):
     out = run_two(True)
     status, msg = out[0]
     assert status == pb.BACKEND_ERROR and 'did not finish' in msg
+
+
+def test_two_gpu_loaded_index_parts_equal_one_device(cuda):
+    # AnnB200IndexCreateSharded: a loaded index's FP32 rows row-sharded over
+    # two GPUs answers exactly as the same index on one GPU (which equals the
+    # reference's loaded-index search), unfiltered and over ordinal lists
+    import ctypes
+    import torch
+    import pgvector_b200 as pb
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs two GPUs')
+    os.environ['NCCL_NVLS_ENABLE'] = '0'
+    lib = pb.load()
+    n, d, nq = 50001, 96, 40
+    x = synth.mixture(n, d, 25, seed=31)
+    q = synth.mixture_queries(nq, d, 25, seed=32)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    one, two = ctypes.c_void_p(), ctypes.c_void_p()
+    devs = (ctypes.c_int * 2)(0, 1)
+    assert lib.AnnB200IndexCreate(0, d, n, P(x), ctypes.byref(one)) == 0
+    assert lib.AnnB200IndexCreateSharded(2, devs, d, n, P(x), ctypes.byref(two)) == 0
+    try:
+        rng = np.random.default_rng(33)
+        cases = [(None, 10), (None, 100), (np.sort(rng.choice(n, 7000, replace=False)).astype(np.uint64), 25),
+                 (np.arange(24990, 25020, dtype=np.uint64), 12), (np.arange(5, 40, dtype=np.uint64), 50)]
+        for ords, k in cases:
+            out = []
+            for ix in (one, two):
+                dist = np.zeros((nq, k), np.float32)
+                o = np.zeros((nq, k), np.uint64)
+                cnt = np.zeros(nq, np.uint32)
+                assert lib.AnnB200IndexSearch(ix, P(q), nq, None if ords is None else P(ords),
+                                              0 if ords is None else len(ords), k, P(dist), P(o), P(cnt)) == 0
+                out.append((dist.view(np.uint32).tolist(), o.tolist(), cnt.tolist()))
+            assert out[0] == out[1], k
+    finally:
+        lib.AnnB200IndexDestroy(one)
+        lib.AnnB200IndexDestroy(two)
