@@ -75,6 +75,9 @@ extern "C"
 								 * distance (ann/server/backend.h:45-50) */
 #define ANNB200_FORCE_SIMT 2u	/* score on CUDA cores even where the tcgen05
 								 * tensor-core scan applies */
+#define ANNB200_FORCE_F16 8u	/* E4M3 rows: convert the codes to FP16 on
+								 * chip for kind::f16 MMAs instead of the
+								 * FP8 tensor scan (same results) */
 #define ANNB200_INDEX_L2 4u		/* L2 in the loaded-index form: the FP32
 								 * sqrtf of tail + (left + right) lane sums
 								 * (Distance, ann/server/indexfile.c:3133-3151)

@@ -28,7 +28,7 @@ from ._lib import (OK, INVALID, UNSUPPORTED, NOMEM, BACKEND_ERROR, AnnB200Error,
 F32, F16, E4M3, NVFP4, BIT = 0, 1, 2, 3, 4
 L2, IP, COSINE, HAMMING = 0, 1, 2, 3
 SHARD_HOST = 1
-WINDOW, FORCE_SIMT = 1, 2
+WINDOW, FORCE_SIMT, FORCE_F16 = 1, 2, 8
 
 DTYPE_NAMES = {'f32': F32, 'float32': F32, 'f16': F16, 'float16': F16, 'halfvec': F16, 'e4m3': E4M3,
                'fp8': E4M3, 'nvfp4': NVFP4, 'bit': BIT}
@@ -78,7 +78,7 @@ class Shard:
             pass
 
     def search(self, queries, k, metric, rows=None, window=False, force_simt=False, out_cap=None,
-               stream=None, status=None):
+               stream=None, status=None, force_f16=False):
         """Exact search of a query batch; returns (dist f64 [nq][cap], id i64
         [nq][cap], count u32 [nq]) CUDA tensors."""
         import torch
@@ -89,7 +89,7 @@ class Shard:
         dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
         ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
         count = torch.empty((nq,), dtype=torch.int32, device=dev)
-        flags = (WINDOW if window else 0) | (FORCE_SIMT if force_simt else 0)
+        flags = (WINDOW if window else 0) | (FORCE_SIMT if force_simt else 0) | (FORCE_F16 if force_f16 else 0)
         if rows is not None and rows.numel() == 0:
             # an empty list is a non-NULL pointer with no entries (NULL means every row)
             rows = torch.zeros((1,), dtype=torch.int32, device=dev)
@@ -173,7 +173,7 @@ class Shard:
                                        _ptr(status), _stream(stream)))
         return probes
 
-    def score_matrix(self, queries, metric, rows=None, force_simt=False, stream=None):
+    def score_matrix(self, queries, metric, rows=None, force_simt=False, stream=None, force_f16=False):
         """Approximate distances [nq][n] (squared for L2) and each query's
         error bound, as the scan computes them."""
         import torch
@@ -182,7 +182,8 @@ class Shard:
         out = torch.empty((nq, max(n, 1)), dtype=torch.float32, device=queries.device)
         err = torch.empty((nq,), dtype=torch.float64, device=queries.device)
         check(load().AnnB200ScoreMatrix(self._handle, _ptr(queries), nq, _ptr(rows), n if rows is not None else 0,
-                                        int(metric), FORCE_SIMT if force_simt else 0, _ptr(out), _ptr(err),
+                                        int(metric), (FORCE_SIMT if force_simt else 0) | (FORCE_F16 if force_f16 else 0),
+                                        _ptr(out), _ptr(err),
                                         _stream(stream)))
         return out[:, :n], err
 

@@ -48,7 +48,9 @@ struct QueryState {
   double *err;     // bound on |approximate - exact| in the distance domain
   float *thr;      // v-domain threshold of the filter scan
   int32_t *status; // ANN_OK / ANN_INVALID
-  __half *q16;     // [nq_pad][kpad] FP16 queries for the tensor scan
+  __half *q16;     // [nq_pad][kpad] FP16 queries for the tensor scan (FP8 scan: E4M3 bytes, see qscale)
+  float *qscale;   // FP8 scan: per query the power of two s with q ~ s * (hi + lo), hi and lo
+                   // E4M3 terms at q16 (bytes [nq_pad][kpad]) and lo_off bytes further
 };
 
 // A shard's rows and per-row statistics on the device.
@@ -78,6 +80,8 @@ struct ScanArgs {
   uint32_t metric;
   int mode;
   int raw_scale;            // scores are on raw codes: multiply by the row scale
+  int f8;                   // E4M3 rows scored by FP8 MMAs against the queries' two E4M3 terms
+  const float *qscale;      // f8: [nq] the terms' power-of-two scales
   const float *thr;         // [nq] v-domain thresholds (FILTER)
   float *mat;               // MATRIX: mat[q * mat_ld + i]
   uint64_t mat_ld;
@@ -400,9 +404,11 @@ cudaError_t launch_tc_scan_lists(const ScanArgs &a, const ListPlan &p, uint64_t 
 void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, uint32_t *maxn2, cudaStream_t st);
 // lo_off: FP32 rows on tensor cores -- q16 receives the queries' BF16 high
 // halves and, lo_off elements further, their low halves (0: an FP16 copy).
+// f8: the queries as two E4M3 terms with a power-of-two scale each (the FP8
+// tensor scan): hi bytes at q16, lo bytes lo_off bytes further.
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         uint32_t *flags, cudaStream_t st, uint64_t lo_off = 0);
+                         uint32_t *flags, cudaStream_t st, uint64_t lo_off = 0, int f8 = 0);
 void launch_fill_thresholds(uint32_t nq, const QueryState &qs, cudaStream_t st);
 void launch_check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t *flags, cudaStream_t st);
 void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, uint32_t k, uint32_t metric,

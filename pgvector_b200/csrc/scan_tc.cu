@@ -58,6 +58,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_BUF = 256;      // staged appends a warp buffers before a flush
 constexpr int TMEM_COLS = 512;
 constexpr unsigned long long kWaitNs = 4000000000ull;
+// E4M3 rows on FP8 tensor cores (see TcCfg<QF8>)
+constexpr int QF8 = 0x20 | DT_E4M3;
 
 struct TcArgs {
   ScanArgs a;
@@ -68,6 +70,7 @@ struct TcArgs {
   uint32_t qtiles;
   uint64_t rtiles;
   uint64_t wait_ns;    // limit of each pipeline wait (the drains keep kWaitNs)
+  int32_t q_lo_row;    // FP8 scan: row of the query map holding the low terms' first query
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -144,6 +147,17 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// E4M3 A and B (the instruction descriptor's format fields are 0 for E4M3,
+// as for FP16 under kind::f16), FP32 accumulator, K = 32.
+__device__ __forceinline__ void tc_mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -254,7 +268,7 @@ __device__ __forceinline__ float acc_score(uint32_t r, int32_t nbits) {
 // and only a chunk with a passing score in the warp takes the staging path.
 template <int Q>
 __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr, uint64_t vi, uint32_t q_base,
-                                              uint32_t bn, const float *thr_s, Appender &app) {
+                                              uint32_t bn, const float *thr_s, const float *qsc_s, Appender &app) {
   const int32_t nbits = (int32_t)(a.s.row_bytes * 8);
   const bool valid = vi < a.count;
   const uint64_t pos = a.base + vi * a.stride;
@@ -268,6 +282,10 @@ __device__ __forceinline__ void epilogue_rows(const ScanArgs &a, uint32_t taddr,
     TMEM_LD32(taddr + c0, r);
     tmem_ld_wait();
     const uint32_t q0 = q_base + c0;
+    if (Q == QF8) {   // the FP8 scan's sums are in units of each query's term scale (a power of two)
+#pragma unroll
+      for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__uint_as_float(r[j]) * qsc_s[q0 + j]);
+    }
     if (a.mode == MODE_MATRIX) {
       if (valid) {
 #pragma unroll
@@ -339,6 +357,18 @@ constexpr int F32_STAGE = 2 * A_BYTES + 2 * F32_BN * 128;
 template <> struct TcCfg<DT_F32> {
   static constexpr int STG = 2, BSTG = 2, RSTG = 2, RAWB = BM * 256, RAW_X = 64, NT = 192 + 32 * CONV_WARPS;
   static constexpr int RING = STG * F32_STAGE;
+};
+// E4M3 rows on FP8 tensor cores: TMA brings 128 codes of each of 128 rows a
+// k-block in the 128-byte swizzle straight to the A tile, and kind::f8f6f4
+// MMAs (K = 32) run them against the queries as two E4M3 terms -- hi and lo
+// with one power-of-two scale a query, s * (hi + lo) within about 2^-8 of
+// each query element -- both into one accumulator. No conversion: a stage
+// holds the A tile and the two query terms' tiles (at most 256 queries).
+constexpr int F8_BN = 256;
+constexpr int F8_STAGE = A_BYTES + 2 * F8_BN * 128;
+template <> struct TcCfg<QF8> {
+  static constexpr int STG = 2, BSTG = 2, RSTG = 0, RAWB = 0, RAW_X = 0, NT = 192;
+  static constexpr int RING = STG * F8_STAGE;
 };
 // FP16 rows named by a candidate list (or a strided sample): 4 gather warps
 // copy them from the shard into the A tiles, TMA loads only the queries.
@@ -494,9 +524,10 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   constexpr int RSTG1 = RSTG > 0 ? RSTG : 1;  // (the FP16 kernels have no raw ring)
   constexpr bool SPLIT = Q == DT_F32;         // two BF16 halves of rows and queries, three MMAs a K step
   constexpr bool QUANT = Q == DT_E4M3 || Q == DT_NVFP4 || Q == DT_BIT || SPLIT;
-  constexpr int STAGE = SPLIT ? F32_STAGE : STAGE_BYTES;
+  constexpr bool F8 = Q == QF8;
+  constexpr int STAGE = SPLIT ? F32_STAGE : (F8 ? F8_STAGE : STAGE_BYTES);
   constexpr bool GATHER = Q == GF16;
-  constexpr int32_t QX = Q == DT_BIT ? 128 : 64;   // query elements a k-block (128 bytes)
+  constexpr int32_t QX = (Q == DT_BIT || F8) ? 128 : 64;   // query elements a k-block (128 bytes)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // A and B tiles of stage s (separate rings for the gathered kernel)
@@ -519,6 +550,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   volatile uint32_t *abort = tmem_slot + 1;
   uint4 *stage_buf = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(full) + 256);  // 4 warps x EPI_BUF
   float *thr_s = reinterpret_cast<float *>(stage_buf + 4 * EPI_BUF);
+  float *qsc_s = thr_s + (t.a.nq + 255) / 256 * 256;          // FP8 scan: per-query term scales
 
   const ScanArgs &a = t.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -547,6 +579,8 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
   if (a.mode == MODE_FILTER)
     for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += C::NT)
       thr_s[i] = i < a.nq ? a.thr[i] : __int_as_float(0x7fc00000);
+  if (F8)
+    for (uint32_t i = threadIdx.x; i < (a.nq + 255) / 256 * 256; i += C::NT) qsc_s[i] = i < a.nq ? a.qscale[i] : 0.0f;
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
@@ -567,7 +601,8 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       constexpr int RING = QUANT ? RSTG1 : (GATHER ? BSTG : STG);
       uint64_t *ring_full = QUANT ? rawfull : (GATHER ? bfull : full);
       uint64_t *ring_empty = QUANT ? rawempty : (GATHER ? bempty : empty);
-      const uint32_t tx_bytes = QUANT ? (uint32_t)RAWB : (GATHER ? 0u : (uint32_t)A_BYTES) + t.bn * 128u;
+      const uint32_t tx_bytes =
+          QUANT ? (uint32_t)RAWB : (GATHER ? 0u : (uint32_t)A_BYTES) + (F8 ? 2u : 1u) * t.bn * 128u;
       uint64_t it = 0;
       bool ok = true;
       for (uint64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
@@ -585,8 +620,12 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           if (QUANT) {
             tma_load_2d(smem_u32(raw + s * RAWB), &rows_map, (int32_t)(kb * C::RAW_X), arow, ring_full + s);
           } else {
-            if (!GATHER) tma_load_2d(smem_u32(a_tile(s)), &rows_map, (int32_t)(kb * 64), arow, ring_full + s);
+            if (!GATHER)
+              tma_load_2d(smem_u32(a_tile(s)), &rows_map, (int32_t)(kb * (F8 ? 128 : 64)), arow, ring_full + s);
             tma_load_2d(smem_u32(b_tile(s)), &query_map, (int32_t)(kb * QX), (int32_t)(qt * t.bn), ring_full + s);
+            if (F8)   // the low terms, F8_BN rows of the stage further
+              tma_load_2d(smem_u32(b_tile(s) + F8_BN * 128), &query_map, (int32_t)(kb * QX),
+                          t.q_lo_row + (int32_t)(qt * t.bn), ring_full + s);
           }
           it++;
         }
@@ -623,6 +662,9 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
           for (uint32_t kk = 0; kk < 4; kk++) {   // K = 16 halves or 32 int8: 32 bytes an MMA
             if (Q == DT_BIT) {
               tc_mma_i8(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+            } else if (F8) {   // 32 codes an MMA: x . hi, then x . lo into the same sums
+              tc_mma_f8(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
+              tc_mma_f8(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + F8_BN * 128 + kk * 32), idesc, 1u);
             } else if (SPLIT) {   // hi.hi + hi.lo + lo.hi (lo.lo is left to the error bound)
               const uint32_t sal = sa + A_BYTES, sbl = sb + F32_BN * 128;
               tc_mma_f16(d_tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (kb | kk) != 0);
@@ -752,7 +794,7 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       epilogue_rows<Q>(a, tmem_base + ab * 256 + ((uint32_t)(quad * 32) << 16), rt * BM + quad * 32 + lane,
-                       qt * t.bn, t.bn, thr_s, app);
+                       qt * t.bn, t.bn, thr_s, qsc_s, app);
       tc_fence_before();
       mbar_arrive(tempty + ab);
     }
@@ -1369,7 +1411,7 @@ void launch_gather_rows(const uint8_t *codes, uint64_t row_bytes, uint64_t rows,
 template <int Q>
 size_t tc_scan_smem_t(uint32_t nq) {
   return 1024 + (size_t)TcCfg<Q>::RING + (size_t)TcCfg<Q>::RSTG * TcCfg<Q>::RAWB + 256 +
-         4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) * sizeof(float);
+         4 * EPI_BUF * sizeof(uint4) + (size_t)((nq + 255) / 256 * 256) * sizeof(float) * (Q == QF8 ? 2 : 1);
 }
 
 // Largest query count one tensor-scan launch takes (thresholds in shared memory).
@@ -1451,7 +1493,16 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   t.qtiles = (a.nq + bn - 1) / bn;
   t.rtiles = (a.count + BM - 1) / BM;
   t.wait_ns = pipeline_wait_ns();
+  t.q_lo_row = (int32_t)(t.qtiles * bn);
   if (a.count == 0 || a.nq == 0) return cudaSuccess;
+  if (a.f8) {
+    // kpad: the query terms' bytes a row (a multiple of 128); rows_map: 128-byte
+    // swizzled boxes of 128 codes x 128 rows; query_map: the terms as bytes
+    // [2 * qtiles * bn][kpad], boxes of 128 bytes x bn rows, 128-byte swizzle
+    if (a.s.dtype != DT_E4M3 || bn > (uint32_t)F8_BN || kpad % 128) return cudaErrorInvalidValue;
+    t.kblocks = kpad / 128;
+    return launch_tc_t<QF8>(rows_map, query_map, query_map, t, sms, st);
+  }
   switch (a.s.dtype) {
     case DT_F16:
       return (a.ids || a.stride != 1) ? launch_tc_t<GF16>(rows_map, query_map, qlo, t, sms, st)

@@ -20,6 +20,8 @@
 
 #include <cuda_bf16.h>
 
+#include <cuda_fp8.h>
+
 #include "internal.cuh"
 
 namespace annb200 {
@@ -354,6 +356,7 @@ struct PrepArgs {
   const uint32_t *maxn2;   // shard's largest squared row norm (float bits)
   QueryState qs;
   uint32_t *flags;         // [5] counts invalid queries
+  int f8;                  // two E4M3 terms (bytes) instead of the FP16 copy; lo_off in bytes
 };
 
 // One block a query: validity, norms, the FP16 copy and the error bound
@@ -366,13 +369,52 @@ __global__ void prep_queries(PrepArgs p) {
   const float *qv = p.queries + (uint64_t)q * p.dims;
   __shared__ double red[4][32];
   __shared__ int bad;
+  __shared__ float s_scale;
   if (threadIdx.x == 0) bad = 0;
+  if (p.f8) {
+    // the FP8 scan's query terms share one power-of-two scale s with
+    // max |q| / s <= 448 (E4M3's largest value): s * (hi + lo) holds q to
+    // about 2^-8 of each element, and multiplying by s is exact
+    float mx = 0.0f;
+    for (uint32_t d = threadIdx.x; d < p.dims; d += blockDim.x) mx = fmaxf(mx, fabsf(qv[d]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[0][threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double m = 0.0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = fmax(m, red[0][w]);
+      double sc = 1.0;
+      if (m > 0.0 && isfinite(m)) {
+        const double v = m / 448.0;
+        sc = ldexp(1.0, ilogb(v));
+        if (sc < v) sc *= 2.0;
+      }
+      s_scale = (float)sc;
+      p.qs.qscale[q] = (float)sc;
+    }
+  }
   __syncthreads();
   double r2 = 0.0, t2 = 0.0, n2 = 0.0, l2 = 0.0;
   for (uint32_t d = threadIdx.x; d < p.kpad || d < p.dims; d += blockDim.x) {
     float x = d < p.dims ? qv[d] : 0.0f;
     if (d < p.dims && !isfinite(x)) bad = 1;
-    if (p.use_q16 && d < p.kpad && p.lo_off) {
+    if (p.f8 && d < p.kpad) {
+      // hi = RN_e4m3(x / s), lo = RN_e4m3(x / s - hi) (the difference is
+      // exact: it is at most 2^-4 of x / s); the scan sees s * (hi + lo)
+      const float sc = s_scale;
+      const float y = isfinite(x) ? x / sc : 0.0f;
+      const __nv_fp8_storage_t h = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+      const float hv = __half2float(__half(__nv_cvt_fp8_to_halfraw(h, __NV_E4M3)));
+      const __nv_fp8_storage_t l = __nv_cvt_float_to_fp8(y - hv, __NV_SATFINITE, __NV_E4M3);
+      const float lv = __half2float(__half(__nv_cvt_fp8_to_halfraw(l, __NV_E4M3)));
+      uint8_t *q8 = reinterpret_cast<uint8_t *>(p.qs.q16);
+      q8[(uint64_t)q * p.kpad + d] = h;
+      q8[p.lo_off + (uint64_t)q * p.kpad + d] = l;
+      const double t = (double)sc * ((double)hv + (double)lv);
+      t2 += t * t;
+      r2 += ((double)x - t) * ((double)x - t);
+    } else if (p.use_q16 && d < p.kpad && p.lo_off) {
       // two BF16 halves: hi = RN(x), lo = RN(x - hi); the scan sees hi + lo
       const __nv_bfloat16 h = __float2bfloat16_rn(x);
       const float hf = __bfloat162float(h);
@@ -420,7 +462,7 @@ __global__ void prep_queries(PrepArgs p) {
   // the reference's query norm: FP64, dimension order (cpu.c:96-101)
   double qn = 0.0;
   for (uint32_t d = 0; d < p.dims; d++) qn = __dadd_rn(qn, __dmul_rn((double)qv[d], (double)qv[d]));
-  if (!p.use_q16) {
+  if (!p.use_q16 && !p.f8) {
     t2 = n2;
     r2 = 0.0;
   }
@@ -435,9 +477,10 @@ __global__ void prep_queries(PrepArgs p) {
   // subnormal product. Zero for the FP16 copy. (Cosine over FP32 rows is
   // scored on CUDA cores: these absolute terms would scale with 1/||x||.)
   const double sd = sqrt((double)p.kpad);
+  const bool split = p.lo_off && !p.f8;
   const double esplit =
-      p.lo_off ? ldexp(1.0, -16) * tnorm + ldexp(1.0, -8) * lnorm + ldexp(1.0, -134) * sd * (tnorm + lnorm) : 0.0;
-  const double etiny = p.lo_off ? 3.0 * p.kpad * ldexp(1.0, -126) : 0.0;
+      split ? ldexp(1.0, -16) * tnorm + ldexp(1.0, -8) * lnorm + ldexp(1.0, -134) * sd * (tnorm + lnorm) : 0.0;
+  const double etiny = split ? 3.0 * p.kpad * ldexp(1.0, -126) : 0.0;
   double err;
   switch (p.metric) {
     case M_L2: {
@@ -1329,7 +1372,7 @@ void launch_shard_stats(const ShardView &s, float *n2, float *rn, double *n2x, u
 
 void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint32_t metric, uint32_t kpad,
                          int use_q16, double gamma, const uint32_t *maxn2, const QueryState &qs, int bits,
-                         uint32_t *flags, cudaStream_t st, uint64_t lo_off) {
+                         uint32_t *flags, cudaStream_t st, uint64_t lo_off, int f8) {
   if (bits) {
     prep_queries_bits<<<(nq + 255) / 256, 256, 0, st>>>(nq, qs);
     if (use_q16 && nq)
@@ -1337,7 +1380,7 @@ void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint3
                                             reinterpret_cast<int8_t *>(qs.q16));
     return;
   }
-  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, lo_off, gamma, maxn2, qs, flags};
+  PrepArgs p{queries, nq, dims, metric, kpad, use_q16, lo_off, gamma, maxn2, qs, flags, f8};
   prep_queries<<<nq, 256, 0, st>>>(p);
 }
 

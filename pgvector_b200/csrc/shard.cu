@@ -330,8 +330,13 @@ bool encode_query_map(CUtensorMap *map, const ShardView &v, const void *q, uint3
 // exactly formed FP16 product sum into the FP32 accumulator, so K/16 rounding
 // steps, each allowed 4 ulps (2^-21) of the magnitudes involved. CUDA-core
 // scan: one FP32 rounding per fused multiply-add, allowed 2 ulps each.
-double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims, bool split = false) {
+// FP8 scan: two MMAs (the query's two terms) a 32-element K step, each
+// allowed 16 ulps (2^-19) of the magnitudes involved -- four times the FP16
+// scan's allowance, for an accumulator whose FP8 product alignment the
+// documents leave open; tests/test_error_model_gpu.py measures the margin.
+double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims, bool split = false, bool f8 = false) {
   if (bits) return 0.0;
+  if (tc && f8) return (2.0 * kpad / 32.0 + 2.0) * std::ldexp(1.0, -19);
   if (tc && split) return (3.0 * kpad / 16.0 + 2.0) * std::ldexp(1.0, -21);   // three MMAs a K step
   if (tc) return ((double)kpad / 16.0 + 2.0) * std::ldexp(1.0, -21);
   return (double)dims * std::ldexp(1.0, -22);
@@ -370,6 +375,15 @@ struct AnnB200Shard {
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
 };
+
+namespace {
+// E4M3 rows go to the FP8 tensor scan when TMA can read their codes in
+// 128-byte swizzled boxes (the shard's seg map), unless the call asks for
+// the FP16 conversion (ANNB200_FORCE_F16).
+bool use_f8(const AnnB200Shard *sh, uint32_t flags) {
+  return sh->view.dtype == DT_E4M3 && sh->seg_map_ok && !(flags & ANNB200_FORCE_F16);
+}
+}  // namespace
 
 namespace annb200 {
 int report_error(int status, const char *fmt, ...) {
@@ -576,12 +590,13 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const uint64_t n = rows ? nrows : v.rows;
   const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16 && tc_metric(v, metric);
   const bool split = tc && v.dtype == DT_F32;   // FP32 rows: BF16 halves of rows and queries
-  const uint32_t kpad = tc ? tc_kpad(v) : 0;
+  const bool f8 = tc && use_f8(sh, flags);      // E4M3 rows: FP8 MMAs, queries as two E4M3 terms
+  const uint32_t kpad = tc ? (f8 ? (v.dims + 127) / 128 * 128 : tc_kpad(v)) : 0;
   const uint32_t bn = tc ? tc_bn(v, nq) : 0;
   const uint32_t qtiles = tc ? (nq + bn - 1) / bn : 0;
   const uint32_t nq_pad = qtiles * bn;
   const uint64_t lo_off = split ? (uint64_t)nq_pad * kpad : 0;   // the low halves' block
-  const double gamma = scan_gamma(bits, tc, kpad, v.dims, split);
+  const double gamma = scan_gamma(bits, tc, kpad, v.dims, split, f8);
   const bool sample = k > 0 && n > kNoSampleRows;
   const uint64_t stride = sample ? std::max<uint64_t>(1, n / std::max<uint64_t>(kSampleRows, 8ull * k)) : 1;
   const uint64_t S = sample ? n / stride : 0;
@@ -592,7 +607,8 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
                o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
                o_q16 = c.take<__half>((size_t)nq_pad * kpad * (split ? 2 : 1)), o_mat = c.take<float>((size_t)S * nq),
                o_cnt = c.take<uint32_t>(nq), o_thr0 = c.take<float>(nq), o_flags = c.take<uint32_t>(16),
-               o_big = c.take<uint32_t>(nq), o_exact = c.take<double>((size_t)nq * kSortCap);
+               o_big = c.take<uint32_t>(nq), o_exact = c.take<double>((size_t)nq * kSortCap),
+               o_qsc = c.take<float>(nq);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
   double *exact = (double *)(w + o_exact);
@@ -604,6 +620,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   qs.thr = (float *)(w + o_thr);
   qs.status = (int32_t *)(w + o_status);
   qs.q16 = (__half *)(w + o_q16);
+  qs.qscale = (float *)(w + o_qsc);
   float *mat = (float *)(w + o_mat);
   uint32_t *cnt = (uint32_t *)(w + o_cnt);
   float *thr0 = (float *)(w + o_thr0);
@@ -617,7 +634,11 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
   CK(cudaMemsetAsync(big, 0, nq * sizeof(uint32_t), st), "memset");
   CK(cudaMemsetAsync(cnt, 0, nq * sizeof(uint32_t), st), "memset");
-  if (tc && nq_pad > nq)
+  if (f8 && nq_pad > nq)
+    for (int term = 0; term < 2; term++)   // padding query rows of both E4M3 terms score zero
+      CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)term * nq_pad + nq) * kpad, 0, (size_t)(nq_pad - nq) * kpad, st),
+         "memset");
+  else if (tc && nq_pad > nq)
     for (int half = 0; half < (split ? 2 : 1); half++)   // padding query rows (of both halves) score zero
       CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)half * lo_off + (size_t)nq * kpad) * tc_qelem(v), 0,
                          (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
@@ -629,8 +650,8 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     counted(1);
   }
   int h = clock.begin(ST_PREP);
-  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc, gamma, sh->maxn2, qs, bits, dflags, st,
-                      lo_off);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc && !f8, gamma, sh->maxn2, qs, bits, dflags,
+                      st, f8 ? (uint64_t)nq_pad * kpad : lo_off, f8);
   clock.end(h);
   counted(bits && tc ? 2 : 1);
   CK(cudaGetLastError(), "query preparation");
@@ -642,13 +663,16 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   a.nq = nq;
   a.metric = metric;
   a.raw_scale = tc && (v.dtype == DT_E4M3 || v.dtype == DT_NVFP4);   // scores on raw codes
+  a.f8 = f8;
+  a.qscale = qs.qscale;
   a.thr = qs.thr;
   a.cnt = cnt;
   a.flags = dflags;
 
   CUtensorMap query_map, query_lo_map;
-  if (tc && (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
-             (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn))))
+  if (f8 ? !encode_u8_seg_map(&query_map, qs.q16, kpad, 2ull * nq_pad, kpad, bn)
+         : (tc && (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
+                   (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn)))))
     return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
   // One scan launch timed as `stage`. Tensor path: rows come from the shard
   // itself when the candidates are a contiguous run, else from `staged`
@@ -661,10 +685,12 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
     int hk = clock.begin(stage);
     cudaError_t e;
     if (tc && !staged) {
-      e = tc_launch(sh->rows_map, (int64_t)a.base);
+      e = tc_launch(f8 ? sh->seg_map : sh->rows_map, (int64_t)a.base);
     } else if (tc) {
       CUtensorMap staged_map;
-      if (!encode_rows_map(&staged_map, v.dtype, staged, v.dims, a.count, v.row_bytes)) return cudaErrorInvalidValue;
+      if (!(f8 ? encode_u8_seg_map(&staged_map, staged, v.dims, a.count, v.row_bytes)
+               : encode_rows_map(&staged_map, v.dtype, staged, v.dims, a.count, v.row_bytes)))
+        return cudaErrorInvalidValue;
       e = tc_launch(staged_map, 0);
     } else {
       launch_simt_scan(a, st);
@@ -1495,14 +1521,16 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   const bool bits = v.dtype == DT_BIT;
   const bool tc = sh->rows_map_ok && !(flags & ANNB200_FORCE_SIMT) && nq >= 16 && tc_metric(v, metric);
   const bool split = tc && v.dtype == DT_F32;   // FP32 rows: BF16 halves of rows and queries
-  const uint32_t kpad = tc ? tc_kpad(v) : 0;
+  const bool f8 = tc && use_f8(sh, flags);
+  const uint32_t kpad = tc ? (f8 ? (v.dims + 127) / 128 * 128 : tc_kpad(v)) : 0;
   const uint32_t bn = tc ? tc_bn(v, nq) : 0;
   const uint32_t nq_pad = tc ? (nq + bn - 1) / bn * bn : 0;
   const uint64_t lo_off = split ? (uint64_t)nq_pad * kpad : 0;
   Carver c;
   const size_t o_qn2 = c.take<float>(nq), o_rnq = c.take<float>(nq), o_qn2d = c.take<double>(nq),
                o_err = c.take<double>(nq), o_thr = c.take<float>(nq), o_status = c.take<int32_t>(nq),
-               o_q16 = c.take<__half>((size_t)nq_pad * kpad * (split ? 2 : 1)), o_flags = c.take<uint32_t>(16);
+               o_q16 = c.take<__half>((size_t)nq_pad * kpad * (split ? 2 : 1)), o_flags = c.take<uint32_t>(16),
+               o_qsc = c.take<float>(nq);
   CK(sh->ws.reserve(c.off), "workspace");
   uint8_t *w = (uint8_t *)sh->ws.p;
   QueryState qs;
@@ -1513,16 +1541,22 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   qs.thr = (float *)(w + o_thr);
   qs.status = (int32_t *)(w + o_status);
   qs.q16 = (__half *)(w + o_q16);
+  qs.qscale = (float *)(w + o_qsc);
   uint32_t *dflags = (uint32_t *)(w + o_flags);
   CK(cudaMemsetAsync(dflags, 0, 64, st), "memset");
-  if (tc && nq_pad > nq)
+  if (f8 && nq_pad > nq)
+    for (int term = 0; term < 2; term++)
+      CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)term * nq_pad + nq) * kpad, 0, (size_t)(nq_pad - nq) * kpad, st),
+         "memset");
+  else if (tc && nq_pad > nq)
     for (int half = 0; half < (split ? 2 : 1); half++)
       CK(cudaMemsetAsync((uint8_t *)qs.q16 + ((size_t)half * lo_off + (size_t)nq * kpad) * tc_qelem(v), 0,
                          (size_t)(nq_pad - nq) * kpad * tc_qelem(v), st),
          "memset");
   if (rows) launch_check_rows(rows, nrows, v.rows, dflags, st);
-  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc,
-                      scan_gamma(bits, tc, kpad, v.dims, split), sh->maxn2, qs, bits, dflags, st, lo_off);
+  launch_prep_queries((const float *)queries, nq, v.dims, metric, kpad, tc && !f8,
+                      scan_gamma(bits, tc, kpad, v.dims, split, f8), sh->maxn2, qs, bits, dflags, st,
+                      f8 ? (uint64_t)nq_pad * kpad : lo_off, f8);
   counted(bits && tc ? 2 : 1);
   ScanArgs a{};
   a.s = v;
@@ -1538,21 +1572,25 @@ extern "C" int AnnB200ScoreMatrix(AnnB200Shard *sh, const void *queries, uint32_
   a.mat_ld = n;
   a.flags = dflags;
   a.raw_scale = tc && (v.dtype == DT_E4M3 || v.dtype == DT_NVFP4);
+  a.f8 = f8;
+  a.qscale = qs.qscale;
   if (tc) {
     CUtensorMap query_map, query_lo_map;
-    if (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
-        (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn)))
+    if (f8 ? !encode_u8_seg_map(&query_map, qs.q16, kpad, 2ull * nq_pad, kpad, bn)
+           : (!encode_query_map(&query_map, v, qs.q16, kpad, nq_pad, bn) ||
+              (split && !encode_query_map(&query_lo_map, v, qs.q16 + lo_off, kpad, nq_pad, bn))))
       return fail(BACKEND_ERROR, "tensor map of the query block could not be encoded");
     auto tc_launch = [&](const CUtensorMap &rows_map) -> cudaError_t {
       return launch_tc_scan(a, rows_map, 0, query_map, split ? &query_lo_map : nullptr, kpad, bn, sh->sms, st);
     };
     if (!rows || v.dtype == DT_F16) {
-      CK(tc_launch(sh->rows_map), "score scan");   // FP16 row lists: gathered by the scan
+      CK(tc_launch(f8 ? sh->seg_map : sh->rows_map), "score scan");   // FP16 row lists: gathered by the scan
     } else {
       CK(sh->staging.reserve(n * v.row_bytes), "staging");
       launch_gather_rows(v.codes, v.row_bytes, v.rows, rows, 0, 1, n, (uint8_t *)sh->staging.p, st);
       CUtensorMap staged;
-      if (!encode_rows_map(&staged, v.dtype, sh->staging.p, v.dims, n, v.row_bytes))
+      if (!(f8 ? encode_u8_seg_map(&staged, sh->staging.p, v.dims, n, v.row_bytes)
+               : encode_rows_map(&staged, v.dtype, sh->staging.p, v.dims, n, v.row_bytes)))
         return fail(BACKEND_ERROR, "tensor map of the staged rows could not be encoded");
       CK(tc_launch(staged), "score scan");
       counted(1);

@@ -48,10 +48,11 @@ def test_bound_holds_on_f16_rows(cuda, metric, simt):
     assert ratio < 0.5
 
 
-@pytest.mark.parametrize('dtype,dims', [(2, 1024), (3, 768), (3, 224)])
+@pytest.mark.parametrize('dtype,dims,f16', [(2, 1024, False), (2, 1024, True), (2, 200, False), (3, 768, False),
+                                           (3, 224, False)])
 @pytest.mark.parametrize('metric', [1, 0, 2])
 @pytest.mark.parametrize('simt', [False, True])
-def test_bound_holds_on_quantized_rows(cuda, dtype, dims, metric, simt):
+def test_bound_holds_on_quantized_rows(cuda, dtype, dims, f16, metric, simt):
     # exact: FP64 arithmetic on the rows decoded to FP32 as the reference
     # decodes them (code x scale products rounded to FP32)
     import torch
@@ -69,14 +70,16 @@ def test_bound_holds_on_quantized_rows(cuda, dtype, dims, metric, simt):
         shard = pb.Shard(pb.NVFP4, dims, torch.from_numpy(codes).to(cuda), torch.from_numpy(bs).to(cuda),
                          torch.from_numpy(rs).to(cuda))
     dec = oracle.decode_rows(dtype, dims, codes, block_scales=bs, row_scales=rs).astype(np.float64)
-    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), metric, force_simt=simt)
+    # E4M3 rows: the FP8 tensor scan (queries as two E4M3 terms), or with
+    # f16 the codes converted to FP16 for kind::f16 MMAs
+    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), metric, force_simt=simt, force_f16=f16)
     approx = approx.cpu().numpy().astype(np.float64)
     err = err.cpu().numpy()
     ex = exact(dec, q.astype(np.float64), metric)
     diff = np.abs(approx - ex)
     ratio = (diff / err[:, None]).max()
-    print('dtype %d metric %d simt %s: max |approx - exact| = %.3g, max ratio to bound = %.4f'
-          % (dtype, metric, simt, diff.max(), ratio))
+    print('dtype %d dims %d f16 %s metric %d simt %s: max |approx - exact| = %.3g, max ratio to bound = %.4f'
+          % (dtype, dims, f16, metric, simt, diff.max(), ratio))
     assert (diff <= err[:, None]).all()
     assert ratio < 0.5
 
@@ -123,3 +126,34 @@ def test_bound_holds_on_f32_rows(cuda, dims, metric, simt):
           % (dims, metric, simt, diff.max(), ratio))
     assert (diff <= err[:, None]).all()
     assert ratio < 0.5
+
+
+@pytest.mark.parametrize('dims', [1024, 4096])
+def test_fp8_accumulation_error(cuda, dims):
+    # The FP8 tensor scan's accumulation alone: queries that are exactly a
+    # power of two times E4M3 values (their low terms are zero, nothing is
+    # lost to their rounding), so |approx - exact| is what the tensor core's
+    # sums of E4M3 products lose. Measured against sum |x_i q_i| it must stay
+    # a quarter of the share of the bound scan_gamma allows for it.
+    import torch
+    import oracle
+    import pgvector_b200 as pb
+    n, nq = 8000, 64
+    rng = np.random.default_rng(dims)
+    x = (rng.standard_normal((n, dims)) * np.exp(rng.uniform(-3, 3, (1, dims)))).astype(np.float32)
+    codes, rs = oracle.quantize_fp8(x)
+    qc, _ = oracle.quantize_fp8(rng.standard_normal((nq, dims)).astype(np.float32) * 50)
+    q = (oracle.decode_rows(oracle.E4M3, dims, qc) * np.float32(2.0 ** -3)).astype(np.float32)
+    shard = pb.Shard(pb.E4M3, dims, torch.from_numpy(codes).to(cuda), None, torch.from_numpy(rs).to(cuda))
+    approx, err = shard.score_matrix(torch.from_numpy(q).to(cuda), 1)
+    dec = oracle.decode_rows(oracle.E4M3, dims, codes, row_scales=rs).astype(np.float64)
+    q64 = q.astype(np.float64)
+    ex = -(q64 @ dec.T)
+    mag = np.abs(q64) @ np.abs(dec).T
+    rel = np.abs(approx.cpu().numpy().astype(np.float64) - ex) / mag
+    kpad = (dims + 127) // 128 * 128
+    allowed = (2.0 * kpad / 32 + 2.0) * 2.0 ** -19
+    print('dims %d: largest accumulation error %.3g of sum |x q| (2^%.1f); the bound allows %.3g'
+          % (dims, rel.max(), np.log2(max(rel.max(), 1e-300)), allowed))
+    assert rel.max() <= allowed / 4
+    assert (np.abs(approx.cpu().numpy() - ex) <= err.cpu().numpy()[:, None]).all()

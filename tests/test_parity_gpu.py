@@ -25,17 +25,17 @@ def to_dev(a, cuda):
 
 
 def gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, rs=None, window=False,
-               force_simt=False, cap=None):
+               force_simt=False, cap=None, force_f16=False):
     import pgvector_b200 as pb
     shard = pb.Shard(dtype, dims, to_dev(codes, cuda), None if bs is None else to_dev(bs, cuda),
                      None if rs is None else to_dev(rs, cuda))
     d, i, c = shard.search(to_dev(queries, cuda), k, metric, rows=None if ids is None else to_dev(ids, cuda),
-                           window=window, force_simt=force_simt, out_cap=cap)
+                           window=window, force_simt=force_simt, out_cap=cap, force_f16=force_f16)
     return d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy()
 
 
 def assert_same(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None, rs=None, window=False,
-                force_simt=False, check=None):
+                force_simt=False, check=None, force_f16=False):
     """The device answers the whole batch; the oracle answers the queries
     `check` selects (all of them by default) and those must be equal."""
     n = codes.shape[0] if ids is None else len(ids)
@@ -44,7 +44,8 @@ def assert_same(cuda, dtype, dims, codes, queries, k, metric, ids=None, bs=None,
     od, oi, oc, os_ = oracle.search(dtype, dims, codes, queries[sel], k, metric, ids=ids, block_scales=bs,
                                     row_scales=rs, window=window, cap=cap)
     assert (os_ == 0).all()
-    gd, gi, gc = gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids, bs, rs, window, force_simt, cap)
+    gd, gi, gc = gpu_search(cuda, dtype, dims, codes, queries, k, metric, ids, bs, rs, window, force_simt, cap,
+                            force_f16)
     gd, gi, gc = gd[sel], gi[sel], gc[sel]
     assert np.array_equal(gc, oc.astype(gc.dtype)), (gc[:8], oc[:8])
     for q in range(len(sel)):
@@ -158,6 +159,26 @@ def test_quantized_tensor_and_simt_paths(cuda, dtype, dims, simt):
     assert_same(cuda, dtype, dims, codes, q, 100, 1, bs=bs, rs=rs, force_simt=simt)
     assert_same(cuda, dtype, dims, codes, q, 50, 0, ids=ids, bs=bs, rs=rs, force_simt=simt)
     assert_same(cuda, dtype, dims, codes, q, 20, 2, ids=ids, bs=bs, rs=rs, window=True, force_simt=simt)
+
+
+@pytest.mark.parametrize('dims', [1024, 200, 96, 64, 1000])
+@pytest.mark.parametrize('f16', [False, True])
+def test_e4m3_fp8_and_fp16_tensor_paths(cuda, dims, f16):
+    # E4M3 rows on FP8 tensor cores (codes straight from TMA, queries as two
+    # E4M3 terms with a power-of-two scale each) and through the on-chip FP16
+    # conversion (ANNB200_FORCE_F16): both bit-exact with the oracle, for
+    # every metric, whole shard, a row list (staged rows), window mode,
+    # heavy ties and dims that end inside a 128-code k-block
+    x = synth.mixture(36000, dims, 48, seed=90 + dims)
+    q = synth.mixture_queries(64, dims, 48, seed=91 + dims)
+    q[5] *= 1e-3                                        # a small query: its terms' scale is small too
+    x[9000:9300] = x[77]                                # ties ordered by row id
+    codes, rs = oracle.quantize_fp8(x)
+    _, ids = synth.bitmap(36000, 0.4, seed=92)
+    for metric in (1, 0, 2):
+        assert_same(cuda, oracle.E4M3, dims, codes, q, 60, metric, rs=rs, force_f16=f16)
+    assert_same(cuda, oracle.E4M3, dims, codes, q, 30, 1, ids=ids, rs=rs, force_f16=f16)
+    assert_same(cuda, oracle.E4M3, dims, codes, q[:20], 10, 0, ids=ids[:5000], rs=rs, window=True, force_f16=f16)
 
 
 @pytest.mark.parametrize('dims', [128, 200, 36, 37])
