@@ -597,8 +597,15 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   const uint32_t nq_pad = qtiles * bn;
   const uint64_t lo_off = split ? (uint64_t)nq_pad * kpad : 0;   // the low halves' block
   const double gamma = scan_gamma(bits, tc, kpad, v.dims, split, f8);
+  // the bound's sample: 16,384 rows (at least 8k), or a sixteenth of the
+  // candidates when that is fewer -- a row-sharded rank's smaller share
+  // needs no larger sample for the same bound quality (its k-th sampled
+  // score sits near the 16k-th row either way), and the sample scan and its
+  // selection are fixed costs of every rank
   const bool sample = k > 0 && n > kNoSampleRows;
-  const uint64_t stride = sample ? std::max<uint64_t>(1, n / std::max<uint64_t>(kSampleRows, 8ull * k)) : 1;
+  const uint64_t target = std::min<uint64_t>(std::max<uint64_t>(kSampleRows, 8ull * k),
+                                             std::max<uint64_t>(8ull * k, n / 16));
+  const uint64_t stride = sample ? std::max<uint64_t>(1, n / target) : 1;
   const uint64_t S = sample ? n / stride : 0;
 
   // ---- workspace
