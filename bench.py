@@ -170,6 +170,10 @@ class ClockSampler:
             time.sleep(0.005)
         self.skip = max(len(self.samples), len(self.lines))
 
+    def mark(self):
+        """Count readings from here on (the measured region starts)."""
+        self.skip = max(len(self.samples), len(self.lines))
+
     def _poll(self):
         n = self.nvml
         while self.running:
@@ -444,7 +448,52 @@ def build_config1(args, rank, world, dev):
         od, oi, oc, _ = oracle.search(oracle.F32, args.dims, x[lo:hi], queries[:nq].cpu().numpy(), args.k, 0)
         return od, oi + lo, oc
     w.local_oracle = local_oracle
+    w.vtable = lambda: vtable_paths(args, x, synth.mixture_queries(args.batch, args.dims, args.centres,
+                                                                    seed=args.seed))
     return w
+
+
+def vtable_paths(args, x, q, seconds=3.0):
+    """Config 1 through the worker's own entry points, host buffers in and
+    out, timed by the host clock (the calls are synchronous):
+      gathered  -- the backend vtable's search_gathered (ops 7/10): lane
+                   batches of 64 gathered jobs, each one query against 8,192
+                   of the corpus's rows (an op-10 chunk), k = 10, one call a
+                   batch (rows staged, one device submission);
+      index     -- a loaded index's search (AnnB200IndexSearch, the worker's
+                   search_index): the 100,000-row corpus, all queries of the
+                   batch in one call, k = 10."""
+    import ctypes
+    import pgvector_b200 as pb
+    lib = pb.load()
+    out = {}
+    rows_per_job, jobs_per_call = 8192, 64
+    jobs = [(q[j % len(q)], x[(j * 1531) % (len(x) - rows_per_job):][:rows_per_job], args.k, 0)
+            for j in range(jobs_per_call)]
+    pb.search_gathered(jobs)
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or calls < 3:
+        res = pb.search_gathered(jobs)
+        calls += 1
+    secs = (time.perf_counter() - t0) / calls
+    out['gathered'] = {'jobs_per_s': jobs_per_call / secs, 'ms_per_call': secs * 1e3, 'jobs_per_call': jobs_per_call,
+                       'rows_per_job': rows_per_job, 'ok': all(st == 0 and len(r) >= args.k for st, r in res)}
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ix = ctypes.c_void_p()
+    pb.check(lib.AnnB200IndexCreate(0, args.dims, len(x), P(x), ctypes.byref(ix)))
+    nq = len(q)
+    dist = np.zeros((nq, args.k), np.float32)
+    ords = np.zeros((nq, args.k), np.uint64)
+    cnt = np.zeros(nq, np.uint32)
+    pb.check(lib.AnnB200IndexSearch(ix, P(q), nq, None, 0, args.k, P(dist), P(ords), P(cnt)))
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or calls < 3:
+        pb.check(lib.AnnB200IndexSearch(ix, P(q), nq, None, 0, args.k, P(dist), P(ords), P(cnt)))
+        calls += 1
+    secs = (time.perf_counter() - t0) / calls
+    lib.AnnB200IndexDestroy(ix)
+    out['index'] = {'queries_per_s': nq / secs, 'ms_per_call': secs * 1e3, 'queries_per_call': nq}
+    return out
 
 
 def build_config2(args, rank, world, dev):
@@ -927,6 +976,12 @@ def main():
     if world > 1:
         dist.init_process_group('nccl', timeout=timedelta(seconds=180), device_id=dev)
     lib = pb.load()
+    # the clock sampler starts before the workload is built, so that its
+    # start-up (NVML's first calls) is long over when anything is timed; its
+    # readings count from the warm-up on
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
     w = {1: build_config1, 2: build_config2, 3: build_config3, 4: build_config4,
          5: build_config5}[args.config](args, rank, world, dev)
     # N > 1: the library's own NCCL communicator carries the per-rank lists
@@ -946,11 +1001,9 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident value (the clock sampler starts before warm-up so
-    # its start-up stays outside the timed region)
-    clocks = ClockSampler(local) if rank == 0 else None
+    # ---- device-resident value
     if clocks:
-        clocks.start()
+        clocks.mark()
     for _ in range(args.warmup):
         w.step(*w.inputs)
     barrier()
@@ -959,14 +1012,17 @@ def main():
     lib.AnnB200StageTimes(stage_ms, stage_calls, 10, 1)
     launches0 = lib.AnnB200LaunchCount()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
     e0.record()
     nrows_local = 0
-    for _ in range(args.steps):
+    for j in range(args.steps):
         out = w.step(*w.inputs)
         nrows_local = out[3]
+        marks[j].record()
     e1.record()
     barrier()
+    step_ms = [e0.elapsed_time(marks[0])] + [marks[j - 1].elapsed_time(marks[j]) for j in range(1, args.steps)]
     clock_info = clocks.stop() if clocks else None
     launches = lib.AnnB200LaunchCount() - launches0
     lib.AnnB200StageTimes(stage_ms, stage_calls, 10, 0)
@@ -1086,11 +1142,15 @@ def main():
             if world > 1 else 'single GPU')
         # the per-step stage times and the check close the line, so that a
         # reader keeping only its end still has them
+        if getattr(w, 'vtable', None) and world == 1:
+            cfg['worker_entry_points'] = w.vtable()
         line = {'metric': METRIC, 'value': value, 'unit': 'queries/s', 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True,
                 'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg,
                 'e2e': e2e, 'gpu_launches': int(launches), 'roofline': roofline, 'cpu_baseline': cpu,
                 'clocks': clock_info, 'verified_vs_oracle': verified, 'timed_steps': args.steps,
+                'step_ms': {'min': round(min(step_ms), 4), 'median': round(statistics.median(step_ms), 4),
+                            'max': round(max(step_ms), 4), 'slowest_step': int(np.argmax(step_ms))},
                 'stage_ms_per_step': stages}
         print(json.dumps(line), flush=True)
     w.shard.close()

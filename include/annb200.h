@@ -142,6 +142,42 @@ int			AnnB200Search(AnnB200Shard *shard, const void *queries, uint32_t nq,
 						  int32_t *status, void *stream);
 
 /*
+ * A batch of independent searches, each over its own FP32 rows in device
+ * memory, with one synchronisation for the whole batch: the reference's
+ * "one call = one device submission" for a lane's gathered jobs
+ * (search_gathered, ann/server/backend.h:129-130, called per lane batch at
+ * ann/server/server.c:1541). Per job: AnnB200Search of queries (nq <=
+ * 4096) over rows [0, nrows) (ids = row numbers) with its k, metric (L2,
+ * IP, cosine), flags and out_cap, results into its device arrays, its
+ * AnnStatus in result. With ANNB200_REJECT_NONFINITE a job whose rows hold
+ * a non-finite value fails with ANN_INVALID (the gathered job's rule). The
+ * shard is the reusable context the jobs are bound to in turn (its rows
+ * are replaced). A job whose candidate lists overflow runs again,
+ * synchronously. Returns ANN_OK when the batch ran (see each result).
+ */
+#define ANNB200_REJECT_NONFINITE 16u
+typedef struct AnnB200BatchJob
+{
+	const float *rows;			/* device [nrows][dims] */
+	uint32_t	nrows;
+	uint32_t	dims;
+	const float *queries;		/* device [nq][dims] */
+	uint32_t	nq;
+	uint32_t	k;
+	uint32_t	metric;
+	uint32_t	flags;			/* ANNB200_WINDOW, ANNB200_REJECT_NONFINITE, ... */
+	uint32_t	out_cap;
+	uint32_t	reserved;
+	double	   *out_dist;		/* device [nq][out_cap] */
+	int64_t    *out_id;
+	uint32_t   *out_count;		/* device [nq] */
+	int32_t    *status;			/* device [nq], or NULL */
+	int			result;			/* AnnStatus */
+	int			reserved2;
+} AnnB200BatchJob;
+int			AnnB200SearchBatch(AnnB200Shard *shard, AnnB200BatchJob *jobs, uint32_t n, void *stream);
+
+/*
  * Row-sharded search across GPUs (one rank a GPU). The reference spreads a
  * loaded index over the GPUs as row-range shards (placement
  * ann/server/cuvs.c:2845-2862) and merges the per-shard top-k lists on the

@@ -51,6 +51,7 @@ SIGNATURES = {
     'AnnB200IndexDropBitsets': (None, [c_void_p, c_uint32, c_void_p]),
     'AnnB200IndexCreateSharded': (c_int, [c_int, c_void_p, c_uint32, c_uint64, c_void_p, ctypes.POINTER(c_void_p)]),
     'AnnB200SearchTyped': (c_int, [c_void_p, c_uint32]),
+    'AnnB200SearchBatch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p]),
     'AnnB200IndexSearch': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_void_p, c_void_p,
                                    c_void_p]),
     'AnnB200MergeTopk': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32,

@@ -87,6 +87,13 @@ typedef struct Lane
 	double	   *hostDist;		/* pinned result staging */
 	int64_t    *hostId;
 	size_t		hostCap;
+	/* a batch of gathered jobs: their rows and queries staged in pinned memory */
+	float	   *hostIn;
+	size_t		hostInBytes;
+	uint32_t   *hostCounts;		/* pinned */
+	size_t		hostCountsBytes;
+	int32_t    *statuses;		/* device: a status a job */
+	size_t		statusesBytes;
 	/* a quantized index's FP32 re-score: two chunks of queries in flight */
 	int			rescoreReady;
 	cudaStream_t rescoreStream;
@@ -227,103 +234,119 @@ AllFinite(const float *v, size_t n)
 }
 
 /*
- * One gathered job (AnnGatheredExact semantics, ann/server/cpu.c:218-276):
- * results hold every row within the gathered tolerance of the k-th distance,
- * sorted by (distance, id).
+ * A gathered job with no rows to search or k = 0 still answers as the
+ * reference does (AnnGatheredExact, ann/server/cpu.c:218-276): ANN_INVALID
+ * for a non-finite query or row value (cpu.c:97-99, 246-251) or a zero
+ * query under cosine, else no results.
+ */
+#define GATHER_MAX_THREADS 32
+
+/* One share of a gathered batch's staging copies: jobs [begin, end). */
+typedef struct StageTask
+{
+	AnnGatheredJob *jobs;
+	const uint32_t *slot;
+	const size_t *at;			/* each job's start in the staging area (floats) */
+	float	   *dst;
+	uint32_t	begin;
+	uint32_t	end;
+} StageTask;
+
+static size_t Align16(size_t floats);
+
+static void *
+StageJobs(void *arg)
+{
+	StageTask  *t = arg;
+
+	for (uint32_t b = t->begin; b < t->end; b++)
+	{
+		const AnnGatheredJob *job = &t->jobs[t->slot[b]];
+		size_t		rv = (size_t) job->rows * job->dimensions;
+
+		memcpy(t->dst + t->at[b], job->vectors, rv * sizeof(float));
+		memcpy(t->dst + t->at[b] + Align16(rv), job->query, job->dimensions * sizeof(float));
+	}
+	return NULL;
+}
+
+/*
+ * Copy the batch's rows and queries into pinned staging on up to
+ * ANN_B200_GATHER_THREADS host threads (default the online CPUs, at most
+ * 16; about 8 MB a thread at least): a lane's batch of op-10 chunks is
+ * hundreds of MB, which one thread copies at a fraction of the memory
+ * bandwidth.
  */
 static void
-GatheredJob(AnnGatheredJob *job)
+StageAll(AnnGatheredJob *jobs, const uint32_t *slot, const size_t *at, uint32_t m, float *dst, size_t bytes)
 {
-	Lane	   *lane;
-	size_t		values = (size_t) job->rows * job->dimensions;
-	uint32_t	count = 0;
-	double		qnorm = 0;
-	int			status;
+	StageTask	task[GATHER_MAX_THREADS];
+	pthread_t	tid[GATHER_MAX_THREADS];
+	int			started[GATHER_MAX_THREADS] = {0};
+	long		threads = EnvLong("ANN_B200_GATHER_THREADS", 0);
 
-	job->nresults = 0;
-	if (job->dimensions == 0 || job->dimensions > ANN_MAX_DIM || job->metric > 2)
+	if (threads <= 0)
 	{
-		job->status = ANN_INVALID;
-		return;
+		threads = sysconf(_SC_NPROCESSORS_ONLN);
+		if (threads > 16)
+			threads = 16;
 	}
-	if (!AllFinite(job->query, job->dimensions) || !AllFinite(job->vectors, values))
+	if (threads > GATHER_MAX_THREADS)
+		threads = GATHER_MAX_THREADS;
+	if ((size_t) threads > bytes / (8u << 20) + 1)
+		threads = (long) (bytes / (8u << 20) + 1);
+	if (threads > (long) m)
+		threads = m;
+	if (threads < 1)
+		threads = 1;
+	for (long t = 0; t < threads; t++)
 	{
-		/* the reference rejects non-finite queries (cpu.c:97-99) and L2 rows
-		 * whose distance is not finite (cpu.c:246-251) */
-		job->status = ANN_INVALID;
-		return;
+		task[t] = (StageTask) {jobs, slot, at, dst, (uint32_t) ((uint64_t) m * t / threads),
+			(uint32_t) ((uint64_t) m * (t + 1) / threads)};
+		if (t > 0)
+			started[t] = pthread_create(&tid[t], NULL, StageJobs, &task[t]) == 0;
 	}
+	StageJobs(&task[0]);
+	for (long t = 1; t < threads; t++)
+	{
+		if (started[t])
+			pthread_join(tid[t], NULL);
+		else
+			StageJobs(&task[t]);
+	}
+}
+
+/* floats rounded up to 64 bytes: each staged job's rows and query start aligned */
+static size_t
+Align16(size_t floats)
+{
+	return (floats + 15) & ~(size_t) 15;
+}
+
+/* A finite query, with a nonzero norm under cosine (cpu.c:97-99, 139-142). */
+static int
+QueryValid(const AnnGatheredJob *job)
+{
+	double		qnorm = 0;
+
+	if (!AllFinite(job->query, job->dimensions))
+		return 0;
 	for (uint32_t d = 0; d < job->dimensions; d++)
 		qnorm += (double) job->query[d] * job->query[d];
-	if (job->metric == 2 && qnorm == 0)
-	{
-		job->status = ANN_INVALID;
-		return;
-	}
-	if (job->rows == 0 || job->k == 0)
-	{
-		job->status = ANN_OK;
-		return;
-	}
-	if (InjectLost())
-	{
-		job->status = ANN_BACKEND_ERROR;
-		return;
-	}
-	lane = LaneGet();
-	if (lane == NULL)
-	{
-		job->status = ANN_BACKEND_ERROR;
-		return;
-	}
-	if (!Grow(&lane->rows, &lane->rowsBytes, values * sizeof(float)) ||
-		!Grow((void **) &lane->query, &lane->queryBytes, job->dimensions * sizeof(float)) ||
-		!LaneResults(lane, job->rows))
-	{
-		job->status = ANN_NOMEM;
-		return;
-	}
-	if (cudaMemcpyAsync(lane->rows, job->vectors, values * sizeof(float), cudaMemcpyHostToDevice,
-						lane->stream) != cudaSuccess ||
-		cudaMemcpyAsync(lane->query, job->query, job->dimensions * sizeof(float), cudaMemcpyHostToDevice,
-						lane->stream) != cudaSuccess)
-	{
-		job->status = ANN_BACKEND_ERROR;
-		return;
-	}
-	if (lane->shard == NULL)
-		status = AnnB200ShardCreate(lane->device, ANNB200_F32, job->dimensions, job->rows, lane->rows,
-									NULL, NULL, 0, 0, lane->stream, &lane->shard);
-	else
-		status = AnnB200ShardAssign(lane->shard, ANNB200_F32, job->dimensions, job->rows, lane->rows,
-									NULL, NULL, 0, lane->stream);
-	if (status == ANN_OK)
-		status = AnnB200Search(lane->shard, lane->query, 1, NULL, 0, job->k, job->metric, ANNB200_WINDOW,
-							   job->rows, lane->dist, lane->id, lane->count, NULL, lane->stream);
-	if (status == ANN_OK &&
-		(cudaMemcpyAsync(&count, lane->count, sizeof(count), cudaMemcpyDeviceToHost, lane->stream) != cudaSuccess ||
-		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
-		status = ANN_BACKEND_ERROR;
-	if (status == ANN_OK && count &&
-		(cudaMemcpyAsync(lane->hostDist, lane->dist, count * sizeof(double), cudaMemcpyDeviceToHost,
-						 lane->stream) != cudaSuccess ||
-		 cudaMemcpyAsync(lane->hostId, lane->id, count * sizeof(int64_t), cudaMemcpyDeviceToHost,
-						 lane->stream) != cudaSuccess ||
-		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
-		status = ANN_BACKEND_ERROR;
-	if (status != ANN_OK)
-	{
-		job->status = (AnnStatus) status;
-		return;
-	}
-	for (uint32_t i = 0; i < count; i++)
-	{
-		job->results[i].id = (uint32_t) lane->hostId[i];
-		job->results[i].distance = lane->hostDist[i];
-	}
-	job->nresults = count;
-	job->status = ANN_OK;
-	atomic_fetch_add(&DeviceJobs, 1);
+	return job->metric != 2 || qnorm != 0;
+}
+
+static AnnStatus
+TrivialStatus(const AnnGatheredJob *job)
+{
+	double		qnorm = 0;
+
+	if (!AllFinite(job->query, job->dimensions) ||
+		!AllFinite(job->vectors, (size_t) job->rows * job->dimensions))
+		return ANN_INVALID;
+	for (uint32_t d = 0; d < job->dimensions; d++)
+		qnorm += (double) job->query[d] * job->query[d];
+	return job->metric == 2 && qnorm == 0 ? ANN_INVALID : ANN_OK;
 }
 
 /* ---------------------------------------------------------------- loaded indexes */
@@ -854,7 +877,6 @@ ListCandidates(const AnnB200Index *ix, Lane *lane, QuantSlot *slot, const uint32
 	}
 }
 
-#define GATHER_MAX_THREADS 32
 
 /*
  * Copy the candidates' FP32 rows of queries [0, mm) into pinned staging:
@@ -1843,11 +1865,144 @@ AnnB200SearchTyped(AnnB200TypedJob *jobs, uint32_t n)
 	return ANN_OK;
 }
 
+/*
+ * A lane's batch of gathered jobs as one device submission (the reference's
+ * contract for search_gathered, ann/server/backend.h:129-130): every job's
+ * rows and query are staged into pinned memory and cross in one copy, the
+ * searches run as one AnnB200SearchBatch (the rows' finiteness checked on
+ * the device), and the results come back in one copy. Jobs the host can
+ * settle (bad dimensions or metric, no rows, k = 0) are answered first.
+ */
 static void
 SearchGathered(AnnGatheredJob *jobs, uint32_t count)
 {
+	Lane	   *lane;
+	AnnB200BatchJob *batch = NULL;
+	uint32_t   *slot = NULL;
+	size_t	   *starts = NULL;
+	size_t		values = 0,
+				results = 0;
+	uint32_t	m = 0;
+	int			status = ANN_OK;
+
 	for (uint32_t i = 0; i < count; i++)
-		GatheredJob(&jobs[i]);
+	{
+		AnnGatheredJob *job = &jobs[i];
+
+		job->nresults = 0;
+		job->status = ANN_OK;
+		if (job->dimensions == 0 || job->dimensions > ANN_MAX_DIM || job->metric > 2)
+			job->status = ANN_INVALID;
+		else if (job->rows == 0 || job->k == 0)
+			job->status = TrivialStatus(job);
+		else if (!QueryValid(job))
+			job->status = ANN_INVALID;
+		else if (InjectLost())
+			job->status = ANN_BACKEND_ERROR;
+		else
+		{
+			values += Align16((size_t) job->rows * job->dimensions) + Align16(job->dimensions);
+			results += job->rows;
+			m++;
+		}
+	}
+	if (m == 0)
+		return;
+	batch = calloc(m, sizeof(*batch));
+	slot = calloc(m, sizeof(*slot));
+	if (batch == NULL || slot == NULL)
+	{
+		for (uint32_t i = 0; i < count; i++)
+			if (jobs[i].status == ANN_OK && jobs[i].rows && jobs[i].k)
+				jobs[i].status = ANN_NOMEM;
+		free(batch);
+		free(slot);
+		return;
+	}
+	for (uint32_t i = 0, b = 0; i < count; i++)
+		if (jobs[i].status == ANN_OK && jobs[i].rows && jobs[i].k)
+			slot[b++] = i;
+	lane = LaneGet();
+	if (lane == NULL)
+		status = ANN_BACKEND_ERROR;
+	if (status == ANN_OK &&
+		(!GrowHost((void **) &lane->hostIn, &lane->hostInBytes, values * sizeof(float)) ||
+		 !Grow(&lane->rows, &lane->rowsBytes, values * sizeof(float)) ||
+		 !LaneResults(lane, results) ||
+		 !Grow((void **) &lane->counts, &lane->countsBytes, m * sizeof(uint32_t)) ||
+		 !Grow((void **) &lane->statuses, &lane->statusesBytes, m * sizeof(int32_t)) ||
+		 !GrowHost((void **) &lane->hostCounts, &lane->hostCountsBytes, m * sizeof(uint32_t))))
+		status = ANN_NOMEM;
+	if (status == ANN_OK && (starts = malloc(sizeof(*starts) * m)) == NULL)
+		status = ANN_NOMEM;
+	if (status == ANN_OK)
+	{
+		size_t		at = 0,
+					res = 0;
+		uint32_t	b = 0;
+
+		for (uint32_t i = 0; i < count; i++)
+		{
+			AnnGatheredJob *job = &jobs[i];
+			size_t		rv = (size_t) job->rows * job->dimensions;
+
+			if (job->status != ANN_OK || job->rows == 0 || job->k == 0)
+				continue;
+			starts[b] = at;
+			batch[b] = (AnnB200BatchJob) {
+				.rows = (const float *) lane->rows + at, .nrows = job->rows, .dims = job->dimensions,
+				.queries = (const float *) lane->rows + at + Align16(rv), .nq = 1, .k = job->k,
+				.metric = job->metric,
+				.flags = ANNB200_WINDOW | ANNB200_REJECT_NONFINITE, .out_cap = job->rows,
+				.out_dist = lane->dist + res, .out_id = lane->id + res, .out_count = lane->counts + b,
+				.status = lane->statuses + b};
+			b++;
+			at += Align16(rv) + Align16(job->dimensions);
+			res += job->rows;
+		}
+		StageAll(jobs, slot, starts, m, lane->hostIn, values * sizeof(float));
+		if (cudaMemcpyAsync(lane->rows, lane->hostIn, values * sizeof(float), cudaMemcpyHostToDevice,
+							lane->stream) != cudaSuccess)
+			status = ANN_BACKEND_ERROR;
+	}
+	/* the lane's reusable context: a shard bound to each job in turn */
+	if (status == ANN_OK && lane->shard == NULL)
+		status = AnnB200ShardCreate(lane->device, ANNB200_F32, batch[0].dims, batch[0].nrows, batch[0].rows,
+									NULL, NULL, 0, 0, lane->stream, &lane->shard);
+	if (status == ANN_OK)
+		status = AnnB200SearchBatch(lane->shard, batch, m, lane->stream);
+	if (status == ANN_OK &&
+		(cudaMemcpyAsync(lane->hostCounts, lane->counts, m * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostDist, lane->dist, results * sizeof(double), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaMemcpyAsync(lane->hostId, lane->id, results * sizeof(int64_t), cudaMemcpyDeviceToHost,
+						 lane->stream) != cudaSuccess ||
+		 cudaStreamSynchronize(lane->stream) != cudaSuccess))
+		status = ANN_BACKEND_ERROR;
+	for (uint32_t b = 0, res = 0; b < m; b++)
+	{
+		AnnGatheredJob *job = &jobs[slot[b]];
+
+		if (status != ANN_OK || batch[b].result != ANN_OK)
+		{
+			job->status = (AnnStatus) (status != ANN_OK ? status : batch[b].result);
+			res += job->rows;
+			continue;
+		}
+		for (uint32_t i = 0; i < lane->hostCounts[b]; i++)
+		{
+			job->results[i].id = (uint32_t) lane->hostId[res + i];
+			job->results[i].distance = lane->hostDist[res + i];
+		}
+		job->nresults = lane->hostCounts[b];
+		job->status = ANN_OK;
+		atomic_fetch_add(&DeviceJobs, 1);
+		res += job->rows;
+	}
+	free(batch);
+	free(slot);
+	free(starts);
 }
 
 static uint64_t

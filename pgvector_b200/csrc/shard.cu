@@ -435,7 +435,7 @@ extern "C" void AnnB200ShardDestroy(AnnB200Shard *s) {
 // from the host (owned), and compute the per-row norms.
 static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t rows, const void *codes,
                       const void *block_scales, const float *row_scales, int64_t first_id, bool host,
-                      cudaStream_t st) {
+                      cudaStream_t st, bool sync = true) {
   if (dtype > DT_BIT) return fail(INVALID, "unknown storage format %u", dtype);
   if (dims == 0 || dims > (dtype == DT_BIT ? 65536u : 16000u)) return fail(INVALID, "dimensions %u out of range", dims);
   if (rows > 0xffffffffull) return fail(INVALID, "a shard holds at most 2^32-1 rows");
@@ -496,7 +496,7 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
     if (dtype != DT_BIT && rows) counted(2);
     e = cudaGetLastError();
   }
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && sync) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "shard upload");
   // the tensor scan gathers 128-byte row pieces by TMA (row pitch a multiple of 16 bytes)
   s->rows_map_ok = tc_format(dtype, dims, v.row_bytes) && rows > 0 && rows < (1ull << 31) &&
@@ -922,6 +922,105 @@ extern "C" int AnnB200Search(AnnB200Shard *sh, const void *queries, uint32_t nq,
     if (r != OK) return r;
   }
   if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  return OK;
+}
+
+// ---------------------------------------------------------------- batches of independent searches
+
+namespace {
+
+// A 4-byte word per job: nonzero when the job's rows hold a non-finite value.
+__global__ void nonfinite_rows(const float *v, uint64_t n, uint32_t *flag) {
+  bool bad = false;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    bad |= !isfinite(v[i]);
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u);
+}
+
+constexpr size_t kJobWords = 16;   // a job's flag words: the search's 8, then the rows check
+
+}  // namespace
+
+extern "C" int AnnB200SearchBatch(AnnB200Shard *sh, AnnB200BatchJob *jobs, uint32_t n, void *stream) {
+  if (!sh) return fail(INVALID, "shard is NULL");
+  if (n && !jobs) return fail(INVALID, "jobs is NULL");
+  if (n == 0) return OK;
+  DeviceGuard g(sh->device);
+  std::lock_guard<std::mutex> lock(sh->mu);
+  cudaStream_t st = (cudaStream_t)stream;
+  static thread_local DeviceBuffer fl[64];
+  static thread_local std::vector<uint32_t> hfl;
+  if (sh->device < 0 || sh->device >= 64) return fail(UNSUPPORTED, "device %d", sh->device);
+  DeviceBuffer &words = fl[sh->device];
+  CK(words.reserve((size_t)n * kJobWords * 4), "batch flags");
+  CK(cudaMemsetAsync(words.p, 0, (size_t)n * kJobWords * 4, st), "memset");
+  hfl.assign((size_t)n * kJobWords, 0);
+  uint32_t *w = (uint32_t *)words.p;
+  // every job's rows, then its search, all enqueued; one synchronisation
+  std::vector<char> queued(n, 0);
+  for (uint32_t j = 0; j < n; j++) {
+    AnnB200BatchJob &b = jobs[j];
+    b.result = OK;
+    if (b.dims == 0 || b.dims > 16000u || b.metric > M_COS || !b.queries || !b.out_dist || !b.out_id ||
+        !b.out_count || (b.nrows && !b.rows)) {
+      b.result = fail(INVALID, "batch job %u: bad dimensions, metric or pointer", j);
+      continue;
+    }
+    if (b.nq > tc_scan_max_queries()) {
+      b.result = fail(UNSUPPORTED, "batch job %u: more than %u queries", j, tc_scan_max_queries());
+      continue;
+    }
+    if (!(b.flags & ANNB200_WINDOW) && b.out_cap < b.k) {
+      b.result = fail(INVALID, "batch job %u: out_cap < k", j);
+      continue;
+    }
+    if (b.nq == 0) continue;
+    if ((b.flags & ANNB200_REJECT_NONFINITE) && b.nrows) {
+      const uint64_t vals = (uint64_t)b.nrows * b.dims;
+      const unsigned blocks = (unsigned)std::min<uint64_t>((vals + 255) / 256, (uint64_t)sh->sms * 8);
+      nonfinite_rows<<<blocks, 256, 0, st>>>(b.rows, vals, w + (size_t)j * kJobWords + 8);
+      counted(1);
+    }
+    int r = shard_bind(sh, DT_F32, b.dims, b.nrows, b.rows, nullptr, nullptr, 0, false, st, false);
+    bool any_invalid = false;
+    if (r == OK)
+      r = search_block(sh, b.queries, b.nq, nullptr, 0, b.k, b.metric, b.flags & ~ANNB200_REJECT_NONFINITE,
+                       b.out_cap, b.out_dist, b.out_id, b.out_count, b.status, st, &any_invalid,
+                       w + (size_t)j * kJobWords);
+    if (r != OK) {
+      b.result = r;
+      continue;
+    }
+    queued[j] = 1;
+  }
+  CK(cudaMemcpyAsync(hfl.data(), w, (size_t)n * kJobWords * 4, cudaMemcpyDeviceToHost, st), "batch flags");
+  CK(cudaStreamSynchronize(st), "batch");
+  for (uint32_t j = 0; j < n; j++) {
+    if (!queued[j]) continue;
+    AnnB200BatchJob &b = jobs[j];
+    const uint32_t *f = hfl.data() + (size_t)j * kJobWords;
+    if (f[8]) {
+      b.result = fail(INVALID, "batch job %u: a row holds a non-finite value", j);
+      continue;
+    }
+    if (f[0] & FLAG_TIMEOUT) {
+      b.result = fail(BACKEND_ERROR, "tensor scan pipeline timed out");
+      continue;
+    }
+    if (f[0] & (FLAG_OVERFLOW | FLAG_BIGSORT)) {
+      // the rare case: this job again, synchronously (larger lists, the large sort)
+      bool any_invalid = false;
+      int r = shard_bind(sh, DT_F32, b.dims, b.nrows, b.rows, nullptr, nullptr, 0, false, st);
+      if (r == OK)
+        r = search_block(sh, b.queries, b.nq, nullptr, 0, b.k, b.metric, b.flags & ~ANNB200_REJECT_NONFINITE,
+                         b.out_cap, b.out_dist, b.out_id, b.out_count, b.status, st, &any_invalid);
+      if (r == OK && any_invalid) r = fail(INVALID, "a query is not finite, or has zero norm under cosine");
+      b.result = r;
+      continue;
+    }
+    if (f[0] & FLAG_OUT_CAP) b.result = fail(INVALID, "window results exceed out_cap");
+    else if (f[5]) b.result = fail(INVALID, "a query is not finite, or has zero norm under cosine");
+  }
   return OK;
 }
 

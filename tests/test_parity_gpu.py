@@ -325,6 +325,22 @@ def test_backend_gathered_jobs_match_reference(cuda):
     jobs_done = pb.backend().device_jobs
     import ctypes
     assert ctypes.CFUNCTYPE(ctypes.c_uint64)(jobs_done)() >= 13
+    # one call, one submission: valid jobs beside ones the device rejects (a
+    # non-finite row value: ANN_INVALID, cpu.c:246-251) and ones the host
+    # settles, each answered as the reference answers it
+    bad = jobs[1][1].copy()
+    bad[7, 0] = np.inf
+    mixed = [jobs[0], (jobs[1][0], bad, 10, 1), jobs[2], (jobs[3][0], jobs[3][1], 0, 0),
+             (np.zeros(jobs[4][0].shape, np.float32), jobs[4][1], 5, 2), jobs[5]]
+    got = pb.search_gathered(mixed)
+    assert [g[0] for g in got] == [0, 1, 0, 0, 1, 0]
+    for j in (0, 2, 5):
+        qv, v, k, metric = mixed[j]
+        d, i, c, s = oracle.search(oracle.F32, qv.shape[0], v, qv[None], k, metric, window=True)
+        assert [r[0] for r in got[j][1]] == list(i[0, :c[0]]) and [r[1] for r in got[j][1]] == list(d[0, :c[0]])
+    # a batch of 64 jobs in one call equals the jobs one at a time
+    many = [jobs[j % 12] for j in range(64)]
+    assert pb.search_gathered(many) == [pb.search_gathered([j])[0] for j in many]
 
 
 def test_backend_in_memory_index(cuda):
