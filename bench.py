@@ -34,6 +34,7 @@ k=100, row-sharded.
 """
 import argparse
 import ctypes
+import gc
 import json
 import os
 import statistics
@@ -1001,7 +1002,13 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident value
+    # ---- device-resident value. Python's cyclic garbage collector runs at
+    # moments of its own choosing and a full pass over this process's objects
+    # takes tens of ms, during which the host launches nothing (a timed step
+    # once took 48 ms instead of 2.2): collect now, and keep it off while
+    # anything is timed.
+    gc.collect()
+    gc.disable()
     if clocks:
         clocks.mark()
     for _ in range(args.warmup):
@@ -1059,6 +1066,8 @@ def main():
                'h2d_bytes_per_step': int(sum(h.numel() * h.element_size() for h in hin)),
                'd2h_bytes_per_step': int(hd.numel() * 8 + hi_.numel() * 8) if rank == 0 else 0,
                'ms_per_step': ems / args.steps}
+
+    gc.enable()
 
     # ---- roofline of the dominant pass (stage 3: every scan launch of one
     # step's filter / list pass, timed by the library's stage clock on its
