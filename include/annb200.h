@@ -68,6 +68,9 @@ extern "C"
 /* AnnB200ShardCreate flags */
 #define ANNB200_SHARD_HOST 1u	/* inputs are host pointers: copy them into
 								 * device memory the shard owns */
+#define ANNB200_SHARD_F32_TO_F16 2u	/* with ANNB200_SHARD_HOST and ANNB200_F16:
+									 * codes are host FP32 rows, kept on the
+									 * device as FP16 (round to nearest) */
 
 /* AnnB200Search / AnnB200MergeTopk flags */
 #define ANNB200_WINDOW 1u		/* gathered-job results: every row within
@@ -422,6 +425,9 @@ int			AnnB200IndexSearchBitsets(AnnB200Index *index, const float *queries, uint3
 									  const uint64_t *shard_first, const uint64_t *shard_rows,
 									  uint32_t flags, uint32_t k, float *out_dist,
 									  uint64_t *out_ordinal, uint32_t *out_count);
+/* 1 for an index served from a copy of its rows (quantized or FP16) with
+ * the FP32 re-score of each shard's candidates, else 0. */
+int			AnnB200IndexCopyRoute(const AnnB200Index *index);
 /* The device holding an index's FP32 rows, or -1 (row-sharded, quantized copy). */
 int			AnnB200IndexDevice(const AnnB200Index *index);
 /*
@@ -446,6 +452,11 @@ void		AnnB200IndexDropBitsets(AnnB200Index *index, uint32_t nshards, void **devi
  *
  * dtype ANNB200_E4M3 or ANNB200_NVFP4; block_scales NVFP4 only; nshards
  * index shards of shard_rows[s] consecutive rows (nshards 0: one shard).
+ * dtype ANNB200_F16 is the same route over an FP16 copy: the manifest's
+ * "dtype float16" (ann/common/INDEX_FORMAT.md; the reference keeps its
+ * CAGRA dataset in FP16 and re-scores in FP32, --fp16-exact): codes are
+ * host FP16 rows, or NULL to make the copy from `vectors` on the device
+ * (round to nearest); no scales.
  * AnnB200IndexSearch on such an index is the reference's quantized scan
  * route (SearchGather, ann/server/cuvs.c:4585-4930): in each index shard
  * the min(k + slack, eligible) rows nearest to the query by the exact L2

@@ -178,8 +178,9 @@ def quant_index_search(dtype, vectors, codes, queries, k, bounds, ordinals=None,
             if kk == 0 or k == 0:
                 continue
             bs = None if block_scales is None else block_scales[lo:hi]
+            rs = None if row_scales is None else row_scales[lo:hi]
             _, ids, cnt, _ = search(dtype, dims, codes[lo:hi], q[None], kk, 0, ids=local, block_scales=bs,
-                                    row_scales=row_scales[lo:hi], threads=threads)
+                                    row_scales=rs, threads=threads)
             cand += [lo + int(i) for i in ids[0, :cnt[0]]]
         cand = np.array(cand, dtype=np.int64)
         if len(cand) == 0:

@@ -47,6 +47,7 @@ SIGNATURES = {
     'AnnB200IndexSearchBitsets': (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p,
                                           c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
     'AnnB200IndexDevice': (c_int, [c_void_p]),
+    'AnnB200IndexCopyRoute': (c_int, [c_void_p]),
     'AnnB200IndexKeepBitsets': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p]),
     'AnnB200IndexDropBitsets': (None, [c_void_p, c_uint32, c_void_p]),
     'AnnB200IndexCreateSharded': (c_int, [c_int, c_void_p, c_uint32, c_uint64, c_void_p, ctypes.POINTER(c_void_p)]),

@@ -658,14 +658,16 @@ AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype
 	int			prev = 0;
 	int			status = ANN_OK;
 	uint64_t	blocks = (dims + 15) / 16;
-	uint64_t	rowBytes = blocks * (dtype == ANNB200_NVFP4 ? 8 : 16);
+	uint64_t	rowBytes = dtype == ANNB200_F16 ? (uint64_t) dims * 2 : blocks * (dtype == ANNB200_NVFP4 ? 8 : 16);
 	uint64_t	total = 0;
+	int			half = dtype == ANNB200_F16;
 
 	if (out == NULL)
 		return ANN_INVALID;
 	*out = NULL;
-	if (dims == 0 || rows == 0 || rows > UINT32_MAX || codes == NULL || row_scales == NULL || vectors == NULL ||
-		(dtype != ANNB200_E4M3 && dtype != ANNB200_NVFP4) || (dtype == ANNB200_NVFP4 && block_scales == NULL) ||
+	if (dims == 0 || rows == 0 || rows > UINT32_MAX || vectors == NULL ||
+		(dtype != ANNB200_E4M3 && dtype != ANNB200_NVFP4 && !half) ||
+		(!half && (codes == NULL || row_scales == NULL)) || (dtype == ANNB200_NVFP4 && block_scales == NULL) ||
 		(nshards && shard_rows == NULL))
 		return ANN_INVALID;
 	for (uint32_t s = 0; s < nshards; s++)
@@ -706,10 +708,16 @@ AnnB200IndexCreateQuant(int device, uint32_t dims, uint64_t rows, uint32_t dtype
 	{
 		uint64_t	first = ix->bounds[s];
 
-		status = AnnB200ShardCreate(device, dtype, dims, ix->bounds[s + 1] - first,
-									(const uint8_t *) codes + first * rowBytes,
-									block_scales ? (const uint8_t *) block_scales + first * blocks : NULL,
-									row_scales + first, (int64_t) first, ANNB200_SHARD_HOST, NULL, &ix->shards[s]);
+		if (half && codes == NULL)	/* the FP32 rows kept as FP16 on the device */
+			status = AnnB200ShardCreate(device, ANNB200_F16, dims, ix->bounds[s + 1] - first, vectors + first * dims,
+										NULL, NULL, (int64_t) first, ANNB200_SHARD_HOST | ANNB200_SHARD_F32_TO_F16,
+										NULL, &ix->shards[s]);
+		else
+			status = AnnB200ShardCreate(device, dtype, dims, ix->bounds[s + 1] - first,
+										(const uint8_t *) codes + first * rowBytes,
+										block_scales ? (const uint8_t *) block_scales + first * blocks : NULL,
+										row_scales ? row_scales + first : NULL, (int64_t) first, ANNB200_SHARD_HOST,
+										NULL, &ix->shards[s]);
 	}
 	if (status == ANN_OK && EnvLong("ANN_B200_QUANT_MAPPED", 1) != 0)
 		MapRows(ix);
@@ -1666,6 +1674,12 @@ AnnB200IndexDropBitsets(AnnB200Index *ix, uint32_t nshards, void **device)
  * them elsewhere (a row-sharded index, one served from its quantized copy):
  * where a cached filter's bitsets may be kept for AnnB200IndexSearchBitsets.
  */
+int
+AnnB200IndexCopyRoute(const AnnB200Index *ix)
+{
+	return ix != NULL && ix->shard == NULL && ix->nparts <= 1;
+}
+
 int
 AnnB200IndexDevice(const AnnB200Index *ix)
 {

@@ -429,6 +429,7 @@ cudaError_t launch_merge_ranked(const void *dist, uint64_t dist_stride, const vo
                                 uint32_t list_cap, uint32_t k, uint32_t out_cap, double *out_dist, int64_t *out_id,
                                 uint32_t *out_count, cudaStream_t st);
 uint32_t bitmap_blocks(uint64_t nbits);
+void launch_f32_to_f16(const float *in, __half *out, uint64_t n, cudaStream_t st);
 void launch_v_to_distance(float *m, uint64_t n, uint32_t nq, uint32_t metric, const QueryState &qs, cudaStream_t st);
 void launch_bitmap_rows(const uint32_t *words, uint64_t nbits, uint32_t *rows, uint32_t *blockcnt,
                         unsigned long long *total, cudaStream_t st,

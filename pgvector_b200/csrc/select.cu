@@ -1324,9 +1324,20 @@ __global__ void __launch_bounds__(RG_WARPS * 32) rescore_gather(const float *__r
   if (lane == 0) out[w] = __double2float_rn(__dsqrt_rn(sum));
 }
 
+// FP32 -> FP16 (round to nearest even): a shard made from FP32 rows but kept
+// as halves (a loaded index whose manifest says dtype float16).
+__global__ void f32_to_f16(const float *__restrict__ in, __half *__restrict__ out, uint64_t n) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(in[i]);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
+
+void launch_f32_to_f16(const float *in, __half *out, uint64_t n, cudaStream_t st) {
+  if (n) f32_to_f16<<<(unsigned)std::min<uint64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(in, out, n);
+}
 
 void launch_rescore_rows(const float *queries, uint32_t nq, uint32_t dims, const float *rows, uint32_t stride,
                          const uint32_t *counts, float *out, cudaStream_t st) {

@@ -435,7 +435,7 @@ extern "C" void AnnB200ShardDestroy(AnnB200Shard *s) {
 // from the host (owned), and compute the per-row norms.
 static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t rows, const void *codes,
                       const void *block_scales, const float *row_scales, int64_t first_id, bool host,
-                      cudaStream_t st, bool sync = true) {
+                      cudaStream_t st, bool sync = true, bool to_half = false) {
   if (dtype > DT_BIT) return fail(INVALID, "unknown storage format %u", dtype);
   if (dims == 0 || dims > (dtype == DT_BIT ? 65536u : 16000u)) return fail(INVALID, "dimensions %u out of range", dims);
   if (rows > 0xffffffffull) return fail(INVALID, "a shard holds at most 2^32-1 rows");
@@ -459,7 +459,31 @@ static int shard_bind(AnnB200Shard *s, uint32_t dtype, uint32_t dims, uint64_t r
   const size_t bs_bytes = dtype == DT_NVFP4 ? rows * v.bblocks : 0;
   const size_t rs_bytes = (dtype == DT_E4M3 || dtype == DT_NVFP4) ? rows * sizeof(float) : 0;
   cudaError_t e = cudaSuccess;
-  if (host) {
+  if (host && to_half) {
+    // host FP32 rows kept as FP16: copied in chunks through a device buffer
+    // and rounded to nearest on the device
+    const uint64_t chunk_rows = std::max<uint64_t>(1, (64ull << 20) / ((uint64_t)dims * 4));
+    void *tmp = nullptr;
+    e = cudaMalloc(&s->owned[0], code_bytes);
+    if (e == cudaSuccess && rows) e = cudaMalloc(&tmp, std::min<uint64_t>(rows, chunk_rows) * dims * 4);
+    for (uint64_t r0 = 0; e == cudaSuccess && r0 < rows; r0 += chunk_rows) {
+      const uint64_t m = std::min<uint64_t>(chunk_rows, rows - r0);
+      e = cudaMemcpyAsync(tmp, (const float *)codes + r0 * dims, m * dims * 4, cudaMemcpyHostToDevice, st);
+      if (e == cudaSuccess) {
+        launch_f32_to_f16((const float *)tmp, (__half *)s->owned[0] + r0 * dims, m * dims, st);
+        counted(1);
+        e = cudaGetLastError();
+      }
+    }
+    if (tmp) {
+      cudaError_t e2 = cudaStreamSynchronize(st);
+      if (e == cudaSuccess) e = e2;
+      cudaFree(tmp);
+    }
+    v.codes = (const uint8_t *)s->owned[0];
+    v.bscales = nullptr;
+    v.rowscale = nullptr;
+  } else if (host) {
     const void *src[3] = {codes, block_scales, row_scales};
     const size_t bytes[3] = {code_bytes, bs_bytes, rs_bytes};
     for (int i = 0; i < 3 && e == cudaSuccess; i++) {
@@ -531,8 +555,13 @@ extern "C" int AnnB200ShardCreate(int device, uint32_t dtype, uint32_t dims, uin
     AnnB200ShardDestroy(s);
     return r;
   }
+  const bool to_half = (flags & ANNB200_SHARD_F32_TO_F16) != 0;
+  if (to_half && (dtype != DT_F16 || !(flags & ANNB200_SHARD_HOST))) {
+    AnnB200ShardDestroy(s);
+    return fail(INVALID, "FP32 rows kept as FP16 need storage format F16 and host rows");
+  }
   int r = shard_bind(s, dtype, dims, rows, codes, block_scales, row_scales, first_id, flags & ANNB200_SHARD_HOST,
-                     (cudaStream_t)stream);
+                     (cudaStream_t)stream, true, to_half);
   if (r != OK) {
     std::string keep = g_error;
     AnnB200ShardDestroy(s);

@@ -19,6 +19,8 @@
  *                  merge) when ANN_B200_INDEX_DEVICES asks for it or one
  *                  GPU cannot hold them; where no GPU set holds them and
  *                  the directory has a quantized copy, that copy instead
+ *                  (a "dtype float16" directory: an FP16 copy made on the
+ *                  device from vectors.f32, served the same way)
  *                  (AnnB200IndexCreateQuant: the reference's quantized scan
  *                  route, file->quantActive set as the reference's backend
  *                  sets it). The device copy hangs off file->device and is
@@ -124,6 +126,29 @@ CreateDevice(AnnIndexFile *file, AnnB200Index **index)
 	AnnStatus	status;
 
 	file->quantActive = 0;
+	if (strcmp(file->dtype, "float16") == 0 && !(copy && strcmp(copy, "fp32") == 0) &&
+		!(quant && copy && strcmp(copy, "quant") == 0))
+	{
+		/*
+		 * "dtype float16": the device keeps the rows in FP16 (half the
+		 * memory of FP32; the reference keeps its CAGRA dataset so, with
+		 * --fp16-exact re-scoring in FP32): each shard's k + slack nearest by
+		 * the FP16 rows, their FP32 rows re-scored, as the quantized route
+		 */
+		uint64_t	rows[ANN_INDEX_MAX_SHARDS];
+
+		for (uint32_t s = 0; s < file->nshards; s++)
+			rows[s] = file->shards[s].rows;
+		status = (AnnStatus) AnnB200IndexCreateQuant(-1, file->dimensions, file->rows, ANNB200_F16, NULL, NULL, NULL,
+													 file->vectors, file->nshards,
+													 file->nshards ? rows : NULL, AnnIndexConfig.quant_slack,
+													 AnnIndexConfig.slack_ratio, index);
+		if (status != ANN_NOMEM || !quant)
+			return status;
+		status = CreateQuant(file, index);
+		file->quantActive = status == ANN_OK;
+		return status;
+	}
 	if (quant && copy && strcmp(copy, "quant") == 0)
 		status = CreateQuant(file, index);
 	else
@@ -166,8 +191,8 @@ LoadIndex(const char *name, const char *directory)
 static void
 Finish(AnnIndexJob *job, const AnnIndexFile *file, const float *dist, const uint64_t *ordinal, uint32_t n)
 {
-	/* the quantized scan route answers as an exact scan (cuvs.c:4927) */
-	int			quant = file->quantActive;
+	/* the quantized (or FP16) scan route answers as an exact scan (cuvs.c:4927) */
+	int			quant = AnnB200IndexCopyRoute((const AnnB200Index *) file->device);
 
 	if (n > job->k)
 		n = job->k;
@@ -200,7 +225,7 @@ SameGroup(AnnIndexJob *jobs, AnnIndexFile **files, const char *done, uint32_t fi
 
 	if (done[i] || files[i] != files[first] || a->filtered != b->filtered)
 		return 0;
-	if (files[first]->quantActive && a->k != b->k)
+	if (AnnB200IndexCopyRoute((const AnnB200Index *) files[first]->device) && a->k != b->k)
 		return 0;
 	if (!a->filtered)
 		return 1;

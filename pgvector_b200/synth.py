@@ -91,14 +91,15 @@ def ivf_probes(queries, centroids, nprobe):
     return np.argsort(d2, axis=1, kind='stable')[:, :nprobe].astype(np.uint32)
 
 
-def write_index_dir(directory, keys, vectors, shards=1, quant=None):
+def write_index_dir(directory, keys, vectors, shards=1, quant=None, dtype='float32'):
     """An index directory in the worker's documented format
     (ann/common/INDEX_FORMAT.md, version 1): rows sorted by key into
     keys.i64 and vectors.f32, and a manifest naming `shards` contiguous
     graphless shards. `quant` adds a quantized copy of the rows (given in
     the same order as `vectors`): ('fp8', codes, row_scales) writes
     vectors.e4m3, ('nvfp4', codes, block_scales, row_scales) vectors.nvfp4
-    and scales.e4m3, both rowscale.f32 and the manifest's quant line.
+    and scales.e4m3, both rowscale.f32 and the manifest's quant line;
+    `dtype` is the manifest's dtype line (float32 or float16).
     Returns (sorted keys, rows in key order)."""
     import os
     order = np.argsort(np.asarray(keys, dtype=np.int64), kind='stable')
@@ -109,7 +110,7 @@ def write_index_dir(directory, keys, vectors, shards=1, quant=None):
     k.astype('<i8').tofile(os.path.join(directory, 'keys.i64'))
     v.astype('<f4').tofile(os.path.join(directory, 'vectors.f32'))
     bounds = [n * i // shards for i in range(shards + 1)]
-    lines = ['pgvector-ann-index 1', 'dimensions %d' % d, 'rows %d' % n, 'metric l2', 'dtype float32',
+    lines = ['pgvector-ann-index 1', 'dimensions %d' % d, 'rows %d' % n, 'metric l2', 'dtype %s' % dtype,
              'shards %d' % shards]
     lines += ['shard %d %d %d -' % (i, bounds[i], bounds[i + 1] - bounds[i]) for i in range(shards)]
     if quant is not None:

@@ -122,7 +122,7 @@ def test_quantized_index_arguments_checked_on_host():
     rows = (ctypes.c_uint64 * 2)(3, 2)
     cases = [
         (0, 0, 4, pb.NVFP4, P(codes), P(scales), P(rs), P(v), 0, None),      # dims 0
-        (0, 16, 4, pb.F16, P(codes), P(scales), P(rs), P(v), 0, None),       # not a quantized format
+        (0, 16, 4, pb.BIT, P(codes), P(scales), P(rs), P(v), 0, None),       # not a copy format
         (0, 16, 4, pb.NVFP4, P(codes), None, P(rs), P(v), 0, None),          # NVFP4 without block scales
         (0, 16, 4, pb.E4M3, P(codes), None, P(rs), None, 0, None),           # no FP32 rows
         (0, 16, 4, pb.E4M3, P(codes), None, P(rs), P(v), 2, rows),           # shards cover 5 rows, not 4

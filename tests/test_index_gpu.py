@@ -562,3 +562,64 @@ def test_bitsets_kept_on_device(cuda):
         assert all(dev[s] is None for s in range(shards))
     finally:
         lib.AnnB200IndexDestroy(ix)
+
+
+def test_fp16_copy_route_library(cuda):
+    # AnnB200IndexCreateQuant(ANNB200_F16, codes NULL): the FP32 rows kept as
+    # FP16 on the device (made there, round to nearest), each shard's k + slack
+    # nearest by the FP16 rows, their FP32 rows re-scored: equal to the
+    # restated route over the same FP16 rows
+    import pgvector_b200 as pb
+    lib = pb.load()
+    n, d = 24000, 72
+    x = synth.mixture(n, d, 40, seed=81)
+    q = synth.mixture_queries(40, d, 40, seed=82)
+    h = x.astype(np.float16)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ix = ctypes.c_void_p()
+    shard_rows = (ctypes.c_uint64 * 2)(9000, 15000)
+    assert lib.AnnB200IndexCreateQuant(0, d, n, pb.F16, None, None, None, P(x), 2, shard_rows, 32, 120,
+                                       ctypes.byref(ix)) == 0
+    try:
+        assert lib.AnnB200IndexCopyRoute(ix) == 1
+        filt = np.sort(np.random.default_rng(83).choice(n, 3000, replace=False)).astype(np.uint64)
+        for k, ords in ((10, None), (50, filt)):
+            dist = np.zeros((40, k), np.float32)
+            o = np.zeros((40, k), np.uint64)
+            cnt = np.zeros(40, np.uint32)
+            assert lib.AnnB200IndexSearch(ix, P(q), 40, None if ords is None else P(ords),
+                                          0 if ords is None else len(ords), k, P(dist), P(o), P(cnt)) == 0
+            want = oracle.quant_index_search(oracle.F16, x, h.view(np.uint16), q, k, [0, 9000, n], ordinals=ords,
+                                             quant_slack=32, slack_ratio=120, threads=8)
+            for i in range(40):
+                assert cnt[i] == len(want[i])
+                assert [int(v) for v in o[i, :cnt[i]]] == [w for w, _ in want[i]], (k, i)
+                assert dist[i, :cnt[i]].view(np.uint32).tolist() == [w.view(np.uint32).item() for _, w in want[i]]
+    finally:
+        lib.AnnB200IndexDestroy(ix)
+
+
+def test_float16_directory_served_from_fp16_copy(backends, tmp_path):
+    # a "dtype float16" directory: the worker keeps an FP16 copy on the
+    # device and answers by the FP16 route (route ANN_ROUTE_EXACT), its hits
+    # those of the restated route
+    rng = np.random.default_rng(85)
+    n, d = 20000, 40
+    x = synth.mixture(n, d, 30, seed=85)
+    keys = rng.choice(np.arange(-10 ** 8, 10 ** 8), n, replace=False)
+    skeys, rows = synth.write_index_dir(str(tmp_path / 'h'), keys, x, shards=2, dtype='float16')
+    cpu, ours = backends
+    assert load(ours, 'b200_h', str(tmp_path / 'h')) == 0
+    q = synth.mixture_queries(20, d, 30, seed=86)
+    jobs = Jobs()
+    for i in range(20):
+        jobs.add('IX', q[i], 15)
+    got = jobs.run(ours, rename={'IX': 'b200_h'})
+    # the worker's defaults: --quant-slack 256, --slack-ratio 100 (AnnIndexConfig)
+    want = oracle.quant_index_search(oracle.F16, rows, rows.astype(np.float16).view(np.uint16), q, 15,
+                                     [0, n // 2, n], quant_slack=256, slack_ratio=100, threads=8)
+    for (status, route, hits), w in zip(got, want):
+        assert status == 0 and route == 2
+        assert [h[2] for h in hits] == [o for o, _ in w]
+        assert [h[1] for h in hits] == [v.view(np.uint32).item() for _, v in w]
+        assert [h[0] for h in hits] == [int(skeys[o]) for o, _ in w]
