@@ -576,7 +576,7 @@ def build_config3(args, rank, world, dev):
     w.ops = 'e4m3'
     w.data = 'synthetic (seeded 4,096-centre Gaussian mixture, FP8-quantised on the GPU with the builder\'s rules)'
     w.row_bytes = pad + 4                                   # codes + row scale
-    w.profile = 'tc_scan_e4m3_config3.md'
+    w.profile = 'tc_scan_fp8_config3.md'
 
     def step(q):
         d, i, c = w.shard.search_sharded(w.comm, q, args.k, pb.IP)
