@@ -108,6 +108,55 @@ __device__ uint32_t block_radix_select(KeyAt key_at, uint32_t n, uint32_t k, uin
   return prefix;
 }
 
+// block_radix_select over keys held in registers: thread t holds elements
+// t, t + blockDim.x, ... in kr[0..R); slots past n are not counted. Same
+// passes, same result.
+template <int R>
+__device__ uint32_t block_radix_select_regs(const uint32_t (&kr)[R], uint32_t n, uint32_t k, uint32_t *hist,
+                                            uint32_t *scratch) {
+  __shared__ uint32_t s_prefix, s_k;
+  uint32_t prefix = 0, mask = 0;
+  if (threadIdx.x == 0) s_k = k;
+  const int shifts[3] = {21, 10, 0};
+  const int widths[3] = {11, 11, 10};
+  __syncthreads();
+  for (int p = 0; p < 3; p++) {
+    const int shift = shifts[p], nb = 1 << widths[p];
+    const uint32_t want = s_k;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    if (threadIdx.x == 0) s_prefix = prefix;
+#pragma unroll
+    for (int j = 0; j < R; j++) {
+      const uint32_t i = threadIdx.x + j * blockDim.x;
+      if (i < n && (kr[j] & mask) == prefix) atomicAdd(&hist[(kr[j] >> shift) & (nb - 1)], 1u);
+    }
+    __syncthreads();
+    const int per = (nb + blockDim.x - 1) / blockDim.x;
+    const int b0 = threadIdx.x * per;
+    uint32_t local = 0;
+    for (int b = b0; b < b0 + per && b < nb; b++) local += hist[b];
+    uint32_t total;
+    uint32_t before = block_exclusive_scan(local, scratch, &total);
+    if (before < want && want <= before + local) {
+      uint32_t c = before;
+      for (int b = b0; b < b0 + per && b < nb; b++) {
+        if (c + hist[b] >= want) {
+          s_prefix = prefix | ((uint32_t)b << shift);
+          s_k = want - c;
+          break;
+        }
+        c += hist[b];
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    mask |= (uint32_t)(nb - 1) << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
 // ---------------------------------------------------------------- exact distances
 
 // Raw storage of 8 consecutive dimensions of a row, per format: loaded first,
@@ -554,6 +603,11 @@ struct BoundArgs {
 
 // Per query: the k-th smallest sampled v bounds the k-th exact distance;
 // thr = threshold_v of it (or +inf when the sample holds fewer than k rows).
+// The query's sampled scores are read once, all loads in flight at once, into
+// registers (KB_REG a thread: the whole sample up to NT * KB_REG scores); the
+// three radix passes then read registers instead of re-reading the row.
+constexpr int KB_REG = 32;
+
 __global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t scratch[32];
@@ -564,8 +618,20 @@ __global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
   }
   const float *m = b.mat + (uint64_t)q * b.ld;
   uint32_t key = 0xffffffffu;
-  if (b.n >= b.k)
+  if (b.n >= b.k && b.n <= (uint64_t)NT * KB_REG) {
+    uint32_t kr[KB_REG];
+#pragma unroll
+    for (int j = 0; j < KB_REG; j++) {
+      const uint32_t i = threadIdx.x + j * NT;
+      kr[j] = i < b.n ? float_key(__ldg(m + i)) : 0xffffffffu;
+    }
+    // element i lives in thread i % NT, slot i / NT: the select visits a
+    // thread's own elements only (i = threadIdx.x + j * NT), so it indexes
+    // its registers with the unrolled j
+    key = block_radix_select_regs<KB_REG>(kr, (uint32_t)b.n, b.k, hist, scratch);
+  } else if (b.n >= b.k) {
     key = block_radix_select([&](uint32_t i) { return float_key(m[i]); }, (uint32_t)b.n, b.k, hist, scratch);
+  }
   if (threadIdx.x == 0) {
     float v = key == 0xffffffffu ? __int_as_float(0x7f800000) : key_float(key);
     double rnq = (double)b.qs.rnq[q], qn2 = b.qs.qn2d[q];
