@@ -887,9 +887,18 @@ __device__ __forceinline__ void e2m1x8_values(uint32_t w, float (&v)[8]) {
 }
 constexpr int RS_STRIDE = 144;  // bytes a staged row chunk: 128 + 16 of padding (bank-conflict free)
 
+// Inner product and cosine sum FP64 products of FP32 values in dimension
+// order (ann/server/cpu.c:118-126: dot += (double) x * (double) q). Such a
+// product is exact in FP64 (24-bit significands give at most 48 bits; no
+// FP32 pair overflows or underflows it), so the fused multiply-add
+// fma(x, q, dot) rounds exactly as the reference's add of the rounded
+// product does: one FP64 operation a dimension instead of two. The query
+// is converted to FP64 once a block (qd, shared memory) when it fits.
+constexpr uint32_t kQdMax = 2048;
+
 template <int DT>
 __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, uint32_t q, uint32_t m, uint32_t i0,
-                              uint8_t (*stage)[32 * RS_STRIDE]) {
+                              uint8_t (*stage)[32 * RS_STRIDE], const double *qd) {
   const int lane = threadIdx.x & 31;
   const uint2 *e = a.cand + (uint64_t)q * a.cap;
   const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
@@ -1009,10 +1018,18 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
               tail = __fadd_rn(tail, __fmul_rn(diff, diff));
             }
           }
+        } else if (qd && d + 8 <= dims) {
+          const double2 *q2 = reinterpret_cast<const double2 *>(qd + d);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const double2 qq = q2[j];
+            dot = __fma_rn((double)x[2 * j], qq.x, dot);
+            dot = __fma_rn((double)x[2 * j + 1], qq.y, dot);
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 8; j++)
-            if (d + j < dims) dot = __dadd_rn(dot, __dmul_rn((double)x[j], (double)qx[j]));
+            if (d + j < dims) dot = __fma_rn((double)x[j], (double)qx[j], dot);
         }
       }
     }
@@ -1037,13 +1054,21 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
 // queries keep about k survivors, so a grid sized for the largest possible
 // count (4,096) would be mostly blocks with nothing to do.
 template <int DT>
-__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact) {
+__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact, int use_qd) {
   __shared__ __align__(16) uint8_t stage[RS_WARPS][2][32 * RS_STRIDE];
+  extern __shared__ double qd_dyn[];
   const uint32_t q = blockIdx.y;
   const uint32_t m = a.cnt[q];
   const int warp = threadIdx.x >> 5;
+  if (use_qd) {
+    if ((uint32_t)(blockIdx.x * RS_WARPS * 32) >= m) return;   // no survivors for this block (whole block)
+    const float *qv = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.queries) +
+                                                      (uint64_t)q * a.qbytes);
+    for (uint32_t d = threadIdx.x; d < a.s.dims; d += blockDim.x) qd_dyn[d] = (double)qv[d];
+    __syncthreads();
+  }
   for (uint32_t i0 = (blockIdx.x * RS_WARPS + warp) * 32; i0 < m; i0 += gridDim.x * RS_WARPS * 32)
-    rescore_group<DT>(a, exact, q, m, i0, stage[warp]);
+    rescore_group<DT>(a, exact, q, m, i0, stage[warp], use_qd ? qd_dyn : nullptr);
 }
 
 // Per query: sort the survivors by (exact distance, global row id) and write
@@ -1501,12 +1526,14 @@ cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t s
     }
   } else {
     const dim3 grid(2, l.nq);
+    const int use_qd = l.metric != M_L2 && l.s.dtype != DT_BIT && l.s.dims <= kQdMax;
+    const size_t qsm = use_qd ? (size_t)l.s.dims * sizeof(double) : 0;
     switch (l.s.dtype) {
-      case DT_F32: rescore<DT_F32><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
-      case DT_F16: rescore<DT_F16><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
-      case DT_E4M3: rescore<DT_E4M3><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
-      case DT_NVFP4: rescore<DT_NVFP4><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
-      default: rescore<DT_BIT><<<grid, RS_WARPS * 32, 0, st>>>(a, ex); break;
+      case DT_F32: rescore<DT_F32><<<grid, RS_WARPS * 32, qsm, st>>>(a, ex, use_qd); break;
+      case DT_F16: rescore<DT_F16><<<grid, RS_WARPS * 32, qsm, st>>>(a, ex, use_qd); break;
+      case DT_E4M3: rescore<DT_E4M3><<<grid, RS_WARPS * 32, qsm, st>>>(a, ex, use_qd); break;
+      case DT_NVFP4: rescore<DT_NVFP4><<<grid, RS_WARPS * 32, qsm, st>>>(a, ex, use_qd); break;
+      default: rescore<DT_BIT><<<grid, RS_WARPS * 32, 0, st>>>(a, ex, 0); break;
     }
   }
   const size_t smem = (size_t)kSortCap * (8 + 8);
