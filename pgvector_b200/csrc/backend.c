@@ -602,11 +602,15 @@ MapCapBytes(void)
 static void
 MapRows(AnnB200Index *ix)
 {
-	long		page = sysconf(_SC_PAGESIZE);
+	/*
+	 * Exactly the rows' bytes: a range rounded out to whole pages could take
+	 * in the ends of neighbouring allocations (heap arrays sit side by side),
+	 * and a later copy from one of them would then start inside a
+	 * registered range and run past it, which the runtime refuses.
+	 */
 	uintptr_t	start = (uintptr_t) ix->vectors;
-	uintptr_t	base = start & ~((uintptr_t) page - 1);
-	uintptr_t	end = start + (uintptr_t) ix->rows * ix->dims * sizeof(float);
-	size_t		len = (size_t) ((end - base + (uintptr_t) page - 1) & ~((uintptr_t) page - 1));
+	uintptr_t	base = start;
+	size_t		len = (size_t) ix->rows * ix->dims * sizeof(float);
 	unsigned	flags = cudaHostRegisterMapped | cudaHostRegisterPortable;
 	void	   *dev = NULL;
 	int			debug = EnvLong("ANN_B200_DEBUG", 0) > 0;

@@ -431,8 +431,9 @@ def test_quantized_index_registration_cap_and_release(cuda, monkeypatch, capfd):
 
     def create():
         ix = ctypes.c_void_p()
-        assert lib.AnnB200IndexCreateQuant(0, d, n, pb.E4M3, P(codes), None, P(rs), P(x), 0, None, 32, 100,
-                                           ctypes.byref(ix)) == 0
+        st = lib.AnnB200IndexCreateQuant(0, d, n, pb.E4M3, P(codes), None, P(rs), P(x), 0, None, 32, 100,
+                                         ctypes.byref(ix))
+        assert st == 0, (st, lib.AnnB200LastError(), capfd.readouterr().err)
         return ix, capfd.readouterr().err
 
     def answer(ix):
