@@ -144,10 +144,36 @@ bool timing_on() {
 // a later call, or all of them (waiting) when AnnB200StageTimes reports --
 // so the timing adds no host synchronisation to the calls it times.
 struct Span {
-  int stage;
+  int stage, dev;
   cudaEvent_t a, b;
 };
 std::vector<Span> g_pending;   // under g_stage_mu
+
+// Events of read spans go back to a pool per device instead of being
+// destroyed: creating and destroying two events a span cost more host time
+// than the shorter stages themselves.
+std::vector<std::pair<int, cudaEvent_t>> g_event_pool;   // (device, event), under g_stage_mu
+
+cudaEvent_t pooled_event(int dev) {
+  {
+    std::lock_guard<std::mutex> lock(g_stage_mu);
+    for (size_t i = g_event_pool.size(); i-- > 0;)
+      if (g_event_pool[i].first == dev) {
+        cudaEvent_t e = g_event_pool[i].second;
+        g_event_pool[i] = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+      }
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+void pool_event(int dev, cudaEvent_t e) {   // under g_stage_mu
+  if (g_event_pool.size() < 4096) g_event_pool.push_back({dev, e});
+  else cudaEventDestroy(e);
+}
 
 // Fold completed spans into the totals (all of them, waiting, when `wait`).
 void collect_spans(bool wait) {
@@ -166,8 +192,8 @@ void collect_spans(bool wait) {
       g_stage_calls[sp.stage] += 1;
     }
     cudaGetLastError();
-    cudaEventDestroy(sp.a);
-    cudaEventDestroy(sp.b);
+    pool_event(sp.dev, sp.a);
+    pool_event(sp.dev, sp.b);
   }
   g_pending.resize(keep);
 }
@@ -177,16 +203,17 @@ void collect_spans(bool wait) {
 struct StageClock {
   cudaStream_t st;
   bool on;
+  int dev = 0;
   std::vector<Span> spans;
   explicit StageClock(cudaStream_t s) : st(s), on(timing_on()) {
-    if (on) collect_spans(false);
+    if (!on) return;
+    cudaGetDevice(&dev);
+    collect_spans(false);
   }
   int begin(int stage) {
     if (!on) return -1;
     if (g_stage_override >= 0) stage = g_stage_override;
-    Span sp{stage, nullptr, nullptr};
-    cudaEventCreate(&sp.a);
-    cudaEventCreate(&sp.b);
+    Span sp{stage, dev, pooled_event(dev), pooled_event(dev)};
     cudaEventRecord(sp.a, st);
     spans.push_back(sp);
     return (int)spans.size() - 1;
