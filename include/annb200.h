@@ -565,6 +565,15 @@ unsigned long long AnnB200LaunchCount(void);
 #define ANNB200_STAGES 10
 int			AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset);
 
+/*
+ * Switch the stage timing on (1) or off (0) for later calls, whatever
+ * ANN_B200_KERNEL_TIMING said; -1 only asks. Returns the previous state.
+ * Timing records two CUDA events around each stage and reads them back in
+ * later calls, which costs host time on the request path: a caller that
+ * times its requests end to end keeps it off and samples stages apart.
+ */
+int			AnnB200StageTiming(int on);
+
 #ifdef __cplusplus
 }
 #endif

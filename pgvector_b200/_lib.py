@@ -65,6 +65,7 @@ SIGNATURES = {
     'AnnB200ScoreMatrix': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
                                    c_void_p, c_void_p, c_void_p]),
     'AnnB200StageTimes': (c_int, [c_void_p, c_void_p, c_uint32, c_int]),
+    'AnnB200StageTiming': (c_int, [c_int]),
     'AnnB200CommId': (c_int, [c_void_p]),
     'AnnB200CommCreate': (c_int, [c_int, c_int, c_int, c_void_p, ctypes.POINTER(c_void_p)]),
     'AnnB200CommCreateAll': (c_int, [c_int, c_void_p, c_void_p]),

@@ -268,6 +268,7 @@ extern "C" void AnnB200CommDestroy(AnnB200Comm *c) {
     if (c->host_heads) cudaFreeHost(c->host_heads);
     if (c->host_status) cudaFreeHost(c->host_status);
     if (c->done) cudaEventDestroy(c->done);
+    if (c->bounds) cudaFree(c->bounds);
   }
   delete c;
 }
@@ -307,6 +308,22 @@ int comm_reserve(AnnB200Comm *c, size_t packet_bytes, size_t head_bytes) {
     return report_error(e == cudaErrorMemoryAllocation ? NOMEM : BACKEND_ERROR, "exchange buffers: %s",
                         cudaGetErrorString(e));
   }
+  return OK;
+}
+
+int comm_reserve_bounds(AnnB200Comm *c, uint32_t nq) {
+  const size_t want = (size_t)nq * (1 + (size_t)c->nranks) * sizeof(double);
+  if (want <= c->bounds_bytes) return OK;
+  if (c->bounds) cudaFree(c->bounds);
+  c->bounds = nullptr;
+  c->bounds_bytes = 0;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&c->bounds), want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return report_error(e == cudaErrorMemoryAllocation ? NOMEM : BACKEND_ERROR, "bounds exchange: %s",
+                        cudaGetErrorString(e));
+  }
+  c->bounds_bytes = want;
   return OK;
 }
 

@@ -29,6 +29,9 @@ struct AnnB200Comm {
   size_t host_heads_bytes = 0;
   int32_t *host_status = nullptr;   // pinned: this rank's status, copied into its packet
   cudaEvent_t done = nullptr;
+  // the mid-search exchange of per-query bounds: this rank's, then every rank's
+  double *bounds = nullptr;
+  size_t bounds_bytes = 0;
 };
 
 namespace annb200 {
@@ -45,5 +48,9 @@ int comm_wait(AnnB200Comm *c, cudaStream_t st);
 
 // Grow-only device / pinned buffers of the communicator.
 int comm_reserve(AnnB200Comm *c, size_t packet_bytes, size_t head_bytes);
+
+// Grow-only device buffer of the bounds exchange: nq doubles of this rank's
+// followed by nranks x nq of everyone's.
+int comm_reserve_bounds(AnnB200Comm *c, uint32_t nq);
 
 }  // namespace annb200

@@ -319,23 +319,29 @@ __device__ __forceinline__ double widen(double d) {
 }
 
 // Given an approximate distance-domain value D that at least k rows reach
-// (their approximate scores are <= D), the v-domain threshold every row of
-// the final answer passes: exact d_k <= D + err; the answer keeps rows with
-// exact distance <= C (C = d_k, or its widened window); their approximate
-// score is <= C + err. For L2 the domain is the squared distance and the
-// window applies to the distance itself.
-__device__ __forceinline__ float threshold_v(uint32_t metric, double D, double err, int window,
-                                            double qn2, double rnq) {
-  if (!(D < __longlong_as_double(0x7ff0000000000000ll))) return __int_as_float(0x7f800000);
+// (their approximate scores are <= D), an upper bound of the exact k-th
+// distance: those k rows' exact distances are each within err of their
+// approximate ones, so d_k <= U = D + err.
+__device__ __forceinline__ double kth_upper(double D, double err) { return D + err; }
+
+// The v-domain threshold every row of the final answer passes, given an
+// upper bound U of the exact k-th distance (from this shard's rows or from
+// any rank's of a sharded search): the answer keeps rows with exact distance
+// <= C (C = d_k, or its widened window), and their approximate score is
+// <= C + err (err: this shard's error bound of the query). For L2 the
+// domain is the squared distance and the window applies to the distance
+// itself.
+__device__ __forceinline__ float threshold_upper(uint32_t metric, double U, double err, int window, double qn2,
+                                                 double rnq) {
+  if (!(U < __longlong_as_double(0x7ff0000000000000ll))) return __int_as_float(0x7f800000);
   double t;
   if (metric == M_L2) {
-    double up = D + err;
-    double c = sqrt(up > 0.0 ? up : 0.0);
+    double c = sqrt(U > 0.0 ? U : 0.0);
     if (window) c = widen(c);
     c = c * (1.0 + 1e-12) + 1e-300;
     t = c * c + err;
   } else {
-    double c = D + err;
+    double c = U;
     if (window) c = widen(c);
     t = c + err + fabs(c) * 1e-12;
   }
@@ -344,6 +350,13 @@ __device__ __forceinline__ float threshold_v(uint32_t metric, double D, double e
   if ((double)f < v) f = nextafterf(f, __int_as_float(0x7f800000));
   // one more step up for the FP32 rounding of the scan's own v
   return nextafterf(f, __int_as_float(0x7f800000));
+}
+
+// The threshold from this shard's own k-th approximate value D.
+__device__ __forceinline__ float threshold_v(uint32_t metric, double D, double err, int window,
+                                            double qn2, double rnq) {
+  if (!(D < __longlong_as_double(0x7ff0000000000000ll))) return __int_as_float(0x7f800000);
+  return threshold_upper(metric, kth_upper(D, err), err, window, qn2, rnq);
 }
 
 // Arguments of the per-query selection kernels (tighten, finalize).
@@ -368,6 +381,7 @@ struct SelectLaunch {
   uint32_t out_cap;
   int64_t first_id;
   int index_form;           // L2 distances in the loaded-index form (FP32 sqrtf)
+  double *upper;            // survivors: each query's bound U of its k-th exact distance (NaN: none), or NULL
 };
 
 // ---------------------------------------------------------------- launchers
@@ -415,6 +429,11 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
                       int window, const QueryState &qs, cudaStream_t st);
 void launch_tighten(const SelectLaunch &l, cudaStream_t st);
 void launch_survivors(const SelectLaunch &l, cudaStream_t st);
+// Second cut of a sharded search's survivors: every rank's bounds U
+// ([nranks][ld] doubles, NaN where a rank has none) -> the smallest, and each
+// query keeps only the survivors that can beat it.
+void launch_survivors_global(const SelectLaunch &l, const double *upper_all, uint32_t nranks, uint32_t ld,
+                             cudaStream_t st);
 cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t st);
 void launch_finalize_big(const SelectLaunch &l, uint32_t q, unsigned long long *key, unsigned long long *pos,
                          uint32_t p2, cudaStream_t st);

@@ -413,9 +413,12 @@ struct PrepArgs {
 //   |acc - dot| <= gamma*||x||*||q16|| + ||x||*||q - q16|| + FP32 epilogue
 // rounding, with ||x|| <= sqrt(maxn2); the L2 bound also covers the rounding
 // of the reference's own FP32 eight-lane sum.
+constexpr uint32_t kPrepSqMax = 6144;   // dims whose squares fit the kernel's shared memory (48 KB)
+
 __global__ void prep_queries(PrepArgs p) {
   const uint32_t q = blockIdx.x;
   const float *qv = p.queries + (uint64_t)q * p.dims;
+  extern __shared__ double sq[];   // x[d]^2 (exact in FP64) when dims <= kPrepSqMax
   __shared__ double red[4][32];
   __shared__ int bad;
   __shared__ float s_scale;
@@ -484,6 +487,7 @@ __global__ void prep_queries(PrepArgs p) {
       r2 += ((double)x - hx) * ((double)x - hx);
     }
     n2 += (double)x * (double)x;
+    if (d < p.dims && p.dims <= kPrepSqMax) sq[d] = __dmul_rn((double)x, (double)x);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -508,9 +512,14 @@ __global__ void prep_queries(PrepArgs p) {
     n2 += red[2][w];
     l2 += red[3][w];
   }
-  // the reference's query norm: FP64, dimension order (cpu.c:96-101)
+  // the reference's query norm: FP64, dimension order (cpu.c:96-101); the
+  // squares (exact: FP32 x FP32 fits FP64) were formed in parallel above,
+  // only the ordered sum is serial
   double qn = 0.0;
-  for (uint32_t d = 0; d < p.dims; d++) qn = __dadd_rn(qn, __dmul_rn((double)qv[d], (double)qv[d]));
+  if (p.dims <= kPrepSqMax)
+    for (uint32_t d = 0; d < p.dims; d++) qn = __dadd_rn(qn, sq[d]);
+  else
+    for (uint32_t d = 0; d < p.dims; d++) qn = __dadd_rn(qn, __dmul_rn((double)qv[d], (double)qv[d]));
   if (!p.use_q16 && !p.f8) {
     t2 = n2;
     r2 = 0.0;
@@ -664,28 +673,13 @@ struct SelectArgs {
   uint32_t out_cap;
   int64_t first_id;
   int index_form;         // L2 distances in the loaded-index form (FP32 sqrtf)
+  double *upper;          // survivors: the bound U of each query's k-th exact distance (NaN: none), or NULL
 };
 
-// Lower a query's threshold with the k-th smallest v among its candidates and
-// drop the entries above it. Returns the survivor count (all threads).
-__device__ uint32_t tighten_one(const SelectArgs &a, uint32_t q, uint32_t c, uint32_t *hist, uint32_t *scratch,
-                                float *thr_out) {
+// Keep the entries of a candidate list (c entries at e) whose score is <= t,
+// in place. Returns the kept count (all threads).
+__device__ uint32_t compact_le(uint2 *e, uint32_t c, float t, uint32_t *scratch) {
   __shared__ uint32_t s_m;
-  __shared__ float s_thr;
-  uint2 *e = a.cand + (uint64_t)q * a.cap;
-  float t = a.qs.thr[q];
-  if (c > a.k) {
-    uint32_t key = block_radix_select([&](uint32_t i) { return float_key(__uint_as_float(e[i].x)); }, c, a.k, hist,
-                                      scratch);
-    if (threadIdx.x == 0) {
-      double rnq = (double)a.qs.rnq[q], qn2 = a.qs.qn2d[q];
-      float v = key_float(key);
-      float t2 = threshold_v(a.metric, v_to_dist(a.metric, (double)v, qn2, rnq), a.qs.err[q], a.window, qn2, rnq);
-      s_thr = t2 < t ? t2 : t;
-    }
-    __syncthreads();
-    t = s_thr;
-  }
   if (threadIdx.x == 0) s_m = 0;
   __syncthreads();
   for (uint32_t base = 0; base < c; base += blockDim.x) {
@@ -704,8 +698,35 @@ __device__ uint32_t tighten_one(const SelectArgs &a, uint32_t q, uint32_t c, uin
     if (threadIdx.x == 0) s_m = m0 + total;
     __syncthreads();
   }
-  *thr_out = t;
   return s_m;
+}
+
+// Lower a query's threshold with the k-th smallest v among its candidates and
+// drop the entries above it. Returns the survivor count (all threads);
+// *upper_out (thread 0, when given) gets the bound U of the k-th exact
+// distance those candidates give (NaN when there are not more than k).
+__device__ uint32_t tighten_one(const SelectArgs &a, uint32_t q, uint32_t c, uint32_t *hist, uint32_t *scratch,
+                                float *thr_out, double *upper_out = nullptr) {
+  __shared__ float s_thr;
+  uint2 *e = a.cand + (uint64_t)q * a.cap;
+  float t = a.qs.thr[q];
+  if (upper_out && threadIdx.x == 0) *upper_out = __longlong_as_double(0x7ff8000000000000ll);
+  if (c > a.k) {
+    uint32_t key = block_radix_select([&](uint32_t i) { return float_key(__uint_as_float(e[i].x)); }, c, a.k, hist,
+                                      scratch);
+    if (threadIdx.x == 0) {
+      double rnq = (double)a.qs.rnq[q], qn2 = a.qs.qn2d[q];
+      float v = key_float(key);
+      const double D = v_to_dist(a.metric, (double)v, qn2, rnq);
+      float t2 = threshold_v(a.metric, D, a.qs.err[q], a.window, qn2, rnq);
+      s_thr = t2 < t ? t2 : t;
+      if (upper_out && D < __longlong_as_double(0x7ff0000000000000ll)) *upper_out = kth_upper(D, a.qs.err[q]);
+    }
+    __syncthreads();
+    t = s_thr;
+  }
+  *thr_out = t;
+  return compact_le(e, c, t, scratch);
 }
 
 __global__ void __launch_bounds__(NT) tighten(SelectArgs a) {
@@ -796,10 +817,12 @@ __global__ void __launch_bounds__(NT) survivors(SelectArgs a) {
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t scratch[32];
   const uint32_t q = blockIdx.x;
+  const double none = __longlong_as_double(0x7ff8000000000000ll);
   if (a.qs.status[q]) {
     if (threadIdx.x == 0) {
       a.cnt[q] = 0;
       a.out_count[q] = 0;
+      if (a.upper) a.upper[q] = none;
     }
     return;
   }
@@ -810,11 +833,12 @@ __global__ void __launch_bounds__(NT) survivors(SelectArgs a) {
       atomicMax(a.flags + 1, c);
       a.cnt[q] = 0;
       a.out_count[q] = 0;
+      if (a.upper) a.upper[q] = none;
     }
     return;
   }
   float t;
-  const uint32_t m = tighten_one(a, q, c, hist, scratch, &t);
+  const uint32_t m = tighten_one(a, q, c, hist, scratch, &t, a.upper ? a.upper + q : nullptr);
   if (threadIdx.x == 0) {
     atomicAdd(a.flags + 3, c);   // statistics: candidates and survivors
     atomicAdd(a.flags + 4, m);
@@ -827,6 +851,30 @@ __global__ void __launch_bounds__(NT) survivors(SelectArgs a) {
     } else {
       a.cnt[q] = m;
     }
+  }
+}
+
+// The sharded search's second cut: the smallest of every rank's bounds U of
+// the query's k-th exact distance bounds the merged answer's k-th distance
+// too, so a survivor whose approximate score cannot reach it is dropped
+// here instead of being re-scored, sorted and sent. A query keeps its local
+// cut when no rank has a bound (NaN everywhere), and queries left to the
+// large sort or to a new pass (count 0) are untouched.
+__global__ void __launch_bounds__(NT) survivors_global(SelectArgs a, const double *upper_all, uint32_t nranks,
+                                                       uint32_t ld) {
+  __shared__ uint32_t scratch[32];
+  const uint32_t q = blockIdx.x;
+  if (a.qs.status[q]) return;
+  const uint32_t m = a.cnt[q];
+  if (m == 0) return;
+  double U = __longlong_as_double(0x7ff8000000000000ll);
+  for (uint32_t r = 0; r < nranks; r++) U = fmin(U, upper_all[(uint64_t)r * ld + q]);   // NaN: no bound
+  if (!(U < __longlong_as_double(0x7ff0000000000000ll))) return;
+  const float t = threshold_upper(a.metric, U, a.qs.err[q], a.window, a.qs.qn2d[q], (double)a.qs.rnq[q]);
+  const uint32_t m2 = compact_le(a.cand + (uint64_t)q * a.cap, m, t, scratch);
+  if (threadIdx.x == 0) {
+    a.cnt[q] = m2;
+    atomicSub(a.flags + 4, m - m2);   // statistics: survivors
   }
 }
 
@@ -1483,7 +1531,7 @@ void launch_prep_queries(const float *queries, uint32_t nq, uint32_t dims, uint3
     return;
   }
   PrepArgs p{queries, nq, dims, metric, kpad, use_q16, lo_off, gamma, maxn2, qs, flags, f8};
-  prep_queries<<<nq, 256, 0, st>>>(p);
+  prep_queries<<<nq, 256, dims <= kPrepSqMax ? dims * sizeof(double) : 0, st>>>(p);
 }
 
 void launch_fill_thresholds(uint32_t nq, const QueryState &qs, cudaStream_t st) {
@@ -1503,13 +1551,18 @@ void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, ui
 static SelectArgs to_args(const SelectLaunch &l) {
   SelectArgs a{l.s,   l.staged, l.row_ids, l.ids,   l.queries, l.nq,  l.k,        l.metric,   l.window,    l.qbytes,   l.qs,
                l.cnt, l.cand,  l.cap,     l.flags, l.big,    l.out_dist, l.out_id,    l.out_count, l.out_cap,
-               l.first_id, l.index_form};
+               l.first_id, l.index_form, l.upper};
   return a;
 }
 
 void launch_tighten(const SelectLaunch &l, cudaStream_t st) { tighten<<<l.nq, NT, 0, st>>>(to_args(l)); }
 
 void launch_survivors(const SelectLaunch &l, cudaStream_t st) { survivors<<<l.nq, NT, 0, st>>>(to_args(l)); }
+
+void launch_survivors_global(const SelectLaunch &l, const double *upper_all, uint32_t nranks, uint32_t ld,
+                             cudaStream_t st) {
+  survivors_global<<<l.nq, NT, 0, st>>>(to_args(l), upper_all, nranks, ld);
+}
 
 // Exact rescoring of the survivors (flat grid) and the per-query ordering.
 cudaError_t launch_finalize(const SelectLaunch &l, double *exact, cudaStream_t st) {

@@ -131,13 +131,16 @@ bool debug_on() {
   return on;
 }
 
-bool timing_on() {
-  static const int on = [] {
+// Stage timing: ANN_B200_KERNEL_TIMING at the first call, then AnnB200StageTiming.
+std::atomic<int> &timing_state() {
+  static std::atomic<int> on([] {
     const char *v = getenv("ANN_B200_KERNEL_TIMING");
-    return v && *v && *v != '0';
-  }();
+    return (v && *v && *v != '0') ? 1 : 0;
+  }());
   return on;
 }
+
+bool timing_on() { return timing_state().load(std::memory_order_relaxed) != 0; }
 
 // Recorded stage spans whose events have not been read yet. A call never
 // waits for its stage events: they are read once complete -- at the start of
@@ -629,17 +632,44 @@ int big_sorts(AnnB200Shard *sh, const SelectLaunch &sl, const uint32_t *big, uin
   return OK;
 }
 
+// The bounds exchange in the middle of a deferred sharded search. Each
+// query block's survivors kernel writes this rank's bound U of every
+// query's k-th exact distance (from its own candidates), one all-gather
+// shares them, and survivors_global cuts every rank's survivors again at
+// the smallest: with R ranks a rank then re-scores, sorts and sends about
+// k / R survivors a query instead of k. Every rank takes part in exactly one
+// exchange a query block whatever happens to its own search -- a block that
+// failed, or had nothing to search, sends NaN (no bound) -- so the ranks'
+// collectives stay paired.
+struct BoundsExchange {
+  AnnB200Comm *comm;
+  uint32_t nq;         // doubles a rank sends: the largest query block
+  uint32_t done = 0;   // exchanges taken part in
+  double *send() const { return comm->bounds; }
+  double *recv() const { return comm->bounds + nq; }
+  int run(cudaStream_t st) {
+    done++;
+    return comm_allgather(comm, send(), recv(), (size_t)nq * sizeof(double), st);
+  }
+  int skip(cudaStream_t st) {
+    cudaMemsetAsync(send(), 0xff, (size_t)nq * sizeof(double), st);   // all-ones bytes: NaN
+    return run(st);
+  }
+};
+
 // One search over queries [q0, q0+nq) (nq within one tensor-scan launch).
 //
 // defer_flags (device, 8 words) selects the deferred form the sharded search
 // uses: everything is enqueued on st with no host synchronisation, and the
 // search's flag words are copied to defer_flags when its kernels end; the
 // caller inspects them later and runs the search again synchronously if a
-// candidate list overflowed or a query needs the large sort.
+// candidate list overflowed or a query needs the large sort. A deferred
+// search with `bx` takes part in the bounds exchange once, between its
+// survivors and their exact re-score (or not at all if it ends earlier).
 int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint32_t *rows, uint64_t nrows,
                  uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
                  uint32_t *out_count, int32_t *status, cudaStream_t st, bool *any_invalid,
-                 uint32_t *defer_flags = nullptr) {
+                 uint32_t *defer_flags = nullptr, BoundsExchange *bx = nullptr) {
   const ShardView &v = sh->view;
   const bool bits = v.dtype == DT_BIT;
   const bool window = flags & ANNB200_WINDOW;
@@ -896,9 +926,21 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
           counted(1);
         }
       }
+      const bool mid = bx && defer_flags;
       h = clock.begin(ST_TIGHTEN);
+      sl.upper = mid ? bx->send() : nullptr;
       launch_survivors(sl, st);
       clock.end(h);
+      if (mid) {
+        h = clock.begin(ST_MERGE);
+        int r = bx->run(st);
+        clock.end(h);
+        if (r != OK) return r;
+        h = clock.begin(ST_TIGHTEN);
+        launch_survivors_global(sl, bx->recv(), (uint32_t)bx->comm->nranks, bx->nq, st);
+        clock.end(h);
+        counted(1);
+      }
       h = clock.begin(ST_FINAL);
       CK(launch_finalize(sl, exact, st), "finalize");
       clock.end(h);
@@ -1116,7 +1158,7 @@ struct Packet {
 // local status; the caller puts it in the header.
 int local_search(AnnB200Shard *sh, uint8_t *pk, const Packet &pl, const void *queries, uint32_t nq,
                  const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags, int32_t *status,
-                 cudaStream_t st, bool deferred) {
+                 cudaStream_t st, bool deferred, BoundsExchange *bx) {
   const ShardView &v = sh->view;
   const uint32_t block = tc_scan_max_queries();
   const uint64_t qbytes = v.dtype == DT_BIT ? v.row_bytes : (uint64_t)v.dims * 4;
@@ -1126,8 +1168,13 @@ int local_search(AnnB200Shard *sh, uint8_t *pk, const Packet &pl, const void *qu
     int r = search_block(sh, (const uint8_t *)queries + q0 * qbytes, m, rows, nrows, k, metric, flags, k,
                          (double *)(pk + pl.dist) + (uint64_t)q0 * k, (int64_t *)(pk + pl.ids) + (uint64_t)q0 * k,
                          (uint32_t *)(pk + pl.counts) + q0, status ? status + q0 : nullptr, st, &any_invalid,
-                         deferred ? (uint32_t *)(pk + 16 + 32 * b) : nullptr);
+                         deferred ? (uint32_t *)(pk + 16 + 32 * b) : nullptr, deferred ? bx : nullptr);
     if (r != OK) return r;
+    // a block that ended before its exchange (nothing to search) still takes part
+    while (deferred && bx && bx->done < b + 1) {
+      r = bx->skip(st);
+      if (r != OK) return r;
+    }
   }
   if (any_invalid) return fail(INVALID, "a query is not finite, or has zero norm under cosine");
   return OK;
@@ -1137,13 +1184,16 @@ int local_search(AnnB200Shard *sh, uint8_t *pk, const Packet &pl, const void *qu
 
 namespace {
 
-// The exchange both sharded searches share: `local(pk, deferred)` searches
-// this rank's shard into its packet (deferred: enqueued only, flags to the
-// header) and returns a local status; `local_ok` is this rank's argument
-// check. See AnnB200SearchSharded.
+// The exchange both sharded searches share: `local(pk, deferred, bx)`
+// searches this rank's shard into its packet (deferred: enqueued only, flags
+// to the header) and returns a local status; `local` is this rank's argument
+// check. A deferred local search that uses the bounds exchange takes part in
+// `bound_blocks` of them (bx); whichever it did not reach run here, with no
+// bounds, so that every rank's collectives pair up. See AnnB200SearchSharded.
 template <typename Local>
 int sharded_exchange(AnnB200Shard *sh, AnnB200Comm *comm, int local, uint32_t nq, uint32_t k, uint32_t out_cap,
-                     double *out_dist, int64_t *out_id, uint32_t *out_count, cudaStream_t st, Local local_fn) {
+                     double *out_dist, int64_t *out_id, uint32_t *out_count, cudaStream_t st, uint32_t bound_blocks,
+                     uint32_t bound_nq, Local local_fn) {
   if (nq == 0) return local;        // every rank sees the same nq: no exchange at all
   DeviceGuard g(sh->device);
   std::lock_guard<std::mutex> lock_comm(comm->mu);
@@ -1152,17 +1202,24 @@ int sharded_exchange(AnnB200Shard *sh, AnnB200Comm *comm, int local, uint32_t nq
   // without room for the exchange this rank cannot join it: the others end
   // by the communicator's time limit
   int r = comm_reserve(comm, pl.bytes, kHead);
+  if (r == OK && bound_blocks) r = comm_reserve_bounds(comm, bound_nq);
   if (r != OK) return r;
   uint8_t *pk = (uint8_t *)comm->send;
   const uint8_t *all = (const uint8_t *)comm->recv;
   std::string local_msg;
   for (int round = 0; round < 2; round++) {
     CK(cudaMemsetAsync(pk, 0, pl.dist, st), "memset");       // header and counts
+    BoundsExchange bx{comm, bound_nq};
     if (local == OK) {
-      local = local_fn(pk, pl, round == 0);
+      local = local_fn(pk, pl, round == 0, bound_blocks ? &bx : nullptr);
       if (local != OK) CK(cudaMemsetAsync(pk, 0, pl.dist, st), "memset");
     }
     if (local != OK) local_msg = g_error;
+    if (round == 0)
+      while (bx.done < bound_blocks) {
+        r = bx.skip(st);
+        if (r != OK) return r;   // this rank's NCCL failed: the others end by the time limit
+      }
     *comm->host_status = local;
     CK(cudaMemcpyAsync(pk, comm->host_status, 4, cudaMemcpyHostToDevice, st), "status");
     StageClock clock(st);
@@ -1236,10 +1293,12 @@ extern "C" int AnnB200SearchSharded(AnnB200Shard *sh, AnnB200Comm *comm, const v
     local = fail(UNSUPPORTED, "ranks x k must not exceed %d", kSortCap);
   else if (nq > kShardBlocks * tc_scan_max_queries())
     local = fail(UNSUPPORTED, "at most %u queries a sharded call", kShardBlocks * tc_scan_max_queries());
+  const uint32_t block = tc_scan_max_queries();
   return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream,
-                          [&](uint8_t *pk, const Packet &pl, bool deferred) {
+                          (nq + block - 1) / block, std::min(nq, block),
+                          [&](uint8_t *pk, const Packet &pl, bool deferred, BoundsExchange *bx) {
                             return local_search(sh, pk, pl, queries, nq, rows, nrows, k, metric, flags, status,
-                                                (cudaStream_t)stream, deferred);
+                                                (cudaStream_t)stream, deferred, bx);
                           });
 }
 
@@ -1536,8 +1595,8 @@ extern "C" int AnnB200SearchListsSharded(AnnB200Shard *sh, AnnB200Comm *comm, co
     local = fail(UNSUPPORTED, "ranks x k must not exceed %d", kSortCap);
   // the list search synchronises on its own (its windows): the exchange's
   // header carries only its status
-  return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream,
-                          [&](uint8_t *pk, const Packet &pl, bool) {
+  return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream, 0, 0,
+                          [&](uint8_t *pk, const Packet &pl, bool, BoundsExchange *) {
                             return search_lists_all(sh, queries, nq, list_offsets, nlists, probes, nprobe, row_ids, k,
                                                     metric, flags, k, (double *)(pk + pl.dist),
                                                     (int64_t *)(pk + pl.ids), (uint32_t *)(pk + pl.counts), status,
@@ -1630,10 +1689,25 @@ int bitmap_rows_at(const uint32_t *words, uint64_t nbits, uint32_t base, uint32_
   clock.end(h);
   counted(3);
   CK(cudaGetLastError(), "bitmap rows");
-  unsigned long long found = 0;
-  CK(cudaMemcpyAsync(&found, total, 8, cudaMemcpyDeviceToHost, st), "bitmap count");
+  // the count comes back through pinned memory: a pageable destination
+  // costs the copy a staging pass through the driver
+  struct PinnedCount {
+    unsigned long long *p = nullptr;
+    PinnedCount() {
+      void *v = nullptr;
+      if (cudaMallocHost(&v, 8) == cudaSuccess) p = (unsigned long long *)v;
+      else cudaGetLastError();
+    }
+    ~PinnedCount() {
+      if (p) cudaFreeHost(p);
+    }
+  };
+  static thread_local PinnedCount found;
+  unsigned long long pageable = 0;
+  unsigned long long *dst = found.p ? found.p : &pageable;
+  CK(cudaMemcpyAsync(dst, total, 8, cudaMemcpyDeviceToHost, st), "bitmap count");
   CK(cudaStreamSynchronize(st), "bitmap rows");
-  *count = found;
+  *count = *dst;
   return OK;
 }
 
@@ -1650,6 +1724,11 @@ extern "C" int AnnB200BitmapRowsFrom(const uint32_t *words, uint64_t nbits, uint
 }
 
 extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(); }
+
+extern "C" int AnnB200StageTiming(int on) {
+  if (on < 0) return timing_on() ? 1 : 0;
+  return timing_state().exchange(on ? 1 : 0);
+}
 
 extern "C" int AnnB200StageTimes(double *ms, unsigned long long *calls, uint32_t n, int reset) {
   collect_spans(true);

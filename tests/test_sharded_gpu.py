@@ -100,6 +100,15 @@ def free_port():
 
 
 ROWS, DIMS, NQ, K = 60000, 192, 200, 64
+# two query blocks (the tensor scan takes 4,096 queries a launch), each with
+# its own exchange of bounds between the ranks
+MB_ROWS, MB_DIMS, MB_NQ, MB_K = 6000, 64, 4100, 16
+
+
+def multi_block_case():
+    x = synth.mixture(MB_ROWS, MB_DIMS, 20, seed=24)
+    q = synth.mixture_queries(MB_NQ, MB_DIMS, 20, seed=25)
+    return x, q
 
 
 def two_gpu_case():
@@ -143,6 +152,18 @@ def two_gpu_worker(rank, world, port, out, missing):
             d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=rows)
             torch.cuda.synchronize()
             out[rank] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+            # rank 1 has no candidate rows: its search ends before the bounds
+            # exchange, which it still takes part in
+            mine = rows if rank == 0 else rows[:0]
+            d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=mine)
+            out[(rank, 'empty')] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+            # two query blocks over an unfiltered FP32 shard
+            x, q2 = multi_block_case()
+            b2 = sharded.shard_bounds(MB_ROWS, world)
+            s2 = pb.Shard(pb.F32, MB_DIMS, to_dev(x[b2[rank]:b2[rank + 1]], dev), first_id=b2[rank])
+            d, i, c = s2.search_sharded(comm, to_dev(q2, dev), MB_K, pb.L2)
+            out[(rank, 'blocks')] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+            s2.close()
             dist.barrier()
         shard.close()
     finally:
@@ -170,10 +191,15 @@ def test_two_gpu_sharded_search_equals_whole(cuda):
     out = run_two(False)
     h, q, _, ids = two_gpu_case()
     od, oi, oc, _ = oracle.search(oracle.F16, DIMS, h, q, K, 2, ids=ids)
+    half = sharded.shard_bounds(ROWS, 2)[1]
+    ed, ei, ec, _ = oracle.search(oracle.F16, DIMS, h, q, K, 2, ids=ids[ids < half])
+    x, q2 = multi_block_case()
+    md, mi, mc, _ = oracle.search(oracle.F32, MB_DIMS, x, q2, MB_K, 0)
     for r in range(2):
-        d, i, c = out[r]
-        assert np.array_equal(c, oc.astype(c.dtype))
-        assert np.array_equal(i, oi) and np.array_equal(d, od)
+        for (d, i, c), (wd, wi, wc) in ((out[r], (od, oi, oc)), (out[(r, 'empty')], (ed, ei, ec)),
+                                        (out[(r, 'blocks')], (md, mi, mc))):
+            assert np.array_equal(c, wc.astype(c.dtype))
+            assert np.array_equal(i, wi) and np.array_equal(d, wd)
 
 
 def test_two_gpu_missing_rank_times_out(cuda):
