@@ -117,6 +117,33 @@ typedef struct AnnIndexJob
 } AnnIndexJob;
 
 /* The backend vtable, in the reference's positional order (backend.h:114-151). */
+/*
+ * A typed gathered job (the typed search operation, number 32, that a worker
+ * built with it dispatches): host rows in a storage format (0 FP32, 1 FP16,
+ * 2 FP8-E4M3 + row scales, 3 NVFP4 + block and row scales, 4 bits) and a
+ * batch of queries, answered with each query's gathered-job window. The
+ * layout is AnnB200TypedJob's (annb200.h).
+ */
+typedef struct AnnTypedJob
+{
+	uint32_t	dtype;
+	uint32_t	metric;			/* 0 L2, 1 negative inner product, 2 cosine, 3 Hamming */
+	uint32_t	dimensions;
+	uint32_t	rows;
+	uint32_t	nq;
+	uint32_t	k;
+	uint32_t	cap;			/* result room a query */
+	uint32_t	reserved;
+	const void *queries;		/* FP32 [nq][dimensions]; Hamming: [nq][ceil(dimensions / 8)] bytes */
+	const void *codes;
+	const void *block_scales;
+	const float *row_scales;
+	double	   *distances;		/* [nq][cap] */
+	uint32_t   *ids;			/* [nq][cap] */
+	uint32_t   *nresults;		/* [nq] */
+	int			status;
+} AnnTypedJob;
+
 typedef struct AnnBackend
 {
 	const char *name;
@@ -138,6 +165,12 @@ typedef struct AnnBackend
 	void		(*search_index) (AnnIndexJob *, uint32_t);
 	const char *(*lost) (void);
 	int			(*scan_preferred) (const struct AnnIndexFile *file, uint32_t k);
+	/*
+	 * An addition after the reference's last slot: typed gathered jobs for
+	 * the typed search operation; sets each job's status. A worker built
+	 * without the operation never reads it.
+	 */
+	void		(*search_typed) (AnnTypedJob *, uint32_t);
 } AnnBackend;
 
 #define ANN_EXIT_DEVICE_LOST 70

@@ -41,6 +41,9 @@ def build(reference=None):
         subprocess.run(['make', '-s', '-C', HERE, 'ref', 'REF=' + ref], check=True)
         if os.path.exists(os.path.join(os.path.dirname(HERE), 'pgvector_b200', 'libannb200.so')):
             subprocess.run(['make', '-s', '-C', HERE, 'worker', 'REF=' + ref], check=True)
+            # the reference worker with the typed search operation (both backends)
+            from . import worker_typed
+            worker_typed.build(ref)
 
 
 def lib():

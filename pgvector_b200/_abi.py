@@ -70,4 +70,6 @@ class AnnBackend(ctypes.Structure):
                 ('min_rows', ctypes.c_uint32), ('max_k', ctypes.c_uint32), ('build', BUILD), ('search', SEARCH),
                 ('destroy', DESTROY), ('search_gathered', SEARCH_GATHERED), ('device_jobs', ctypes.c_void_p),
                 ('load_index', ctypes.c_void_p), ('search_index', ctypes.c_void_p), ('lost', ctypes.c_void_p),
-                ('scan_preferred', ctypes.c_void_p)]
+                ('scan_preferred', ctypes.c_void_p),
+                # after the reference's last slot: the typed search operation's jobs
+                ('search_typed', ctypes.c_void_p)]

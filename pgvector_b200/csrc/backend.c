@@ -2204,12 +2204,26 @@ Lost(void)
 	return NULL;
 }
 
+/*
+ * The typed search operation's jobs: AnnTypedJob is AnnB200TypedJob's layout
+ * (checked below), so the worker's jobs are searched in place.
+ */
+_Static_assert(sizeof(AnnTypedJob) == sizeof(AnnB200TypedJob), "typed job layout");
+_Static_assert(offsetof(AnnTypedJob, queries) == offsetof(AnnB200TypedJob, queries), "typed job layout");
+_Static_assert(offsetof(AnnTypedJob, status) == offsetof(AnnB200TypedJob, status), "typed job layout");
+
+static void
+SearchTypedJobs(AnnTypedJob *jobs, uint32_t count)
+{
+	(void) AnnB200SearchTyped((AnnB200TypedJob *) jobs, count);
+}
+
 const AnnBackend *
 AnnB200Backend(void)
 {
 	static const AnnBackend backend = {
 		"b200", 7, 7, "flat", "fp32", 1, 0, UINT32_MAX, Build, Search, Destroy,
-		SearchGathered, DeviceJobCount, NULL, NULL, Lost, NULL
+		SearchGathered, DeviceJobCount, NULL, NULL, Lost, NULL, SearchTypedJobs
 	};
 
 	return &backend;

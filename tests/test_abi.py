@@ -53,8 +53,10 @@ def test_backend_vtable_matches_worker_layout():
     assert b.algorithm == b'flat' and b.storage == b'fp32'
     assert b.device_jobs and b.lost
     assert not b.load_index and not b.search_index and not b.scan_preferred
-    # positional layout: 17 slots, pointers after the 8 scalar fields
-    assert ctypes.sizeof(_abi.AnnBackend) == 8 * 3 + 4 * 2 + 4 + 4 * 2 + 8 * 9 + 4
+    assert b.search_typed
+    # positional layout: the reference's 17 slots, pointers after the 8
+    # scalar fields, then the typed search slot
+    assert ctypes.sizeof(_abi.AnnBackend) == 8 * 3 + 4 * 2 + 4 + 4 * 2 + 8 * 9 + 4 + 8
 
 
 def test_gathered_job_struct_layout():
