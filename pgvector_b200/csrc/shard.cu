@@ -375,6 +375,17 @@ double scan_gamma(bool bits, bool tc, uint32_t kpad, uint32_t dims, bool split =
 constexpr uint64_t kChunkRows = 589824;     // most rows one gathered tensor-scan chunk covers
 constexpr uint64_t kNoSampleRows = 32768;  // at most this many candidates: no sample pass
 constexpr uint64_t kSampleRows = 16384;    // sample size of the bound
+
+// The bound's sample size: kSampleRows, or ANN_B200_SAMPLE_ROWS (a tuning
+// knob, at least 1,024), read once.
+uint64_t sample_rows() {
+  static const uint64_t n = [] {
+    const char *v = getenv("ANN_B200_SAMPLE_ROWS");
+    const long long x = v && *v ? atoll(v) : 0;
+    return x >= 1024 ? (uint64_t)x : kSampleRows;
+  }();
+  return n;
+}
 constexpr uint32_t kBaseCap = 16384;       // initial candidate capacity a query
 
 }  // namespace
@@ -689,7 +700,7 @@ int search_block(AnnB200Shard *sh, const void *queries, uint32_t nq, const uint3
   // score sits near the 16k-th row either way), and the sample scan and its
   // selection are fixed costs of every rank
   const bool sample = k > 0 && n > kNoSampleRows;
-  const uint64_t target = std::min<uint64_t>(std::max<uint64_t>(kSampleRows, 8ull * k),
+  const uint64_t target = std::min<uint64_t>(std::max<uint64_t>(sample_rows(), 8ull * k),
                                              std::max<uint64_t>(8ull * k, n / 16));
   const uint64_t stride = sample ? std::max<uint64_t>(1, n / target) : 1;
   const uint64_t S = sample ? n / stride : 0;
