@@ -226,6 +226,33 @@ class ClockSampler:
 METRIC_CODE = {1: 0, 2: 2, 3: 1, 4: 0, 5: 3}   # L2, cosine, inner product, L2, Hamming
 
 
+def cpu_sample_device(args, rows, queries):
+    """Config 2's host sample made on the GPU (numpy takes minutes for a
+    million 768-d rows): `rows` rows of the bench's own seeded mixture,
+    unit-normalised and rounded to FP16 as the shard stores them, copied to
+    host memory as FP32, and `queries` of its queries. Only the data is made
+    on the device; the timed work runs on the host cores."""
+    import numpy as np
+    import torch
+    dev = torch.device('cuda', torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed)
+    centres = torch.randn((args.centres, args.dims), generator=g, device=dev)
+    x = np.empty((rows, args.dims), np.float32)
+
+    def fill(a, b, v):
+        x[a:b] = v.to(torch.float16).to(torch.float32).cpu().numpy()
+    mixture_rows(args, dev, 0, rows, centres, fill, normalize=True)
+    g.manual_seed(args.seed + 7919)
+    lab = torch.randint(0, args.centres, (queries,), generator=g, device=dev)
+    qv = centres[lab] + 0.1 * torch.randn((queries, args.dims), generator=g, device=dev)
+    qv /= qv.norm(dim=1, keepdim=True)
+    q = qv.to(torch.float16).to(torch.float32).cpu().numpy()
+    del centres, qv
+    torch.cuda.empty_cache()
+    return x, q
+
+
 def cpu_sample(args, rows, queries):
     """A bounded host sample of the workload's distribution: `rows` rows
     decoded to FP32 exactly as the device format stores them (config 5: the
@@ -233,6 +260,13 @@ def cpu_sample(args, rows, queries):
     import numpy as np
     import oracle
     from pgvector_b200 import synth
+    if args.config == 2 and rows > 100_000:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return cpu_sample_device(args, rows, queries)
+        except ImportError:
+            pass
     if args.config == 5:
         x, proto = synth.bit_rows(rows, args.dims, args.centres, flip=0.05, seed=args.seed)
         rng = np.random.default_rng(args.seed + 7919)
@@ -319,8 +353,12 @@ def ivf_cpu_run(sample, args, threads, budget_s=None, count=None):
 _SAMPLES = {}
 
 
-def cpu_measure(args, threads, budget_s=None, count=None):
-    """(queries/s at full size, sample description, kind) of the host path."""
+def cpu_measure(args, threads, budget_s=None, count=None, rows=None):
+    """(queries/s at full size, sample description, kind) of the host path.
+    `rows`: candidate rows a query of the sample scans (default: config 1's
+    whole corpus, config 2's whole candidate set; a sample of the others,
+    whose corpora do not fit host memory); the rate is scaled linearly to the
+    full candidate count when they are fewer."""
     if args.config == 4:
         rows = 200_000
         if 4 not in _SAMPLES:
@@ -331,15 +369,21 @@ def cpu_measure(args, threads, budget_s=None, count=None):
                 'the per-query work equals the full configuration\'s' %
                 (done, args.k, args.nprobe, rows // max(1, len(sample[3]) - 1), secs, threads))
         return done / secs, desc, kind
-    rows = {1: args.rows, 2: 50_000, 5: 200_000}.get(args.config, 20_000)   # config 1: the whole corpus
-    if args.config not in _SAMPLES:
+    full = full_candidates(args)
+    if rows is None:
+        rows = {1: args.rows, 2: full, 5: 200_000}.get(args.config, 20_000)
+    have = _SAMPLES.get(args.config)
+    if have is None or have[0].shape[0] < rows:
         _SAMPLES[args.config] = cpu_sample(args, rows, 64)
     x, q = _SAMPLES[args.config]
+    x = x[:rows]          # leading rows: a contiguous view
     done, secs, kind = cpu_run(x, q, args.k, threads, METRIC_CODE[args.config], budget_s=budget_s, count=count)
-    full = full_candidates(args)
     desc = ('%d gathered jobs (metric %d, k=%d) over %d candidate rows of the config-%d distribution in %.1f s on '
-            '%d threads, scaled linearly to %d candidate rows' %
-            (done, METRIC_CODE[args.config], args.k, rows, args.config, secs, threads, full))
+            '%d threads' % (done, METRIC_CODE[args.config], args.k, rows, args.config, secs, threads))
+    if rows != full:
+        desc += ', scaled linearly to %d candidate rows (x%.2f)' % (full, full / rows)
+    else:
+        desc += ' (the full configuration\'s candidate set: no scaling)'
     return done / secs * rows / full, desc, kind
 
 
@@ -357,27 +401,62 @@ def reference_arm(args):
         return 0
     threads = os.cpu_count() or 1
     per_step = max(threads, 8)
+    rows = None
+    if args.config == 2:
+        # each step: per_step queries over the whole candidate set when such a
+        # step fits the run's budget (all steps within about two minutes),
+        # else over the largest leading sample of it that does, scaled
+        full = full_candidates(args)
+        cpu_sample_cached(args, full)
+        probe = min(full, 100_000)
+        qps_p, _, _ = cpu_measure(args, threads, count=per_step, rows=probe)
+        est_full = per_step / (qps_p * full / probe) * full / probe     # seconds a full-size step
+        budget = min(4.0, 120.0 / max(1, args.steps + args.warmup))
+        rows = full if est_full <= budget else max(probe, int(full * budget / est_full))
     for _ in range(args.warmup):
-        cpu_measure(args, threads, count=per_step)
-    rates, desc, kind = [], '', 'reference'
+        cpu_measure(args, threads, count=per_step, rows=rows)
+    rates, desc, kind, walls = [], '', 'reference', []
     for _ in range(args.steps):
-        qps, desc, kind = cpu_measure(args, threads, count=per_step)
+        t0 = time.perf_counter()
+        qps, desc, kind = cpu_measure(args, threads, count=per_step, rows=rows)
+        walls.append(time.perf_counter() - t0)
         rates.append(qps)
     qps = len(rates) / sum(1.0 / r for r in rates)
     line = {'metric': METRIC, 'value': qps, 'unit': 'queries/s', 'n_gpus': args.gpus, 'steps': args.steps,
-            'warmup': args.warmup, 'ms_per_step': args.batch / qps * 1e3,
+            'warmup': args.warmup, 'ms_per_step': 1e3 * sum(walls) / len(walls),
+            'step': '%d queries a step on %d host threads (the CPU serves them one a thread)' % (per_step, threads),
             'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f64',
             'data': 'synthetic (seeded Gaussian mixture of the configuration)',
-            'config': {'workload': WORKLOADS[args.config], 'global_batch': args.batch, 'rows': args.rows,
-                       'dims': args.dims, 'k': args.k, 'parallelism': 'host threads'},
+            'config': workload_config(args), 'parallelism': '%d host threads' % threads,
             'impl': 'reference',
             'cpu_baseline': {'value': qps, 'unit': 'queries/s', 'cores': threads, 'kind': kind,
                              'sample': '%d queries a step: %s' % (per_step, desc)},
             'e2e': {'value': qps, 'unit': 'queries/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
-    if args.config == 2:
-        line['config']['selectivity'] = args.selectivity
     print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_sample_cached(args, rows):
+    if args.config not in _SAMPLES or _SAMPLES[args.config][0].shape[0] < rows:
+        _SAMPLES[args.config] = cpu_sample(args, rows, 64)
+
+
+def workload_config(args):
+    """The `config` of both arms' lines: the workload, nothing of the
+    implementation (that goes in `parallelism`)."""
+    cfg = {'workload': WORKLOADS[args.config], 'global_batch': args.batch, 'rows': args.rows, 'dims': args.dims,
+           'k': args.k}
+    if args.config == 2:
+        cfg['selectivity'] = args.selectivity
+    if args.config == 4:
+        cfg.update({'nlist': args.centres, 'nprobe': args.nprobe})
+    row_bytes = {1: args.dims * 4, 2: args.dims * 2 + 4, 3: (args.dims + 15) // 16 * 16 + 4,
+                 4: args.dims // 2 + args.dims // 16 + 4, 5: args.dims // 8}.get(args.config, args.dims * 4)
+    gb = full_candidates(args) * row_bytes / 1e9
+    cfg['l2'] = ('inputs larger than L2: about %.2f GB of candidate rows a step' % gb if gb > 0.126 else
+                 'inputs fit in L2 (%.0f MB): the GPU arm writes a 256 MB buffer before every step, its time '
+                 'included' % (gb * 1e3))
+    return cfg
 
 
 # ---------------------------------------------------------------- workloads
@@ -435,8 +514,6 @@ def build_config1(args, rank, world, dev):
     # the corpus (51 MB) fits in L2: every step first overwrites a buffer
     # twice L2's size, and that time is part of the step
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    w.l2 = 'inputs fit in L2 (%.0f MB): a 256 MB buffer is written before every step, its time included' % (
-        (hi - lo) * args.dims * 4 / 1e6)
 
     def step(q):
         flush.fill_(1)
@@ -1156,26 +1233,21 @@ def main():
 
     if rank == 0:
         cand = int(nrows_local) * world if args.config != 4 else None
-        cfg = {'workload': WORKLOADS[args.config], 'global_batch': args.batch, 'rows': args.rows, 'dims': args.dims,
-               'k': args.k}
-        if args.config == 2:
-            cfg['selectivity'] = args.selectivity
-        if args.config == 4:
-            cfg.update({'nlist': args.centres, 'nprobe': args.nprobe})
-        cfg['l2'] = getattr(w, 'l2', None) or 'inputs larger than L2 (%.2f GB of candidate rows a step on rank 0)' % (
-            (w.pass_rows if args.config == 4 else nrows_local) * w.row_bytes / 1e9)
-        if cand is not None:
-            cfg['candidate_rows'] = cand
-        cfg['parallelism'] = ('%s x%d, NCCL all-gather of top-k + device merge' % (
+        # the workload (the same dict the reference arm prints); what this
+        # implementation does with it goes beside
+        cfg = workload_config(args)
+        impl = {'parallelism': ('%s x%d, NCCL all-gather of top-k + device merge' % (
             'row-sharded (IVF lists cut at rank boundaries)' if args.config == 4 else 'row-sharded', world)
-            if world > 1 else 'single GPU')
+            if world > 1 else 'single GPU')}
+        if cand is not None:
+            impl['candidate_rows'] = cand
+        if getattr(w, 'vtable', None) and world == 1:
+            impl['worker_entry_points'] = w.vtable()
         # the per-step stage times and the check close the line, so that a
         # reader keeping only its end still has them
-        if getattr(w, 'vtable', None) and world == 1:
-            cfg['worker_entry_points'] = w.vtable()
         line = {'metric': METRIC, 'value': value, 'unit': 'queries/s', 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True,
-                'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg,
+                'scaling': 'strong', 'vs_baseline': None, 'dtype': w.dtype, 'data': w.data, 'config': cfg, **impl,
                 'e2e': e2e, 'gpu_launches': int(launches), 'roofline': roofline, 'cpu_baseline': cpu,
                 'clocks': clock_info, 'verified_vs_oracle': verified, 'timed_steps': args.steps,
                 'step_ms': {'min': round(min(step_ms), 4), 'median': round(statistics.median(step_ms), 4),
