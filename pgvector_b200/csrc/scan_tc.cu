@@ -71,6 +71,7 @@ struct TcArgs {
   uint64_t rtiles;
   uint64_t wait_ns;    // limit of each pipeline wait (the drains keep kWaitNs)
   int32_t q_lo_row;    // FP8 scan: row of the query map holding the low terms' first query
+  uint32_t pf_tiles;   // gathered FP16 rows: L2 prefetch this many of the CTA's tiles ahead
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -754,8 +755,10 @@ __global__ void __launch_bounds__(TcCfg<Q>::NT, 1)
         const uint64_t id = val[j] ? cand_row(a.ids, a.base + vi * a.stride, a.s.rows) : 0;
         src[j] = a.s.codes + id * rb;
       }
-      const uint64_t next = tile + gridDim.x;
-      if (next < ntiles) {
+      // the tile pf_tiles ahead (at this CTA's first tile, every tile up to it)
+      for (uint32_t d = tile == blockIdx.x ? 1 : t.pf_tiles; d <= t.pf_tiles; d++) {
+        const uint64_t next = tile + (uint64_t)d * gridDim.x;
+        if (next >= ntiles) break;
         const uint64_t vn = (next / t.qtiles) * BM + gt;
         if (vn < a.count) {
           const uint8_t *row = a.s.codes + cand_row(a.ids, a.base + vn * a.stride, a.s.rows) * rb;
@@ -1417,6 +1420,17 @@ size_t tc_scan_smem_t(uint32_t nq) {
 // Largest query count one tensor-scan launch takes (thresholds in shared memory).
 uint32_t tc_scan_max_queries() { return 4096; }
 
+// How many of a CTA's tiles ahead the gathering FP16 scan asks L2 for:
+// ANN_B200_PREFETCH_TILES (1-4), a tuning knob, else 1.
+uint32_t prefetch_tiles() {
+  static const uint32_t n = [] {
+    const char *v = getenv("ANN_B200_PREFETCH_TILES");
+    const int x = v && *v ? atoi(v) : 1;
+    return (uint32_t)(x < 1 ? 1 : x > 4 ? 4 : x);
+  }();
+  return n;
+}
+
 // The limit of each pipeline wait in the flat tensor scan: 4 s, or, for
 // tests of the time-out path, ANN_B200_PIPELINE_WAIT_NS (read at every
 // launch). A wait that runs out sets FLAG_TIMEOUT and the search fails with
@@ -1493,6 +1507,7 @@ cudaError_t launch_tc_scan(const ScanArgs &a, const CUtensorMap &rows_map, int64
   t.qtiles = (a.nq + bn - 1) / bn;
   t.rtiles = (a.count + BM - 1) / BM;
   t.wait_ns = pipeline_wait_ns();
+  t.pf_tiles = prefetch_tiles();
   t.q_lo_row = (int32_t)(t.qtiles * bn);
   if (a.count == 0 || a.nq == 0) return cudaSuccess;
   if (a.f8) {
