@@ -219,9 +219,12 @@ int			AnnB200CommSize(const AnnB200Comm *comm);
  * shards, bit for bit. comm NULL: AnnB200Search. nranks * k <= 4096, nq <=
  * 32768.
  *
- * Each rank's search is enqueued on stream without a host round trip; one
- * all-gather (per rank: a header with its status and flags, then its
- * counts, distances and ids) and the device merge follow, then the one
+ * Each rank's search is enqueued on stream without a host round trip. Two
+ * all-gathers: between the filter pass and the exact re-score, each rank's
+ * bound of every query's k-th exact distance (8 bytes a query), so that a
+ * rank re-scores and sends only the survivors that can reach the merged top
+ * k; then the packets (per rank: a header with its status and flags, then
+ * its counts, distances and ids) and the device merge, then the one
  * synchronisation. Every rank reads every rank's header, so all ranks
  * succeed or fail together, and when a rank's candidate list overflowed
  * they all search again synchronously and exchange once more; no rank
@@ -234,6 +237,21 @@ int			AnnB200SearchSharded(AnnB200Shard *shard, AnnB200Comm *comm, const void *q
 								 const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric,
 								 uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
 								 uint32_t *out_count, int32_t *status, void *stream);
+
+/*
+ * AnnB200SearchSharded (comm NULL: AnnB200Search) over the shard rows whose
+ * bits are set in a device bitmap -- bit r of word r / 32, nbits <= the
+ * shard's rows -- in one call: the bitmap's expansion to ascending rows (as
+ * AnnB200BitmapRows; the reference's expand_* kernels before a bitmap
+ * search, ann/server/cuvs.c:1910-1968) into a buffer of the shard, then the
+ * search. *nrows (optional) receives the rows the bitmap selected. A bad
+ * bitmap is this rank's status: with comm it still joins the exchange.
+ * Arguments otherwise as AnnB200SearchSharded. Synchronous.
+ */
+int			AnnB200SearchBitmap(AnnB200Shard *shard, AnnB200Comm *comm, const void *queries, uint32_t nq,
+								const uint32_t *words, uint64_t nbits, uint32_t k, uint32_t metric,
+								uint32_t flags, uint32_t out_cap, double *out_dist, int64_t *out_id,
+								uint32_t *out_count, int32_t *status, uint64_t *nrows, void *stream);
 
 /*
  * IVF list gather: exact k-nearest search of each query over the rows of the

@@ -119,6 +119,25 @@ class Shard:
                                           _ptr(status), _stream(stream)))
         return dist, ids, count
 
+    def search_bitmap(self, comm, queries, k, metric, words, nbits, stream=None, status=None, force_simt=False):
+        """AnnB200SearchBitmap: search_sharded (comm None: one GPU) over the
+        rows whose bits are set in a u32 device bitmap of nbits rows, the
+        expansion and the search in one call. Returns (dist, id, count,
+        rows selected)."""
+        import torch
+        nq = int(queries.shape[0])
+        cap = max(int(k), 1)
+        dev = queries.device
+        dist = torch.empty((nq, cap), dtype=torch.float64, device=dev)
+        ids = torch.empty((nq, cap), dtype=torch.int64, device=dev)
+        count = torch.empty((nq,), dtype=torch.int32, device=dev)
+        n = ctypes.c_uint64()
+        check(load().AnnB200SearchBitmap(self._handle, comm.handle if comm is not None else None, _ptr(queries), nq,
+                                         _ptr(words), int(nbits), int(k), int(metric),
+                                         FORCE_SIMT if force_simt else 0, cap, _ptr(dist), _ptr(ids), _ptr(count),
+                                         _ptr(status), ctypes.byref(n), _stream(stream)))
+        return dist, ids, count, n.value
+
     def search_lists_sharded(self, comm, queries, k, metric, offsets, probes, row_ids=None, stream=None,
                              status=None, force_simt=False):
         """One rank of a sharded IVF list search (AnnB200SearchListsSharded):

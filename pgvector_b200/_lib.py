@@ -78,6 +78,8 @@ SIGNATURES = {
                                           c_void_p, c_void_p, c_void_p, c_void_p]),
     'AnnB200SearchSharded': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
                                      c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    'AnnB200SearchBitmap': (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32,
+                                    c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

@@ -413,6 +413,8 @@ struct AnnB200Shard {
   CUtensorMap seg_map;         // E4M3 / NVFP4 codes, 128-byte swizzled boxes 128 x 128 (IVF tensor scan)
   bool seg_map_ok = false;
   DeviceBuffer staging;        // gathered candidate rows (contiguous) for the tensor scan
+  std::mutex rows_mu;          // AnnB200SearchBitmap's row list
+  DeviceBuffer bitmap_rows;
   cudaStream_t side = nullptr; // gathers the next chunk's rows while the current one is scanned
   cudaEvent_t ev[5] = {};      // [0,1] slot gathered, [2,3] slot scanned, [4] pass start
 };
@@ -1280,21 +1282,26 @@ int sharded_exchange(AnnB200Shard *sh, AnnB200Comm *comm, int local, uint32_t nq
 
 }  // namespace
 
-extern "C" int AnnB200SearchSharded(AnnB200Shard *sh, AnnB200Comm *comm, const void *queries, uint32_t nq,
-                                    const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags,
-                                    uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
-                                    int32_t *status, void *stream) {
-  if (!comm)
+namespace {
+
+// AnnB200SearchSharded with `local` the caller's own status of this rank
+// (a failure of its own preparation: the rank still joins the exchange).
+int sharded_search(AnnB200Shard *sh, AnnB200Comm *comm, int local, const void *queries, uint32_t nq,
+                   const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags, uint32_t out_cap,
+                   double *out_dist, int64_t *out_id, uint32_t *out_count, int32_t *status, void *stream) {
+  if (!comm) {
+    if (local != OK) return local;
     return AnnB200Search(sh, queries, nq, rows, nrows, k, metric, flags, out_cap, out_dist, out_id, out_count, status,
                          stream);
+  }
   if (!sh) return fail(INVALID, "shard is NULL");
   if (comm->device != sh->device)
     return fail(INVALID, "the communicator's device %d is not the shard's %d", comm->device, sh->device);
   // Checks that depend on this rank alone become its status: the rank still
   // joins the exchange, and every rank returns the failure.
   const ShardView &v = sh->view;
-  int local = OK;
-  if (flags & ANNB200_WINDOW) local = fail(UNSUPPORTED, "a sharded search returns the strict top k");
+  if (local != OK) {
+  } else if (flags & ANNB200_WINDOW) local = fail(UNSUPPORTED, "a sharded search returns the strict top k");
   else if (v.dtype == DT_BIT ? metric != M_HAM : metric > M_COS)
     local = fail(UNSUPPORTED, "metric %u does not apply to storage format %u", metric, v.dtype);
   else if (!queries || !out_dist || !out_id || !out_count) local = fail(INVALID, "NULL query or result pointer");
@@ -1311,6 +1318,16 @@ extern "C" int AnnB200SearchSharded(AnnB200Shard *sh, AnnB200Comm *comm, const v
                             return local_search(sh, pk, pl, queries, nq, rows, nrows, k, metric, flags, status,
                                                 (cudaStream_t)stream, deferred, bx);
                           });
+}
+
+}  // namespace
+
+extern "C" int AnnB200SearchSharded(AnnB200Shard *sh, AnnB200Comm *comm, const void *queries, uint32_t nq,
+                                    const uint32_t *rows, uint64_t nrows, uint32_t k, uint32_t metric, uint32_t flags,
+                                    uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
+                                    int32_t *status, void *stream) {
+  return sharded_search(sh, comm, OK, queries, nq, rows, nrows, k, metric, flags, out_cap, out_dist, out_id,
+                        out_count, status, stream);
 }
 
 // The coarse probe: each query's nprobe nearest centroids, as a search of
@@ -1637,7 +1654,12 @@ extern "C" int AnnB200MergeTopk(const double *dist, const int64_t *ids, const ui
     counted(1);
     return OK;
   }
-  static thread_local DeviceBuffer fl;
+  // a buffer of this host thread on the current device (a thread may merge on several)
+  static thread_local DeviceBuffer fls[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(UNSUPPORTED, "device %d", dev);
+  DeviceBuffer &fl = fls[dev];
   CK(fl.reserve(64), "merge flags");
   CK(cudaMemsetAsync(fl.p, 0, 16, st), "memset");
   int h = clock.begin(ST_MERGE);
@@ -1690,7 +1712,12 @@ int bitmap_rows_at(const uint32_t *words, uint64_t nbits, uint32_t base, uint32_
   if (!words || !rows) return fail(INVALID, "NULL pointer");
   if (nbits > 0xffffffffull || (uint64_t)base + nbits > 0x100000000ull)
     return fail(INVALID, "row numbers past 2^32");
-  static thread_local DeviceBuffer scratch;
+  // a buffer of this host thread on the current device (a thread may expand on several)
+  static thread_local DeviceBuffer scratches[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(UNSUPPORTED, "device %d", dev);
+  DeviceBuffer &scratch = scratches[dev];
   const uint32_t nb = bitmap_blocks(nbits);
   CK(scratch.reserve(align256((size_t)nb * 4) + 8), "bitmap scratch");
   unsigned long long *total = (unsigned long long *)((uint8_t *)scratch.p + align256((size_t)nb * 4));
@@ -1732,6 +1759,32 @@ extern "C" int AnnB200BitmapRows(const uint32_t *words, uint64_t nbits, uint32_t
 extern "C" int AnnB200BitmapRowsFrom(const uint32_t *words, uint64_t nbits, uint32_t first_row, uint32_t *rows,
                                      uint64_t *count, void *stream) {
   return bitmap_rows_at(words, nbits, first_row, rows, count, (cudaStream_t)stream);
+}
+
+// The bitmap's rows go to a buffer of the shard (its own lock: the search
+// takes the shard's), then the search over them -- one call, so the host
+// turns from the count's read-back straight to the search's launches.
+extern "C" int AnnB200SearchBitmap(AnnB200Shard *sh, AnnB200Comm *comm, const void *queries, uint32_t nq,
+                                   const uint32_t *words, uint64_t nbits, uint32_t k, uint32_t metric, uint32_t flags,
+                                   uint32_t out_cap, double *out_dist, int64_t *out_id, uint32_t *out_count,
+                                   int32_t *status, uint64_t *nrows_out, void *stream) {
+  if (nrows_out) *nrows_out = 0;
+  if (!sh) return fail(INVALID, "shard is NULL");
+  std::lock_guard<std::mutex> lock(sh->rows_mu);
+  DeviceGuard g(sh->device);
+  uint64_t n = 0;
+  int local = OK;
+  if (nbits > sh->view.rows) local = fail(INVALID, "the bitmap has more bits than the shard has rows");
+  else if (nbits && !words) local = fail(INVALID, "bitmap words are NULL");
+  else if (cudaError_t e = sh->bitmap_rows.reserve(std::max<uint64_t>(nbits, 1) * sizeof(uint32_t)))
+    local = fail(e == cudaErrorMemoryAllocation ? NOMEM : BACKEND_ERROR, "bitmap rows: %s", cudaGetErrorString(e));
+  else
+    local = bitmap_rows_at(words, nbits, 0, (uint32_t *)sh->bitmap_rows.p, &n, (cudaStream_t)stream);
+  if (local != OK) cudaGetLastError();
+  if (nrows_out) *nrows_out = n;
+  // an empty row list is a search over no rows (not over the whole shard)
+  return sharded_search(sh, comm, local, queries, nq, (const uint32_t *)sh->bitmap_rows.p, n, k, metric, flags,
+                        out_cap, out_dist, out_id, out_count, status, stream);
 }
 
 extern "C" unsigned long long AnnB200LaunchCount(void) { return g_launches.load(); }

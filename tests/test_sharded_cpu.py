@@ -165,7 +165,7 @@ def test_shard_bounds_word_aligned():
 
 def check_worker(rank, world, port, out):
     # bench.py's multi-rank check: each rank answers with the oracle over its
-    # own rows; rank 0 holds every rank's list and judges merged answers
+    # own rows; rank 0 holds every rank's list and checks merged answers
     import bench
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
     torch.distributed.init_process_group('gloo', rank=rank, world_size=world)

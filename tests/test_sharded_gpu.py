@@ -58,11 +58,27 @@ def test_one_rank_exchange_equals_oracle(cuda):
         x = synth.mixture(50000, 256, 40, seed=11, normalize=True)
         h = synth.to_half_bits(x)
         q = synth.mixture_queries(300, 256, 40, seed=12, normalize=True).astype(np.float16).astype(np.float32)
-        _, ids = synth.bitmap(50000, 0.5, seed=13)
+        words, ids = synth.bitmap(50000, 0.5, seed=13)
         shard = pb.Shard(pb.F16, 256, to_dev(h, cuda), first_id=1000)
         got = shard.search_sharded(comm, to_dev(q, cuda), 50, pb.COSINE, rows=to_dev(ids, cuda))
         od, oi, oc, _ = oracle.search(oracle.F16, 256, h, q, 50, 2, ids=ids)
-        same(got, (od, np.where(oi >= 0, oi + 1000, -1), oc), 300)
+        want = (od, np.where(oi >= 0, oi + 1000, -1), oc)
+        same(got, want, 300)
+        # the same filter as a bitmap (AnnB200SearchBitmap), through the
+        # communicator and without one
+        for c in (comm, None):
+            d, i, cnt, n = shard.search_bitmap(c, to_dev(q, cuda), 50, pb.COSINE, to_dev(words.view(np.int32), cuda),
+                                               50000)
+            assert n == len(ids)
+            same((d, i, cnt), want, 300)
+        # an empty bitmap: no rows, no results; a bitmap longer than the shard: INVALID
+        zero = np.zeros_like(words)
+        d, i, cnt, n = shard.search_bitmap(comm, to_dev(q, cuda), 50, pb.COSINE, to_dev(zero.view(np.int32), cuda),
+                                           50000)
+        assert n == 0 and int(cnt.sum()) == 0
+        with pytest.raises(pb.AnnB200Error) as err:
+            shard.search_bitmap(comm, to_dev(q, cuda), 50, pb.COSINE, to_dev(words.view(np.int32), cuda), 50001)
+        assert err.value.status == pb.INVALID
         # bit rows, Hamming, whole shard
         rows, proto = synth.bit_rows(40000, 512, 64, flip=0.05, seed=14)
         qs = rows[np.arange(0, 40000, 997)][:40] ^ 1
