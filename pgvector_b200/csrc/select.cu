@@ -982,10 +982,13 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
   const uint8_t *qb = reinterpret_cast<const uint8_t *>(qv);
   const bool qvec = (reinterpret_cast<uintptr_t>(qv) & 15u) == 0;   // the query read 16 bytes at a time
   float bs = 0.0f;                                                   // NVFP4: the current 16-dim block's scale
+  // one staging buffer a warp: the next chunk's loads go to registers while
+  // this one is summed, and are stored after every lane is done with it
+  // (the loop's closing __syncwarp), which leaves room for 8 blocks an SM
   uint4 v[8];
   load_chunk(0, v);
   for (uint32_t c = 0; c < chunks; c++) {
-    const int buf = c & 1;
+    const int buf = 0;
     store_chunk(buf, v);
     __syncwarp();
     if (c + 1 < chunks) load_chunk(c + 1, v);   // in flight while this chunk is summed
@@ -1102,8 +1105,8 @@ __device__ void rescore_group(const SelectArgs &a, unsigned long long *exact, ui
 // queries keep about k survivors, so a grid sized for the largest possible
 // count (4,096) would be mostly blocks with nothing to do.
 template <int DT>
-__global__ void __launch_bounds__(RS_WARPS * 32) rescore(SelectArgs a, unsigned long long *exact, int use_qd) {
-  __shared__ __align__(16) uint8_t stage[RS_WARPS][2][32 * RS_STRIDE];
+__global__ void __launch_bounds__(RS_WARPS * 32, 8) rescore(SelectArgs a, unsigned long long *exact, int use_qd) {
+  __shared__ __align__(16) uint8_t stage[RS_WARPS][1][32 * RS_STRIDE];
   extern __shared__ double qd_dyn[];
   const uint32_t q = blockIdx.y;
   const uint32_t m = a.cnt[q];
