@@ -81,6 +81,9 @@ extern "C"
 #define ANNB200_FORCE_F16 8u	/* E4M3 rows: convert the codes to FP16 on
 								 * chip for kind::f16 MMAs instead of the
 								 * FP8 tensor scan (same results) */
+#define ANNB200_BOUNDS_EXCHANGE 32u	/* sharded searches: exchange the ranks'
+									 * bounds of the k-th distance before the
+									 * exact re-score (a second all-gather) */
 #define ANNB200_INDEX_L2 4u		/* L2 in the loaded-index form: the FP32
 								 * sqrtf of tail + (left + right) lane sums
 								 * (Distance, ann/server/indexfile.c:3133-3151)
@@ -219,13 +222,14 @@ int			AnnB200CommSize(const AnnB200Comm *comm);
  * shards, bit for bit. comm NULL: AnnB200Search. nranks * k <= 4096, nq <=
  * 32768.
  *
- * Each rank's search is enqueued on stream without a host round trip. Two
- * all-gathers: between the filter pass and the exact re-score, each rank's
- * bound of every query's k-th exact distance (8 bytes a query), so that a
- * rank re-scores and sends only the survivors that can reach the merged top
- * k; then the packets (per rank: a header with its status and flags, then
- * its counts, distances and ids) and the device merge, then the one
- * synchronisation. Every rank reads every rank's header, so all ranks
+ * Each rank's search is enqueued on stream without a host round trip; one
+ * all-gather (per rank: a header with its status and flags, then its
+ * counts, distances and ids) and the device merge follow, then the one
+ * synchronisation. With ANNB200_BOUNDS_EXCHANGE (every rank passes it or
+ * none does) a second all-gather runs between the filter pass and the
+ * exact re-score: each rank's bound of every query's k-th exact distance
+ * (8 bytes a query), so that a rank re-scores and sends only the survivors
+ * that can reach the merged top k. Every rank reads every rank's header, so all ranks
  * succeed or fail together, and when a rank's candidate list overflowed
  * they all search again synchronously and exchange once more; no rank
  * leaves a collective the others enter. If the exchange does not finish

@@ -28,7 +28,7 @@ from ._lib import (OK, INVALID, UNSUPPORTED, NOMEM, BACKEND_ERROR, AnnB200Error,
 F32, F16, E4M3, NVFP4, BIT = 0, 1, 2, 3, 4
 L2, IP, COSINE, HAMMING = 0, 1, 2, 3
 SHARD_HOST = 1
-WINDOW, FORCE_SIMT, FORCE_F16 = 1, 2, 8
+WINDOW, FORCE_SIMT, FORCE_F16, BOUNDS_EXCHANGE = 1, 2, 8, 32
 
 DTYPE_NAMES = {'f32': F32, 'float32': F32, 'f16': F16, 'float16': F16, 'halfvec': F16, 'e4m3': E4M3,
                'fp8': E4M3, 'nvfp4': NVFP4, 'bit': BIT}
@@ -98,7 +98,8 @@ class Shard:
                                    _ptr(status), _stream(stream)))
         return dist, ids, count
 
-    def search_sharded(self, comm, queries, k, metric, rows=None, stream=None, status=None, force_simt=False):
+    def search_sharded(self, comm, queries, k, metric, rows=None, stream=None, status=None, force_simt=False,
+                       bounds_exchange=False):
         """One rank of a row-sharded search (AnnB200SearchSharded): every rank
         of `comm` calls this with its own shard and candidate rows and the
         same queries; each gets the k best over all ranks' rows. Returns
@@ -115,11 +116,12 @@ class Shard:
             rows = torch.zeros((1,), dtype=torch.int32, device=dev)
         check(load().AnnB200SearchSharded(self._handle, comm.handle if comm is not None else None, _ptr(queries), nq,
                                           _ptr(rows), nrows if rows is not None else 0, int(k), int(metric),
-                                          FORCE_SIMT if force_simt else 0, cap, _ptr(dist), _ptr(ids), _ptr(count),
-                                          _ptr(status), _stream(stream)))
+                                          (FORCE_SIMT if force_simt else 0) | (BOUNDS_EXCHANGE if bounds_exchange else 0),
+                                          cap, _ptr(dist), _ptr(ids), _ptr(count), _ptr(status), _stream(stream)))
         return dist, ids, count
 
-    def search_bitmap(self, comm, queries, k, metric, words, nbits, stream=None, status=None, force_simt=False):
+    def search_bitmap(self, comm, queries, k, metric, words, nbits, stream=None, status=None, force_simt=False,
+                      bounds_exchange=False):
         """AnnB200SearchBitmap: search_sharded (comm None: one GPU) over the
         rows whose bits are set in a u32 device bitmap of nbits rows, the
         expansion and the search in one call. Returns (dist, id, count,
@@ -134,8 +136,9 @@ class Shard:
         n = ctypes.c_uint64()
         check(load().AnnB200SearchBitmap(self._handle, comm.handle if comm is not None else None, _ptr(queries), nq,
                                          _ptr(words), int(nbits), int(k), int(metric),
-                                         FORCE_SIMT if force_simt else 0, cap, _ptr(dist), _ptr(ids), _ptr(count),
-                                         _ptr(status), ctypes.byref(n), _stream(stream)))
+                                         (FORCE_SIMT if force_simt else 0) | (BOUNDS_EXCHANGE if bounds_exchange else 0),
+                                         cap, _ptr(dist), _ptr(ids), _ptr(count), _ptr(status), ctypes.byref(n),
+                                         _stream(stream)))
         return dist, ids, count, n.value
 
     def search_lists_sharded(self, comm, queries, k, metric, offsets, probes, row_ids=None, stream=None,
@@ -346,4 +349,4 @@ def search_typed(jobs):
 
 __all__ = ['Shard', 'search_typed', 'merge_topk', 'bitmap_rows', 'bitmap_rows_static', 'backend', 'search_gathered', 'device_count', 'load', 'check',
            'AnnB200Error', 'F32', 'F16', 'E4M3', 'NVFP4', 'BIT', 'L2', 'IP', 'COSINE', 'HAMMING', 'WINDOW',
-           'FORCE_SIMT', 'OK', 'INVALID', 'UNSUPPORTED', 'NOMEM', 'BACKEND_ERROR']
+           'FORCE_SIMT', 'FORCE_F16', 'BOUNDS_EXCHANGE', 'OK', 'INVALID', 'UNSUPPORTED', 'NOMEM', 'BACKEND_ERROR']

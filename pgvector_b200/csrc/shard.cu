@@ -1311,9 +1311,12 @@ int sharded_search(AnnB200Shard *sh, AnnB200Comm *comm, int local, const void *q
     local = fail(UNSUPPORTED, "ranks x k must not exceed %d", kSortCap);
   else if (nq > kShardBlocks * tc_scan_max_queries())
     local = fail(UNSUPPORTED, "at most %u queries a sharded call", kShardBlocks * tc_scan_max_queries());
+  // the bounds exchange only when asked (every rank passes the same flags):
+  // by default the ranks' lists cross in the one all-gather
   const uint32_t block = tc_scan_max_queries();
+  const bool bounds = flags & ANNB200_BOUNDS_EXCHANGE;
   return sharded_exchange(sh, comm, local, nq, k, out_cap, out_dist, out_id, out_count, (cudaStream_t)stream,
-                          (nq + block - 1) / block, std::min(nq, block),
+                          bounds ? (nq + block - 1) / block : 0, bounds ? std::min(nq, block) : 0,
                           [&](uint8_t *pk, const Packet &pl, bool deferred, BoundsExchange *bx) {
                             return local_search(sh, pk, pl, queries, nq, rows, nrows, k, metric, flags, status,
                                                 (cudaStream_t)stream, deferred, bx);

@@ -66,9 +66,9 @@ def test_one_rank_exchange_equals_oracle(cuda):
         same(got, want, 300)
         # the same filter as a bitmap (AnnB200SearchBitmap), through the
         # communicator and without one
-        for c in (comm, None):
+        for c, bx in ((comm, False), (comm, True), (None, False)):
             d, i, cnt, n = shard.search_bitmap(c, to_dev(q, cuda), 50, pb.COSINE, to_dev(words.view(np.int32), cuda),
-                                               50000)
+                                               50000, bounds_exchange=bx)
             assert n == len(ids)
             same((d, i, cnt), want, 300)
         # an empty bitmap: no rows, no results; a bitmap longer than the shard: INVALID
@@ -168,16 +168,18 @@ def two_gpu_worker(rank, world, port, out, missing):
             d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=rows)
             torch.cuda.synchronize()
             out[rank] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
+            d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=rows, bounds_exchange=True)
+            out[(rank, 'bounds')] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
             # rank 1 has no candidate rows: its search ends before the bounds
             # exchange, which it still takes part in
             mine = rows if rank == 0 else rows[:0]
-            d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=mine)
+            d, i, c = shard.search_sharded(comm, qd, K, pb.COSINE, rows=mine, bounds_exchange=True)
             out[(rank, 'empty')] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
             # two query blocks over an unfiltered FP32 shard
             x, q2 = multi_block_case()
             b2 = sharded.shard_bounds(MB_ROWS, world)
             s2 = pb.Shard(pb.F32, MB_DIMS, to_dev(x[b2[rank]:b2[rank + 1]], dev), first_id=b2[rank])
-            d, i, c = s2.search_sharded(comm, to_dev(q2, dev), MB_K, pb.L2)
+            d, i, c = s2.search_sharded(comm, to_dev(q2, dev), MB_K, pb.L2, bounds_exchange=True)
             out[(rank, 'blocks')] = (d.cpu().numpy(), i.cpu().numpy(), c.cpu().numpy())
             s2.close()
             dist.barrier()
@@ -212,8 +214,8 @@ def test_two_gpu_sharded_search_equals_whole(cuda):
     x, q2 = multi_block_case()
     md, mi, mc, _ = oracle.search(oracle.F32, MB_DIMS, x, q2, MB_K, 0)
     for r in range(2):
-        for (d, i, c), (wd, wi, wc) in ((out[r], (od, oi, oc)), (out[(r, 'empty')], (ed, ei, ec)),
-                                        (out[(r, 'blocks')], (md, mi, mc))):
+        for (d, i, c), (wd, wi, wc) in ((out[r], (od, oi, oc)), (out[(r, 'bounds')], (od, oi, oc)),
+                                        (out[(r, 'empty')], (ed, ei, ec)), (out[(r, 'blocks')], (md, mi, mc))):
             assert np.array_equal(c, wc.astype(c.dtype))
             assert np.array_equal(i, wi) and np.array_equal(d, wd)
 
