@@ -221,3 +221,18 @@ def test_multi_rank_check_catches_bad_merges():
     off = tuple(t.clone() for t in one)
     off[0][0, 5] = np.nextafter(float(off[0][0, 5]), np.inf)
     assert not bench.check_rescored(off, [part], 1)
+
+
+def test_bench_arms_share_the_workload_config(monkeypatch):
+    # bench.py's two arms (ours, and --impl reference) print the same
+    # `config`: the workload only; how each arm ran it sits beside it
+    import sys
+    import bench
+    for config in (1, 2, 3, 4, 5):
+        monkeypatch.setattr(sys, 'argv', ['bench.py', '--config', str(config)])
+        args = bench.args_parse()
+        cfg = bench.workload_config(args)
+        assert cfg['workload'] == bench.WORKLOADS[config]
+        assert {'global_batch', 'rows', 'dims', 'k', 'l2'} <= set(cfg)
+        assert 'parallelism' not in cfg and 'candidate_rows' not in cfg
+        assert ('selectivity' in cfg) == (config == 2)
