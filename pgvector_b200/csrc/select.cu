@@ -617,7 +617,11 @@ struct BoundArgs {
 // three radix passes then read registers instead of re-reading the row.
 constexpr int KB_REG = 32;
 
-__global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
+// BT threads a block: 256 when the sample fits 256 x KB_REG registers (a
+// row-sharded rank's smaller sample), so four blocks share an SM instead of
+// two (the registers hold the scores).
+template <int BT>
+__global__ void __launch_bounds__(BT, 1024 / BT) kth_bound(BoundArgs b) {
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t scratch[32];
   const uint32_t q = blockIdx.x;
@@ -627,15 +631,15 @@ __global__ void __launch_bounds__(NT) kth_bound(BoundArgs b) {
   }
   const float *m = b.mat + (uint64_t)q * b.ld;
   uint32_t key = 0xffffffffu;
-  if (b.n >= b.k && b.n <= (uint64_t)NT * KB_REG) {
+  if (b.n >= b.k && b.n <= (uint64_t)BT * KB_REG) {
     uint32_t kr[KB_REG];
 #pragma unroll
     for (int j = 0; j < KB_REG; j++) {
-      const uint32_t i = threadIdx.x + j * NT;
+      const uint32_t i = threadIdx.x + j * BT;
       kr[j] = i < b.n ? float_key(__ldg(m + i)) : 0xffffffffu;
     }
-    // element i lives in thread i % NT, slot i / NT: the select visits a
-    // thread's own elements only (i = threadIdx.x + j * NT), so it indexes
+    // element i lives in thread i % BT, slot i / BT: the select visits a
+    // thread's own elements only (i = threadIdx.x + j * BT), so it indexes
     // its registers with the unrolled j
     key = block_radix_select_regs<KB_REG>(kr, (uint32_t)b.n, b.k, hist, scratch);
   } else if (b.n >= b.k) {
@@ -1548,7 +1552,8 @@ void launch_check_rows(const uint32_t *ids, uint64_t n, uint64_t rows, uint32_t 
 void launch_kth_bound(const float *mat, uint64_t ld, uint64_t n, uint32_t nq, uint32_t k, uint32_t metric,
                       int window, const QueryState &qs, cudaStream_t st) {
   BoundArgs b{mat, ld, n, k, metric, window, qs};
-  kth_bound<<<nq, NT, 0, st>>>(b);
+  if (n <= 256ull * KB_REG) kth_bound<256><<<nq, 256, 0, st>>>(b);
+  else kth_bound<NT><<<nq, NT, 0, st>>>(b);
 }
 
 static SelectArgs to_args(const SelectLaunch &l) {
